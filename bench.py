@@ -1,0 +1,344 @@
+"""Decode throughput of the B200 engine on LAICompute's Llama decode loop.
+
+Default workload: the SmolLM-135M-shaped Llama with Q8_0 projections (hidden
+576, 30 layers, 9/3 heads, ffn 1536, vocab 49152, tied Q8_0 embeddings),
+random-init from a fixed seed, 64 independent sequences, 128 random prompt
+ids each, then decode steps. One "step" = one token for every sequence.
+
+  value  tokens/s of K device-chained decode steps (laic_dev_decode: each step
+         feeds every sequence its own sampled id without leaving the device),
+         CUDA events on the engine stream, max over ranks
+  e2e    tokens/s of K laic_dev_step calls (the C ABI a caller uses): host ids
+         in through pinned memory, sampled ids back to the host, every step
+
+Multi-GPU (torchrun, one rank per GPU): the 135M model does not shard per
+layer, so every rank decodes its own 64 sequences (replicas, weak scaling).
+
+--impl reference times the reference's own CPU decode loop (oracle/_ref, the
+reference sources compiled with its native flags) on the same model and
+prompt, one sequence at a time as the reference runs.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from laicompute_b200 import synth  # noqa: E402
+
+WORKLOADS = {
+    # name: (arch, seed, prompt_len, batch, description)
+    "smollm135m-q8_0": (synth.SMOL_135M_Q8, 2, 128, 64, "SmolLM-135M-shaped Llama, Q8_0 projections"),
+    "smollm135m-f16": (synth.SMOL_135M_F16, 1, 8, 1, "SmolLM-135M-shaped Llama, F16"),
+    "llama1b-q4_0": (synth.LLAMA_1B_Q4, 4, 512, 32, "1B-shaped Llama, Q4_0 projections, F16 embeddings"),
+}
+DEFAULT_WORKLOAD = "smollm135m-q8_0"
+
+
+def measured_peak_gbs():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def model_path(name: str, rank: int) -> str:
+    arch, seed, _, _, _ = WORKLOADS[name]
+    d = os.path.join(tempfile.gettempdir(), "laic_bench_models")
+    os.makedirs(d, exist_ok=True)
+    path = os.path.join(d, f"{name}.seed{seed}.r{rank}.gguf")
+    if not os.path.exists(path):
+        tmp = path + ".part"
+        synth.write_model(tmp, arch, seed=seed)
+        os.replace(tmp, path)
+    return path
+
+
+class ClockSampler:
+    """nvidia-smi clock and throttle-reason samples of one GPU during a timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str) -> None:
+        self.uuid = uuid
+        self.rows = []
+        self.proc = None
+        self.t = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", self.uuid, f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "20"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+            time.sleep(0.15)
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.1)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.t.join(timeout=5)
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+            except (ValueError, IndexError):
+                continue
+            for name, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    import torch
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def allreduce_max(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int) -> None:
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def cpu_reference(name: str, path: str, warmup: int, steps: int) -> dict:
+    """The reference's CPU decode loop on one sequence (oracle/_ref, native flags)."""
+    from oracle import oracle as O
+    arch, seed, plen, _, _ = WORKLOADS[name]
+    prompt = synth.prompt_ids(arch.vocab, plen, seed=seed + 100)
+    exe, kind = None, "reference"
+    for variant in ("native", "v3"):
+        cand = O.ref_driver(variant)
+        if cand and subprocess.run([cand], capture_output=True).returncode == 2:  # usage exit: runs on this CPU
+            exe = cand
+            break
+    if exe is None:
+        return {"unavailable": "reference driver not built or not runnable on this CPU"}
+    with tempfile.NamedTemporaryFile(suffix=".u32", delete=False) as f:
+        prompt.tofile(f.name)
+        pf = f.name
+    try:
+        r = subprocess.run([exe, "time", path, "--prompt", pf, "--warmup", str(warmup), "--steps", str(steps)],
+                           capture_output=True, text=True, check=True)
+    finally:
+        os.unlink(pf)
+    info = json.loads(r.stdout.strip().splitlines()[-1])
+    return {"value": info["tok_s"], "unit": "tokens/s", "cores": info["threads"], "kind": kind,
+            "sample": f"{os.path.basename(exe)}: {plen}-token prompt (untimed), {warmup} warm-up + {steps} timed "
+                      f"decode steps of one sequence on {info['threads']} threads (the reference decodes one "
+                      f"sequence at a time, so its tokens/s does not depend on the batch)",
+            "prefill_s": info["prefill_s"]}
+
+
+def run_reference(args) -> None:
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    name = args.workload
+    arch, seed, plen, batch, desc = WORKLOADS[name]
+    path = model_path(name, 0)
+    steps = min(args.steps, args.ref_steps)
+    res = cpu_reference(name, path, max(1, min(args.warmup, 3)), steps)
+    if "unavailable" in res:
+        print(json.dumps({"impl": "reference", "unavailable": res["unavailable"]}))
+        return
+    out = {
+        "impl": "reference", "metric": "decode tokens/s", "value": round(res["value"], 3), "unit": "tokens/s",
+        "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": round(1000.0 / res["value"], 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{name} decode", "model": desc, "batch": batch, "prompt": plen,
+                   "note": "reference CPU loop, one sequence at a time"},
+        "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": round(res["value"], 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out))
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS))
+    ap.add_argument("--batch", type=int, default=0, help="sequences per GPU (0 = the workload's)")
+    ap.add_argument("--sample", action="store_true", help="temperature 0.8 / top-k 40 instead of greedy")
+    ap.add_argument("--ref-steps", type=int, default=64, help="cap of timed CPU decode steps")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-batch1", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    world, rank, local = dist_setup()
+    import torch
+    from laicompute_b200.engine import Engine, sample_params
+
+    name = args.workload
+    arch, seed, plen, batch, desc = WORKLOADS[name]
+    if args.batch:
+        batch = args.batch
+    path = model_path(name, rank)
+    ctx_need = plen + 2 * args.warmup + 2 * args.steps + 2
+    eng = Engine(path, max_seqs=batch, device=local, kv_capacity=ctx_need)
+    slots = np.arange(batch, dtype=np.int32)
+    prompts = np.stack([synth.prompt_ids(arch.vocab, plen, seed=seed + 100 + 1000 * rank + i) for i in range(batch)])
+    if args.sample:
+        params = [sample_params(0.8, 40, 1.0, 1.0, 4242 + 1000 * rank + i) for i in range(batch)]
+    else:
+        params = [sample_params()] * batch
+    for j in range(plen - 1):
+        eng.prefill(prompts[:, j], slots)
+    first, _ = eng.step(prompts[:, -1], slots, params)
+
+    # ---- device-resident decode loop (value)
+    ids_w, _ = eng.decode(first, slots, params, steps=args.warmup)
+    tok = ids_w[-1]
+    uuid = str(torch.cuda.get_device_properties(local).uuid)
+    uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(uuid) as clk:
+        ids, dev_ms = eng.decode(tok, slots, params, steps=args.steps)
+    barrier(world)
+    torch.cuda.synchronize()
+    max_ms = allreduce_max(dev_ms, world)
+    value = batch * args.steps * world / (max_ms / 1000.0)
+    tok = ids[-1]
+
+    # ---- end to end through laic_dev_step: host ids in, sampled ids out, every step
+    ext = torch.cuda.ExternalStream(eng.stream, device=torch.device("cuda", local))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(args.warmup):
+        tok, _ = eng.step(tok, slots, params)
+    barrier(world)
+    torch.cuda.synchronize()
+    e0.record(ext)
+    for _ in range(args.steps):
+        tok, _ = eng.step(tok, slots, params)
+    e1.record(ext)
+    e1.synchronize()
+    e2e_ms = allreduce_max(e0.elapsed_time(e1), world)
+    e2e_value = batch * args.steps * world / (e2e_ms / 1000.0)
+
+    # ---- per-kernel roofline (eager launches with CUDA events around each)
+    st = eng.stats()
+    prof = eng.profile(np.tile(tok, 4), 4)
+    dom = max(prof.items(), key=lambda kv: kv[1][1])
+    dname, (dl, dus, dbytes) = dom
+    peak, peak_kind = measured_peak_gbs()
+    achieved = (dbytes / dl) / (dus / dl * 1e-6) / 1e9
+    kv_read = prof["attention"][2] / max(1, prof["attention"][0]) * arch.layers  # KV bytes read per step
+
+    out = None
+    if rank == 0:
+        out = {
+            "metric": "decode tokens/s", "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(max_ms / args.steps, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"{name} decode, batch {batch} per GPU, prompt {plen}, "
+                                   f"{'T=0.8/top-k 40' if args.sample else 'greedy'}",
+                       "model": desc, "batch_per_gpu": batch, "prompt": plen,
+                       "parallelism": f"replicas x{world}", "kv": "fp16",
+                       "l2": "inputs larger than L2: weights %.0f MB + KV read %.0f MB per step"
+                             % (st.weight_bytes / 1e6, kv_read / 1e6)},
+            "hbm_gbs_step": round((st.weight_bytes + kv_read) / (max_ms / args.steps * 1e-3) / 1e9, 1),
+            "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s", "h2d_bytes_per_step": batch * (4 + 4 + 24),
+                    "d2h_bytes_per_step": batch * 4},
+            "gpu_launches": int(args.steps * (st.launches_per_step + 1)),
+            "roofline": {"bound": "hbm", "kernel": dname, "achieved": round(achieved, 1), "peak": peak,
+                         "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                         "bytes_per_launch": round(dbytes / dl), "us_per_launch": round(dus / dl, 3),
+                         "kernels": {k: {"launches": v[0], "us_per_launch": round(v[1] / v[0], 3),
+                                         "gbs": round(v[2] / v[1] * 1e-3, 1)} for k, v in prof.items()}},
+            "clocks": clk.summary(),
+        }
+    eng.close()
+
+    # ---- batch-1 decode (the latency case) on the same model
+    if not args.no_batch1:
+        e1b = Engine(path, max_seqs=1, device=local, kv_capacity=ctx_need)
+        for t in prompts[0, :-1]:
+            e1b.prefill([t], [0])
+        f1, _ = e1b.step([prompts[0, -1]], [0])
+        w, _ = e1b.decode(f1, [0], None, steps=args.warmup)
+        barrier(world)
+        _, ms1 = e1b.decode(w[-1], [0], None, steps=args.steps)
+        ms1 = allreduce_max(ms1, world)
+        if out is not None:
+            s1 = e1b.stats()
+            out["batch1"] = {"value": round(args.steps * world / (ms1 / 1000.0), 2), "unit": "tokens/s",
+                             "ms_per_step": round(ms1 / args.steps, 5),
+                             "hbm_gbs": round(s1.weight_bytes / (ms1 / args.steps * 1e-3) / 1e9, 1)}
+        e1b.close()
+
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        res = cpu_reference(name, path, 1, min(args.steps, 16))
+        if "unavailable" not in res:
+            out["cpu_baseline"] = {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        else:
+            out["cpu_baseline"] = None
+    if rank == 0:
+        print(json.dumps(out))
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

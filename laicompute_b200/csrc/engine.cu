@@ -1,0 +1,928 @@
+// B200 decode engine behind the C ABI of include/laic_b200.h.
+//
+// One laic_dev holds a Llama model's weights in HBM (uploaded once per GGUF
+// tensor), an FP16 (or FP32) KV cache with `max_seqs` slots, and per-step
+// CUDA graphs: a decode step (LlamaRuntime::step + sample, reference
+// src/inference_v2.cpp:31-32) is one graph replay whose only host traffic is
+// the input ids in and the sampled ids out.
+//
+// Per layer the step runs four dequant-fused matvec launches and one attention
+// launch (reference :31):
+//   qkv   rmsnorm(attn_norm) -> fused [Wq;Wk;Wv] -> RoPE -> q, K/V cache append
+//   attn  split-K GQA decode attention -> attn
+//   o     Wo attn, added into the residual
+//   gu    rmsnorm(ffn_norm) -> interleaved [Wgate;Wup] -> silu(g)*u
+//   down  Wdown act, added into the residual
+// then rmsnorm(output_norm) -> lm_head -> sampler. Kernels use programmatic
+// dependent launch so each one's launch and prologue overlap the previous one.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <random>
+#include <string>
+#include <vector>
+
+#include "../../include/laic_b200.h"
+#include "attention.cuh"
+#include "matvec.cuh"
+#include "misc.cuh"
+#include "sampler.cuh"
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const std::string& msg) {
+    g_err = msg;
+    return code;
+}
+
+#define CK(x)                                                                                      \
+    do {                                                                                           \
+        cudaError_t e_ = (x);                                                                      \
+        if (e_ != cudaSuccess) return fail(LAIC_E_CUDA, std::string(#x) + ": " + cudaGetErrorString(e_)); \
+    } while (0)
+
+using laic::T_F16;
+using laic::T_F32;
+using laic::T_Q4_0;
+using laic::T_Q8_0;
+
+size_t elem_bytes(int type, size_t n) {
+    switch (type) {
+    case T_F32: return n * 4;
+    case T_F16: return n * 2;
+    case T_Q4_0: return n / 32 * 18;
+    case T_Q8_0: return n / 32 * 34;
+    }
+    return 0;
+}
+
+// A projection matrix in the device layout of matvec.cuh.
+struct Mat {
+    int type = -1;
+    int rows = 0, in = 0, nb = 0;
+    void* w = nullptr;
+    unsigned short* d = nullptr;
+    size_t bytes() const {  // bytes one matvec streams
+        if (type == T_F16) return (size_t)rows * in * 2;
+        if (type == T_Q4_0) return (size_t)rows * nb * 18;
+        if (type == T_Q8_0) return (size_t)rows * nb * 34;
+        return 0;
+    }
+};
+
+int mat_alloc(Mat& m, int type, int rows, int in) {
+    if (type != T_F16 && type != T_Q4_0 && type != T_Q8_0)
+        return fail(LAIC_E_UNSUPPORTED, "unsupported matrix type " + std::to_string(type) + " (F16, Q8_0, Q4_0 only)");
+    if (in % 32) return fail(LAIC_E_UNSUPPORTED, "row length must be a multiple of 32");
+    m.type = type; m.rows = rows; m.in = in; m.nb = in / 32;
+    if (type == T_F16) {
+        CK(cudaMalloc(&m.w, (size_t)rows * in * 2));
+    } else {
+        const size_t qb = type == T_Q4_0 ? 16 : 32;
+        CK(cudaMalloc(&m.w, (size_t)rows * m.nb * qb));
+        CK(cudaMalloc(&m.d, (size_t)rows * m.nb * 2));
+    }
+    return LAIC_OK;
+}
+
+void mat_free(Mat& m) {
+    if (m.w) cudaFree(m.w);
+    if (m.d) cudaFree(m.d);
+    m.w = nullptr; m.d = nullptr;
+}
+
+// Copy GGUF rows [row0, row0+nrows) (raw block bytes) into matrix rows
+// r*row_mul + row_add through a device staging buffer.
+int mat_fill(Mat& m, const uint8_t* host, int nrows, int row_mul, long long row_add, cudaStream_t st) {
+    const size_t row_bytes = elem_bytes(m.type, (size_t)m.in);
+    const size_t chunk_rows = std::max<size_t>(1, (64u << 20) / row_bytes);
+    void* staging = nullptr;
+    CK(cudaMalloc(&staging, std::min<size_t>(chunk_rows, (size_t)nrows) * row_bytes));
+    for (size_t r0 = 0; r0 < (size_t)nrows; r0 += chunk_rows) {
+        const size_t n = std::min(chunk_rows, (size_t)nrows - r0);
+        CK(cudaMemcpyAsync(staging, host + r0 * row_bytes, n * row_bytes, cudaMemcpyHostToDevice, st));
+        const long long add = (long long)r0 * row_mul + row_add;
+        if (m.type == T_F16) {
+            const int vpr = m.in / 8;
+            laic::repack_f16_rows_kernel<<<592, 256, 0, st>>>((const uint4*)staging, (uint4*)m.w, (long long)n, vpr,
+                                                              row_mul, add);
+        } else {
+            const int bb = m.type == T_Q4_0 ? 18 : 34, qb = m.type == T_Q4_0 ? 16 : 32;
+            laic::repack_blocks_kernel<<<592, 256, 0, st>>>((const uint8_t*)staging, (uint8_t*)m.w, m.d, (long long)n,
+                                                            m.nb, bb, qb, row_mul, add);
+        }
+        CK(cudaGetLastError());
+    }
+    CK(cudaStreamSynchronize(st));
+    cudaFree(staging);
+    return LAIC_OK;
+}
+
+// ---------------------------------------------------------------------------
+// launch helpers
+// ---------------------------------------------------------------------------
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                     Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+int g_num_sms = 0;
+int num_sms() {
+    if (!g_num_sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+        if (g_num_sms <= 0) g_num_sms = 148;
+    }
+    return g_num_sms;
+}
+
+using MatvecFn = void (*)(laic::MatvecParams);
+
+template <int WT, int NS, int EPI, typename KV>
+MatvecFn mv_fn() {
+    auto f = laic::matvec_kernel<WT, NS, EPI, KV>;
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        attr_set = true;
+    }
+    return f;
+}
+
+template <int WT, int NS>
+MatvecFn mv_pick_epi(int epi, bool kv32) {
+    switch (epi) {
+    case laic::EPI_STORE: return mv_fn<WT, NS, laic::EPI_STORE, __half>();
+    case laic::EPI_ADD: return mv_fn<WT, NS, laic::EPI_ADD, __half>();
+    case laic::EPI_SWIGLU: return mv_fn<WT, NS, laic::EPI_SWIGLU, __half>();
+    default: return kv32 ? mv_fn<WT, NS, laic::EPI_QKV, float>() : mv_fn<WT, NS, laic::EPI_QKV, __half>();
+    }
+}
+
+MatvecFn mv_pick(int type, int ns, int epi, bool kv32) {
+    if (type == T_Q4_0) return ns == 1 ? mv_pick_epi<T_Q4_0, 1>(epi, kv32) : mv_pick_epi<T_Q4_0, 2>(epi, kv32);
+    if (type == T_Q8_0) return ns == 1 ? mv_pick_epi<T_Q8_0, 1>(epi, kv32) : mv_pick_epi<T_Q8_0, 2>(epi, kv32);
+    return ns == 1 ? mv_pick_epi<T_F16, 1>(epi, kv32) : mv_pick_epi<T_F16, 2>(epi, kv32);
+}
+
+int rows_per_group(int type) { return type == T_F16 ? 4 : 8; }
+
+cudaError_t launch_matvec(const Mat& m, laic::MatvecParams p, int epi, bool kv32, cudaStream_t st, bool pdl) {
+    p.w = m.w; p.d = m.d; p.rows = m.rows; p.in = m.in; p.nb = m.nb;
+    const int ns = p.nseq == 1 ? 1 : 2;
+    const int groups = (m.rows + rows_per_group(m.type) - 1) / rows_per_group(m.type);
+    const int per_sm = ns == 1 ? 2 : 1;
+    const int grid = std::max(1, std::min((groups + 7) / 8, num_sms() * per_sm));
+    const size_t smem = (size_t)ns * m.in * sizeof(float);
+    return launch_k(mv_pick(m.type, ns, epi, kv32), dim3(grid), dim3(256), smem, st, pdl, p);
+}
+
+using AttnFn = void (*)(laic::AttnParams);
+template <int D, int GM>
+AttnFn attn_fn_g(bool kv32) {
+    return kv32 ? laic::attn_decode_kernel<D, GM, float, true> : laic::attn_decode_kernel<D, GM, __half, false>;
+}
+template <int D>
+AttnFn attn_fn_d(int G, bool kv32) {
+    if (G <= 1) return attn_fn_g<D, 1>(kv32);
+    if (G <= 2) return attn_fn_g<D, 2>(kv32);
+    if (G <= 4) return attn_fn_g<D, 4>(kv32);
+    return attn_fn_g<D, 8>(kv32);
+}
+AttnFn attn_pick(int D, int G, bool kv32) {
+    if (D == 32) return attn_fn_d<32>(G, kv32);
+    if (D == 64) return attn_fn_d<64>(G, kv32);
+    if (D == 128) return attn_fn_d<128>(G, kv32);
+    return nullptr;
+}
+
+// ---------------------------------------------------------------------------
+// the engine
+// ---------------------------------------------------------------------------
+struct Layer {
+    Mat qkv, o, gu, down;
+    float* attn_norm = nullptr;
+    float* ffn_norm = nullptr;
+    unsigned have = 0;  // bit per uploaded tensor
+};
+enum : unsigned { H_ANORM = 1, H_Q = 2, H_K = 4, H_V = 8, H_O = 16, H_FNORM = 32, H_GATE = 64, H_UP = 128, H_DOWN = 256,
+                  H_ALL = 511 };
+
+enum StepMode : int { MODE_PREFILL = 0, MODE_STEP = 1, MODE_CHAIN = 2 };
+
+}  // namespace
+
+struct laic_dev {
+    laic_dev_desc a{};
+    laic_dev_opts o{};
+    int device = 0;
+    cudaStream_t st = nullptr;
+    int H = 0, Hkv = 0, D = 0, G = 0, h = 0, kv = 0, F = 0, V = 0, L = 0, S = 0, cap = 0, rope_pairs = 0;
+    bool kv32 = false, use_graph = true, use_pdl = true;
+
+    Mat embd, lm;
+    bool have_embd = false, have_out = false, have_onorm = false;
+    float* out_norm = nullptr;
+    std::vector<Layer> layers;
+
+    float *x = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr, *logits = nullptr;
+    void *kc = nullptr, *vc = nullptr;
+    long long kv_layer_stride = 0, kv_slot_stride = 0;
+    int* pos = nullptr;
+    unsigned* counts = nullptr;
+    float2* rope_cs = nullptr;
+    float* attn_part = nullptr;
+    unsigned* attn_cnt = nullptr;
+    int max_split = 1;
+
+    unsigned *d_tokens = nullptr, *d_out_ids = nullptr, *d_hist = nullptr;
+    int *d_slots = nullptr, *d_err = nullptr, *d_hist_count = nullptr;
+    size_t hist_cap = 0;  // entries of d_hist
+    laic::SampleDev* d_params = nullptr;
+    unsigned *h_tokens = nullptr, *h_out_ids = nullptr;
+    int* h_slots = nullptr;
+    laic::SampleDev* h_params = nullptr;
+    std::vector<long long> h_pos;
+
+    std::map<std::pair<int, int>, cudaGraphExec_t> graphs;  // (nseq, mode) -> graph
+    int last_split = 1;
+
+    // ------------------------------------------------------------------
+    int nsplit_for(int nseq) const {
+        const int pairs = nseq * Hkv;
+        int s = (2 * num_sms() + pairs - 1) / pairs;
+        return std::max(1, std::min(s, max_split));
+    }
+
+    bool ready(std::string& missing) const {
+        if (!have_embd) { missing = "token_embd.weight"; return false; }
+        if (!have_out && embd.rows != V) { missing = "output.weight"; return false; }
+        if (!have_onorm) { missing = "output_norm.weight"; return false; }
+        for (int l = 0; l < L; ++l) {
+            if ((layers[l].have & H_ALL) != H_ALL) {
+                static const char* nm[] = {"attn_norm", "attn_q", "attn_k", "attn_v", "attn_output",
+                                           "ffn_norm", "ffn_gate", "ffn_up", "ffn_down"};
+                for (int b = 0; b < 9; ++b)
+                    if (!(layers[l].have & (1u << b))) { missing = "blk." + std::to_string(l) + "." + nm[b] + ".weight"; break; }
+                return false;
+            }
+        }
+        return true;
+    }
+
+    const Mat& lm_head() const { return have_out ? lm : embd; }
+
+    // Enqueue one step. `timer` (nullable) records events around launches for profiling.
+    struct Timer {
+        std::vector<std::pair<std::string, std::pair<cudaEvent_t, cudaEvent_t>>> ev;
+        std::vector<double> bytes;
+    };
+
+    int enqueue(int nseq, int mode, cudaStream_t s, Timer* timer) {
+        const bool full = mode != MODE_PREFILL;
+        const bool pdl = use_pdl && !timer;
+        auto t_begin = [&](const char* name, double b) {
+            if (!timer) return;
+            cudaEvent_t e0, e1;
+            cudaEventCreate(&e0);
+            cudaEventCreate(&e1);
+            cudaEventRecord(e0, s);
+            timer->ev.push_back({name, {e0, e1}});
+            timer->bytes.push_back(b);
+        };
+        auto t_end = [&]() {
+            if (timer) cudaEventRecord(timer->ev.back().second.second, s);
+        };
+        if (mode != MODE_CHAIN) {  // a chained step reads the ids the previous step sampled
+            CK(cudaMemcpyAsync(d_tokens, h_tokens, nseq * sizeof(unsigned), cudaMemcpyHostToDevice, s));
+            CK(cudaMemcpyAsync(d_slots, h_slots, nseq * sizeof(int), cudaMemcpyHostToDevice, s));
+            if (full) CK(cudaMemcpyAsync(d_params, h_params, nseq * sizeof(laic::SampleDev), cudaMemcpyHostToDevice, s));
+        }
+
+        laic::EmbedParams ep{embd.type, embd.w, embd.d, h, embd.nb, d_tokens, d_slots, x, counts, V};
+        t_begin("embed", 0);
+        CK(launch_k(laic::embed_kernel, dim3(nseq), dim3(256), 0, s, pdl, ep));
+        t_end();
+
+        const int nsplit = nsplit_for(nseq);
+        last_split = nsplit;
+        AttnFn afn = attn_pick(D, G, kv32);
+        const size_t kvb = kv32 ? 4 : 2;
+        double attn_bytes = 0;
+        if (timer)
+            for (int i = 0; i < nseq; ++i)
+                attn_bytes += (double)(h_pos[h_slots[i]] + 1) * Hkv * D * 2 * kvb + 8.0 * h;
+
+        for (int l = 0; l < L; ++l) {
+            Layer& ly = layers[l];
+            laic::MatvecParams p{};
+            p.nseq = nseq;
+            p.eps = a.rms_eps;
+            // qkv
+            p.x = x; p.ldx = h; p.norm_w = ly.attn_norm; p.out = q; p.ldo = h;
+            p.q_rows = h; p.kv_rows = kv; p.head_dim = D; p.rope_pairs = rope_pairs; p.rope_cs = rope_cs;
+            p.slots = d_slots; p.pos = pos;
+            p.kc = (char*)kc + (size_t)l * kv_layer_stride * kvb;
+            p.vc = (char*)vc + (size_t)l * kv_layer_stride * kvb;
+            p.kv_slot_stride = kv_slot_stride; p.kv_cap = cap;
+            t_begin("qkv", (double)ly.qkv.bytes() + 4.0 * nseq * (h + ly.qkv.rows));
+            CK(launch_matvec(ly.qkv, p, laic::EPI_QKV, kv32, s, pdl));
+            t_end();
+            // attention
+            laic::AttnParams ap{};
+            ap.q = q; ap.ldq = h; ap.out = attn; ap.ldo = h;
+            ap.kc = p.kc; ap.vc = p.vc; ap.slot_stride = kv_slot_stride; ap.cap = cap;
+            ap.heads = H; ap.kv_heads = Hkv; ap.slots = d_slots; ap.pos = pos; ap.nsplit = nsplit;
+            ap.part = attn_part; ap.counters = attn_cnt; ap.sqrt_d = sqrtf((float)D);
+            t_begin("attention", attn_bytes);
+            CK(launch_k(afn, dim3(nsplit, Hkv, nseq), dim3(laic::kAttnWarps * 32), 0, s, pdl, ap));
+            t_end();
+            // o + residual
+            laic::MatvecParams po{};
+            po.nseq = nseq; po.x = attn; po.ldx = h; po.out = x; po.ldo = h;
+            t_begin("o", (double)ly.o.bytes() + 12.0 * nseq * h);
+            CK(launch_matvec(ly.o, po, laic::EPI_ADD, kv32, s, pdl));
+            t_end();
+            // gate/up + swiglu
+            laic::MatvecParams pg{};
+            pg.nseq = nseq; pg.eps = a.rms_eps; pg.x = x; pg.ldx = h; pg.norm_w = ly.ffn_norm; pg.out = act; pg.ldo = F;
+            t_begin("gate_up", (double)ly.gu.bytes() + 4.0 * nseq * (h + F));
+            CK(launch_matvec(ly.gu, pg, laic::EPI_SWIGLU, kv32, s, pdl));
+            t_end();
+            // down + residual
+            laic::MatvecParams pd{};
+            pd.nseq = nseq; pd.x = act; pd.ldx = F; pd.out = x; pd.ldo = h;
+            t_begin("down", (double)ly.down.bytes() + 4.0 * nseq * (F + 2 * h));
+            CK(launch_matvec(ly.down, pd, laic::EPI_ADD, kv32, s, pdl));
+            t_end();
+        }
+        if (full) {
+            laic::MatvecParams pl{};
+            pl.nseq = nseq; pl.eps = a.rms_eps; pl.x = x; pl.ldx = h; pl.norm_w = out_norm; pl.out = logits; pl.ldo = V;
+            t_begin("lm_head", (double)lm_head().bytes() + 4.0 * nseq * (h + V));
+            CK(launch_matvec(lm_head(), pl, laic::EPI_STORE, kv32, s, pdl));
+            t_end();
+            laic::SamplerParams sp{logits, V, V, d_slots, counts, d_params, nseq, d_out_ids, d_tokens, pos, d_err};
+            t_begin("sampler", (double)nseq * V * 4);
+            CK(launch_k(laic::sample_kernel, dim3(nseq), dim3(laic::kSampleThreads), 0, s, pdl, sp));
+            t_end();
+            if (mode == MODE_CHAIN)
+                CK(launch_k(laic::record_ids_kernel, dim3(1), dim3(256), 0, s, pdl, (const unsigned*)d_out_ids, d_hist,
+                            d_hist_count, nseq));
+            else
+                CK(cudaMemcpyAsync(h_out_ids, d_out_ids, nseq * sizeof(unsigned), cudaMemcpyDeviceToHost, s));
+        } else {
+            t_begin("advance", 0);
+            CK(launch_k(laic::advance_pos_kernel, dim3(1), dim3(256), 0, s, pdl, (const int*)d_slots, pos, nseq));
+            t_end();
+        }
+        return LAIC_OK;
+    }
+
+    int run(int nseq, int mode) {
+        if (!use_graph) return enqueue(nseq, mode, st, nullptr);
+        auto key = std::make_pair(nseq, mode);
+        auto it = graphs.find(key);
+        if (it == graphs.end()) {
+            cudaGraph_t g = nullptr;
+            CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+            int rc = enqueue(nseq, mode, st, nullptr);
+            cudaError_t ce = cudaStreamEndCapture(st, &g);
+            if (rc) { if (g) cudaGraphDestroy(g); return rc; }
+            if (ce != cudaSuccess) return fail(LAIC_E_CUDA, std::string("graph capture: ") + cudaGetErrorString(ce));
+            cudaGraphExec_t ex = nullptr;
+            ce = cudaGraphInstantiate(&ex, g, 0);
+            cudaGraphDestroy(g);
+            if (ce != cudaSuccess) return fail(LAIC_E_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(ce));
+            it = graphs.emplace(key, ex).first;
+        }
+        CK(cudaGraphLaunch(it->second, st));
+        return LAIC_OK;
+    }
+
+    int check_batch(int nseq, const uint32_t* tokens, const int32_t* slots) {
+        if (nseq <= 0 || nseq > S) return fail(LAIC_E_INVALID, "nseq must be in [1, max_seqs]");
+        if (!tokens || !slots) return fail(LAIC_E_INVALID, "null tokens or slots");
+        std::string missing;
+        if (!ready(missing)) return fail(LAIC_E_MISSING, "missing tensor: " + missing);
+        std::vector<char> seen(S, 0);
+        for (int i = 0; i < nseq; ++i) {
+            if (slots[i] < 0 || slots[i] >= S) return fail(LAIC_E_INVALID, "slot out of range");
+            if (seen[slots[i]]) return fail(LAIC_E_INVALID, "slot listed twice in one step");
+            seen[slots[i]] = 1;
+            if (tokens[i] >= (uint32_t)V || tokens[i] >= (uint32_t)embd.rows) return fail(LAIC_E_INVALID, "invalid embedding tensor");
+            if (h_pos[slots[i]] >= cap) return fail(LAIC_E_CONTEXT, "context length exceeded");
+        }
+        return LAIC_OK;
+    }
+};
+
+namespace {
+
+int parse_layer(const std::string& name, int& layer, std::string& part) {
+    if (name.rfind("blk.", 0) != 0) return 0;
+    size_t dot = name.find('.', 4);
+    if (dot == std::string::npos) return 0;
+    try { layer = std::stoi(name.substr(4, dot - 4)); } catch (...) { return 0; }
+    std::string rest = name.substr(dot + 1);
+    const std::string suf = ".weight";
+    if (rest.size() <= suf.size() || rest.compare(rest.size() - suf.size(), suf.size(), suf) != 0) return 0;
+    part = rest.substr(0, rest.size() - suf.size());
+    return 1;
+}
+
+int upload_norm(float** dst, int type, const void* data, size_t n, size_t nbytes) {
+    if (type != T_F32 && type != T_F16) return fail(LAIC_E_UNSUPPORTED, "norm weights must be F32 or F16");
+    if (nbytes < elem_bytes(type, n)) return fail(LAIC_E_INVALID, "tensor data out of range");
+    std::vector<float> v(n);
+    if (type == T_F32) std::memcpy(v.data(), data, n * 4);
+    else {
+        const uint16_t* hsrc = (const uint16_t*)data;
+        for (size_t i = 0; i < n; ++i) {
+            __half_raw r; r.x = hsrc[i];
+            v[i] = __half2float(__half(r));
+        }
+    }
+    if (!*dst) CK(cudaMalloc(dst, n * 4));
+    CK(cudaMemcpy(*dst, v.data(), n * 4, cudaMemcpyHostToDevice));
+    return LAIC_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* laic_last_error(void) { return g_err.c_str(); }
+
+int laic_dev_create(const laic_dev_desc* desc, const laic_dev_opts* opts, laic_dev** out) {
+    if (!desc || !out) return fail(LAIC_E_INVALID, "null argument");
+    *out = nullptr;
+    laic_dev_opts o{};
+    o.max_seqs = 1; o.tp_size = 1;
+    if (opts) o = *opts;
+    if (o.tp_size > 1) return fail(LAIC_E_UNSUPPORTED, "tensor parallelism is not built into this library yet");
+    const laic_dev_desc& a = *desc;
+    if (!a.hidden || !a.layers || !a.heads || !a.kv_heads || a.hidden % a.heads || a.heads % a.kv_heads || !a.ffn || !a.vocab)
+        return fail(LAIC_E_INVALID, "invalid llama architecture metadata");
+    const uint32_t D = a.hidden / a.heads;
+    const uint32_t rd = a.rope_dim ? a.rope_dim : D;
+    if (!rd || rd > D || (rd & 1)) return fail(LAIC_E_INVALID, "invalid RoPE dimension");
+    if (D != 32 && D != 64 && D != 128) return fail(LAIC_E_UNSUPPORTED, "head_dim must be 32, 64 or 128");
+    if (a.heads / a.kv_heads > 8) return fail(LAIC_E_UNSUPPORTED, "at most 8 query heads per kv head");
+    if (a.hidden % 32 || a.ffn % 32) return fail(LAIC_E_UNSUPPORTED, "hidden and ffn must be multiples of 32");
+    if (o.max_seqs < 1) return fail(LAIC_E_INVALID, "max_seqs must be >= 1");
+    const uint32_t ctx = a.ctx ? a.ctx : 2048;
+    int cap = o.kv_capacity > 0 ? std::min<int>(o.kv_capacity, (int)ctx) : (int)ctx;
+
+    CK(cudaSetDevice(o.device));
+    std::unique_ptr<laic_dev> d(new laic_dev());
+    d->a = a; d->a.ctx = ctx; d->a.rope_dim = rd;
+    d->o = o; d->device = o.device;
+    d->H = a.heads; d->Hkv = a.kv_heads; d->D = D; d->G = a.heads / a.kv_heads; d->h = a.hidden;
+    d->kv = a.kv_heads * D; d->F = a.ffn; d->V = a.vocab; d->L = a.layers; d->S = o.max_seqs; d->cap = cap;
+    d->rope_pairs = rd / 2;
+    d->kv32 = (o.flags & LAIC_FLAG_KV_F32) != 0;
+    d->use_graph = !(o.flags & LAIC_FLAG_NO_GRAPH);
+    d->use_pdl = !(o.flags & LAIC_FLAG_NO_PDL);
+    d->layers.resize(a.layers);
+    d->h_pos.assign(o.max_seqs, 0);
+    CK(cudaStreamCreateWithFlags(&d->st, cudaStreamNonBlocking));
+    // set kernel attributes now: graph capture must not see attribute calls
+    for (int t : {T_F16, T_Q4_0, T_Q8_0})
+        for (int ns : {1, 2})
+            for (int e : {laic::EPI_STORE, laic::EPI_ADD, laic::EPI_SWIGLU, laic::EPI_QKV}) mv_pick(t, ns, e, d->kv32);
+
+    const size_t S = o.max_seqs, kvb = d->kv32 ? 4 : 2;
+    CK(cudaMalloc(&d->x, S * d->h * 4));
+    CK(cudaMalloc(&d->q, S * d->h * 4));
+    CK(cudaMalloc(&d->attn, S * d->h * 4));
+    CK(cudaMalloc(&d->act, S * d->F * 4));
+    CK(cudaMalloc(&d->logits, S * d->V * 4));
+    d->kv_slot_stride = (long long)d->Hkv * cap * D;
+    d->kv_layer_stride = d->kv_slot_stride * (long long)S;
+    const size_t kv_bytes = (size_t)d->kv_layer_stride * d->L * kvb;
+    CK(cudaMalloc(&d->kc, kv_bytes));
+    CK(cudaMalloc(&d->vc, kv_bytes));
+    CK(cudaMemset(d->kc, 0, kv_bytes));
+    CK(cudaMemset(d->vc, 0, kv_bytes));
+    CK(cudaMalloc(&d->pos, S * 4));
+    CK(cudaMemset(d->pos, 0, S * 4));
+    CK(cudaMalloc(&d->counts, S * d->V * 4));
+    CK(cudaMemset(d->counts, 0, S * d->V * 4));
+
+    // RoPE table with the reference's float arithmetic (src/inference_v2.cpp:25):
+    // a = float(pos) * pow(theta, -float(i)/float(head_dim)), (cos a, sin a)
+    std::vector<float2> cs((size_t)cap * d->rope_pairs);
+    const float theta = a.rope_theta > 0 ? a.rope_theta : 10000.f;
+    for (int p = 0; p < cap; ++p)
+        for (int j = 0; j < d->rope_pairs; ++j) {
+            const int i = 2 * j;
+            const float ang = float(p) * std::pow(theta, -float(i) / float(D));
+            cs[(size_t)p * d->rope_pairs + j] = make_float2(std::cos(ang), std::sin(ang));
+        }
+    CK(cudaMalloc(&d->rope_cs, std::max<size_t>(1, cs.size()) * sizeof(float2)));
+    if (!cs.empty()) CK(cudaMemcpy(d->rope_cs, cs.data(), cs.size() * sizeof(float2), cudaMemcpyHostToDevice));
+
+    d->max_split = std::max(1, std::min(64, (cap + 31) / 32));
+    CK(cudaMalloc(&d->attn_part, S * d->Hkv * d->max_split * d->G * (D + 2) * 4));
+    CK(cudaMalloc(&d->attn_cnt, S * d->Hkv * 4));
+    CK(cudaMemset(d->attn_cnt, 0, S * d->Hkv * 4));
+
+    CK(cudaMalloc(&d->d_tokens, S * 4));
+    CK(cudaMalloc(&d->d_out_ids, S * 4));
+    CK(cudaMalloc(&d->d_slots, S * 4));
+    CK(cudaMalloc(&d->d_err, 4));
+    CK(cudaMemset(d->d_err, 0, 4));
+    CK(cudaMalloc(&d->d_hist_count, 4));
+    CK(cudaMalloc(&d->d_params, S * sizeof(laic::SampleDev)));
+    CK(cudaMallocHost(&d->h_tokens, S * 4));
+    CK(cudaMallocHost(&d->h_out_ids, S * 4));
+    CK(cudaMallocHost(&d->h_slots, S * 4));
+    CK(cudaMallocHost(&d->h_params, S * sizeof(laic::SampleDev)));
+    CK(cudaDeviceSynchronize());
+    *out = d.release();
+    return LAIC_OK;
+}
+
+void laic_dev_destroy(laic_dev* d) {
+    if (!d) return;
+    cudaSetDevice(d->device);
+    cudaStreamSynchronize(d->st);
+    for (auto& kv : d->graphs) cudaGraphExecDestroy(kv.second);
+    for (auto& l : d->layers) {
+        mat_free(l.qkv); mat_free(l.o); mat_free(l.gu); mat_free(l.down);
+        if (l.attn_norm) cudaFree(l.attn_norm);
+        if (l.ffn_norm) cudaFree(l.ffn_norm);
+    }
+    mat_free(d->embd); mat_free(d->lm);
+    void* bufs[] = {d->out_norm, d->x, d->q, d->attn, d->act, d->logits, d->kc, d->vc, d->pos, d->counts,
+                    d->rope_cs, d->attn_part, d->attn_cnt, d->d_tokens, d->d_out_ids, d->d_slots, d->d_err, d->d_params,
+                    d->d_hist, d->d_hist_count};
+    for (void* b : bufs) if (b) cudaFree(b);
+    void* hb[] = {d->h_tokens, d->h_out_ids, d->h_slots, d->h_params};
+    for (void* b : hb) if (b) cudaFreeHost(b);
+    if (d->st) cudaStreamDestroy(d->st);
+    delete d;
+}
+
+int laic_dev_upload(laic_dev* d, const char* cname, int32_t type, const uint64_t* shape, int32_t ndim,
+                    const void* data, size_t nbytes) {
+    if (!d || !cname || !shape || !data) return fail(LAIC_E_INVALID, "null argument");
+    CK(cudaSetDevice(d->device));
+    const std::string name(cname);
+    size_t n = 1;
+    for (int i = 0; i < ndim; ++i) n *= shape[i];
+    if (nbytes < elem_bytes(type, n)) return fail(LAIC_E_INVALID, "tensor data out of range: " + name);
+    auto shape_is = [&](uint64_t in, uint64_t out) { return ndim == 2 && shape[0] == in && shape[1] == out; };
+    // any graph captured before this upload points at old buffers
+    for (auto& kv : d->graphs) cudaGraphExecDestroy(kv.second);
+    d->graphs.clear();
+
+    if (name == "output_norm.weight") {
+        if (n != (size_t)d->h) return fail(LAIC_E_INVALID, "invalid norm tensor: " + name);
+        int rc = upload_norm(&d->out_norm, type, data, n, nbytes);
+        if (!rc) d->have_onorm = true;
+        return rc;
+    }
+    if (name == "token_embd.weight" || name == "output.weight") {
+        const bool is_embd = name == "token_embd.weight";
+        if (ndim != 2 || shape[0] != (uint64_t)d->h) return fail(LAIC_E_INVALID, "unexpected weight shape: " + name);
+        if (!is_embd && shape[1] != (uint64_t)d->V) return fail(LAIC_E_INVALID, "unexpected weight shape: " + name);
+        Mat& m = is_embd ? d->embd : d->lm;
+        mat_free(m);
+        int rc = mat_alloc(m, type, (int)shape[1], d->h);
+        if (rc) return rc;
+        rc = mat_fill(m, (const uint8_t*)data, (int)shape[1], 1, 0, d->st);
+        if (rc) return rc;
+        if (is_embd) d->have_embd = true; else d->have_out = true;
+        return LAIC_OK;
+    }
+    int l;
+    std::string part;
+    if (!parse_layer(name, l, part) || l < 0 || l >= d->L) return LAIC_OK;  // not used by the decode path
+    Layer& ly = d->layers[l];
+    const int h = d->h, kv = d->kv, F = d->F;
+    auto ensure = [&](Mat& m, int rows, int in) -> int {
+        if (m.w && m.type != type) return fail(LAIC_E_UNSUPPORTED, "fused projections need one type: " + name);
+        if (!m.w) return mat_alloc(m, type, rows, in);
+        return LAIC_OK;
+    };
+    int rc = LAIC_OK;
+    if (part == "attn_norm" || part == "ffn_norm") {
+        if (n != (size_t)h) return fail(LAIC_E_INVALID, "invalid norm tensor: " + name);
+        const bool an = part == "attn_norm";
+        rc = upload_norm(an ? &ly.attn_norm : &ly.ffn_norm, type, data, n, nbytes);
+        if (!rc) ly.have |= an ? H_ANORM : H_FNORM;
+    } else if (part == "attn_q" || part == "attn_k" || part == "attn_v") {
+        const int out = part == "attn_q" ? h : kv;
+        if (!shape_is(h, out)) return fail(LAIC_E_INVALID, "unexpected weight shape: " + name);
+        if ((rc = ensure(ly.qkv, h + 2 * kv, h))) return rc;
+        const long long off = part == "attn_q" ? 0 : part == "attn_k" ? h : h + kv;
+        rc = mat_fill(ly.qkv, (const uint8_t*)data, out, 1, off, d->st);
+        if (!rc) ly.have |= part == "attn_q" ? H_Q : part == "attn_k" ? H_K : H_V;
+    } else if (part == "attn_output") {
+        if (!shape_is(h, h)) return fail(LAIC_E_INVALID, "unexpected weight shape: " + name);
+        if ((rc = ensure(ly.o, h, h))) return rc;
+        rc = mat_fill(ly.o, (const uint8_t*)data, h, 1, 0, d->st);
+        if (!rc) ly.have |= H_O;
+    } else if (part == "ffn_gate" || part == "ffn_up") {
+        if (!shape_is(h, F)) return fail(LAIC_E_INVALID, "unexpected weight shape: " + name);
+        if ((rc = ensure(ly.gu, 2 * F, h))) return rc;
+        rc = mat_fill(ly.gu, (const uint8_t*)data, F, 2, part == "ffn_gate" ? 0 : 1, d->st);
+        if (!rc) ly.have |= part == "ffn_gate" ? H_GATE : H_UP;
+    } else if (part == "ffn_down") {
+        if (!shape_is(F, h)) return fail(LAIC_E_INVALID, "unexpected weight shape: " + name);
+        if ((rc = ensure(ly.down, h, F))) return rc;
+        rc = mat_fill(ly.down, (const uint8_t*)data, h, 1, 0, d->st);
+        if (!rc) ly.have |= H_DOWN;
+    }
+    return rc;
+}
+
+static int fill_inputs(laic_dev* d, int32_t nseq, const uint32_t* tokens, const int32_t* slots) {
+    int rc = d->check_batch(nseq, tokens, slots);
+    if (rc) return rc;
+    std::memcpy(d->h_tokens, tokens, nseq * 4);
+    std::memcpy(d->h_slots, slots, nseq * 4);
+    return LAIC_OK;
+}
+
+int laic_dev_prefill(laic_dev* d, int32_t nseq, const uint32_t* tokens, const int32_t* slots) {
+    if (!d) return fail(LAIC_E_INVALID, "null device");
+    CK(cudaSetDevice(d->device));
+    int rc = fill_inputs(d, nseq, tokens, slots);
+    if (rc) return rc;
+    if ((rc = d->run(nseq, MODE_PREFILL))) return rc;
+    CK(cudaStreamSynchronize(d->st));
+    for (int i = 0; i < nseq; ++i) d->h_pos[slots[i]] += 1;
+    return LAIC_OK;
+}
+
+static double canonical_draw(uint64_t seed) {
+    std::mt19937_64 rng(seed ? seed : std::random_device{}());
+    return std::generate_canonical<double, std::numeric_limits<double>::digits>(rng);
+}
+
+static int fill_params(laic_dev* d, int32_t nseq, const laic_sample_params* params, int32_t nparams) {
+    laic_sample_params greedy{0.f, 0, 1.f, 1.f, 0};
+    if (!params) { params = &greedy; nparams = 1; }
+    if (nparams != 1 && nparams != nseq) return fail(LAIC_E_INVALID, "nparams must be 1 or nseq");
+    for (int i = 0; i < nseq; ++i) {
+        const laic_sample_params& sp = params[nparams == 1 ? 0 : i];
+        laic::SampleDev& o = d->h_params[i];
+        o.temperature = sp.temperature; o.top_k = sp.top_k; o.top_p = sp.top_p; o.repeat_penalty = sp.repeat_penalty;
+        // the reference re-seeds mt19937_64 on every sample() call: one canonical draw per call
+        o.u = sp.temperature > 0.f ? canonical_draw(sp.seed) : 0.0;
+    }
+    return LAIC_OK;
+}
+
+static int check_sampler_err(laic_dev* d) {
+    int err = 0;
+    CK(cudaMemcpy(&err, d->d_err, 4, cudaMemcpyDeviceToHost));
+    if (err) {
+        CK(cudaMemset(d->d_err, 0, 4));
+        return fail(LAIC_E_UNSUPPORTED, "sampling request needs more than 1024 candidates (top_k or top_p mass)");
+    }
+    return LAIC_OK;
+}
+
+int laic_dev_step(laic_dev* d, int32_t nseq, const uint32_t* tokens, const int32_t* slots,
+                  const laic_sample_params* params, int32_t nparams, uint32_t* out_ids, float* out_logits) {
+    if (!d) return fail(LAIC_E_INVALID, "null device");
+    CK(cudaSetDevice(d->device));
+    int rc = fill_inputs(d, nseq, tokens, slots);
+    if (rc) return rc;
+    if ((rc = fill_params(d, nseq, params, nparams))) return rc;
+    if ((rc = d->run(nseq, MODE_STEP))) return rc;
+    if (out_logits)
+        CK(cudaMemcpyAsync(out_logits, d->logits, (size_t)nseq * d->V * 4, cudaMemcpyDeviceToHost, d->st));
+    CK(cudaStreamSynchronize(d->st));
+    for (int i = 0; i < nseq; ++i) d->h_pos[slots[i]] += 1;
+    if ((rc = check_sampler_err(d))) return rc;
+    if (out_ids) std::memcpy(out_ids, d->h_out_ids, nseq * 4);
+    return LAIC_OK;
+}
+
+int laic_dev_reset_slot(laic_dev* d, int32_t slot) {
+    if (!d || slot < 0 || slot >= d->S) return fail(LAIC_E_INVALID, "slot out of range");
+    CK(cudaSetDevice(d->device));
+    CK(cudaStreamSynchronize(d->st));
+    CK(cudaMemset(d->pos + slot, 0, 4));
+    CK(cudaMemset(d->counts + (size_t)slot * d->V, 0, (size_t)d->V * 4));
+    d->h_pos[slot] = 0;
+    return LAIC_OK;
+}
+
+int laic_dev_slot_pos(laic_dev* d, int32_t slot, int64_t* pos) {
+    if (!d || !pos || slot < 0 || slot >= d->S) return fail(LAIC_E_INVALID, "slot out of range");
+    *pos = d->h_pos[slot];
+    return LAIC_OK;
+}
+
+int laic_dev_fill_kv(laic_dev* d, int32_t slot, int32_t npos, uint64_t seed) {
+    if (!d || slot < 0 || slot >= d->S) return fail(LAIC_E_INVALID, "slot out of range");
+    if (npos < 0 || npos > d->cap) return fail(LAIC_E_CONTEXT, "context length exceeded");
+    CK(cudaSetDevice(d->device));
+    if (npos > 0) {
+        const long long slot_off = (long long)slot * d->kv_slot_stride;
+        if (d->kv32)
+            laic::fill_kv_kernel<float><<<1184, 256, 0, d->st>>>((float*)d->kc, (float*)d->vc, d->kv_layer_stride, slot_off,
+                                                               d->Hkv, d->cap, d->D, npos, d->L, seed);
+        else
+            laic::fill_kv_kernel<__half><<<1184, 256, 0, d->st>>>((__half*)d->kc, (__half*)d->vc, d->kv_layer_stride,
+                                                                slot_off, d->Hkv, d->cap, d->D, npos, d->L, seed);
+        CK(cudaGetLastError());
+    }
+    CK(cudaMemcpyAsync(d->pos + slot, &npos, 4, cudaMemcpyHostToDevice, d->st));
+    CK(cudaStreamSynchronize(d->st));
+    d->h_pos[slot] = npos;
+    return LAIC_OK;
+}
+
+int laic_dev_sync(laic_dev* d) {
+    if (!d) return fail(LAIC_E_INVALID, "null device");
+    CK(cudaSetDevice(d->device));
+    CK(cudaStreamSynchronize(d->st));
+    return LAIC_OK;
+}
+
+void* laic_dev_stream(laic_dev* d) { return d ? (void*)d->st : nullptr; }
+
+int laic_dev_stats_get(laic_dev* d, laic_dev_stats* s) {
+    if (!d || !s) return fail(LAIC_E_INVALID, "null argument");
+    std::memset(s, 0, sizeof *s);
+    uint64_t wb = 0;
+    for (auto& l : d->layers) wb += l.qkv.bytes() + l.o.bytes() + l.gu.bytes() + l.down.bytes() + 8ull * d->h;
+    wb += d->lm_head().bytes() + 4ull * d->h;
+    s->weight_bytes = wb;
+    s->kv_bytes_per_pos = (uint64_t)d->L * d->kv * 2 * (d->kv32 ? 4 : 2);
+    s->launches_per_step = 1 + 5 * d->L + 2;  // embed, 5 per layer, lm_head, sampler
+    s->launches_per_prefill = 1 + 5 * d->L + 1;
+    s->attn_splits = d->last_split;
+    s->tp_size = 1;
+    return LAIC_OK;
+}
+
+int laic_dev_decode(laic_dev* d, int32_t nseq, const uint32_t* tokens, const int32_t* slots,
+                    const laic_sample_params* params, int32_t nparams, int32_t steps, uint32_t* out_ids,
+                    double* device_ms) {
+    if (!d) return fail(LAIC_E_INVALID, "null device");
+    if (steps < 1 || !out_ids) return fail(LAIC_E_INVALID, "steps must be >= 1 and out_ids non-null");
+    CK(cudaSetDevice(d->device));
+    int rc = fill_inputs(d, nseq, tokens, slots);
+    if (rc) return rc;
+    for (int i = 0; i < nseq; ++i)
+        if (d->h_pos[slots[i]] + steps > d->cap) return fail(LAIC_E_CONTEXT, "context length exceeded");
+    if ((rc = fill_params(d, nseq, params, nparams))) return rc;
+    const size_t need = (size_t)steps * nseq;
+    if (need > d->hist_cap) {
+        if (d->d_hist) cudaFree(d->d_hist);
+        d->d_hist = nullptr;
+        d->hist_cap = 0;
+        CK(cudaMalloc(&d->d_hist, need * sizeof(unsigned)));
+        d->hist_cap = need;
+        for (auto& kv : d->graphs) cudaGraphExecDestroy(kv.second);  // they captured the old buffer
+        d->graphs.clear();
+    }
+    CK(cudaMemcpyAsync(d->d_tokens, d->h_tokens, nseq * 4, cudaMemcpyHostToDevice, d->st));
+    CK(cudaMemcpyAsync(d->d_slots, d->h_slots, nseq * 4, cudaMemcpyHostToDevice, d->st));
+    CK(cudaMemcpyAsync(d->d_params, d->h_params, nseq * sizeof(laic::SampleDev), cudaMemcpyHostToDevice, d->st));
+    CK(cudaMemsetAsync(d->d_hist_count, 0, 4, d->st));
+    cudaEvent_t e0, e1;
+    CK(cudaEventCreate(&e0));
+    CK(cudaEventCreate(&e1));
+    CK(cudaEventRecord(e0, d->st));
+    for (int k = 0; k < steps && rc == LAIC_OK; ++k) rc = d->run(nseq, MODE_CHAIN);
+    CK(cudaEventRecord(e1, d->st));
+    CK(cudaStreamSynchronize(d->st));
+    float ms = 0;
+    cudaEventElapsedTime(&ms, e0, e1);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (rc) return rc;
+    for (int i = 0; i < nseq; ++i) d->h_pos[slots[i]] += steps;
+    if (device_ms) *device_ms = ms;
+    CK(cudaMemcpy(out_ids, d->d_hist, need * sizeof(unsigned), cudaMemcpyDeviceToHost));
+    return check_sampler_err(d);
+}
+
+int laic_dev_profile(laic_dev* d, int32_t nseq, const uint32_t* tokens, int32_t steps, laic_kernel_record* out,
+                     int32_t max_out, int32_t* n_out) {
+    if (!d || !tokens || steps < 1 || !out || !n_out) return fail(LAIC_E_INVALID, "bad argument");
+    CK(cudaSetDevice(d->device));
+    std::vector<int32_t> slots(nseq);
+    for (int i = 0; i < nseq; ++i) slots[i] = i;
+    std::vector<laic_kernel_record> recs;
+    for (int it = 0; it < steps; ++it) {
+        int rc = fill_inputs(d, nseq, tokens + (size_t)it * nseq, slots.data());
+        if (rc) return rc;
+        if ((rc = fill_params(d, nseq, nullptr, 0))) return rc;
+        laic_dev::Timer t;
+        rc = d->enqueue(nseq, MODE_STEP, d->st, &t);
+        CK(cudaStreamSynchronize(d->st));
+        for (int i = 0; i < nseq; ++i) d->h_pos[i] += 1;
+        for (size_t k = 0; k < t.ev.size(); ++k) {
+            float ms = 0;
+            cudaEventElapsedTime(&ms, t.ev[k].second.first, t.ev[k].second.second);
+            cudaEventDestroy(t.ev[k].second.first);
+            cudaEventDestroy(t.ev[k].second.second);
+            auto it2 = std::find_if(recs.begin(), recs.end(),
+                                    [&](const laic_kernel_record& r) { return t.ev[k].first == r.name; });
+            if (it2 == recs.end()) {
+                laic_kernel_record r{};
+                std::snprintf(r.name, sizeof r.name, "%s", t.ev[k].first.c_str());
+                recs.push_back(r);
+                it2 = recs.end() - 1;
+            }
+            it2->launches += 1;
+            it2->total_us += ms * 1000.0;
+            it2->bytes += t.bytes[k];
+        }
+        if (rc) return rc;
+    }
+    *n_out = std::min<int32_t>(max_out, (int32_t)recs.size());
+    for (int i = 0; i < *n_out; ++i) out[i] = recs[i];
+    return LAIC_OK;
+}
+
+int laic_nccl_unique_id(void* out128) {
+    (void)out128;
+    return fail(LAIC_E_UNSUPPORTED, "tensor parallelism is not built into this library yet");
+}
+
+// ---- single tensors --------------------------------------------------------
+}  // extern "C"
+
+struct laic_tensor {
+    int device = 0;
+    Mat m;
+};
+
+extern "C" {
+
+int laic_tensor_create(int32_t device, int32_t type, uint64_t in, uint64_t out, const void* data, size_t nbytes,
+                       laic_tensor** t) {
+    if (!data || !t || !in || !out) return fail(LAIC_E_INVALID, "bad argument");
+    if (nbytes < elem_bytes(type, in * out)) return fail(LAIC_E_INVALID, "tensor data out of range");
+    CK(cudaSetDevice(device));
+    std::unique_ptr<laic_tensor> x(new laic_tensor());
+    x->device = device;
+    int rc = mat_alloc(x->m, type, (int)out, (int)in);
+    if (rc) return rc;
+    cudaStream_t st;
+    CK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+    rc = mat_fill(x->m, (const uint8_t*)data, (int)out, 1, 0, st);
+    cudaStreamDestroy(st);
+    if (rc) { mat_free(x->m); return rc; }
+    *t = x.release();
+    return LAIC_OK;
+}
+
+void laic_tensor_destroy(laic_tensor* t) {
+    if (!t) return;
+    cudaSetDevice(t->device);
+    mat_free(t->m);
+    delete t;
+}
+
+uint64_t laic_tensor_bytes(laic_tensor* t) { return t ? t->m.bytes() : 0; }
+
+int laic_tensor_matvec(laic_tensor* t, const float* x, float* y, int32_t batch, void* stream) {
+    if (!t || !x || !y || batch < 1) return fail(LAIC_E_INVALID, "bad argument");
+    CK(cudaSetDevice(t->device));
+    laic::MatvecParams p{};
+    p.nseq = batch; p.x = x; p.ldx = t->m.in; p.out = y; p.ldo = t->m.rows;
+    CK(launch_matvec(t->m, p, laic::EPI_STORE, false, (cudaStream_t)stream, false));
+    return LAIC_OK;
+}
+
+int laic_tensor_dequant(laic_tensor* t, float* out, void* stream) {
+    if (!t || !out) return fail(LAIC_E_INVALID, "bad argument");
+    CK(cudaSetDevice(t->device));
+    laic::dequant_kernel<<<1184, 256, 0, (cudaStream_t)stream>>>(t->m.type, t->m.w, t->m.d, t->m.in, t->m.nb,
+                                                                  t->m.rows, out);
+    CK(cudaGetLastError());
+    return LAIC_OK;
+}
+
+}  // extern "C"
