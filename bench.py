@@ -234,7 +234,7 @@ def main() -> None:
     if args.batch:
         batch = args.batch
     path = model_path(name, rank)
-    ctx_need = plen + 2 * args.warmup + 2 * args.steps + 2
+    ctx_need = plen + 2 * args.warmup + 2 * args.steps + 64  # decode, e2e and profiling steps
     eng = Engine(path, max_seqs=batch, device=local, kv_capacity=ctx_need)
     slots = np.arange(batch, dtype=np.int32)
     prompts = np.stack([synth.prompt_ids(arch.vocab, plen, seed=seed + 100 + 1000 * rank + i) for i in range(batch)])
