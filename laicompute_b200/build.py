@@ -13,6 +13,7 @@ import glob
 import os
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 
 PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
@@ -52,21 +53,22 @@ def build(verbose: bool = False) -> str:
     os.makedirs(os.path.dirname(LIB), exist_ok=True)
     os.makedirs(os.path.dirname(BIN), exist_ok=True)
     hdrs = _headers()
-    objs = []
+    objs, jobs = [], []
     for src in sorted(glob.glob(os.path.join(CSRC, "*.cu"))):
         obj = os.path.join(BUILD, os.path.basename(src) + ".o")
         if _stale(obj, [src, *hdrs]):
-            if verbose:
-                print("nvcc", os.path.basename(src))
-            _run([NVCC, *NVFLAGS, "-c", src, "-o", obj])
+            jobs.append(("nvcc", src, [NVCC, *NVFLAGS, "-c", src, "-o", obj]))
         objs.append(obj)
     for src in sorted(glob.glob(os.path.join(CSRC, "host", "*.cpp"))):
         obj = os.path.join(BUILD, "host_" + os.path.basename(src) + ".o")
         if _stale(obj, [src, *hdrs]):
-            if verbose:
-                print("g++", os.path.basename(src))
-            _run(["g++", *CXXFLAGS, "-c", src, "-o", obj])
+            jobs.append(("g++", src, ["g++", *CXXFLAGS, "-c", src, "-o", obj]))
         objs.append(obj)
+    for tool, src, _ in jobs:
+        if verbose:
+            print(tool, os.path.basename(src))
+    with ThreadPoolExecutor(max_workers=max(1, os.cpu_count() or 1)) as ex:
+        list(ex.map(lambda j: _run(j[2]), jobs))
     if _stale(LIB, objs):
         _run([NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lpthread"])
     tool = os.path.join(CSRC, "tools", "laic_generate.cpp")

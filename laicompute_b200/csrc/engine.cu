@@ -29,8 +29,10 @@
 
 #include "../../include/laic_b200.h"
 #include "attention.cuh"
-#include "matvec.cuh"
+#include "launch.cuh"
 #include "misc.cuh"
+#include "mma_matvec.cuh"
+#include "mv_streamk.cuh"
 #include "sampler.cuh"
 
 namespace {
@@ -63,17 +65,14 @@ size_t elem_bytes(int type, size_t n) {
     return 0;
 }
 
-// A projection matrix in the device layout of matvec.cuh.
+// A projection matrix in the fragment-tile layout of mma_matvec.cuh.
 struct Mat {
     int type = -1;
-    int rows = 0, in = 0, nb = 0;
-    void* w = nullptr;
-    unsigned short* d = nullptr;
-    size_t bytes() const {  // bytes one matvec streams
-        if (type == T_F16) return (size_t)rows * in * 2;
-        if (type == T_Q4_0) return (size_t)rows * nb * 18;
-        if (type == T_Q8_0) return (size_t)rows * nb * 34;
-        return 0;
+    int rows = 0, ntiles = 0, in = 0, nb = 0;
+    uint8_t* q = nullptr;
+    uint8_t* s = nullptr;
+    size_t bytes() const {  // GGUF bytes of the matrix: what one matvec must stream
+        return elem_bytes(type, (size_t)rows * in);
     }
 };
 
@@ -81,25 +80,26 @@ int mat_alloc(Mat& m, int type, int rows, int in) {
     if (type != T_F16 && type != T_Q4_0 && type != T_Q8_0)
         return fail(LAIC_E_UNSUPPORTED, "unsupported matrix type " + std::to_string(type) + " (F16, Q8_0, Q4_0 only)");
     if (in % 32) return fail(LAIC_E_UNSUPPORTED, "row length must be a multiple of 32");
-    m.type = type; m.rows = rows; m.in = in; m.nb = in / 32;
-    if (type == T_F16) {
-        CK(cudaMalloc(&m.w, (size_t)rows * in * 2));
-    } else {
-        const size_t qb = type == T_Q4_0 ? 16 : 32;
-        CK(cudaMalloc(&m.w, (size_t)rows * m.nb * qb));
-        CK(cudaMalloc(&m.d, (size_t)rows * m.nb * 2));
+    m.type = type; m.rows = rows; m.in = in; m.nb = in / 32; m.ntiles = (rows + 15) / 16;
+    const size_t qbytes = (size_t)m.ntiles * m.nb * laic::tile_qbytes(type);
+    CK(cudaMalloc(&m.q, qbytes));
+    CK(cudaMemset(m.q, 0, qbytes));
+    if (type != T_F16) {
+        const size_t sbytes = (size_t)m.ntiles * m.nb * laic::kTileSBytes;
+        CK(cudaMalloc(&m.s, sbytes));
+        CK(cudaMemset(m.s, 0, sbytes));
     }
     return LAIC_OK;
 }
 
 void mat_free(Mat& m) {
-    if (m.w) cudaFree(m.w);
-    if (m.d) cudaFree(m.d);
-    m.w = nullptr; m.d = nullptr;
+    if (m.q) cudaFree(m.q);
+    if (m.s) cudaFree(m.s);
+    m.q = nullptr; m.s = nullptr;
 }
 
-// Copy GGUF rows [row0, row0+nrows) (raw block bytes) into matrix rows
-// r*row_mul + row_add through a device staging buffer.
+// Copy GGUF rows (raw block bytes) into matrix rows r*row_mul + row_add
+// through a device staging buffer, repacking into fragment tiles.
 int mat_fill(Mat& m, const uint8_t* host, int nrows, int row_mul, long long row_add, cudaStream_t st) {
     const size_t row_bytes = elem_bytes(m.type, (size_t)m.in);
     const size_t chunk_rows = std::max<size_t>(1, (64u << 20) / row_bytes);
@@ -108,19 +108,11 @@ int mat_fill(Mat& m, const uint8_t* host, int nrows, int row_mul, long long row_
     for (size_t r0 = 0; r0 < (size_t)nrows; r0 += chunk_rows) {
         const size_t n = std::min(chunk_rows, (size_t)nrows - r0);
         CK(cudaMemcpyAsync(staging, host + r0 * row_bytes, n * row_bytes, cudaMemcpyHostToDevice, st));
-        const long long add = (long long)r0 * row_mul + row_add;
-        if (m.type == T_F16) {
-            const int vpr = m.in / 8;
-            laic::repack_f16_rows_kernel<<<592, 256, 0, st>>>((const uint4*)staging, (uint4*)m.w, (long long)n, vpr,
-                                                              row_mul, add);
-        } else {
-            const int bb = m.type == T_Q4_0 ? 18 : 34, qb = m.type == T_Q4_0 ? 16 : 32;
-            laic::repack_blocks_kernel<<<592, 256, 0, st>>>((const uint8_t*)staging, (uint8_t*)m.w, m.d, (long long)n,
-                                                            m.nb, bb, qb, row_mul, add);
-        }
+        laic::repack_tiles_kernel<<<1184, 256, 0, st>>>(m.type, (const uint8_t*)staging, (long long)n, m.nb, row_mul,
+                                                        (long long)r0 * row_mul + row_add, m.q, m.s);
         CK(cudaGetLastError());
+        CK(cudaStreamSynchronize(st));
     }
-    CK(cudaStreamSynchronize(st));
     cudaFree(staging);
     return LAIC_OK;
 }
@@ -128,21 +120,7 @@ int mat_fill(Mat& m, const uint8_t* host, int nrows, int row_mul, long long row_
 // ---------------------------------------------------------------------------
 // launch helpers
 // ---------------------------------------------------------------------------
-template <typename... KArgs, typename... Args>
-cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
-                     Args&&... args) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
-}
+using laic::launch_k;
 
 int g_num_sms = 0;
 int num_sms() {
@@ -155,45 +133,105 @@ int num_sms() {
     return g_num_sms;
 }
 
-using MatvecFn = void (*)(laic::MatvecParams);
+// Launch shape of one fragment-tile matvec: n-tiles, K split, ring, grid, shared memory.
+struct MvShape {
+    bool sk = false;  // team kernel (small batches whose activations fit in shared memory)
+    int nt = 1, nk = 1, kr = 1, kb = 1, stages = 2, grid = 1;
+    size_t smem = 0;
+    size_t part_floats = 0;  // split-K scratch it needs
+};
 
-template <int WT, int NS, int EPI, typename KV>
-MatvecFn mv_fn() {
-    auto f = laic::matvec_kernel<WT, NS, EPI, KV>;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        attr_set = true;
+constexpr size_t kSmemBudget = 220 * 1024;
+
+MvShape mv_shape(const Mat& m, int B) {
+    MvShape sh;
+    if (B <= 16) {
+        const size_t smem = laic::sk_smem_bytes(m.type, m.nb, B);
+        if (smem <= kSmemBudget) {
+            sh.sk = true;
+            sh.nt = B <= 4 ? 1 : B <= 8 ? 2 : 4;  // hi and lo activation columns side by side
+            sh.grid = std::max(1, std::min(num_sms(), m.ntiles));  // each CTA owns whole row tiles
+            sh.smem = smem;
+            sh.part_floats = 0;
+            return sh;
+        }
     }
-    return f;
-}
-
-template <int WT, int NS>
-MatvecFn mv_pick_epi(int epi, bool kv32) {
-    switch (epi) {
-    case laic::EPI_STORE: return mv_fn<WT, NS, laic::EPI_STORE, __half>();
-    case laic::EPI_ADD: return mv_fn<WT, NS, laic::EPI_ADD, __half>();
-    case laic::EPI_SWIGLU: return mv_fn<WT, NS, laic::EPI_SWIGLU, __half>();
-    default: return kv32 ? mv_fn<WT, NS, laic::EPI_QKV, float>() : mv_fn<WT, NS, laic::EPI_QKV, __half>();
+    sh.nt = B <= 8 ? 1 : B <= 16 ? 2 : B <= 32 ? 4 : 8;
+    sh.kb = m.type == T_F16 ? 16 : 32;
+    const size_t sbytes = m.type == T_F16 ? 0 : laic::kTileSBytes;
+    const size_t stage_bytes = (size_t)sh.kb * (laic::tile_qbytes(m.type) + sbytes);
+    const size_t fixed = (size_t)laic::kConsumerWarps * 16 * sh.nt * 8 * 4 + 16 * (size_t)B * 4 + sh.nt * 8 * 8 + 1024;
+    const int G = num_sms();
+    double best = 1e30;
+    for (int nk = 1; nk <= std::min(m.nb, 64); ++nk) {
+        const int kr = (m.nb + nk - 1) / nk;
+        if ((m.nb + kr - 1) / kr != nk) continue;  // no empty split
+        const size_t xs = (size_t)kr * B * 128;
+        if (fixed + xs + 2 * stage_bytes > kSmemBudget) continue;
+        const int cta_per_k = G / nk;
+        if (cta_per_k < 1) break;
+        const int tiles_per = (m.ntiles + cta_per_k - 1) / cta_per_k;
+        const double cost = (double)tiles_per * (kr + 3) + (nk > 1 ? 2.0 : 0.0);
+        if (cost < best - 1e-9) {
+            best = cost;
+            sh.nk = nk;
+            sh.kr = kr;
+            sh.stages = (int)std::min<size_t>(8, (kSmemBudget - fixed - xs) / stage_bytes);
+            sh.grid = nk * std::min(cta_per_k, m.ntiles);
+            sh.smem = fixed + xs + sh.stages * stage_bytes;
+        }
     }
+    sh.part_floats = sh.nk > 1 ? (size_t)m.ntiles * sh.nk * 16 * B : 0;
+    return sh;
 }
 
-MatvecFn mv_pick(int type, int ns, int epi, bool kv32) {
-    if (type == T_Q4_0) return ns == 1 ? mv_pick_epi<T_Q4_0, 1>(epi, kv32) : mv_pick_epi<T_Q4_0, 2>(epi, kv32);
-    if (type == T_Q8_0) return ns == 1 ? mv_pick_epi<T_Q8_0, 1>(epi, kv32) : mv_pick_epi<T_Q8_0, 2>(epi, kv32);
-    return ns == 1 ? mv_pick_epi<T_F16, 1>(epi, kv32) : mv_pick_epi<T_F16, 2>(epi, kv32);
+// Split-K scratch shared by every matvec launch of a stream (launches are serialised).
+struct MvScratch {
+    float* part = nullptr;
+    unsigned* tile_cnt = nullptr;
+    int* err = nullptr;
+    size_t part_cap = 0, cnt_cap = 0;
+};
+
+int mv_scratch_reserve(MvScratch& sc, size_t part_floats, size_t ntiles) {
+    if (!sc.err) {
+        CK(cudaMalloc(&sc.err, 4));
+        CK(cudaMemset(sc.err, 0, 4));
+    }
+    if (part_floats > sc.part_cap) {
+        if (sc.part) cudaFree(sc.part);
+        sc.part = nullptr;
+        CK(cudaMalloc(&sc.part, part_floats * 4));
+        sc.part_cap = part_floats;
+    }
+    if (ntiles > sc.cnt_cap) {
+        if (sc.tile_cnt) cudaFree(sc.tile_cnt);
+        sc.tile_cnt = nullptr;
+        CK(cudaMalloc(&sc.tile_cnt, ntiles * 4));
+        CK(cudaMemset(sc.tile_cnt, 0, ntiles * 4));
+        sc.cnt_cap = ntiles;
+    }
+    return LAIC_OK;
 }
 
-int rows_per_group(int type) { return type == T_F16 ? 4 : 8; }
+void mv_scratch_free(MvScratch& sc) {
+    if (sc.part) cudaFree(sc.part);
+    if (sc.tile_cnt) cudaFree(sc.tile_cnt);
+    if (sc.err) cudaFree(sc.err);
+    sc = MvScratch{};
+}
 
-cudaError_t launch_matvec(const Mat& m, laic::MatvecParams p, int epi, bool kv32, cudaStream_t st, bool pdl) {
-    p.w = m.w; p.d = m.d; p.rows = m.rows; p.in = m.in; p.nb = m.nb;
-    const int ns = p.nseq == 1 ? 1 : 2;
-    const int groups = (m.rows + rows_per_group(m.type) - 1) / rows_per_group(m.type);
-    const int per_sm = ns == 1 ? 2 : 1;
-    const int grid = std::max(1, std::min((groups + 7) / 8, num_sms() * per_sm));
-    const size_t smem = (size_t)ns * m.in * sizeof(float);
-    return launch_k(mv_pick(m.type, ns, epi, kv32), dim3(grid), dim3(256), smem, st, pdl, p);
+cudaError_t launch_matvec(const Mat& m, laic::MvParams p, int epi, bool kv32, const MvScratch& sc, cudaStream_t st,
+                          bool pdl) {
+    const MvShape sh = mv_shape(m, p.nseq);
+    p.q = m.q; p.s = m.s; p.rows = m.rows; p.ntiles = m.ntiles; p.in = m.in; p.nb = m.nb;
+    if (sh.sk) {
+        p.err = sc.err;
+        return laic::mv_sk_launch(m.type, sh.nt, epi, kv32, p, sh.grid, sh.smem, st, pdl);
+    }
+    p.nk = sh.nk; p.kr = sh.kr; p.kb = sh.kb; p.stages = sh.stages;
+    p.part = sc.part; p.tile_cnt = sc.tile_cnt; p.err = sc.err;
+    return laic::mv_launch(m.type, sh.nt, epi, kv32, p, sh.grid, sh.smem, st, pdl);
 }
 
 using AttnFn = void (*)(laic::AttnParams);
@@ -264,6 +302,7 @@ struct laic_dev {
     std::vector<long long> h_pos;
 
     std::map<std::pair<int, int>, cudaGraphExec_t> graphs;  // (nseq, mode) -> graph
+    MvScratch mvs;  // split-K partials and tickets of the matvec launches
     int last_split = 1;
 
     // ------------------------------------------------------------------
@@ -318,7 +357,7 @@ struct laic_dev {
             if (full) CK(cudaMemcpyAsync(d_params, h_params, nseq * sizeof(laic::SampleDev), cudaMemcpyHostToDevice, s));
         }
 
-        laic::EmbedParams ep{embd.type, embd.w, embd.d, h, embd.nb, d_tokens, d_slots, x, counts, V};
+        laic::EmbedParams ep{embd.type, embd.q, embd.s, h, embd.nb, d_tokens, d_slots, x, counts, V};
         t_begin("embed", 0);
         CK(launch_k(laic::embed_kernel, dim3(nseq), dim3(256), 0, s, pdl, ep));
         t_end();
@@ -334,7 +373,7 @@ struct laic_dev {
 
         for (int l = 0; l < L; ++l) {
             Layer& ly = layers[l];
-            laic::MatvecParams p{};
+            laic::MvParams p{};
             p.nseq = nseq;
             p.eps = a.rms_eps;
             // qkv
@@ -345,7 +384,7 @@ struct laic_dev {
             p.vc = (char*)vc + (size_t)l * kv_layer_stride * kvb;
             p.kv_slot_stride = kv_slot_stride; p.kv_cap = cap;
             t_begin("qkv", (double)ly.qkv.bytes() + 4.0 * nseq * (h + ly.qkv.rows));
-            CK(launch_matvec(ly.qkv, p, laic::EPI_QKV, kv32, s, pdl));
+            CK(launch_matvec(ly.qkv, p, laic::EPI_QKV, kv32, mvs, s, pdl));
             t_end();
             // attention
             laic::AttnParams ap{};
@@ -357,29 +396,29 @@ struct laic_dev {
             CK(launch_k(afn, dim3(nsplit, Hkv, nseq), dim3(laic::kAttnWarps * 32), 0, s, pdl, ap));
             t_end();
             // o + residual
-            laic::MatvecParams po{};
+            laic::MvParams po{};
             po.nseq = nseq; po.x = attn; po.ldx = h; po.out = x; po.ldo = h;
             t_begin("o", (double)ly.o.bytes() + 12.0 * nseq * h);
-            CK(launch_matvec(ly.o, po, laic::EPI_ADD, kv32, s, pdl));
+            CK(launch_matvec(ly.o, po, laic::EPI_ADD, kv32, mvs, s, pdl));
             t_end();
             // gate/up + swiglu
-            laic::MatvecParams pg{};
+            laic::MvParams pg{};
             pg.nseq = nseq; pg.eps = a.rms_eps; pg.x = x; pg.ldx = h; pg.norm_w = ly.ffn_norm; pg.out = act; pg.ldo = F;
             t_begin("gate_up", (double)ly.gu.bytes() + 4.0 * nseq * (h + F));
-            CK(launch_matvec(ly.gu, pg, laic::EPI_SWIGLU, kv32, s, pdl));
+            CK(launch_matvec(ly.gu, pg, laic::EPI_SWIGLU, kv32, mvs, s, pdl));
             t_end();
             // down + residual
-            laic::MatvecParams pd{};
+            laic::MvParams pd{};
             pd.nseq = nseq; pd.x = act; pd.ldx = F; pd.out = x; pd.ldo = h;
             t_begin("down", (double)ly.down.bytes() + 4.0 * nseq * (F + 2 * h));
-            CK(launch_matvec(ly.down, pd, laic::EPI_ADD, kv32, s, pdl));
+            CK(launch_matvec(ly.down, pd, laic::EPI_ADD, kv32, mvs, s, pdl));
             t_end();
         }
         if (full) {
-            laic::MatvecParams pl{};
+            laic::MvParams pl{};
             pl.nseq = nseq; pl.eps = a.rms_eps; pl.x = x; pl.ldx = h; pl.norm_w = out_norm; pl.out = logits; pl.ldo = V;
             t_begin("lm_head", (double)lm_head().bytes() + 4.0 * nseq * (h + V));
-            CK(launch_matvec(lm_head(), pl, laic::EPI_STORE, kv32, s, pdl));
+            CK(launch_matvec(lm_head(), pl, laic::EPI_STORE, kv32, mvs, s, pdl));
             t_end();
             laic::SamplerParams sp{logits, V, V, d_slots, counts, d_params, nseq, d_out_ids, d_tokens, pos, d_err};
             t_begin("sampler", (double)nseq * V * 4);
@@ -398,7 +437,28 @@ struct laic_dev {
         return LAIC_OK;
     }
 
+    // Size the split-K scratch for `nseq` sequences (before any capture).
+    int reserve_scratch(int nseq) {
+        size_t part = 0, tiles = 0;
+        auto see = [&](const Mat& m) {
+            if (!m.q) return;
+            part = std::max(part, mv_shape(m, nseq).part_floats);
+            tiles = std::max(tiles, (size_t)m.ntiles);
+        };
+        for (auto& l : layers) { see(l.qkv); see(l.o); see(l.gu); see(l.down); }
+        see(lm_head());
+        const bool grows = part > mvs.part_cap || tiles > mvs.cnt_cap;
+        int rc = mv_scratch_reserve(mvs, part, tiles);
+        if (!rc && grows) {  // graphs captured the old buffers
+            for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+            graphs.clear();
+        }
+        return rc;
+    }
+
     int run(int nseq, int mode) {
+        int rc0 = reserve_scratch(nseq);
+        if (rc0) return rc0;
         if (!use_graph) return enqueue(nseq, mode, st, nullptr);
         auto key = std::make_pair(nseq, mode);
         auto it = graphs.find(key);
@@ -490,6 +550,7 @@ int laic_dev_create(const laic_dev_desc* desc, const laic_dev_opts* opts, laic_d
     if (a.heads / a.kv_heads > 8) return fail(LAIC_E_UNSUPPORTED, "at most 8 query heads per kv head");
     if (a.hidden % 32 || a.ffn % 32) return fail(LAIC_E_UNSUPPORTED, "hidden and ffn must be multiples of 32");
     if (o.max_seqs < 1) return fail(LAIC_E_INVALID, "max_seqs must be >= 1");
+    if (o.max_seqs > 64) return fail(LAIC_E_UNSUPPORTED, "at most 64 sequence slots per device");
     const uint32_t ctx = a.ctx ? a.ctx : 2048;
     int cap = o.kv_capacity > 0 ? std::min<int>(o.kv_capacity, (int)ctx) : (int)ctx;
 
@@ -507,9 +568,7 @@ int laic_dev_create(const laic_dev_desc* desc, const laic_dev_opts* opts, laic_d
     d->h_pos.assign(o.max_seqs, 0);
     CK(cudaStreamCreateWithFlags(&d->st, cudaStreamNonBlocking));
     // set kernel attributes now: graph capture must not see attribute calls
-    for (int t : {T_F16, T_Q4_0, T_Q8_0})
-        for (int ns : {1, 2})
-            for (int e : {laic::EPI_STORE, laic::EPI_ADD, laic::EPI_SWIGLU, laic::EPI_QKV}) mv_pick(t, ns, e, d->kv32);
+    CK(laic::mv_set_attributes());
 
     const size_t S = o.max_seqs, kvb = d->kv32 ? 4 : 2;
     CK(cudaMalloc(&d->x, S * d->h * 4));
@@ -574,6 +633,7 @@ void laic_dev_destroy(laic_dev* d) {
         if (l.ffn_norm) cudaFree(l.ffn_norm);
     }
     mat_free(d->embd); mat_free(d->lm);
+    mv_scratch_free(d->mvs);
     void* bufs[] = {d->out_norm, d->x, d->q, d->attn, d->act, d->logits, d->kc, d->vc, d->pos, d->counts,
                     d->rope_cs, d->attn_part, d->attn_cnt, d->d_tokens, d->d_out_ids, d->d_slots, d->d_err, d->d_params,
                     d->d_hist, d->d_hist_count};
@@ -622,8 +682,8 @@ int laic_dev_upload(laic_dev* d, const char* cname, int32_t type, const uint64_t
     Layer& ly = d->layers[l];
     const int h = d->h, kv = d->kv, F = d->F;
     auto ensure = [&](Mat& m, int rows, int in) -> int {
-        if (m.w && m.type != type) return fail(LAIC_E_UNSUPPORTED, "fused projections need one type: " + name);
-        if (!m.w) return mat_alloc(m, type, rows, in);
+        if (m.q && m.type != type) return fail(LAIC_E_UNSUPPORTED, "fused projections need one type: " + name);
+        if (!m.q) return mat_alloc(m, type, rows, in);
         return LAIC_OK;
     };
     int rc = LAIC_OK;
@@ -698,6 +758,13 @@ static int fill_params(laic_dev* d, int32_t nseq, const laic_sample_params* para
 
 static int check_sampler_err(laic_dev* d) {
     int err = 0;
+    if (d->mvs.err) {
+        CK(cudaMemcpy(&err, d->mvs.err, 4, cudaMemcpyDeviceToHost));
+        if (err) {
+            CK(cudaMemset(d->mvs.err, 0, 4));
+            return fail(LAIC_E_CUDA, "a matvec pipeline wait timed out");
+        }
+    }
     CK(cudaMemcpy(&err, d->d_err, 4, cudaMemcpyDeviceToHost));
     if (err) {
         CK(cudaMemset(d->d_err, 0, 4));
@@ -876,6 +943,7 @@ int laic_nccl_unique_id(void* out128) {
 struct laic_tensor {
     int device = 0;
     Mat m;
+    MvScratch sc;
 };
 
 extern "C" {
@@ -885,6 +953,7 @@ int laic_tensor_create(int32_t device, int32_t type, uint64_t in, uint64_t out, 
     if (!data || !t || !in || !out) return fail(LAIC_E_INVALID, "bad argument");
     if (nbytes < elem_bytes(type, in * out)) return fail(LAIC_E_INVALID, "tensor data out of range");
     CK(cudaSetDevice(device));
+    CK(laic::mv_set_attributes());
     std::unique_ptr<laic_tensor> x(new laic_tensor());
     x->device = device;
     int rc = mat_alloc(x->m, type, (int)out, (int)in);
@@ -902,6 +971,7 @@ void laic_tensor_destroy(laic_tensor* t) {
     if (!t) return;
     cudaSetDevice(t->device);
     mat_free(t->m);
+    mv_scratch_free(t->sc);
     delete t;
 }
 
@@ -910,17 +980,21 @@ uint64_t laic_tensor_bytes(laic_tensor* t) { return t ? t->m.bytes() : 0; }
 int laic_tensor_matvec(laic_tensor* t, const float* x, float* y, int32_t batch, void* stream) {
     if (!t || !x || !y || batch < 1) return fail(LAIC_E_INVALID, "bad argument");
     CK(cudaSetDevice(t->device));
-    laic::MatvecParams p{};
+    if (batch > 64) return fail(LAIC_E_UNSUPPORTED, "at most 64 sequences per matvec");
+    const MvShape sh = mv_shape(t->m, batch);
+    int rc = mv_scratch_reserve(t->sc, sh.part_floats, (size_t)t->m.ntiles);
+    if (rc) return rc;
+    laic::MvParams p{};
     p.nseq = batch; p.x = x; p.ldx = t->m.in; p.out = y; p.ldo = t->m.rows;
-    CK(launch_matvec(t->m, p, laic::EPI_STORE, false, (cudaStream_t)stream, false));
+    CK(launch_matvec(t->m, p, laic::EPI_STORE, false, t->sc, (cudaStream_t)stream, false));
     return LAIC_OK;
 }
 
 int laic_tensor_dequant(laic_tensor* t, float* out, void* stream) {
     if (!t || !out) return fail(LAIC_E_INVALID, "bad argument");
     CK(cudaSetDevice(t->device));
-    laic::dequant_kernel<<<1184, 256, 0, (cudaStream_t)stream>>>(t->m.type, t->m.w, t->m.d, t->m.in, t->m.nb,
-                                                                  t->m.rows, out);
+    laic::tile_dequant_kernel<<<1184, 256, 0, (cudaStream_t)stream>>>(t->m.type, t->m.q, t->m.s, t->m.in, t->m.nb,
+                                                                       t->m.rows, out);
     CK(cudaGetLastError());
     return LAIC_OK;
 }

@@ -1,0 +1,37 @@
+// Host-side launch helper: cudaLaunchKernelEx with optional programmatic
+// dependent launch (the kernel may start while its predecessor drains; it
+// orders itself with griddepcontrol.wait before touching dependent data).
+#pragma once
+#include <cuda_runtime.h>
+
+#include <utility>
+
+namespace laic {
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                     Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+struct MvParams;
+// Launch the fragment-tile matvec for one weight type (defined in mv_<type>.cu).
+cudaError_t mv_launch(int type, int nt, int epi, bool kv32, const MvParams& p, int grid, size_t smem, cudaStream_t st,
+                      bool pdl);
+// Launch the team matvec (defined in mv_<type>.cu), nt = 1, 2 or 4.
+cudaError_t mv_sk_launch(int type, int nt, int epi, bool kv32, const MvParams& p, int grid, size_t smem,
+                         cudaStream_t st, bool pdl);
+// Raise the dynamic shared memory limit of every instantiation (call before any graph capture).
+cudaError_t mv_set_attributes();
+
+}  // namespace laic

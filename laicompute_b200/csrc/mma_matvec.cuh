@@ -1,0 +1,472 @@
+// Dequant-fused matrix-vector / skinny-GEMM for decode on sm_100a.
+//
+// Replaces LlamaRuntime::matvec (reference src/inference_v2.cpp:29) and its two
+// row-dot paths, quant_dot (:21, quant_v2::value per element) and dot_cached
+// (:22, compute::dot_f16), for 1..64 sequences. Each projection of a layer is
+// one launch that also carries the elementwise work around it:
+//   prologue  rmsnorm of the residual (src/inference_v2.cpp:24 and :30)
+//   epilogue  store | residual add (compute::axpy_f32, src/compute_dot.cpp:64-72)
+//             | SwiGLU (gate/up rows interleaved, :23 and :31)
+//             | QKV: RoPE (:25) on q and k, then K/V appended to the device cache
+//
+// Data path.
+//  * Weights live in a "fragment tile" layout built once at upload: 16 rows x
+//    32 columns (one GGUF block column) form a tile-block whose bytes are laid
+//    out so that lane L of a warp reads exactly the A-operand fragment of
+//    mma.m16n8k16 it needs (rows g and g+8, g = L/4, for 8 of the 32 columns).
+//    Block quants and binary16 scales keep their file values.
+//  * A producer warp streams the tile-blocks of the CTA's work into a shared
+//    memory ring with 1-D bulk TMA copies (cp.async.bulk + mbarrier), issued
+//    before the programmatic-dependent-launch wait: weights never depend on
+//    the previous kernel, so the stream starts while that kernel drains.
+//  * Consumer warps turn quants into exact binary16 integers with one
+//    AND/OR per pair (0x6400 exponent trick) and one packed subtract, and run
+//    mma.sync m16n8k16 (fp16 in, fp32 accumulate) against the activations,
+//    which are split into binary16 hi + lo parts (hi + lo carries 22 bits of
+//    the fp32 value): y = sum_blocks d * (q . x_hi + q . x_lo) in fp32.
+//  * The K dimension may be split across CTAs; the last CTA of a row tile
+//    (atomic ticket, no spinning) adds the partials in a fixed order and runs
+//    the epilogue, so results are deterministic.
+#pragma once
+#include "common.cuh"
+#include "tiles.cuh"
+
+namespace laic {
+
+enum : int { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2, EPI_QKV = 3 };
+
+constexpr int kConsumerWarps = 8;
+constexpr int kMvThreads = (kConsumerWarps + 1) * 32;
+
+
+struct MvParams {
+    const uint8_t* q;          // [ntiles][nb][tile_qbytes]
+    const uint8_t* s;          // [ntiles][nb][32]   (Q4_0/Q8_0)
+    int rows, ntiles, in, nb;
+    int nseq;
+    const float* x;            // input [nseq][ldx]
+    int ldx;
+    const float* norm_w;       // rmsnorm weight [in] (nullptr: no norm)
+    float eps;
+    int nk, kr, kb, stages;    // K splits, blocks per split, blocks per ring stage, ring depth
+    float* part;               // split-K partials [ntiles][nk][16][nseq] (scratch)
+    unsigned* tile_cnt;        // [ntiles] tickets, zero between launches (scratch)
+    int* err;                  // set when a bounded wait runs out
+    float* out;                // epilogue output
+    int ldo;
+    // EPI_QKV
+    int q_rows, kv_rows, head_dim, rope_pairs;
+    const float2* rope_cs;     // [ctx][rope_pairs] (cos, sin)
+    const int* slots;          // [nseq]
+    const int* pos;            // [max_seqs]
+    void* kc;                  // this layer's K cache
+    void* vc;                  // this layer's V cache
+    long long kv_slot_stride;  // elements between slots
+    int kv_cap;
+};
+
+// ---------------------------------------------------------------------------
+// PTX helpers: mbarrier, bulk copy, mma
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// try_wait that lets the hardware suspend the thread (up to ~0.1 ms) until the
+// phase completes, so waiting warps do not take issue slots from working ones.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(100000u)
+        : "memory");
+    return ok != 0;
+}
+// Wait for a barrier phase with a time limit (~1 s of SM clocks); on timeout
+// record the failure and return false so the caller can leave cleanly.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait_sleep(bar, parity)) {
+        if (clock64() - t0 > 2000000000LL) {
+            atomicExch(err, 1);
+            return false;
+        }
+    }
+    return true;
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t a0, const uint32_t a1, const uint32_t a2,
+                                         const uint32_t a3, const uint32_t b0, const uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Same product with a zero accumulator input (no zeroed registers to set up).
+__device__ __forceinline__ void mma16816_z(float (&d)[4], const uint32_t a0, const uint32_t a1, const uint32_t a2,
+                                           const uint32_t a3, const uint32_t b0, const uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
+}
+// Accumulating product without the volatile qualifier, so the compiler may interleave independent tiles.
+__device__ __forceinline__ void mma16816_acc(float (&d)[4], const uint32_t a0, const uint32_t a1, const uint32_t a2,
+                                             const uint32_t a3, const uint32_t b0, const uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t h2_sub(uint32_t a, uint32_t b) {
+    __half2 r = __hsub2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
+    return *reinterpret_cast<uint32_t*>(&r);
+}
+__device__ __forceinline__ uint32_t h2_fma(uint32_t a, uint32_t b, uint32_t c) {
+    __half2 r = __hfma2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b), *reinterpret_cast<__half2*>(&c));
+    return *reinterpret_cast<uint32_t*>(&r);
+}
+
+// Q4_0 word (8 nibbles, elements e0..e7 of one row's 8-column group) ->
+// four half2 registers (e0,e4) (e1,e5) (e2,e6) (e3,e7) holding q-8 exactly.
+__device__ __forceinline__ void decode_q4(uint32_t w, uint32_t (&r)[4]) {
+    const uint32_t M = 0x64006400u;                 // binary16 1024 in both halves
+    const uint32_t k1032 = 0x64086408u;             // 1032
+    const uint32_t k1_16 = 0x2C002C00u;             // 1/16
+    const uint32_t km72 = 0xD480D480u;              // -72
+    const uint32_t w8 = w >> 8;
+    r[0] = h2_sub((w & 0x000F000Fu) | M, k1032);            // (1024+n) - 1032
+    r[1] = h2_fma((w & 0x00F000F0u) | M, k1_16, km72);      // (1024+16n)/16 - 72
+    r[2] = h2_sub((w8 & 0x000F000Fu) | M, k1032);
+    r[3] = h2_fma((w8 & 0x00F000F0u) | M, k1_16, km72);
+}
+// Q8_0: 8 int8 of one row in fragment order (e0 e4 e1 e5 | e2 e6 e3 e7) -> four half2 = q.
+__device__ __forceinline__ void decode_q8(uint32_t u0, uint32_t u1, uint32_t (&r)[4]) {
+    const uint32_t C = 0x64646464u, k1152 = 0x64806480u;  // 1024 + 128
+    u0 ^= 0x80808080u;
+    u1 ^= 0x80808080u;
+    r[0] = h2_sub(__byte_perm(u0, C, 0x4140), k1152);
+    r[1] = h2_sub(__byte_perm(u0, C, 0x4342), k1152);
+    r[2] = h2_sub(__byte_perm(u1, C, 0x4140), k1152);
+    r[3] = h2_sub(__byte_perm(u1, C, 0x4342), k1152);
+}
+
+template <typename KV> __device__ __forceinline__ KV kv_from(float v);
+template <> __device__ __forceinline__ __half kv_from<__half>(float v) { return __float2half_rn(v); }
+template <> __device__ __forceinline__ float kv_from<float>(float v) { return v; }
+
+// Host-side sizing shared with the launcher.
+__host__ __device__ constexpr int mv_ring_bytes(int type, int kb, int stages) {
+    return stages * kb * (tile_qbytes(type) + (type == T_F16 ? 0 : kTileSBytes));
+}
+
+// ---------------------------------------------------------------------------
+// the kernel: NT n-tiles of 8 sequences (NT*8 >= nseq)
+// ---------------------------------------------------------------------------
+template <int WT, int NT, int EPI, typename KV>
+__global__ void __launch_bounds__(kMvThreads, 1) mv_mma_kernel(const MvParams p) {
+    constexpr int QB = tile_qbytes(WT);
+    constexpr int SB = WT == T_F16 ? 0 : kTileSBytes;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, c = lane & 3;
+    const int B = p.nseq;
+    const int stage_bytes = p.kb * (QB + SB);
+
+    uint8_t* ring = smem;
+    uint8_t* xs = ring + p.stages * stage_bytes;                       // [kr][B][4][32 B]
+    float* red = reinterpret_cast<float*>(xs + (size_t)p.kr * B * 128);  // [8 warps][16][NT*8]
+    float* fin = red + kConsumerWarps * 16 * NT * 8;                  // [16][B]
+    float* xinv = fin + 16 * B;                                       // [B] 1/scale of each sequence
+    float* xnrm = xinv + NT * 8;                                      // [B] rmsnorm inv
+    uint64_t* full = reinterpret_cast<uint64_t*>(xnrm + NT * 8);
+    uint64_t* empty = full + p.stages;
+    int* ticket = reinterpret_cast<int*>(empty + p.stages);
+
+    const int k_split = blockIdx.x % p.nk;
+    const int cta_per_k = gridDim.x / p.nk;
+    const int t_first = blockIdx.x / p.nk;
+    const int b_lo = k_split * p.kr;
+    const int b_hi = min(p.nb, b_lo + p.kr);
+    const int nblk = max(0, b_hi - b_lo);
+    const int stages_per_tile = (nblk + p.kb - 1) / p.kb;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < p.stages; ++i) { mbar_init(full + i, 1); mbar_init(empty + i, kConsumerWarps); }
+        mbar_fence_init();
+    }
+    __syncthreads();
+
+    if (warp == kConsumerWarps) {
+        // ---------------- producer: stream this CTA's tile-blocks ----------------
+        if (lane == 0 && nblk > 0) {
+            int it = 0;
+            bool ok = true;
+            for (int t = t_first; t < p.ntiles && ok; t += cta_per_k) {
+                for (int st = 0; st < stages_per_tile; ++st, ++it) {
+                    const int slot = it % p.stages;
+                    const uint32_t ph = (uint32_t)(it / p.stages) & 1u;
+                    if (!mbar_wait(empty + slot, ph ^ 1u, p.err)) { ok = false; break; }
+                    const int b0 = b_lo + st * p.kb;
+                    const int n = min(p.kb, b_hi - b0);
+                    uint8_t* dst = ring + slot * stage_bytes;
+                    const size_t tb = (size_t)t * p.nb + b0;
+                    mbar_expect_tx(full + slot, (uint32_t)(n * (QB + SB)));
+                    bulk_g2s(dst, p.q + tb * QB, (uint32_t)(n * QB), full + slot);
+                    if (SB) bulk_g2s(dst + p.kb * QB, p.s + tb * SB, (uint32_t)(n * SB), full + slot);
+                }
+            }
+            // leave only after every copy issued into this CTA's shared memory has landed
+            const int issued = it;
+            for (int j = max(0, issued - p.stages); j < issued; ++j)
+                mbar_wait(full + (j % p.stages), (uint32_t)(j / p.stages) & 1u, p.err);
+        }
+        return;
+    }
+
+    // ---------------- consumers ----------------
+    const int ctid = threadIdx.x;  // 0 .. 255
+    constexpr int NC = kConsumerWarps * 32;
+    pdl_wait();
+
+    // prologue: activations of this K split -> binary16 hi/lo in fragment order
+    {
+        if (p.norm_w) {
+            for (int s = warp; s < B; s += kConsumerWarps) {
+                const float* src = p.x + (size_t)s * p.ldx;
+                float ss = 0.f;
+                for (int e = lane; e < p.in; e += 32) { const float v = src[e]; ss = fmaf(v, v, ss); }
+                ss = warp_sum(ss);
+                if (lane == 0) xnrm[s] = 1.f / sqrtf(ss / float(p.in) + p.eps);
+            }
+            named_sync(1, NC);
+        }
+        // per-sequence power-of-two scale so the largest |x| of this split sits in [2^10, 2^11)
+        for (int s = warp; s < B; s += kConsumerWarps) {
+            const float* src = p.x + (size_t)s * p.ldx;
+            float m = 0.f;
+            for (int e = b_lo * 32 + lane; e < b_hi * 32; e += 32) {
+                float v = src[e];
+                if (p.norm_w) v = v * (xnrm[s] * p.norm_w[e]);
+                m = fmaxf(m, fabsf(v));
+            }
+            m = warp_max(m);
+            if (lane == 0) {
+                int ex = 0;
+                if (m > 0.f && isfinite(m)) { frexpf(m, &ex); ex = max(-100, min(100, ex)); }
+                xinv[s] = ldexpf(1.f, ex - 11);  // m * 2^(11-ex) in [2^10, 2^11)
+            }
+        }
+        named_sync(1, NC);
+        __half* xh = reinterpret_cast<__half*>(xs);
+        const int ne = nblk * 32;
+        for (int i = ctid; i < ne * B; i += NC) {
+            const int s = i / ne, el = i % ne;
+            const int e = b_lo * 32 + el;
+            float v = p.x[(size_t)s * p.ldx + e];
+            if (p.norm_w) v = v * (xnrm[s] * p.norm_w[e]);
+            v = v * (1.f / xinv[s]);  // exact: a power of two
+            const __half hi = __float2half_rn(v);
+            const __half lo = __float2half_rn(v - __half2float(hi));
+            const int bl = el >> 5, cc = (el >> 3) & 3, k = el & 7;
+            __half* dst = xh + ((size_t)(bl * B + s) * 4 + cc) * 16;
+            dst[frag_pos(k)] = hi;
+            dst[8 + frag_pos(k)] = lo;
+        }
+        named_sync(1, NC);
+    }
+    pdl_launch_dependents();
+
+    int it = 0;
+    bool aborted = false;  // a wait ran out: keep the barrier protocol, skip the math
+    for (int t = t_first; t < p.ntiles; t += cta_per_k) {
+        float acc[NT][4];
+#pragma unroll
+        for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+
+        for (int st = 0; st < stages_per_tile; ++st, ++it) {
+            const int slot = it % p.stages;
+            if (!aborted && !mbar_wait(full + slot, (uint32_t)(it / p.stages) & 1u, p.err)) aborted = true;
+            const uint8_t* sq = ring + slot * stage_bytes;
+            const uint8_t* ss = sq + p.kb * QB;
+            const int n = aborted ? 0 : min(p.kb, b_hi - (b_lo + st * p.kb));
+            for (int bi = warp; bi < n; bi += kConsumerWarps) {
+                const int bl = st * p.kb + bi;  // block index within the split
+                uint32_t ra[4], rb[4];          // rows g and g+8, four half2 each
+                if (WT == T_Q4_0) {
+                    const uint2 w = *reinterpret_cast<const uint2*>(sq + bi * QB + lane * 8);
+                    decode_q4(w.x, ra);
+                    decode_q4(w.y, rb);
+                } else if (WT == T_Q8_0) {
+                    const uint4 w = *reinterpret_cast<const uint4*>(sq + bi * QB + lane * 16);
+                    decode_q8(w.x, w.y, ra);
+                    decode_q8(w.z, w.w, rb);
+                } else {
+                    const uint4 w0 = *reinterpret_cast<const uint4*>(sq + bi * QB + lane * 32);
+                    const uint4 w1 = *reinterpret_cast<const uint4*>(sq + bi * QB + lane * 32 + 16);
+                    ra[0] = w0.x; ra[1] = w0.y; ra[2] = w0.z; ra[3] = w0.w;
+                    rb[0] = w1.x; rb[1] = w1.y; rb[2] = w1.z; rb[3] = w1.w;
+                }
+                float dg = 1.f, dg8 = 1.f;
+                if (WT != T_F16) {
+                    const uint32_t dp = *reinterpret_cast<const uint32_t*>(ss + bi * SB + g * 4);
+                    const float2 df = __half22float2(*reinterpret_cast<const __half2*>(&dp));
+                    dg = df.x; dg8 = df.y;
+                }
+#pragma unroll
+                for (int j = 0; j < NT; ++j) {
+                    const int s = j * 8 + g;
+                    uint4 xh = make_uint4(0, 0, 0, 0), xl = make_uint4(0, 0, 0, 0);
+                    if (s < B) {
+                        const uint4* xp = reinterpret_cast<const uint4*>(xs + ((size_t)(bl * B + s) * 4 + c) * 32);
+                        xh = xp[0];
+                        xl = xp[1];
+                    }
+                    if (WT == T_F16) {
+                        mma16816(acc[j], ra[0], rb[0], ra[1], rb[1], xh.x, xh.y);
+                        mma16816(acc[j], ra[0], rb[0], ra[1], rb[1], xl.x, xl.y);
+                        mma16816(acc[j], ra[2], rb[2], ra[3], rb[3], xh.z, xh.w);
+                        mma16816(acc[j], ra[2], rb[2], ra[3], rb[3], xl.z, xl.w);
+                    } else {
+                        float tmp[4] = {0.f, 0.f, 0.f, 0.f};
+                        mma16816(tmp, ra[0], rb[0], ra[1], rb[1], xh.x, xh.y);
+                        mma16816(tmp, ra[0], rb[0], ra[1], rb[1], xl.x, xl.y);
+                        mma16816(tmp, ra[2], rb[2], ra[3], rb[3], xh.z, xh.w);
+                        mma16816(tmp, ra[2], rb[2], ra[3], rb[3], xl.z, xl.w);
+                        acc[j][0] = fmaf(dg, tmp[0], acc[j][0]);
+                        acc[j][1] = fmaf(dg, tmp[1], acc[j][1]);
+                        acc[j][2] = fmaf(dg8, tmp[2], acc[j][2]);
+                        acc[j][3] = fmaf(dg8, tmp[3], acc[j][3]);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty + slot);
+        }
+
+        // ---- reduce the 8 consumer warps: red[w][row][n]
+        float* rw = red + warp * 16 * NT * 8;
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+            rw[g * NT * 8 + j * 8 + 2 * c] = acc[j][0];
+            rw[g * NT * 8 + j * 8 + 2 * c + 1] = acc[j][1];
+            rw[(g + 8) * NT * 8 + j * 8 + 2 * c] = acc[j][2];
+            rw[(g + 8) * NT * 8 + j * 8 + 2 * c + 1] = acc[j][3];
+        }
+        named_sync(1, NC);
+        for (int i = ctid; i < 16 * B; i += NC) {
+            const int r = i / B, s = i % B;
+            float v = 0.f;
+#pragma unroll
+            for (int w = 0; w < kConsumerWarps; ++w) v += red[w * 16 * NT * 8 + r * NT * 8 + s];
+            fin[r * B + s] = v * xinv[s];
+        }
+        named_sync(1, NC);
+
+        // ---- split-K: the last CTA of this row tile adds the partials in split order
+        if (p.nk > 1) {
+            float* pt = p.part + (size_t)t * p.nk * 16 * B;
+            for (int i = ctid; i < 16 * B; i += NC) pt[(size_t)k_split * 16 * B + i] = fin[i];
+            __threadfence();
+            named_sync(1, NC);
+            if (ctid == 0) *ticket = (int)atomicAdd(p.tile_cnt + t, 1u) == p.nk - 1;
+            named_sync(1, NC);
+            if (!*ticket) continue;
+            __threadfence();
+            for (int i = ctid; i < 16 * B; i += NC) {
+                float v = 0.f;
+                for (int k = 0; k < p.nk; ++k) v += __ldcg(pt + (size_t)k * 16 * B + i);
+                fin[i] = v;
+            }
+            if (ctid == 0) p.tile_cnt[t] = 0u;
+            named_sync(1, NC);
+        }
+
+        // ---- epilogue on fin[16][B]
+        const int r0 = t * 16;
+        for (int i = ctid; i < 16 * B; i += NC) {
+            const int rl = i / B, s = i % B, r = r0 + rl;
+            if (r >= p.rows) continue;
+            const float val = fin[i];
+            if (EPI == EPI_STORE) {
+                p.out[(size_t)s * p.ldo + r] = val;
+            } else if (EPI == EPI_ADD) {
+                p.out[(size_t)s * p.ldo + r] += val;
+            } else if (EPI == EPI_SWIGLU) {
+                // row 2o = gate o, row 2o+1 = up o: out[o] = silu(gate) * up
+                if ((rl & 1) == 0) {
+                    const float up = fin[(rl + 1) * B + s];
+                    p.out[(size_t)s * p.ldo + (r >> 1)] = (val / (1.f + expf(-val))) * up;
+                }
+            } else {  // EPI_QKV
+                const int slot = p.slots[s], ps = p.pos[slot];
+                int rr = r, region = 0;  // 0 q, 1 k, 2 v
+                if (rr >= p.q_rows) { rr -= p.q_rows; region = 1; if (rr >= p.kv_rows) { rr -= p.kv_rows; region = 2; } }
+                const int d = rr % p.head_dim;
+                float o = val;
+                if (region < 2 && d < 2 * p.rope_pairs) {
+                    const float2 cs = p.rope_cs[(size_t)ps * p.rope_pairs + (d >> 1)];
+                    const float other = fin[(rl ^ 1) * B + s];
+                    // adjacent-pair rotation, unfused to keep the reference's rounding
+                    if ((d & 1) == 0) o = __fsub_rn(__fmul_rn(val, cs.x), __fmul_rn(other, cs.y));
+                    else o = __fadd_rn(__fmul_rn(other, cs.y), __fmul_rn(val, cs.x));
+                }
+                if (region == 0) {
+                    p.out[(size_t)s * p.ldo + rr] = o;
+                } else {
+                    KV* base = reinterpret_cast<KV*>(region == 1 ? p.kc : p.vc);
+                    base[(size_t)slot * p.kv_slot_stride + ((size_t)(rr / p.head_dim) * p.kv_cap + ps) * p.head_dim + d] =
+                        kv_from<KV>(o);
+                }
+            }
+        }
+        named_sync(1, NC);  // fin/red reused by the next tile
+    }
+}
+
+}  // namespace laic

@@ -1,0 +1,54 @@
+// Dispatch of the fragment-tile matvec over weight type, n-tiles and epilogue.
+#include "launch.cuh"
+#include "mma_matvec.cuh"
+#include "mv_streamk.cuh"
+
+namespace laic {
+
+void (*mv_kernel_q4_0(int nt, int epi, bool kv32))(MvParams);
+void (*mv_kernel_q8_0(int nt, int epi, bool kv32))(MvParams);
+void (*mv_kernel_f16(int nt, int epi, bool kv32))(MvParams);
+void (*mv_sk_kernel_q4_0(int nt, int epi, bool kv32))(MvParams);
+void (*mv_sk_kernel_q8_0(int nt, int epi, bool kv32))(MvParams);
+void (*mv_sk_kernel_f16(int nt, int epi, bool kv32))(MvParams);
+
+static void (*mv_sk_kernel(int type, int nt, int epi, bool kv32))(MvParams) {
+    if (type == T_Q4_0) return mv_sk_kernel_q4_0(nt, epi, kv32);
+    if (type == T_Q8_0) return mv_sk_kernel_q8_0(nt, epi, kv32);
+    return mv_sk_kernel_f16(nt, epi, kv32);
+}
+
+cudaError_t mv_sk_launch(int type, int nt, int epi, bool kv32, const MvParams& p, int grid, size_t smem,
+                         cudaStream_t st, bool pdl) {
+    return launch_k(mv_sk_kernel(type, nt, epi, kv32), dim3(grid), dim3(kSkWarps * 32), smem, st, pdl, p);
+}
+
+static void (*mv_kernel(int type, int nt, int epi, bool kv32))(MvParams) {
+    if (type == T_Q4_0) return mv_kernel_q4_0(nt, epi, kv32);
+    if (type == T_Q8_0) return mv_kernel_q8_0(nt, epi, kv32);
+    return mv_kernel_f16(nt, epi, kv32);
+}
+
+cudaError_t mv_launch(int type, int nt, int epi, bool kv32, const MvParams& p, int grid, size_t smem, cudaStream_t st,
+                      bool pdl) {
+    return launch_k(mv_kernel(type, nt, epi, kv32), dim3(grid), dim3(kMvThreads), smem, st, pdl, p);
+}
+
+cudaError_t mv_set_attributes() {
+    for (int type : {T_Q4_0, T_Q8_0, T_F16})
+        for (int nt : {1, 2, 4, 8})
+            for (int epi : {EPI_STORE, EPI_ADD, EPI_SWIGLU, EPI_QKV})
+                for (bool kv32 : {false, true}) {
+                    cudaError_t e = cudaFuncSetAttribute(mv_kernel(type, nt, epi, kv32),
+                                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+                    if (e != cudaSuccess) return e;
+                    if (nt <= 4) {
+                        e = cudaFuncSetAttribute(mv_sk_kernel(type, nt, epi, kv32),
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+                        if (e != cudaSuccess) return e;
+                    }
+                }
+    return cudaSuccess;
+}
+
+}  // namespace laic

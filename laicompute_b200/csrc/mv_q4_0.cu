@@ -1,0 +1,41 @@
+// Instantiations of the fragment-tile matvec for one weight type.
+#include "launch.cuh"
+#include "mma_matvec.cuh"
+#include "mv_streamk.cuh"
+
+namespace laic {
+
+template <int NT>
+static void (*pick_q4_0(int epi, bool kv32))(MvParams) {
+    switch (epi) {
+    case EPI_STORE: return mv_mma_kernel<T_Q4_0, NT, EPI_STORE, __half>;
+    case EPI_ADD: return mv_mma_kernel<T_Q4_0, NT, EPI_ADD, __half>;
+    case EPI_SWIGLU: return mv_mma_kernel<T_Q4_0, NT, EPI_SWIGLU, __half>;
+    default: return kv32 ? mv_mma_kernel<T_Q4_0, NT, EPI_QKV, float> : mv_mma_kernel<T_Q4_0, NT, EPI_QKV, __half>;
+    }
+}
+
+void (*mv_kernel_q4_0(int nt, int epi, bool kv32))(MvParams) {
+    switch (nt) {
+    case 1: return pick_q4_0<1>(epi, kv32);
+    case 2: return pick_q4_0<2>(epi, kv32);
+    case 4: return pick_q4_0<4>(epi, kv32);
+    default: return pick_q4_0<8>(epi, kv32);
+    }
+}
+
+template <int NT>
+static void (*pick_sk_q4_0(int epi, bool kv32))(MvParams) {
+    switch (epi) {
+    case EPI_STORE: return mv_sk_kernel<T_Q4_0, NT, EPI_STORE, __half>;
+    case EPI_ADD: return mv_sk_kernel<T_Q4_0, NT, EPI_ADD, __half>;
+    case EPI_SWIGLU: return mv_sk_kernel<T_Q4_0, NT, EPI_SWIGLU, __half>;
+    default: return kv32 ? mv_sk_kernel<T_Q4_0, NT, EPI_QKV, float> : mv_sk_kernel<T_Q4_0, NT, EPI_QKV, __half>;
+    }
+}
+
+void (*mv_sk_kernel_q4_0(int nt, int epi, bool kv32))(MvParams) {
+    return nt == 1 ? pick_sk_q4_0<1>(epi, kv32) : nt == 2 ? pick_sk_q4_0<2>(epi, kv32) : pick_sk_q4_0<4>(epi, kv32);
+}
+
+}  // namespace laic

@@ -1,0 +1,347 @@
+// Team variant of the fragment-tile matvec for small batches (the decode
+// latency path: one to a few sequences whose activations fit in shared memory).
+//
+// Each CTA owns a contiguous run of whole 16-row tiles. Its warps form teams
+// of k warps; a team works on one tile at a time and warp i of the team takes
+// the i-th contiguous slice of the tile's K range. Every warp streams its
+// slices through its own shared-memory ring with 1-D bulk TMA copies issued by
+// its lane 0 (the first stages go out before the programmatic-dependent-launch
+// wait: weights never depend on the previous kernel), decodes and multiplies
+// with mma.sync like mv_mma_kernel, then drops its 16 x B partial sums into a
+// per-warp shared-memory slot and takes a shared-memory ticket. The warp that
+// completes a tile adds the team's partials in warp order (deterministic) and
+// runs the epilogue. The streaming loop never waits on global memory, and no
+// CTA-wide barrier is taken after the activation prologue.
+#pragma once
+#include "mma_matvec.cuh"
+
+namespace laic {
+
+constexpr int kSkWarps = 16;
+constexpr int kSkRingBytes = 9 * 1024;   // per warp: two stages in flight
+constexpr int kSkSlots = 2;              // tile slots per team (a team's warps may drift apart)
+// tile-blocks per ring stage (about 4.5 KB for every type)
+__host__ __device__ constexpr int sk_kb(int type) { return type == T_Q4_0 ? 16 : type == T_Q8_0 ? 8 : 4; }
+__host__ __device__ constexpr int sk_stage_bytes(int type) {
+    return sk_kb(type) * (tile_qbytes(type) + (type == T_F16 ? 0 : kTileSBytes));
+}
+__host__ __device__ constexpr int sk_stages(int type) { return kSkRingBytes / sk_stage_bytes(type); }
+// warps per tile: long rows are split over more warps
+__host__ __device__ inline int sk_team(int nb) {
+    return nb >= 256 ? 16 : nb >= 128 ? 8 : nb >= 64 ? 4 : nb >= 32 ? 2 : 1;
+}
+
+// tickets, merged-tile marks, per-warp statistics, 1/rms and split scale per sequence
+__host__ __device__ inline size_t sk_small_bytes(int B) {
+    return ((size_t)kSkWarps * kSkSlots * 2 * 4 + (size_t)kSkWarps * B * 2 * 4 + 2 * (size_t)B * 4 + 15) / 16 * 16;
+}
+// Shared memory of one CTA: rings, activations (whole K), partial slots + tickets, statistics, barriers.
+__host__ __device__ inline size_t sk_smem_bytes(int type, int nb, int B) {
+    const size_t rings = (size_t)kSkWarps * sk_stages(type) * sk_stage_bytes(type);
+    const size_t xs = (size_t)nb * B * 128;
+    const size_t parts = (size_t)kSkWarps * kSkSlots * 16 * B * 4;  // [warp][slot][16][B]
+    return rings + xs + parts + sk_small_bytes(B) + (size_t)kSkWarps * sk_stages(type) * 8;
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// One 16x32 tile-block: decode this lane's A fragments, multiply with the
+// activation columns (hi and lo parts side by side) and add d * result.
+// `xlane` points at this lane's activation record of block 0 (a padding column
+// reuses the last real one); records of consecutive blocks are `xstride` apart.
+template <int WT, int NT>
+__device__ __forceinline__ void tile_block(uint32_t q, uint32_t sc, const uint32_t (&xlane)[NT], int b, int xstride,
+                                           int lane, float (&acc)[NT][4]) {
+    const int g = lane >> 2;
+    uint32_t ra[4], rb[4];
+    if (WT == T_Q4_0) {
+        const uint2 w = lds64(q + lane * 8);
+        decode_q4(w.x, ra);
+        decode_q4(w.y, rb);
+    } else if (WT == T_Q8_0) {
+        const uint4 w = lds128(q + lane * 16);
+        decode_q8(w.x, w.y, ra);
+        decode_q8(w.z, w.w, rb);
+    } else {
+        const uint4 w0 = lds128(q + lane * 32);
+        const uint4 w1 = lds128(q + lane * 32 + 16);
+        ra[0] = w0.x; ra[1] = w0.y; ra[2] = w0.z; ra[3] = w0.w;
+        rb[0] = w1.x; rb[1] = w1.y; rb[2] = w1.z; rb[3] = w1.w;
+    }
+    float dg = 1.f, dg8 = 1.f;
+    if (WT != T_F16) {
+        const uint32_t dp = lds32(sc + g * 4);
+        const float2 df = __half22float2(*reinterpret_cast<const __half2*>(&dp));
+        dg = df.x; dg8 = df.y;
+    }
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+        // padding columns load a real record: their products land in output columns nobody reads
+        const uint4 xv = lds128(xlane[j] + b * xstride);
+        if (WT == T_F16) {
+            mma16816_acc(acc[j], ra[0], rb[0], ra[1], rb[1], xv.x, xv.y);
+            mma16816_acc(acc[j], ra[2], rb[2], ra[3], rb[3], xv.z, xv.w);
+        } else {
+            float t[4];
+            mma16816_z(t, ra[0], rb[0], ra[1], rb[1], xv.x, xv.y);
+            mma16816_acc(t, ra[2], rb[2], ra[3], rb[3], xv.z, xv.w);
+            acc[j][0] = fmaf(dg, t[0], acc[j][0]);
+            acc[j][1] = fmaf(dg, t[1], acc[j][1]);
+            acc[j][2] = fmaf(dg8, t[2], acc[j][2]);
+            acc[j][3] = fmaf(dg8, t[3], acc[j][3]);
+        }
+    }
+}
+
+template <int WT, int NT, int EPI, typename KV>
+__global__ void __launch_bounds__(kSkWarps * 32, 1) mv_sk_kernel(const MvParams p) {
+    constexpr int QB = tile_qbytes(WT);
+    constexpr int SB = WT == T_F16 ? 0 : kTileSBytes;
+    constexpr int KB = sk_kb(WT);
+    constexpr int R = sk_stages(WT);
+    constexpr int STAGE = sk_stage_bytes(WT);
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, c = lane & 3;
+    const int B = p.nseq;
+    const int nb = p.nb;
+
+    uint8_t* ring = smem + warp * R * STAGE;
+    uint8_t* xs = smem + kSkWarps * R * STAGE;
+    float* parts = reinterpret_cast<float*>(xs + (size_t)nb * B * 128);  // [warp][slot][16][B]
+    uint8_t* small = reinterpret_cast<uint8_t*>(parts + kSkWarps * kSkSlots * 16 * B);
+    int* tickets = reinterpret_cast<int*>(small);                        // [team leader][slot]
+    int* merged = tickets + kSkWarps * kSkSlots;                         // [team leader][slot] last merged tile + 1
+    float* wstat = reinterpret_cast<float*>(merged + kSkWarps * kSkSlots);  // [warps][B][2]
+    float* inv = wstat + kSkWarps * B * 2;                               // [B] rmsnorm 1/rms
+    float* xsc = inv + B;                                                // [B] power-of-two split scale
+    uint64_t* bars = reinterpret_cast<uint64_t*>(small + sk_small_bytes(B)) + warp * R;
+
+    // this CTA's tiles, this warp's team and K slice
+    const int k = sk_team(nb);
+    const int teams = kSkWarps / k, team = warp / k, wi = warp % k, leader = team * k;
+    const int t_lo = (int)((long long)blockIdx.x * p.ntiles / gridDim.x);
+    const int t_hi = (int)((long long)(blockIdx.x + 1) * p.ntiles / gridDim.x);
+    const int b_lo = wi * nb / k, b_hi = (wi + 1) * nb / k;  // slice of every tile
+    const int slice = b_hi - b_lo;
+    const int st_per_tile = (slice + KB - 1) / KB;
+    int my_tiles = 0;
+    for (int t = t_lo + team; t < t_hi; t += teams) ++my_tiles;
+    const int nst = my_tiles * st_per_tile;
+
+    // The warp's stages walk its tiles (t_lo + team + i*teams) and, within each,
+    // its slice in KB-block steps. Positions advance incrementally (no divisions).
+    int iss_ti = 0, iss_st = 0, iss_slot = 0;  // next stage to issue
+    auto issue = [&]() {
+        const int t = t_lo + team + iss_ti * teams;
+        const int b0 = b_lo + iss_st * KB;
+        const int n = min(KB, b_hi - b0);
+        const size_t first = (size_t)t * nb + b0;
+        uint8_t* dst = ring + iss_slot * STAGE;
+        mbar_expect_tx(bars + iss_slot, (uint32_t)(n * (QB + SB)));
+        bulk_g2s(dst, p.q + first * QB, (uint32_t)(n * QB), bars + iss_slot);
+        if (SB) bulk_g2s(dst + KB * QB, p.s + first * SB, (uint32_t)(n * SB), bars + iss_slot);
+        if (++iss_st == st_per_tile) { iss_st = 0; ++iss_ti; }
+        if (++iss_slot == R) iss_slot = 0;
+    };
+    int issued = 0;
+    if (lane == 0) {
+        for (int r = 0; r < R; ++r) mbar_init(bars + r, 1);
+        mbar_fence_init();
+        for (; issued < min(R, nst); ++issued) issue();
+    }
+    for (int i = threadIdx.x; i < 2 * kSkWarps * kSkSlots; i += blockDim.x) tickets[i] = 0;  // and merged[]
+    __syncwarp();
+    pdl_launch_dependents();
+    pdl_wait();
+
+    // ---- prologue: the whole activation vector -> binary16 hi/lo in fragment order
+    {
+        const int nv = p.in >> 2;  // float4 per sequence
+#pragma unroll
+        for (int s = 0; s < NT * 8; ++s) {
+            if (s < B) {
+                float ss = 0.f, mx = 0.f;
+                const float4* src = reinterpret_cast<const float4*>(p.x + (size_t)s * p.ldx);
+                const float4* nw4 = reinterpret_cast<const float4*>(p.norm_w);
+#pragma unroll 4
+                for (int f = threadIdx.x; f < nv; f += blockDim.x) {
+                    const float4 v = src[f];
+                    const float4 w = p.norm_w ? nw4[f] : make_float4(1.f, 1.f, 1.f, 1.f);
+                    ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+                    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x * w.x), fabsf(v.y * w.y)), fmaxf(fabsf(v.z * w.z), fabsf(v.w * w.w))));
+                }
+                ss = warp_sum(ss);
+                mx = warp_max(mx);
+                if (lane == 0) { wstat[(warp * B + s) * 2] = ss; wstat[(warp * B + s) * 2 + 1] = mx; }
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x < B) {
+            const int s = threadIdx.x;
+            float a = 0.f, m = 0.f;
+            for (int w = 0; w < kSkWarps; ++w) { a += wstat[(w * B + s) * 2]; m = fmaxf(m, wstat[(w * B + s) * 2 + 1]); }
+            const float iv = p.norm_w ? 1.f / sqrtf(a / float(p.in) + p.eps) : 1.f;
+            m *= iv;
+            int ex = 0;
+            if (m > 0.f && isfinite(m)) { frexpf(m, &ex); ex = max(-100, min(100, ex)); }
+            inv[s] = iv;
+            xsc[s] = ldexpf(1.f, ex - 11);  // max |x| * 2^(11-ex) lies in [2^10, 2^11)
+        }
+        __syncthreads();
+        __half* xh = reinterpret_cast<__half*>(xs);
+        for (int idx = threadIdx.x; idx < B * nv; idx += blockDim.x) {
+            const int s = idx / nv, f = idx % nv;
+            const float4 v4 = reinterpret_cast<const float4*>(p.x + (size_t)s * p.ldx)[f];
+            const float4 w4 = p.norm_w ? reinterpret_cast<const float4*>(p.norm_w)[f] : make_float4(1.f, 1.f, 1.f, 1.f);
+            const float vv[4] = {v4.x, v4.y, v4.z, v4.w}, ww[4] = {w4.x, w4.y, w4.z, w4.w};
+            const float up = 1.f / xsc[s];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int e = 4 * f + q;
+                float v = vv[q];
+                if (p.norm_w) v = v * (inv[s] * ww[q]);
+                v *= up;  // exact: a power of two
+                const __half hi = __float2half_rn(v);
+                const __half lo = __float2half_rn(v - __half2float(hi));
+                // column 2s holds the hi part of sequence s, column 2s+1 the lo part
+                __half* dst = xh + ((size_t)((e >> 5) * 2 * B + 2 * s) * 4 + ((e >> 3) & 3)) * 8;
+                dst[frag_pos(e & 7)] = hi;
+                dst[32 + frag_pos(e & 7)] = lo;
+            }
+        }
+        __syncthreads();
+    }
+
+    // ---- finish one tile: this warp's partial -> slot; the last of the team adds and runs the epilogue
+    float acc[NT][4];
+    auto finish = [&](int t, int tile_idx) {
+        const int slot = tile_idx % kSkSlots;
+        float* mine = parts + ((size_t)warp * kSkSlots + slot) * 16 * B;
+        if (tile_idx >= kSkSlots) {
+            // the slot's previous tile must be merged before this warp overwrites its partial
+            if (lane == 0) {
+                const long long t0 = clock64();
+                while (*reinterpret_cast<volatile int*>(merged + leader * kSkSlots + slot) < tile_idx - kSkSlots + 1) {
+                    if (clock64() - t0 > 2000000000LL) { atomicExch(p.err, 1); break; }
+                }
+            }
+            __syncwarp();
+        }
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+            const int sq = j * 4 + c;  // columns 2sq (hi) and 2sq+1 (lo)
+            if (sq < B) {
+                mine[g * B + sq] = acc[j][0] + acc[j][1];
+                mine[(g + 8) * B + sq] = acc[j][2] + acc[j][3];
+            }
+            acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+        }
+        __threadfence_block();
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) last = atomicAdd(tickets + leader * kSkSlots + slot, 1) == k - 1;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (!last) return;
+        __threadfence_block();
+        float* fin = mine;  // the team's sum is written over this warp's slot
+        for (int e = lane; e < 16 * B; e += 32) {
+            float v = 0.f;
+            for (int w = 0; w < k; ++w) v += parts[((size_t)(leader + w) * kSkSlots + slot) * 16 * B + e];
+            const int s = e % B;
+            fin[e] = v * xsc[s];
+        }
+        if (lane == 0) {
+            tickets[leader * kSkSlots + slot] = 0;
+            __threadfence_block();
+            merged[leader * kSkSlots + slot] = tile_idx + 1;
+        }
+        __syncwarp();
+        const int r0 = t * 16;
+        for (int e = lane; e < 16 * B; e += 32) {
+            const int rl = e / B, s = e % B, r = r0 + rl;
+            if (r >= p.rows) continue;
+            const float val = fin[e];
+            if (EPI == EPI_STORE) {
+                p.out[(size_t)s * p.ldo + r] = val;
+            } else if (EPI == EPI_ADD) {
+                p.out[(size_t)s * p.ldo + r] += val;
+            } else if (EPI == EPI_SWIGLU) {
+                if ((rl & 1) == 0) {
+                    const float up = fin[(rl + 1) * B + s];
+                    p.out[(size_t)s * p.ldo + (r >> 1)] = (val / (1.f + expf(-val))) * up;
+                }
+            } else {  // EPI_QKV
+                const int sl = p.slots[s], ps = p.pos[sl];
+                int rr = r, region = 0;
+                if (rr >= p.q_rows) { rr -= p.q_rows; region = 1; if (rr >= p.kv_rows) { rr -= p.kv_rows; region = 2; } }
+                const int d = rr % p.head_dim;
+                float o = val;
+                if (region < 2 && d < 2 * p.rope_pairs) {
+                    const float2 cs = p.rope_cs[(size_t)ps * p.rope_pairs + (d >> 1)];
+                    const float other = fin[(rl ^ 1) * B + s];
+                    // adjacent-pair rotation, unfused to keep the reference's rounding
+                    if ((d & 1) == 0) o = __fsub_rn(__fmul_rn(val, cs.x), __fmul_rn(other, cs.y));
+                    else o = __fadd_rn(__fmul_rn(other, cs.y), __fmul_rn(val, cs.x));
+                }
+                if (region == 0) {
+                    p.out[(size_t)s * p.ldo + rr] = o;
+                } else {
+                    KV* base = reinterpret_cast<KV*>(region == 1 ? p.kc : p.vc);
+                    base[(size_t)sl * p.kv_slot_stride + ((size_t)(rr / p.head_dim) * p.kv_cap + ps) * p.head_dim + d] =
+                        kv_from<KV>(o);
+                }
+            }
+        }
+        __syncwarp();
+    };
+
+    // ---- stream this warp's slices
+#pragma unroll
+    for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    // this lane's activation column in each n-tile
+    uint32_t xlane[NT];  // shared-memory addresses
+    const int xstride = 2 * B * 4 * 16;  // bytes between the records of consecutive blocks
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+        const int col = min(j * 8 + g, 2 * B - 1);
+        xlane[j] = smem_u32(xs) + (col * 4 + c) * 16;
+    }
+    const uint32_t ring_a = smem_u32(ring);
+    bool aborted = false;
+    int slot = 0, cur_ti = 0, cur_st = 0;
+    uint32_t phase = 0;
+    for (int s = 0; s < nst; ++s) {
+        if (!aborted && !mbar_wait(bars + slot, phase, p.err)) aborted = true;
+        const int b0 = b_lo + cur_st * KB;
+        const int n = aborted ? 0 : min(KB, b_hi - b0);
+        const uint32_t sq = ring_a + slot * STAGE;
+        const uint32_t ssc = sq + KB * QB;
+        if (n == KB) {
+#pragma unroll
+            for (int j = 0; j < KB; ++j) tile_block<WT, NT>(sq + j * QB, ssc + j * SB, xlane, b0 + j, xstride, lane, acc);
+        } else {
+            for (int j = 0; j < n; ++j) tile_block<WT, NT>(sq + j * QB, ssc + j * SB, xlane, b0 + j, xstride, lane, acc);
+        }
+        __syncwarp();
+        if (lane == 0 && !aborted && s + R < nst) {
+            fence_proxy_async_smem();  // this warp's reads of the slot precede the copy that refills it
+            issue();
+            ++issued;
+        }
+        if (++slot == R) { slot = 0; phase ^= 1u; }
+        if (++cur_st == st_per_tile) {
+            finish(t_lo + team + cur_ti * teams, cur_ti);
+            cur_st = 0;
+            ++cur_ti;
+        }
+    }
+    if (aborted && lane == 0) {
+        // leave only after the copies still in flight into this warp's ring have landed
+        for (int s = max(0, issued - R); s < issued; ++s) mbar_wait(bars + (s % R), (uint32_t)(s / R) & 1u, p.err);
+    }
+}
+
+}  // namespace laic
