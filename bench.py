@@ -260,6 +260,7 @@ def main() -> None:
     max_ms = allreduce_max(dev_ms, world)
     value = batch * args.steps * world / (max_ms / 1000.0)
     tok = ids[-1]
+    launches_chained = eng.stats().launches_per_step  # kernels per chained step, as timed
 
     # ---- end to end through laic_dev_step: host ids in, sampled ids out, every step
     ext = torch.cuda.ExternalStream(eng.stream, device=torch.device("cuda", local))
@@ -300,7 +301,7 @@ def main() -> None:
             "hbm_gbs_step": round((st.weight_bytes + kv_read) / (max_ms / args.steps * 1e-3) / 1e9, 1),
             "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s", "h2d_bytes_per_step": batch * (4 + 4 + 24),
                     "d2h_bytes_per_step": batch * 4},
-            "gpu_launches": int(args.steps * (st.launches_per_step + 1)),
+            "gpu_launches": int(args.steps * launches_chained),
             "roofline": {"bound": "hbm", "kernel": dname, "achieved": round(achieved, 1), "peak": peak,
                          "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
                          "bytes_per_launch": round(dbytes / dl), "us_per_launch": round(dus / dl, 3),

@@ -91,8 +91,8 @@ typedef struct laic_sample_params {
 typedef struct laic_dev_stats {
     uint64_t weight_bytes;      /* device bytes of weights read once per full step */
     uint64_t kv_bytes_per_pos;  /* KV bytes written per sequence per step (all layers, K+V) */
-    uint32_t launches_per_step; /* kernels in one full step */
-    uint32_t launches_per_prefill;
+    uint32_t launches_per_step; /* kernels in the most recently enqueued full step (chained: incl. the id record) */
+    uint32_t launches_per_prefill; /* kernels in the most recently enqueued prefill step */
     uint32_t attn_splits;       /* split-K factor of the last captured step */
     uint32_t tp_size;
 } laic_dev_stats;

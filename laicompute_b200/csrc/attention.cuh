@@ -131,18 +131,17 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
         for (int g = 0; g < GMAX; ++g) s[g] = 0.f;
         if (valid) {
             const KV* kr = kb + (size_t)t * D;
-#pragma unroll 4
-            for (int ch = 0; ch < D; ch += 8) {
-                float kf[8];
-                if constexpr (D >= 8) KvLoad<KV, 8>::load(kr + ch, kf);
+            // the whole key row first (all loads in flight), then the dot products
+            float kf[D];
 #pragma unroll
-                for (int g = 0; g < GMAX; ++g) {
-                    if (g < G) {
+            for (int ch = 0; ch < D; ch += 8) KvLoad<KV, 8>::load(kr + ch, kf + ch);
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) {
-                            if (EXACT) s[g] = __fadd_rn(s[g], __fmul_rn(qs[g][ch + j], kf[j]));
-                            else s[g] = fmaf(qs[g][ch + j], kf[j], s[g]);
-                        }
+            for (int g = 0; g < GMAX; ++g) {
+                if (g < G) {
+#pragma unroll
+                    for (int d = 0; d < D; ++d) {
+                        if (EXACT) s[g] = __fadd_rn(s[g], __fmul_rn(qs[g][d], kf[d]));
+                        else s[g] = fmaf(qs[g][d], kf[d], s[g]);
                     }
                 }
             }
@@ -167,10 +166,26 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
         }
         __syncwarp();
         const int cnt = min(32, t1 - base);
-#pragma unroll 4
-        for (int j = 0; j < cnt; ++j) {
+        const KV* vrow = vb + (size_t)base * D + lane * DPL;
+        int j = 0;
+        for (; j + 8 <= cnt; j += 8) {  // eight value rows in flight
+            float vf[8][DPL];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) KvLoad<KV, DPL>::load(vrow + (size_t)(j + u) * D, vf[u]);
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+#pragma unroll
+                for (int g = 0; g < GMAX; ++g) {
+                    if (g < G) {
+                        const float pj = ps[warp][g][j + u];
+#pragma unroll
+                        for (int k = 0; k < DPL; ++k) acc[g][k] = fmaf(pj, vf[u][k], acc[g][k]);
+                    }
+                }
+        }
+        for (; j < cnt; ++j) {
             float vf[DPL];
-            KvLoad<KV, DPL>::load(vb + (size_t)(base + j) * D + lane * DPL, vf);
+            KvLoad<KV, DPL>::load(vrow + (size_t)j * D, vf);
 #pragma unroll
             for (int g = 0; g < GMAX; ++g) {
                 if (g < G) {

@@ -185,32 +185,76 @@ MvShape mv_shape(const Mat& m, int B) {
     return sh;
 }
 
-// Split-K scratch shared by every matvec launch of a stream (launches are serialised).
+// Scratch shared by every matvec launch of a stream (launches are serialised):
+// split-K partials and tickets, and the prepared activations of the tile kernel.
 struct MvScratch {
     float* part = nullptr;
     unsigned* tile_cnt = nullptr;
     int* err = nullptr;
-    size_t part_cap = 0, cnt_cap = 0;
+    uint8_t* xg = nullptr;
+    float* xinv = nullptr;
+    size_t part_cap = 0, cnt_cap = 0, xg_cap = 0, xinv_cap = 0;
 };
 
-int mv_scratch_reserve(MvScratch& sc, size_t part_floats, size_t ntiles) {
+struct MvNeed {  // scratch one launch shape needs
+    size_t part_floats = 0, ntiles = 0, xg_bytes = 0, xinv_floats = 0;
+    void merge(const MvNeed& o) {
+        part_floats = std::max(part_floats, o.part_floats);
+        ntiles = std::max(ntiles, o.ntiles);
+        xg_bytes = std::max(xg_bytes, o.xg_bytes);
+        xinv_floats = std::max(xinv_floats, o.xinv_floats);
+    }
+};
+
+MvNeed mv_need(const Mat& m, int B) {
+    const MvShape sh = mv_shape(m, B);
+    MvNeed n;
+    n.part_floats = sh.part_floats;
+    n.ntiles = (size_t)m.ntiles;
+    if (!sh.sk) {
+        n.xg_bytes = (size_t)m.nb * B * 128;
+        n.xinv_floats = (size_t)sh.nk * B;
+    }
+    return n;
+}
+
+// Grow the scratch to `need`; returns whether any buffer moved (captured graphs are stale then).
+int mv_scratch_reserve(MvScratch& sc, const MvNeed& need, bool* moved = nullptr) {
+    bool mv = false;
     if (!sc.err) {
         CK(cudaMalloc(&sc.err, 4));
         CK(cudaMemset(sc.err, 0, 4));
     }
-    if (part_floats > sc.part_cap) {
+    if (need.part_floats > sc.part_cap) {
         if (sc.part) cudaFree(sc.part);
         sc.part = nullptr;
-        CK(cudaMalloc(&sc.part, part_floats * 4));
-        sc.part_cap = part_floats;
+        CK(cudaMalloc(&sc.part, need.part_floats * 4));
+        sc.part_cap = need.part_floats;
+        mv = true;
     }
-    if (ntiles > sc.cnt_cap) {
+    if (need.ntiles > sc.cnt_cap) {
         if (sc.tile_cnt) cudaFree(sc.tile_cnt);
         sc.tile_cnt = nullptr;
-        CK(cudaMalloc(&sc.tile_cnt, ntiles * 4));
-        CK(cudaMemset(sc.tile_cnt, 0, ntiles * 4));
-        sc.cnt_cap = ntiles;
+        CK(cudaMalloc(&sc.tile_cnt, need.ntiles * 4));
+        CK(cudaMemset(sc.tile_cnt, 0, need.ntiles * 4));
+        sc.cnt_cap = need.ntiles;
+        mv = true;
     }
+    if (need.xg_bytes > sc.xg_cap) {
+        if (sc.xg) cudaFree(sc.xg);
+        sc.xg = nullptr;
+        CK(cudaMalloc(&sc.xg, need.xg_bytes));
+        sc.xg_cap = need.xg_bytes;
+        mv = true;
+    }
+    if (need.xinv_floats > sc.xinv_cap) {
+        if (sc.xinv) cudaFree(sc.xinv);
+        sc.xinv = nullptr;
+        CK(cudaMalloc(&sc.xinv, need.xinv_floats * 4));
+        sc.xinv_cap = need.xinv_floats;
+        mv = true;
+    }
+    if (moved) *moved = mv;
     return LAIC_OK;
 }
 
@@ -218,19 +262,29 @@ void mv_scratch_free(MvScratch& sc) {
     if (sc.part) cudaFree(sc.part);
     if (sc.tile_cnt) cudaFree(sc.tile_cnt);
     if (sc.err) cudaFree(sc.err);
+    if (sc.xg) cudaFree(sc.xg);
+    if (sc.xinv) cudaFree(sc.xinv);
     sc = MvScratch{};
 }
 
+// One projection: the team kernel for small batches, else activation
+// preparation + tile kernel. `launches` counts the kernels enqueued.
 cudaError_t launch_matvec(const Mat& m, laic::MvParams p, int epi, bool kv32, const MvScratch& sc, cudaStream_t st,
-                          bool pdl) {
+                          bool pdl, int* launches = nullptr) {
     const MvShape sh = mv_shape(m, p.nseq);
     p.q = m.q; p.s = m.s; p.rows = m.rows; p.ntiles = m.ntiles; p.in = m.in; p.nb = m.nb;
     if (sh.sk) {
         p.err = sc.err;
+        if (launches) *launches += 1;
         return laic::mv_sk_launch(m.type, sh.nt, epi, kv32, p, sh.grid, sh.smem, st, pdl);
     }
+    laic::XPrepParams xp{p.x, p.ldx, p.norm_w, p.eps, m.in, m.nb, p.nseq, sh.kr, sc.xg, sc.xinv};
+    cudaError_t e = laic::xprep_launch(xp, sh.nk, st, pdl);
+    if (e != cudaSuccess) return e;
     p.nk = sh.nk; p.kr = sh.kr; p.kb = sh.kb; p.stages = sh.stages;
     p.part = sc.part; p.tile_cnt = sc.tile_cnt; p.err = sc.err;
+    p.xg = sc.xg; p.xinvg = sc.xinv;
+    if (launches) *launches += 2;
     return laic::mv_launch(m.type, sh.nt, epi, kv32, p, sh.grid, sh.smem, st, pdl);
 }
 
@@ -308,7 +362,7 @@ struct laic_dev {
     // ------------------------------------------------------------------
     int nsplit_for(int nseq) const {
         const int pairs = nseq * Hkv;
-        int s = (2 * num_sms() + pairs - 1) / pairs;
+        int s = (8 * num_sms() + pairs - 1) / pairs;  // about eight CTAs per SM
         return std::max(1, std::min(s, max_split));
     }
 
@@ -329,6 +383,7 @@ struct laic_dev {
     }
 
     const Mat& lm_head() const { return have_out ? lm : embd; }
+    int launches_step = 0, launches_prefill = 0;  // kernels in the last enqueued step / prefill
 
     // Enqueue one step. `timer` (nullable) records events around launches for profiling.
     struct Timer {
@@ -339,6 +394,7 @@ struct laic_dev {
     int enqueue(int nseq, int mode, cudaStream_t s, Timer* timer) {
         const bool full = mode != MODE_PREFILL;
         const bool pdl = use_pdl && !timer;
+        int nl = 0;  // kernels enqueued
         auto t_begin = [&](const char* name, double b) {
             if (!timer) return;
             cudaEvent_t e0, e1;
@@ -360,6 +416,7 @@ struct laic_dev {
         laic::EmbedParams ep{embd.type, embd.q, embd.s, h, embd.nb, d_tokens, d_slots, x, counts, V};
         t_begin("embed", 0);
         CK(launch_k(laic::embed_kernel, dim3(nseq), dim3(256), 0, s, pdl, ep));
+        ++nl;
         t_end();
 
         const int nsplit = nsplit_for(nseq);
@@ -384,7 +441,7 @@ struct laic_dev {
             p.vc = (char*)vc + (size_t)l * kv_layer_stride * kvb;
             p.kv_slot_stride = kv_slot_stride; p.kv_cap = cap;
             t_begin("qkv", (double)ly.qkv.bytes() + 4.0 * nseq * (h + ly.qkv.rows));
-            CK(launch_matvec(ly.qkv, p, laic::EPI_QKV, kv32, mvs, s, pdl));
+            CK(launch_matvec(ly.qkv, p, laic::EPI_QKV, kv32, mvs, s, pdl, &nl));
             t_end();
             // attention
             laic::AttnParams ap{};
@@ -394,62 +451,66 @@ struct laic_dev {
             ap.part = attn_part; ap.counters = attn_cnt; ap.sqrt_d = sqrtf((float)D);
             t_begin("attention", attn_bytes);
             CK(launch_k(afn, dim3(nsplit, Hkv, nseq), dim3(laic::kAttnWarps * 32), 0, s, pdl, ap));
+            ++nl;
             t_end();
             // o + residual
             laic::MvParams po{};
             po.nseq = nseq; po.x = attn; po.ldx = h; po.out = x; po.ldo = h;
             t_begin("o", (double)ly.o.bytes() + 12.0 * nseq * h);
-            CK(launch_matvec(ly.o, po, laic::EPI_ADD, kv32, mvs, s, pdl));
+            CK(launch_matvec(ly.o, po, laic::EPI_ADD, kv32, mvs, s, pdl, &nl));
             t_end();
             // gate/up + swiglu
             laic::MvParams pg{};
             pg.nseq = nseq; pg.eps = a.rms_eps; pg.x = x; pg.ldx = h; pg.norm_w = ly.ffn_norm; pg.out = act; pg.ldo = F;
             t_begin("gate_up", (double)ly.gu.bytes() + 4.0 * nseq * (h + F));
-            CK(launch_matvec(ly.gu, pg, laic::EPI_SWIGLU, kv32, mvs, s, pdl));
+            CK(launch_matvec(ly.gu, pg, laic::EPI_SWIGLU, kv32, mvs, s, pdl, &nl));
             t_end();
             // down + residual
             laic::MvParams pd{};
             pd.nseq = nseq; pd.x = act; pd.ldx = F; pd.out = x; pd.ldo = h;
             t_begin("down", (double)ly.down.bytes() + 4.0 * nseq * (F + 2 * h));
-            CK(launch_matvec(ly.down, pd, laic::EPI_ADD, kv32, mvs, s, pdl));
+            CK(launch_matvec(ly.down, pd, laic::EPI_ADD, kv32, mvs, s, pdl, &nl));
             t_end();
         }
         if (full) {
             laic::MvParams pl{};
             pl.nseq = nseq; pl.eps = a.rms_eps; pl.x = x; pl.ldx = h; pl.norm_w = out_norm; pl.out = logits; pl.ldo = V;
             t_begin("lm_head", (double)lm_head().bytes() + 4.0 * nseq * (h + V));
-            CK(launch_matvec(lm_head(), pl, laic::EPI_STORE, kv32, mvs, s, pdl));
+            CK(launch_matvec(lm_head(), pl, laic::EPI_STORE, kv32, mvs, s, pdl, &nl));
             t_end();
             laic::SamplerParams sp{logits, V, V, d_slots, counts, d_params, nseq, d_out_ids, d_tokens, pos, d_err};
             t_begin("sampler", (double)nseq * V * 4);
             CK(launch_k(laic::sample_kernel, dim3(nseq), dim3(laic::kSampleThreads), 0, s, pdl, sp));
+            ++nl;
             t_end();
             if (mode == MODE_CHAIN)
+            {
                 CK(launch_k(laic::record_ids_kernel, dim3(1), dim3(256), 0, s, pdl, (const unsigned*)d_out_ids, d_hist,
                             d_hist_count, nseq));
-            else
+                ++nl;
+            } else
                 CK(cudaMemcpyAsync(h_out_ids, d_out_ids, nseq * sizeof(unsigned), cudaMemcpyDeviceToHost, s));
         } else {
             t_begin("advance", 0);
             CK(launch_k(laic::advance_pos_kernel, dim3(1), dim3(256), 0, s, pdl, (const int*)d_slots, pos, nseq));
+            ++nl;
             t_end();
         }
+        (full ? launches_step : launches_prefill) = nl;
         return LAIC_OK;
     }
 
-    // Size the split-K scratch for `nseq` sequences (before any capture).
+    // Size the matvec scratch for `nseq` sequences (before any capture).
     int reserve_scratch(int nseq) {
-        size_t part = 0, tiles = 0;
+        MvNeed need;
         auto see = [&](const Mat& m) {
-            if (!m.q) return;
-            part = std::max(part, mv_shape(m, nseq).part_floats);
-            tiles = std::max(tiles, (size_t)m.ntiles);
+            if (m.q) need.merge(mv_need(m, nseq));
         };
         for (auto& l : layers) { see(l.qkv); see(l.o); see(l.gu); see(l.down); }
         see(lm_head());
-        const bool grows = part > mvs.part_cap || tiles > mvs.cnt_cap;
-        int rc = mv_scratch_reserve(mvs, part, tiles);
-        if (!rc && grows) {  // graphs captured the old buffers
+        bool moved = false;
+        int rc = mv_scratch_reserve(mvs, need, &moved);
+        if (!rc && moved) {  // graphs captured the old buffers
             for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
             graphs.clear();
         }
@@ -843,8 +904,8 @@ int laic_dev_stats_get(laic_dev* d, laic_dev_stats* s) {
     wb += d->lm_head().bytes() + 4ull * d->h;
     s->weight_bytes = wb;
     s->kv_bytes_per_pos = (uint64_t)d->L * d->kv * 2 * (d->kv32 ? 4 : 2);
-    s->launches_per_step = 1 + 5 * d->L + 2;  // embed, 5 per layer, lm_head, sampler
-    s->launches_per_prefill = 1 + 5 * d->L + 1;
+    s->launches_per_step = d->launches_step;  // of the most recently enqueued step (chained: + id record)
+    s->launches_per_prefill = d->launches_prefill;
     s->attn_splits = d->last_split;
     s->tp_size = 1;
     return LAIC_OK;
@@ -981,8 +1042,7 @@ int laic_tensor_matvec(laic_tensor* t, const float* x, float* y, int32_t batch, 
     if (!t || !x || !y || batch < 1) return fail(LAIC_E_INVALID, "bad argument");
     CK(cudaSetDevice(t->device));
     if (batch > 64) return fail(LAIC_E_UNSUPPORTED, "at most 64 sequences per matvec");
-    const MvShape sh = mv_shape(t->m, batch);
-    int rc = mv_scratch_reserve(t->sc, sh.part_floats, (size_t)t->m.ntiles);
+    int rc = mv_scratch_reserve(t->sc, mv_need(t->m, batch));
     if (rc) return rc;
     laic::MvParams p{};
     p.nseq = batch; p.x = x; p.ldx = t->m.in; p.out = y; p.ldo = t->m.rows;

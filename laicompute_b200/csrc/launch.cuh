@@ -25,6 +25,9 @@ cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sme
 }
 
 struct MvParams;
+struct XPrepParams;
+// Launch the activation preparation of the tile kernel: grid (nk, nseq).
+cudaError_t xprep_launch(const XPrepParams& p, int nk, cudaStream_t st, bool pdl);
 // Launch the fragment-tile matvec for one weight type (defined in mv_<type>.cu).
 cudaError_t mv_launch(int type, int nt, int epi, bool kv32, const MvParams& p, int grid, size_t smem, cudaStream_t st,
                       bool pdl);

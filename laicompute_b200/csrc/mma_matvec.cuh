@@ -63,6 +63,21 @@ struct MvParams {
     void* vc;                  // this layer's V cache
     long long kv_slot_stride;  // elements between slots
     int kv_cap;
+    // tile kernel: activations already split by xprep_kernel
+    const uint8_t* xg;         // [nb][nseq][4][32 B] binary16 hi/lo in fragment order
+    const float* xinvg;        // [nk][nseq] power-of-two scale of each K split
+};
+
+// Activation preparation for the tile kernel (one launch before it).
+struct XPrepParams {
+    const float* x;            // [nseq][ldx]
+    int ldx;
+    const float* norm_w;       // rmsnorm weight [in] (nullptr: no norm)
+    float eps;
+    int in, nb, nseq;
+    int kr;                    // blocks per K split of the consuming matvec
+    uint8_t* xg;               // out: [nb][nseq][4][32 B]
+    float* xinv;               // out: [nk][nseq]
 };
 
 // ---------------------------------------------------------------------------
@@ -223,10 +238,10 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_mma_kernel(const MvParams p)
     float* red = reinterpret_cast<float*>(xs + (size_t)p.kr * B * 128);  // [8 warps][16][NT*8]
     float* fin = red + kConsumerWarps * 16 * NT * 8;                  // [16][B]
     float* xinv = fin + 16 * B;                                       // [B] 1/scale of each sequence
-    float* xnrm = xinv + NT * 8;                                      // [B] rmsnorm inv
-    uint64_t* full = reinterpret_cast<uint64_t*>(xnrm + NT * 8);
+    uint64_t* full = reinterpret_cast<uint64_t*>(xinv + NT * 8 + 2);  // 8-byte aligned
     uint64_t* empty = full + p.stages;
-    int* ticket = reinterpret_cast<int*>(empty + p.stages);
+    uint64_t* xbar = empty + p.stages;                                // the activation copy
+    int* ticket = reinterpret_cast<int*>(xbar + 1);
 
     const int k_split = blockIdx.x % p.nk;
     const int cta_per_k = gridDim.x / p.nk;
@@ -238,6 +253,7 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_mma_kernel(const MvParams p)
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < p.stages; ++i) { mbar_init(full + i, 1); mbar_init(empty + i, kConsumerWarps); }
+        mbar_init(xbar, 1);
         mbar_fence_init();
     }
     __syncthreads();
@@ -245,12 +261,24 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_mma_kernel(const MvParams p)
     if (warp == kConsumerWarps) {
         // ---------------- producer: stream this CTA's tile-blocks ----------------
         if (lane == 0 && nblk > 0) {
+            // The weights do not depend on the previous kernel: fill the ring
+            // first, then wait for the activations (programmatic dependency)
+            // before the first blocking wait on a ring slot.
+            bool x_issued = false;
+            auto issue_x = [&]() {
+                pdl_wait();
+                const uint32_t xb = (uint32_t)nblk * B * 128;
+                mbar_expect_tx(xbar, xb);
+                bulk_g2s(xs, p.xg + (size_t)b_lo * B * 128, xb, xbar);
+                x_issued = true;
+            };
             int it = 0;
             bool ok = true;
             for (int t = t_first; t < p.ntiles && ok; t += cta_per_k) {
                 for (int st = 0; st < stages_per_tile; ++st, ++it) {
                     const int slot = it % p.stages;
                     const uint32_t ph = (uint32_t)(it / p.stages) & 1u;
+                    if (!x_issued && it >= p.stages) issue_x();
                     if (!mbar_wait(empty + slot, ph ^ 1u, p.err)) { ok = false; break; }
                     const int b0 = b_lo + st * p.kb;
                     const int n = min(p.kb, b_hi - b0);
@@ -261,10 +289,12 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_mma_kernel(const MvParams p)
                     if (SB) bulk_g2s(dst + p.kb * QB, p.s + tb * SB, (uint32_t)(n * SB), full + slot);
                 }
             }
+            if (!x_issued) issue_x();
             // leave only after every copy issued into this CTA's shared memory has landed
             const int issued = it;
             for (int j = max(0, issued - p.stages); j < issued; ++j)
                 mbar_wait(full + (j % p.stages), (uint32_t)(j / p.stages) & 1u, p.err);
+            mbar_wait(xbar, 0u, p.err);
         }
         return;
     }
@@ -274,56 +304,14 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_mma_kernel(const MvParams p)
     constexpr int NC = kConsumerWarps * 32;
     pdl_wait();
 
-    // prologue: activations of this K split -> binary16 hi/lo in fragment order
-    {
-        if (p.norm_w) {
-            for (int s = warp; s < B; s += kConsumerWarps) {
-                const float* src = p.x + (size_t)s * p.ldx;
-                float ss = 0.f;
-                for (int e = lane; e < p.in; e += 32) { const float v = src[e]; ss = fmaf(v, v, ss); }
-                ss = warp_sum(ss);
-                if (lane == 0) xnrm[s] = 1.f / sqrtf(ss / float(p.in) + p.eps);
-            }
-            named_sync(1, NC);
-        }
-        // per-sequence power-of-two scale so the largest |x| of this split sits in [2^10, 2^11)
-        for (int s = warp; s < B; s += kConsumerWarps) {
-            const float* src = p.x + (size_t)s * p.ldx;
-            float m = 0.f;
-            for (int e = b_lo * 32 + lane; e < b_hi * 32; e += 32) {
-                float v = src[e];
-                if (p.norm_w) v = v * (xnrm[s] * p.norm_w[e]);
-                m = fmaxf(m, fabsf(v));
-            }
-            m = warp_max(m);
-            if (lane == 0) {
-                int ex = 0;
-                if (m > 0.f && isfinite(m)) { frexpf(m, &ex); ex = max(-100, min(100, ex)); }
-                xinv[s] = ldexpf(1.f, ex - 11);  // m * 2^(11-ex) in [2^10, 2^11)
-            }
-        }
-        named_sync(1, NC);
-        __half* xh = reinterpret_cast<__half*>(xs);
-        const int ne = nblk * 32;
-        for (int i = ctid; i < ne * B; i += NC) {
-            const int s = i / ne, el = i % ne;
-            const int e = b_lo * 32 + el;
-            float v = p.x[(size_t)s * p.ldx + e];
-            if (p.norm_w) v = v * (xnrm[s] * p.norm_w[e]);
-            v = v * (1.f / xinv[s]);  // exact: a power of two
-            const __half hi = __float2half_rn(v);
-            const __half lo = __float2half_rn(v - __half2float(hi));
-            const int bl = el >> 5, cc = (el >> 3) & 3, k = el & 7;
-            __half* dst = xh + ((size_t)(bl * B + s) * 4 + cc) * 16;
-            dst[frag_pos(k)] = hi;
-            dst[8 + frag_pos(k)] = lo;
-        }
-        named_sync(1, NC);
-    }
+    // activations of this K split: the producer's bulk copy of the prepared
+    // records, plus the split's scale per sequence
+    bool aborted = nblk > 0 && !mbar_wait(xbar, 0u, p.err);
+    for (int s = ctid; s < B; s += NC) xinv[s] = p.xinvg[(size_t)k_split * B + s];
+    named_sync(1, NC);
     pdl_launch_dependents();
 
-    int it = 0;
-    bool aborted = false;  // a wait ran out: keep the barrier protocol, skip the math
+    int it = 0;  // `aborted`: a wait ran out: keep the barrier protocol, skip the math
     for (int t = t_first; t < p.ntiles; t += cta_per_k) {
         float acc[NT][4];
 #pragma unroll
@@ -466,6 +454,86 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_mma_kernel(const MvParams p)
             }
         }
         named_sync(1, NC);  // fin/red reused by the next tile
+    }
+}
+
+// ---------------------------------------------------------------------------
+// activation preparation: grid (nk, nseq), one CTA per (K split, sequence)
+// ---------------------------------------------------------------------------
+// rmsnorm (when norm_w is set) of the sequence's row, a power-of-two scale
+// per K split that puts the split's max |x| into [2^10, 2^11), and the scaled
+// values as binary16 hi + lo in the tile kernel's fragment order.
+constexpr int kXPrepThreads = 256;
+
+static __global__ void __launch_bounds__(kXPrepThreads) xprep_kernel(const XPrepParams p) {
+    __shared__ float red[kXPrepThreads / 32][2];
+    __shared__ float stat[2];
+    pdl_launch_dependents();  // the matvec may start streaming its weights
+    pdl_wait();
+    const int k = blockIdx.x, s = blockIdx.y;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int b_lo = k * p.kr, b_hi = min(p.nb, b_lo + p.kr);
+    const int nv = p.in >> 2, v_lo = b_lo * 8, v_hi = b_hi * 8;  // float4 indices
+    const float4* x4 = reinterpret_cast<const float4*>(p.x + (size_t)s * p.ldx);
+    const float4* w4 = reinterpret_cast<const float4*>(p.norm_w);
+    float ss = 0.f, mx = 0.f;
+    if (p.norm_w) {
+        for (int f = threadIdx.x; f < nv; f += kXPrepThreads) {
+            const float4 v = x4[f];
+            ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+            if (f >= v_lo && f < v_hi) {
+                const float4 w = w4[f];
+                mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x * w.x), fabsf(v.y * w.y)), fmaxf(fabsf(v.z * w.z), fabsf(v.w * w.w))));
+            }
+        }
+    } else {
+        for (int f = v_lo + threadIdx.x; f < v_hi; f += kXPrepThreads) {
+            const float4 v = x4[f];
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        }
+    }
+    ss = warp_sum(ss);
+    mx = warp_max(mx);
+    if (lane == 0) { red[warp][0] = ss; red[warp][1] = mx; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float a = 0.f, m = 0.f;
+        for (int w = 0; w < kXPrepThreads / 32; ++w) { a += red[w][0]; m = fmaxf(m, red[w][1]); }
+        const float iv = p.norm_w ? 1.f / sqrtf(a / float(p.in) + p.eps) : 1.f;
+        m *= iv;
+        int ex = 0;
+        if (m > 0.f && isfinite(m)) { frexpf(m, &ex); ex = max(-100, min(100, ex)); }
+        const float xi = ldexpf(1.f, ex - 11);
+        stat[0] = iv;
+        stat[1] = xi;
+        p.xinv[(size_t)k * p.nseq + s] = xi;
+    }
+    __syncthreads();
+    const float iv = stat[0], up = 1.f / stat[1];  // exact: a power of two
+    // one 8-element group (one lane's fragment record) per thread
+    const int ng = (b_hi - b_lo) * 4;
+    for (int gi = threadIdx.x; gi < ng; gi += kXPrepThreads) {
+        const int f = v_lo + 2 * gi;
+        const float4 a0 = x4[f], a1 = x4[f + 1];
+        float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        if (p.norm_w) {
+            const float4 c0 = w4[f], c1 = w4[f + 1];
+            const float w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] = v[e] * (iv * w[e]);
+        }
+        __align__(16) __half hi[8], lo[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const float u = v[e] * up;
+            const __half h = __float2half_rn(u);
+            hi[frag_pos(e)] = h;
+            lo[frag_pos(e)] = __float2half_rn(u - __half2float(h));
+        }
+        const int bl = b_lo + (gi >> 2), c = gi & 3;
+        uint4* dst = reinterpret_cast<uint4*>(p.xg + (((size_t)bl * p.nseq + s) * 4 + c) * 32);
+        dst[0] = *reinterpret_cast<const uint4*>(hi);
+        dst[1] = *reinterpret_cast<const uint4*>(lo);
     }
 }
 

@@ -34,6 +34,10 @@ cudaError_t mv_launch(int type, int nt, int epi, bool kv32, const MvParams& p, i
     return launch_k(mv_kernel(type, nt, epi, kv32), dim3(grid), dim3(kMvThreads), smem, st, pdl, p);
 }
 
+cudaError_t xprep_launch(const XPrepParams& p, int nk, cudaStream_t st, bool pdl) {
+    return launch_k(xprep_kernel, dim3(nk, p.nseq), dim3(kXPrepThreads), 0, st, pdl, p);
+}
+
 cudaError_t mv_set_attributes() {
     for (int type : {T_Q4_0, T_Q8_0, T_F16})
         for (int nt : {1, 2, 4, 8})
