@@ -178,6 +178,22 @@ LAIC_API int laic_tensor_dequant(laic_tensor* t, float* out_dev, void* stream);
 /* Device bytes of the tensor's blocks (the algorithmic bytes of one matvec). */
 LAIC_API uint64_t laic_tensor_bytes(laic_tensor* t);
 
+/* Bytes of the fixed working-memory array behind laic_tensor_matvec_noalloc (per device). */
+#define LAIC_FIXED_SCRATCH_BYTES (8u << 20)
+/* Same product as laic_tensor_matvec, for hosts that must not allocate device
+ * memory once they are serving: the call takes no memory from the CUDA
+ * allocator (laic_tensor_matvec grows a per-tensor scratch on demand). Its
+ * working memory is one array of LAIC_FIXED_SCRATCH_BYTES compiled into the
+ * library; a matrix/batch that needs more returns LAIC_E_INVALID with the size
+ * in laic_last_error(). The first call on a device looks up the array's address
+ * (setup) and should come before any stream capture. All calls on a device
+ * share the array, which keeps the last call's contents (the parts that must
+ * start at zero are cleared on `stream` by every call); calls that overlap in
+ * time race on it, so order them on one stream. No counterpart in the
+ * reference, whose matvec runs on the host. */
+LAIC_API int laic_tensor_matvec_noalloc(laic_tensor* t, const float* x_dev, float* y_dev, int32_t batch,
+                                        void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -23,6 +23,7 @@
 #include <cstring>
 #include <map>
 #include <memory>
+#include <mutex>
 #include <random>
 #include <string>
 #include <vector>
@@ -1056,6 +1057,86 @@ int laic_tensor_dequant(laic_tensor* t, float* out, void* stream) {
     laic::tile_dequant_kernel<<<1184, 256, 0, (cudaStream_t)stream>>>(t->m.type, t->m.q, t->m.s, t->m.in, t->m.nb,
                                                                        t->m.rows, out);
     CK(cudaGetLastError());
+    return LAIC_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// laic_tensor_matvec_noalloc: the single-tensor product with fixed working memory
+// ---------------------------------------------------------------------------
+// Some hosts hand all device memory to their own arena at start-up (weights,
+// KV cache) and must not call the CUDA allocator afterwards: cudaMalloc and
+// cudaFree may synchronise the device and stall every stream, and a failed
+// allocation in the middle of a request cannot be recovered there. For them
+// the entry point below takes its working memory (split-K partials and
+// tickets, prepared activations, error flag) from one array compiled into
+// this library instead of from the allocator.
+//
+// The array is shared by every call on a device and keeps whatever the last
+// call left in it; the ticket counters and the error flag, which must start
+// at zero, are cleared on the stream at the start of every call. Two calls
+// whose kernels overlap in time (different streams, or host threads without
+// ordering) race on the array.
+namespace {
+
+constexpr size_t kFixedScratchBytes = LAIC_FIXED_SCRATCH_BYTES;
+static __device__ __align__(256) unsigned char g_fixed_scratch[kFixedScratchBytes];
+
+constexpr int kFixedMaxDevices = 64;
+std::mutex g_fixed_mu;
+unsigned char* g_fixed_base[kFixedMaxDevices] = {};
+
+// Device address of the array on `device` (which must be current); looked up
+// once per device, at that device's first call.
+int fixed_scratch_base(int device, unsigned char** base) {
+    if (device < 0 || device >= kFixedMaxDevices) return fail(LAIC_E_INVALID, "device ordinal out of range");
+    std::lock_guard<std::mutex> lock(g_fixed_mu);
+    if (!g_fixed_base[device]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_fixed_scratch);
+        if (e != cudaSuccess) return fail(LAIC_E_CUDA, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+        g_fixed_base[device] = static_cast<unsigned char*>(p);
+    }
+    *base = g_fixed_base[device];
+    return LAIC_OK;
+}
+
+size_t round256(size_t n) { return (n + 255) / 256 * 256; }
+
+}  // namespace
+
+extern "C" {
+
+int laic_tensor_matvec_noalloc(laic_tensor* t, const float* x, float* y, int32_t batch, void* stream) {
+    if (!t || !x || !y || batch < 1) return fail(LAIC_E_INVALID, "bad argument");
+    CK(cudaSetDevice(t->device));
+    if (batch > 64) return fail(LAIC_E_UNSUPPORTED, "at most 64 sequences per matvec");
+    const MvNeed need = mv_need(t->m, batch);
+    // carve: [error flag | tickets] (cleared each call) [partials] [activations] [split scales]
+    const size_t zero_bytes = 256 + round256(need.ntiles * 4);
+    const size_t part_off = zero_bytes;
+    const size_t xg_off = part_off + round256(need.part_floats * 4);
+    const size_t xinv_off = xg_off + round256(need.xg_bytes);
+    const size_t total = xinv_off + round256(need.xinv_floats * 4);
+    if (total > kFixedScratchBytes)
+        return fail(LAIC_E_INVALID, "laic_tensor_matvec_noalloc: this matrix at batch " + std::to_string(batch) +
+                                        " needs " + std::to_string(total) + " bytes of working memory, more than the " +
+                                        std::to_string(kFixedScratchBytes) + " bytes of the fixed array");
+    unsigned char* base = nullptr;
+    int rc = fixed_scratch_base(t->device, &base);
+    if (rc) return rc;
+    const cudaStream_t st = (cudaStream_t)stream;
+    CK(cudaMemsetAsync(base, 0, zero_bytes, st));
+    MvScratch sc;
+    sc.err = reinterpret_cast<int*>(base);
+    sc.tile_cnt = reinterpret_cast<unsigned*>(base + 256);
+    sc.part = reinterpret_cast<float*>(base + part_off);
+    sc.xg = base + xg_off;
+    sc.xinv = reinterpret_cast<float*>(base + xinv_off);
+    laic::MvParams p{};
+    p.nseq = batch; p.x = x; p.ldx = t->m.in; p.out = y; p.ldo = t->m.rows;
+    CK(launch_matvec(t->m, p, laic::EPI_STORE, false, sc, st, false));
     return LAIC_OK;
 }
 
