@@ -42,7 +42,12 @@ WORKLOADS = {
     "smollm135m-q8_0": (synth.SMOL_135M_Q8, 2, 128, 64, "SmolLM-135M-shaped Llama, Q8_0 projections"),
     "smollm135m-f16": (synth.SMOL_135M_F16, 1, 8, 1, "SmolLM-135M-shaped Llama, F16"),
     "llama1b-q4_0": (synth.LLAMA_1B_Q4, 4, 512, 32, "1B-shaped Llama, Q4_0 projections, F16 embeddings"),
+    "llama8b-q4_0": (synth.LLAMA_8B_Q4, 5, 1024, 1, "8B-shaped Llama, Q4_0 projections, tied Q4_0 embeddings"),
 }
+# KV positions allocated per slot, where the workload asks for more than it decodes
+KV_CAPACITY = {"llama8b-q4_0": 8192}
+# CPU sample of the large models: (prompt tokens, timed decode steps) — a reference step takes seconds
+CPU_SAMPLE = {"llama1b-q4_0": (64, 16), "llama8b-q4_0": (32, 8)}
 DEFAULT_WORKLOAD = "smollm135m-q8_0"
 
 
@@ -62,7 +67,8 @@ def model_path(name: str, rank: int) -> str:
     path = os.path.join(d, f"{name}.seed{seed}.r{rank}.gguf")
     if not os.path.exists(path):
         tmp = path + ".part"
-        synth.write_model(tmp, arch, seed=seed)
+        # quantised tensors of the large models are drawn as random blocks (quantising 8B values takes minutes)
+        synth.write_model(tmp, arch, seed=seed, direct_blocks=arch.hidden >= 2048)
         os.replace(tmp, path)
     return path
 
@@ -156,6 +162,8 @@ def cpu_reference(name: str, path: str, warmup: int, steps: int) -> dict:
     """The reference's CPU decode loop on one sequence (oracle/_ref, native flags)."""
     from oracle import oracle as O
     arch, seed, plen, _, _ = WORKLOADS[name]
+    if name in CPU_SAMPLE:
+        plen, steps = CPU_SAMPLE[name][0], min(steps, CPU_SAMPLE[name][1])
     prompt = synth.prompt_ids(arch.vocab, plen, seed=seed + 100)
     exe, kind = None, "reference"
     for variant in ("native", "v3"):
@@ -178,7 +186,7 @@ def cpu_reference(name: str, path: str, warmup: int, steps: int) -> dict:
             "sample": f"{os.path.basename(exe)}: {plen}-token prompt (untimed), {warmup} warm-up + {steps} timed "
                       f"decode steps of one sequence on {info['threads']} threads (the reference decodes one "
                       f"sequence at a time, so its tokens/s does not depend on the batch)",
-            "prefill_s": info["prefill_s"]}
+            "prefill_s": info["prefill_s"], "steps": steps}
 
 
 def run_reference(args) -> None:
@@ -196,7 +204,7 @@ def run_reference(args) -> None:
         return
     out = {
         "impl": "reference", "metric": "decode tokens/s", "value": round(res["value"], 3), "unit": "tokens/s",
-        "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": round(1000.0 / res["value"], 3),
+        "n_gpus": world, "steps": res["steps"], "warmup": args.warmup, "ms_per_step": round(1000.0 / res["value"], 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": f"{name} decode", "model": desc, "batch": batch, "prompt": plen,
                    "note": "reference CPU loop, one sequence at a time"},
@@ -235,6 +243,7 @@ def main() -> None:
         batch = args.batch
     path = model_path(name, rank)
     ctx_need = plen + 2 * args.warmup + 2 * args.steps + 64  # decode, e2e and profiling steps
+    ctx_need = max(ctx_need, KV_CAPACITY.get(name, 0))
     eng = Engine(path, max_seqs=batch, device=local, kv_capacity=ctx_need)
     slots = np.arange(batch, dtype=np.int32)
     prompts = np.stack([synth.prompt_ids(arch.vocab, plen, seed=seed + 100 + 1000 * rank + i) for i in range(batch)])
@@ -314,7 +323,7 @@ def main() -> None:
     eng.close()
 
     # ---- batch-1 decode (the latency case) on the same model
-    if not args.no_batch1:
+    if not args.no_batch1 and batch > 1:
         e1b = Engine(path, max_seqs=1, device=local, kv_capacity=ctx_need)
         for t in prompts[0, :-1]:
             e1b.prefill([t], [0])

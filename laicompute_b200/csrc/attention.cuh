@@ -18,6 +18,7 @@
 // sequential multiply-add order).
 #pragma once
 #include "common.cuh"
+#include "mma_matvec.cuh"  // smem_u32, mma16816
 
 namespace laic {
 
@@ -37,6 +38,7 @@ struct AttnParams {
     float* part;               // [nseq][kv_heads][nsplit][G][D+2] (scratch)
     unsigned* counters;        // [nseq][kv_heads], zero between launches (scratch)
     float sqrt_d;
+    int* err;                  // set when a bounded wait runs out (chunked kernel)
 };
 
 template <typename KV, int N> struct KvLoad;
@@ -252,6 +254,296 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
         for (int j = 0; j < p.nsplit; ++j) M = fmaxf(M, __ldcg(src + j * sstride + D));
         float L = 0.f, A = 0.f;
         for (int j = 0; j < p.nsplit; ++j) {
+            const float mj = __ldcg(src + j * sstride + D);
+            if (mj == -INFINITY) continue;
+            const float e = expf(mj - M);
+            L = fmaf(__ldcg(src + j * sstride + D + 1), e, L);
+            A = fmaf(__ldcg(src + j * sstride + dd), e, A);
+        }
+        p.out[(size_t)seq * p.ldo + ((size_t)kvh * G + g) * D + dd] = A / L;
+    }
+    if (threadIdx.x == 0) p.counters[pair] = 0u;
+}
+
+// ---------------------------------------------------------------------------
+// FP16 KV: tensor-core decode attention over chunks staged in shared memory
+// ---------------------------------------------------------------------------
+// Grid (nsplit, kv_head, seq). A (sequence, kv head) pair's n = pos + 1
+// positions form ceil(n / kAttnChunk) chunks; the first min(nsplit, chunks)
+// splits take contiguous runs of them and the rest exit at once, so the work
+// follows the live context rather than the capacity.
+//
+// A chunk's K and V rows (contiguous in the cache) are copied into shared
+// memory with 16-byte cp.async, in an XOR-swizzled layout so that ldmatrix
+// reads of eight rows hit eight different bank groups. Rows before the newest
+// position were written by earlier steps and are fetched before the
+// programmatic-dependency wait (overlapping the QKV projection still running);
+// the newest row, written by that projection, is fetched after it.
+//
+// Each warp takes 32 positions of the chunk. The group's G <= 8 query heads
+// are the 8 columns of mma.m16n8k16 (fp16 in, fp32 accumulate):
+//   scores  S[32 pos][8 heads]  = K q^T   (A = K rows by ldmatrix, B = q)
+//   values  O^T[D][8 heads]    += V^T P^T (A = V by ldmatrix.trans, B = p)
+// q and p enter as binary16 hi + lo pairs (two products each), which keeps
+// them to ~22 significant bits; K and V are the cache's binary16 values.
+// Online softmax per head across chunks, then the warps of the CTA and the
+// splits are merged with the usual log-sum-exp weights.
+constexpr int kAttnChunk = 128;  // positions per chunk: 32 per warp
+
+__host__ __device__ constexpr size_t attn_chunk_smem(int D) { return (size_t)kAttnChunk * D * 2 * 2; }
+
+// element offset of 16-byte column chunk `cc` of row `r` in a swizzled [rows][D] binary16 buffer
+template <int D>
+__device__ __forceinline__ int attn_swz(int r, int cc) {
+    if constexpr (D == 32) return (r * 4 + (cc ^ ((r >> 1) & 3))) * 8;
+    else return (r * (D / 8) + (cc ^ (r & 7))) * 8;
+}
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+__device__ __forceinline__ uint32_t pack_h2(__half a, __half b) {
+    return (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
+}
+
+template <int D, int GMAX>
+__global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const AttnParams p) {
+    constexpr int KS = D / 16;  // k-steps of the score product = m-tiles of the value product
+    constexpr int CPR = D / 8;  // 16-byte chunks per row
+    constexpr int NW = kAttnWarps;
+    static_assert(D == 32 || D == 64 || D == 128, "head_dim 32, 64 or 128");
+    static_assert(GMAX <= 8, "at most 8 query heads per KV head");
+    extern __shared__ __align__(128) uint8_t smem[];
+    __half* Ks = reinterpret_cast<__half*>(smem);
+    __half* Vs = Ks + kAttnChunk * D;
+    __shared__ __align__(16) __half Ps[NW][2][8][40];  // per warp: p hi/lo [head][position] (rows padded)
+    __shared__ float cm[NW][8], cl[NW][8];
+    __shared__ int is_last;
+
+    const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int gq = lane >> 2, c = lane & 3;
+    const int G = p.heads / p.kv_heads;
+
+    // positions of this sequence: final for this step before the dependency wait
+    const int slot = p.slots[seq];
+    const int n = p.pos[slot] + 1;
+    const int nch = (n + kAttnChunk - 1) / kAttnChunk;
+    const int active = min(p.nsplit, nch);
+    if (split >= active) {
+        pdl_launch_dependents();
+        return;
+    }
+    const int ch0 = split * nch / active, ch1 = (split + 1) * nch / active;
+    const __half* kb = reinterpret_cast<const __half*>(p.kc) + (size_t)slot * p.slot_stride + (size_t)kvh * p.cap * D;
+    const __half* vb = reinterpret_cast<const __half*>(p.vc) + (size_t)slot * p.slot_stride + (size_t)kvh * p.cap * D;
+
+    // rows [r0, r1) of the chunk that starts at c0, all threads
+    auto load_rows = [&](int r0, int r1, int c0) {
+        for (int i = threadIdx.x; i < (r1 - r0) * CPR; i += blockDim.x) {
+            const int r = r0 + i / CPR, cc = i % CPR, rl = r - c0;
+            cp_async16(Ks + attn_swz<D>(rl, cc), kb + (size_t)r * D + cc * 8);
+            cp_async16(Vs + attn_swz<D>(rl, cc), vb + (size_t)r * D + cc * 8);
+        }
+        cp_async_commit();
+    };
+    // value rows past the chunk's end up to the next 32 are read by the last
+    // warp's products (with p = 0): make them zeros, not stale bits
+    auto zero_tail = [&](int rows) {
+        const int end = min(kAttnChunk, (rows + 31) & ~31);
+        for (int i = threadIdx.x; i < (end - rows) * CPR; i += blockDim.x) {
+            const int rl = rows + i / CPR, cc = i % CPR;
+            *reinterpret_cast<uint4*>(Vs + attn_swz<D>(rl, cc)) = make_uint4(0, 0, 0, 0);
+        }
+    };
+    {
+        const int c0 = ch0 * kAttnChunk, c1 = min(n, c0 + kAttnChunk);
+        load_rows(c0, min(c1, n - 1), c0);  // older rows, before the dependency wait
+        zero_tail(c1 - c0);
+    }
+    pdl_launch_dependents();
+    pdl_wait();
+
+    // B fragments of the score product: q of head gq (zero past G), scaled by 1/sqrt(d), hi + lo
+    uint32_t qh[KS][2], ql[KS][2];
+    {
+        const float rs = 1.f / p.sqrt_d;
+        const float* qg = p.q + (size_t)seq * p.ldq + ((size_t)kvh * G + gq) * D;
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks)
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const int d0 = ks * 16 + 2 * c + 8 * j;
+                const float v0 = gq < G ? qg[d0] * rs : 0.f, v1 = gq < G ? qg[d0 + 1] * rs : 0.f;
+                const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
+                qh[ks][j] = pack_h2(h0, h1);
+                ql[ks][j] = pack_h2(__float2half_rn(v0 - __half2float(h0)), __float2half_rn(v1 - __half2float(h1)));
+            }
+    }
+
+    float m_[2] = {-INFINITY, -INFINITY}, l_[2] = {0.f, 0.f};  // heads 2c, 2c+1
+    float o[KS][4];  // O^T: dims (mt*16 + gq, +8) x heads (2c, 2c+1)
+#pragma unroll
+    for (int mt = 0; mt < KS; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+    const uint32_t ks_a = smem_u32(Ks), vs_a = smem_u32(Vs);
+    const int li = lane >> 3, lr = lane & 7;  // ldmatrix: this lane addresses row lr of matrix li
+
+    for (int ch = ch0; ch < ch1; ++ch) {
+        const int c0 = ch * kAttnChunk, c1 = min(n, c0 + kAttnChunk);
+        if (ch == ch0 && c1 == n) load_rows(n - 1, n, c0);  // the newest row, after the wait
+        cp_async_wait_all();
+        __syncthreads();
+        const int wp = warp * 32;  // this warp's first row in the chunk
+        if (c0 + wp < c1) {
+            // ---- scores: two m-tiles of 16 positions
+            float s[2][4];
+#pragma unroll
+            for (int mt2 = 0; mt2 < 2; ++mt2) {
+                s[mt2][0] = s[mt2][1] = s[mt2][2] = s[mt2][3] = 0.f;
+                const int rr = wp + mt2 * 16 + (li & 1) * 8 + lr;
+#pragma unroll
+                for (int ks = 0; ks < KS; ++ks) {
+                    uint32_t a[4];
+                    ldsm_x4(ks_a + 2 * attn_swz<D>(rr, ks * 2 + (li >> 1)), a);
+                    mma16816(s[mt2], a[0], a[1], a[2], a[3], qh[ks][0], qh[ks][1]);
+                    mma16816(s[mt2], a[0], a[1], a[2], a[3], ql[ks][0], ql[ks][1]);
+                }
+            }
+            // ---- online softmax per head (this lane: heads 2c and 2c+1)
+            float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+            for (int mt2 = 0; mt2 < 2; ++mt2)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int pos = c0 + wp + mt2 * 16 + gq + (e >> 1) * 8;
+                    if (pos >= c1) s[mt2][e] = -INFINITY;
+                    mx[e & 1] = fmaxf(mx[e & 1], s[mt2][e]);
+                }
+            float corr[2], sum[2] = {0.f, 0.f};
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 4));
+                mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 8));
+                mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 16));
+                const float mnew = fmaxf(m_[h], mx[h]);  // finite: the warp has a live position
+                corr[h] = expf(m_[h] - mnew);
+                m_[h] = mnew;
+            }
+#pragma unroll
+            for (int mt2 = 0; mt2 < 2; ++mt2)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int h = e & 1;
+                    const float pv = expf(s[mt2][e] - m_[h]);
+                    sum[h] += pv;
+                    const int pl = mt2 * 16 + gq + (e >> 1) * 8;
+                    const __half hi = __float2half_rn(pv);
+                    Ps[warp][0][2 * c + h][pl] = hi;
+                    Ps[warp][1][2 * c + h][pl] = __float2half_rn(pv - __half2float(hi));
+                }
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                sum[h] += __shfl_xor_sync(0xffffffffu, sum[h], 4);
+                sum[h] += __shfl_xor_sync(0xffffffffu, sum[h], 8);
+                sum[h] += __shfl_xor_sync(0xffffffffu, sum[h], 16);
+                l_[h] = l_[h] * corr[h] + sum[h];
+            }
+#pragma unroll
+            for (int mt = 0; mt < KS; ++mt) {
+                o[mt][0] *= corr[0]; o[mt][1] *= corr[1];
+                o[mt][2] *= corr[0]; o[mt][3] *= corr[1];
+            }
+            __syncwarp();
+            // ---- values: O^T += V^T P^T over two k-steps of 16 positions
+#pragma unroll
+            for (int kp = 0; kp < 2; ++kp) {
+                const uint32_t* ph = reinterpret_cast<const uint32_t*>(&Ps[warp][0][gq][kp * 16 + 2 * c]);
+                const uint32_t* pl = reinterpret_cast<const uint32_t*>(&Ps[warp][1][gq][kp * 16 + 2 * c]);
+                const uint32_t bh0 = ph[0], bh1 = ph[4], bl0 = pl[0], bl1 = pl[4];  // +4 words = +8 positions
+                const int rr = wp + kp * 16 + (li >> 1) * 8 + lr;
+#pragma unroll
+                for (int mt = 0; mt < KS; ++mt) {
+                    uint32_t a[4];
+                    ldsm_x4_t(vs_a + 2 * attn_swz<D>(rr, mt * 2 + (li & 1)), a);
+                    mma16816(o[mt], a[0], a[1], a[2], a[3], bh0, bh1);
+                    mma16816(o[mt], a[0], a[1], a[2], a[3], bl0, bl1);
+                }
+            }
+            __syncwarp();
+        }
+        __syncthreads();  // the chunk buffers are free
+        if (ch + 1 < ch1) {
+            const int n0 = (ch + 1) * kAttnChunk, n1 = min(n, n0 + kAttnChunk);
+            load_rows(n0, n1, n0);
+            zero_tail(n1 - n0);
+        }
+    }
+
+    // ---- merge the warps of this CTA (the chunk buffer holds their accumulators now)
+    float* cacc = reinterpret_cast<float*>(smem);  // [NW][8][D]
+    if (gq == 0) {
+        cm[warp][2 * c] = m_[0]; cm[warp][2 * c + 1] = m_[1];
+        cl[warp][2 * c] = l_[0]; cl[warp][2 * c + 1] = l_[1];
+    }
+#pragma unroll
+    for (int mt = 0; mt < KS; ++mt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int d = mt * 16 + gq + (e >> 1) * 8, h = 2 * c + (e & 1);
+            cacc[((size_t)warp * 8 + h) * D + d] = o[mt][e];
+        }
+    __syncthreads();
+
+    const size_t pair = (size_t)seq * p.kv_heads + kvh;
+    const int PD = D + 2;
+    for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+        const int g = i / D, dd = i % D;
+        float M = -INFINITY;
+        for (int w = 0; w < NW; ++w) M = fmaxf(M, cm[w][g]);
+        float L = 0.f, A = 0.f;
+        if (M != -INFINITY) {
+            for (int w = 0; w < NW; ++w) {
+                if (cm[w][g] == -INFINITY) continue;
+                const float e = expf(cm[w][g] - M);
+                L = fmaf(cl[w][g], e, L);
+                A = fmaf(cacc[((size_t)w * 8 + g) * D + dd], e, A);
+            }
+        }
+        if (active == 1) {
+            p.out[(size_t)seq * p.ldo + ((size_t)kvh * G + g) * D + dd] = A / L;
+        } else {
+            float* dst = p.part + ((pair * p.nsplit + split) * G + g) * PD;
+            dst[dd] = A;
+            if (dd == 0) { dst[D] = M; dst[D + 1] = L; }
+        }
+    }
+    if (active == 1) return;
+
+    // ---- the last of the active splits merges them (atomic ticket, no spinning)
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) is_last = atomicAdd(p.counters + pair, 1u) == (unsigned)(active - 1);
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+        const int g = i / D, dd = i % D;
+        const float* src = p.part + (pair * p.nsplit * G + g) * PD;
+        const size_t sstride = (size_t)G * PD;
+        float M = -INFINITY;
+        for (int j = 0; j < active; ++j) M = fmaxf(M, __ldcg(src + j * sstride + D));
+        float L = 0.f, A = 0.f;
+        for (int j = 0; j < active; ++j) {
             const float mj = __ldcg(src + j * sstride + D);
             if (mj == -INFINITY) continue;
             const float e = expf(mj - M);

@@ -292,7 +292,7 @@ cudaError_t launch_matvec(const Mat& m, laic::MvParams p, int epi, bool kv32, co
 using AttnFn = void (*)(laic::AttnParams);
 template <int D, int GM>
 AttnFn attn_fn_g(bool kv32) {
-    return kv32 ? laic::attn_decode_kernel<D, GM, float, true> : laic::attn_decode_kernel<D, GM, __half, false>;
+    return kv32 ? laic::attn_decode_kernel<D, GM, float, true> : laic::attn_mma_kernel<D, GM>;
 }
 template <int D>
 AttnFn attn_fn_d(int G, bool kv32) {
@@ -301,12 +301,15 @@ AttnFn attn_fn_d(int G, bool kv32) {
     if (G <= 4) return attn_fn_g<D, 4>(kv32);
     return attn_fn_g<D, 8>(kv32);
 }
+// FP32 KV (parity mode): the register kernel with the reference's score order;
+// FP16 KV: the tensor-core kernel over chunks staged in shared memory.
 AttnFn attn_pick(int D, int G, bool kv32) {
     if (D == 32) return attn_fn_d<32>(G, kv32);
     if (D == 64) return attn_fn_d<64>(G, kv32);
     if (D == 128) return attn_fn_d<128>(G, kv32);
     return nullptr;
 }
+size_t attn_smem(int D, bool kv32) { return kv32 ? 0 : laic::attn_chunk_smem(D); }
 
 // ---------------------------------------------------------------------------
 // the engine
@@ -363,8 +366,14 @@ struct laic_dev {
     // ------------------------------------------------------------------
     int nsplit_for(int nseq) const {
         const int pairs = nseq * Hkv;
-        int s = (8 * num_sms() + pairs - 1) / pairs;  // about eight CTAs per SM
-        return std::max(1, std::min(s, max_split));
+        if (kv32) {
+            const int s = (8 * num_sms() + pairs - 1) / pairs;  // about eight CTAs per SM
+            return std::max(1, std::min(s, max_split));
+        }
+        // chunked kernel: at most one split per chunk of the capacity, about four CTAs per SM
+        const int chunks = (cap + laic::kAttnChunk - 1) / laic::kAttnChunk;
+        const int s = (4 * num_sms() + pairs - 1) / pairs;
+        return std::max(1, std::min(std::min(s, chunks), max_split));
     }
 
     bool ready(std::string& missing) const {
@@ -449,9 +458,9 @@ struct laic_dev {
             ap.q = q; ap.ldq = h; ap.out = attn; ap.ldo = h;
             ap.kc = p.kc; ap.vc = p.vc; ap.slot_stride = kv_slot_stride; ap.cap = cap;
             ap.heads = H; ap.kv_heads = Hkv; ap.slots = d_slots; ap.pos = pos; ap.nsplit = nsplit;
-            ap.part = attn_part; ap.counters = attn_cnt; ap.sqrt_d = sqrtf((float)D);
+            ap.part = attn_part; ap.counters = attn_cnt; ap.sqrt_d = sqrtf((float)D); ap.err = mvs.err;
             t_begin("attention", attn_bytes);
-            CK(launch_k(afn, dim3(nsplit, Hkv, nseq), dim3(laic::kAttnWarps * 32), 0, s, pdl, ap));
+            CK(launch_k(afn, dim3(nsplit, Hkv, nseq), dim3(laic::kAttnWarps * 32), attn_smem(D, kv32), s, pdl, ap));
             ++nl;
             t_end();
             // o + residual
@@ -631,6 +640,9 @@ int laic_dev_create(const laic_dev_desc* desc, const laic_dev_opts* opts, laic_d
     CK(cudaStreamCreateWithFlags(&d->st, cudaStreamNonBlocking));
     // set kernel attributes now: graph capture must not see attribute calls
     CK(laic::mv_set_attributes());
+    if (!d->kv32)
+        CK(cudaFuncSetAttribute(attn_pick(D, d->G, false), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)laic::attn_chunk_smem(D)));
 
     const size_t S = o.max_seqs, kvb = d->kv32 ? 4 : 2;
     CK(cudaMalloc(&d->x, S * d->h * 4));

@@ -246,9 +246,32 @@ def _type_of(arch: LlamaArch, name: str) -> int:
     return arch.weight_type
 
 
+def random_blocks(n: int, ggml_type: int, rng: np.random.Generator, std: float = 0.02) -> bytes:
+    """Q4_0 / Q8_0 blocks drawn directly (uniform quants, scales of the size a
+    N(0, std) block quantises to), for models too large to quantise quickly."""
+    nb = n // 32
+    if ggml_type == gguf.Q4_0:
+        d = np.float32(std * 2.2 / 8.0) * (np.float32(1.0) + np.float32(0.1) * rng.standard_normal(nb, dtype=np.float32))
+        out = np.empty((nb, 18), dtype=np.uint8)
+        out[:, 0:2] = d.astype("<f2").view(np.uint8).reshape(-1, 2)
+        out[:, 2:] = np.frombuffer(rng.bytes(nb * 16), dtype=np.uint8).reshape(nb, 16)
+        return out.tobytes()
+    if ggml_type == gguf.Q8_0:
+        d = np.float32(std * 2.2 / 127.0) * (np.float32(1.0) + np.float32(0.1) * rng.standard_normal(nb, dtype=np.float32))
+        out = np.empty((nb, 34), dtype=np.uint8)
+        out[:, 0:2] = d.astype("<f2").view(np.uint8).reshape(-1, 2)
+        q = np.frombuffer(rng.bytes(nb * 32), dtype=np.int8).reshape(nb, 32)
+        out[:, 2:] = np.maximum(q, -127).view(np.uint8)
+        return out.tobytes()
+    raise ValueError(f"no direct block generator for ggml type {ggml_type}")
+
+
 def write_model(path: str, arch: LlamaArch, seed: int = 0, std: float = 0.02,
-                bos: int | None = None, eos: int | None = None) -> str:
-    """Write a synthetic Llama GGUF for ``arch``; returns ``path``."""
+                bos: int | None = None, eos: int | None = None, direct_blocks: bool = False) -> str:
+    """Write a synthetic Llama GGUF for ``arch``; returns ``path``.
+
+    ``direct_blocks`` draws quantised tensors as random blocks instead of
+    quantising N(0, std) values (same sizes and value range, much faster)."""
     rng = np.random.default_rng(seed)
     tokens, merges = gpt2_vocab(arch.vocab)
     eos_id = arch.vocab - 1 if eos is None else eos
@@ -279,6 +302,9 @@ def write_model(path: str, arch: LlamaArch, seed: int = 0, std: float = 0.02,
         n = int(np.prod(shape))
         if len(shape) == 1:
             x = np.ones(n, dtype=np.float32)
+        elif direct_blocks and gt in (gguf.Q4_0, gguf.Q8_0):
+            tensors.append((name, shape, gt, random_blocks(n, gt, rng, std)))
+            continue
         else:
             x = (rng.standard_normal(n, dtype=np.float32) * np.float32(std)).astype(np.float32)
         tensors.append((name, shape, gt, encode(x, gt)))
