@@ -13,6 +13,8 @@ ids each, then decode steps. One "step" = one token for every sequence.
 
 Multi-GPU (torchrun, one rank per GPU): the 135M model does not shard per
 layer, so every rank decodes its own 64 sequences (replicas, weak scaling).
+--workload llama8b-q4_0 (8B-shaped, Q4_0, batch 1) is split tensor-parallel
+over the run's GPUs (NCCL allreduce after o and down; strong scaling).
 
 --impl reference times the reference's own CPU decode loop (oracle/_ref, the
 reference sources compiled with its native flags) on the same model and
@@ -44,6 +46,8 @@ WORKLOADS = {
     "llama1b-q4_0": (synth.LLAMA_1B_Q4, 4, 512, 32, "1B-shaped Llama, Q4_0 projections, F16 embeddings"),
     "llama8b-q4_0": (synth.LLAMA_8B_Q4, 5, 1024, 1, "8B-shaped Llama, Q4_0 projections, tied Q4_0 embeddings"),
 }
+# workloads split tensor-parallel over the GPUs of the run (the others run one replica per GPU)
+TP_WORKLOADS = {"llama8b-q4_0"}
 # KV positions allocated per slot, where the workload asks for more than it decodes
 KV_CAPACITY = {"llama8b-q4_0": 8192}
 # CPU sample of the large models: (prompt tokens, timed decode steps) — a reference step takes seconds
@@ -61,10 +65,11 @@ def measured_peak_gbs():
 
 
 def model_path(name: str, rank: int) -> str:
+    """The workload's GGUF (rank = None: one file shared by the ranks of a tensor-parallel run)."""
     arch, seed, _, _, _ = WORKLOADS[name]
     d = os.path.join(tempfile.gettempdir(), "laic_bench_models")
     os.makedirs(d, exist_ok=True)
-    path = os.path.join(d, f"{name}.seed{seed}.r{rank}.gguf")
+    path = os.path.join(d, f"{name}.seed{seed}" + ("" if rank is None else f".r{rank}") + ".gguf")
     if not os.path.exists(path):
         tmp = path + ".part"
         # quantised tensors of the large models are drawn as random blocks (quantising 8B values takes minutes)
@@ -235,20 +240,34 @@ def main() -> None:
 
     world, rank, local = dist_setup()
     import torch
-    from laicompute_b200.engine import Engine, sample_params
+    from laicompute_b200.engine import Engine, nccl_unique_id, sample_params
 
     name = args.workload
     arch, seed, plen, batch, desc = WORKLOADS[name]
     if args.batch:
         batch = args.batch
-    path = model_path(name, rank)
+    tp = world if (name in TP_WORKLOADS and world > 1) else 1
+    if tp > 1:  # one model file, written by rank 0; the ranks hold shards of one engine
+        if rank == 0:
+            path = model_path(name, None)
+        barrier(world)
+        path = model_path(name, None)
+        nid = [nccl_unique_id() if rank == 0 else None]
+        import torch.distributed as dist
+        dist.broadcast_object_list(nid, src=0, device=torch.device("cuda", local))
+        tp_kw = dict(tp_size=tp, tp_rank=rank, nccl_id=nid[0])
+    else:
+        path = model_path(name, rank)
+        tp_kw = {}
+    seq_rank = 0 if tp > 1 else rank  # tensor-parallel ranks decode the same sequences
     ctx_need = plen + 2 * args.warmup + 2 * args.steps + 64  # decode, e2e and profiling steps
     ctx_need = max(ctx_need, KV_CAPACITY.get(name, 0))
-    eng = Engine(path, max_seqs=batch, device=local, kv_capacity=ctx_need)
+    eng = Engine(path, max_seqs=batch, device=local, kv_capacity=ctx_need, **tp_kw)
     slots = np.arange(batch, dtype=np.int32)
-    prompts = np.stack([synth.prompt_ids(arch.vocab, plen, seed=seed + 100 + 1000 * rank + i) for i in range(batch)])
+    prompts = np.stack([synth.prompt_ids(arch.vocab, plen, seed=seed + 100 + 1000 * seq_rank + i)
+                        for i in range(batch)])
     if args.sample:
-        params = [sample_params(0.8, 40, 1.0, 1.0, 4242 + 1000 * rank + i) for i in range(batch)]
+        params = [sample_params(0.8, 40, 1.0, 1.0, 4242 + 1000 * seq_rank + i) for i in range(batch)]
     else:
         params = [sample_params()] * batch
     for j in range(plen - 1):
@@ -269,7 +288,8 @@ def main() -> None:
     barrier(world)
     torch.cuda.synchronize()
     max_ms = allreduce_max(dev_ms, world)
-    value = batch * args.steps * world / (max_ms / 1000.0)
+    replicas = world // tp  # independent sequence batches in the job
+    value = batch * args.steps * replicas / (max_ms / 1000.0)
     tok = ids[-1]
     launches_chained = eng.stats().launches_per_step  # kernels per chained step, as timed
 
@@ -286,7 +306,7 @@ def main() -> None:
     e1.record(ext)
     e1.synchronize()
     e2e_ms = allreduce_max(e0.elapsed_time(e1), world)
-    e2e_value = batch * args.steps * world / (e2e_ms / 1000.0)
+    e2e_value = batch * args.steps * replicas / (e2e_ms / 1000.0)
 
     # ---- per-kernel roofline (eager launches with CUDA events around each)
     st = eng.stats()
@@ -302,11 +322,12 @@ def main() -> None:
         out = {
             "metric": "decode tokens/s", "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(max_ms / args.steps, 5),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "higher_is_better": True, "scaling": "strong" if tp > 1 else "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
             "config": {"workload": f"{name} decode, batch {batch} per GPU, prompt {plen}, "
                                    f"{'T=0.8/top-k 40' if args.sample else 'greedy'}",
                        "model": desc, "batch_per_gpu": batch, "prompt": plen,
-                       "parallelism": f"replicas x{world}", "kv": "fp16",
+                       "parallelism": f"tp{tp}" if tp > 1 else f"replicas x{world}", "kv": "fp16",
                        "l2": "inputs larger than L2: weights %.0f MB + KV read %.0f MB per step"
                              % (st.weight_bytes / 1e6, kv_read / 1e6)},
             "hbm_gbs_step": round((st.weight_bytes + kv_read) / (max_ms / args.steps * 1e-3) / 1e9, 1),

@@ -157,7 +157,10 @@ typedef struct laic_kernel_record {
 } laic_kernel_record;
 
 /* Run `steps` full greedy steps of slots 0..nseq-1 (token ids from tokens[steps][nseq])
- * launching kernels one by one with CUDA events around each launch. */
+ * launching kernels one by one with CUDA events around each launch. Each step
+ * is queued behind a short stream-holding kernel, so the launches run back to
+ * back and the events time the kernels rather than host launch gaps (there is
+ * no programmatic overlap between them in this mode). */
 LAIC_API int laic_dev_profile(laic_dev* dev, int32_t nseq, const uint32_t* tokens, int32_t steps,
                               laic_kernel_record* out, int32_t max_out, int32_t* n_out);
 

@@ -31,7 +31,8 @@ CXXFLAGS = ["-std=c++17", "-O2", "-fPIC", "-Wall", f"-I{INCLUDE}"]
 
 
 def _headers() -> list[str]:
-    return glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(INCLUDE, "**", "*.h*"), recursive=True)
+    return (glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(CSRC, "*.h"))
+            + glob.glob(os.path.join(INCLUDE, "**", "*.h*"), recursive=True))
 
 
 def _stale(out: str, deps: list[str]) -> bool:
@@ -59,6 +60,11 @@ def build(verbose: bool = False) -> str:
         if _stale(obj, [src, *hdrs]):
             jobs.append(("nvcc", src, [NVCC, *NVFLAGS, "-c", src, "-o", obj]))
         objs.append(obj)
+    for src in sorted(glob.glob(os.path.join(CSRC, "*.cpp"))):  # engine internals (not exported)
+        obj = os.path.join(BUILD, os.path.basename(src) + ".o")
+        if _stale(obj, [src, *hdrs]):
+            jobs.append(("g++", src, ["g++", *CXXFLAGS, "-fvisibility=hidden", "-c", src, "-o", obj]))
+        objs.append(obj)
     for src in sorted(glob.glob(os.path.join(CSRC, "host", "*.cpp"))):
         obj = os.path.join(BUILD, "host_" + os.path.basename(src) + ".o")
         if _stale(obj, [src, *hdrs]):
@@ -70,7 +76,7 @@ def build(verbose: bool = False) -> str:
     with ThreadPoolExecutor(max_workers=max(1, os.cpu_count() or 1)) as ex:
         list(ex.map(lambda j: _run(j[2]), jobs))
     if _stale(LIB, objs):
-        _run([NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lpthread"])
+        _run([NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lpthread", "-ldl"])
     tool = os.path.join(CSRC, "tools", "laic_generate.cpp")
     if _stale(BIN, [tool, LIB, *hdrs]):
         _run(["g++", *CXXFLAGS, tool, "-o", BIN, f"-L{os.path.dirname(LIB)}", "-llaic_b200",

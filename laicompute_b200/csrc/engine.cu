@@ -15,6 +15,14 @@
 //   down  Wdown act, added into the residual
 // then rmsnorm(output_norm) -> lm_head -> sampler. Kernels use programmatic
 // dependent launch so each one's launch and prologue overlap the previous one.
+//
+// Tensor parallelism (tp_size > 1, one process per GPU): each rank holds
+// H/tp query heads and Hkv/tp KV heads (their rows of Wq/Wk/Wv and their KV
+// cache), F/tp rows of Wgate/Wup, the matching column slices of Wo and Wdown,
+// and V/tp rows of the lm_head. After o and after down the ranks' partial
+// products are summed with one in-place NCCL allreduce on the residual (rank
+// 0 adds its partial to the residual, the others overwrite it with theirs);
+// the lm_head slices are all-gathered so every rank samples the same ids.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -34,6 +42,7 @@
 #include "misc.cuh"
 #include "mma_matvec.cuh"
 #include "mv_streamk.cuh"
+#include "nccl_dl.h"
 #include "sampler.cuh"
 
 namespace {
@@ -332,8 +341,15 @@ struct laic_dev {
     laic_dev_opts o{};
     int device = 0;
     cudaStream_t st = nullptr;
-    int H = 0, Hkv = 0, D = 0, G = 0, h = 0, kv = 0, F = 0, V = 0, L = 0, S = 0, cap = 0, rope_pairs = 0;
+    // H, Hkv, kv (= Hkv * D), hq (= H * D) and F are this rank's shares; h and V are the full sizes
+    int H = 0, Hkv = 0, D = 0, G = 0, h = 0, kv = 0, hq = 0, F = 0, V = 0, Vl = 0, L = 0, S = 0, cap = 0,
+        rope_pairs = 0;
     bool kv32 = false, use_graph = true, use_pdl = true;
+    int tp = 1, tr = 0;  // tensor-parallel size and rank
+    laic::ncclComm_t comm = nullptr;
+    const laic::NcclApi* nccl = nullptr;
+    float *logits_l = nullptr, *logits_g = nullptr;  // tp > 1: this rank's vocabulary rows; every rank's
+    bool have_lm = false;  // tp > 1: lm holds this rank's lm_head rows
 
     Mat embd, lm;
     bool have_embd = false, have_out = false, have_onorm = false;
@@ -378,7 +394,8 @@ struct laic_dev {
 
     bool ready(std::string& missing) const {
         if (!have_embd) { missing = "token_embd.weight"; return false; }
-        if (!have_out && embd.rows != V) { missing = "output.weight"; return false; }
+        if (tp == 1 && !have_out && embd.rows != V) { missing = "output.weight"; return false; }
+        if (tp > 1 && !have_lm) { missing = "output.weight"; return false; }
         if (!have_onorm) { missing = "output_norm.weight"; return false; }
         for (int l = 0; l < L; ++l) {
             if ((layers[l].have & H_ALL) != H_ALL) {
@@ -392,7 +409,7 @@ struct laic_dev {
         return true;
     }
 
-    const Mat& lm_head() const { return have_out ? lm : embd; }
+    const Mat& lm_head() const { return (have_out || tp > 1) ? lm : embd; }
     int launches_step = 0, launches_prefill = 0;  // kernels in the last enqueued step / prefill
 
     // Enqueue one step. `timer` (nullable) records events around launches for profiling.
@@ -401,9 +418,22 @@ struct laic_dev {
         std::vector<double> bytes;
     };
 
+    // Tensor parallel: sum the ranks' partial o / down products held in the residual.
+    template <typename TB, typename TE>
+    int allreduce_residual(int nseq, cudaStream_t s, TB& t_begin, TE& t_end) {
+        if (tp == 1) return LAIC_OK;
+        t_begin("allreduce", 8.0 * nseq * h * (tp - 1) / tp);
+        const laic::ncclResult_t r = nccl->AllReduce(x, x, (size_t)nseq * h, laic::ncclFloat32, laic::ncclSum, comm, s);
+        if (r != laic::ncclSuccess) return fail(LAIC_E_NCCL, std::string("ncclAllReduce: ") + nccl->GetErrorString(r));
+        t_end();
+        return LAIC_OK;
+    }
+
     int enqueue(int nseq, int mode, cudaStream_t s, Timer* timer) {
         const bool full = mode != MODE_PREFILL;
         const bool pdl = use_pdl && !timer;
+        // o and down: rank 0 adds its partial to the residual, the other ranks store theirs (then allreduce)
+        const int residual_epi = (tp > 1 && tr != 0) ? laic::EPI_STORE : laic::EPI_ADD;
         int nl = 0;  // kernels enqueued
         auto t_begin = [&](const char* name, double b) {
             if (!timer) return;
@@ -444,8 +474,8 @@ struct laic_dev {
             p.nseq = nseq;
             p.eps = a.rms_eps;
             // qkv
-            p.x = x; p.ldx = h; p.norm_w = ly.attn_norm; p.out = q; p.ldo = h;
-            p.q_rows = h; p.kv_rows = kv; p.head_dim = D; p.rope_pairs = rope_pairs; p.rope_cs = rope_cs;
+            p.x = x; p.ldx = h; p.norm_w = ly.attn_norm; p.out = q; p.ldo = hq;
+            p.q_rows = hq; p.kv_rows = kv; p.head_dim = D; p.rope_pairs = rope_pairs; p.rope_cs = rope_cs;
             p.slots = d_slots; p.pos = pos;
             p.kc = (char*)kc + (size_t)l * kv_layer_stride * kvb;
             p.vc = (char*)vc + (size_t)l * kv_layer_stride * kvb;
@@ -455,7 +485,7 @@ struct laic_dev {
             t_end();
             // attention
             laic::AttnParams ap{};
-            ap.q = q; ap.ldq = h; ap.out = attn; ap.ldo = h;
+            ap.q = q; ap.ldq = hq; ap.out = attn; ap.ldo = hq;
             ap.kc = p.kc; ap.vc = p.vc; ap.slot_stride = kv_slot_stride; ap.cap = cap;
             ap.heads = H; ap.kv_heads = Hkv; ap.slots = d_slots; ap.pos = pos; ap.nsplit = nsplit;
             ap.part = attn_part; ap.counters = attn_cnt; ap.sqrt_d = sqrtf((float)D); ap.err = mvs.err;
@@ -465,10 +495,11 @@ struct laic_dev {
             t_end();
             // o + residual
             laic::MvParams po{};
-            po.nseq = nseq; po.x = attn; po.ldx = h; po.out = x; po.ldo = h;
-            t_begin("o", (double)ly.o.bytes() + 12.0 * nseq * h);
-            CK(launch_matvec(ly.o, po, laic::EPI_ADD, kv32, mvs, s, pdl, &nl));
+            po.nseq = nseq; po.x = attn; po.ldx = hq; po.out = x; po.ldo = h;
+            t_begin("o", (double)ly.o.bytes() + 4.0 * nseq * hq + 8.0 * nseq * h);
+            CK(launch_matvec(ly.o, po, residual_epi, kv32, mvs, s, pdl, &nl));
             t_end();
+            if (int rc = allreduce_residual(nseq, s, t_begin, t_end)) return rc;
             // gate/up + swiglu
             laic::MvParams pg{};
             pg.nseq = nseq; pg.eps = a.rms_eps; pg.x = x; pg.ldx = h; pg.norm_w = ly.ffn_norm; pg.out = act; pg.ldo = F;
@@ -479,15 +510,29 @@ struct laic_dev {
             laic::MvParams pd{};
             pd.nseq = nseq; pd.x = act; pd.ldx = F; pd.out = x; pd.ldo = h;
             t_begin("down", (double)ly.down.bytes() + 4.0 * nseq * (F + 2 * h));
-            CK(launch_matvec(ly.down, pd, laic::EPI_ADD, kv32, mvs, s, pdl, &nl));
+            CK(launch_matvec(ly.down, pd, residual_epi, kv32, mvs, s, pdl, &nl));
             t_end();
+            if (int rc = allreduce_residual(nseq, s, t_begin, t_end)) return rc;
         }
         if (full) {
             laic::MvParams pl{};
-            pl.nseq = nseq; pl.eps = a.rms_eps; pl.x = x; pl.ldx = h; pl.norm_w = out_norm; pl.out = logits; pl.ldo = V;
-            t_begin("lm_head", (double)lm_head().bytes() + 4.0 * nseq * (h + V));
+            pl.nseq = nseq; pl.eps = a.rms_eps; pl.x = x; pl.ldx = h; pl.norm_w = out_norm;
+            pl.out = tp > 1 ? logits_l : logits; pl.ldo = tp > 1 ? Vl : V;
+            t_begin("lm_head", (double)lm_head().bytes() + 4.0 * nseq * (h + Vl));
             CK(launch_matvec(lm_head(), pl, laic::EPI_STORE, kv32, mvs, s, pdl, &nl));
             t_end();
+            if (tp > 1) {  // every rank's vocabulary rows -> logits [nseq][V] on every rank
+                t_begin("gather", 4.0 * nseq * V);
+                float* dst = nseq == 1 ? logits : logits_g;
+                const laic::ncclResult_t r = nccl->AllGather(logits_l, dst, (size_t)nseq * Vl, laic::ncclFloat32, comm, s);
+                if (r != laic::ncclSuccess) return fail(LAIC_E_NCCL, std::string("ncclAllGather: ") + nccl->GetErrorString(r));
+                if (nseq > 1) {
+                    CK(launch_k(laic::gather_logits_kernel, dim3(num_sms()), dim3(256), 0, s, pdl, (const float*)logits_g,
+                                logits, tp, nseq, Vl));
+                    ++nl;
+                }
+                t_end();
+            }
             laic::SamplerParams sp{logits, V, V, d_slots, counts, d_params, nseq, d_out_ids, d_tokens, pos, d_err};
             t_begin("sampler", (double)nseq * V * 4);
             CK(launch_k(laic::sample_kernel, dim3(nseq), dim3(laic::kSampleThreads), 0, s, pdl, sp));
@@ -610,8 +655,17 @@ int laic_dev_create(const laic_dev_desc* desc, const laic_dev_opts* opts, laic_d
     laic_dev_opts o{};
     o.max_seqs = 1; o.tp_size = 1;
     if (opts) o = *opts;
-    if (o.tp_size > 1) return fail(LAIC_E_UNSUPPORTED, "tensor parallelism is not built into this library yet");
     const laic_dev_desc& a = *desc;
+    const int tp = std::max(1, o.tp_size);
+    if (tp > 1) {
+        if (tp > 8) return fail(LAIC_E_UNSUPPORTED, "tp_size must be at most 8 (one node)");
+        if (o.tp_rank < 0 || o.tp_rank >= tp) return fail(LAIC_E_INVALID, "tp_rank out of range");
+        if (!o.nccl_id) return fail(LAIC_E_INVALID, "tp_size > 1 needs nccl_id (laic_nccl_unique_id on rank 0)");
+        if (!a.heads || !a.kv_heads || a.heads % tp || a.kv_heads % tp)
+            return fail(LAIC_E_UNSUPPORTED, "heads and kv_heads must be multiples of tp_size");
+        if (a.ffn % (32 * (uint32_t)tp)) return fail(LAIC_E_UNSUPPORTED, "ffn / tp_size must be a multiple of 32");
+        if (a.vocab % tp) return fail(LAIC_E_UNSUPPORTED, "vocab must be a multiple of tp_size");
+    }
     if (!a.hidden || !a.layers || !a.heads || !a.kv_heads || a.hidden % a.heads || a.heads % a.kv_heads || !a.ffn || !a.vocab)
         return fail(LAIC_E_INVALID, "invalid llama architecture metadata");
     const uint32_t D = a.hidden / a.heads;
@@ -629,8 +683,10 @@ int laic_dev_create(const laic_dev_desc* desc, const laic_dev_opts* opts, laic_d
     std::unique_ptr<laic_dev> d(new laic_dev());
     d->a = a; d->a.ctx = ctx; d->a.rope_dim = rd;
     d->o = o; d->device = o.device;
-    d->H = a.heads; d->Hkv = a.kv_heads; d->D = D; d->G = a.heads / a.kv_heads; d->h = a.hidden;
-    d->kv = a.kv_heads * D; d->F = a.ffn; d->V = a.vocab; d->L = a.layers; d->S = o.max_seqs; d->cap = cap;
+    d->tp = tp; d->tr = tp > 1 ? o.tp_rank : 0;
+    d->H = a.heads / tp; d->Hkv = a.kv_heads / tp; d->D = D; d->G = a.heads / a.kv_heads; d->h = a.hidden;
+    d->kv = d->Hkv * D; d->hq = d->H * D; d->F = a.ffn / tp; d->V = a.vocab; d->Vl = a.vocab / tp;
+    d->L = a.layers; d->S = o.max_seqs; d->cap = cap;
     d->rope_pairs = rd / 2;
     d->kv32 = (o.flags & LAIC_FLAG_KV_F32) != 0;
     d->use_graph = !(o.flags & LAIC_FLAG_NO_GRAPH);
@@ -646,10 +702,21 @@ int laic_dev_create(const laic_dev_desc* desc, const laic_dev_opts* opts, laic_d
 
     const size_t S = o.max_seqs, kvb = d->kv32 ? 4 : 2;
     CK(cudaMalloc(&d->x, S * d->h * 4));
-    CK(cudaMalloc(&d->q, S * d->h * 4));
-    CK(cudaMalloc(&d->attn, S * d->h * 4));
+    CK(cudaMalloc(&d->q, S * d->hq * 4));
+    CK(cudaMalloc(&d->attn, S * d->hq * 4));
     CK(cudaMalloc(&d->act, S * d->F * 4));
     CK(cudaMalloc(&d->logits, S * d->V * 4));
+    if (tp > 1) {
+        CK(cudaMalloc(&d->logits_l, S * d->Vl * 4));
+        CK(cudaMalloc(&d->logits_g, S * d->V * 4));
+        std::string why;
+        d->nccl = laic::nccl_api(why);
+        if (!d->nccl) return fail(LAIC_E_NCCL, why);
+        laic::ncclUniqueId id;
+        std::memcpy(&id, o.nccl_id, sizeof id);
+        const laic::ncclResult_t r = d->nccl->CommInitRank(&d->comm, tp, id, d->tr);
+        if (r != laic::ncclSuccess) return fail(LAIC_E_NCCL, std::string("ncclCommInitRank: ") + d->nccl->GetErrorString(r));
+    }
     d->kv_slot_stride = (long long)d->Hkv * cap * D;
     d->kv_layer_stride = d->kv_slot_stride * (long long)S;
     const size_t kv_bytes = (size_t)d->kv_layer_stride * d->L * kvb;
@@ -700,7 +767,9 @@ void laic_dev_destroy(laic_dev* d) {
     if (!d) return;
     cudaSetDevice(d->device);
     cudaStreamSynchronize(d->st);
-    for (auto& kv : d->graphs) cudaGraphExecDestroy(kv.second);
+    for (auto& kv : d->graphs) cudaGraphExecDestroy(kv.second);  // graphs holding NCCL calls go first
+    d->graphs.clear();
+    if (d->comm) d->nccl->CommDestroy(d->comm);
     for (auto& l : d->layers) {
         mat_free(l.qkv); mat_free(l.o); mat_free(l.gu); mat_free(l.down);
         if (l.attn_norm) cudaFree(l.attn_norm);
@@ -710,7 +779,7 @@ void laic_dev_destroy(laic_dev* d) {
     mv_scratch_free(d->mvs);
     void* bufs[] = {d->out_norm, d->x, d->q, d->attn, d->act, d->logits, d->kc, d->vc, d->pos, d->counts,
                     d->rope_cs, d->attn_part, d->attn_cnt, d->d_tokens, d->d_out_ids, d->d_slots, d->d_err, d->d_params,
-                    d->d_hist, d->d_hist_count};
+                    d->d_hist, d->d_hist_count, d->logits_l, d->logits_g};
     for (void* b : bufs) if (b) cudaFree(b);
     void* hb[] = {d->h_tokens, d->h_out_ids, d->h_slots, d->h_params};
     for (void* b : hb) if (b) cudaFreeHost(b);
@@ -741,6 +810,18 @@ int laic_dev_upload(laic_dev* d, const char* cname, int32_t type, const uint64_t
         const bool is_embd = name == "token_embd.weight";
         if (ndim != 2 || shape[0] != (uint64_t)d->h) return fail(LAIC_E_INVALID, "unexpected weight shape: " + name);
         if (!is_embd && shape[1] != (uint64_t)d->V) return fail(LAIC_E_INVALID, "unexpected weight shape: " + name);
+        if (d->tp > 1 && (is_embd ? !d->have_out : true)) {
+            // this rank's lm_head rows (the output matrix, or the tied embedding until one arrives)
+            if (is_embd && shape[1] != (uint64_t)d->V) return fail(LAIC_E_INVALID, "unexpected weight shape: " + name);
+            mat_free(d->lm);
+            int rc = mat_alloc(d->lm, type, d->Vl, d->h);
+            if (rc) return rc;
+            const size_t rb = elem_bytes(type, (size_t)d->h);
+            rc = mat_fill(d->lm, (const uint8_t*)data + (size_t)d->tr * d->Vl * rb, d->Vl, 1, 0, d->st);
+            if (rc) return rc;
+            d->have_lm = true;
+            if (!is_embd) { d->have_out = true; return LAIC_OK; }
+        }
         Mat& m = is_embd ? d->embd : d->lm;
         mat_free(m);
         int rc = mat_alloc(m, type, (int)shape[1], d->h);
@@ -754,7 +835,20 @@ int laic_dev_upload(laic_dev* d, const char* cname, int32_t type, const uint64_t
     std::string part;
     if (!parse_layer(name, l, part) || l < 0 || l >= d->L) return LAIC_OK;  // not used by the decode path
     Layer& ly = d->layers[l];
-    const int h = d->h, kv = d->kv, F = d->F;
+    // h: hidden; hq, kv, F: this rank's query width, kv width and ffn rows; *_full: the GGUF's
+    const int h = d->h, kv = d->kv, F = d->F, hq = d->hq, tr = d->tr;
+    const int kv_full = (int)d->a.kv_heads * d->D, F_full = (int)d->a.ffn;
+    const uint8_t* src = (const uint8_t*)data;
+    // rows [r0, ...) of a [rows][in] tensor; columns [c0, c0 + nc) of each row gathered on the host
+    auto rows_from = [&](int r0, int in) { return src + (size_t)r0 * elem_bytes(type, (size_t)in); };
+    std::vector<uint8_t> colbuf;
+    auto cols_of = [&](int rows, int in, int c0, int nc) -> const uint8_t* {
+        if (c0 == 0 && nc == in) return src;
+        const size_t rb = elem_bytes(type, (size_t)in), cb = elem_bytes(type, (size_t)nc), ob = elem_bytes(type, (size_t)c0);
+        colbuf.resize((size_t)rows * cb);
+        for (int r = 0; r < rows; ++r) std::memcpy(colbuf.data() + (size_t)r * cb, src + (size_t)r * rb + ob, cb);
+        return colbuf.data();
+    };
     auto ensure = [&](Mat& m, int rows, int in) -> int {
         if (m.q && m.type != type) return fail(LAIC_E_UNSUPPORTED, "fused projections need one type: " + name);
         if (!m.q) return mat_alloc(m, type, rows, in);
@@ -767,26 +861,27 @@ int laic_dev_upload(laic_dev* d, const char* cname, int32_t type, const uint64_t
         rc = upload_norm(an ? &ly.attn_norm : &ly.ffn_norm, type, data, n, nbytes);
         if (!rc) ly.have |= an ? H_ANORM : H_FNORM;
     } else if (part == "attn_q" || part == "attn_k" || part == "attn_v") {
-        const int out = part == "attn_q" ? h : kv;
-        if (!shape_is(h, out)) return fail(LAIC_E_INVALID, "unexpected weight shape: " + name);
-        if ((rc = ensure(ly.qkv, h + 2 * kv, h))) return rc;
-        const long long off = part == "attn_q" ? 0 : part == "attn_k" ? h : h + kv;
-        rc = mat_fill(ly.qkv, (const uint8_t*)data, out, 1, off, d->st);
-        if (!rc) ly.have |= part == "attn_q" ? H_Q : part == "attn_k" ? H_K : H_V;
+        const bool isq = part == "attn_q";
+        if (!shape_is(h, isq ? h : kv_full)) return fail(LAIC_E_INVALID, "unexpected weight shape: " + name);
+        if ((rc = ensure(ly.qkv, hq + 2 * kv, h))) return rc;
+        const int out = isq ? hq : kv;  // this rank's heads: rows [tr * out, (tr + 1) * out)
+        const long long off = isq ? 0 : part == "attn_k" ? hq : hq + kv;
+        rc = mat_fill(ly.qkv, rows_from(tr * out, h), out, 1, off, d->st);
+        if (!rc) ly.have |= isq ? H_Q : part == "attn_k" ? H_K : H_V;
     } else if (part == "attn_output") {
         if (!shape_is(h, h)) return fail(LAIC_E_INVALID, "unexpected weight shape: " + name);
-        if ((rc = ensure(ly.o, h, h))) return rc;
-        rc = mat_fill(ly.o, (const uint8_t*)data, h, 1, 0, d->st);
+        if ((rc = ensure(ly.o, h, hq))) return rc;
+        rc = mat_fill(ly.o, cols_of(h, h, tr * hq, hq), h, 1, 0, d->st);  // columns of this rank's heads
         if (!rc) ly.have |= H_O;
     } else if (part == "ffn_gate" || part == "ffn_up") {
-        if (!shape_is(h, F)) return fail(LAIC_E_INVALID, "unexpected weight shape: " + name);
+        if (!shape_is(h, F_full)) return fail(LAIC_E_INVALID, "unexpected weight shape: " + name);
         if ((rc = ensure(ly.gu, 2 * F, h))) return rc;
-        rc = mat_fill(ly.gu, (const uint8_t*)data, F, 2, part == "ffn_gate" ? 0 : 1, d->st);
+        rc = mat_fill(ly.gu, rows_from(tr * F, h), F, 2, part == "ffn_gate" ? 0 : 1, d->st);
         if (!rc) ly.have |= part == "ffn_gate" ? H_GATE : H_UP;
     } else if (part == "ffn_down") {
-        if (!shape_is(F, h)) return fail(LAIC_E_INVALID, "unexpected weight shape: " + name);
+        if (!shape_is(F_full, h)) return fail(LAIC_E_INVALID, "unexpected weight shape: " + name);
         if ((rc = ensure(ly.down, h, F))) return rc;
-        rc = mat_fill(ly.down, (const uint8_t*)data, h, 1, 0, d->st);
+        rc = mat_fill(ly.down, cols_of(h, F_full, tr * F, F), h, 1, 0, d->st);  // this rank's ffn columns
         if (!rc) ly.have |= H_DOWN;
     }
     return rc;
@@ -920,7 +1015,7 @@ int laic_dev_stats_get(laic_dev* d, laic_dev_stats* s) {
     s->launches_per_step = d->launches_step;  // of the most recently enqueued step (chained: + id record)
     s->launches_per_prefill = d->launches_prefill;
     s->attn_splits = d->last_split;
-    s->tp_size = 1;
+    s->tp_size = d->tp;
     return LAIC_OK;
 }
 
@@ -974,11 +1069,16 @@ int laic_dev_profile(laic_dev* d, int32_t nseq, const uint32_t* tokens, int32_t 
     std::vector<int32_t> slots(nseq);
     for (int i = 0; i < nseq; ++i) slots[i] = i;
     std::vector<laic_kernel_record> recs;
+    int rc0 = d->reserve_scratch(nseq);
+    if (rc0) return rc0;
     for (int it = 0; it < steps; ++it) {
         int rc = fill_inputs(d, nseq, tokens + (size_t)it * nseq, slots.data());
         if (rc) return rc;
         if ((rc = fill_params(d, nseq, nullptr, 0))) return rc;
         laic_dev::Timer t;
+        // hold the stream while the host queues the step, so the events time the kernels, not the host
+        laic::hold_kernel<<<1, 1, 0, d->st>>>(20000000LL);
+        CK(cudaGetLastError());
         rc = d->enqueue(nseq, MODE_STEP, d->st, &t);
         CK(cudaStreamSynchronize(d->st));
         for (int i = 0; i < nseq; ++i) d->h_pos[i] += 1;
@@ -1007,8 +1107,15 @@ int laic_dev_profile(laic_dev* d, int32_t nseq, const uint32_t* tokens, int32_t 
 }
 
 int laic_nccl_unique_id(void* out128) {
-    (void)out128;
-    return fail(LAIC_E_UNSUPPORTED, "tensor parallelism is not built into this library yet");
+    if (!out128) return fail(LAIC_E_INVALID, "null argument");
+    std::string why;
+    const laic::NcclApi* api = laic::nccl_api(why);
+    if (!api) return fail(LAIC_E_NCCL, why);
+    laic::ncclUniqueId id;
+    const laic::ncclResult_t r = api->GetUniqueId(&id);
+    if (r != laic::ncclSuccess) return fail(LAIC_E_NCCL, std::string("ncclGetUniqueId: ") + api->GetErrorString(r));
+    std::memcpy(out128, &id, sizeof id);
+    return LAIC_OK;
 }
 
 // ---- single tensors --------------------------------------------------------

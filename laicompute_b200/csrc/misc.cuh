@@ -30,6 +30,29 @@ __global__ void embed_kernel(const EmbedParams p) {
     pdl_launch_dependents();
 }
 
+// Keeps the stream busy for about `ns` nanoseconds (at most 0.2 s), so that the
+// launches queued behind it run back to back instead of waiting on the host.
+__global__ void hold_kernel(long long ns) {
+    ns = ns < 200000000LL ? ns : 200000000LL;
+    unsigned long long t0, t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    do {
+        __nanosleep(1000);
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    } while ((long long)(t - t0) < ns);
+}
+
+// Tensor parallel: all-gathered logits [ranks][nseq][vl] -> [nseq][ranks * vl].
+__global__ void gather_logits_kernel(const float* g, float* out, int ranks, int nseq, int vl) {
+    pdl_wait();
+    const long long n = (long long)ranks * nseq * vl;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const long long t = i / vl;
+        const int v = (int)(i - t * vl), s = (int)(t % nseq), r = (int)(t / nseq);
+        out[((long long)s * ranks + r) * vl + v] = g[i];
+    }
+}
+
 // End of a prefill step (no sampler): every listed slot moves to the next position.
 __global__ void advance_pos_kernel(const int* slots, int* pos, int nseq) {
     pdl_wait();

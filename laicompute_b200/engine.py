@@ -159,6 +159,13 @@ class Engine:
         return np.array(ids, dtype=np.uint32), (np.stack(all_logits) if want_logits else None)
 
 
+def nccl_unique_id() -> bytes:
+    """128-byte NCCL id for the ranks of one tensor-parallel engine (create on rank 0, share)."""
+    buf = ctypes.create_string_buffer(128)
+    check(lib().laic_nccl_unique_id(buf))
+    return buf.raw
+
+
 class Matrix:
     """One uploaded weight matrix ([out][in], GGUF shape {in, out}) for the single-tensor entry points."""
 
