@@ -506,25 +506,32 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const AttnPar
 
     const size_t pair = (size_t)seq * p.kv_heads + kvh;
     const int PD = D + 2;
+    // per head: the warps' log-sum-exp weights, once
+    __shared__ float mw[64][8];  // weights of the warps, then of the splits
+    __shared__ float mM[8], mL[8];
+    if (threadIdx.x < G) {
+        const int g = threadIdx.x;
+        float M = -INFINITY, L = 0.f;
+        for (int w = 0; w < NW; ++w) M = fmaxf(M, cm[w][g]);
+        for (int w = 0; w < NW; ++w) {
+            const float e = cm[w][g] == -INFINITY ? 0.f : expf(cm[w][g] - M);
+            mw[w][g] = e;
+            L = fmaf(cl[w][g], e, L);
+        }
+        mM[g] = M; mL[g] = L;
+    }
+    __syncthreads();
     for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
         const int g = i / D, dd = i % D;
-        float M = -INFINITY;
-        for (int w = 0; w < NW; ++w) M = fmaxf(M, cm[w][g]);
-        float L = 0.f, A = 0.f;
-        if (M != -INFINITY) {
-            for (int w = 0; w < NW; ++w) {
-                if (cm[w][g] == -INFINITY) continue;
-                const float e = expf(cm[w][g] - M);
-                L = fmaf(cl[w][g], e, L);
-                A = fmaf(cacc[((size_t)w * 8 + g) * D + dd], e, A);
-            }
-        }
+        float A = 0.f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) A = fmaf(cacc[((size_t)w * 8 + g) * D + dd], mw[w][g], A);
         if (active == 1) {
-            p.out[(size_t)seq * p.ldo + ((size_t)kvh * G + g) * D + dd] = A / L;
+            p.out[(size_t)seq * p.ldo + ((size_t)kvh * G + g) * D + dd] = A / mL[g];
         } else {
             float* dst = p.part + ((pair * p.nsplit + split) * G + g) * PD;
             dst[dd] = A;
-            if (dd == 0) { dst[D] = M; dst[D + 1] = L; }
+            if (dd == 0) { dst[D] = mM[g]; dst[D + 1] = mL[g]; }
         }
     }
     if (active == 1) return;
@@ -536,21 +543,26 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const AttnPar
     __syncthreads();
     if (!is_last) return;
     __threadfence();
+    const size_t sstride = (size_t)G * PD;
+    const float* base = p.part + pair * p.nsplit * sstride;
+    if (threadIdx.x < G) {  // per head: the splits' weights (active <= 64 splits)
+        const int g = threadIdx.x;
+        float M = -INFINITY, L = 0.f;
+        for (int j = 0; j < active; ++j) M = fmaxf(M, __ldcg(base + j * sstride + g * PD + D));
+        for (int j = 0; j < active; ++j) {
+            const float mj = __ldcg(base + j * sstride + g * PD + D);
+            const float e = mj == -INFINITY ? 0.f : expf(mj - M);
+            mw[j][g] = e;
+            L = fmaf(__ldcg(base + j * sstride + g * PD + D + 1), e, L);
+        }
+        mL[g] = L;
+    }
+    __syncthreads();
     for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
         const int g = i / D, dd = i % D;
-        const float* src = p.part + (pair * p.nsplit * G + g) * PD;
-        const size_t sstride = (size_t)G * PD;
-        float M = -INFINITY;
-        for (int j = 0; j < active; ++j) M = fmaxf(M, __ldcg(src + j * sstride + D));
-        float L = 0.f, A = 0.f;
-        for (int j = 0; j < active; ++j) {
-            const float mj = __ldcg(src + j * sstride + D);
-            if (mj == -INFINITY) continue;
-            const float e = expf(mj - M);
-            L = fmaf(__ldcg(src + j * sstride + D + 1), e, L);
-            A = fmaf(__ldcg(src + j * sstride + dd), e, A);
-        }
-        p.out[(size_t)seq * p.ldo + ((size_t)kvh * G + g) * D + dd] = A / L;
+        float A = 0.f;
+        for (int j = 0; j < active; ++j) A = fmaf(__ldcg(base + j * sstride + g * PD + dd), mw[j][g], A);
+        p.out[(size_t)seq * p.ldo + ((size_t)kvh * G + g) * D + dd] = A / mL[g];
     }
     if (threadIdx.x == 0) p.counters[pair] = 0u;
 }

@@ -159,7 +159,8 @@ MvShape mv_shape(const Mat& m, int B) {
         const size_t smem = laic::sk_smem_bytes(m.type, m.nb, B);
         if (smem <= kSmemBudget) {
             sh.sk = true;
-            sh.nt = B <= 4 ? 1 : B <= 8 ? 2 : 4;  // hi and lo activation columns side by side
+            // one sequence of Q4_0 / Q8_0: integer dot products (nt 0); else hi and lo columns side by side
+            sh.nt = (B == 1 && m.type != T_F16) ? 0 : B <= 4 ? 1 : B <= 8 ? 2 : 4;
             sh.grid = std::max(1, std::min(num_sms(), m.ntiles));  // each CTA owns whole row tiles
             sh.smem = smem;
             sh.part_floats = 0;

@@ -51,6 +51,11 @@ cudaError_t mv_set_attributes() {
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
                         if (e != cudaSuccess) return e;
                     }
+                    if (nt == 1 && type != T_F16) {  // the integer variant (nt 0)
+                        e = cudaFuncSetAttribute(mv_sk_kernel(type, 0, epi, kv32),
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+                        if (e != cudaSuccess) return e;
+                    }
                 }
     return cudaSuccess;
 }

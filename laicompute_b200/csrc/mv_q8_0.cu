@@ -35,7 +35,9 @@ static void (*pick_sk_q8_0(int epi, bool kv32))(MvParams) {
 }
 
 void (*mv_sk_kernel_q8_0(int nt, int epi, bool kv32))(MvParams) {
-    return nt == 1 ? pick_sk_q8_0<1>(epi, kv32) : nt == 2 ? pick_sk_q8_0<2>(epi, kv32) : pick_sk_q8_0<4>(epi, kv32);
+    // nt 0: the single-sequence integer variant
+    return nt == 0 ? pick_sk_q8_0<0>(epi, kv32) : nt == 1 ? pick_sk_q8_0<1>(epi, kv32)
+         : nt == 2 ? pick_sk_q8_0<2>(epi, kv32) : pick_sk_q8_0<4>(epi, kv32);
 }
 
 }  // namespace laic

@@ -12,6 +12,20 @@
 // completes a tile adds the team's partials in warp order (deterministic) and
 // runs the epilogue. The streaming loop never waits on global memory, and no
 // CTA-wide barrier is taken after the activation prologue.
+//
+// NT = 0 is the single-sequence integer variant for Q4_0 / Q8_0: the same
+// tiles and rings, but each lane forms exact integer dot products of its
+// quants with the activation split into three int8 digits (dp4a), instead of
+// converting quants to binary16 for mma.sync, where one sequence fills 2 of
+// the 8 product columns. Per 32-column block the activation is scaled by a
+// power of two that puts its largest magnitude in [2^19, 2^20), rounded to an
+// integer x (21 bits, exact in the digits below) and written as balanced
+// base-128 digits x = p0 * 2^14 + p1 * 2^7 + p2 (each in [-64, 64]). For a
+// row's 8 columns c..c+7 of the block:
+//   sum_k q_k x_k = 2^14 sum q p0 + 2^7 sum q p1 + sum q p2
+// with q the stored quant (Q4_0: the nibble n, corrected by -8 * sum x; Q8_0:
+// the int8 value), all in int32 without rounding; then
+//   acc += float(sum) * d * 2^-scale   (d the block scale, FP32 accumulate).
 #pragma once
 #include "mma_matvec.cuh"
 
@@ -45,6 +59,69 @@ __host__ __device__ inline size_t sk_smem_bytes(int type, int nb, int B) {
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// d = sum of the four products of unsigned bytes of a and signed bytes of b, plus c
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// Activation record of one 32-column block for the integer variant: for each
+// 8-column group c (32 bytes at c * 32): digits p0, p1, p2 as two words each
+// (the quants' byte order of this lane's fragment), then -8 * sum x over the
+// group (Q4_0, else 0) and the block's scale 2^-s as a float.
+constexpr int kDpRecBytes = 128;
+
+// Byte of element k (0..7) of an 8-column group inside the two words of a
+// lane's fragment: Q4_0 packs (e0,e1) (e2,e3) (e4,e5) (e6,e7) as nibble pairs,
+// read as low nibbles (e0 e2 e4 e6) and high nibbles (e1 e3 e5 e7);
+// Q8_0 stores e0 e4 e1 e5 | e2 e6 e3 e7.
+template <int WT>
+__device__ __forceinline__ int dp_byte_of(int k) {
+    if (WT == T_Q4_0) return (k & 1) * 4 + (k >> 1);
+    return frag_pos(k);
+}
+
+// One 16x32 tile-block of the integer variant: rows g and g+8, columns 8c..8c+7.
+template <int WT>
+__device__ __forceinline__ void tile_block_dp(uint32_t q, uint32_t sc, uint32_t xrec, int lane, float (&acc)[2]) {
+    const int g = lane >> 2;
+    const uint4 xa = lds128(xrec), xb = lds128(xrec + 16);
+    const int x8 = (int)xb.z;
+    const float sinv = __uint_as_float(xb.w);
+    const uint32_t dp = lds32(sc + g * 4);
+    const float2 df = __half22float2(*reinterpret_cast<const __half2*>(&dp));
+    uint32_t wl[2], wh[2];  // per row: the two quant words in the activation digits' byte order
+    if (WT == T_Q4_0) {
+        const uint2 w = lds64(q + lane * 8);
+        wl[0] = w.x & 0x0F0F0F0Fu; wh[0] = (w.x >> 4) & 0x0F0F0F0Fu;
+        wl[1] = w.y & 0x0F0F0F0Fu; wh[1] = (w.y >> 4) & 0x0F0F0F0Fu;
+    } else {
+        const uint4 w = lds128(q + lane * 16);
+        wl[0] = w.x; wh[0] = w.y; wl[1] = w.z; wh[1] = w.w;
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        int s0, s1, s2;
+        if (WT == T_Q4_0) {
+            s2 = dp4a_us(wh[r], xb.y, dp4a_us(wl[r], xb.x, x8));  // x8 = -8 * sum x (the nibbles' offset)
+            s1 = dp4a_us(wh[r], xa.w, dp4a_us(wl[r], xa.z, 0));
+            s0 = dp4a_us(wh[r], xa.y, dp4a_us(wl[r], xa.x, 0));
+        } else {
+            s2 = dp4a_ss(wh[r], xb.y, dp4a_ss(wl[r], xb.x, 0));
+            s1 = dp4a_ss(wh[r], xa.w, dp4a_ss(wl[r], xa.z, 0));
+            s0 = dp4a_ss(wh[r], xa.y, dp4a_ss(wl[r], xa.x, 0));
+        }
+        const int v = s0 * 16384 + s1 * 128 + s2;  // exact: |v| < 2^30
+        acc[r] = fmaf((float)v, (r ? df.y : df.x) * sinv, acc[r]);
+    }
 }
 
 // One 16x32 tile-block: decode this lane's A fragments, multiply with the
@@ -105,7 +182,9 @@ __global__ void __launch_bounds__(kSkWarps * 32, 1) mv_sk_kernel(const MvParams 
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, c = lane & 3;
-    const int B = p.nseq;
+    constexpr bool DP = NT == 0;  // integer variant, one sequence
+    static_assert(!DP || WT != T_F16, "the integer variant takes Q4_0 or Q8_0");
+    const int B = DP ? 1 : p.nseq;
     const int nb = p.nb;
 
     uint8_t* ring = smem + warp * R * STAGE;
@@ -158,7 +237,74 @@ __global__ void __launch_bounds__(kSkWarps * 32, 1) mv_sk_kernel(const MvParams 
     pdl_wait();
 
     // ---- prologue: the whole activation vector -> binary16 hi/lo in fragment order
-    {
+    //      (integer variant: int8 digit records, one warp per 32-column block)
+    if constexpr (DP) {
+        const float4* src = reinterpret_cast<const float4*>(p.x);
+        const float4* nw4 = reinterpret_cast<const float4*>(p.norm_w);
+        float ss = 0.f;
+        if (p.norm_w) {
+            for (int f = threadIdx.x; f < (p.in >> 2); f += blockDim.x) {
+                const float4 v = src[f];
+                ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+            }
+            ss = warp_sum(ss);
+            if (lane == 0) wstat[warp * 2] = ss;
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                float a = 0.f;
+                for (int w = 0; w < kSkWarps; ++w) a += wstat[w * 2];
+                inv[0] = 1.f / sqrtf(a / float(p.in) + p.eps);
+            }
+            __syncthreads();
+        }
+        if (threadIdx.x == 0) xsc[0] = 1.f;  // the digit scales are applied per block
+        const float iv = p.norm_w ? inv[0] : 1.f;
+        // one thread per 8-column group (four per block); the block's four threads are adjacent
+        // lanes. Every lane runs each round (the shuffles need the whole warp); lanes past the
+        // last group compute on zeros and store nothing.
+        for (int base = 0; base < nb * 4; base += blockDim.x) {
+            const int gi = base + threadIdx.x;
+            const bool live = gi < nb * 4;
+            const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 a0 = live ? src[2 * gi] : z4, a1 = live ? src[2 * gi + 1] : z4;
+            float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            if (p.norm_w && live) {
+                const float4 w0 = nw4[2 * gi], w1 = nw4[2 * gi + 1];
+                const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+                for (int k = 0; k < 8; ++k) v[k] = v[k] * (iv * w[k]);
+            }
+            float mx = 0.f;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) mx = fmaxf(mx, fabsf(v[k]));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            int ex = 0;
+            if (mx > 0.f && isfinite(mx)) frexpf(mx, &ex);  // mx in [2^(ex-1), 2^ex)
+            uint32_t dw[3][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}};  // digit words p0 p1 p2, quant byte order
+            int gs = 0;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const int xi = (int)rintf(ldexpf(v[k], 20 - ex));  // |xi| <= 2^20
+                const int p2 = ((xi + 64) & 127) - 64;
+                const int t1 = (xi - p2) >> 7;
+                const int p1 = ((t1 + 64) & 127) - 64;
+                const int p0 = (t1 - p1) >> 7;
+                gs += xi;
+                const int pos = dp_byte_of<WT>(k), wd = pos >> 2, sh = (pos & 3) * 8;
+                dw[0][wd] |= (uint32_t)(p0 & 0xFF) << sh;
+                dw[1][wd] |= (uint32_t)(p1 & 0xFF) << sh;
+                dw[2][wd] |= (uint32_t)(p2 & 0xFF) << sh;
+            }
+            if (live) {
+                uint4* rec = reinterpret_cast<uint4*>(xs + (size_t)gi * 32);  // block gi/4, group gi%4
+                rec[0] = make_uint4(dw[0][0], dw[0][1], dw[1][0], dw[1][1]);
+                rec[1] = make_uint4(dw[2][0], dw[2][1], (uint32_t)(WT == T_Q4_0 ? -8 * gs : 0),
+                                    __float_as_uint(ldexpf(1.f, ex - 20)));
+            }
+        }
+        __syncthreads();
+    } else {
         const int nv = p.in >> 2;  // float4 per sequence
 #pragma unroll
         for (int s = 0; s < NT * 8; ++s) {
@@ -216,7 +362,7 @@ __global__ void __launch_bounds__(kSkWarps * 32, 1) mv_sk_kernel(const MvParams 
     }
 
     // ---- finish one tile: this warp's partial -> slot; the last of the team adds and runs the epilogue
-    float acc[NT][4];
+    float acc[DP ? 1 : NT][4];  // integer variant: acc[0][0..1] = rows g and g+8 of this lane's columns
     auto finish = [&](int t, int tile_idx) {
         const int slot = tile_idx % kSkSlots;
         float* mine = parts + ((size_t)warp * kSkSlots + slot) * 16 * B;
@@ -230,14 +376,25 @@ __global__ void __launch_bounds__(kSkWarps * 32, 1) mv_sk_kernel(const MvParams 
             }
             __syncwarp();
         }
+        if constexpr (DP) {
+            // the four lanes of a row hold its four 8-column groups
+            float r0 = acc[0][0], r1 = acc[0][1];
+            r0 += __shfl_xor_sync(0xffffffffu, r0, 1);
+            r1 += __shfl_xor_sync(0xffffffffu, r1, 1);
+            r0 += __shfl_xor_sync(0xffffffffu, r0, 2);
+            r1 += __shfl_xor_sync(0xffffffffu, r1, 2);
+            if (c == 0) { mine[g] = r0; mine[g + 8] = r1; }
+            acc[0][0] = acc[0][1] = 0.f;
+        } else {
 #pragma unroll
-        for (int j = 0; j < NT; ++j) {
-            const int sq = j * 4 + c;  // columns 2sq (hi) and 2sq+1 (lo)
-            if (sq < B) {
-                mine[g * B + sq] = acc[j][0] + acc[j][1];
-                mine[(g + 8) * B + sq] = acc[j][2] + acc[j][3];
+            for (int j = 0; j < NT; ++j) {
+                const int sq = j * 4 + c;  // columns 2sq (hi) and 2sq+1 (lo)
+                if (sq < B) {
+                    mine[g * B + sq] = acc[j][0] + acc[j][1];
+                    mine[(g + 8) * B + sq] = acc[j][2] + acc[j][3];
+                }
+                acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
             }
-            acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
         }
         __threadfence_block();
         __syncwarp();
@@ -300,14 +457,18 @@ __global__ void __launch_bounds__(kSkWarps * 32, 1) mv_sk_kernel(const MvParams 
 
     // ---- stream this warp's slices
 #pragma unroll
-    for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    for (int j = 0; j < (DP ? 1 : NT); ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
     // this lane's activation column in each n-tile
-    uint32_t xlane[NT];  // shared-memory addresses
-    const int xstride = 2 * B * 4 * 16;  // bytes between the records of consecutive blocks
+    uint32_t xlane[DP ? 1 : NT];  // shared-memory addresses
+    const int xstride = DP ? kDpRecBytes : 2 * B * 4 * 16;  // bytes between the records of consecutive blocks
+    if constexpr (DP) {
+        xlane[0] = smem_u32(xs) + c * 32;  // this lane's 8-column group of each block record
+    } else {
 #pragma unroll
-    for (int j = 0; j < NT; ++j) {
-        const int col = min(j * 8 + g, 2 * B - 1);
-        xlane[j] = smem_u32(xs) + (col * 4 + c) * 16;
+        for (int j = 0; j < NT; ++j) {
+            const int col = min(j * 8 + g, 2 * B - 1);
+            xlane[j] = smem_u32(xs) + (col * 4 + c) * 16;
+        }
     }
     const uint32_t ring_a = smem_u32(ring);
     bool aborted = false;
@@ -319,7 +480,16 @@ __global__ void __launch_bounds__(kSkWarps * 32, 1) mv_sk_kernel(const MvParams 
         const int n = aborted ? 0 : min(KB, b_hi - b0);
         const uint32_t sq = ring_a + slot * STAGE;
         const uint32_t ssc = sq + KB * QB;
-        if (n == KB) {
+        if constexpr (DP) {
+            float (&a2)[2] = *reinterpret_cast<float(*)[2]>(&acc[0][0]);
+            const uint32_t xr = xlane[0] + b0 * kDpRecBytes;
+            if (n == KB) {
+#pragma unroll
+                for (int j = 0; j < KB; ++j) tile_block_dp<WT>(sq + j * QB, ssc + j * SB, xr + j * kDpRecBytes, lane, a2);
+            } else {
+                for (int j = 0; j < n; ++j) tile_block_dp<WT>(sq + j * QB, ssc + j * SB, xr + j * kDpRecBytes, lane, a2);
+            }
+        } else if (n == KB) {
 #pragma unroll
             for (int j = 0; j < KB; ++j) tile_block<WT, NT>(sq + j * QB, ssc + j * SB, xlane, b0 + j, xstride, lane, acc);
         } else {

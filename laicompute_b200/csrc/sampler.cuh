@@ -107,12 +107,31 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplerPar
     const bool pen = sp.repeat_penalty != 1.f;
     auto L = [&](int i) { return pen ? penalized(lg[i], cnt[i], sp.repeat_penalty) : lg[i]; };
 
-    // block argmax with lowest index on ties; also the maximum for the softmax
+    // block argmax with lowest index on ties; also the maximum for the softmax.
+    // Each thread walks its indices in increasing order (four per float4, several
+    // float4 loads in flight), so a strict > keeps its first maximum.
     float bv = -INFINITY;
     int bi = 0x7fffffff;
-    for (int i = tid; i < V; i += kSampleThreads) {
-        const float v = L(i);
+    auto consider = [&](float v, int i) {
         if (v > bv || bi == 0x7fffffff) { bv = v; bi = i; }
+    };
+    const bool vec = (V % 4 == 0) && (p.ldl % 4 == 0);
+    if (vec) {
+        const float4* lg4 = reinterpret_cast<const float4*>(lg);
+        const uint4* cn4 = reinterpret_cast<const uint4*>(cnt);
+        const int V4 = V / 4;
+#pragma unroll 8
+        for (int i4 = tid; i4 < V4; i4 += kSampleThreads) {
+            float4 v = lg4[i4];
+            if (pen) {
+                const uint4 c = cn4[i4];
+                v.x = penalized(v.x, c.x, sp.repeat_penalty); v.y = penalized(v.y, c.y, sp.repeat_penalty);
+                v.z = penalized(v.z, c.z, sp.repeat_penalty); v.w = penalized(v.w, c.w, sp.repeat_penalty);
+            }
+            consider(v.x, 4 * i4); consider(v.y, 4 * i4 + 1); consider(v.z, 4 * i4 + 2); consider(v.w, 4 * i4 + 3);
+        }
+    } else {
+        for (int i = tid; i < V; i += kSampleThreads) consider(L(i), i);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {

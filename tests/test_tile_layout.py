@@ -182,3 +182,67 @@ def test_fragment_emulation_matches_dense(t_, B):
     wd = O.dequant(t_, raw, rows * nb * 32).reshape(rows, nb * 32).astype(np.float64)
     ref = wd @ x.astype(np.float64).T
     assert np.allclose(y, ref, rtol=0, atol=1e-6 * np.abs(wd).sum(axis=1, keepdims=True).max())
+
+
+def dp_byte_of(t_, k):
+    """Byte (0..7) of element k of an 8-column group in a lane's two quant words."""
+    return (k & 1) * 4 + (k >> 1) if t_ == gguf.Q4_0 else frag_pos(k)
+
+
+def digits(x):
+    """Per 32-column block: integers |xi| <= 2^20 and balanced base-128 digits (the integer variant's prologue)."""
+    mx = np.abs(x).max()
+    ex = int(np.frexp(np.float32(mx))[1]) if mx > 0 else 0
+    xi = np.rint(np.ldexp(x.astype(np.float32), 20 - ex)).astype(np.int64)
+    p2 = ((xi + 64) & 127) - 64
+    t1 = (xi - p2) >> 7
+    p1 = ((t1 + 64) & 127) - 64
+    p0 = (t1 - p1) >> 7
+    assert np.all(np.abs(np.stack([p0, p1, p2])) <= 64)
+    assert np.array_equal(p0 * 16384 + p1 * 128 + p2, xi)
+    return xi, (p0, p1, p2), np.float32(np.ldexp(1.0, ex - 20))
+
+
+def emulate_integer(t_, q, s, x, rows, nb):
+    """Replay the one-sequence integer variant (mv_streamk.cuh, NT = 0) on the fragment layout."""
+    ntiles = (rows + 15) // 16
+    y = np.zeros(ntiles * 16)
+    for b in range(nb):
+        xi, pcs, sinv = digits(x[b * 32:(b + 1) * 32])
+        for t in range(ntiles):
+            chunk = q[(t * nb + b) * QB[t_]:(t * nb + b + 1) * QB[t_]]
+            for lane in range(32):
+                g, c = lane >> 2, lane & 3
+                # digit words of group c in the quants' byte order
+                dw = np.zeros((3, 8), np.int64)
+                for k in range(8):
+                    for pi in range(3):
+                        dw[pi, dp_byte_of(t_, k)] = pcs[pi][8 * c + k]
+                x8 = -8 * int(xi[8 * c:8 * c + 8].sum()) if t_ == gguf.Q4_0 else 0
+                for r, row in ((0, g), (1, g + 8)):
+                    if t_ == gguf.Q4_0:
+                        w = int(chunk[lane * 8 + 4 * r:lane * 8 + 4 * r + 4].view("<u4")[0])
+                        qb = [((w & 0x0F0F0F0F) >> (8 * j)) & 0xFF for j in range(4)] + \
+                             [(((w >> 4) & 0x0F0F0F0F) >> (8 * j)) & 0xFF for j in range(4)]
+                    else:
+                        qb = list(chunk[lane * 16 + 8 * r:lane * 16 + 8 * r + 8].view(np.int8).astype(np.int64))
+                    sums = [int(np.dot(qb, dw[pi])) for pi in range(3)]
+                    v = sums[0] * 16384 + sums[1] * 128 + sums[2] + x8
+                    d = s[scale_offset(nb, t * 16 + row, b):][:2].view("<f2")[0]
+                    y[t * 16 + row] += float(v) * float(d) * float(sinv)
+    return y[:rows]
+
+
+@pytest.mark.parametrize("t_", [gguf.Q4_0, gguf.Q8_0])
+def test_integer_variant_emulation_matches_dense(t_):
+    rows, nb = 20, 3
+    rng = np.random.default_rng(7 + t_)
+    w = rng.standard_normal(rows * nb * 32, dtype=np.float32) * np.float32(0.05)
+    raw = np.frombuffer(synth.encode(w, t_), dtype=np.uint8)
+    q, s = repack(t_, raw, rows, nb)
+    x = rng.standard_normal(nb * 32).astype(np.float32) * np.float32(3.0)
+    x[5] = np.float32(40.0)  # a large entry in one block
+    y = emulate_integer(t_, q, s, x, rows, nb)
+    wd = O.dequant(t_, raw, rows * nb * 32).reshape(rows, nb * 32).astype(np.float64)
+    ref = wd @ x.astype(np.float64)
+    assert np.allclose(y, ref, rtol=0, atol=1e-6 * (np.abs(wd) @ np.abs(x)).max())
