@@ -173,6 +173,9 @@ MvShape mv_shape(const Mat& m, int B) {
     const size_t stage_bytes = (size_t)sh.kb * (laic::tile_qbytes(m.type) + sbytes);
     const size_t fixed = (size_t)laic::kConsumerWarps * 16 * sh.nt * 8 * 4 + 16 * (size_t)B * 4 + sh.nt * 8 * 8 + 1024;
     const int G = num_sms();
+    // rough microseconds: a consumer warp's tile-block (mma count grows with the n-tiles), a tile's
+    // reduction and epilogue, and the split-K merge (partials to L2, fence, ticket, second pass)
+    const double t_blk = 0.05 + 0.025 * sh.nt, t_tile = 1.0, t_merge = 4.0;
     double best = 1e30;
     for (int nk = 1; nk <= std::min(m.nb, 64); ++nk) {
         const int kr = (m.nb + nk - 1) / nk;
@@ -182,7 +185,8 @@ MvShape mv_shape(const Mat& m, int B) {
         const int cta_per_k = G / nk;
         if (cta_per_k < 1) break;
         const int tiles_per = (m.ntiles + cta_per_k - 1) / cta_per_k;
-        const double cost = (double)tiles_per * (kr + 3) + (nk > 1 ? 2.0 : 0.0);
+        const int blk_rounds = (kr + laic::kConsumerWarps - 1) / laic::kConsumerWarps;
+        const double cost = (double)tiles_per * (blk_rounds * t_blk + t_tile) + (nk > 1 ? t_merge : 0.0);
         if (cost < best - 1e-9) {
             best = cost;
             sh.nk = nk;

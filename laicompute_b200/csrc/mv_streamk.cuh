@@ -31,18 +31,34 @@
 
 namespace laic {
 
-constexpr int kSkWarps = 16;
-constexpr int kSkRingBytes = 9 * 1024;   // per warp: two stages in flight
-constexpr int kSkSlots = 2;              // tile slots per team (a team's warps may drift apart)
-// tile-blocks per ring stage (about 4.5 KB for every type)
-__host__ __device__ constexpr int sk_kb(int type) { return type == T_Q4_0 ? 16 : type == T_Q8_0 ? 8 : 4; }
+// Launch shape (overridable at build time for tuning sweeps).
+#ifndef LAIC_SK_WARPS
+#define LAIC_SK_WARPS 16
+#endif
+#ifndef LAIC_SK_RING_BYTES
+#define LAIC_SK_RING_BYTES (9 * 1024)
+#endif
+#ifndef LAIC_SK_STAGE_BYTES
+#define LAIC_SK_STAGE_BYTES 4608
+#endif
+constexpr int kSkWarps = LAIC_SK_WARPS;          // warps per CTA
+constexpr int kSkRingBytes = LAIC_SK_RING_BYTES;  // per warp: stages in flight
+constexpr int kSkSlots = 2;                       // tile slots per team (a team's warps may drift apart)
+// largest power of two dividing the warp count: the widest team
+constexpr int kSkMaxTeam = (kSkWarps & -kSkWarps) < 16 ? (kSkWarps & -kSkWarps) : 16;
+// tile-blocks per ring stage (about LAIC_SK_STAGE_BYTES for every type)
+__host__ __device__ constexpr int sk_kb(int type) {
+    return LAIC_SK_STAGE_BYTES / (tile_qbytes(type) + (type == T_F16 ? 0 : kTileSBytes)) > 0
+               ? LAIC_SK_STAGE_BYTES / (tile_qbytes(type) + (type == T_F16 ? 0 : kTileSBytes)) : 1;
+}
 __host__ __device__ constexpr int sk_stage_bytes(int type) {
     return sk_kb(type) * (tile_qbytes(type) + (type == T_F16 ? 0 : kTileSBytes));
 }
 __host__ __device__ constexpr int sk_stages(int type) { return kSkRingBytes / sk_stage_bytes(type); }
 // warps per tile: long rows are split over more warps
 __host__ __device__ inline int sk_team(int nb) {
-    return nb >= 256 ? 16 : nb >= 128 ? 8 : nb >= 64 ? 4 : nb >= 32 ? 2 : 1;
+    const int k = nb >= 256 ? 16 : nb >= 128 ? 8 : nb >= 64 ? 4 : nb >= 32 ? 2 : 1;
+    return k < kSkMaxTeam ? k : kSkMaxTeam;
 }
 
 // tickets, merged-tile marks, per-warp statistics, 1/rms and split scale per sequence
