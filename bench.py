@@ -231,6 +231,8 @@ def main() -> None:
     ap.add_argument("--ref-steps", type=int, default=64, help="cap of timed CPU decode steps")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batch1", action="store_true")
+    ap.add_argument("--step-kernel", action="store_true",
+                    help="one sequence of Q4_0/Q8_0 layers: the one-launch decode-step kernel")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -262,7 +264,7 @@ def main() -> None:
     seq_rank = 0 if tp > 1 else rank  # tensor-parallel ranks decode the same sequences
     ctx_need = plen + 2 * args.warmup + 2 * args.steps + 64  # decode, e2e and profiling steps
     ctx_need = max(ctx_need, KV_CAPACITY.get(name, 0))
-    eng = Engine(path, max_seqs=batch, device=local, kv_capacity=ctx_need, **tp_kw)
+    eng = Engine(path, max_seqs=batch, device=local, kv_capacity=ctx_need, step_kernel=args.step_kernel, **tp_kw)
     slots = np.arange(batch, dtype=np.int32)
     prompts = np.stack([synth.prompt_ids(arch.vocab, plen, seed=seed + 100 + 1000 * seq_rank + i)
                         for i in range(batch)])
@@ -315,7 +317,9 @@ def main() -> None:
     dname, (dl, dus, dbytes) = dom
     peak, peak_kind = measured_peak_gbs()
     achieved = (dbytes / dl) / (dus / dl * 1e-6) / 1e9
-    kv_read = prof["attention"][2] / max(1, prof["attention"][0]) * arch.layers  # KV bytes read per step
+    # KV bytes read per step in the timed decode: every sequence reads its whole context (all layers, K+V)
+    mid_pos = plen + args.warmup + args.steps / 2.0
+    kv_read = st.kv_bytes_per_pos * batch * mid_pos
 
     out = None
     if rank == 0:

@@ -316,22 +316,32 @@ __device__ __forceinline__ uint32_t pack_h2(__half a, __half b) {
     return (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
 }
 
-template <int D, int GMAX>
-__global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const AttnParams p) {
+// Barrier of the attention warps: the whole CTA of attn_mma_kernel, or the
+// four warps of the decode-step kernel that run its attention phase.
+__device__ __forceinline__ void attn_group_sync(int id) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(kAttnWarps * 32) : "memory");
+}
+
+// One split of one (sequence, kv head) pair, run by kAttnWarps warps (tid 0..127)
+// on `smem` (attn_chunk_smem(D) bytes). PDL: fetch older rows before the
+// programmatic-dependency wait (standalone kernel); else everything after entry.
+template <int D, int GMAX, bool PDL>
+__device__ __forceinline__ void attn_mma_body(const AttnParams& p, int split, int kvh, int seq, uint8_t* smem,
+                                              int tid, int bar_id) {
     constexpr int KS = D / 16;  // k-steps of the score product = m-tiles of the value product
     constexpr int CPR = D / 8;  // 16-byte chunks per row
     constexpr int NW = kAttnWarps;
+    constexpr int NT = kAttnWarps * 32;
     static_assert(D == 32 || D == 64 || D == 128, "head_dim 32, 64 or 128");
     static_assert(GMAX <= 8, "at most 8 query heads per KV head");
-    extern __shared__ __align__(128) uint8_t smem[];
+    auto gsync = [&]() { attn_group_sync(bar_id); };
     __half* Ks = reinterpret_cast<__half*>(smem);
     __half* Vs = Ks + kAttnChunk * D;
     __shared__ __align__(16) __half Ps[NW][2][8][40];  // per warp: p hi/lo [head][position] (rows padded)
     __shared__ float cm[NW][8], cl[NW][8];
     __shared__ int is_last;
 
-    const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int lane = tid & 31, warp = tid >> 5;
     const int gq = lane >> 2, c = lane & 3;
     const int G = p.heads / p.kv_heads;
 
@@ -341,7 +351,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const AttnPar
     const int nch = (n + kAttnChunk - 1) / kAttnChunk;
     const int active = min(p.nsplit, nch);
     if (split >= active) {
-        pdl_launch_dependents();
+        if (PDL) pdl_launch_dependents();
         return;
     }
     const int ch0 = split * nch / active, ch1 = (split + 1) * nch / active;
@@ -350,7 +360,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const AttnPar
 
     // rows [r0, r1) of the chunk that starts at c0, all threads
     auto load_rows = [&](int r0, int r1, int c0) {
-        for (int i = threadIdx.x; i < (r1 - r0) * CPR; i += blockDim.x) {
+        for (int i = tid; i < (r1 - r0) * CPR; i += NT) {
             const int r = r0 + i / CPR, cc = i % CPR, rl = r - c0;
             cp_async16(Ks + attn_swz<D>(rl, cc), kb + (size_t)r * D + cc * 8);
             cp_async16(Vs + attn_swz<D>(rl, cc), vb + (size_t)r * D + cc * 8);
@@ -361,18 +371,20 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const AttnPar
     // warp's products (with p = 0): make them zeros, not stale bits
     auto zero_tail = [&](int rows) {
         const int end = min(kAttnChunk, (rows + 31) & ~31);
-        for (int i = threadIdx.x; i < (end - rows) * CPR; i += blockDim.x) {
+        for (int i = tid; i < (end - rows) * CPR; i += NT) {
             const int rl = rows + i / CPR, cc = i % CPR;
             *reinterpret_cast<uint4*>(Vs + attn_swz<D>(rl, cc)) = make_uint4(0, 0, 0, 0);
         }
     };
     {
         const int c0 = ch0 * kAttnChunk, c1 = min(n, c0 + kAttnChunk);
-        load_rows(c0, min(c1, n - 1), c0);  // older rows, before the dependency wait
+        load_rows(c0, PDL ? min(c1, n - 1) : c1, c0);  // PDL: older rows, before the dependency wait
         zero_tail(c1 - c0);
     }
-    pdl_launch_dependents();
-    pdl_wait();
+    if (PDL) {
+        pdl_launch_dependents();
+        pdl_wait();
+    }
 
     // B fragments of the score product: q of head gq (zero past G), scaled by 1/sqrt(d), hi + lo
     uint32_t qh[KS][2], ql[KS][2];
@@ -384,7 +396,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const AttnPar
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
                 const int d0 = ks * 16 + 2 * c + 8 * j;
-                const float v0 = gq < G ? qg[d0] * rs : 0.f, v1 = gq < G ? qg[d0 + 1] * rs : 0.f;
+                const float v0 = gq < G ? __ldcg(qg + d0) * rs : 0.f, v1 = gq < G ? __ldcg(qg + d0 + 1) * rs : 0.f;
                 const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
                 qh[ks][j] = pack_h2(h0, h1);
                 ql[ks][j] = pack_h2(__float2half_rn(v0 - __half2float(h0)), __float2half_rn(v1 - __half2float(h1)));
@@ -400,9 +412,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const AttnPar
 
     for (int ch = ch0; ch < ch1; ++ch) {
         const int c0 = ch * kAttnChunk, c1 = min(n, c0 + kAttnChunk);
-        if (ch == ch0 && c1 == n) load_rows(n - 1, n, c0);  // the newest row, after the wait
+        if (PDL && ch == ch0 && c1 == n) load_rows(n - 1, n, c0);  // the newest row, after the wait
         cp_async_wait_all();
-        __syncthreads();
+        gsync();
         const int wp = warp * 32;  // this warp's first row in the chunk
         if (c0 + wp < c1) {
             // ---- scores: two m-tiles of 16 positions
@@ -481,7 +493,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const AttnPar
             }
             __syncwarp();
         }
-        __syncthreads();  // the chunk buffers are free
+        gsync();  // the chunk buffers are free
         if (ch + 1 < ch1) {
             const int n0 = (ch + 1) * kAttnChunk, n1 = min(n, n0 + kAttnChunk);
             load_rows(n0, n1, n0);
@@ -502,15 +514,15 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const AttnPar
             const int d = mt * 16 + gq + (e >> 1) * 8, h = 2 * c + (e & 1);
             cacc[((size_t)warp * 8 + h) * D + d] = o[mt][e];
         }
-    __syncthreads();
+    gsync();
 
     const size_t pair = (size_t)seq * p.kv_heads + kvh;
     const int PD = D + 2;
     // per head: the warps' log-sum-exp weights, once
     __shared__ float mw[64][8];  // weights of the warps, then of the splits
     __shared__ float mM[8], mL[8];
-    if (threadIdx.x < G) {
-        const int g = threadIdx.x;
+    if (tid < G) {
+        const int g = tid;
         float M = -INFINITY, L = 0.f;
         for (int w = 0; w < NW; ++w) M = fmaxf(M, cm[w][g]);
         for (int w = 0; w < NW; ++w) {
@@ -520,8 +532,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const AttnPar
         }
         mM[g] = M; mL[g] = L;
     }
-    __syncthreads();
-    for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+    gsync();
+    for (int i = tid; i < G * D; i += NT) {
         const int g = i / D, dd = i % D;
         float A = 0.f;
 #pragma unroll
@@ -538,15 +550,15 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const AttnPar
 
     // ---- the last of the active splits merges them (atomic ticket, no spinning)
     __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) is_last = atomicAdd(p.counters + pair, 1u) == (unsigned)(active - 1);
-    __syncthreads();
+    gsync();
+    if (tid == 0) is_last = atomicAdd(p.counters + pair, 1u) == (unsigned)(active - 1);
+    gsync();
     if (!is_last) return;
     __threadfence();
     const size_t sstride = (size_t)G * PD;
     const float* base = p.part + pair * p.nsplit * sstride;
-    if (threadIdx.x < G) {  // per head: the splits' weights (active <= 64 splits)
-        const int g = threadIdx.x;
+    if (tid < G) {  // per head: the splits' weights (active <= 64 splits)
+        const int g = tid;
         float M = -INFINITY, L = 0.f;
         for (int j = 0; j < active; ++j) M = fmaxf(M, __ldcg(base + j * sstride + g * PD + D));
         for (int j = 0; j < active; ++j) {
@@ -557,14 +569,20 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const AttnPar
         }
         mL[g] = L;
     }
-    __syncthreads();
-    for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+    gsync();
+    for (int i = tid; i < G * D; i += NT) {
         const int g = i / D, dd = i % D;
         float A = 0.f;
         for (int j = 0; j < active; ++j) A = fmaf(__ldcg(base + j * sstride + g * PD + dd), mw[j][g], A);
         p.out[(size_t)seq * p.ldo + ((size_t)kvh * G + g) * D + dd] = A / mL[g];
     }
-    if (threadIdx.x == 0) p.counters[pair] = 0u;
+    if (tid == 0) p.counters[pair] = 0u;
+}
+
+template <int D, int GMAX>
+__global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const AttnParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    attn_mma_body<D, GMAX, true>(p, blockIdx.x, blockIdx.y, blockIdx.z, smem, threadIdx.x, 1);
 }
 
 }  // namespace laic

@@ -44,6 +44,7 @@
 #include "mv_streamk.cuh"
 #include "nccl_dl.h"
 #include "sampler.cuh"
+#include "step_kernel.cuh"
 
 namespace {
 
@@ -356,6 +357,15 @@ struct laic_dev {
     float *logits_l = nullptr, *logits_g = nullptr;  // tp > 1: this rank's vocabulary rows; every rank's
     bool have_lm = false;  // tp > 1: lm holds this rank's lm_head rows
 
+    // one-sequence decode-step kernel (all layers in one cooperative launch)
+    laic::StepLayer* d_step_layers = nullptr;
+    unsigned* step_bar = nullptr;
+    uint8_t *step_rec_x = nullptr, *step_rec_act = nullptr;  // activation digit records between phases
+    float* step_ss = nullptr;
+    int step_type = -1;
+    size_t step_smem = 0;
+    bool step_ready = false, step_checked = false, use_step_kernel = false;
+
     Mat embd, lm;
     bool have_embd = false, have_out = false, have_onorm = false;
     float* out_norm = nullptr;
@@ -473,7 +483,25 @@ struct laic_dev {
             for (int i = 0; i < nseq; ++i)
                 attn_bytes += (double)(h_pos[h_slots[i]] + 1) * Hkv * D * 2 * kvb + 8.0 * h;
 
-        for (int l = 0; l < L; ++l) {
+        const bool step_path = nseq == 1 && step_ready;
+        if (step_path) {  // every layer in one cooperative launch
+            double wb = 0;
+            for (auto& ly : layers) wb += ly.qkv.bytes() + ly.o.bytes() + ly.gu.bytes() + ly.down.bytes();
+            t_begin("layers", wb + attn_bytes * L);
+            CK(cudaMemsetAsync(step_bar, 0, 4, s));
+            laic::StepParams sp{};
+            sp.layers = d_step_layers; sp.L = L;
+            sp.h = h; sp.F = F; sp.hq = hq; sp.kv = kv; sp.D = D; sp.heads = H; sp.kv_heads = Hkv;
+            sp.rope_pairs = rope_pairs; sp.eps = a.rms_eps; sp.sqrt_d = sqrtf((float)D);
+            sp.x = x; sp.q = q; sp.attn = attn; sp.act = act; sp.rope_cs = rope_cs;
+            sp.slots = d_slots; sp.pos = pos; sp.kv_slot_stride = kv_slot_stride; sp.kv_cap = cap;
+            sp.part = attn_part; sp.counters = attn_cnt; sp.bar = step_bar; sp.err = mvs.err;
+            sp.rec_x = step_rec_x; sp.rec_act = step_rec_act; sp.ss_x = step_ss;
+            CK(laic::step_launch(step_type, D, G, sp, num_sms(), step_smem, s));
+            ++nl;
+            t_end();
+        }
+        for (int l = 0; l < L && !step_path; ++l) {
             Layer& ly = layers[l];
             laic::MvParams p{};
             p.nseq = nseq;
@@ -560,8 +588,56 @@ struct laic_dev {
         return LAIC_OK;
     }
 
+    // Whether one sequence can run as the decode-step kernel: every layer projection Q4_0
+    // (or every one Q8_0), FP16 KV, one GPU, head_dim 64 or 128, and one CTA fits per SM.
+    // Builds the device layer table (before any capture).
+    int prepare_step() {
+        if (step_checked) return LAIC_OK;
+        step_checked = true;
+        step_ready = false;
+        // (at most 64 chunks of 128 positions: the attention split buffers hold 64 partials per head)
+        if (!use_step_kernel || kv32 || tp != 1 || (D != 64 && D != 128) || G > 8 || L < 1 ||
+            cap > 64 * laic::kAttnChunk)
+            return LAIC_OK;
+        const int type = layers[0].qkv.type;
+        if (type != T_Q4_0 && type != T_Q8_0) return LAIC_OK;
+        for (auto& l : layers)
+            if (!l.qkv.q || !l.o.q || !l.gu.q || !l.down.q || l.qkv.type != type || l.o.type != type ||
+                l.gu.type != type || l.down.type != type || !l.attn_norm || !l.ffn_norm)
+                return LAIC_OK;
+        const int nb_max = std::max(std::max(h, hq), F) / 32;
+        const size_t smem = laic::step_smem(type, nb_max, D);
+        if (smem > 220 * 1024) return LAIC_OK;
+        int bps = 0;
+        CK(laic::step_prepare(type, D, G, smem, &bps));
+        if (bps < 1) return LAIC_OK;
+        const size_t kvb = 2;
+        std::vector<laic::StepLayer> tab(L);
+        for (int l = 0; l < L; ++l) {
+            const Layer& ly = layers[l];
+            tab[l].qkv = {ly.qkv.q, ly.qkv.s}; tab[l].o = {ly.o.q, ly.o.s};
+            tab[l].gu = {ly.gu.q, ly.gu.s}; tab[l].down = {ly.down.q, ly.down.s};
+            tab[l].attn_norm = ly.attn_norm; tab[l].ffn_norm = ly.ffn_norm;
+            tab[l].kc = (char*)kc + (size_t)l * kv_layer_stride * kvb;
+            tab[l].vc = (char*)vc + (size_t)l * kv_layer_stride * kvb;
+        }
+        if (d_step_layers) cudaFree(d_step_layers);
+        d_step_layers = nullptr;
+        CK(cudaMalloc(&d_step_layers, sizeof(laic::StepLayer) * L));
+        CK(cudaMemcpy(d_step_layers, tab.data(), sizeof(laic::StepLayer) * L, cudaMemcpyHostToDevice));
+        if (!step_bar) CK(cudaMalloc(&step_bar, 4));
+        if (!step_rec_x) CK(cudaMalloc(&step_rec_x, (size_t)h * 4));
+        if (!step_rec_act) CK(cudaMalloc(&step_rec_act, (size_t)F * 4));
+        if (!step_ss) CK(cudaMalloc(&step_ss, (size_t)h / 8 * 4));
+        step_type = type;
+        step_smem = smem;
+        step_ready = true;
+        return LAIC_OK;
+    }
+
     // Size the matvec scratch for `nseq` sequences (before any capture).
     int reserve_scratch(int nseq) {
+        if (int rc = prepare_step()) return rc;
         MvNeed need;
         auto see = [&](const Mat& m) {
             if (m.q) need.merge(mv_need(m, nseq));
@@ -696,6 +772,7 @@ int laic_dev_create(const laic_dev_desc* desc, const laic_dev_opts* opts, laic_d
     d->kv32 = (o.flags & LAIC_FLAG_KV_F32) != 0;
     d->use_graph = !(o.flags & LAIC_FLAG_NO_GRAPH);
     d->use_pdl = !(o.flags & LAIC_FLAG_NO_PDL);
+    d->use_step_kernel = (o.flags & LAIC_FLAG_STEP_KERNEL) != 0;
     d->layers.resize(a.layers);
     d->h_pos.assign(o.max_seqs, 0);
     CK(cudaStreamCreateWithFlags(&d->st, cudaStreamNonBlocking));
@@ -784,7 +861,8 @@ void laic_dev_destroy(laic_dev* d) {
     mv_scratch_free(d->mvs);
     void* bufs[] = {d->out_norm, d->x, d->q, d->attn, d->act, d->logits, d->kc, d->vc, d->pos, d->counts,
                     d->rope_cs, d->attn_part, d->attn_cnt, d->d_tokens, d->d_out_ids, d->d_slots, d->d_err, d->d_params,
-                    d->d_hist, d->d_hist_count, d->logits_l, d->logits_g};
+                    d->d_hist, d->d_hist_count, d->logits_l, d->logits_g, d->d_step_layers, d->step_bar,
+                    d->step_rec_x, d->step_rec_act, d->step_ss};
     for (void* b : bufs) if (b) cudaFree(b);
     void* hb[] = {d->h_tokens, d->h_out_ids, d->h_slots, d->h_params};
     for (void* b : hb) if (b) cudaFreeHost(b);
@@ -804,6 +882,7 @@ int laic_dev_upload(laic_dev* d, const char* cname, int32_t type, const uint64_t
     // any graph captured before this upload points at old buffers
     for (auto& kv : d->graphs) cudaGraphExecDestroy(kv.second);
     d->graphs.clear();
+    d->step_checked = false;
 
     if (name == "output_norm.weight") {
         if (n != (size_t)d->h) return fail(LAIC_E_INVALID, "invalid norm tensor: " + name);

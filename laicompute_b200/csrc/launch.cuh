@@ -37,4 +37,11 @@ cudaError_t mv_sk_launch(int type, int nt, int epi, bool kv32, const MvParams& p
 // Raise the dynamic shared memory limit of every instantiation (call before any graph capture).
 cudaError_t mv_set_attributes();
 
+struct StepParams;
+// One-sequence decode-step kernel (step.cu): shared memory it needs, attribute setup with the
+// resulting CTAs per SM (call before capture), and its cooperative launch (one CTA per SM).
+size_t step_smem(int type, int nb_max, int D);
+cudaError_t step_prepare(int type, int D, int G, size_t smem, int* blocks_per_sm);
+cudaError_t step_launch(int type, int D, int G, const StepParams& p, int grid, size_t smem, cudaStream_t st);
+
 }  // namespace laic

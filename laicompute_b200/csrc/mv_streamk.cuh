@@ -188,6 +188,121 @@ __device__ __forceinline__ void tile_block(uint32_t q, uint32_t sc, const uint32
     }
 }
 
+// One 8-column group of the activation (thread-per-group, whole warp active):
+// optional rmsnorm scaling, the group's power-of-two scale (shared with the
+// three other groups of its block through the adjacent lanes), the digits in
+// the quants' byte order, and the record store when `live`.
+template <int WT>
+__device__ __forceinline__ void dp_group_record(float (&v)[8], const float* norm_w, float iv, int gi, bool live,
+                                                uint8_t* xs) {
+    if (norm_w && live) {
+        const float4 w0 = reinterpret_cast<const float4*>(norm_w)[2 * gi];
+        const float4 w1 = reinterpret_cast<const float4*>(norm_w)[2 * gi + 1];
+        const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = v[k] * (iv * w[k]);
+    }
+    float mx = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) mx = fmaxf(mx, fabsf(v[k]));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    int ex = 0;
+    if (mx > 0.f && isfinite(mx)) frexpf(mx, &ex);  // mx in [2^(ex-1), 2^ex)
+    uint32_t dw[3][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}};  // digit words p0 p1 p2, quant byte order
+    int gs = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const int xi = (int)rintf(ldexpf(v[k], 20 - ex));  // |xi| <= 2^20
+        const int p2 = ((xi + 64) & 127) - 64;
+        const int t1 = (xi - p2) >> 7;
+        const int p1 = ((t1 + 64) & 127) - 64;
+        const int p0 = (t1 - p1) >> 7;
+        gs += xi;
+        const int pos = dp_byte_of<WT>(k), wd = pos >> 2, sh = (pos & 3) * 8;
+        dw[0][wd] |= (uint32_t)(p0 & 0xFF) << sh;
+        dw[1][wd] |= (uint32_t)(p1 & 0xFF) << sh;
+        dw[2][wd] |= (uint32_t)(p2 & 0xFF) << sh;
+    }
+    if (live) {
+        uint4* rec = reinterpret_cast<uint4*>(xs + (size_t)gi * 32);  // block gi/4, group gi%4
+        rec[0] = make_uint4(dw[0][0], dw[0][1], dw[1][0], dw[1][1]);
+        rec[1] = make_uint4(dw[2][0], dw[2][1], (uint32_t)(WT == T_Q4_0 ? -8 * gs : 0),
+                            __float_as_uint(ldexpf(1.f, ex - 20)));
+    }
+}
+
+// Activation digit records of the integer variant for one sequence (whole CTA):
+// rmsnorm by norm_w when given, then per 32-column block the power-of-two
+// scale and the balanced base-128 digits, one thread per 8-column group.
+// Reads the activations through L2 (they may come from other CTAs of the same
+// kernel). Ends with a CTA barrier.
+template <int WT>
+__device__ __forceinline__ void dp_build_records(const float* x, const float* norm_w, float eps, int in, uint8_t* xs,
+                                                 float* wstat, float* inv) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nb = in / 32, ng = nb * 4;  // 8-column groups
+    const float4* src = reinterpret_cast<const float4*>(x);
+    const float4* nw4 = reinterpret_cast<const float4*>(norm_w);
+    constexpr int RMAX = 4;  // groups per thread held in registers (rows up to 4 * 8 * blockDim columns)
+    const int nt = blockDim.x;
+    if (ng > RMAX * nt) {  // too long to hold: the sum of squares first, then the groups round by round
+        float ss = 0.f;
+        if (norm_w) {
+            for (int f = threadIdx.x; f < (in >> 2); f += nt) {
+                const float4 v = __ldcg(src + f);
+                ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+            }
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) wstat[warp * 2] = ss;
+        __syncthreads();
+        float a = 0.f;
+        for (int w = 0; w < kSkWarps; ++w) a += wstat[w * 2];
+        const float iv = norm_w ? 1.f / sqrtf(a / float(in) + eps) : 1.f;
+        for (int base = 0; base < ng; base += nt) {
+            const int gi = base + threadIdx.x;
+            const bool live = gi < ng;
+            const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 a0 = live ? __ldcg(src + 2 * gi) : z4, a1 = live ? __ldcg(src + 2 * gi + 1) : z4;
+            float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            dp_group_record<WT>(v, norm_w, iv, gi, live, xs);
+        }
+    } else {  // one load of every group, then the statistics and the records from registers
+        float v[RMAX][8];
+        float ss = 0.f;
+#pragma unroll
+        for (int r = 0; r < RMAX; ++r) {
+            const int gi = r * nt + threadIdx.x;
+            const bool live = gi < ng;
+            const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 a0 = live ? __ldcg(src + 2 * gi) : z4, a1 = live ? __ldcg(src + 2 * gi + 1) : z4;
+            v[r][0] = a0.x; v[r][1] = a0.y; v[r][2] = a0.z; v[r][3] = a0.w;
+            v[r][4] = a1.x; v[r][5] = a1.y; v[r][6] = a1.z; v[r][7] = a1.w;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) ss = fmaf(v[r][k], v[r][k], ss);
+        }
+        float iv = 1.f;
+        if (norm_w) {
+            ss = warp_sum(ss);
+            if (lane == 0) wstat[warp * 2] = ss;
+            __syncthreads();
+            float a = 0.f;
+            for (int w = 0; w < kSkWarps; ++w) a += wstat[w * 2];
+            iv = 1.f / sqrtf(a / float(in) + eps);
+        }
+#pragma unroll
+        for (int r = 0; r < RMAX; ++r) {
+            if (r * nt >= ng) break;  // uniform over the CTA
+            const int gi = r * nt + threadIdx.x;
+            dp_group_record<WT>(v[r], norm_w, iv, gi, gi < ng, xs);
+        }
+    }
+    (void)nw4;
+    if (inv) *inv = 1.f;  // (statistics live in registers; kept for callers that read it)
+    __syncthreads();
+}
+
 template <int WT, int NT, int EPI, typename KV>
 __global__ void __launch_bounds__(kSkWarps * 32, 1) mv_sk_kernel(const MvParams p) {
     constexpr int QB = tile_qbytes(WT);
@@ -255,70 +370,8 @@ __global__ void __launch_bounds__(kSkWarps * 32, 1) mv_sk_kernel(const MvParams 
     // ---- prologue: the whole activation vector -> binary16 hi/lo in fragment order
     //      (integer variant: int8 digit records, one warp per 32-column block)
     if constexpr (DP) {
-        const float4* src = reinterpret_cast<const float4*>(p.x);
-        const float4* nw4 = reinterpret_cast<const float4*>(p.norm_w);
-        float ss = 0.f;
-        if (p.norm_w) {
-            for (int f = threadIdx.x; f < (p.in >> 2); f += blockDim.x) {
-                const float4 v = src[f];
-                ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
-            }
-            ss = warp_sum(ss);
-            if (lane == 0) wstat[warp * 2] = ss;
-            __syncthreads();
-            if (threadIdx.x == 0) {
-                float a = 0.f;
-                for (int w = 0; w < kSkWarps; ++w) a += wstat[w * 2];
-                inv[0] = 1.f / sqrtf(a / float(p.in) + p.eps);
-            }
-            __syncthreads();
-        }
+        dp_build_records<WT>(p.x, p.norm_w, p.eps, p.in, xs, wstat, inv);
         if (threadIdx.x == 0) xsc[0] = 1.f;  // the digit scales are applied per block
-        const float iv = p.norm_w ? inv[0] : 1.f;
-        // one thread per 8-column group (four per block); the block's four threads are adjacent
-        // lanes. Every lane runs each round (the shuffles need the whole warp); lanes past the
-        // last group compute on zeros and store nothing.
-        for (int base = 0; base < nb * 4; base += blockDim.x) {
-            const int gi = base + threadIdx.x;
-            const bool live = gi < nb * 4;
-            const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
-            const float4 a0 = live ? src[2 * gi] : z4, a1 = live ? src[2 * gi + 1] : z4;
-            float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-            if (p.norm_w && live) {
-                const float4 w0 = nw4[2 * gi], w1 = nw4[2 * gi + 1];
-                const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-#pragma unroll
-                for (int k = 0; k < 8; ++k) v[k] = v[k] * (iv * w[k]);
-            }
-            float mx = 0.f;
-#pragma unroll
-            for (int k = 0; k < 8; ++k) mx = fmaxf(mx, fabsf(v[k]));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-            int ex = 0;
-            if (mx > 0.f && isfinite(mx)) frexpf(mx, &ex);  // mx in [2^(ex-1), 2^ex)
-            uint32_t dw[3][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}};  // digit words p0 p1 p2, quant byte order
-            int gs = 0;
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const int xi = (int)rintf(ldexpf(v[k], 20 - ex));  // |xi| <= 2^20
-                const int p2 = ((xi + 64) & 127) - 64;
-                const int t1 = (xi - p2) >> 7;
-                const int p1 = ((t1 + 64) & 127) - 64;
-                const int p0 = (t1 - p1) >> 7;
-                gs += xi;
-                const int pos = dp_byte_of<WT>(k), wd = pos >> 2, sh = (pos & 3) * 8;
-                dw[0][wd] |= (uint32_t)(p0 & 0xFF) << sh;
-                dw[1][wd] |= (uint32_t)(p1 & 0xFF) << sh;
-                dw[2][wd] |= (uint32_t)(p2 & 0xFF) << sh;
-            }
-            if (live) {
-                uint4* rec = reinterpret_cast<uint4*>(xs + (size_t)gi * 32);  // block gi/4, group gi%4
-                rec[0] = make_uint4(dw[0][0], dw[0][1], dw[1][0], dw[1][1]);
-                rec[1] = make_uint4(dw[2][0], dw[2][1], (uint32_t)(WT == T_Q4_0 ? -8 * gs : 0),
-                                    __float_as_uint(ldexpf(1.f, ex - 20)));
-            }
-        }
         __syncthreads();
     } else {
         const int nv = p.in >> 2;  // float4 per sequence
@@ -378,7 +431,8 @@ __global__ void __launch_bounds__(kSkWarps * 32, 1) mv_sk_kernel(const MvParams 
     }
 
     // ---- finish one tile: this warp's partial -> slot; the last of the team adds and runs the epilogue
-    float acc[DP ? 1 : NT][4];  // integer variant: acc[0][0..1] = rows g and g+8 of this lane's columns
+    float acc[DP ? 1 : NT][4];
+    float dacc[2] = {0.f, 0.f};  // integer variant: rows g and g+8 of this lane's columns
     auto finish = [&](int t, int tile_idx) {
         const int slot = tile_idx % kSkSlots;
         float* mine = parts + ((size_t)warp * kSkSlots + slot) * 16 * B;
@@ -394,13 +448,13 @@ __global__ void __launch_bounds__(kSkWarps * 32, 1) mv_sk_kernel(const MvParams 
         }
         if constexpr (DP) {
             // the four lanes of a row hold its four 8-column groups
-            float r0 = acc[0][0], r1 = acc[0][1];
+            float r0 = dacc[0], r1 = dacc[1];
             r0 += __shfl_xor_sync(0xffffffffu, r0, 1);
             r1 += __shfl_xor_sync(0xffffffffu, r1, 1);
             r0 += __shfl_xor_sync(0xffffffffu, r0, 2);
             r1 += __shfl_xor_sync(0xffffffffu, r1, 2);
             if (c == 0) { mine[g] = r0; mine[g + 8] = r1; }
-            acc[0][0] = acc[0][1] = 0.f;
+            dacc[0] = dacc[1] = 0.f;
         } else {
 #pragma unroll
             for (int j = 0; j < NT; ++j) {
@@ -497,13 +551,12 @@ __global__ void __launch_bounds__(kSkWarps * 32, 1) mv_sk_kernel(const MvParams 
         const uint32_t sq = ring_a + slot * STAGE;
         const uint32_t ssc = sq + KB * QB;
         if constexpr (DP) {
-            float (&a2)[2] = *reinterpret_cast<float(*)[2]>(&acc[0][0]);
             const uint32_t xr = xlane[0] + b0 * kDpRecBytes;
             if (n == KB) {
 #pragma unroll
-                for (int j = 0; j < KB; ++j) tile_block_dp<WT>(sq + j * QB, ssc + j * SB, xr + j * kDpRecBytes, lane, a2);
+                for (int j = 0; j < KB; ++j) tile_block_dp<WT>(sq + j * QB, ssc + j * SB, xr + j * kDpRecBytes, lane, dacc);
             } else {
-                for (int j = 0; j < n; ++j) tile_block_dp<WT>(sq + j * QB, ssc + j * SB, xr + j * kDpRecBytes, lane, a2);
+                for (int j = 0; j < n; ++j) tile_block_dp<WT>(sq + j * QB, ssc + j * SB, xr + j * kDpRecBytes, lane, dacc);
             }
         } else if (n == KB) {
 #pragma unroll

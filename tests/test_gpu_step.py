@@ -1,0 +1,49 @@
+"""The one-sequence decode-step kernel (all layers in one cooperative launch)
+against the oracle (reference LlamaRuntime::step, src/inference_v2.cpp:31)
+and against the per-layer launch path, on Q4_0 (head dim 128, GQA groups of 4)
+and Q8_0 (head dim 64) models at contexts spanning several attention chunks."""
+import os
+import tempfile
+
+import numpy as np
+import pytest
+
+from laicompute_b200 import gguf, synth
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_RTOL = 1e-3
+
+ARCHS = {
+    "q4_d128_g4": synth.tiny_arch(gguf.Q4_0, gguf.F16, hidden=512, layers=3, heads=4, kv_heads=1, ffn=512,
+                                  vocab=512, ctx=1024, rope_theta=500000.0, name="step_q4"),
+    "q8_d64_g2": synth.tiny_arch(gguf.Q8_0, hidden=256, layers=3, heads=4, kv_heads=2, ffn=768, vocab=512,
+                                 ctx=1024, name="step_q8"),
+}
+
+
+@pytest.mark.parametrize("arch", sorted(ARCHS))
+def test_step_kernel_matches_oracle_and_layer_path(arch):
+    from laicompute_b200.engine import Engine
+    a = ARCHS[arch]
+    with tempfile.TemporaryDirectory() as d:
+        path = synth.write_model(os.path.join(d, "m.gguf"), a, seed=51)
+        prompt = synth.prompt_ids(a.vocab, 300, seed=52)
+        ref_ids, ref_logits = O.OracleModel(path).generate(prompt, 16)
+        e = Engine(path, kv_capacity=1024, step_kernel=True)
+        ids, logits = e.generate(prompt, 16, want_logits=True)
+        stats = e.stats()
+        e.close()
+        e2 = Engine(path, kv_capacity=1024, step_kernel=False)
+        ids2, logits2 = e2.generate(prompt, 16, want_logits=True)
+        stats2 = e2.stats()
+        e2.close()
+    assert stats.launches_per_step < stats2.launches_per_step  # the step kernel ran
+    err = np.abs(logits - ref_logits).max(axis=1) / np.abs(ref_logits).max(axis=1)
+    assert err.max() <= LOGIT_RTOL, err.max()
+    assert np.array_equal(ids, ref_ids)
+    assert np.array_equal(ids2, ref_ids)
+    # same integer dot products, different split of the work: FP32-rounding level apart
+    d2 = np.abs(logits - logits2).max(axis=1) / np.abs(logits2).max(axis=1)
+    assert d2.max() <= 1e-4, d2.max()
