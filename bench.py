@@ -317,6 +317,14 @@ def main() -> None:
     dname, (dl, dus, dbytes) = dom
     peak, peak_kind = measured_peak_gbs()
     achieved = (dbytes / dl) / (dus / dl * 1e-6) / 1e9
+    traffic = None  # DRAM bytes per launch: ncu's bytes per algorithmic byte (profiles/traffic.json) x ours
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            ratio = json.load(f).get(name, {}).get(dname)
+        if ratio:
+            traffic = int(round(ratio * dbytes / dl))
+    except (OSError, ValueError):
+        pass
     # KV bytes read per step in the timed decode: every sequence reads its whole context (all layers, K+V)
     mid_pos = plen + args.warmup + args.steps / 2.0
     kv_read = st.kv_bytes_per_pos * batch * mid_pos
@@ -339,7 +347,7 @@ def main() -> None:
                     "d2h_bytes_per_step": batch * 4},
             "gpu_launches": int(args.steps * launches_chained),
             "roofline": {"bound": "hbm", "kernel": dname, "achieved": round(achieved, 1), "peak": peak,
-                         "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                         "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
                          "bytes_per_launch": round(dbytes / dl), "us_per_launch": round(dus / dl, 3),
                          "kernels": {k: {"launches": v[0], "us_per_launch": round(v[1] / v[0], 3),
                                          "gbs": round(v[2] / v[1] * 1e-3, 1)} for k, v in prof.items()}},
