@@ -283,10 +283,19 @@ void mv_scratch_free(MvScratch& sc) {
     sc = MvScratch{};
 }
 
+// Activation records a producing kernel already wrote for a tile-kernel projection.
+struct RecIn {
+    const uint8_t* xg = nullptr;
+    int mode = 0;             // 1: rmsnorm scale from ss; 2: unit scale
+    const float* ss = nullptr;
+    int ss_tiles = 0;
+};
+
 // One projection: the team kernel for small batches, else activation
-// preparation + tile kernel. `launches` counts the kernels enqueued.
+// preparation (unless `rin` brings the records) + tile kernel. `launches`
+// counts the kernels enqueued.
 cudaError_t launch_matvec(const Mat& m, laic::MvParams p, int epi, bool kv32, const MvScratch& sc, cudaStream_t st,
-                          bool pdl, int* launches = nullptr) {
+                          bool pdl, int* launches = nullptr, const RecIn* rin = nullptr) {
     const MvShape sh = mv_shape(m, p.nseq);
     p.q = m.q; p.s = m.s; p.rows = m.rows; p.ntiles = m.ntiles; p.in = m.in; p.nb = m.nb;
     if (sh.sk) {
@@ -294,13 +303,18 @@ cudaError_t launch_matvec(const Mat& m, laic::MvParams p, int epi, bool kv32, co
         if (launches) *launches += 1;
         return laic::mv_sk_launch(m.type, sh.nt, epi, kv32, p, sh.grid, sh.smem, st, pdl);
     }
-    laic::XPrepParams xp{p.x, p.ldx, p.norm_w, p.eps, m.in, m.nb, p.nseq, sh.kr, sc.xg, sc.xinv};
-    cudaError_t e = laic::xprep_launch(xp, sh.nk, st, pdl);
-    if (e != cudaSuccess) return e;
     p.nk = sh.nk; p.kr = sh.kr; p.kb = sh.kb; p.stages = sh.stages;
     p.part = sc.part; p.tile_cnt = sc.tile_cnt; p.err = sc.err;
-    p.xg = sc.xg; p.xinvg = sc.xinv;
-    if (launches) *launches += 2;
+    if (rin && rin->xg) {
+        p.xg = rin->xg; p.scale_mode = rin->mode; p.ss = rin->ss; p.ss_tiles = rin->ss_tiles; p.ss_n = m.in;
+    } else {
+        laic::XPrepParams xp{p.x, p.ldx, p.norm_w, p.eps, m.in, m.nb, p.nseq, sh.kr, sc.xg, sc.xinv};
+        cudaError_t e = laic::xprep_launch(xp, sh.nk, st, pdl);
+        if (e != cudaSuccess) return e;
+        p.xg = sc.xg; p.xinvg = sc.xinv; p.scale_mode = 0;
+        if (launches) *launches += 1;
+    }
+    if (launches) *launches += 1;
     return laic::mv_launch(m.type, sh.nt, epi, kv32, p, sh.grid, sh.smem, st, pdl);
 }
 
@@ -361,6 +375,10 @@ struct laic_dev {
     laic::StepLayer* d_step_layers = nullptr;
     unsigned* step_bar = nullptr;
     uint8_t *step_rec_x = nullptr, *step_rec_act = nullptr;  // activation digit records between phases
+    // more than 16 sequences on one GPU: binary16 hi/lo activation records written by the producing
+    // kernels (embedding, o/down residual epilogues, SwiGLU) for the tile-kernel projections
+    uint8_t *rec_x = nullptr, *rec_act = nullptr;
+    float* rec_ss = nullptr;  // [h / 16 row tiles][max_seqs] sums of squares of the residual
     float* step_ss = nullptr;
     int step_type = -1;
     size_t step_smem = 0;
@@ -468,7 +486,10 @@ struct laic_dev {
             if (full) CK(cudaMemcpyAsync(d_params, h_params, nseq * sizeof(laic::SampleDev), cudaMemcpyHostToDevice, s));
         }
 
+        const bool recs = nseq > 16 && tp == 1 && rec_x;  // records travel between the tile-kernel projections
+        const int ntiles_h = (h + 15) / 16;
         laic::EmbedParams ep{embd.type, embd.q, embd.s, h, embd.nb, d_tokens, d_slots, x, counts, V};
+        if (recs) { ep.rec_out = rec_x; ep.rec_w = layers[0].attn_norm; ep.ss_out = rec_ss; ep.nseq = nseq; }
         t_begin("embed", 0);
         CK(launch_k(laic::embed_kernel, dim3(nseq), dim3(256), 0, s, pdl, ep));
         ++nl;
@@ -514,7 +535,9 @@ struct laic_dev {
             p.vc = (char*)vc + (size_t)l * kv_layer_stride * kvb;
             p.kv_slot_stride = kv_slot_stride; p.kv_cap = cap;
             t_begin("qkv", (double)ly.qkv.bytes() + 4.0 * nseq * (h + ly.qkv.rows));
-            CK(launch_matvec(ly.qkv, p, laic::EPI_QKV, kv32, mvs, s, pdl, &nl));
+            RecIn r_qkv;
+            if (recs) { r_qkv.xg = rec_x; r_qkv.mode = 1; r_qkv.ss = rec_ss; r_qkv.ss_tiles = l == 0 ? 1 : ntiles_h; }
+            CK(launch_matvec(ly.qkv, p, laic::EPI_QKV, kv32, mvs, s, pdl, &nl, &r_qkv));
             t_end();
             // attention
             laic::AttnParams ap{};
@@ -529,6 +552,7 @@ struct laic_dev {
             // o + residual
             laic::MvParams po{};
             po.nseq = nseq; po.x = attn; po.ldx = hq; po.out = x; po.ldo = h;
+            if (recs) { po.rec_out = rec_x; po.rec_w = ly.ffn_norm; po.ss_out = rec_ss; }
             t_begin("o", (double)ly.o.bytes() + 4.0 * nseq * hq + 8.0 * nseq * h);
             CK(launch_matvec(ly.o, po, residual_epi, kv32, mvs, s, pdl, &nl));
             t_end();
@@ -536,14 +560,22 @@ struct laic_dev {
             // gate/up + swiglu
             laic::MvParams pg{};
             pg.nseq = nseq; pg.eps = a.rms_eps; pg.x = x; pg.ldx = h; pg.norm_w = ly.ffn_norm; pg.out = act; pg.ldo = F;
+            RecIn r_gu;
+            if (recs) { r_gu.xg = rec_x; r_gu.mode = 1; r_gu.ss = rec_ss; r_gu.ss_tiles = ntiles_h; pg.rec_out = rec_act; }
             t_begin("gate_up", (double)ly.gu.bytes() + 4.0 * nseq * (h + F));
-            CK(launch_matvec(ly.gu, pg, laic::EPI_SWIGLU, kv32, mvs, s, pdl, &nl));
+            CK(launch_matvec(ly.gu, pg, laic::EPI_SWIGLU, kv32, mvs, s, pdl, &nl, &r_gu));
             t_end();
             // down + residual
             laic::MvParams pd{};
             pd.nseq = nseq; pd.x = act; pd.ldx = F; pd.out = x; pd.ldo = h;
+            RecIn r_dn;
+            if (recs) {
+                r_dn.xg = rec_act; r_dn.mode = 2;
+                pd.rec_out = rec_x; pd.ss_out = rec_ss;
+                pd.rec_w = l + 1 < L ? layers[l + 1].attn_norm : out_norm;  // next: QKV, or the lm_head
+            }
             t_begin("down", (double)ly.down.bytes() + 4.0 * nseq * (F + 2 * h));
-            CK(launch_matvec(ly.down, pd, residual_epi, kv32, mvs, s, pdl, &nl));
+            CK(launch_matvec(ly.down, pd, residual_epi, kv32, mvs, s, pdl, &nl, &r_dn));
             t_end();
             if (int rc = allreduce_residual(nseq, s, t_begin, t_end)) return rc;
         }
@@ -552,7 +584,9 @@ struct laic_dev {
             pl.nseq = nseq; pl.eps = a.rms_eps; pl.x = x; pl.ldx = h; pl.norm_w = out_norm;
             pl.out = tp > 1 ? logits_l : logits; pl.ldo = tp > 1 ? Vl : V;
             t_begin("lm_head", (double)lm_head().bytes() + 4.0 * nseq * (h + Vl));
-            CK(launch_matvec(lm_head(), pl, laic::EPI_STORE, kv32, mvs, s, pdl, &nl));
+            RecIn r_lm;
+            if (recs && L > 0) { r_lm.xg = rec_x; r_lm.mode = 1; r_lm.ss = rec_ss; r_lm.ss_tiles = ntiles_h; }
+            CK(launch_matvec(lm_head(), pl, laic::EPI_STORE, kv32, mvs, s, pdl, &nl, &r_lm));
             t_end();
             if (tp > 1) {  // every rank's vocabulary rows -> logits [nseq][V] on every rank
                 t_begin("gather", 4.0 * nseq * V);
@@ -808,6 +842,11 @@ int laic_dev_create(const laic_dev_desc* desc, const laic_dev_opts* opts, laic_d
     CK(cudaMemset(d->vc, 0, kv_bytes));
     CK(cudaMalloc(&d->pos, S * 4));
     CK(cudaMemset(d->pos, 0, S * 4));
+    if (S > 16) {  // activation records between tile-kernel projections
+        CK(cudaMalloc(&d->rec_x, S * d->h * 4));
+        CK(cudaMalloc(&d->rec_act, S * d->F * 4));
+        CK(cudaMalloc(&d->rec_ss, S * ((d->h + 15) / 16) * 4));
+    }
     CK(cudaMalloc(&d->counts, S * d->V * 4));
     CK(cudaMemset(d->counts, 0, S * d->V * 4));
 
@@ -862,7 +901,7 @@ void laic_dev_destroy(laic_dev* d) {
     void* bufs[] = {d->out_norm, d->x, d->q, d->attn, d->act, d->logits, d->kc, d->vc, d->pos, d->counts,
                     d->rope_cs, d->attn_part, d->attn_cnt, d->d_tokens, d->d_out_ids, d->d_slots, d->d_err, d->d_params,
                     d->d_hist, d->d_hist_count, d->logits_l, d->logits_g, d->d_step_layers, d->step_bar,
-                    d->step_rec_x, d->step_rec_act, d->step_ss};
+                    d->step_rec_x, d->step_rec_act, d->step_ss, d->rec_x, d->rec_act, d->rec_ss};
     for (void* b : bufs) if (b) cudaFree(b);
     void* hb[] = {d->h_tokens, d->h_out_ids, d->h_slots, d->h_params};
     for (void* b : hb) if (b) cudaFreeHost(b);

@@ -4,6 +4,7 @@
 #pragma once
 #include "common.cuh"
 #include "tiles.cuh"
+#include "mma_matvec.cuh"  // store_act_record
 
 namespace laic {
 
@@ -17,15 +18,32 @@ struct EmbedParams {
     float* x;                // [nseq][hidden]
     unsigned* counts;        // [max_seqs][vocab] history counts (repeat penalty)
     int vocab;
+    // optional: binary16 hi/lo records of x * rec_w for a tile-kernel projection, and sum x^2
+    uint8_t* rec_out;        // [hidden / 32][nseq][4][32 B]
+    const float* rec_w;      // the first rmsnorm weight
+    float* ss_out;           // [nseq]
+    int nseq;
 };
 
 // x[s] = row tokens[s] of token_embd; the token joins its slot's history.
 __global__ void embed_kernel(const EmbedParams p) {
+    __shared__ float red[32];
     const int s = blockIdx.x;
     pdl_wait();
     const unsigned tok = p.tokens[s];
-    for (int i = threadIdx.x; i < p.hidden; i += blockDim.x)
-        p.x[(size_t)s * p.hidden + i] = tile_value(p.type, p.q, p.s, p.nb, (int)tok, i);
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < p.hidden; i += blockDim.x) {
+        const float v = tile_value(p.type, p.q, p.s, p.nb, (int)tok, i);
+        p.x[(size_t)s * p.hidden + i] = v;
+        if (p.rec_out) {
+            ss = fmaf(v, v, ss);
+            store_act_record(p.rec_out, p.nseq, i, s, v * p.rec_w[i]);
+        }
+    }
+    if (p.rec_out) {
+        ss = block_sum(ss, red);
+        if (threadIdx.x == 0) p.ss_out[s] = ss;
+    }
     if (threadIdx.x == 0) p.counts[(size_t)p.slots[s] * p.vocab + tok] += 1u;
     pdl_launch_dependents();
 }

@@ -66,7 +66,26 @@ struct MvParams {
     // tile kernel: activations already split by xprep_kernel
     const uint8_t* xg;         // [nb][nseq][4][32 B] binary16 hi/lo in fragment order
     const float* xinvg;        // [nk][nseq] power-of-two scale of each K split
+    // tile kernel, records made by the producing kernel instead of xprep_kernel (then unscaled):
+    int scale_mode;            // 0: xinvg; 1: rmsnorm 1/rms from `ss`; 2: unit scale
+    const float* ss;           // [ss_tiles][nseq] partial sums of squares of the rmsnorm input
+    int ss_tiles, ss_n;        // partials per sequence, elements per row
+    // tile kernel EPI_ADD / EPI_SWIGLU: records of the output for the next tile-kernel projection
+    uint8_t* rec_out;          // [rows or rows/2 / 32][nseq][4][32 B] (nullptr: none)
+    const float* rec_w;        // EPI_ADD: the next rmsnorm weight (records of out * w), or nullptr
+    float* ss_out;             // EPI_ADD: [row tiles][nseq] sums of squares of the new residual
 };
+
+// Activation record of element e of sequence s (binary16 hi + lo, fragment order), the
+// layout xprep_kernel writes: records [e / 32][nseq][(e / 8) % 4][8 hi | 8 lo].
+__device__ __forceinline__ void store_act_record(uint8_t* rec, int nseq, int e, int s, float v) {
+    __half* h = reinterpret_cast<__half*>(rec);
+    const size_t base = (((size_t)(e >> 5) * nseq + s) * 4 + ((e >> 3) & 3)) * 16;
+    const int k = frag_pos(e & 7);
+    const __half hi = __float2half_rn(v);
+    h[base + k] = hi;
+    h[base + 8 + k] = __float2half_rn(v - __half2float(hi));
+}
 
 // Activation preparation for the tile kernel (one launch before it).
 struct XPrepParams {
@@ -307,7 +326,17 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_mma_kernel(const MvParams p)
     // activations of this K split: the producer's bulk copy of the prepared
     // records, plus the split's scale per sequence
     bool aborted = nblk > 0 && !mbar_wait(xbar, 0u, p.err);
-    for (int s = ctid; s < B; s += NC) xinv[s] = p.xinvg[(size_t)k_split * B + s];
+    for (int s = ctid; s < B; s += NC) {
+        float sc = 1.f;
+        if (p.scale_mode == 0) {
+            sc = p.xinvg[(size_t)k_split * B + s];
+        } else if (p.scale_mode == 1) {  // rmsnorm over the whole row, from the producer's partial sums
+            float a = 0.f;
+            for (int t = 0; t < p.ss_tiles; ++t) a += __ldcg(p.ss + (size_t)t * B + s);
+            sc = 1.f / sqrtf(a / float(p.ss_n) + p.eps);
+        }
+        xinv[s] = sc;
+    }
     named_sync(1, NC);
     pdl_launch_dependents();
 
@@ -417,6 +446,33 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_mma_kernel(const MvParams p)
 
         // ---- epilogue on fin[16][B]
         const int r0 = t * 16;
+        if ((EPI == EPI_ADD || EPI == EPI_SWIGLU) && p.rec_out) {
+            // one thread per sequence: the tile's outputs, their records for the next projection
+            // and (residual) the tile's sum of squares, in a fixed order
+            for (int s = ctid; s < B; s += NC) {
+                float ssum = 0.f;
+                for (int rl = 0; rl < 16; ++rl) {
+                    const int r = r0 + rl;
+                    if (r >= p.rows) break;
+                    const float val = fin[rl * B + s];
+                    if (EPI == EPI_ADD) {
+                        float* o = p.out + (size_t)s * p.ldo + r;
+                        const float xn = *o + val;
+                        *o = xn;
+                        ssum = fmaf(xn, xn, ssum);
+                        store_act_record(p.rec_out, B, r, s, p.rec_w ? xn * p.rec_w[r] : xn);
+                    } else if ((rl & 1) == 0) {
+                        const float up = fin[(rl + 1) * B + s];
+                        const float a = (val / (1.f + expf(-val))) * up;
+                        p.out[(size_t)s * p.ldo + (r >> 1)] = a;
+                        store_act_record(p.rec_out, B, r >> 1, s, a);
+                    }
+                }
+                if (EPI == EPI_ADD && p.ss_out) p.ss_out[(size_t)t * B + s] = ssum;
+            }
+            named_sync(1, NC);  // fin/red reused by the next tile
+            continue;
+        }
         for (int i = ctid; i < 16 * B; i += NC) {
             const int rl = i / B, s = i % B, r = r0 + rl;
             if (r >= p.rows) continue;

@@ -17,7 +17,7 @@ def _engine(path, **kw):
     return Engine(path, **kw)
 
 
-@pytest.mark.parametrize("nseq", [2, 3, 8])
+@pytest.mark.parametrize("nseq", [2, 3, 8, 24, 40])  # above 16: tile-kernel projections with producer-made records
 @pytest.mark.parametrize("name", ["tiny_q8", "tiny_q4"])
 def test_batched_greedy_matches_oracle(name, nseq):
     path = golden_model(name)
