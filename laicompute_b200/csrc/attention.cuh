@@ -39,7 +39,15 @@ struct AttnParams {
     unsigned* counters;        // [nseq][kv_heads], zero between launches (scratch)
     float sqrt_d;
     int* err;                  // set when a bounded wait runs out (chunked kernel)
+    uint8_t* rec_out;          // optional: binary16 hi/lo records of `out` for a tile-kernel projection
+    int nseq;                  // sequences of the step (the records' layout)
 };
+
+// out[seq][e] = v, plus its activation record when requested.
+__device__ __forceinline__ void attn_store(const AttnParams& p, int seq, int e, float v) {
+    p.out[(size_t)seq * p.ldo + e] = v;
+    if (p.rec_out) store_act_record(p.rec_out, p.nseq, e, seq, v);
+}
 
 template <typename KV, int N> struct KvLoad;
 template <> struct KvLoad<__half, 1> {
@@ -227,7 +235,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
             }
         }
         if (p.nsplit == 1) {
-            p.out[(size_t)seq * p.ldo + ((size_t)kvh * G + g) * D + dd] = A / L;
+            attn_store(p, seq, (kvh * G + g) * D + dd, A / L);
         } else {
             float* dst = p.part + ((pair * p.nsplit + split) * G + g) * PD;
             dst[dd] = A;
@@ -260,7 +268,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
             L = fmaf(__ldcg(src + j * sstride + D + 1), e, L);
             A = fmaf(__ldcg(src + j * sstride + dd), e, A);
         }
-        p.out[(size_t)seq * p.ldo + ((size_t)kvh * G + g) * D + dd] = A / L;
+        attn_store(p, seq, (kvh * G + g) * D + dd, A / L);
     }
     if (threadIdx.x == 0) p.counters[pair] = 0u;
 }
@@ -539,7 +547,7 @@ __device__ __forceinline__ void attn_mma_body(const AttnParams& p, int split, in
 #pragma unroll
         for (int w = 0; w < NW; ++w) A = fmaf(cacc[((size_t)w * 8 + g) * D + dd], mw[w][g], A);
         if (active == 1) {
-            p.out[(size_t)seq * p.ldo + ((size_t)kvh * G + g) * D + dd] = A / mL[g];
+            attn_store(p, seq, (kvh * G + g) * D + dd, A / mL[g]);
         } else {
             float* dst = p.part + ((pair * p.nsplit + split) * G + g) * PD;
             dst[dd] = A;
@@ -574,7 +582,7 @@ __device__ __forceinline__ void attn_mma_body(const AttnParams& p, int split, in
         const int g = i / D, dd = i % D;
         float A = 0.f;
         for (int j = 0; j < active; ++j) A = fmaf(__ldcg(base + j * sstride + g * PD + dd), mw[j][g], A);
-        p.out[(size_t)seq * p.ldo + ((size_t)kvh * G + g) * D + dd] = A / mL[g];
+        attn_store(p, seq, (kvh * G + g) * D + dd, A / mL[g]);
     }
     if (tid == 0) p.counters[pair] = 0u;
 }

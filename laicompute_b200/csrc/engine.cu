@@ -377,7 +377,7 @@ struct laic_dev {
     uint8_t *step_rec_x = nullptr, *step_rec_act = nullptr;  // activation digit records between phases
     // more than 16 sequences on one GPU: binary16 hi/lo activation records written by the producing
     // kernels (embedding, o/down residual epilogues, SwiGLU) for the tile-kernel projections
-    uint8_t *rec_x = nullptr, *rec_act = nullptr;
+    uint8_t *rec_x = nullptr, *rec_act = nullptr, *rec_attn = nullptr;
     float* rec_ss = nullptr;  // [h / 16 row tiles][max_seqs] sums of squares of the residual
     float* step_ss = nullptr;
     int step_type = -1;
@@ -545,6 +545,7 @@ struct laic_dev {
             ap.kc = p.kc; ap.vc = p.vc; ap.slot_stride = kv_slot_stride; ap.cap = cap;
             ap.heads = H; ap.kv_heads = Hkv; ap.slots = d_slots; ap.pos = pos; ap.nsplit = nsplit;
             ap.part = attn_part; ap.counters = attn_cnt; ap.sqrt_d = sqrtf((float)D); ap.err = mvs.err;
+            ap.nseq = nseq; ap.rec_out = recs ? rec_attn : nullptr;
             t_begin("attention", attn_bytes);
             CK(launch_k(afn, dim3(nsplit, Hkv, nseq), dim3(laic::kAttnWarps * 32), attn_smem(D, kv32), s, pdl, ap));
             ++nl;
@@ -552,9 +553,10 @@ struct laic_dev {
             // o + residual
             laic::MvParams po{};
             po.nseq = nseq; po.x = attn; po.ldx = hq; po.out = x; po.ldo = h;
-            if (recs) { po.rec_out = rec_x; po.rec_w = ly.ffn_norm; po.ss_out = rec_ss; }
+            RecIn r_o;
+            if (recs) { po.rec_out = rec_x; po.rec_w = ly.ffn_norm; po.ss_out = rec_ss; r_o.xg = rec_attn; r_o.mode = 2; }
             t_begin("o", (double)ly.o.bytes() + 4.0 * nseq * hq + 8.0 * nseq * h);
-            CK(launch_matvec(ly.o, po, residual_epi, kv32, mvs, s, pdl, &nl));
+            CK(launch_matvec(ly.o, po, residual_epi, kv32, mvs, s, pdl, &nl, &r_o));
             t_end();
             if (int rc = allreduce_residual(nseq, s, t_begin, t_end)) return rc;
             // gate/up + swiglu
@@ -845,6 +847,7 @@ int laic_dev_create(const laic_dev_desc* desc, const laic_dev_opts* opts, laic_d
     if (S > 16) {  // activation records between tile-kernel projections
         CK(cudaMalloc(&d->rec_x, S * d->h * 4));
         CK(cudaMalloc(&d->rec_act, S * d->F * 4));
+        CK(cudaMalloc(&d->rec_attn, S * d->hq * 4));
         CK(cudaMalloc(&d->rec_ss, S * ((d->h + 15) / 16) * 4));
     }
     CK(cudaMalloc(&d->counts, S * d->V * 4));
@@ -901,7 +904,7 @@ void laic_dev_destroy(laic_dev* d) {
     void* bufs[] = {d->out_norm, d->x, d->q, d->attn, d->act, d->logits, d->kc, d->vc, d->pos, d->counts,
                     d->rope_cs, d->attn_part, d->attn_cnt, d->d_tokens, d->d_out_ids, d->d_slots, d->d_err, d->d_params,
                     d->d_hist, d->d_hist_count, d->logits_l, d->logits_g, d->d_step_layers, d->step_bar,
-                    d->step_rec_x, d->step_rec_act, d->step_ss, d->rec_x, d->rec_act, d->rec_ss};
+                    d->step_rec_x, d->step_rec_act, d->step_ss, d->rec_x, d->rec_act, d->rec_ss, d->rec_attn};
     for (void* b : bufs) if (b) cudaFree(b);
     void* hb[] = {d->h_tokens, d->h_out_ids, d->h_slots, d->h_params};
     for (void* b : hb) if (b) cudaFreeHost(b);
