@@ -28,6 +28,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -37,6 +38,7 @@
 #include <vector>
 
 #include "../../include/laic_b200.h"
+#include "allreduce.cuh"
 #include "attention.cuh"
 #include "launch.cuh"
 #include "misc.cuh"
@@ -368,6 +370,12 @@ struct laic_dev {
     int tp = 1, tr = 0;  // tensor-parallel size and rank
     laic::ncclComm_t comm = nullptr;
     const laic::NcclApi* nccl = nullptr;
+    // one-shot peer-memory allreduce of the residual (else NCCL): mailboxes of every rank
+    bool ar_p2p = false;
+    laic::ArParams ar{};
+    float* ar_box = nullptr;      // this rank's mailbox data
+    unsigned* ar_flags = nullptr; // this rank's mailbox flags
+    unsigned* ar_ctr = nullptr;   // [epoch, done]
     float *logits_l = nullptr, *logits_g = nullptr;  // tp > 1: this rank's vocabulary rows; every rank's
     bool have_lm = false;  // tp > 1: lm holds this rank's lm_head rows
 
@@ -453,12 +461,60 @@ struct laic_dev {
 
     // Tensor parallel: sum the ranks' partial o / down products held in the residual.
     template <typename TB, typename TE>
-    int allreduce_residual(int nseq, cudaStream_t s, TB& t_begin, TE& t_end) {
+    int allreduce_residual(int nseq, cudaStream_t s, TB& t_begin, TE& t_end, int* nl) {
         if (tp == 1) return LAIC_OK;
         t_begin("allreduce", 8.0 * nseq * h * (tp - 1) / tp);
-        const laic::ncclResult_t r = nccl->AllReduce(x, x, (size_t)nseq * h, laic::ncclFloat32, laic::ncclSum, comm, s);
-        if (r != laic::ncclSuccess) return fail(LAIC_E_NCCL, std::string("ncclAllReduce: ") + nccl->GetErrorString(r));
+        if (ar_p2p) {
+            laic::ArParams ap = ar;
+            ap.x = x; ap.n = nseq * h;
+            CK(launch_k(laic::allreduce_oneshot_kernel, dim3(laic::kArCtas), dim3(laic::kArThreads), 0, s, use_pdl, ap));
+            ++*nl;
+        } else {
+            const laic::ncclResult_t r = nccl->AllReduce(x, x, (size_t)nseq * h, laic::ncclFloat32, laic::ncclSum, comm, s);
+            if (r != laic::ncclSuccess) return fail(LAIC_E_NCCL, std::string("ncclAllReduce: ") + nccl->GetErrorString(r));
+        }
         t_end();
+        return LAIC_OK;
+    }
+
+    // Map every rank's mailbox (CUDA IPC handles exchanged with one NCCL all-gather). Leaves
+    // ar_p2p false, and NCCL in charge, if a rank cannot map a peer.
+    int setup_p2p_allreduce() {
+        if (tp < 2 || tp > laic::kArMaxRanks) return LAIC_OK;
+        const int nmax = S * h;
+        CK(cudaMalloc(&ar_box, (size_t)2 * tp * nmax * 4));
+        CK(cudaMalloc(&ar_flags, (size_t)2 * tp * laic::kArCtas * 4));
+        CK(cudaMemset(ar_flags, 0, (size_t)2 * tp * laic::kArCtas * 4));
+        CK(cudaMalloc(&ar_ctr, 8));
+        CK(cudaMemset(ar_ctr, 0, 8));
+        cudaIpcMemHandle_t hd[2];
+        CK(cudaIpcGetMemHandle(&hd[0], ar_box));
+        CK(cudaIpcGetMemHandle(&hd[1], ar_flags));
+        const size_t hb = sizeof hd;
+        void* dev = nullptr;
+        CK(cudaMalloc(&dev, hb * (tp + 1)));
+        CK(cudaMemcpy((char*)dev + hb * tp, hd, hb, cudaMemcpyHostToDevice));
+        const laic::ncclResult_t r = nccl->AllGather((char*)dev + hb * tp, dev, hb / 4, laic::ncclFloat32, comm, st);
+        if (r != laic::ncclSuccess) { cudaFree(dev); return fail(LAIC_E_NCCL, std::string("ncclAllGather: ") + nccl->GetErrorString(r)); }
+        std::vector<cudaIpcMemHandle_t> all(2 * tp);
+        CK(cudaStreamSynchronize(st));
+        CK(cudaMemcpy(all.data(), dev, hb * tp, cudaMemcpyDeviceToHost));
+        cudaFree(dev);
+        ar = laic::ArParams{};
+        ar.rank = tr; ar.ranks = tp; ar.nmax = nmax; ar.epoch = ar_ctr; ar.done = ar_ctr + 1;
+        bool ok = true;
+        for (int q = 0; q < tp && ok; ++q) {
+            if (q == tr) { ar.box[q] = ar_box; ar.flags[q] = ar_flags; continue; }
+            void *pb = nullptr, *pf = nullptr;
+            if (cudaIpcOpenMemHandle(&pb, all[2 * q], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess ||
+                cudaIpcOpenMemHandle(&pf, all[2 * q + 1], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+                cudaGetLastError();
+                ok = false;
+                break;
+            }
+            ar.box[q] = (float*)pb; ar.flags[q] = (unsigned*)pf;
+        }
+        ar_p2p = ok;
         return LAIC_OK;
     }
 
@@ -558,7 +614,7 @@ struct laic_dev {
             t_begin("o", (double)ly.o.bytes() + 4.0 * nseq * hq + 8.0 * nseq * h);
             CK(launch_matvec(ly.o, po, residual_epi, kv32, mvs, s, pdl, &nl, &r_o));
             t_end();
-            if (int rc = allreduce_residual(nseq, s, t_begin, t_end)) return rc;
+            if (int rc = allreduce_residual(nseq, s, t_begin, t_end, &nl)) return rc;
             // gate/up + swiglu
             laic::MvParams pg{};
             pg.nseq = nseq; pg.eps = a.rms_eps; pg.x = x; pg.ldx = h; pg.norm_w = ly.ffn_norm; pg.out = act; pg.ldo = F;
@@ -579,7 +635,7 @@ struct laic_dev {
             t_begin("down", (double)ly.down.bytes() + 4.0 * nseq * (F + 2 * h));
             CK(launch_matvec(ly.down, pd, residual_epi, kv32, mvs, s, pdl, &nl, &r_dn));
             t_end();
-            if (int rc = allreduce_residual(nseq, s, t_begin, t_end)) return rc;
+            if (int rc = allreduce_residual(nseq, s, t_begin, t_end, &nl)) return rc;
         }
         if (full) {
             laic::MvParams pl{};
@@ -834,6 +890,7 @@ int laic_dev_create(const laic_dev_desc* desc, const laic_dev_opts* opts, laic_d
         std::memcpy(&id, o.nccl_id, sizeof id);
         const laic::ncclResult_t r = d->nccl->CommInitRank(&d->comm, tp, id, d->tr);
         if (r != laic::ncclSuccess) return fail(LAIC_E_NCCL, std::string("ncclCommInitRank: ") + d->nccl->GetErrorString(r));
+        d->ar.err = nullptr;
     }
     d->kv_slot_stride = (long long)d->Hkv * cap * D;
     d->kv_layer_stride = d->kv_slot_stride * (long long)S;
@@ -882,6 +939,15 @@ int laic_dev_create(const laic_dev_desc* desc, const laic_dev_opts* opts, laic_d
     CK(cudaMallocHost(&d->h_out_ids, S * 4));
     CK(cudaMallocHost(&d->h_slots, S * 4));
     CK(cudaMallocHost(&d->h_params, S * sizeof(laic::SampleDev)));
+    if (tp > 1) {
+        // the residual allreduce through peer memory unless LAIC_TP_NCCL_ALLREDUCE=1 asks for NCCL
+        const char* env = std::getenv("LAIC_TP_NCCL_ALLREDUCE");
+        if (!(env && env[0] == '1')) {
+            if (int rc = mv_scratch_reserve(d->mvs, MvNeed{})) return rc;  // the error flag
+            if (int rc = d->setup_p2p_allreduce()) return rc;
+            d->ar.err = d->mvs.err;
+        }
+    }
     CK(cudaDeviceSynchronize());
     *out = d.release();
     return LAIC_OK;
@@ -893,6 +959,11 @@ void laic_dev_destroy(laic_dev* d) {
     cudaStreamSynchronize(d->st);
     for (auto& kv : d->graphs) cudaGraphExecDestroy(kv.second);  // graphs holding NCCL calls go first
     d->graphs.clear();
+    for (int q = 0; q < d->tp && d->ar_p2p; ++q) {
+        if (q == d->tr) continue;
+        if (d->ar.box[q]) cudaIpcCloseMemHandle(d->ar.box[q]);
+        if (d->ar.flags[q]) cudaIpcCloseMemHandle(d->ar.flags[q]);
+    }
     if (d->comm) d->nccl->CommDestroy(d->comm);
     for (auto& l : d->layers) {
         mat_free(l.qkv); mat_free(l.o); mat_free(l.gu); mat_free(l.down);
@@ -904,7 +975,7 @@ void laic_dev_destroy(laic_dev* d) {
     void* bufs[] = {d->out_norm, d->x, d->q, d->attn, d->act, d->logits, d->kc, d->vc, d->pos, d->counts,
                     d->rope_cs, d->attn_part, d->attn_cnt, d->d_tokens, d->d_out_ids, d->d_slots, d->d_err, d->d_params,
                     d->d_hist, d->d_hist_count, d->logits_l, d->logits_g, d->d_step_layers, d->step_bar,
-                    d->step_rec_x, d->step_rec_act, d->step_ss, d->rec_x, d->rec_act, d->rec_ss, d->rec_attn};
+                    d->step_rec_x, d->step_rec_act, d->step_ss, d->rec_x, d->rec_act, d->rec_ss, d->rec_attn, d->ar_box, d->ar_flags, d->ar_ctr};
     for (void* b : bufs) if (b) cudaFree(b);
     void* hb[] = {d->h_tokens, d->h_out_ids, d->h_slots, d->h_params};
     for (void* b : hb) if (b) cudaFreeHost(b);
