@@ -119,6 +119,15 @@ LAIC_API int laic_dev_upload(laic_dev* dev, const char* name, int32_t ggml_type,
  * discarded. Advances each slot's position by one. */
 LAIC_API int laic_dev_prefill(laic_dev* dev, int32_t nseq, const uint32_t* tokens, const int32_t* slots);
 
+/* The n prompt tokens of one slot in one pass (the KV cache for positions
+ * pos..pos+n-1, the slot's position and history advanced): the same effect
+ * as n laic_dev_prefill calls, with the projections as dense fp16 tensor-core
+ * GEMMs over all n tokens (replaces the per-token prompt loop of
+ * LlamaRuntime::generate_ids, reference src/inference_v2.cpp:34). Weights are
+ * dequantised to binary16 for it. The FP32-KV parity mode and tensor-parallel
+ * engines run the per-token steps instead. */
+LAIC_API int laic_dev_prefill_batch(laic_dev* dev, int32_t slot, const uint32_t* tokens, int32_t n);
+
 /* LlamaRuntime::step(token) followed by sample(): one token per listed slot,
  * the full forward pass, then the token choice on the device. `params` holds
  * nparams entries (1 = shared by all sequences, else one per sequence).

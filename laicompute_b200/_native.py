@@ -20,6 +20,7 @@ EXPORTS = (
     "laic_dev_reset_slot", "laic_dev_slot_pos", "laic_dev_fill_kv", "laic_dev_sync", "laic_dev_stats_get",
     "laic_dev_stream", "laic_dev_decode", "laic_dev_profile", "laic_nccl_unique_id", "laic_tensor_create", "laic_tensor_destroy",
     "laic_tensor_matvec", "laic_tensor_dequant", "laic_tensor_bytes", "laic_tensor_matvec_noalloc",
+    "laic_dev_prefill_batch",
 )
 
 
@@ -77,6 +78,7 @@ def lib() -> ctypes.CDLL:
     L.laic_dev_destroy.restype = None
     L.laic_dev_upload.argtypes = [P, ctypes.c_char_p, I32, ctypes.POINTER(U64), I32, P, SZ]
     L.laic_dev_prefill.argtypes = [P, I32, P, P]
+    L.laic_dev_prefill_batch.argtypes = [P, I32, P, I32]
     L.laic_dev_step.argtypes = [P, I32, P, P, ctypes.POINTER(SampleParams), I32, P, P]
     L.laic_dev_reset_slot.argtypes = [P, I32]
     L.laic_dev_slot_pos.argtypes = [P, I32, ctypes.POINTER(ctypes.c_int64)]
@@ -100,7 +102,7 @@ def lib() -> ctypes.CDLL:
     for name in ("laic_dev_create", "laic_dev_upload", "laic_dev_prefill", "laic_dev_step", "laic_dev_reset_slot",
                  "laic_dev_slot_pos", "laic_dev_fill_kv", "laic_dev_sync", "laic_dev_stats_get",
                  "laic_dev_decode", "laic_dev_profile", "laic_nccl_unique_id", "laic_tensor_create", "laic_tensor_matvec",
-                 "laic_tensor_dequant", "laic_tensor_matvec_noalloc"):
+                 "laic_tensor_dequant", "laic_tensor_matvec_noalloc", "laic_dev_prefill_batch"):
         getattr(L, name).restype = I32
     _lib = L
     return L

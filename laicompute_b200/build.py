@@ -30,6 +30,23 @@ NVFLAGS = ["-std=c++17", "-O3", "-lineinfo", *ARCH, "-Xcompiler", "-fPIC,-fvisib
 CXXFLAGS = ["-std=c++17", "-O2", "-fPIC", "-Wall", f"-I{INCLUDE}"]
 
 
+def _cutlass_root() -> str:
+    """CUTLASS/CuTe headers vendored in this image's Python packages (for the prefill GEMM)."""
+    import sysconfig
+    site = sysconfig.get_paths()["purelib"]
+    for cand in (os.path.join(site, "flashinfer", "data", "cutlass"), os.path.join(site, "tilelang", "3rdparty", "cutlass")):
+        if os.path.exists(os.path.join(cand, "include", "cute", "arch", "mma_sm100_umma.hpp")):
+            return cand
+    raise RuntimeError("CUTLASS headers with sm100 support not found")
+
+
+def _nvflags(src: str) -> list:
+    if os.path.basename(src) != "gemm_sm100.cu":
+        return NVFLAGS
+    root = _cutlass_root()
+    return [*NVFLAGS, f"-I{root}/include", f"-I{root}/tools/util/include", "--expt-relaxed-constexpr"]
+
+
 def _headers() -> list[str]:
     return (glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(CSRC, "*.h"))
             + glob.glob(os.path.join(INCLUDE, "**", "*.h*"), recursive=True))
@@ -58,7 +75,7 @@ def build(verbose: bool = False) -> str:
     for src in sorted(glob.glob(os.path.join(CSRC, "*.cu"))):
         obj = os.path.join(BUILD, os.path.basename(src) + ".o")
         if _stale(obj, [src, *hdrs]):
-            jobs.append(("nvcc", src, [NVCC, *NVFLAGS, "-c", src, "-o", obj]))
+            jobs.append(("nvcc", src, [NVCC, *_nvflags(src), "-c", src, "-o", obj]))
         objs.append(obj)
     for src in sorted(glob.glob(os.path.join(CSRC, "*.cpp"))):  # engine internals (not exported)
         obj = os.path.join(BUILD, os.path.basename(src) + ".o")

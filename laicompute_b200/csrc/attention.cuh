@@ -41,6 +41,7 @@ struct AttnParams {
     int* err;                  // set when a bounded wait runs out (chunked kernel)
     uint8_t* rec_out;          // optional: binary16 hi/lo records of `out` for a tile-kernel projection
     int nseq;                  // sequences of the step (the records' layout)
+    const int* npos;           // optional: per query row, its position (batched prefill: causal per row)
 };
 
 // out[seq][e] = v, plus its activation record when requested.
@@ -111,7 +112,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
 
     pdl_wait();
     const int slot = p.slots[seq];
-    const int n = p.pos[slot] + 1;
+    const int n = (p.npos ? p.npos[seq] : p.pos[slot]) + 1;
     const int ntiles = (n + 31) >> 5;
     const int tps = (ntiles + p.nsplit - 1) / p.nsplit;
     const int tile0 = split * tps, tile1 = min(ntiles, tile0 + tps);
@@ -355,7 +356,7 @@ __device__ __forceinline__ void attn_mma_body(const AttnParams& p, int split, in
 
     // positions of this sequence: final for this step before the dependency wait
     const int slot = p.slots[seq];
-    const int n = p.pos[slot] + 1;
+    const int n = (p.npos ? p.npos[seq] : p.pos[slot]) + 1;
     const int nch = (n + kAttnChunk - 1) / kAttnChunk;
     const int active = min(p.nsplit, nch);
     if (split >= active) {

@@ -45,6 +45,7 @@
 #include "mma_matvec.cuh"
 #include "mv_streamk.cuh"
 #include "nccl_dl.h"
+#include "prefill.cuh"
 #include "sampler.cuh"
 #include "step_kernel.cuh"
 
@@ -386,6 +387,15 @@ struct laic_dev {
     // more than 16 sequences on one GPU: binary16 hi/lo activation records written by the producing
     // kernels (embedding, o/down residual epilogues, SwiGLU) for the tile-kernel projections
     uint8_t *rec_x = nullptr, *rec_act = nullptr, *rec_attn = nullptr;
+
+    // batched prompt prefill (tensor-core GEMMs over the prompt's tokens)
+    static constexpr int kPfRows = 512;  // tokens per pass
+    float *pf_x = nullptr, *pf_c = nullptr, *pf_q = nullptr, *pf_attn = nullptr;
+    __half *pf_a = nullptr, *pf_w = nullptr;
+    int *pf_slots = nullptr, *pf_npos = nullptr;
+    unsigned* pf_tokens = nullptr;
+    void* pf_ws = nullptr;
+    size_t pf_ws_bytes = 0;
     float* rec_ss = nullptr;  // [h / 16 row tiles][max_seqs] sums of squares of the residual
     float* step_ss = nullptr;
     int step_type = -1;
@@ -727,6 +737,95 @@ struct laic_dev {
         return LAIC_OK;
     }
 
+    int prefill_alloc() {
+        if (pf_x) return LAIC_OK;
+        const size_t T = kPfRows;
+        size_t wmax = 0, cmax = 0;
+        for (auto& l : layers)
+            for (const Mat* m : {&l.qkv, &l.o, &l.gu, &l.down}) {
+                wmax = std::max(wmax, (size_t)m->rows * m->in);
+                cmax = std::max(cmax, (size_t)m->rows);
+            }
+        const size_t amax = std::max((size_t)std::max(h, hq), (size_t)F);
+        CK(cudaMalloc(&pf_x, T * h * 4));
+        CK(cudaMalloc(&pf_c, T * cmax * 4));
+        CK(cudaMalloc(&pf_q, T * hq * 4));
+        CK(cudaMalloc(&pf_attn, T * hq * 4));
+        CK(cudaMalloc(&pf_a, T * amax * 2));
+        CK(cudaMalloc(&pf_w, wmax * 2));
+        CK(cudaMalloc(&pf_slots, T * 4));
+        CK(cudaMalloc(&pf_npos, T * 4));
+        CK(cudaMalloc(&pf_tokens, T * 4));
+        for (auto& l : layers)
+            for (const Mat* m : {&l.qkv, &l.o, &l.gu, &l.down})
+                pf_ws_bytes = std::max(pf_ws_bytes, laic::gemm_f16_workspace((int)T, m->rows, m->in));
+        if (pf_ws_bytes) CK(cudaMalloc(&pf_ws, pf_ws_bytes));
+        return LAIC_OK;
+    }
+
+    // C[T][rows] = A[T][in] x W^T for one projection (weights dequantised to binary16 first).
+    int prefill_gemm(const Mat& m, int T, cudaStream_t s) {
+        const int grid = 8 * num_sms();
+        laic::dequant_f16_kernel<<<grid, 256, 0, s>>>(m.type, m.q, m.s, m.nb, m.rows, pf_w);
+        CK(cudaGetLastError());
+        const cudaError_t e = laic::gemm_f16(T, m.rows, m.in, pf_a, pf_w, pf_c, pf_ws, pf_ws_bytes, s);
+        if (e != cudaSuccess) return fail(LAIC_E_CUDA, std::string("prefill gemm: ") + cudaGetErrorString(e));
+        return LAIC_OK;
+    }
+
+    // The prompt tokens of one slot through every layer together (KV cache filled, position
+    // advanced, tokens added to the slot's history), like n prefill steps.
+    int prefill_batch(int slot, const uint32_t* tokens, int n) {
+        if (int rc = prefill_alloc()) return rc;
+        cudaStream_t s = st;
+        const int grid = 8 * num_sms();
+        const size_t kvb = 2;
+        for (int t0 = 0; t0 < n; t0 += kPfRows) {
+            const int T = std::min(kPfRows, n - t0);
+            const int p0 = (int)h_pos[slot];
+            CK(cudaMemcpyAsync(pf_tokens, tokens + t0, (size_t)T * 4, cudaMemcpyHostToDevice, s));
+            laic::prefill_rows_kernel<<<(T + 255) / 256, 256, 0, s>>>(slot, p0, T, pf_slots, pf_npos);
+            laic::EmbedParams ep{embd.type, embd.q, embd.s, h, embd.nb, pf_tokens, pf_slots, pf_x, counts, V};
+            laic::embed_kernel<<<T, 256, 0, s>>>(ep);
+            CK(cudaGetLastError());
+            for (int l = 0; l < L; ++l) {
+                Layer& ly = layers[l];
+                __half* kcl = (__half*)((char*)kc + ((size_t)l * kv_layer_stride + (size_t)slot * kv_slot_stride) * kvb);
+                __half* vcl = (__half*)((char*)vc + ((size_t)l * kv_layer_stride + (size_t)slot * kv_slot_stride) * kvb);
+                // qkv
+                laic::rmsnorm_f16_kernel<<<T, 256, 0, s>>>(pf_x, h, ly.attn_norm, a.rms_eps, h, pf_a, h);
+                if (int rc = prefill_gemm(ly.qkv, T, s)) return rc;
+                laic::QkvPostParams qp{pf_c, T, hq, kv, D, rope_pairs, p0, rope_cs, pf_q, kcl, vcl, cap};
+                laic::qkv_post_kernel<<<grid, 256, 0, s>>>(qp);
+                // attention: one query row per token, causal through its own position
+                laic::AttnParams ap{};
+                ap.q = pf_q; ap.ldq = hq; ap.out = pf_attn; ap.ldo = hq;
+                ap.kc = (char*)kc + (size_t)l * kv_layer_stride * kvb; ap.vc = (char*)vc + (size_t)l * kv_layer_stride * kvb;
+                ap.slot_stride = kv_slot_stride; ap.cap = cap; ap.heads = H; ap.kv_heads = Hkv;
+                ap.slots = pf_slots; ap.pos = pos; ap.npos = pf_npos; ap.nsplit = 1;
+                ap.part = attn_part; ap.counters = attn_cnt; ap.sqrt_d = sqrtf((float)D); ap.err = mvs.err; ap.nseq = T;
+                CK(laic::launch_k(attn_pick(D, G, false), dim3(1, Hkv, T), dim3(laic::kAttnWarps * 32), attn_smem(D, false),
+                                  s, false, ap));
+                // o + residual
+                laic::to_f16_kernel<<<grid, 256, 0, s>>>(pf_attn, pf_a, (size_t)T * hq);
+                if (int rc = prefill_gemm(ly.o, T, s)) return rc;
+                laic::residual_add_kernel<<<grid, 256, 0, s>>>(pf_x, pf_c, (size_t)T * h);
+                // gate/up + swiglu, down + residual
+                laic::rmsnorm_f16_kernel<<<T, 256, 0, s>>>(pf_x, h, ly.ffn_norm, a.rms_eps, h, pf_a, h);
+                if (int rc = prefill_gemm(ly.gu, T, s)) return rc;
+                laic::swiglu_f16_kernel<<<grid, 256, 0, s>>>(pf_c, T, F, pf_a);
+                if (int rc = prefill_gemm(ly.down, T, s)) return rc;
+                laic::residual_add_kernel<<<grid, 256, 0, s>>>(pf_x, pf_c, (size_t)T * h);
+                CK(cudaGetLastError());
+            }
+            laic::add_pos_kernel<<<1, 32, 0, s>>>(pos, slot, T);
+            CK(cudaGetLastError());
+            CK(cudaStreamSynchronize(s));  // the token buffer is reused by the next pass
+            h_pos[slot] += T;
+        }
+        return LAIC_OK;
+    }
+
     // Size the matvec scratch for `nseq` sequences (before any capture).
     int reserve_scratch(int nseq) {
         if (int rc = prepare_step()) return rc;
@@ -975,7 +1074,9 @@ void laic_dev_destroy(laic_dev* d) {
     void* bufs[] = {d->out_norm, d->x, d->q, d->attn, d->act, d->logits, d->kc, d->vc, d->pos, d->counts,
                     d->rope_cs, d->attn_part, d->attn_cnt, d->d_tokens, d->d_out_ids, d->d_slots, d->d_err, d->d_params,
                     d->d_hist, d->d_hist_count, d->logits_l, d->logits_g, d->d_step_layers, d->step_bar,
-                    d->step_rec_x, d->step_rec_act, d->step_ss, d->rec_x, d->rec_act, d->rec_ss, d->rec_attn, d->ar_box, d->ar_flags, d->ar_ctr};
+                    d->step_rec_x, d->step_rec_act, d->step_ss, d->rec_x, d->rec_act, d->rec_ss, d->rec_attn, d->ar_box, d->ar_flags, d->ar_ctr,
+                    d->pf_x, d->pf_c, d->pf_q, d->pf_attn, d->pf_a, d->pf_w, d->pf_slots, d->pf_npos, d->pf_tokens,
+                    d->pf_ws};
     for (void* b : bufs) if (b) cudaFree(b);
     void* hb[] = {d->h_tokens, d->h_out_ids, d->h_slots, d->h_params};
     for (void* b : hb) if (b) cudaFreeHost(b);
@@ -1090,6 +1191,29 @@ static int fill_inputs(laic_dev* d, int32_t nseq, const uint32_t* tokens, const 
     std::memcpy(d->h_tokens, tokens, nseq * 4);
     std::memcpy(d->h_slots, slots, nseq * 4);
     return LAIC_OK;
+}
+
+int laic_dev_prefill_batch(laic_dev* d, int32_t slot, const uint32_t* tokens, int32_t n) {
+    if (!d || !tokens) return fail(LAIC_E_INVALID, "null argument");
+    if (n < 0) return fail(LAIC_E_INVALID, "negative token count");
+    if (n == 0) return LAIC_OK;
+    CK(cudaSetDevice(d->device));
+    if (slot < 0 || slot >= d->S) return fail(LAIC_E_INVALID, "slot out of range");
+    std::string missing;
+    if (!d->ready(missing)) return fail(LAIC_E_MISSING, "missing tensor: " + missing);
+    for (int i = 0; i < n; ++i)
+        if (tokens[i] >= (uint32_t)d->V || tokens[i] >= (uint32_t)d->embd.rows)
+            return fail(LAIC_E_INVALID, "invalid embedding tensor");
+    if (d->h_pos[slot] + n > d->cap) return fail(LAIC_E_CONTEXT, "context length exceeded");
+    if (d->kv32 || d->tp > 1 || !(d->D == 32 || d->D == 64 || d->D == 128)) {
+        // FP32-KV parity mode and tensor parallel runs: the per-token steps
+        for (int i = 0; i < n; ++i) {
+            const int32_t sl = slot;
+            if (int rc = laic_dev_prefill(d, 1, tokens + i, &sl)) return rc;
+        }
+        return LAIC_OK;
+    }
+    return d->prefill_batch(slot, tokens, n);
 }
 
 int laic_dev_prefill(laic_dev* d, int32_t nseq, const uint32_t* tokens, const int32_t* slots) {

@@ -37,6 +37,11 @@ cudaError_t mv_sk_launch(int type, int nt, int epi, bool kv32, const MvParams& p
 // Raise the dynamic shared memory limit of every instantiation (call before any graph capture).
 cudaError_t mv_set_attributes();
 
+// Batched prefill GEMM (gemm_sm100.cu): C[M][N] fp32 = A[M][K] fp16 x W[N][K]^T fp16.
+size_t gemm_f16_workspace(int M, int N, int K);
+cudaError_t gemm_f16(int M, int N, int K, const void* A, const void* W, float* C, void* workspace, size_t ws_bytes,
+                     cudaStream_t st);
+
 struct StepParams;
 // One-sequence decode-step kernel (step.cu): shared memory it needs, attribute setup with the
 // resulting CTAs per SM (call before capture), and its cooperative launch (one CTA per SM).

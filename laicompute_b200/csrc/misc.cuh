@@ -44,7 +44,7 @@ __global__ void embed_kernel(const EmbedParams p) {
         ss = block_sum(ss, red);
         if (threadIdx.x == 0) p.ss_out[s] = ss;
     }
-    if (threadIdx.x == 0) p.counts[(size_t)p.slots[s] * p.vocab + tok] += 1u;
+    if (threadIdx.x == 0) atomicAdd(p.counts + (size_t)p.slots[s] * p.vocab + tok, 1u);  // rows may share a slot
     pdl_launch_dependents();
 }
 

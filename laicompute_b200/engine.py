@@ -82,6 +82,11 @@ class Engine:
         t, s = self._arrays(tokens, slots)
         check(lib().laic_dev_prefill(self.h, len(t), t.ctypes.data, s.ctypes.data))
 
+    def prefill_batch(self, tokens, slot: int = 0) -> None:
+        """The prompt tokens of one slot in one pass (tensor-core GEMMs over all of them)."""
+        t = np.ascontiguousarray(np.atleast_1d(tokens), dtype=np.uint32)
+        check(lib().laic_dev_prefill_batch(self.h, slot, t.ctypes.data, len(t)))
+
     def step(self, tokens, slots=None, params=None, want_logits: bool = False):
         """Forward pass + sampling for one token per slot; returns (ids, logits or None)."""
         t, s = self._arrays(tokens, slots)
@@ -144,12 +149,16 @@ class Engine:
         return {recs[i].name.decode(): (recs[i].launches, recs[i].total_us, recs[i].bytes) for i in range(n.value)}
 
     def generate(self, prompt: np.ndarray, steps: int, params: Optional[SampleParams] = None, slot: int = 0,
-                 want_logits: bool = False):
-        """Single-sequence generation with the reference loop (no EOS stop)."""
+                 want_logits: bool = False, batched_prefill: bool = False):
+        """Single-sequence generation with the reference loop (no EOS stop); `batched_prefill`
+        runs the prompt (all but its last token) in one pass."""
         prompt = np.asarray(prompt, dtype=np.uint32)
         self.reset_slot(slot)
-        for tok in prompt[:-1]:
-            self.prefill([tok], [slot])
+        if batched_prefill:
+            self.prefill_batch(prompt[:-1], slot)
+        else:
+            for tok in prompt[:-1]:
+                self.prefill([tok], [slot])
         ids, all_logits = [], []
         tok = int(prompt[-1])
         for i in range(steps):
