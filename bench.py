@@ -272,8 +272,17 @@ def main() -> None:
         params = [sample_params(0.8, 40, 1.0, 1.0, 4242 + 1000 * seq_rank + i) for i in range(batch)]
     else:
         params = [sample_params()] * batch
-    for j in range(plen - 1):
-        eng.prefill(prompts[:, j], slots)
+    # the prompts (all but their last token) in batched passes, timed as a side figure
+    torch.cuda.synchronize()
+    t_pf = time.perf_counter()
+    if tp > 1:
+        for j in range(plen - 1):
+            eng.prefill(prompts[:, j], slots)
+    else:
+        for i in range(batch):
+            eng.prefill_batch(prompts[i, :-1], int(slots[i]))
+    eng.sync()
+    prefill_s = time.perf_counter() - t_pf
     first, _ = eng.step(prompts[:, -1], slots, params)
 
     # ---- device-resident decode loop (value)
@@ -346,6 +355,8 @@ def main() -> None:
             "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s", "h2d_bytes_per_step": batch * (4 + 4 + 24),
                     "d2h_bytes_per_step": batch * 4},
             "gpu_launches": int(args.steps * launches_chained),
+            "prefill": {"tokens_per_s": round(batch * (plen - 1) / prefill_s, 1), "prompt_tokens": plen - 1,
+                        "sequences": batch, "batched": tp == 1, "timing": "host wall clock, engine synchronised"},
             "roofline": {"bound": "hbm", "kernel": dname, "achieved": round(achieved, 1), "peak": peak,
                          "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
                          "bytes_per_launch": round(dbytes / dl), "us_per_launch": round(dus / dl, 3),
@@ -358,8 +369,7 @@ def main() -> None:
     # ---- batch-1 decode (the latency case) on the same model
     if not args.no_batch1 and batch > 1:
         e1b = Engine(path, max_seqs=1, device=local, kv_capacity=ctx_need)
-        for t in prompts[0, :-1]:
-            e1b.prefill([t], [0])
+        e1b.prefill_batch(prompts[0, :-1], 0)
         f1, _ = e1b.step([prompts[0, -1]], [0])
         w, _ = e1b.decode(f1, [0], None, steps=args.warmup)
         barrier(world)

@@ -5,9 +5,9 @@
 // reference's loop (chat-template wrap, encode, BOS, one step per prompt
 // token, sample -> EOS check -> callback -> step) but each step is one call
 // into the device engine, which returns the sampled id. The prompt's tokens
-// before the last one go through laic_dev_prefill (their logits are never
-// read); the last prompt token and every generated token go through
-// laic_dev_step (forward pass + sampling). The reference computes one more
+// before the last one go through laic_dev_prefill_batch in one pass (their
+// logits are never read); the last prompt token and every generated token go
+// through laic_dev_step (forward pass + sampling). The reference computes one more
 // forward pass after the final generated token whose logits it never uses;
 // that pass is skipped.
 #include "laic/inference.hpp"
@@ -110,9 +110,9 @@ std::vector<uint32_t> LlamaRuntime::generate_from_ids(const std::vector<uint32_t
     stop_requested_.store(false, std::memory_order_relaxed);
     const int32_t slot = 0;
     check(laic_dev_reset_slot(dev_, slot));
-    for (size_t i = 0; i + 1 < ids.size(); ++i) {
+    if (ids.size() > 1) {
         if (stop_requested()) throw std::runtime_error("generation stopped");
-        check(laic_dev_prefill(dev_, 1, &ids[i], &slot));
+        check(laic_dev_prefill_batch(dev_, slot, ids.data(), int32_t(ids.size() - 1)));
     }
     laic_sample_params sp{cfg.temperature, uint32_t(cfg.top_k), cfg.top_p, cfg.repeat_penalty, cfg.seed};
     std::vector<uint32_t> generated;

@@ -8,13 +8,19 @@ reference sources). Writes:
                          generated ids for four sampling settings, and the
                          reference dequantisation of three tensors (first 2048
                          values and the sha256 of the whole float32 array)
+  generate_text.json     the reference's public generate_ids path (text prompt ->
+                         chat-template wrap, tokenizer, BOS, prompt steps, sampling,
+                         EOS stop) on the tiny models: greedy and sampled ids, and
+                         for the sampled ones the per-step distance of the draw
+                         from a decision boundary (from the reference's logits)
   smollm135m_*.npz       reference outputs on the 135M-shaped models of the
                          benchmark workloads (the GGUF is regenerated from its
                          seed by laicompute_b200.synth; its sha256 is recorded):
                          ids, per-step argmax / max / top-2 margin / sum and
                          the first 64 logits
 
-Run from the repository root:  python tests/golden/make_golden.py
+Run from the repository root:  python tests/golden/make_golden.py [generate]
+("generate" writes only generate_text.json).
 """
 from __future__ import annotations
 
@@ -124,10 +130,98 @@ def make_smollm(workdir: str) -> None:
         print(name, "done")
 
 
+GEN_PROMPTS = ("Hello world", "The B200 decodes one token at a time.")
+# Sampled cases keep top_k = 0: with 0 < top_k < vocab and top_p = 1 the reference
+# walks the unspecified order std::nth_element leaves behind.
+GEN_CONFIGS = ({"max_tokens": 16},
+               {"max_tokens": 16, "temperature": 1.0, "top_k": 0, "top_p": 1.0, "repeat_penalty": 1.0, "seed": 7},
+               {"max_tokens": 16, "temperature": 0.7, "top_k": 0, "top_p": 0.9, "repeat_penalty": 1.3, "seed": 99})
+
+
+def _generate_prompt_ids(path: str, text: str) -> list:
+    """The prompt ids generate_ids builds (src/inference_v2.cpp:34): chat-template wrap, encode, BOS."""
+    meta = gguf.GgufFile(path).metadata
+    if "<|im_start|>" in str(meta.get("tokenizer.chat_template", "")) and "<|im_start|>" not in text:
+        text = "<|im_start|>user\n" + text + "<|im_end|>\n<|im_start|>assistant\n"
+    out = subprocess.run([O.ref_driver("strict"), "encode", path, text], check=True, capture_output=True, text=True)
+    ids = [int(v) for v in out.stdout.split()]
+    bos = meta.get("tokenizer.ggml.bos_token_id")
+    if meta.get("tokenizer.ggml.add_bos_token", False) and ids and ids[0] != bos:
+        ids.insert(0, bos)
+    return ids
+
+
+def _sample_margins(logits: np.ndarray, history: list, cfg: dict, ids: list) -> tuple:
+    """Per generated step, how far the reference's draw sits from a decision boundary of
+    sample() (src/inference_v2.cpp:32, top_k = 0): the smallest distance of u from the
+    candidate CDF and of top_p from the cumulative mass around its cut (probability
+    units), and max|logit| / temperature (the scale a logit error is divided by)."""
+    u = O.canonical_u(cfg["seed"])
+    T, pen, top_p = cfg["temperature"], cfg["repeat_penalty"], cfg["top_p"]
+    hist = list(history)
+    margins, scales = [], []
+    for s, tok in enumerate(ids):
+        l = logits[s].astype(np.float32).copy()
+        if pen != 1.0:
+            for h in hist:  # once per history entry, repeats included
+                l[h] = l[h] / np.float32(pen) if l[h] >= 0 else l[h] * np.float32(pen)
+        z = np.exp((l.astype(np.float64) - float(l.max())) / T)
+        p = z / z.sum()
+        order = np.arange(len(p))
+        m = np.inf
+        if top_p < 1.0:
+            order = np.argsort(-p, kind="stable")
+            acc = np.cumsum(p[order])
+            keep = int(np.searchsorted(acc, top_p, side="left")) + 1
+            m = min(m, abs(acc[keep - 1] - top_p), abs(acc[keep - 2] - top_p) if keep > 1 else np.inf)
+            order = order[:keep]
+        q = p[order] / p[order].sum()
+        m = min(m, float(np.min(np.abs(np.cumsum(q) - u))))
+        margins.append(float(m))
+        scales.append(float(np.abs(l).max() / T))
+        hist.append(tok)
+    return margins, scales
+
+
+def make_generate() -> None:
+    """Reference generate_ids on text prompts (its own tokenizer, template and EOS stop),
+    with the per-step decision margins of the sampled cases from the reference's logits."""
+    import json
+    exe = O.ref_driver("strict")
+    cases = []
+    for name in sorted(TINY):
+        path = os.path.join(HERE, name + ".gguf")
+        for text in GEN_PROMPTS:
+            for cfg in GEN_CONFIGS:
+                args = [exe, "generate", path, text, "--max-tokens", str(cfg["max_tokens"])]
+                for k, flag in (("temperature", "--temperature"), ("top_k", "--top-k"), ("top_p", "--top-p"),
+                                ("repeat_penalty", "--repeat-penalty"), ("seed", "--seed")):
+                    if k in cfg:
+                        args += [flag, str(cfg[k])]
+                out = subprocess.run(args, check=True, capture_output=True, text=True).stdout.split()
+                case = {"model": name, "prompt": text, **cfg, "ids": [int(v) for v in out]}
+                if "temperature" in cfg:
+                    prompt = _generate_prompt_ids(path, text)
+                    sp = O.params(cfg["temperature"], cfg["top_k"], cfg["top_p"], cfg["repeat_penalty"], cfg["seed"])
+                    dids, logits, _ = O.ref_dump(path, np.array(prompt, dtype=np.uint32), cfg["max_tokens"], sp)
+                    n = len(case["ids"])
+                    assert dids[:n].tolist() == case["ids"], "step loop and generate_ids disagree"
+                    case["margin"], case["scale"] = _sample_margins(logits[len(prompt) - 1:], prompt, cfg,
+                                                                    case["ids"])
+                cases.append(case)
+    with open(os.path.join(HERE, "generate_text.json"), "w") as f:
+        json.dump(cases, f, indent=1)
+    print("generate_text.json:", len(cases), "cases")
+
+
 if __name__ == "__main__":
     if O.ref_driver("strict") is None:
         O.build()
+    if len(sys.argv) > 1 and sys.argv[1] == "generate":
+        make_generate()
+        sys.exit(0)
     make_tiny()
+    make_generate()
     work = tempfile.mkdtemp(prefix="laic_golden_")
     try:
         make_smollm(work)

@@ -3,11 +3,14 @@
 //   host_check MODEL dec ID...       decoded bytes as hex, one line per id
 //   host_check MODEL val TENSOR I... GgufTensor::value, one per line
 //   host_check MODEL meta            vocab, bos, eos, add_bos, tensor count
+//   host_check MODEL gen TEXT MAX [TEMP TOPK TOPP PENALTY SEED]
+//                                    LlamaRuntime::generate_ids on the GPU, one id per line
 #include <cstdio>
 #include <cstdlib>
 #include <string>
 
 #include "laic/gguf.hpp"
+#include "laic/inference.hpp"
 #include "laic/tokenizer.hpp"
 
 int main(int argc, char** argv) {
@@ -18,7 +21,20 @@ int main(int argc, char** argv) {
         laic::Gpt2Tokenizer tok;
         tok.load(m);
         const std::string cmd = argv[2];
-        if (cmd == "enc" && argc > 3) {
+        if (cmd == "gen" && argc > 4) {
+            laic::LlamaRuntime rt;
+            rt.load(argv[1]);
+            laic::GenerationConfig cfg;
+            cfg.max_tokens = size_t(std::atoll(argv[4]));
+            if (argc > 9) {
+                cfg.temperature = float(std::atof(argv[5]));
+                cfg.top_k = size_t(std::atoll(argv[6]));
+                cfg.top_p = float(std::atof(argv[7]));
+                cfg.repeat_penalty = float(std::atof(argv[8]));
+                cfg.seed = uint64_t(std::strtoull(argv[9], nullptr, 10));
+            }
+            for (uint32_t id : rt.generate_ids(argv[3], cfg)) std::printf("%u\n", id);
+        } else if (cmd == "enc" && argc > 3) {
             for (uint32_t id : tok.encode(argv[3])) std::printf("%u\n", id);
         } else if (cmd == "dec") {
             for (int i = 3; i < argc; ++i) {
