@@ -157,9 +157,28 @@ struct MvShape {
 
 constexpr size_t kSmemBudget = 220 * 1024;
 
-MvShape mv_shape(const Mat& m, int B) {
+// Largest batch the team kernel takes; larger batches go to the tile kernel.
+#ifndef LAIC_SK_MAX_BATCH
+#define LAIC_SK_MAX_BATCH 16
+#endif
+// Models with at most this many projection weights per layer run every batch from
+// LAIC_TILE_MIN_BATCH up on the tile kernel with activation records.
+#ifndef LAIC_SMALL_LAYER_WEIGHTS
+#define LAIC_SMALL_LAYER_WEIGHTS 16.0e6
+#endif
+#ifndef LAIC_TILE_MIN_BATCH
+#define LAIC_TILE_MIN_BATCH 1
+#endif
+// In such steps the lm_head stays on the team kernel up to this batch.
+#ifndef LAIC_LM_TEAM_MAX_BATCH
+#define LAIC_LM_TEAM_MAX_BATCH 4
+#endif
+
+// team_ok false: the tile kernel whatever the batch (a step whose projections pass activation
+// records between them).
+MvShape mv_shape(const Mat& m, int B, bool team_ok = true) {
     MvShape sh;
-    if (B <= 16) {
+    if (team_ok && B <= LAIC_SK_MAX_BATCH) {
         const size_t smem = laic::sk_smem_bytes(m.type, m.nb, B);
         if (smem <= kSmemBudget) {
             sh.sk = true;
@@ -226,13 +245,17 @@ struct MvNeed {  // scratch one launch shape needs
 };
 
 MvNeed mv_need(const Mat& m, int B) {
-    const MvShape sh = mv_shape(m, B);
     MvNeed n;
-    n.part_floats = sh.part_floats;
-    n.ntiles = (size_t)m.ntiles;
-    if (!sh.sk) {
-        n.xg_bytes = (size_t)m.nb * B * 128;
-        n.xinv_floats = (size_t)sh.nk * B;
+    for (bool team_ok : {true, false}) {  // either kernel may run this shape
+        const MvShape sh = mv_shape(m, B, team_ok);
+        MvNeed k;
+        k.part_floats = sh.part_floats;
+        k.ntiles = (size_t)m.ntiles;
+        if (!sh.sk) {
+            k.xg_bytes = (size_t)m.nb * B * 128;
+            k.xinv_floats = (size_t)sh.nk * B;
+        }
+        n.merge(k);
     }
     return n;
 }
@@ -298,8 +321,8 @@ struct RecIn {
 // preparation (unless `rin` brings the records) + tile kernel. `launches`
 // counts the kernels enqueued.
 cudaError_t launch_matvec(const Mat& m, laic::MvParams p, int epi, bool kv32, const MvScratch& sc, cudaStream_t st,
-                          bool pdl, int* launches = nullptr, const RecIn* rin = nullptr) {
-    const MvShape sh = mv_shape(m, p.nseq);
+                          bool pdl, int* launches = nullptr, const RecIn* rin = nullptr, bool team_ok = true) {
+    const MvShape sh = mv_shape(m, p.nseq, team_ok);
     p.q = m.q; p.s = m.s; p.rows = m.rows; p.ntiles = m.ntiles; p.in = m.in; p.nb = m.nb;
     if (sh.sk) {
         p.err = sc.err;
@@ -431,6 +454,18 @@ struct laic_dev {
     int last_split = 1;
 
     // ------------------------------------------------------------------
+    // Steps whose projections all run on the tile kernel, passing activation records from
+    // each producing epilogue to the next projection: batches past the team kernel's, and
+    // any batch of a model with small layers (there every launch is latency-bound and the
+    // records save the norm and activation preparation of each projection).
+    bool small_layers() const {
+        const double per_layer = (double)h * (hq + 2.0 * kv) + (double)hq * h + 3.0 * h * F;
+        return per_layer <= LAIC_SMALL_LAYER_WEIGHTS;
+    }
+    bool tile_step(int nseq) const {
+        return tp == 1 && (nseq > LAIC_SK_MAX_BATCH || (small_layers() && nseq >= LAIC_TILE_MIN_BATCH));
+    }
+
     int nsplit_for(int nseq) const {
         const int pairs = nseq * Hkv;
         if (kv32) {
@@ -552,7 +587,8 @@ struct laic_dev {
             if (full) CK(cudaMemcpyAsync(d_params, h_params, nseq * sizeof(laic::SampleDev), cudaMemcpyHostToDevice, s));
         }
 
-        const bool recs = nseq > 16 && tp == 1 && rec_x;  // records travel between the tile-kernel projections
+        const bool step_path = nseq == 1 && step_ready;
+        const bool recs = !step_path && tile_step(nseq) && rec_x;  // records travel between the tile-kernel projections
         const int ntiles_h = (h + 15) / 16;
         laic::EmbedParams ep{embd.type, embd.q, embd.s, h, embd.nb, d_tokens, d_slots, x, counts, V};
         if (recs) { ep.rec_out = rec_x; ep.rec_w = layers[0].attn_norm; ep.ss_out = rec_ss; ep.nseq = nseq; }
@@ -570,7 +606,6 @@ struct laic_dev {
             for (int i = 0; i < nseq; ++i)
                 attn_bytes += (double)(h_pos[h_slots[i]] + 1) * Hkv * D * 2 * kvb + 8.0 * h;
 
-        const bool step_path = nseq == 1 && step_ready;
         if (step_path) {  // every layer in one cooperative launch
             double wb = 0;
             for (auto& ly : layers) wb += ly.qkv.bytes() + ly.o.bytes() + ly.gu.bytes() + ly.down.bytes();
@@ -603,7 +638,7 @@ struct laic_dev {
             t_begin("qkv", (double)ly.qkv.bytes() + 4.0 * nseq * (h + ly.qkv.rows));
             RecIn r_qkv;
             if (recs) { r_qkv.xg = rec_x; r_qkv.mode = 1; r_qkv.ss = rec_ss; r_qkv.ss_tiles = l == 0 ? 1 : ntiles_h; }
-            CK(launch_matvec(ly.qkv, p, laic::EPI_QKV, kv32, mvs, s, pdl, &nl, &r_qkv));
+            CK(launch_matvec(ly.qkv, p, laic::EPI_QKV, kv32, mvs, s, pdl, &nl, &r_qkv, !recs));
             t_end();
             // attention
             laic::AttnParams ap{};
@@ -622,7 +657,7 @@ struct laic_dev {
             RecIn r_o;
             if (recs) { po.rec_out = rec_x; po.rec_w = ly.ffn_norm; po.ss_out = rec_ss; r_o.xg = rec_attn; r_o.mode = 2; }
             t_begin("o", (double)ly.o.bytes() + 4.0 * nseq * hq + 8.0 * nseq * h);
-            CK(launch_matvec(ly.o, po, residual_epi, kv32, mvs, s, pdl, &nl, &r_o));
+            CK(launch_matvec(ly.o, po, residual_epi, kv32, mvs, s, pdl, &nl, &r_o, !recs));
             t_end();
             if (int rc = allreduce_residual(nseq, s, t_begin, t_end, &nl)) return rc;
             // gate/up + swiglu
@@ -631,7 +666,7 @@ struct laic_dev {
             RecIn r_gu;
             if (recs) { r_gu.xg = rec_x; r_gu.mode = 1; r_gu.ss = rec_ss; r_gu.ss_tiles = ntiles_h; pg.rec_out = rec_act; }
             t_begin("gate_up", (double)ly.gu.bytes() + 4.0 * nseq * (h + F));
-            CK(launch_matvec(ly.gu, pg, laic::EPI_SWIGLU, kv32, mvs, s, pdl, &nl, &r_gu));
+            CK(launch_matvec(ly.gu, pg, laic::EPI_SWIGLU, kv32, mvs, s, pdl, &nl, &r_gu, !recs));
             t_end();
             // down + residual
             laic::MvParams pd{};
@@ -643,7 +678,7 @@ struct laic_dev {
                 pd.rec_w = l + 1 < L ? layers[l + 1].attn_norm : out_norm;  // next: QKV, or the lm_head
             }
             t_begin("down", (double)ly.down.bytes() + 4.0 * nseq * (F + 2 * h));
-            CK(launch_matvec(ly.down, pd, residual_epi, kv32, mvs, s, pdl, &nl, &r_dn));
+            CK(launch_matvec(ly.down, pd, residual_epi, kv32, mvs, s, pdl, &nl, &r_dn, !recs));
             t_end();
             if (int rc = allreduce_residual(nseq, s, t_begin, t_end, &nl)) return rc;
         }
@@ -654,7 +689,9 @@ struct laic_dev {
             t_begin("lm_head", (double)lm_head().bytes() + 4.0 * nseq * (h + Vl));
             RecIn r_lm;
             if (recs && L > 0) { r_lm.xg = rec_x; r_lm.mode = 1; r_lm.ss = rec_ss; r_lm.ss_tiles = ntiles_h; }
-            CK(launch_matvec(lm_head(), pl, laic::EPI_STORE, kv32, mvs, s, pdl, &nl, &r_lm));
+            // the lm_head only consumes: the team kernel (its own norm of x) where it is faster
+            CK(launch_matvec(lm_head(), pl, laic::EPI_STORE, kv32, mvs, s, pdl, &nl, &r_lm,
+                             !recs || nseq <= LAIC_LM_TEAM_MAX_BATCH));
             t_end();
             if (tp > 1) {  // every rank's vocabulary rows -> logits [nseq][V] on every rank
                 t_begin("gather", 4.0 * nseq * V);
@@ -1000,7 +1037,7 @@ int laic_dev_create(const laic_dev_desc* desc, const laic_dev_opts* opts, laic_d
     CK(cudaMemset(d->vc, 0, kv_bytes));
     CK(cudaMalloc(&d->pos, S * 4));
     CK(cudaMemset(d->pos, 0, S * 4));
-    if (S > 16) {  // activation records between tile-kernel projections
+    if (d->tile_step(S)) {  // activation records between tile-kernel projections
         CK(cudaMalloc(&d->rec_x, S * d->h * 4));
         CK(cudaMalloc(&d->rec_act, S * d->F * 4));
         CK(cudaMalloc(&d->rec_attn, S * d->hq * 4));

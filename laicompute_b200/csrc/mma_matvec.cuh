@@ -331,8 +331,17 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_mma_kernel(const MvParams p)
         if (p.scale_mode == 0) {
             sc = p.xinvg[(size_t)k_split * B + s];
         } else if (p.scale_mode == 1) {  // rmsnorm over the whole row, from the producer's partial sums
+            // added in tile order; the loads go out 16 at a time (one L2 round trip each)
             float a = 0.f;
-            for (int t = 0; t < p.ss_tiles; ++t) a += __ldcg(p.ss + (size_t)t * B + s);
+            int t = 0;
+            for (; t + 16 <= p.ss_tiles; t += 16) {
+                float v[16];
+#pragma unroll
+                for (int u = 0; u < 16; ++u) v[u] = __ldcg(p.ss + (size_t)(t + u) * B + s);
+#pragma unroll
+                for (int u = 0; u < 16; ++u) a += v[u];
+            }
+            for (; t < p.ss_tiles; ++t) a += __ldcg(p.ss + (size_t)t * B + s);
             sc = 1.f / sqrtf(a / float(p.ss_n) + p.eps);
         }
         xinv[s] = sc;
@@ -447,28 +456,37 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_mma_kernel(const MvParams p)
         // ---- epilogue on fin[16][B]
         const int r0 = t * 16;
         if ((EPI == EPI_ADD || EPI == EPI_SWIGLU) && p.rec_out) {
-            // one thread per sequence: the tile's outputs, their records for the next projection
-            // and (residual) the tile's sum of squares, in a fixed order
-            for (int s = ctid; s < B; s += NC) {
-                float ssum = 0.f;
-                for (int rl = 0; rl < 16; ++rl) {
-                    const int r = r0 + rl;
-                    if (r >= p.rows) break;
-                    const float val = fin[rl * B + s];
-                    if (EPI == EPI_ADD) {
-                        float* o = p.out + (size_t)s * p.ldo + r;
-                        const float xn = *o + val;
-                        *o = xn;
-                        ssum = fmaf(xn, xn, ssum);
-                        store_act_record(p.rec_out, B, r, s, p.rec_w ? xn * p.rec_w[r] : xn);
-                    } else if ((rl & 1) == 0) {
-                        const float up = fin[(rl + 1) * B + s];
-                        const float a = (val / (1.f + expf(-val))) * up;
-                        p.out[(size_t)s * p.ldo + (r >> 1)] = a;
-                        store_act_record(p.rec_out, B, r >> 1, s, a);
+            // the tile's outputs and their records for the next projection, one element per
+            // thread (consecutive threads: consecutive rows of one sequence); then (residual)
+            // the tile's sum of squares per sequence, in row order, from the new values in fin
+            const int rows_here = min(16, p.rows - r0);
+            if (EPI == EPI_ADD) {
+                for (int i = ctid; i < 16 * B; i += NC) {
+                    const int rl = i & 15, s = i >> 4, r = r0 + rl;
+                    if (rl >= rows_here) continue;
+                    float* o = p.out + (size_t)s * p.ldo + r;
+                    const float xn = *o + fin[rl * B + s];
+                    *o = xn;
+                    fin[rl * B + s] = xn;
+                    store_act_record(p.rec_out, B, r, s, p.rec_w ? xn * p.rec_w[r] : xn);
+                }
+                if (p.ss_out) {
+                    named_sync(1, NC);
+                    for (int s = ctid; s < B; s += NC) {
+                        float ssum = 0.f;
+                        for (int rl = 0; rl < rows_here; ++rl) ssum = fmaf(fin[rl * B + s], fin[rl * B + s], ssum);
+                        p.ss_out[(size_t)t * B + s] = ssum;
                     }
                 }
-                if (EPI == EPI_ADD && p.ss_out) p.ss_out[(size_t)t * B + s] = ssum;
+            } else {
+                for (int i = ctid; i < 8 * B; i += NC) {
+                    const int rp = i & 7, s = i >> 3, rl = 2 * rp, r = r0 + rl;
+                    if (rl >= rows_here) continue;
+                    const float val = fin[rl * B + s], up = fin[(rl + 1) * B + s];
+                    const float a = (val / (1.f + expf(-val))) * up;
+                    p.out[(size_t)s * p.ldo + (r >> 1)] = a;
+                    store_act_record(p.rec_out, B, r >> 1, s, a);
+                }
             }
             named_sync(1, NC);  // fin/red reused by the next tile
             continue;

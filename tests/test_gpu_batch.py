@@ -83,3 +83,32 @@ def test_per_sequence_sampling_params():
         a.append(int(tok[0])); b.append(int(tok[1]))
     assert np.array_equal(np.array(a, dtype=np.uint32), g["ids_greedy"])
     assert np.array_equal(np.array(b, dtype=np.uint32), g["ids_full"])
+
+
+@pytest.mark.parametrize("nseq", [1, 4, 17])
+def test_large_layer_model_matches_oracle(nseq):
+    """A model whose layers are above the small-layer bound: batches up to 16 run the
+    team kernel (one sequence: its integer dot products), larger ones the tile kernel
+    with activation records; logits within 1e-3 of max|logit|, greedy ids identical."""
+    from laicompute_b200 import gguf, synth
+    a = synth.tiny_arch(gguf.Q4_0, None, layers=2, vocab=512, ctx=64, name="big", hidden=1024, heads=8, kv_heads=2,
+                        ffn=5120)
+    with tempfile.TemporaryDirectory() as d:
+        path = synth.write_model(os.path.join(d, "m.gguf"), a, seed=71)
+        m = O.OracleModel(path)
+        rng = np.random.default_rng(72 + nseq)
+        prompts = rng.integers(0, m.vocab, size=(nseq, 4)).astype(np.uint32)
+        steps = 6
+        ref = [m.generate(p, steps) for p in prompts]
+        e = _engine(path, max_seqs=nseq)
+        slots = np.arange(nseq, dtype=np.int32)
+        for j in range(prompts.shape[1] - 1):
+            e.prefill(prompts[:, j], slots)
+        tok = prompts[:, -1].copy()
+        for k in range(steps):
+            tok, lg = e.step(tok, slots, want_logits=True)
+            for i in range(nseq):
+                r = ref[i][1][k]
+                assert np.abs(lg[i] - r).max() <= 1e-3 * np.abs(r).max(), (i, k)
+                assert int(tok[i]) == int(ref[i][0][k]), (i, k)
+        e.close()
