@@ -151,6 +151,7 @@ int num_sms() {
 struct MvShape {
     bool sk = false;  // team kernel (small batches whose activations fit in shared memory)
     int nt = 1, nk = 1, kr = 1, kb = 1, stages = 2, grid = 1;
+    int groups = 1, sgrp = 1;  // tile kernel: sequence groups (grid.y) of sgrp sequences
     size_t smem = 0;
     size_t part_floats = 0;  // split-K scratch it needs
 };
@@ -190,33 +191,44 @@ MvShape mv_shape(const Mat& m, int B, bool team_ok = true) {
             return sh;
         }
     }
-    sh.nt = B <= 8 ? 1 : B <= 16 ? 2 : B <= 32 ? 4 : 8;
     sh.kb = m.type == T_F16 ? 16 : 32;
     const size_t sbytes = m.type == T_F16 ? 0 : laic::kTileSBytes;
     const size_t stage_bytes = (size_t)sh.kb * (laic::tile_qbytes(m.type) + sbytes);
-    const size_t fixed = (size_t)laic::kConsumerWarps * 16 * sh.nt * 8 * 4 + 16 * (size_t)B * 4 + sh.nt * 8 * 8 + 1024;
     const int G = num_sms();
     // rough microseconds: a consumer warp's tile-block (mma count grows with the n-tiles), a tile's
-    // reduction and epilogue, and the split-K merge (partials to L2, fence, ticket, second pass)
-    const double t_blk = 0.05 + 0.025 * sh.nt, t_tile = 1.0, t_merge = 4.0;
+    // reduction and epilogue, the CTA's activation copy (~150 KB/us per SM from L2), and the
+    // split-K merge (partials to L2, fence, ticket, second pass)
+    const double t_tile = 1.0, t_merge = 4.0, x_kb_per_us = 150.0;
     double best = 1e30;
-    for (int nk = 1; nk <= std::min(m.nb, 64); ++nk) {
-        const int kr = (m.nb + nk - 1) / nk;
-        if ((m.nb + kr - 1) / kr != nk) continue;  // no empty split
-        const size_t xs = (size_t)kr * B * 128;
-        if (fixed + xs + 2 * stage_bytes > kSmemBudget) continue;
-        const int cta_per_k = G / nk;
-        if (cta_per_k < 1) break;
-        const int tiles_per = (m.ntiles + cta_per_k - 1) / cta_per_k;
-        const int blk_rounds = (kr + laic::kConsumerWarps - 1) / laic::kConsumerWarps;
-        const double cost = (double)tiles_per * (blk_rounds * t_blk + t_tile) + (nk > 1 ? t_merge : 0.0);
-        if (cost < best - 1e-9) {
-            best = cost;
-            sh.nk = nk;
-            sh.kr = kr;
-            sh.stages = (int)std::min<size_t>(8, (kSmemBudget - fixed - xs) / stage_bytes);
-            sh.grid = nk * std::min(cta_per_k, m.ntiles);
-            sh.smem = fixed + xs + sh.stages * stage_bytes;
+    const int b8 = (B + 7) / 8 * 8;
+    for (int sgrp : {b8, 32, 16, 8}) {  // sequences per group (whole n-tiles); groups = grid.y
+        if (sgrp != b8 && sgrp >= b8) continue;  // smaller groups only
+        const int groups = (B + sgrp - 1) / sgrp;
+        const int nt = sgrp <= 8 ? 1 : sgrp <= 16 ? 2 : sgrp <= 32 ? 4 : 8;
+        const double t_blk = 0.05 + 0.025 * nt;
+        const size_t fixed = (size_t)laic::kConsumerWarps * 16 * nt * 8 * 4 + 16 * (size_t)sgrp * 4 + nt * 8 * 8 + 1024;
+        for (int nk = 1; nk <= std::min(m.nb, 64); ++nk) {
+            const int kr = (m.nb + nk - 1) / nk;
+            if ((m.nb + kr - 1) / kr != nk) continue;  // no empty split
+            const size_t xs = (size_t)kr * sgrp * 128;
+            if (fixed + xs + 2 * stage_bytes > kSmemBudget) continue;
+            const int cta_per_k = G / (nk * groups);
+            if (cta_per_k < 1) break;
+            const int tiles_per = (m.ntiles + cta_per_k - 1) / cta_per_k;
+            const int blk_rounds = (kr + laic::kConsumerWarps - 1) / laic::kConsumerWarps;
+            const double cost = (double)tiles_per * (blk_rounds * t_blk + t_tile) + xs / 1024.0 / x_kb_per_us +
+                                (nk > 1 ? t_merge : 0.0);
+            if (cost < best - 1e-9) {
+                best = cost;
+                sh.nt = nt;
+                sh.groups = groups;
+                sh.sgrp = sgrp;
+                sh.nk = nk;
+                sh.kr = kr;
+                sh.stages = (int)std::min<size_t>(8, (kSmemBudget - fixed - xs) / stage_bytes);
+                sh.grid = nk * std::min(cta_per_k, m.ntiles);
+                sh.smem = fixed + xs + sh.stages * stage_bytes;
+            }
         }
     }
     sh.part_floats = sh.nk > 1 ? (size_t)m.ntiles * sh.nk * 16 * B : 0;
@@ -250,7 +262,7 @@ MvNeed mv_need(const Mat& m, int B) {
         const MvShape sh = mv_shape(m, B, team_ok);
         MvNeed k;
         k.part_floats = sh.part_floats;
-        k.ntiles = (size_t)m.ntiles;
+        k.ntiles = (size_t)m.ntiles * sh.groups;  // tickets per (row tile, group)
         if (!sh.sk) {
             k.xg_bytes = (size_t)m.nb * B * 128;
             k.xinv_floats = (size_t)sh.nk * B;
@@ -329,7 +341,7 @@ cudaError_t launch_matvec(const Mat& m, laic::MvParams p, int epi, bool kv32, co
         if (launches) *launches += 1;
         return laic::mv_sk_launch(m.type, sh.nt, epi, kv32, p, sh.grid, sh.smem, st, pdl);
     }
-    p.nk = sh.nk; p.kr = sh.kr; p.kb = sh.kb; p.stages = sh.stages;
+    p.nk = sh.nk; p.kr = sh.kr; p.kb = sh.kb; p.stages = sh.stages; p.sgrp = sh.sgrp;
     p.part = sc.part; p.tile_cnt = sc.tile_cnt; p.err = sc.err;
     if (rin && rin->xg) {
         p.xg = rin->xg; p.scale_mode = rin->mode; p.ss = rin->ss; p.ss_tiles = rin->ss_tiles; p.ss_n = m.in;
@@ -341,7 +353,7 @@ cudaError_t launch_matvec(const Mat& m, laic::MvParams p, int epi, bool kv32, co
         if (launches) *launches += 1;
     }
     if (launches) *launches += 1;
-    return laic::mv_launch(m.type, sh.nt, epi, kv32, p, sh.grid, sh.smem, st, pdl);
+    return laic::mv_launch(m.type, sh.nt, epi, kv32, p, sh.grid, sh.groups, sh.smem, st, pdl);
 }
 
 using AttnFn = void (*)(laic::AttnParams);

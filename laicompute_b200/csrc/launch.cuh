@@ -29,8 +29,8 @@ struct XPrepParams;
 // Launch the activation preparation of the tile kernel: grid (nk, nseq).
 cudaError_t xprep_launch(const XPrepParams& p, int nk, cudaStream_t st, bool pdl);
 // Launch the fragment-tile matvec for one weight type (defined in mv_<type>.cu).
-cudaError_t mv_launch(int type, int nt, int epi, bool kv32, const MvParams& p, int grid, size_t smem, cudaStream_t st,
-                      bool pdl);
+cudaError_t mv_launch(int type, int nt, int epi, bool kv32, const MvParams& p, int grid, int groups, size_t smem,
+                      cudaStream_t st, bool pdl);
 // Launch the team matvec (defined in mv_<type>.cu), nt = 1, 2 or 4; nt = 0 is the one-sequence integer variant.
 cudaError_t mv_sk_launch(int type, int nt, int epi, bool kv32, const MvParams& p, int grid, size_t smem,
                          cudaStream_t st, bool pdl);

@@ -49,8 +49,9 @@ struct MvParams {
     const float* norm_w;       // rmsnorm weight [in] (nullptr: no norm)
     float eps;
     int nk, kr, kb, stages;    // K splits, blocks per split, blocks per ring stage, ring depth
+    int sgrp;                  // tile kernel: sequences per CTA group (grid.y = groups)
     float* part;               // split-K partials [ntiles][nk][16][nseq] (scratch)
-    unsigned* tile_cnt;        // [ntiles] tickets, zero between launches (scratch)
+    unsigned* tile_cnt;        // [ntiles][groups] tickets, zero between launches (scratch)
     int* err;                  // set when a bounded wait runs out
     float* out;                // epilogue output
     int ldo;
@@ -249,14 +250,16 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_mma_kernel(const MvParams p)
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, c = lane & 3;
-    const int B = p.nseq;
+    const int B = p.nseq;                   // all sequences (the global layouts)
+    const int s0 = blockIdx.y * p.sgrp;     // this CTA's sequence group: s0 .. s0 + Bl - 1
+    const int Bl = min(p.sgrp, B - s0);
     const int stage_bytes = p.kb * (QB + SB);
 
     uint8_t* ring = smem;
-    uint8_t* xs = ring + p.stages * stage_bytes;                       // [kr][B][4][32 B]
-    float* red = reinterpret_cast<float*>(xs + (size_t)p.kr * B * 128);  // [8 warps][16][NT*8]
-    float* fin = red + kConsumerWarps * 16 * NT * 8;                  // [16][B]
-    float* xinv = fin + 16 * B;                                       // [B] 1/scale of each sequence
+    uint8_t* xs = ring + p.stages * stage_bytes;                            // [kr][sgrp][4][32 B]
+    float* red = reinterpret_cast<float*>(xs + (size_t)p.kr * p.sgrp * 128);  // [8 warps][16][NT*8]
+    float* fin = red + kConsumerWarps * 16 * NT * 8;                       // [16][Bl]
+    float* xinv = fin + 16 * p.sgrp;                                       // [Bl] 1/scale of each sequence
     uint64_t* full = reinterpret_cast<uint64_t*>(xinv + NT * 8 + 2);  // 8-byte aligned
     uint64_t* empty = full + p.stages;
     uint64_t* xbar = empty + p.stages;                                // the activation copy
@@ -286,9 +289,14 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_mma_kernel(const MvParams p)
             bool x_issued = false;
             auto issue_x = [&]() {
                 pdl_wait();
-                const uint32_t xb = (uint32_t)nblk * B * 128;
-                mbar_expect_tx(xbar, xb);
-                bulk_g2s(xs, p.xg + (size_t)b_lo * B * 128, xb, xbar);
+                mbar_expect_tx(xbar, (uint32_t)nblk * Bl * 128);
+                if (Bl == B) {  // one group: the split's records are contiguous
+                    bulk_g2s(xs, p.xg + (size_t)b_lo * B * 128, (uint32_t)nblk * B * 128, xbar);
+                } else {        // this group's slice of every block
+                    for (int bl = 0; bl < nblk; ++bl)
+                        bulk_g2s(xs + (size_t)bl * Bl * 128, p.xg + ((size_t)(b_lo + bl) * B + s0) * 128,
+                                 (uint32_t)Bl * 128, xbar);
+                }
                 x_issued = true;
             };
             int it = 0;
@@ -326,7 +334,8 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_mma_kernel(const MvParams p)
     // activations of this K split: the producer's bulk copy of the prepared
     // records, plus the split's scale per sequence
     bool aborted = nblk > 0 && !mbar_wait(xbar, 0u, p.err);
-    for (int s = ctid; s < B; s += NC) {
+    for (int sl = ctid; sl < Bl; sl += NC) {
+        const int s = s0 + sl;
         float sc = 1.f;
         if (p.scale_mode == 0) {
             sc = p.xinvg[(size_t)k_split * B + s];
@@ -344,7 +353,7 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_mma_kernel(const MvParams p)
             for (; t < p.ss_tiles; ++t) a += __ldcg(p.ss + (size_t)t * B + s);
             sc = 1.f / sqrtf(a / float(p.ss_n) + p.eps);
         }
-        xinv[s] = sc;
+        xinv[sl] = sc;
     }
     named_sync(1, NC);
     pdl_launch_dependents();
@@ -388,8 +397,8 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_mma_kernel(const MvParams p)
                 for (int j = 0; j < NT; ++j) {
                     const int s = j * 8 + g;
                     uint4 xh = make_uint4(0, 0, 0, 0), xl = make_uint4(0, 0, 0, 0);
-                    if (s < B) {
-                        const uint4* xp = reinterpret_cast<const uint4*>(xs + ((size_t)(bl * B + s) * 4 + c) * 32);
+                    if (s < Bl) {
+                        const uint4* xp = reinterpret_cast<const uint4*>(xs + ((size_t)(bl * Bl + s) * 4 + c) * 32);
                         xh = xp[0];
                         xl = xp[1];
                     }
@@ -425,31 +434,34 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_mma_kernel(const MvParams p)
             rw[(g + 8) * NT * 8 + j * 8 + 2 * c + 1] = acc[j][3];
         }
         named_sync(1, NC);
-        for (int i = ctid; i < 16 * B; i += NC) {
-            const int r = i / B, s = i % B;
+        for (int i = ctid; i < 16 * Bl; i += NC) {
+            const int r = i / Bl, s = i % Bl;
             float v = 0.f;
 #pragma unroll
             for (int w = 0; w < kConsumerWarps; ++w) v += red[w * 16 * NT * 8 + r * NT * 8 + s];
-            fin[r * B + s] = v * xinv[s];
+            fin[r * Bl + s] = v * xinv[s];
         }
         named_sync(1, NC);
 
-        // ---- split-K: the last CTA of this row tile adds the partials in split order
+        // ---- split-K: the last CTA of this (row tile, group) adds the partials in split order
         if (p.nk > 1) {
-            float* pt = p.part + (size_t)t * p.nk * 16 * B;
-            for (int i = ctid; i < 16 * B; i += NC) pt[(size_t)k_split * 16 * B + i] = fin[i];
+            float* pt = p.part + (size_t)t * p.nk * 16 * B;  // [nk][16][B]
+            for (int i = ctid; i < 16 * Bl; i += NC)
+                pt[(size_t)k_split * 16 * B + (i / Bl) * B + s0 + i % Bl] = fin[i];
             __threadfence();
             named_sync(1, NC);
-            if (ctid == 0) *ticket = (int)atomicAdd(p.tile_cnt + t, 1u) == p.nk - 1;
+            unsigned* cnt = p.tile_cnt + (size_t)t * gridDim.y + blockIdx.y;
+            if (ctid == 0) *ticket = (int)atomicAdd(cnt, 1u) == p.nk - 1;
             named_sync(1, NC);
             if (!*ticket) continue;
             __threadfence();
-            for (int i = ctid; i < 16 * B; i += NC) {
+            for (int i = ctid; i < 16 * Bl; i += NC) {
+                const size_t gi = (size_t)(i / Bl) * B + s0 + i % Bl;
                 float v = 0.f;
-                for (int k = 0; k < p.nk; ++k) v += __ldcg(pt + (size_t)k * 16 * B + i);
+                for (int k = 0; k < p.nk; ++k) v += __ldcg(pt + (size_t)k * 16 * B + gi);
                 fin[i] = v;
             }
-            if (ctid == 0) p.tile_cnt[t] = 0u;
+            if (ctid == 0) *cnt = 0u;
             named_sync(1, NC);
         }
 
@@ -461,38 +473,38 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_mma_kernel(const MvParams p)
             // the tile's sum of squares per sequence, in row order, from the new values in fin
             const int rows_here = min(16, p.rows - r0);
             if (EPI == EPI_ADD) {
-                for (int i = ctid; i < 16 * B; i += NC) {
+                for (int i = ctid; i < 16 * Bl; i += NC) {
                     const int rl = i & 15, s = i >> 4, r = r0 + rl;
                     if (rl >= rows_here) continue;
-                    float* o = p.out + (size_t)s * p.ldo + r;
-                    const float xn = *o + fin[rl * B + s];
+                    float* o = p.out + (size_t)(s0 + s) * p.ldo + r;
+                    const float xn = *o + fin[rl * Bl + s];
                     *o = xn;
-                    fin[rl * B + s] = xn;
-                    store_act_record(p.rec_out, B, r, s, p.rec_w ? xn * p.rec_w[r] : xn);
+                    fin[rl * Bl + s] = xn;
+                    store_act_record(p.rec_out, B, r, s0 + s, p.rec_w ? xn * p.rec_w[r] : xn);
                 }
                 if (p.ss_out) {
                     named_sync(1, NC);
-                    for (int s = ctid; s < B; s += NC) {
+                    for (int s = ctid; s < Bl; s += NC) {
                         float ssum = 0.f;
-                        for (int rl = 0; rl < rows_here; ++rl) ssum = fmaf(fin[rl * B + s], fin[rl * B + s], ssum);
-                        p.ss_out[(size_t)t * B + s] = ssum;
+                        for (int rl = 0; rl < rows_here; ++rl) ssum = fmaf(fin[rl * Bl + s], fin[rl * Bl + s], ssum);
+                        p.ss_out[(size_t)t * B + s0 + s] = ssum;
                     }
                 }
             } else {
-                for (int i = ctid; i < 8 * B; i += NC) {
+                for (int i = ctid; i < 8 * Bl; i += NC) {
                     const int rp = i & 7, s = i >> 3, rl = 2 * rp, r = r0 + rl;
                     if (rl >= rows_here) continue;
-                    const float val = fin[rl * B + s], up = fin[(rl + 1) * B + s];
+                    const float val = fin[rl * Bl + s], up = fin[(rl + 1) * Bl + s];
                     const float a = (val / (1.f + expf(-val))) * up;
-                    p.out[(size_t)s * p.ldo + (r >> 1)] = a;
-                    store_act_record(p.rec_out, B, r >> 1, s, a);
+                    p.out[(size_t)(s0 + s) * p.ldo + (r >> 1)] = a;
+                    store_act_record(p.rec_out, B, r >> 1, s0 + s, a);
                 }
             }
             named_sync(1, NC);  // fin/red reused by the next tile
             continue;
         }
-        for (int i = ctid; i < 16 * B; i += NC) {
-            const int rl = i / B, s = i % B, r = r0 + rl;
+        for (int i = ctid; i < 16 * Bl; i += NC) {
+            const int rl = i / Bl, sl = i % Bl, r = r0 + rl, s = s0 + sl;
             if (r >= p.rows) continue;
             const float val = fin[i];
             if (EPI == EPI_STORE) {
@@ -502,7 +514,7 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_mma_kernel(const MvParams p)
             } else if (EPI == EPI_SWIGLU) {
                 // row 2o = gate o, row 2o+1 = up o: out[o] = silu(gate) * up
                 if ((rl & 1) == 0) {
-                    const float up = fin[(rl + 1) * B + s];
+                    const float up = fin[(rl + 1) * Bl + sl];
                     p.out[(size_t)s * p.ldo + (r >> 1)] = (val / (1.f + expf(-val))) * up;
                 }
             } else {  // EPI_QKV
@@ -513,7 +525,7 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_mma_kernel(const MvParams p)
                 float o = val;
                 if (region < 2 && d < 2 * p.rope_pairs) {
                     const float2 cs = p.rope_cs[(size_t)ps * p.rope_pairs + (d >> 1)];
-                    const float other = fin[(rl ^ 1) * B + s];
+                    const float other = fin[(rl ^ 1) * Bl + sl];
                     // adjacent-pair rotation, unfused to keep the reference's rounding
                     if ((d & 1) == 0) o = __fsub_rn(__fmul_rn(val, cs.x), __fmul_rn(other, cs.y));
                     else o = __fadd_rn(__fmul_rn(other, cs.y), __fmul_rn(val, cs.x));

@@ -29,9 +29,9 @@ static void (*mv_kernel(int type, int nt, int epi, bool kv32))(MvParams) {
     return mv_kernel_f16(nt, epi, kv32);
 }
 
-cudaError_t mv_launch(int type, int nt, int epi, bool kv32, const MvParams& p, int grid, size_t smem, cudaStream_t st,
-                      bool pdl) {
-    return launch_k(mv_kernel(type, nt, epi, kv32), dim3(grid), dim3(kMvThreads), smem, st, pdl, p);
+cudaError_t mv_launch(int type, int nt, int epi, bool kv32, const MvParams& p, int grid, int groups, size_t smem,
+                      cudaStream_t st, bool pdl) {
+    return launch_k(mv_kernel(type, nt, epi, kv32), dim3(grid, groups), dim3(kMvThreads), smem, st, pdl, p);
 }
 
 cudaError_t xprep_launch(const XPrepParams& p, int nk, cudaStream_t st, bool pdl) {
