@@ -152,6 +152,7 @@ struct MvShape {
     bool sk = false;  // team kernel (small batches whose activations fit in shared memory)
     int nt = 1, nk = 1, kr = 1, kb = 1, stages = 2, grid = 1;
     int groups = 1, sgrp = 1;  // tile kernel: sequence groups (grid.y) of sgrp sequences
+    bool wide = false;         // the wide kernel (EPI_STORE, warps own whole row tiles)
     size_t smem = 0;
     size_t part_floats = 0;  // split-K scratch it needs
 };
@@ -177,7 +178,8 @@ constexpr size_t kSmemBudget = 220 * 1024;
 
 // team_ok false: the tile kernel whatever the batch (a step whose projections pass activation
 // records between them).
-MvShape mv_shape(const Mat& m, int B, bool team_ok = true) {
+// store: an EPI_STORE launch, which may take the wide kernel.
+MvShape mv_shape(const Mat& m, int B, bool team_ok = true, bool store = false) {
     MvShape sh;
     if (team_ok && B <= LAIC_SK_MAX_BATCH) {
         const size_t smem = laic::sk_smem_bytes(m.type, m.nb, B);
@@ -191,16 +193,39 @@ MvShape mv_shape(const Mat& m, int B, bool team_ok = true) {
             return sh;
         }
     }
+    const int G = num_sms();
+    const int b8 = (B + 7) / 8 * 8;
+    if (store) {
+        // many row tiles: the wide kernel, with two ring stages per warp where they fit, then one;
+        // the largest sequence group that fits (each group streams the matrix once more from L2)
+        for (int S : {16, 8})
+            for (int sgrp : {b8, 32, 16, 8}) {
+                if (sgrp != b8 && sgrp >= b8) continue;
+                const size_t smem = laic::mv_wide_smem(m.type, m.nb, sgrp, S);
+                if (smem > kSmemBudget) continue;
+                const int groups = (B + sgrp - 1) / sgrp;
+                const int cta = G / groups;
+                if (cta < 1 || m.ntiles < 16 * cta) continue;  // at least two tiles per warp
+                sh.wide = true;
+                sh.nt = sgrp <= 8 ? 1 : sgrp <= 16 ? 2 : sgrp <= 32 ? 4 : 8;
+                sh.sgrp = sgrp;
+                sh.groups = groups;
+                sh.grid = cta;
+                sh.stages = S;
+                sh.nk = 1;
+                sh.kr = m.nb;
+                sh.smem = smem;
+                return sh;
+            }
+    }
     sh.kb = m.type == T_F16 ? 16 : 32;
     const size_t sbytes = m.type == T_F16 ? 0 : laic::kTileSBytes;
     const size_t stage_bytes = (size_t)sh.kb * (laic::tile_qbytes(m.type) + sbytes);
-    const int G = num_sms();
     // rough microseconds: a consumer warp's tile-block (mma count grows with the n-tiles), a tile's
     // reduction and epilogue, the CTA's activation copy (~150 KB/us per SM from L2), and the
     // split-K merge (partials to L2, fence, ticket, second pass)
     const double t_tile = 1.0, t_merge = 4.0, x_kb_per_us = 150.0;
     double best = 1e30;
-    const int b8 = (B + 7) / 8 * 8;
     for (int sgrp : {b8, 32, 16, 8}) {  // sequences per group (whole n-tiles); groups = grid.y
         if (sgrp != b8 && sgrp >= b8) continue;  // smaller groups only
         const int groups = (B + sgrp - 1) / sgrp;
@@ -258,8 +283,8 @@ struct MvNeed {  // scratch one launch shape needs
 
 MvNeed mv_need(const Mat& m, int B) {
     MvNeed n;
-    for (bool team_ok : {true, false}) {  // either kernel may run this shape
-        const MvShape sh = mv_shape(m, B, team_ok);
+    for (int v = 0; v < 4; ++v) {  // team or tile, store or not: whichever kernel may run this shape
+        const MvShape sh = mv_shape(m, B, v & 1, v & 2);
         MvNeed k;
         k.part_floats = sh.part_floats;
         k.ntiles = (size_t)m.ntiles * sh.groups;  // tickets per (row tile, group)
@@ -334,7 +359,7 @@ struct RecIn {
 // counts the kernels enqueued.
 cudaError_t launch_matvec(const Mat& m, laic::MvParams p, int epi, bool kv32, const MvScratch& sc, cudaStream_t st,
                           bool pdl, int* launches = nullptr, const RecIn* rin = nullptr, bool team_ok = true) {
-    const MvShape sh = mv_shape(m, p.nseq, team_ok);
+    const MvShape sh = mv_shape(m, p.nseq, team_ok, epi == laic::EPI_STORE);
     p.q = m.q; p.s = m.s; p.rows = m.rows; p.ntiles = m.ntiles; p.in = m.in; p.nb = m.nb;
     if (sh.sk) {
         p.err = sc.err;
@@ -353,6 +378,7 @@ cudaError_t launch_matvec(const Mat& m, laic::MvParams p, int epi, bool kv32, co
         if (launches) *launches += 1;
     }
     if (launches) *launches += 1;
+    if (sh.wide) return laic::mv_wide_launch(m.type, sh.nt, p, sh.grid, sh.groups, sh.smem, st, pdl);
     return laic::mv_launch(m.type, sh.nt, epi, kv32, p, sh.grid, sh.groups, sh.smem, st, pdl);
 }
 

@@ -31,6 +31,9 @@ cudaError_t xprep_launch(const XPrepParams& p, int nk, cudaStream_t st, bool pdl
 // Launch the fragment-tile matvec for one weight type (defined in mv_<type>.cu).
 cudaError_t mv_launch(int type, int nt, int epi, bool kv32, const MvParams& p, int grid, int groups, size_t smem,
                       cudaStream_t st, bool pdl);
+// Launch the wide matvec (EPI_STORE; each warp owns whole row tiles), grid (grid, groups).
+cudaError_t mv_wide_launch(int type, int nt, const MvParams& p, int grid, int groups, size_t smem, cudaStream_t st,
+                           bool pdl);
 // Launch the team matvec (defined in mv_<type>.cu), nt = 1, 2 or 4; nt = 0 is the one-sequence integer variant.
 cudaError_t mv_sk_launch(int type, int nt, int epi, bool kv32, const MvParams& p, int grid, size_t smem,
                          cudaStream_t st, bool pdl);

@@ -544,6 +544,186 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_mma_kernel(const MvParams p)
 }
 
 // ---------------------------------------------------------------------------
+// the wide kernel: y = W x with EPI_STORE for matrices of many row tiles and a
+// short K (the lm_head of a small model). Each consumer warp owns whole row
+// tiles -- all K blocks of a tile in one ring stage, no cross-warp reduction
+// and no CTA barrier per tile -- so the warps stream independently. Stage i of
+// the ring belongs to warp i % 8 (stages: a multiple of 8); the producer fills
+// the stages in tile order. Grid (CTAs, sequence groups) like the tile kernel;
+// tiles t = blockIdx.x + i * gridDim.x. Shared memory:
+//   ring [stages][nb * (QB + SB)] | xs [nb][sgrp][4][32 B] | xinv [sgrp] | barriers
+// ---------------------------------------------------------------------------
+__host__ __device__ constexpr size_t mv_wide_smem(int type, int nb, int sgrp, int stages) {
+    return (size_t)stages * nb * (tile_qbytes(type) + (type == T_F16 ? 0 : kTileSBytes)) + (size_t)nb * sgrp * 128 +
+           (size_t)sgrp * 4 + 16 + (size_t)(2 * stages + 1) * 8;
+}
+
+template <int WT, int NT>
+__global__ void __launch_bounds__(kMvThreads, 1) mv_wide_kernel(const MvParams p) {
+    constexpr int QB = tile_qbytes(WT);
+    constexpr int SB = WT == T_F16 ? 0 : kTileSBytes;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, c = lane & 3;
+    const int B = p.nseq;
+    const int s0 = blockIdx.y * p.sgrp;
+    const int Bl = min(p.sgrp, B - s0);
+    const int nb = p.nb;
+    const int tile_bytes = nb * (QB + SB);
+    const int S = p.stages;
+
+    uint8_t* ring = smem;
+    uint8_t* xs = ring + (size_t)S * tile_bytes;                        // [nb][Bl][4][32 B]
+    float* xinv = reinterpret_cast<float*>(xs + (size_t)nb * p.sgrp * 128);
+    uint64_t* full = reinterpret_cast<uint64_t*>(
+        (reinterpret_cast<uintptr_t>(xinv + p.sgrp) + 15) & ~uintptr_t(15));
+    uint64_t* empty = full + S;
+    uint64_t* xbar = empty + S;
+
+    const int n_local = blockIdx.x < p.ntiles ? (p.ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; ++i) { mbar_init(full + i, 1); mbar_init(empty + i, 1); }
+        mbar_init(xbar, 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+
+    if (warp == kConsumerWarps) {
+        // ---------------- producer ----------------
+        if (lane == 0 && n_local > 0) {
+            bool x_issued = false;
+            auto issue_x = [&]() {
+                pdl_wait();
+                mbar_expect_tx(xbar, (uint32_t)nb * Bl * 128);
+                if (Bl == B) {
+                    bulk_g2s(xs, p.xg, (uint32_t)nb * B * 128, xbar);
+                } else {
+                    for (int bl = 0; bl < nb; ++bl)
+                        bulk_g2s(xs + (size_t)bl * Bl * 128, p.xg + ((size_t)bl * B + s0) * 128, (uint32_t)Bl * 128,
+                                 xbar);
+                }
+                x_issued = true;
+            };
+            int i = 0;
+            for (; i < n_local; ++i) {
+                const int slot = i % S;
+                if (!x_issued && i >= S) issue_x();
+                if (!mbar_wait(empty + slot, ((uint32_t)(i / S) & 1u) ^ 1u, p.err)) break;
+                const size_t t = (size_t)blockIdx.x + (size_t)i * gridDim.x;
+                uint8_t* dst = ring + (size_t)slot * tile_bytes;
+                mbar_expect_tx(full + slot, (uint32_t)tile_bytes);
+                bulk_g2s(dst, p.q + t * nb * QB, (uint32_t)(nb * QB), full + slot);
+                if (SB) bulk_g2s(dst + nb * QB, p.s + t * nb * SB, (uint32_t)(nb * SB), full + slot);
+            }
+            if (!x_issued) issue_x();
+            for (int j = max(0, i - S); j < i; ++j) mbar_wait(full + (j % S), (uint32_t)(j / S) & 1u, p.err);
+            mbar_wait(xbar, 0u, p.err);
+        }
+        return;
+    }
+
+    // ---------------- consumers ----------------
+    const int ctid = threadIdx.x;
+    constexpr int NC = kConsumerWarps * 32;
+    pdl_wait();
+    bool aborted = n_local > 0 && !mbar_wait(xbar, 0u, p.err);
+    for (int sl = ctid; sl < Bl; sl += NC) {
+        const int s = s0 + sl;
+        float sc = 1.f;
+        if (p.scale_mode == 0) {
+            sc = p.xinvg[s];
+        } else if (p.scale_mode == 1) {
+            float a = 0.f;
+            int t = 0;
+            for (; t + 16 <= p.ss_tiles; t += 16) {
+                float v[16];
+#pragma unroll
+                for (int u = 0; u < 16; ++u) v[u] = __ldcg(p.ss + (size_t)(t + u) * B + s);
+#pragma unroll
+                for (int u = 0; u < 16; ++u) a += v[u];
+            }
+            for (; t < p.ss_tiles; ++t) a += __ldcg(p.ss + (size_t)t * B + s);
+            sc = 1.f / sqrtf(a / float(p.ss_n) + p.eps);
+        }
+        xinv[sl] = sc;
+    }
+    named_sync(1, NC);
+    pdl_launch_dependents();
+
+    for (int i = warp; i < n_local; i += kConsumerWarps) {
+        const int slot = i % S;
+        if (!aborted && !mbar_wait(full + slot, (uint32_t)(i / S) & 1u, p.err)) aborted = true;
+        float acc[NT][4];
+#pragma unroll
+        for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+        const uint8_t* sq = ring + (size_t)slot * tile_bytes;
+        const uint8_t* ss = sq + nb * QB;
+        for (int bl = 0; bl < (aborted ? 0 : nb); ++bl) {
+            uint32_t ra[4], rb[4];
+            if (WT == T_Q4_0) {
+                const uint2 w = *reinterpret_cast<const uint2*>(sq + bl * QB + lane * 8);
+                decode_q4(w.x, ra);
+                decode_q4(w.y, rb);
+            } else if (WT == T_Q8_0) {
+                const uint4 w = *reinterpret_cast<const uint4*>(sq + bl * QB + lane * 16);
+                decode_q8(w.x, w.y, ra);
+                decode_q8(w.z, w.w, rb);
+            } else {
+                const uint4 w0 = *reinterpret_cast<const uint4*>(sq + bl * QB + lane * 32);
+                const uint4 w1 = *reinterpret_cast<const uint4*>(sq + bl * QB + lane * 32 + 16);
+                ra[0] = w0.x; ra[1] = w0.y; ra[2] = w0.z; ra[3] = w0.w;
+                rb[0] = w1.x; rb[1] = w1.y; rb[2] = w1.z; rb[3] = w1.w;
+            }
+            float dg = 1.f, dg8 = 1.f;
+            if (WT != T_F16) {
+                const uint32_t dp = *reinterpret_cast<const uint32_t*>(ss + bl * SB + g * 4);
+                const float2 df = __half22float2(*reinterpret_cast<const __half2*>(&dp));
+                dg = df.x; dg8 = df.y;
+            }
+#pragma unroll
+            for (int j = 0; j < NT; ++j) {
+                const int s = j * 8 + g;
+                uint4 xh = make_uint4(0, 0, 0, 0), xl = make_uint4(0, 0, 0, 0);
+                if (s < Bl) {
+                    const uint4* xp = reinterpret_cast<const uint4*>(xs + ((size_t)(bl * Bl + s) * 4 + c) * 32);
+                    xh = xp[0];
+                    xl = xp[1];
+                }
+                if (WT == T_F16) {
+                    mma16816(acc[j], ra[0], rb[0], ra[1], rb[1], xh.x, xh.y);
+                    mma16816(acc[j], ra[0], rb[0], ra[1], rb[1], xl.x, xl.y);
+                    mma16816(acc[j], ra[2], rb[2], ra[3], rb[3], xh.z, xh.w);
+                    mma16816(acc[j], ra[2], rb[2], ra[3], rb[3], xl.z, xl.w);
+                } else {
+                    float tmp[4] = {0.f, 0.f, 0.f, 0.f};
+                    mma16816(tmp, ra[0], rb[0], ra[1], rb[1], xh.x, xh.y);
+                    mma16816(tmp, ra[0], rb[0], ra[1], rb[1], xl.x, xl.y);
+                    mma16816(tmp, ra[2], rb[2], ra[3], rb[3], xh.z, xh.w);
+                    mma16816(tmp, ra[2], rb[2], ra[3], rb[3], xl.z, xl.w);
+                    acc[j][0] = fmaf(dg, tmp[0], acc[j][0]);
+                    acc[j][1] = fmaf(dg, tmp[1], acc[j][1]);
+                    acc[j][2] = fmaf(dg8, tmp[2], acc[j][2]);
+                    acc[j][3] = fmaf(dg8, tmp[3], acc[j][3]);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty + slot);
+        if (aborted) continue;
+        // rows g and g + 8 of the tile, sequences j * 8 + 2c and + 1
+        const int r = (blockIdx.x + i * gridDim.x) * 16 + g;
+#pragma unroll
+        for (int j = 0; j < NT; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int s = j * 8 + 2 * c + (e & 1), rr = r + (e >> 1) * 8;
+                if (s < Bl && rr < p.rows) p.out[(size_t)(s0 + s) * p.ldo + rr] = acc[j][e] * xinv[s];
+            }
+    }
+}
+
+// ---------------------------------------------------------------------------
 // activation preparation: grid (nk, nseq), one CTA per (K split, sequence)
 // ---------------------------------------------------------------------------
 // rmsnorm (when norm_w is set) of the sequence's row, a power-of-two scale

@@ -38,4 +38,13 @@ void (*mv_sk_kernel_f16(int nt, int epi, bool kv32))(MvParams) {
     return nt == 1 ? pick_sk_f16<1>(epi, kv32) : nt == 2 ? pick_sk_f16<2>(epi, kv32) : pick_sk_f16<4>(epi, kv32);
 }
 
+void (*mv_wide_kernel_f16(int nt))(MvParams) {
+    switch (nt) {
+    case 1: return mv_wide_kernel<T_F16, 1>;
+    case 2: return mv_wide_kernel<T_F16, 2>;
+    case 4: return mv_wide_kernel<T_F16, 4>;
+    default: return mv_wide_kernel<T_F16, 8>;
+    }
+}
+
 }  // namespace laic

@@ -11,6 +11,20 @@ void (*mv_kernel_f16(int nt, int epi, bool kv32))(MvParams);
 void (*mv_sk_kernel_q4_0(int nt, int epi, bool kv32))(MvParams);
 void (*mv_sk_kernel_q8_0(int nt, int epi, bool kv32))(MvParams);
 void (*mv_sk_kernel_f16(int nt, int epi, bool kv32))(MvParams);
+void (*mv_wide_kernel_q4_0(int nt))(MvParams);
+void (*mv_wide_kernel_q8_0(int nt))(MvParams);
+void (*mv_wide_kernel_f16(int nt))(MvParams);
+
+static void (*mv_wide_kernel(int type, int nt))(MvParams) {
+    if (type == T_Q4_0) return mv_wide_kernel_q4_0(nt);
+    if (type == T_Q8_0) return mv_wide_kernel_q8_0(nt);
+    return mv_wide_kernel_f16(nt);
+}
+
+cudaError_t mv_wide_launch(int type, int nt, const MvParams& p, int grid, int groups, size_t smem, cudaStream_t st,
+                           bool pdl) {
+    return launch_k(mv_wide_kernel(type, nt), dim3(grid, groups), dim3(kMvThreads), smem, st, pdl, p);
+}
 
 static void (*mv_sk_kernel(int type, int nt, int epi, bool kv32))(MvParams) {
     if (type == T_Q4_0) return mv_sk_kernel_q4_0(nt, epi, kv32);
@@ -39,6 +53,12 @@ cudaError_t xprep_launch(const XPrepParams& p, int nk, cudaStream_t st, bool pdl
 }
 
 cudaError_t mv_set_attributes() {
+    for (int type : {T_Q4_0, T_Q8_0, T_F16})
+        for (int nt : {1, 2, 4, 8}) {
+            cudaError_t e = cudaFuncSetAttribute(mv_wide_kernel(type, nt), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 227 * 1024);
+            if (e != cudaSuccess) return e;
+        }
     for (int type : {T_Q4_0, T_Q8_0, T_F16})
         for (int nt : {1, 2, 4, 8})
             for (int epi : {EPI_STORE, EPI_ADD, EPI_SWIGLU, EPI_QKV})

@@ -40,4 +40,13 @@ void (*mv_sk_kernel_q8_0(int nt, int epi, bool kv32))(MvParams) {
          : nt == 2 ? pick_sk_q8_0<2>(epi, kv32) : pick_sk_q8_0<4>(epi, kv32);
 }
 
+void (*mv_wide_kernel_q8_0(int nt))(MvParams) {
+    switch (nt) {
+    case 1: return mv_wide_kernel<T_Q8_0, 1>;
+    case 2: return mv_wide_kernel<T_Q8_0, 2>;
+    case 4: return mv_wide_kernel<T_Q8_0, 4>;
+    default: return mv_wide_kernel<T_Q8_0, 8>;
+    }
+}
+
 }  // namespace laic

@@ -84,3 +84,11 @@ def test_matvec_matches_oracle(ggml_type, batch, shape):
 def test_matvec_q4_0_large(batch):
     """A 4096x4096 Q4_0 matrix of the 8B-shaped model."""
     _check_matvec(gguf.Q4_0, 4096, 4096, batch, seed=3)
+
+
+@pytest.mark.parametrize("ggml_type", TYPES)
+@pytest.mark.parametrize("batch,rows", [(17, 40000), (40, 12000), (64, 8000)])
+def test_matvec_many_row_tiles(ggml_type, batch, rows):
+    """Batches above 16 of a matrix with thousands of row tiles and a short K (an lm_head's
+    shape): the wide kernel, each warp owning whole row tiles, in one or several sequence groups."""
+    _check_matvec(ggml_type, rows, 576, batch, seed=9)
