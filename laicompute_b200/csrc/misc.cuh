@@ -19,7 +19,7 @@ struct EmbedParams {
     unsigned* counts;        // [max_seqs][vocab] history counts (repeat penalty)
     int vocab;
     // optional: binary16 hi/lo records of x * rec_w for a tile-kernel projection, and sum x^2
-    uint8_t* rec_out;        // [hidden / 32][nseq][4][32 B]
+    uint8_t* rec_out;        // activation records of x * rec_w (rec_off layout)
     const float* rec_w;      // the first rmsnorm weight
     float* ss_out;           // [nseq]
     int nseq;

@@ -65,27 +65,32 @@ struct MvParams {
     long long kv_slot_stride;  // elements between slots
     int kv_cap;
     // tile kernel: activations already split by xprep_kernel
-    const uint8_t* xg;         // [nb][nseq][4][32 B] binary16 hi/lo in fragment order
+    const uint8_t* xg;         // records (rec_off): [nb][hi, lo][nseq][4][16 B] binary16 in fragment order
     const float* xinvg;        // [nk][nseq] power-of-two scale of each K split
     // tile kernel, records made by the producing kernel instead of xprep_kernel (then unscaled):
     int scale_mode;            // 0: xinvg; 1: rmsnorm 1/rms from `ss`; 2: unit scale
     const float* ss;           // [ss_tiles][nseq] partial sums of squares of the rmsnorm input
     int ss_tiles, ss_n;        // partials per sequence, elements per row
     // tile kernel EPI_ADD / EPI_SWIGLU: records of the output for the next tile-kernel projection
-    uint8_t* rec_out;          // [rows or rows/2 / 32][nseq][4][32 B] (nullptr: none)
+    uint8_t* rec_out;          // records (rec_off) of rows or rows/2 elements (nullptr: none)
     const float* rec_w;        // EPI_ADD: the next rmsnorm weight (records of out * w), or nullptr
     float* ss_out;             // EPI_ADD: [row tiles][nseq] sums of squares of the new residual
 };
 
-// Activation record of element e of sequence s (binary16 hi + lo, fragment order), the
-// layout xprep_kernel writes: records [e / 32][nseq][(e / 8) % 4][8 hi | 8 lo].
+// Activation records (the tile and wide kernels' B operands): per GGUF block column bl
+// a hi plane, then a lo plane, each [nseq][4 column groups c][8 binary16 in fragment
+// order]. Byte offset of (bl, part, s, c), part 0 = hi, 1 = lo. The eight lanes of one
+// shared-memory phase (two sequences x four groups) then read 128 consecutive bytes.
+__host__ __device__ __forceinline__ size_t rec_off(int bl, int part, int nseq, int s, int c) {
+    return (((size_t)bl * 2 + part) * nseq + s) * 64 + (size_t)c * 16;
+}
+
+// Record of element e of sequence s (binary16 hi + lo), the layout xprep_kernel writes.
 __device__ __forceinline__ void store_act_record(uint8_t* rec, int nseq, int e, int s, float v) {
-    __half* h = reinterpret_cast<__half*>(rec);
-    const size_t base = (((size_t)(e >> 5) * nseq + s) * 4 + ((e >> 3) & 3)) * 16;
-    const int k = frag_pos(e & 7);
+    const int bl = e >> 5, c = (e >> 3) & 3, k = frag_pos(e & 7);
     const __half hi = __float2half_rn(v);
-    h[base + k] = hi;
-    h[base + 8 + k] = __float2half_rn(v - __half2float(hi));
+    reinterpret_cast<__half*>(rec + rec_off(bl, 0, nseq, s, c))[k] = hi;
+    reinterpret_cast<__half*>(rec + rec_off(bl, 1, nseq, s, c))[k] = __float2half_rn(v - __half2float(hi));
 }
 
 // Activation preparation for the tile kernel (one launch before it).
@@ -96,7 +101,7 @@ struct XPrepParams {
     float eps;
     int in, nb, nseq;
     int kr;                    // blocks per K split of the consuming matvec
-    uint8_t* xg;               // out: [nb][nseq][4][32 B]
+    uint8_t* xg;               // out: records (rec_off)
     float* xinv;               // out: [nk][nseq]
 };
 
@@ -173,6 +178,25 @@ __device__ __forceinline__ uint32_t lds32(uint32_t a) {
     asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
     return v;
 }
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// A sequence group's slice of nblk blocks of activation records (from block b0) into
+// shared memory, 16 bytes per thread and step, by the n threads tid 0..n-1 (cp.async;
+// the caller waits and synchronises).
+__device__ __forceinline__ void load_rec_slice(uint8_t* xs, const uint8_t* xg, int b0, int nblk, int B, int s0, int Bl,
+                                               int tid, int n) {
+    const int per_plane = Bl * 4;
+    for (int i = tid; i < nblk * 2 * per_plane; i += n) {
+        const int c = i & 3, s = (i >> 2) % Bl, plane = i / per_plane;
+        cp_async16(xs + rec_off(plane >> 1, plane & 1, Bl, s, c), xg + rec_off(b0 + (plane >> 1), plane & 1, B, s0 + s, c));
+    }
+    cp_async_commit();
+}
+
 __device__ __forceinline__ void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 
 __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t a0, const uint32_t a1, const uint32_t a2,
@@ -256,7 +280,7 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_mma_kernel(const MvParams p)
     const int stage_bytes = p.kb * (QB + SB);
 
     uint8_t* ring = smem;
-    uint8_t* xs = ring + p.stages * stage_bytes;                            // [kr][sgrp][4][32 B]
+    uint8_t* xs = ring + p.stages * stage_bytes;                            // records of [kr] blocks x [Bl]
     float* red = reinterpret_cast<float*>(xs + (size_t)p.kr * p.sgrp * 128);  // [8 warps][16][NT*8]
     float* fin = red + kConsumerWarps * 16 * NT * 8;                       // [16][Bl]
     float* xinv = fin + 16 * p.sgrp;                                       // [Bl] 1/scale of each sequence
@@ -288,14 +312,12 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_mma_kernel(const MvParams p)
             // before the first blocking wait on a ring slot.
             bool x_issued = false;
             auto issue_x = [&]() {
-                pdl_wait();
-                mbar_expect_tx(xbar, (uint32_t)nblk * Bl * 128);
-                if (Bl == B) {  // one group: the split's records are contiguous
-                    bulk_g2s(xs, p.xg + (size_t)b_lo * B * 128, (uint32_t)nblk * B * 128, xbar);
-                } else {        // this group's slice of every block
-                    for (int bl = 0; bl < nblk; ++bl)
-                        bulk_g2s(xs + (size_t)bl * Bl * 128, p.xg + ((size_t)(b_lo + bl) * B + s0) * 128,
-                                 (uint32_t)Bl * 128, xbar);
+                // one group: the split's records are contiguous, one bulk copy; several
+                // groups: the consumers gather their slice with cp.async instead
+                if (Bl == B) {
+                    pdl_wait();
+                    mbar_expect_tx(xbar, (uint32_t)nblk * B * 128);
+                    bulk_g2s(xs, p.xg + rec_off(b_lo, 0, B, 0, 0), (uint32_t)nblk * B * 128, xbar);
                 }
                 x_issued = true;
             };
@@ -321,7 +343,7 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_mma_kernel(const MvParams p)
             const int issued = it;
             for (int j = max(0, issued - p.stages); j < issued; ++j)
                 mbar_wait(full + (j % p.stages), (uint32_t)(j / p.stages) & 1u, p.err);
-            mbar_wait(xbar, 0u, p.err);
+            if (Bl == B) mbar_wait(xbar, 0u, p.err);
         }
         return;
     }
@@ -332,8 +354,16 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_mma_kernel(const MvParams p)
     pdl_wait();
 
     // activations of this K split: the producer's bulk copy of the prepared
-    // records, plus the split's scale per sequence
-    bool aborted = nblk > 0 && !mbar_wait(xbar, 0u, p.err);
+    // records (or this group's slice, gathered here), plus the split's scale per sequence
+    bool aborted = false;
+    if (nblk > 0) {
+        if (Bl == B) {
+            aborted = !mbar_wait(xbar, 0u, p.err);
+        } else {
+            load_rec_slice(xs, p.xg, b_lo, nblk, B, s0, Bl, ctid, NC);
+            cp_async_wait_all();
+        }
+    }
     for (int sl = ctid; sl < Bl; sl += NC) {
         const int s = s0 + sl;
         float sc = 1.f;
@@ -398,9 +428,8 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_mma_kernel(const MvParams p)
                     const int s = j * 8 + g;
                     uint4 xh = make_uint4(0, 0, 0, 0), xl = make_uint4(0, 0, 0, 0);
                     if (s < Bl) {
-                        const uint4* xp = reinterpret_cast<const uint4*>(xs + ((size_t)(bl * Bl + s) * 4 + c) * 32);
-                        xh = xp[0];
-                        xl = xp[1];
+                        xh = *reinterpret_cast<const uint4*>(xs + rec_off(bl, 0, Bl, s, c));
+                        xl = *reinterpret_cast<const uint4*>(xs + rec_off(bl, 1, Bl, s, c));
                     }
                     if (WT == T_F16) {
                         mma16816(acc[j], ra[0], rb[0], ra[1], rb[1], xh.x, xh.y);
@@ -408,15 +437,15 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_mma_kernel(const MvParams p)
                         mma16816(acc[j], ra[2], rb[2], ra[3], rb[3], xh.z, xh.w);
                         mma16816(acc[j], ra[2], rb[2], ra[3], rb[3], xl.z, xl.w);
                     } else {
-                        float tmp[4] = {0.f, 0.f, 0.f, 0.f};
-                        mma16816(tmp, ra[0], rb[0], ra[1], rb[1], xh.x, xh.y);
-                        mma16816(tmp, ra[0], rb[0], ra[1], rb[1], xl.x, xl.y);
-                        mma16816(tmp, ra[2], rb[2], ra[3], rb[3], xh.z, xh.w);
-                        mma16816(tmp, ra[2], rb[2], ra[3], rb[3], xl.z, xl.w);
-                        acc[j][0] = fmaf(dg, tmp[0], acc[j][0]);
-                        acc[j][1] = fmaf(dg, tmp[1], acc[j][1]);
-                        acc[j][2] = fmaf(dg8, tmp[2], acc[j][2]);
-                        acc[j][3] = fmaf(dg8, tmp[3], acc[j][3]);
+                        float t0[4] = {0.f, 0.f, 0.f, 0.f}, t1[4] = {0.f, 0.f, 0.f, 0.f};
+                        mma16816(t0, ra[0], rb[0], ra[1], rb[1], xh.x, xh.y);
+                        mma16816(t1, ra[2], rb[2], ra[3], rb[3], xh.z, xh.w);
+                        mma16816(t0, ra[0], rb[0], ra[1], rb[1], xl.x, xl.y);
+                        mma16816(t1, ra[2], rb[2], ra[3], rb[3], xl.z, xl.w);
+                        acc[j][0] = fmaf(dg, t0[0] + t1[0], acc[j][0]);
+                        acc[j][1] = fmaf(dg, t0[1] + t1[1], acc[j][1]);
+                        acc[j][2] = fmaf(dg8, t0[2] + t1[2], acc[j][2]);
+                        acc[j][3] = fmaf(dg8, t0[3] + t1[3], acc[j][3]);
                     }
                 }
             }
@@ -551,7 +580,7 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_mma_kernel(const MvParams p)
 // the ring belongs to warp i % 8 (stages: a multiple of 8); the producer fills
 // the stages in tile order. Grid (CTAs, sequence groups) like the tile kernel;
 // tiles t = blockIdx.x + i * gridDim.x. Shared memory:
-//   ring [stages][nb * (QB + SB)] | xs [nb][sgrp][4][32 B] | xinv [sgrp] | barriers
+//   ring [stages][nb * (QB + SB)] | xs: records of nb blocks x sgrp | xinv [sgrp] | barriers
 // ---------------------------------------------------------------------------
 __host__ __device__ constexpr size_t mv_wide_smem(int type, int nb, int sgrp, int stages) {
     return (size_t)stages * nb * (tile_qbytes(type) + (type == T_F16 ? 0 : kTileSBytes)) + (size_t)nb * sgrp * 128 +
@@ -573,7 +602,7 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_wide_kernel(const MvParams p
     const int S = p.stages;
 
     uint8_t* ring = smem;
-    uint8_t* xs = ring + (size_t)S * tile_bytes;                        // [nb][Bl][4][32 B]
+    uint8_t* xs = ring + (size_t)S * tile_bytes;                        // records of [nb] blocks x [Bl]
     float* xinv = reinterpret_cast<float*>(xs + (size_t)nb * p.sgrp * 128);
     uint64_t* full = reinterpret_cast<uint64_t*>(
         (reinterpret_cast<uintptr_t>(xinv + p.sgrp) + 15) & ~uintptr_t(15));
@@ -593,15 +622,11 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_wide_kernel(const MvParams p
         // ---------------- producer ----------------
         if (lane == 0 && n_local > 0) {
             bool x_issued = false;
-            auto issue_x = [&]() {
-                pdl_wait();
-                mbar_expect_tx(xbar, (uint32_t)nb * Bl * 128);
+            auto issue_x = [&]() {  // several groups: the consumers gather their slice
                 if (Bl == B) {
+                    pdl_wait();
+                    mbar_expect_tx(xbar, (uint32_t)nb * B * 128);
                     bulk_g2s(xs, p.xg, (uint32_t)nb * B * 128, xbar);
-                } else {
-                    for (int bl = 0; bl < nb; ++bl)
-                        bulk_g2s(xs + (size_t)bl * Bl * 128, p.xg + ((size_t)bl * B + s0) * 128, (uint32_t)Bl * 128,
-                                 xbar);
                 }
                 x_issued = true;
             };
@@ -618,7 +643,7 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_wide_kernel(const MvParams p
             }
             if (!x_issued) issue_x();
             for (int j = max(0, i - S); j < i; ++j) mbar_wait(full + (j % S), (uint32_t)(j / S) & 1u, p.err);
-            mbar_wait(xbar, 0u, p.err);
+            if (Bl == B) mbar_wait(xbar, 0u, p.err);
         }
         return;
     }
@@ -627,7 +652,15 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_wide_kernel(const MvParams p
     const int ctid = threadIdx.x;
     constexpr int NC = kConsumerWarps * 32;
     pdl_wait();
-    bool aborted = n_local > 0 && !mbar_wait(xbar, 0u, p.err);
+    bool aborted = false;
+    if (n_local > 0) {
+        if (Bl == B) {
+            aborted = !mbar_wait(xbar, 0u, p.err);
+        } else {
+            load_rec_slice(xs, p.xg, 0, nb, B, s0, Bl, ctid, NC);
+            cp_async_wait_all();
+        }
+    }
     for (int sl = ctid; sl < Bl; sl += NC) {
         const int s = s0 + sl;
         float sc = 1.f;
@@ -686,9 +719,8 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_wide_kernel(const MvParams p
                 const int s = j * 8 + g;
                 uint4 xh = make_uint4(0, 0, 0, 0), xl = make_uint4(0, 0, 0, 0);
                 if (s < Bl) {
-                    const uint4* xp = reinterpret_cast<const uint4*>(xs + ((size_t)(bl * Bl + s) * 4 + c) * 32);
-                    xh = xp[0];
-                    xl = xp[1];
+                    xh = *reinterpret_cast<const uint4*>(xs + rec_off(bl, 0, Bl, s, c));
+                    xl = *reinterpret_cast<const uint4*>(xs + rec_off(bl, 1, Bl, s, c));
                 }
                 if (WT == T_F16) {
                     mma16816(acc[j], ra[0], rb[0], ra[1], rb[1], xh.x, xh.y);
@@ -696,15 +728,16 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_wide_kernel(const MvParams p
                     mma16816(acc[j], ra[2], rb[2], ra[3], rb[3], xh.z, xh.w);
                     mma16816(acc[j], ra[2], rb[2], ra[3], rb[3], xl.z, xl.w);
                 } else {
-                    float tmp[4] = {0.f, 0.f, 0.f, 0.f};
-                    mma16816(tmp, ra[0], rb[0], ra[1], rb[1], xh.x, xh.y);
-                    mma16816(tmp, ra[0], rb[0], ra[1], rb[1], xl.x, xl.y);
-                    mma16816(tmp, ra[2], rb[2], ra[3], rb[3], xh.z, xh.w);
-                    mma16816(tmp, ra[2], rb[2], ra[3], rb[3], xl.z, xl.w);
-                    acc[j][0] = fmaf(dg, tmp[0], acc[j][0]);
-                    acc[j][1] = fmaf(dg, tmp[1], acc[j][1]);
-                    acc[j][2] = fmaf(dg8, tmp[2], acc[j][2]);
-                    acc[j][3] = fmaf(dg8, tmp[3], acc[j][3]);
+                    // two independent chains (columns 0-15 and 16-31 of the block)
+                    float t0[4] = {0.f, 0.f, 0.f, 0.f}, t1[4] = {0.f, 0.f, 0.f, 0.f};
+                    mma16816(t0, ra[0], rb[0], ra[1], rb[1], xh.x, xh.y);
+                    mma16816(t1, ra[2], rb[2], ra[3], rb[3], xh.z, xh.w);
+                    mma16816(t0, ra[0], rb[0], ra[1], rb[1], xl.x, xl.y);
+                    mma16816(t1, ra[2], rb[2], ra[3], rb[3], xl.z, xl.w);
+                    acc[j][0] = fmaf(dg, t0[0] + t1[0], acc[j][0]);
+                    acc[j][1] = fmaf(dg, t0[1] + t1[1], acc[j][1]);
+                    acc[j][2] = fmaf(dg8, t0[2] + t1[2], acc[j][2]);
+                    acc[j][3] = fmaf(dg8, t0[3] + t1[3], acc[j][3]);
                 }
             }
         }
@@ -797,9 +830,8 @@ static __global__ void __launch_bounds__(kXPrepThreads) xprep_kernel(const XPrep
             lo[frag_pos(e)] = __float2half_rn(u - __half2float(h));
         }
         const int bl = b_lo + (gi >> 2), c = gi & 3;
-        uint4* dst = reinterpret_cast<uint4*>(p.xg + (((size_t)bl * p.nseq + s) * 4 + c) * 32);
-        dst[0] = *reinterpret_cast<const uint4*>(hi);
-        dst[1] = *reinterpret_cast<const uint4*>(lo);
+        *reinterpret_cast<uint4*>(p.xg + rec_off(bl, 0, p.nseq, s, c)) = *reinterpret_cast<const uint4*>(hi);
+        *reinterpret_cast<uint4*>(p.xg + rec_off(bl, 1, p.nseq, s, c)) = *reinterpret_cast<const uint4*>(lo);
     }
 }
 
