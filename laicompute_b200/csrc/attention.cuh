@@ -42,6 +42,8 @@ struct AttnParams {
     uint8_t* rec_out;          // optional: binary16 hi/lo records of `out` for a tile-kernel projection
     int nseq;                  // sequences of the step (the records' layout)
     const int* npos;           // optional: per query row, its position (batched prefill: causal per row)
+    int nbuf;                  // chunk buffers in shared memory (0 or 1: one); a split takes at most
+                               // this many chunks when nsplit allows, all fetched before the dependency wait
 };
 
 // out[seq][e] = v, plus its activation record when requested.
@@ -339,8 +341,7 @@ __device__ __forceinline__ void attn_mma_body(const AttnParams& p, int split, in
     static_assert(D == 32 || D == 64 || D == 128, "head_dim 32, 64 or 128");
     static_assert(GMAX <= 8, "at most 8 query heads per KV head");
     auto gsync = [&]() { attn_group_sync(bar_id); };
-    __half* Ks = reinterpret_cast<__half*>(smem);
-    __half* Vs = Ks + kAttnChunk * D;
+    __half* Ks = reinterpret_cast<__half*>(smem);  // buffer b: K at Ks + b * 2 * chunk * D, then V
     __shared__ __align__(16) __half Ps[NW][2][8][40];  // per warp: p hi/lo [head][position] (rows padded)
     __shared__ float cm[NW][8], cl[NW][8];
     __shared__ int is_last;
@@ -353,7 +354,8 @@ __device__ __forceinline__ void attn_mma_body(const AttnParams& p, int split, in
     const int slot = p.slots[seq];
     const int n = (p.npos ? p.npos[seq] : p.pos[slot]) + 1;
     const int nch = (n + kAttnChunk - 1) / kAttnChunk;
-    const int active = min(p.nsplit, nch);
+    const int nbuf = max(1, p.nbuf);
+    const int active = min(p.nsplit, (nch + nbuf - 1) / nbuf);  // splits of at most nbuf chunks where possible
     if (split >= active) {
         if (PDL) pdl_launch_dependents();
         return;
@@ -361,33 +363,41 @@ __device__ __forceinline__ void attn_mma_body(const AttnParams& p, int split, in
     const int ch0 = split * nch / active, ch1 = (split + 1) * nch / active;
     const __half* kb = reinterpret_cast<const __half*>(p.kc) + (size_t)slot * p.slot_stride + (size_t)kvh * p.cap * D;
     const __half* vb = reinterpret_cast<const __half*>(p.vc) + (size_t)slot * p.slot_stride + (size_t)kvh * p.cap * D;
+    // chunk ch lives in buffer (ch - ch0) % nbuf
+    auto kbuf = [&](int ch) { return Ks + (size_t)((ch - ch0) % nbuf) * 2 * kAttnChunk * D; };
 
-    // rows [r0, r1) of the chunk that starts at c0, all threads
-    auto load_rows = [&](int r0, int r1, int c0) {
+    // rows [r0, r1) of chunk ch (starting at position c0) into its buffer, all threads
+    auto load_rows = [&](int r0, int r1, int ch) {
+        __half* kd = kbuf(ch);
+        __half* vd = kd + kAttnChunk * D;
+        const int c0 = ch * kAttnChunk;
         for (int i = tid; i < (r1 - r0) * CPR; i += NT) {
             const int r = r0 + i / CPR, cc = i % CPR, rl = r - c0;
-            cp_async16(Ks + attn_swz<D>(rl, cc), kb + (size_t)r * D + cc * 8);
-            cp_async16(Vs + attn_swz<D>(rl, cc), vb + (size_t)r * D + cc * 8);
+            cp_async16(kd + attn_swz<D>(rl, cc), kb + (size_t)r * D + cc * 8);
+            cp_async16(vd + attn_swz<D>(rl, cc), vb + (size_t)r * D + cc * 8);
         }
         cp_async_commit();
     };
-    // value rows past the chunk's end up to the next 32 are read by the last
+    // value rows past a chunk's end up to the next 32 are read by the last
     // warp's products (with p = 0): make them zeros, not stale bits
-    auto zero_tail = [&](int rows) {
+    auto zero_tail = [&](int rows, int ch) {
+        __half* vd = kbuf(ch) + kAttnChunk * D;
         const int end = min(kAttnChunk, (rows + 31) & ~31);
         for (int i = tid; i < (end - rows) * CPR; i += NT) {
             const int rl = rows + i / CPR, cc = i % CPR;
-            *reinterpret_cast<uint4*>(Vs + attn_swz<D>(rl, cc)) = make_uint4(0, 0, 0, 0);
+            *reinterpret_cast<uint4*>(vd + attn_swz<D>(rl, cc)) = make_uint4(0, 0, 0, 0);
         }
     };
-    {
-        const int c0 = ch0 * kAttnChunk, c1 = min(n, c0 + kAttnChunk);
-        load_rows(c0, PDL ? min(c1, n - 1) : c1, c0);  // PDL: older rows, before the dependency wait
-        zero_tail(c1 - c0);
+    // the first nbuf chunks of this split; PDL: only the rows older than this step's
+    for (int ch = ch0; ch < min(ch1, ch0 + nbuf); ++ch) {
+        const int c0 = ch * kAttnChunk, c1 = min(n, c0 + kAttnChunk);
+        load_rows(c0, PDL ? min(c1, n - 1) : c1, ch);
+        zero_tail(c1 - c0, ch);
     }
     if (PDL) {
         pdl_launch_dependents();
         pdl_wait();
+        if (ch1 == nch && ch1 - 1 < ch0 + nbuf) load_rows(n - 1, n, ch1 - 1);  // the newest row, after the wait
     }
 
     // B fragments of the score product: q of head gq (zero past G), scaled by 1/sqrt(d), hi + lo
@@ -411,12 +421,11 @@ __device__ __forceinline__ void attn_mma_body(const AttnParams& p, int split, in
     float o[KS][4];  // O^T: dims (mt*16 + gq, +8) x heads (2c, 2c+1)
 #pragma unroll
     for (int mt = 0; mt < KS; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
-    const uint32_t ks_a = smem_u32(Ks), vs_a = smem_u32(Vs);
     const int li = lane >> 3, lr = lane & 7;  // ldmatrix: this lane addresses row lr of matrix li
 
     for (int ch = ch0; ch < ch1; ++ch) {
         const int c0 = ch * kAttnChunk, c1 = min(n, c0 + kAttnChunk);
-        if (PDL && ch == ch0 && c1 == n) load_rows(n - 1, n, c0);  // the newest row, after the wait
+        const uint32_t ks_a = smem_u32(kbuf(ch)), vs_a = ks_a + kAttnChunk * D * 2;
         cp_async_wait_all();
         gsync();
         const int wp = warp * 32;  // this warp's first row in the chunk
@@ -497,11 +506,11 @@ __device__ __forceinline__ void attn_mma_body(const AttnParams& p, int split, in
             }
             __syncwarp();
         }
-        gsync();  // the chunk buffers are free
-        if (ch + 1 < ch1) {
-            const int n0 = (ch + 1) * kAttnChunk, n1 = min(n, n0 + kAttnChunk);
-            load_rows(n0, n1, n0);
-            zero_tail(n1 - n0);
+        gsync();  // this chunk's buffer is free
+        if (ch + nbuf < ch1) {  // a split longer than its buffers: refill this one
+            const int n0 = (ch + nbuf) * kAttnChunk, n1 = min(n, n0 + kAttnChunk);
+            load_rows(n0, n1, ch + nbuf);
+            zero_tail(n1 - n0, ch + nbuf);
         }
     }
 

@@ -402,7 +402,11 @@ AttnFn attn_pick(int D, int G, bool kv32) {
     if (D == 128) return attn_fn_d<128>(G, kv32);
     return nullptr;
 }
-size_t attn_smem(int D, bool kv32) { return kv32 ? 0 : laic::attn_chunk_smem(D); }
+size_t attn_smem(int D, bool kv32, int nbuf = 1) { return kv32 ? 0 : (size_t)nbuf * laic::attn_chunk_smem(D); }
+// Chunk buffers of the tensor-core attention: with enough (sequence, kv head) pairs to fill
+// the GPU, a split takes up to this many chunks, all fetched before the dependency wait,
+// so short contexts need no split merge.
+int attn_max_nbuf(int D) { return D <= 64 ? 3 : 2; }
 
 // ---------------------------------------------------------------------------
 // the engine
@@ -503,6 +507,8 @@ struct laic_dev {
     bool tile_step(int nseq) const {
         return tp == 1 && (nseq > LAIC_SK_MAX_BATCH || (small_layers() && nseq >= LAIC_TILE_MIN_BATCH));
     }
+
+    int attn_nbuf(int nseq) const { return kv32 || nseq * Hkv < 16 ? 1 : attn_max_nbuf(D); }
 
     int nsplit_for(int nseq) const {
         const int pairs = nseq * Hkv;
@@ -684,9 +690,10 @@ struct laic_dev {
             ap.kc = p.kc; ap.vc = p.vc; ap.slot_stride = kv_slot_stride; ap.cap = cap;
             ap.heads = H; ap.kv_heads = Hkv; ap.slots = d_slots; ap.pos = pos; ap.nsplit = nsplit;
             ap.part = attn_part; ap.counters = attn_cnt; ap.sqrt_d = sqrtf((float)D); ap.err = mvs.err;
-            ap.nseq = nseq; ap.rec_out = recs ? rec_attn : nullptr;
+            ap.nseq = nseq; ap.rec_out = recs ? rec_attn : nullptr; ap.nbuf = attn_nbuf(nseq);
             t_begin("attention", attn_bytes);
-            CK(launch_k(afn, dim3(nsplit, Hkv, nseq), dim3(laic::kAttnWarps * 32), attn_smem(D, kv32), s, pdl, ap));
+            CK(launch_k(afn, dim3(nsplit, Hkv, nseq), dim3(laic::kAttnWarps * 32), attn_smem(D, kv32, ap.nbuf), s, pdl,
+                        ap));
             ++nl;
             t_end();
             // o + residual
@@ -1046,7 +1053,7 @@ int laic_dev_create(const laic_dev_desc* desc, const laic_dev_opts* opts, laic_d
     CK(laic::mv_set_attributes());
     if (!d->kv32)
         CK(cudaFuncSetAttribute(attn_pick(D, d->G, false), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)laic::attn_chunk_smem(D)));
+                                (int)attn_smem(D, false, attn_max_nbuf(D))));
 
     const size_t S = o.max_seqs, kvb = d->kv32 ? 4 : 2;
     CK(cudaMalloc(&d->x, S * d->h * 4));

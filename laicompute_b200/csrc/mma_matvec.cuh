@@ -264,6 +264,38 @@ __host__ __device__ constexpr int mv_ring_bytes(int type, int kb, int stages) {
     return stages * kb * (tile_qbytes(type) + (type == T_F16 ? 0 : kTileSBytes));
 }
 
+// 1/scale of each sequence of a group into xinv[0 .. Bl): xprep's power-of-two scale of the
+// K split (mode 0), the rmsnorm of the whole row from the producers' partial sums of
+// squares (mode 1), or 1 (mode 2). Mode 1 spreads a sequence's partial sums over tps
+// threads of one warp (a power of two) and adds them in a fixed tree order.
+__device__ __forceinline__ void seq_scales(const MvParams& p, int k_split, int s0, int Bl, float* xinv, int tid, int n) {
+    if (p.scale_mode != 1) {
+        for (int sl = tid; sl < Bl; sl += n)
+            xinv[sl] = p.scale_mode == 0 ? p.xinvg[(size_t)k_split * p.nseq + s0 + sl] : 1.f;
+        return;
+    }
+    int tps = 32;
+    while (tps > 1 && tps * Bl > n) tps >>= 1;
+    const int part = tid % tps;
+    for (int sl0 = 0; sl0 < Bl; sl0 += n / tps) {  // the same trip count in every thread
+        const int sl = sl0 + tid / tps;
+        float a = 0.f;
+        if (sl < Bl) {
+            const float* src = p.ss + s0 + sl;
+            int t = part;
+            for (; t + 3 * tps < p.ss_tiles; t += 4 * tps) {
+                const float v0 = __ldcg(src + (size_t)t * p.nseq), v1 = __ldcg(src + (size_t)(t + tps) * p.nseq);
+                const float v2 = __ldcg(src + (size_t)(t + 2 * tps) * p.nseq);
+                const float v3 = __ldcg(src + (size_t)(t + 3 * tps) * p.nseq);
+                a += (v0 + v1) + (v2 + v3);
+            }
+            for (; t < p.ss_tiles; t += tps) a += __ldcg(src + (size_t)t * p.nseq);
+        }
+        for (int o = tps >> 1; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+        if (sl < Bl && part == 0) xinv[sl] = 1.f / sqrtf(a / float(p.ss_n) + p.eps);
+    }
+}
+
 // ---------------------------------------------------------------------------
 // the kernel: NT n-tiles of 8 sequences (NT*8 >= nseq)
 // ---------------------------------------------------------------------------
@@ -356,34 +388,11 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_mma_kernel(const MvParams p)
     // activations of this K split: the producer's bulk copy of the prepared
     // records (or this group's slice, gathered here), plus the split's scale per sequence
     bool aborted = false;
+    if (nblk > 0 && Bl != B) load_rec_slice(xs, p.xg, b_lo, nblk, B, s0, Bl, ctid, NC);  // in flight meanwhile
+    seq_scales(p, k_split, s0, Bl, xinv, ctid, NC);
     if (nblk > 0) {
-        if (Bl == B) {
-            aborted = !mbar_wait(xbar, 0u, p.err);
-        } else {
-            load_rec_slice(xs, p.xg, b_lo, nblk, B, s0, Bl, ctid, NC);
-            cp_async_wait_all();
-        }
-    }
-    for (int sl = ctid; sl < Bl; sl += NC) {
-        const int s = s0 + sl;
-        float sc = 1.f;
-        if (p.scale_mode == 0) {
-            sc = p.xinvg[(size_t)k_split * B + s];
-        } else if (p.scale_mode == 1) {  // rmsnorm over the whole row, from the producer's partial sums
-            // added in tile order; the loads go out 16 at a time (one L2 round trip each)
-            float a = 0.f;
-            int t = 0;
-            for (; t + 16 <= p.ss_tiles; t += 16) {
-                float v[16];
-#pragma unroll
-                for (int u = 0; u < 16; ++u) v[u] = __ldcg(p.ss + (size_t)(t + u) * B + s);
-#pragma unroll
-                for (int u = 0; u < 16; ++u) a += v[u];
-            }
-            for (; t < p.ss_tiles; ++t) a += __ldcg(p.ss + (size_t)t * B + s);
-            sc = 1.f / sqrtf(a / float(p.ss_n) + p.eps);
-        }
-        xinv[sl] = sc;
+        if (Bl == B) aborted = !mbar_wait(xbar, 0u, p.err);
+        else cp_async_wait_all();
     }
     named_sync(1, NC);
     pdl_launch_dependents();
@@ -653,33 +662,11 @@ __global__ void __launch_bounds__(kMvThreads, 1) mv_wide_kernel(const MvParams p
     constexpr int NC = kConsumerWarps * 32;
     pdl_wait();
     bool aborted = false;
+    if (n_local > 0 && Bl != B) load_rec_slice(xs, p.xg, 0, nb, B, s0, Bl, ctid, NC);  // in flight meanwhile
+    seq_scales(p, 0, s0, Bl, xinv, ctid, NC);
     if (n_local > 0) {
-        if (Bl == B) {
-            aborted = !mbar_wait(xbar, 0u, p.err);
-        } else {
-            load_rec_slice(xs, p.xg, 0, nb, B, s0, Bl, ctid, NC);
-            cp_async_wait_all();
-        }
-    }
-    for (int sl = ctid; sl < Bl; sl += NC) {
-        const int s = s0 + sl;
-        float sc = 1.f;
-        if (p.scale_mode == 0) {
-            sc = p.xinvg[s];
-        } else if (p.scale_mode == 1) {
-            float a = 0.f;
-            int t = 0;
-            for (; t + 16 <= p.ss_tiles; t += 16) {
-                float v[16];
-#pragma unroll
-                for (int u = 0; u < 16; ++u) v[u] = __ldcg(p.ss + (size_t)(t + u) * B + s);
-#pragma unroll
-                for (int u = 0; u < 16; ++u) a += v[u];
-            }
-            for (; t < p.ss_tiles; ++t) a += __ldcg(p.ss + (size_t)t * B + s);
-            sc = 1.f / sqrtf(a / float(p.ss_n) + p.eps);
-        }
-        xinv[sl] = sc;
+        if (Bl == B) aborted = !mbar_wait(xbar, 0u, p.err);
+        else cp_async_wait_all();
     }
     named_sync(1, NC);
     pdl_launch_dependents();
