@@ -355,7 +355,9 @@ __device__ __forceinline__ void attn_mma_body(const AttnParams& p, int split, in
     const int n = (p.npos ? p.npos[seq] : p.pos[slot]) + 1;
     const int nch = (n + kAttnChunk - 1) / kAttnChunk;
     const int nbuf = max(1, p.nbuf);
-    const int active = min(p.nsplit, (nch + nbuf - 1) / nbuf);  // splits of at most nbuf chunks where possible
+    // a context that fits the buffers: one split, no merge; else one chunk per split where
+    // nsplit allows (the chunks of a longer split stream through its buffers)
+    const int active = nch <= nbuf ? 1 : min(p.nsplit, nch);
     if (split >= active) {
         if (PDL) pdl_launch_dependents();
         return;

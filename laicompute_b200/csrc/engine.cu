@@ -516,9 +516,15 @@ struct laic_dev {
             const int s = (8 * num_sms() + pairs - 1) / pairs;  // about eight CTAs per SM
             return std::max(1, std::min(s, max_split));
         }
-        // chunked kernel: at most one split per chunk of the capacity, about four CTAs per SM
+        // chunked kernel: at most one split per chunk of the capacity, about four CTAs per SM,
+        // and with several chunk buffers no more CTAs than stay resident at once
         const int chunks = (cap + laic::kAttnChunk - 1) / laic::kAttnChunk;
-        const int s = (4 * num_sms() + pairs - 1) / pairs;
+        int s = (4 * num_sms() + pairs - 1) / pairs;
+        const int nbuf = attn_nbuf(nseq);
+        if (nbuf > 1) {
+            const int per_sm = (int)((227 * 1024) / attn_smem(D, false, nbuf));
+            s = std::min(s, num_sms() * per_sm / pairs);
+        }
         return std::max(1, std::min(std::min(s, chunks), max_split));
     }
 
