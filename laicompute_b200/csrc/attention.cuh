@@ -572,23 +572,39 @@ __device__ __forceinline__ void attn_mma_body(const AttnParams& p, int split, in
     __threadfence();
     const size_t sstride = (size_t)G * PD;
     const float* base = p.part + pair * p.nsplit * sstride;
-    if (tid < G) {  // per head: the splits' weights (active <= 64 splits)
+    __shared__ float ml[64][8];
+    for (int i = tid; i < active * G; i += NT) {  // every split's (max, sum) at once (active <= 64 splits)
+        const int j = i / G, g = i % G;
+        mw[j][g] = __ldcg(base + j * sstride + g * PD + D);
+        ml[j][g] = __ldcg(base + j * sstride + g * PD + D + 1);
+    }
+    gsync();
+    if (tid < G) {  // per head: the splits' weights, in split order
         const int g = tid;
         float M = -INFINITY, L = 0.f;
-        for (int j = 0; j < active; ++j) M = fmaxf(M, __ldcg(base + j * sstride + g * PD + D));
+        for (int j = 0; j < active; ++j) M = fmaxf(M, mw[j][g]);
         for (int j = 0; j < active; ++j) {
-            const float mj = __ldcg(base + j * sstride + g * PD + D);
-            const float e = mj == -INFINITY ? 0.f : expf(mj - M);
+            const float e = mw[j][g] == -INFINITY ? 0.f : expf(mw[j][g] - M);
             mw[j][g] = e;
-            L = fmaf(__ldcg(base + j * sstride + g * PD + D + 1), e, L);
+            L = fmaf(ml[j][g], e, L);
         }
         mL[g] = L;
     }
     gsync();
     for (int i = tid; i < G * D; i += NT) {
         const int g = i / D, dd = i % D;
+        const float* src = base + g * PD + dd;
         float A = 0.f;
-        for (int j = 0; j < active; ++j) A = fmaf(__ldcg(base + j * sstride + g * PD + dd), mw[j][g], A);
+        int j = 0;
+        for (; j + 4 <= active; j += 4) {  // four loads in flight, added in split order
+            const float v0 = __ldcg(src + j * sstride), v1 = __ldcg(src + (j + 1) * sstride);
+            const float v2 = __ldcg(src + (j + 2) * sstride), v3 = __ldcg(src + (j + 3) * sstride);
+            A = fmaf(v0, mw[j][g], A);
+            A = fmaf(v1, mw[j + 1][g], A);
+            A = fmaf(v2, mw[j + 2][g], A);
+            A = fmaf(v3, mw[j + 3][g], A);
+        }
+        for (; j < active; ++j) A = fmaf(__ldcg(src + j * sstride), mw[j][g], A);
         attn_store(p, seq, (kvh * G + g) * D + dd, A / mL[g]);
     }
     if (tid == 0) p.counters[pair] = 0u;
