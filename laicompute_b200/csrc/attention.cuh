@@ -17,6 +17,8 @@
 // FP32 in the parity mode, where scores use the reference's unfused
 // sequential multiply-add order).
 #pragma once
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "mma_matvec.cuh"  // smem_u32, mma16816
 
@@ -328,10 +330,17 @@ __device__ __forceinline__ void attn_group_sync(int id) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(kAttnWarps * 32) : "memory");
 }
 
+// Largest split count merged inside a thread-block cluster (the portable cluster size).
+constexpr int kAttnMaxCluster = 8;
+
 // One split of one (sequence, kv head) pair, run by kAttnWarps warps (tid 0..127)
-// on `smem` (attn_chunk_smem(D) bytes). PDL: fetch older rows before the
-// programmatic-dependency wait (standalone kernel); else everything after entry.
-template <int D, int GMAX, bool PDL>
+// on `smem` (attn_chunk_smem(D) bytes per chunk buffer). PDL: fetch older rows
+// before the programmatic-dependency wait (standalone kernel); else everything
+// after entry. CL: the nsplit CTAs of the pair form one thread-block cluster and
+// merge their partials through distributed shared memory (every CTA of the
+// cluster reaches both cluster barriers); else the last CTA to finish merges
+// them from global scratch (atomic ticket).
+template <int D, int GMAX, bool PDL, bool CL = false>
 __device__ __forceinline__ void attn_mma_body(const AttnParams& p, int split, int kvh, int seq, uint8_t* smem,
                                               int tid, int bar_id) {
     constexpr int KS = D / 16;  // k-steps of the score product = m-tiles of the value product
@@ -358,11 +367,13 @@ __device__ __forceinline__ void attn_mma_body(const AttnParams& p, int split, in
     // a context that fits the buffers: one split, no merge; else one chunk per split where
     // nsplit allows (the chunks of a longer split stream through its buffers)
     const int active = nch <= nbuf ? 1 : min(p.nsplit, nch);
-    if (split >= active) {
+    const bool live = split < active;
+    if (!live && !CL) {
         if (PDL) pdl_launch_dependents();
         return;
     }
-    const int ch0 = split * nch / active, ch1 = (split + 1) * nch / active;
+    // (an idle CTA of a cluster has no chunks and an empty partial)
+    const int ch0 = live ? split * nch / active : 0, ch1 = live ? (split + 1) * nch / active : 0;
     const __half* kb = reinterpret_cast<const __half*>(p.kc) + (size_t)slot * p.slot_stride + (size_t)kvh * p.cap * D;
     const __half* vb = reinterpret_cast<const __half*>(p.vc) + (size_t)slot * p.slot_stride + (size_t)kvh * p.cap * D;
     // chunk ch lives in buffer (ch - ch0) % nbuf
@@ -548,20 +559,54 @@ __device__ __forceinline__ void attn_mma_body(const AttnParams& p, int split, in
         mM[g] = M; mL[g] = L;
     }
     gsync();
+    __shared__ float cpart[CL ? 8 * D : 1], cpM[8], cpL[8];  // cluster mode: this CTA's partial
     for (int i = tid; i < G * D; i += NT) {
         const int g = i / D, dd = i % D;
         float A = 0.f;
 #pragma unroll
         for (int w = 0; w < NW; ++w) A = fmaf(cacc[((size_t)w * 8 + g) * D + dd], mw[w][g], A);
         if (active == 1) {
-            attn_store(p, seq, (kvh * G + g) * D + dd, A / mL[g]);
+            if (live) attn_store(p, seq, (kvh * G + g) * D + dd, A / mL[g]);
+        } else if (CL) {
+            cpart[i] = A;
+            if (dd == 0) { cpM[g] = mM[g]; cpL[g] = mL[g]; }
         } else {
             float* dst = p.part + ((pair * p.nsplit + split) * G + g) * PD;
             dst[dd] = A;
             if (dd == 0) { dst[D] = mM[g]; dst[D + 1] = mL[g]; }
         }
     }
-    if (active == 1) return;
+    if (active == 1) return;  // the same for every CTA of the pair
+
+    if constexpr (CL) {
+        // ---- the splits' partials through distributed shared memory: CTA j of the cluster
+        //      is split j; each CTA merges every nsplit-th slice of the elements
+        namespace cg = cooperative_groups;
+        cg::cluster_group cluster = cg::this_cluster();
+        __shared__ float cw[kAttnMaxCluster][8], cLs[8];
+        cluster.sync();  // every partial is written
+        if (tid < G) {
+            const int g = tid;
+            float M = -INFINITY, L = 0.f;
+            for (int j = 0; j < active; ++j) M = fmaxf(M, *cluster.map_shared_rank(&cpM[g], j));
+            for (int j = 0; j < active; ++j) {
+                const float mj = *cluster.map_shared_rank(&cpM[g], j);
+                const float e = mj == -INFINITY ? 0.f : expf(mj - M);
+                cw[j][g] = e;
+                L = fmaf(*cluster.map_shared_rank(&cpL[g], j), e, L);
+            }
+            cLs[g] = L;
+        }
+        gsync();
+        for (int i = split * NT + tid; i < G * D; i += p.nsplit * NT) {
+            const int g = i / D;
+            float A = 0.f;
+            for (int j = 0; j < active; ++j) A = fmaf(*cluster.map_shared_rank(&cpart[i], j), cw[j][g], A);
+            attn_store(p, seq, (kvh * G + g) * D + i % D, A / cLs[g]);
+        }
+        cluster.sync();  // no CTA leaves while the others may still read its partial
+        return;
+    }
 
     // ---- the last of the active splits merges them (atomic ticket, no spinning)
     __threadfence();
@@ -610,10 +655,11 @@ __device__ __forceinline__ void attn_mma_body(const AttnParams& p, int split, in
     if (tid == 0) p.counters[pair] = 0u;
 }
 
-template <int D, int GMAX>
+// CL: launched with a cluster of (nsplit, 1, 1) CTAs, 2 <= nsplit <= kAttnMaxCluster.
+template <int D, int GMAX, bool CL>
 __global__ void __launch_bounds__(kAttnWarps * 32) attn_mma_kernel(const AttnParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
-    attn_mma_body<D, GMAX, true>(p, blockIdx.x, blockIdx.y, blockIdx.z, smem, threadIdx.x, 1);
+    attn_mma_body<D, GMAX, true, CL>(p, blockIdx.x, blockIdx.y, blockIdx.z, smem, threadIdx.x, 1);
 }
 
 }  // namespace laic

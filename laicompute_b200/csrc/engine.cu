@@ -384,24 +384,28 @@ cudaError_t launch_matvec(const Mat& m, laic::MvParams p, int epi, bool kv32, co
 
 using AttnFn = void (*)(laic::AttnParams);
 template <int D, int GM>
-AttnFn attn_fn_g(bool kv32) {
-    return kv32 ? laic::attn_decode_kernel<D, GM, float, true> : laic::attn_mma_kernel<D, GM>;
+AttnFn attn_fn_g(bool kv32, bool cl) {
+    if (kv32) return laic::attn_decode_kernel<D, GM, float, true>;
+    return cl ? laic::attn_mma_kernel<D, GM, true> : laic::attn_mma_kernel<D, GM, false>;
 }
 template <int D>
-AttnFn attn_fn_d(int G, bool kv32) {
-    if (G <= 1) return attn_fn_g<D, 1>(kv32);
-    if (G <= 2) return attn_fn_g<D, 2>(kv32);
-    if (G <= 4) return attn_fn_g<D, 4>(kv32);
-    return attn_fn_g<D, 8>(kv32);
+AttnFn attn_fn_d(int G, bool kv32, bool cl) {
+    if (G <= 1) return attn_fn_g<D, 1>(kv32, cl);
+    if (G <= 2) return attn_fn_g<D, 2>(kv32, cl);
+    if (G <= 4) return attn_fn_g<D, 4>(kv32, cl);
+    return attn_fn_g<D, 8>(kv32, cl);
 }
 // FP32 KV (parity mode): the register kernel with the reference's score order;
-// FP16 KV: the tensor-core kernel over chunks staged in shared memory.
-AttnFn attn_pick(int D, int G, bool kv32) {
-    if (D == 32) return attn_fn_d<32>(G, kv32);
-    if (D == 64) return attn_fn_d<64>(G, kv32);
-    if (D == 128) return attn_fn_d<128>(G, kv32);
+// FP16 KV: the tensor-core kernel over chunks staged in shared memory, its splits merged
+// inside a thread-block cluster (cl) or through global scratch.
+AttnFn attn_pick(int D, int G, bool kv32, bool cl = false) {
+    if (D == 32) return attn_fn_d<32>(G, kv32, cl);
+    if (D == 64) return attn_fn_d<64>(G, kv32, cl);
+    if (D == 128) return attn_fn_d<128>(G, kv32, cl);
     return nullptr;
 }
+// Cluster merge for 2..8 splits of the tensor-core kernel.
+bool attn_cluster(int nsplit, bool kv32) { return !kv32 && nsplit >= 2 && nsplit <= laic::kAttnMaxCluster; }
 size_t attn_smem(int D, bool kv32, int nbuf = 1) { return kv32 ? 0 : (size_t)nbuf * laic::attn_chunk_smem(D); }
 // Chunk buffers of the tensor-core attention: with enough (sequence, kv head) pairs to fill
 // the GPU, a split takes up to this many chunks, all fetched before the dependency wait,
@@ -508,7 +512,7 @@ struct laic_dev {
         return tp == 1 && (nseq > LAIC_SK_MAX_BATCH || (small_layers() && nseq >= LAIC_TILE_MIN_BATCH));
     }
 
-    int attn_nbuf(int nseq) const { return kv32 || nseq * Hkv < 16 ? 1 : attn_max_nbuf(D); }
+    int attn_nbuf(int nseq) const { (void)nseq; return kv32 ? 1 : attn_max_nbuf(D); }
 
     int nsplit_for(int nseq) const {
         const int pairs = nseq * Hkv;
@@ -517,14 +521,12 @@ struct laic_dev {
             return std::max(1, std::min(s, max_split));
         }
         // chunked kernel: at most one split per chunk of the capacity, about four CTAs per SM,
-        // and with several chunk buffers no more CTAs than stay resident at once
+        // no more CTAs than stay resident at once, and at most one cluster of splits per pair
         const int chunks = (cap + laic::kAttnChunk - 1) / laic::kAttnChunk;
         int s = (4 * num_sms() + pairs - 1) / pairs;
-        const int nbuf = attn_nbuf(nseq);
-        if (nbuf > 1) {
-            const int per_sm = (int)((227 * 1024) / attn_smem(D, false, nbuf));
-            s = std::min(s, num_sms() * per_sm / pairs);
-        }
+        const int per_sm = (int)((227 * 1024) / attn_smem(D, false, attn_nbuf(nseq)));
+        s = std::min(s, num_sms() * per_sm / pairs);
+        s = std::min(s, laic::kAttnMaxCluster);
         return std::max(1, std::min(std::min(s, chunks), max_split));
     }
 
@@ -698,8 +700,12 @@ struct laic_dev {
             ap.part = attn_part; ap.counters = attn_cnt; ap.sqrt_d = sqrtf((float)D); ap.err = mvs.err;
             ap.nseq = nseq; ap.rec_out = recs ? rec_attn : nullptr; ap.nbuf = attn_nbuf(nseq);
             t_begin("attention", attn_bytes);
-            CK(launch_k(afn, dim3(nsplit, Hkv, nseq), dim3(laic::kAttnWarps * 32), attn_smem(D, kv32, ap.nbuf), s, pdl,
-                        ap));
+            if (attn_cluster(nsplit, kv32))
+                CK(laic::launch_cluster_k(attn_pick(D, G, kv32, true), dim3(nsplit, Hkv, nseq), dim3(laic::kAttnWarps * 32),
+                                          attn_smem(D, kv32, ap.nbuf), s, pdl, nsplit, ap));
+            else
+                CK(launch_k(afn, dim3(nsplit, Hkv, nseq), dim3(laic::kAttnWarps * 32), attn_smem(D, kv32, ap.nbuf), s,
+                            pdl, ap));
             ++nl;
             t_end();
             // o + residual
@@ -1058,8 +1064,9 @@ int laic_dev_create(const laic_dev_desc* desc, const laic_dev_opts* opts, laic_d
     // set kernel attributes now: graph capture must not see attribute calls
     CK(laic::mv_set_attributes());
     if (!d->kv32)
-        CK(cudaFuncSetAttribute(attn_pick(D, d->G, false), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)attn_smem(D, false, attn_max_nbuf(D))));
+        for (bool cl : {false, true})
+            CK(cudaFuncSetAttribute(attn_pick(D, d->G, false, cl), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)attn_smem(D, false, attn_max_nbuf(D))));
 
     const size_t S = o.max_seqs, kvb = d->kv32 ? 4 : 2;
     CK(cudaMalloc(&d->x, S * d->h * 4));
