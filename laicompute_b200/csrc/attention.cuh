@@ -21,6 +21,7 @@
 
 #include "common.cuh"
 #include "mma_matvec.cuh"  // smem_u32, mma16816
+#include "mv_streamk.cuh"  // dp_lane_record_rt
 
 namespace laic {
 
@@ -46,12 +47,20 @@ struct AttnParams {
     const int* npos;           // optional: per query row, its position (batched prefill: causal per row)
     int nbuf;                  // chunk buffers in shared memory (0 or 1: one); a split takes at most
                                // this many chunks when nsplit allows, all fetched before the dependency wait
+    uint8_t* rec_dp;           // optional, one sequence: the team kernel's integer records of `out`
+    int rec_type;              //   for a projection of this weight type (T_Q4_0 or T_Q8_0)
 };
 
 // out[seq][e] = v, plus its activation record when requested.
 __device__ __forceinline__ void attn_store(const AttnParams& p, int seq, int e, float v) {
     p.out[(size_t)seq * p.ldo + e] = v;
     if (p.rec_out) store_act_record(p.rec_out, p.nseq, e, seq, v);
+}
+// attn_store where `live`, plus the integer records (one sequence) when requested: every
+// lane of the warp calls it, lanes 8j..8j+7 with the eight elements of one 8-column group.
+__device__ __forceinline__ void attn_emit(const AttnParams& p, int seq, int e, float v, bool live) {
+    if (live) attn_store(p, seq, e, v);
+    if (p.rec_dp) dp_lane_record_rt(p.rec_type, live ? v : 0.f, 0.f, e & 7, live ? e >> 3 : -1, p.rec_dp, 1, 2, 4);
 }
 
 template <typename KV, int N> struct KvLoad;
@@ -560,13 +569,18 @@ __device__ __forceinline__ void attn_mma_body(const AttnParams& p, int split, in
     }
     gsync();
     __shared__ float cpart[CL ? 8 * D : 1], cpM[8], cpL[8];  // cluster mode: this CTA's partial
-    for (int i = tid; i < G * D; i += NT) {
-        const int g = i / D, dd = i % D;
+    for (int ib = 0; ib < G * D; ib += NT) {  // the same trip count in every thread
+        const int i = ib + tid;
+        const bool in = i < G * D;
+        const int g = in ? i / D : 0, dd = i % D;
         float A = 0.f;
+        if (in) {
 #pragma unroll
-        for (int w = 0; w < NW; ++w) A = fmaf(cacc[((size_t)w * 8 + g) * D + dd], mw[w][g], A);
+            for (int w = 0; w < NW; ++w) A = fmaf(cacc[((size_t)w * 8 + g) * D + dd], mw[w][g], A);
+        }
         if (active == 1) {
-            if (live) attn_store(p, seq, (kvh * G + g) * D + dd, A / mL[g]);
+            attn_emit(p, seq, kvh * G * D + i, A / mL[g], in && live);
+        } else if (!in) {
         } else if (CL) {
             cpart[i] = A;
             if (dd == 0) { cpM[g] = mM[g]; cpL[g] = mL[g]; }
@@ -598,11 +612,14 @@ __device__ __forceinline__ void attn_mma_body(const AttnParams& p, int split, in
             cLs[g] = L;
         }
         gsync();
-        for (int i = split * NT + tid; i < G * D; i += p.nsplit * NT) {
-            const int g = i / D;
+        for (int ib = split * NT; ib < G * D; ib += p.nsplit * NT) {
+            const int i = ib + tid;
+            const bool in = i < G * D;
+            const int g = in ? i / D : 0;
             float A = 0.f;
-            for (int j = 0; j < active; ++j) A = fmaf(*cluster.map_shared_rank(&cpart[i], j), cw[j][g], A);
-            attn_store(p, seq, (kvh * G + g) * D + i % D, A / cLs[g]);
+            if (in)
+                for (int j = 0; j < active; ++j) A = fmaf(*cluster.map_shared_rank(&cpart[i], j), cw[j][g], A);
+            attn_emit(p, seq, kvh * G * D + i, A / cLs[g], in);
         }
         cluster.sync();  // no CTA leaves while the others may still read its partial
         return;
@@ -636,12 +653,14 @@ __device__ __forceinline__ void attn_mma_body(const AttnParams& p, int split, in
         mL[g] = L;
     }
     gsync();
-    for (int i = tid; i < G * D; i += NT) {
-        const int g = i / D, dd = i % D;
+    for (int ib = 0; ib < G * D; ib += NT) {
+        const int i = ib + tid;
+        const bool in = i < G * D;
+        const int g = in ? i / D : 0, dd = i % D;
         const float* src = base + g * PD + dd;
         float A = 0.f;
         int j = 0;
-        for (; j + 4 <= active; j += 4) {  // four loads in flight, added in split order
+        for (; in && j + 4 <= active; j += 4) {  // four loads in flight, added in split order
             const float v0 = __ldcg(src + j * sstride), v1 = __ldcg(src + (j + 1) * sstride);
             const float v2 = __ldcg(src + (j + 2) * sstride), v3 = __ldcg(src + (j + 3) * sstride);
             A = fmaf(v0, mw[j][g], A);
@@ -649,8 +668,8 @@ __device__ __forceinline__ void attn_mma_body(const AttnParams& p, int split, in
             A = fmaf(v2, mw[j + 2][g], A);
             A = fmaf(v3, mw[j + 3][g], A);
         }
-        for (; j < active; ++j) A = fmaf(__ldcg(src + j * sstride), mw[j][g], A);
-        attn_store(p, seq, (kvh * G + g) * D + dd, A / mL[g]);
+        for (; in && j < active; ++j) A = fmaf(__ldcg(src + j * sstride), mw[j][g], A);
+        attn_emit(p, seq, kvh * G * D + i, A / mL[g], in);
     }
     if (tid == 0) p.counters[pair] = 0u;
 }

@@ -171,6 +171,11 @@ constexpr size_t kSmemBudget = 220 * 1024;
 #ifndef LAIC_TILE_MIN_BATCH
 #define LAIC_TILE_MIN_BATCH 1
 #endif
+// One-sequence steps of larger models pass the team kernel's integer records between
+// the projections (0: every projection builds them from x itself).
+#ifndef LAIC_DP_RECORDS
+#define LAIC_DP_RECORDS 1
+#endif
 // In such steps the lm_head stays on the team kernel up to this batch.
 #ifndef LAIC_LM_TEAM_MAX_BATCH
 #define LAIC_LM_TEAM_MAX_BATCH 4
@@ -352,6 +357,7 @@ struct RecIn {
     int mode = 0;             // 1: rmsnorm scale from ss; 2: unit scale
     const float* ss = nullptr;
     int ss_tiles = 0;
+    bool dp = false;          // the team kernel's integer records (one sequence), not the tile kernel's
 };
 
 // One projection: the team kernel for small batches, else activation
@@ -363,12 +369,15 @@ cudaError_t launch_matvec(const Mat& m, laic::MvParams p, int epi, bool kv32, co
     p.q = m.q; p.s = m.s; p.rows = m.rows; p.ntiles = m.ntiles; p.in = m.in; p.nb = m.nb;
     if (sh.sk) {
         p.err = sc.err;
+        if (rin && rin->xg && rin->dp && sh.nt == 0) {
+            p.xg = rin->xg; p.scale_mode = rin->mode; p.ss = rin->ss; p.ss_tiles = rin->ss_tiles; p.ss_n = m.in;
+        }
         if (launches) *launches += 1;
         return laic::mv_sk_launch(m.type, sh.nt, epi, kv32, p, sh.grid, sh.smem, st, pdl);
     }
     p.nk = sh.nk; p.kr = sh.kr; p.kb = sh.kb; p.stages = sh.stages; p.sgrp = sh.sgrp;
     p.part = sc.part; p.tile_cnt = sc.tile_cnt; p.err = sc.err;
-    if (rin && rin->xg) {
+    if (rin && rin->xg && !rin->dp) {
         p.xg = rin->xg; p.scale_mode = rin->mode; p.ss = rin->ss; p.ss_tiles = rin->ss_tiles; p.ss_n = m.in;
     } else {
         laic::XPrepParams xp{p.x, p.ldx, p.norm_w, p.eps, m.in, m.nb, p.nseq, sh.kr, sc.xg, sc.xinv};
@@ -641,11 +650,28 @@ struct laic_dev {
 
         const bool step_path = nseq == 1 && step_ready;
         const bool recs = !step_path && tile_step(nseq) && rec_x;  // records travel between the tile-kernel projections
+        // one sequence on the team kernel's integer variant: each producing epilogue (embedding,
+        // attention, o, gate/up, down) writes the next projection's digit records
+        auto dp_mat = [](const Mat& m) {
+            if (m.type != T_Q4_0 && m.type != T_Q8_0) return false;
+            const MvShape sh = mv_shape(m, 1);
+            return sh.sk && sh.nt == 0;
+        };
+        bool dprecs = LAIC_DP_RECORDS && !step_path && !recs && nseq == 1 && tp == 1 && !kv32 && rec_x != nullptr;
+        for (int l = 0; l < L && dprecs; ++l)
+            dprecs = dp_mat(layers[l].qkv) && dp_mat(layers[l].o) && dp_mat(layers[l].gu) && dp_mat(layers[l].down);
+        const bool dp_lm = dprecs && dp_mat(lm_head());
         const int ntiles_h = (h + 15) / 16;
         laic::EmbedParams ep{embd.type, embd.q, embd.s, h, embd.nb, d_tokens, d_slots, x, counts, V};
-        if (recs) { ep.rec_out = rec_x; ep.rec_w = layers[0].attn_norm; ep.ss_out = rec_ss; ep.nseq = nseq; }
+        ep.nseq = nseq;
+        if (recs) { ep.rec_out = rec_x; ep.rec_w = layers[0].attn_norm; ep.ss_out = rec_ss; }
+        // one sequence with integer records: the row in slices of 256 over several CTAs
+        const int ecta = dprecs && L > 0 ? std::max(1, std::min(16, h / 256)) : 1;
+        if (dprecs && L > 0) {
+            ep.rec_dp = rec_x; ep.rec_w = layers[0].attn_norm; ep.ss_out = rec_ss; ep.rec_type = layers[0].qkv.type;
+        }
         t_begin("embed", 0);
-        CK(launch_k(laic::embed_kernel, dim3(nseq), dim3(256), 0, s, pdl, ep));
+        CK(launch_k(laic::embed_kernel, dim3(nseq, ecta), dim3(256), 0, s, pdl, ep));
         ++nl;
         t_end();
 
@@ -689,7 +715,10 @@ struct laic_dev {
             p.kv_slot_stride = kv_slot_stride; p.kv_cap = cap;
             t_begin("qkv", (double)ly.qkv.bytes() + 4.0 * nseq * (h + ly.qkv.rows));
             RecIn r_qkv;
-            if (recs) { r_qkv.xg = rec_x; r_qkv.mode = 1; r_qkv.ss = rec_ss; r_qkv.ss_tiles = l == 0 ? 1 : ntiles_h; }
+            if (recs || dprecs) {
+                r_qkv.xg = rec_x; r_qkv.mode = 1; r_qkv.ss = rec_ss; r_qkv.ss_tiles = l == 0 ? ecta : ntiles_h;
+                r_qkv.dp = dprecs;
+            }
             CK(launch_matvec(ly.qkv, p, laic::EPI_QKV, kv32, mvs, s, pdl, &nl, &r_qkv, !recs));
             t_end();
             // attention
@@ -699,6 +728,7 @@ struct laic_dev {
             ap.heads = H; ap.kv_heads = Hkv; ap.slots = d_slots; ap.pos = pos; ap.nsplit = nsplit;
             ap.part = attn_part; ap.counters = attn_cnt; ap.sqrt_d = sqrtf((float)D); ap.err = mvs.err;
             ap.nseq = nseq; ap.rec_out = recs ? rec_attn : nullptr; ap.nbuf = attn_nbuf(nseq);
+            if (dprecs) { ap.rec_dp = rec_attn; ap.rec_type = ly.o.type; }
             t_begin("attention", attn_bytes);
             if (attn_cluster(nsplit, kv32))
                 CK(laic::launch_cluster_k(attn_pick(D, G, kv32, true), dim3(nsplit, Hkv, nseq), dim3(laic::kAttnWarps * 32),
@@ -712,7 +742,10 @@ struct laic_dev {
             laic::MvParams po{};
             po.nseq = nseq; po.x = attn; po.ldx = hq; po.out = x; po.ldo = h;
             RecIn r_o;
-            if (recs) { po.rec_out = rec_x; po.rec_w = ly.ffn_norm; po.ss_out = rec_ss; r_o.xg = rec_attn; r_o.mode = 2; }
+            if (recs || dprecs) {
+                po.rec_out = rec_x; po.rec_w = ly.ffn_norm; po.ss_out = rec_ss; r_o.xg = rec_attn; r_o.mode = 2;
+                po.rec_type = ly.gu.type; r_o.dp = dprecs;
+            }
             t_begin("o", (double)ly.o.bytes() + 4.0 * nseq * hq + 8.0 * nseq * h);
             CK(launch_matvec(ly.o, po, residual_epi, kv32, mvs, s, pdl, &nl, &r_o, !recs));
             t_end();
@@ -721,7 +754,10 @@ struct laic_dev {
             laic::MvParams pg{};
             pg.nseq = nseq; pg.eps = a.rms_eps; pg.x = x; pg.ldx = h; pg.norm_w = ly.ffn_norm; pg.out = act; pg.ldo = F;
             RecIn r_gu;
-            if (recs) { r_gu.xg = rec_x; r_gu.mode = 1; r_gu.ss = rec_ss; r_gu.ss_tiles = ntiles_h; pg.rec_out = rec_act; }
+            if (recs || dprecs) {
+                r_gu.xg = rec_x; r_gu.mode = 1; r_gu.ss = rec_ss; r_gu.ss_tiles = ntiles_h; pg.rec_out = rec_act;
+                pg.rec_type = ly.down.type; r_gu.dp = dprecs;
+            }
             t_begin("gate_up", (double)ly.gu.bytes() + 4.0 * nseq * (h + F));
             CK(launch_matvec(ly.gu, pg, laic::EPI_SWIGLU, kv32, mvs, s, pdl, &nl, &r_gu, !recs));
             t_end();
@@ -729,10 +765,14 @@ struct laic_dev {
             laic::MvParams pd{};
             pd.nseq = nseq; pd.x = act; pd.ldx = F; pd.out = x; pd.ldo = h;
             RecIn r_dn;
-            if (recs) {
-                r_dn.xg = rec_act; r_dn.mode = 2;
+            if (recs || dprecs) {
+                r_dn.xg = rec_act; r_dn.mode = 2; r_dn.dp = dprecs;
                 pd.rec_out = rec_x; pd.ss_out = rec_ss;
                 pd.rec_w = l + 1 < L ? layers[l + 1].attn_norm : out_norm;  // next: QKV, or the lm_head
+                if (dprecs) {
+                    pd.rec_type = l + 1 < L ? layers[l + 1].qkv.type : lm_head().type;
+                    if (l + 1 == L && !dp_lm) pd.rec_out = nullptr;  // the lm_head normalises x itself
+                }
             }
             t_begin("down", (double)ly.down.bytes() + 4.0 * nseq * (F + 2 * h));
             CK(launch_matvec(ly.down, pd, residual_epi, kv32, mvs, s, pdl, &nl, &r_dn, !recs));
@@ -745,7 +785,9 @@ struct laic_dev {
             pl.out = tp > 1 ? logits_l : logits; pl.ldo = tp > 1 ? Vl : V;
             t_begin("lm_head", (double)lm_head().bytes() + 4.0 * nseq * (h + Vl));
             RecIn r_lm;
-            if (recs && L > 0) { r_lm.xg = rec_x; r_lm.mode = 1; r_lm.ss = rec_ss; r_lm.ss_tiles = ntiles_h; }
+            if ((recs || dp_lm) && L > 0) {
+                r_lm.xg = rec_x; r_lm.mode = 1; r_lm.ss = rec_ss; r_lm.ss_tiles = ntiles_h; r_lm.dp = dp_lm;
+            }
             // the lm_head only consumes: the team kernel (its own norm of x) where it is faster
             CK(launch_matvec(lm_head(), pl, laic::EPI_STORE, kv32, mvs, s, pdl, &nl, &r_lm,
                              !recs || nseq <= LAIC_LM_TEAM_MAX_BATCH));
@@ -1095,7 +1137,7 @@ int laic_dev_create(const laic_dev_desc* desc, const laic_dev_opts* opts, laic_d
     CK(cudaMemset(d->vc, 0, kv_bytes));
     CK(cudaMalloc(&d->pos, S * 4));
     CK(cudaMemset(d->pos, 0, S * 4));
-    if (d->tile_step(S)) {  // activation records between tile-kernel projections
+    if (d->tile_step(S) || d->tp == 1) {  // activation records between the projections
         CK(cudaMalloc(&d->rec_x, S * d->h * 4));
         CK(cudaMalloc(&d->rec_act, S * d->F * 4));
         CK(cudaMalloc(&d->rec_attn, S * d->hq * 4));

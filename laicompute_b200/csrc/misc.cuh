@@ -5,6 +5,7 @@
 #include "common.cuh"
 #include "tiles.cuh"
 #include "mma_matvec.cuh"  // store_act_record
+#include "mv_streamk.cuh"  // dp_lane_record_rt
 
 namespace laic {
 
@@ -23,28 +24,42 @@ struct EmbedParams {
     const float* rec_w;      // the first rmsnorm weight
     float* ss_out;           // [nseq]
     int nseq;
+    // optional, one sequence: the team kernel's integer records of x * rec_w (and ss_out)
+    uint8_t* rec_dp;
+    int rec_type;            // the consuming projection's weight type (T_Q4_0 or T_Q8_0)
 };
 
-// x[s] = row tokens[s] of token_embd; the token joins its slot's history.
+// x[s] = row tokens[s] of token_embd; the token joins its slot's history. Grid (nseq,
+// slices): CTA (s, y) takes slice y of the row (a multiple of blockDim.x elements) and
+// writes its sum of squares to ss_out[y * nseq + s].
 __global__ void embed_kernel(const EmbedParams p) {
     __shared__ float red[32];
     const int s = blockIdx.x;
+    const int per = ((p.hidden + gridDim.y - 1) / gridDim.y + blockDim.x - 1) / blockDim.x * blockDim.x;
+    const int lo = blockIdx.y * per, hi = min(p.hidden, lo + per);
     pdl_wait();
     const unsigned tok = p.tokens[s];
     float ss = 0.f;
-    for (int i = threadIdx.x; i < p.hidden; i += blockDim.x) {
-        const float v = tile_value(p.type, p.q, p.s, p.nb, (int)tok, i);
-        p.x[(size_t)s * p.hidden + i] = v;
-        if (p.rec_out) {
+    for (int ib = lo; ib < lo + per; ib += blockDim.x) {  // the same trip count in every thread
+        const int i = ib + threadIdx.x;
+        const bool in = i < hi;
+        const float v = in ? tile_value(p.type, p.q, p.s, p.nb, (int)tok, i) : 0.f;
+        if (in) p.x[(size_t)s * p.hidden + i] = v;
+        if (p.rec_out && in) {
             ss = fmaf(v, v, ss);
             store_act_record(p.rec_out, p.nseq, i, s, v * p.rec_w[i]);
         }
+        if (p.rec_dp) {  // whole warps: lanes 8j..8j+7 hold one 8-column group
+            ss = fmaf(v, v, ss);
+            dp_lane_record_rt(p.rec_type, in ? v * p.rec_w[i] : 0.f, 0.f, i & 7, in ? i >> 3 : -1, p.rec_dp, 1, 2, 4);
+        }
     }
-    if (p.rec_out) {
+    if (p.rec_out || p.rec_dp) {
         ss = block_sum(ss, red);
-        if (threadIdx.x == 0) p.ss_out[s] = ss;
+        if (threadIdx.x == 0) p.ss_out[(size_t)blockIdx.y * p.nseq + s] = ss;
     }
-    if (threadIdx.x == 0) atomicAdd(p.counts + (size_t)p.slots[s] * p.vocab + tok, 1u);  // rows may share a slot
+    if (threadIdx.x == 0 && blockIdx.y == 0)
+        atomicAdd(p.counts + (size_t)p.slots[s] * p.vocab + tok, 1u);  // rows may share a slot
     pdl_launch_dependents();
 }
 

@@ -75,6 +75,10 @@ struct MvParams {
     uint8_t* rec_out;          // records (rec_off) of rows or rows/2 elements (nullptr: none)
     const float* rec_w;        // EPI_ADD: the next rmsnorm weight (records of out * w), or nullptr
     float* ss_out;             // EPI_ADD: [row tiles][nseq] sums of squares of the new residual
+    // team kernel, one sequence (integer variant): `xg` may bring the integer digit records
+    // (scale_mode, ss, ss_tiles, ss_n as above) and `rec_out` receives them for the next
+    // projection, whose weight type is rec_type (T_Q4_0 or T_Q8_0)
+    int rec_type;
 };
 
 // Activation records (the tile and wide kernels' B operands): per GGUF block column bl

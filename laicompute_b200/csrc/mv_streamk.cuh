@@ -36,10 +36,10 @@ namespace laic {
 #define LAIC_SK_WARPS 16
 #endif
 #ifndef LAIC_SK_RING_BYTES
-#define LAIC_SK_RING_BYTES (9 * 1024)
+#define LAIC_SK_RING_BYTES 4608
 #endif
 #ifndef LAIC_SK_STAGE_BYTES
-#define LAIC_SK_STAGE_BYTES 4608
+#define LAIC_SK_STAGE_BYTES 2304
 #endif
 constexpr int kSkWarps = LAIC_SK_WARPS;          // warps per CTA
 constexpr int kSkRingBytes = LAIC_SK_RING_BYTES;  // per warp: stages in flight
@@ -103,6 +103,54 @@ template <int WT>
 __device__ __forceinline__ int dp_byte_of(int k) {
     if (WT == T_Q4_0) return (k & 1) * 4 + (k >> 1);
     return frag_pos(k);
+}
+
+// A producing epilogue makes the integer variant's records of the values it
+// writes for the next projection, one 8-column group per 8 lanes: `val` is this
+// lane's value (0 where none), `k` its index in the group and `gidx` the group
+// (negative: no record). The group's maximum, digit sum and the record bytes
+// follow dp_group_record; every lane of the warp must call it. Returns the
+// group's sum of `sq` (for the next rmsnorm), valid in the group's lane k = 0.
+template <int WT>
+__device__ __forceinline__ float dp_lane_record(float val, float sq, int k, int gidx, uint8_t* recs, int m1, int m2,
+                                                   int m3) {
+    float mx = fabsf(val);
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, m1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, m2));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, m3));
+    int ex = 0;
+    if (mx > 0.f && isfinite(mx)) frexpf(mx, &ex);
+    const int xi = (int)rintf(ldexpf(val, 20 - ex));
+    const int p2 = ((xi + 64) & 127) - 64;
+    const int t1 = (xi - p2) >> 7;
+    const int p1 = ((t1 + 64) & 127) - 64;
+    const int p0 = (t1 - p1) >> 7;
+    int gs = xi;
+    gs += __shfl_xor_sync(0xffffffffu, gs, m1);
+    gs += __shfl_xor_sync(0xffffffffu, gs, m2);
+    gs += __shfl_xor_sync(0xffffffffu, gs, m3);
+    sq += __shfl_xor_sync(0xffffffffu, sq, m1);
+    sq += __shfl_xor_sync(0xffffffffu, sq, m2);
+    sq += __shfl_xor_sync(0xffffffffu, sq, m3);
+    if (gidx >= 0) {
+        uint8_t* rec = recs + (size_t)gidx * 32;
+        const int pos = dp_byte_of<WT>(k);
+        rec[pos] = (uint8_t)(int8_t)p0;
+        rec[8 + pos] = (uint8_t)(int8_t)p1;
+        rec[16 + pos] = (uint8_t)(int8_t)p2;
+        if (k == 0) {
+            reinterpret_cast<int*>(rec)[6] = WT == T_Q4_0 ? -8 * gs : 0;
+            reinterpret_cast<float*>(rec)[7] = ldexpf(1.f, ex - 20);
+        }
+    }
+    return sq;
+}
+
+// The same for a consumer whose weight type is known at run time (T_Q4_0 or T_Q8_0).
+__device__ __forceinline__ float dp_lane_record_rt(int type, float val, float sq, int k, int gidx, uint8_t* recs, int m1,
+                                                   int m2, int m3) {
+    return type == T_Q4_0 ? dp_lane_record<T_Q4_0>(val, sq, k, gidx, recs, m1, m2, m3)
+                          : dp_lane_record<T_Q8_0>(val, sq, k, gidx, recs, m1, m2, m3);
 }
 
 // One 16x32 tile-block of the integer variant: rows g and g+8, columns 8c..8c+7.
@@ -370,8 +418,32 @@ __global__ void __launch_bounds__(kSkWarps * 32, 1) mv_sk_kernel(const MvParams 
     // ---- prologue: the whole activation vector -> binary16 hi/lo in fragment order
     //      (integer variant: int8 digit records, one warp per 32-column block)
     if constexpr (DP) {
-        dp_build_records<WT>(p.x, p.norm_w, p.eps, p.in, xs, wstat, inv);
-        if (threadIdx.x == 0) xsc[0] = 1.f;  // the digit scales are applied per block
+        if (p.xg) {
+            // records written by the producing kernel's epilogue (of x * norm weight, without
+            // the 1/rms): copy them in; the rmsnorm scale from the producer's partial sums
+            // multiplies the finished rows instead
+            const int nchunk = nb * (kDpRecBytes / 16);
+            for (int i = threadIdx.x; i < nchunk; i += blockDim.x) cp_async16(xs + i * 16, p.xg + (size_t)i * 16);
+            cp_async_commit();
+            if (warp == 0) {
+                float a = 0.f;
+                if (p.scale_mode == 1) {
+                    int t = lane;
+                    for (; t + 96 < p.ss_tiles; t += 128) {
+                        const float v0 = __ldcg(p.ss + t), v1 = __ldcg(p.ss + t + 32);
+                        const float v2 = __ldcg(p.ss + t + 64), v3 = __ldcg(p.ss + t + 96);
+                        a += (v0 + v1) + (v2 + v3);
+                    }
+                    for (; t < p.ss_tiles; t += 32) a += __ldcg(p.ss + t);
+                    a = warp_sum(a);
+                }
+                if (lane == 0) xsc[0] = p.scale_mode == 1 ? 1.f / sqrtf(a / float(p.ss_n) + p.eps) : 1.f;
+            }
+            cp_async_wait_all();
+        } else {
+            dp_build_records<WT>(p.x, p.norm_w, p.eps, p.in, xs, wstat, inv);
+            if (threadIdx.x == 0) xsc[0] = 1.f;  // the digit scales are applied per block
+        }
         __syncthreads();
     } else {
         const int nv = p.in >> 2;  // float4 per sequence
@@ -523,6 +595,29 @@ __global__ void __launch_bounds__(kSkWarps * 32, 1) mv_sk_kernel(const MvParams 
             }
         }
         __syncwarp();
+        if constexpr (DP && (EPI == EPI_ADD || EPI == EPI_SWIGLU)) {
+            if (p.rec_out) {  // the integer records of this tile's outputs for the next projection
+                if (EPI == EPI_ADD) {
+                    // rows r0 + lane (lanes 0..15 wrote them above): records of x * next norm
+                    // weight (groups 2t, 2t + 1) and the tile's sum of x^2
+                    const int r = r0 + lane;
+                    const bool live = lane < 16 && r < p.rows;
+                    const float xn = live ? p.out[r] : 0.f;
+                    const float wv = live && p.rec_w ? p.rec_w[r] : 1.f;
+                    const float sg = dp_lane_record_rt(p.rec_type, live ? xn * wv : 0.f, xn * xn, lane & 7,
+                                                       live ? (r >> 3) : -1, p.rec_out, 1, 2, 4);
+                    const float s8 = __shfl_sync(0xffffffffu, sg, 8);
+                    if (lane == 0 && p.ss_out) p.ss_out[t] = sg + s8;
+                } else {
+                    // outputs r0 / 2 + lane / 2 on the even lanes 0..14: group t
+                    const int o = (r0 >> 1) + (lane >> 1);
+                    const bool live = lane < 16 && (lane & 1) == 0 && r0 + lane < p.rows;
+                    const float a = live ? p.out[o] : 0.f;
+                    dp_lane_record_rt(p.rec_type, a, 0.f, lane >> 1, live ? (o >> 3) : -1, p.rec_out, 2, 4, 8);
+                }
+                __syncwarp();
+            }
+        }
     };
 
     // ---- stream this warp's slices

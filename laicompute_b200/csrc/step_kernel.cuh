@@ -53,7 +53,7 @@ struct StepParams {
     unsigned* counters; // [kv_heads] tickets, zero between launches
     unsigned* bar;      // grid barrier arrivals, zero at launch
     int* err;
-    // activation digit records made by the producing phase's epilogue (see step_group_record)
+    // activation digit records made by the producing phase's epilogue (see dp_lane_record)
     uint8_t* rec_x;     // [h / 8][32 B]: residual x times the next rmsnorm weight (next GU or QKV)
     uint8_t* rec_act;   // [F / 8][32 B]: SwiGLU output (next DOWN)
     float* ss_x;        // [h / 8] sums of squares of x per 8-column group (the next rmsnorm)
@@ -94,47 +94,6 @@ __device__ __forceinline__ void step_grid_sync(unsigned* bar, unsigned target, i
         }
     }
     __syncthreads();
-}
-
-// The epilogue of a projection tile makes the digit records of the values it
-// produces for the next phase, one 8-column group per 8 lanes: `val` is this
-// lane's value (0 where none), `k` its index in the group and `gidx` the group
-// (negative: no record). The group's maximum, digit sum and the record bytes
-// follow dp_group_record; every lane of the warp must call it. Returns the
-// group's sum of `sq` (for the next rmsnorm), valid in the group's lane k = 0.
-template <int WT>
-__device__ __forceinline__ float step_group_record(float val, float sq, int k, int gidx, uint8_t* recs, int m1, int m2,
-                                                   int m3) {
-    float mx = fabsf(val);
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, m1));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, m2));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, m3));
-    int ex = 0;
-    if (mx > 0.f && isfinite(mx)) frexpf(mx, &ex);
-    const int xi = (int)rintf(ldexpf(val, 20 - ex));
-    const int p2 = ((xi + 64) & 127) - 64;
-    const int t1 = (xi - p2) >> 7;
-    const int p1 = ((t1 + 64) & 127) - 64;
-    const int p0 = (t1 - p1) >> 7;
-    int gs = xi;
-    gs += __shfl_xor_sync(0xffffffffu, gs, m1);
-    gs += __shfl_xor_sync(0xffffffffu, gs, m2);
-    gs += __shfl_xor_sync(0xffffffffu, gs, m3);
-    sq += __shfl_xor_sync(0xffffffffu, sq, m1);
-    sq += __shfl_xor_sync(0xffffffffu, sq, m2);
-    sq += __shfl_xor_sync(0xffffffffu, sq, m3);
-    if (gidx >= 0) {
-        uint8_t* rec = recs + (size_t)gidx * 32;
-        const int pos = dp_byte_of<WT>(k);
-        rec[pos] = (uint8_t)(int8_t)p0;
-        rec[8 + pos] = (uint8_t)(int8_t)p1;
-        rec[16 + pos] = (uint8_t)(int8_t)p2;
-        if (k == 0) {
-            reinterpret_cast<int*>(rec)[6] = WT == T_Q4_0 ? -8 * gs : 0;
-            reinterpret_cast<float*>(rec)[7] = ldexpf(1.f, ex - 20);
-        }
-    }
-    return sq;
 }
 
 // Shared memory of the step kernel: rings, a region shared by the activation
@@ -365,7 +324,7 @@ __global__ void __launch_bounds__(kSkWarps * 32, 1) step_kernel(const StepParams
                     if (live) p.x[r] = xn;
                     const float* nwn = mk == SK_O ? ly.ffn_norm : (l + 1 < p.L ? p.layers[l + 1].attn_norm : nullptr);
                     if (nwn) {
-                        const float ssg = step_group_record<WT>(live ? xn * nwn[r] : 0.f, xn * xn, lane & 7,
+                        const float ssg = dp_lane_record<WT>(live ? xn * nwn[r] : 0.f, xn * xn, lane & 7,
                                                                 live ? (r >> 3) : -1, p.rec_x, 1, 2, 4);
                         if (live && (lane & 7) == 0) p.ss_x[r >> 3] = ssg;
                     }
@@ -374,7 +333,7 @@ __global__ void __launch_bounds__(kSkWarps * 32, 1) step_kernel(const StepParams
                     const bool live = lane < 16 && (lane & 1) == 0 && r < mv.rows;
                     const float av = live ? (v / (1.f + expf(-v))) * vo2 : 0.f;
                     if (live) p.act[r >> 1] = av;
-                    step_group_record<WT>(av, 0.f, lane >> 1, live ? t : -1, p.rec_act, 2, 4, 8);
+                    dp_lane_record<WT>(av, 0.f, lane >> 1, live ? t : -1, p.rec_act, 2, 4, 8);
                 } else if (lane < 16 && r < mv.rows) {  // QKV: RoPE on q and k, then q out and K/V appended
                         const int sl = p.slots[0], ps = p.pos[sl];
                         int rr = r, region = 0;

@@ -85,14 +85,15 @@ def test_per_sequence_sampling_params():
     assert np.array_equal(np.array(b, dtype=np.uint32), g["ids_full"])
 
 
-@pytest.mark.parametrize("nseq", [1, 4, 17])
-def test_large_layer_model_matches_oracle(nseq):
+@pytest.mark.parametrize("nseq,wt", [(1, "q4_0"), (1, "q8_0"), (4, "q4_0"), (17, "q4_0")])
+def test_large_layer_model_matches_oracle(nseq, wt):
     """A model whose layers are above the small-layer bound: batches up to 16 run the
-    team kernel (one sequence: its integer dot products), larger ones the tile kernel
-    with activation records; logits within 1e-3 of max|logit|, greedy ids identical."""
+    team kernel (one sequence: its integer dot products, with the digit records written
+    by each producing kernel's epilogue), larger ones the tile kernel with activation
+    records; logits within 1e-3 of max|logit|, greedy ids identical."""
     from laicompute_b200 import gguf, synth
-    a = synth.tiny_arch(gguf.Q4_0, None, layers=2, vocab=512, ctx=64, name="big", hidden=1024, heads=8, kv_heads=2,
-                        ffn=5120)
+    a = synth.tiny_arch({"q4_0": gguf.Q4_0, "q8_0": gguf.Q8_0}[wt], None, layers=2, vocab=512, ctx=64, name="big",
+                        hidden=1024, heads=8, kv_heads=2, ffn=5120)
     with tempfile.TemporaryDirectory() as d:
         path = synth.write_model(os.path.join(d, "m.gguf"), a, seed=71)
         m = O.OracleModel(path)
