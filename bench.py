@@ -353,7 +353,7 @@ def main() -> None:
                              % (st.weight_bytes / 1e6, kv_read / 1e6)},
             "hbm_gbs_step": round((st.weight_bytes + kv_read) / (max_ms / args.steps * 1e-3) / 1e9, 1),
             "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s", "h2d_bytes_per_step": batch * (4 + 4 + 24),
-                    "d2h_bytes_per_step": batch * 4},
+                    "d2h_bytes_per_step": batch * 4 + 8},
             "gpu_launches": int(args.steps * launches_chained),
             "prefill": {"tokens_per_s": round(batch * (plen - 1) / prefill_s, 1), "prompt_tokens": plen - 1,
                         "sequences": batch, "batched": tp == 1, "timing": "host wall clock, engine synchronised"},

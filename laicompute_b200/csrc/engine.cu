@@ -500,6 +500,7 @@ struct laic_dev {
     size_t hist_cap = 0;  // entries of d_hist
     laic::SampleDev* d_params = nullptr;
     unsigned *h_tokens = nullptr, *h_out_ids = nullptr;
+    int* h_err = nullptr;  // pinned: the step's copies of the two device error flags (matvec waits, sampler)
     int* h_slots = nullptr;
     laic::SampleDev* h_params = nullptr;
     std::vector<long long> h_pos;
@@ -814,8 +815,12 @@ struct laic_dev {
                 CK(launch_k(laic::record_ids_kernel, dim3(1), dim3(256), 0, s, pdl, (const unsigned*)d_out_ids, d_hist,
                             d_hist_count, nseq));
                 ++nl;
-            } else
+            } else {
+                // the sampled ids and both error flags come back with the step (no extra round trip)
                 CK(cudaMemcpyAsync(h_out_ids, d_out_ids, nseq * sizeof(unsigned), cudaMemcpyDeviceToHost, s));
+                CK(cudaMemcpyAsync(h_err, mvs.err, 4, cudaMemcpyDeviceToHost, s));
+                CK(cudaMemcpyAsync(h_err + 1, d_err, 4, cudaMemcpyDeviceToHost, s));
+            }
         } else {
             t_begin("advance", 0);
             CK(launch_k(laic::advance_pos_kernel, dim3(1), dim3(256), 0, s, pdl, (const int*)d_slots, pos, nseq));
@@ -1173,6 +1178,8 @@ int laic_dev_create(const laic_dev_desc* desc, const laic_dev_opts* opts, laic_d
     CK(cudaMalloc(&d->d_params, S * sizeof(laic::SampleDev)));
     CK(cudaMallocHost(&d->h_tokens, S * 4));
     CK(cudaMallocHost(&d->h_out_ids, S * 4));
+    CK(cudaMallocHost(&d->h_err, 2 * sizeof(int)));
+    d->h_err[0] = d->h_err[1] = 0;
     CK(cudaMallocHost(&d->h_slots, S * 4));
     CK(cudaMallocHost(&d->h_params, S * sizeof(laic::SampleDev)));
     if (tp > 1) {
@@ -1215,7 +1222,7 @@ void laic_dev_destroy(laic_dev* d) {
                     d->pf_x, d->pf_c, d->pf_q, d->pf_attn, d->pf_a, d->pf_w, d->pf_slots, d->pf_npos, d->pf_tokens,
                     d->pf_ws};
     for (void* b : bufs) if (b) cudaFree(b);
-    void* hb[] = {d->h_tokens, d->h_out_ids, d->h_slots, d->h_params};
+    void* hb[] = {d->h_tokens, d->h_out_ids, d->h_slots, d->h_params, d->h_err};
     for (void* b : hb) if (b) cudaFreeHost(b);
     if (d->st) cudaStreamDestroy(d->st);
     delete d;
@@ -1383,6 +1390,22 @@ static int fill_params(laic_dev* d, int32_t nseq, const laic_sample_params* para
     return LAIC_OK;
 }
 
+// After a synchronised MODE_STEP run: the error flags its graph copied to pinned memory.
+static int check_step_err(laic_dev* d) {
+    const int mv_err = d->h_err[0], sample_err = d->h_err[1];
+    if (mv_err) {
+        CK(cudaMemset(d->mvs.err, 0, 4));
+        d->h_err[0] = 0;
+        return fail(LAIC_E_CUDA, "a matvec pipeline wait timed out");
+    }
+    if (sample_err) {
+        CK(cudaMemset(d->d_err, 0, 4));
+        d->h_err[1] = 0;
+        return fail(LAIC_E_UNSUPPORTED, "sampling request needs more than 1024 candidates (top_k or top_p mass)");
+    }
+    return LAIC_OK;
+}
+
 static int check_sampler_err(laic_dev* d) {
     int err = 0;
     if (d->mvs.err) {
@@ -1412,7 +1435,7 @@ int laic_dev_step(laic_dev* d, int32_t nseq, const uint32_t* tokens, const int32
         CK(cudaMemcpyAsync(out_logits, d->logits, (size_t)nseq * d->V * 4, cudaMemcpyDeviceToHost, d->st));
     CK(cudaStreamSynchronize(d->st));
     for (int i = 0; i < nseq; ++i) d->h_pos[slots[i]] += 1;
-    if ((rc = check_sampler_err(d))) return rc;
+    if ((rc = check_step_err(d))) return rc;
     if (out_ids) std::memcpy(out_ids, d->h_out_ids, nseq * 4);
     return LAIC_OK;
 }

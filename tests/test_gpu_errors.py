@@ -63,3 +63,21 @@ def test_missing_tensor_reported_by_name():
         assert lib().laic_last_error().decode() == "missing tensor: blk.1.ffn_up.weight"
     finally:
         lib().laic_dev_destroy(h)
+
+
+def test_sampler_candidate_limit_reported_then_cleared():
+    """A top-k request above the sampler's 1024 candidates fails that step with
+    LAIC_E_UNSUPPORTED (the flag travels back with the step's own copies); the next
+    step runs normally."""
+    from laicompute_b200 import gguf, synth
+    from laicompute_b200._native import LAIC_E_UNSUPPORTED, LaicError
+    from laicompute_b200.engine import Engine, sample_params
+    arch = synth.tiny_arch(gguf.F16, hidden=64, heads=2, kv_heads=1, ffn=64, vocab=4096, ctx=32, name="v4k")
+    with tempfile.TemporaryDirectory() as d:
+        e = Engine(synth.write_model(os.path.join(d, "m.gguf"), arch, seed=3))
+        e.step([1], [0])
+        with pytest.raises(LaicError) as ex:
+            e.step([2], [0], sample_params(1.0, 2000, 1.0, 1.0, 5))
+        assert ex.value.code == LAIC_E_UNSUPPORTED and "1024 candidates" in str(ex.value)
+        out, _ = e.step([3], [0])
+        assert 0 <= int(out[0]) < arch.vocab
