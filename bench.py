@@ -9,7 +9,9 @@ ids each, then decode steps. One "step" = one token for every sequence.
          feeds every sequence its own sampled id without leaving the device),
          CUDA events on the engine stream, max over ranks
   e2e    tokens/s of K laic_dev_step calls (the C ABI a caller uses): host ids
-         in through pinned memory, sampled ids back to the host, every step
+         in through pinned memory, sampled ids back to the host, every step;
+         the sequences start again from their prompts first, so both numbers
+         cover the same positions
 
 Multi-GPU (torchrun, one rank per GPU): the 135M model does not shard per
 layer, so every rank decodes its own 64 sequences (replicas, weak scaling).
@@ -272,18 +274,25 @@ def main() -> None:
         params = [sample_params(0.8, 40, 1.0, 1.0, 4242 + 1000 * seq_rank + i) for i in range(batch)]
     else:
         params = [sample_params()] * batch
-    # the prompts (all but their last token) in batched passes, timed as a side figure
-    torch.cuda.synchronize()
-    t_pf = time.perf_counter()
-    if tp > 1:
-        for j in range(plen - 1):
-            eng.prefill(prompts[:, j], slots)
-    else:
+    def start_sequences():
+        """Every slot from empty: the prompts (all but their last token) in batched passes,
+        then the first decode step; returns that step's ids and the prefill seconds."""
         for i in range(batch):
-            eng.prefill_batch(prompts[i, :-1], int(slots[i]))
-    eng.sync()
-    prefill_s = time.perf_counter() - t_pf
-    first, _ = eng.step(prompts[:, -1], slots, params)
+            eng.reset_slot(int(slots[i]))
+        torch.cuda.synchronize()
+        t_pf = time.perf_counter()
+        if tp > 1:
+            for j in range(plen - 1):
+                eng.prefill(prompts[:, j], slots)
+        else:
+            for i in range(batch):
+                eng.prefill_batch(prompts[i, :-1], int(slots[i]))
+        eng.sync()
+        pf_s = time.perf_counter() - t_pf
+        ids0, _ = eng.step(prompts[:, -1], slots, params)
+        return ids0, pf_s
+
+    first, prefill_s = start_sequences()  # the prefill is timed as a side figure
 
     # ---- device-resident decode loop (value)
     ids_w, _ = eng.decode(first, slots, params, steps=args.warmup)
@@ -304,9 +313,11 @@ def main() -> None:
     tok = ids[-1]
     launches_chained = eng.stats().launches_per_step  # kernels per chained step, as timed
 
-    # ---- end to end through laic_dev_step: host ids in, sampled ids out, every step
+    # ---- end to end through laic_dev_step: host ids in, sampled ids out, every step, over the
+    #      same positions as the device-resident loop (the sequences start again from the prompt)
     ext = torch.cuda.ExternalStream(eng.stream, device=torch.device("cuda", local))
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    tok, _ = start_sequences()
     for _ in range(args.warmup):
         tok, _ = eng.step(tok, slots, params)
     barrier(world)
