@@ -501,6 +501,9 @@ struct laic_dev {
     laic::SampleDev* d_params = nullptr;
     unsigned *h_tokens = nullptr, *h_out_ids = nullptr;
     int* h_err = nullptr;  // pinned: the step's copies of the two device error flags (matvec waits, sampler)
+    float* samp_v = nullptr;  // sampler slices: [S][kSampleSlices] maxima, ids and per-sequence tickets
+    int* samp_i = nullptr;
+    unsigned* samp_cnt = nullptr;
     int* h_slots = nullptr;
     laic::SampleDev* h_params = nullptr;
     std::vector<long long> h_pos;
@@ -805,9 +808,12 @@ struct laic_dev {
                 }
                 t_end();
             }
-            laic::SamplerParams sp{logits, V, V, d_slots, counts, d_params, nseq, d_out_ids, d_tokens, pos, d_err};
+            laic::SamplerParams sp{logits, V, V, d_slots, counts, d_params, nseq, d_out_ids, d_tokens, pos, d_err,
+                                   samp_v, samp_i, samp_cnt};
+            // a few sequences: the vocabulary's argmax over several CTAs per sequence
+            const int sp_slices = nseq <= 4 ? laic::kSampleSlices : 1;
             t_begin("sampler", (double)nseq * V * 4);
-            CK(launch_k(laic::sample_kernel, dim3(nseq), dim3(laic::kSampleThreads), 0, s, pdl, sp));
+            CK(launch_k(laic::sample_kernel, dim3(nseq, sp_slices), dim3(laic::kSampleThreads), 0, s, pdl, sp));
             ++nl;
             t_end();
             if (mode == MODE_CHAIN)
@@ -1174,6 +1180,10 @@ int laic_dev_create(const laic_dev_desc* desc, const laic_dev_opts* opts, laic_d
     CK(cudaMalloc(&d->d_slots, S * 4));
     CK(cudaMalloc(&d->d_err, 4));
     CK(cudaMemset(d->d_err, 0, 4));
+    CK(cudaMalloc(&d->samp_v, S * laic::kSampleSlices * 4));
+    CK(cudaMalloc(&d->samp_i, S * laic::kSampleSlices * 4));
+    CK(cudaMalloc(&d->samp_cnt, S * 4));
+    CK(cudaMemset(d->samp_cnt, 0, S * 4));
     CK(cudaMalloc(&d->d_hist_count, 4));
     CK(cudaMalloc(&d->d_params, S * sizeof(laic::SampleDev)));
     CK(cudaMallocHost(&d->h_tokens, S * 4));
@@ -1220,7 +1230,7 @@ void laic_dev_destroy(laic_dev* d) {
                     d->d_hist, d->d_hist_count, d->logits_l, d->logits_g, d->d_step_layers, d->step_bar,
                     d->step_rec_x, d->step_rec_act, d->step_ss, d->rec_x, d->rec_act, d->rec_ss, d->rec_attn, d->ar_box, d->ar_flags, d->ar_ctr,
                     d->pf_x, d->pf_c, d->pf_q, d->pf_attn, d->pf_a, d->pf_w, d->pf_slots, d->pf_npos, d->pf_tokens,
-                    d->pf_ws};
+                    d->pf_ws, d->samp_v, d->samp_i, d->samp_cnt};
     for (void* b : bufs) if (b) cudaFree(b);
     void* hb[] = {d->h_tokens, d->h_out_ids, d->h_slots, d->h_params, d->h_err};
     for (void* b : hb) if (b) cudaFreeHost(b);

@@ -42,9 +42,15 @@ struct SamplerParams {
     unsigned* next_tokens; // [nseq] the sampled id is also the next step's input token
     int* pos;              // [max_seqs]
     int* err;              // set to 1 when a request exceeds the sampler's candidate limit
+    // grid.y > 1 (few sequences): each CTA takes a slice of the vocabulary for the argmax, the
+    // last to finish (atomic ticket) combines the slices and runs the rest for the sequence
+    float* part_v;         // [nseq][grid.y] slice maxima (scratch)
+    int* part_i;           // [nseq][grid.y] their ids
+    unsigned* part_cnt;    // [nseq] tickets, zero between launches
 };
 
 constexpr int kSampleThreads = 1024;
+constexpr int kSampleSlices = 16;  // CTAs per sequence for the argmax when a step has few sequences
 constexpr int kMaxCand = 1024;
 
 __device__ __forceinline__ float penalized(float l, unsigned c, float rp) {
@@ -116,12 +122,14 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplerPar
         if (v > bv || bi == 0x7fffffff) { bv = v; bi = i; }
     };
     const bool vec = (V % 4 == 0) && (p.ldl % 4 == 0);
+    const int P = gridDim.y;
     if (vec) {
         const float4* lg4 = reinterpret_cast<const float4*>(lg);
         const uint4* cn4 = reinterpret_cast<const uint4*>(cnt);
         const int V4 = V / 4;
+        const int per = (V4 + P - 1) / P, f_lo = blockIdx.y * per, f_hi = min(V4, f_lo + per);
 #pragma unroll 8
-        for (int i4 = tid; i4 < V4; i4 += kSampleThreads) {
+        for (int i4 = f_lo + tid; i4 < f_hi; i4 += kSampleThreads) {
             float4 v = lg4[i4];
             if (pen) {
                 const uint4 c = cn4[i4];
@@ -131,7 +139,8 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplerPar
             consider(v.x, 4 * i4); consider(v.y, 4 * i4 + 1); consider(v.z, 4 * i4 + 2); consider(v.w, 4 * i4 + 3);
         }
     } else {
-        for (int i = tid; i < V; i += kSampleThreads) consider(L(i), i);
+        const int per = (V + P - 1) / P, e_lo = blockIdx.y * per, e_hi = min(V, e_lo + per);
+        for (int i = e_lo + tid; i < e_hi; i += kSampleThreads) consider(L(i), i);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -153,6 +162,31 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplerPar
         if (lane == 0) { redv[0] = bv; redi[0] = bi; }
     }
     __syncthreads();
+    if (P > 1) {  // this slice's maximum; the last CTA of the sequence goes on with all of them
+        __shared__ int sh_last;
+        if (tid == 0) {
+            p.part_v[(size_t)seq * P + blockIdx.y] = redv[0];
+            p.part_i[(size_t)seq * P + blockIdx.y] = redi[0];
+            __threadfence();
+            sh_last = atomicAdd(p.part_cnt + seq, 1u) == (unsigned)(P - 1);
+        }
+        __syncthreads();
+        if (!sh_last) return;
+        if (tid == 0) {
+            __threadfence();
+            float v = -INFINITY;
+            int id = 0x7fffffff;
+            for (int y = 0; y < P; ++y) {  // slices in id order: a strict > keeps the first maximum
+                const float vy = __ldcg(p.part_v + (size_t)seq * P + y);
+                const int iy = __ldcg(p.part_i + (size_t)seq * P + y);
+                if (iy != 0x7fffffff && (vy > v || id == 0x7fffffff)) { v = vy; id = iy; }
+            }
+            redv[0] = v;
+            redi[0] = id;
+            p.part_cnt[seq] = 0u;
+        }
+        __syncthreads();
+    }
     const float vmax = redv[0];
     const int imax = redi[0];
 
