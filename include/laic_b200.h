@@ -192,6 +192,24 @@ LAIC_API int laic_tensor_dequant(laic_tensor* t, float* out_dev, void* stream);
 /* Device bytes of the tensor's blocks (the algorithmic bytes of one matvec). */
 LAIC_API uint64_t laic_tensor_bytes(laic_tensor* t);
 
+/* Error status of the single-tensor kernels. Their bounded device waits (a
+ * bulk copy that never lands, a partial-sum slot never released) do not fault
+ * the GPU: they set an error word and the kernel returns, leaving y
+ * incomplete. laic_tensor_matvec and laic_tensor_matvec_noalloc return before
+ * their kernels run, so they cannot see it; this call synchronises `stream`,
+ * reads the word of the tensor's own scratch and of the device's fixed array,
+ * clears them and returns LAIC_E_CUDA with the wait's description if either
+ * was set (LAIC_OK otherwise). No counterpart in the reference. */
+LAIC_API int laic_tensor_check(laic_tensor* t, void* stream);
+
+/* Self-test of the bounded-wait error path on one GPU: runs the tensor-parallel
+ * allreduce kernel as rank 0 of two against a peer mailbox that nothing ever
+ * writes, with a flag-wait limit of `spin_cycles` SM clocks. The wait runs out,
+ * the kernel records its code (4, peer never published) in *code and returns;
+ * the call returns LAIC_E_CUDA with that message and the context stays usable.
+ * No counterpart in the reference. */
+LAIC_API int laic_selftest_peer_timeout(int32_t device, int64_t spin_cycles, int32_t* code);
+
 /* Bytes of the fixed working-memory array behind laic_tensor_matvec_noalloc (per device). */
 #define LAIC_FIXED_SCRATCH_BYTES (8u << 20)
 /* Same product as laic_tensor_matvec, for hosts that must not allocate device
@@ -200,11 +218,14 @@ LAIC_API uint64_t laic_tensor_bytes(laic_tensor* t);
  * working memory is one array of LAIC_FIXED_SCRATCH_BYTES compiled into the
  * library; a matrix/batch that needs more returns LAIC_E_INVALID with the size
  * in laic_last_error(). The first call on a device looks up the array's address
- * (setup) and should come before any stream capture. All calls on a device
- * share the array, which keeps the last call's contents (the parts that must
- * start at zero are cleared on `stream` by every call); calls that overlap in
- * time race on it, so order them on one stream. No counterpart in the
- * reference, whose matvec runs on the host. */
+ * (setup) and should come before any stream capture; the address is kept for
+ * the life of the process, so the library must not be used across a
+ * cudaDeviceReset. All calls on a device share the array, which keeps the last
+ * call's contents (the split-K tickets, which must start at zero, are cleared
+ * on `stream` by every call); calls that overlap in time race on it, so order
+ * them on one stream. A device wait that runs out is reported only through
+ * laic_tensor_check. No counterpart in the reference, whose matvec runs on the
+ * host. */
 LAIC_API int laic_tensor_matvec_noalloc(laic_tensor* t, const float* x_dev, float* y_dev, int32_t batch,
                                         void* stream);
 

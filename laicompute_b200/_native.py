@@ -20,7 +20,7 @@ EXPORTS = (
     "laic_dev_reset_slot", "laic_dev_slot_pos", "laic_dev_fill_kv", "laic_dev_sync", "laic_dev_stats_get",
     "laic_dev_stream", "laic_dev_decode", "laic_dev_profile", "laic_nccl_unique_id", "laic_tensor_create", "laic_tensor_destroy",
     "laic_tensor_matvec", "laic_tensor_dequant", "laic_tensor_bytes", "laic_tensor_matvec_noalloc",
-    "laic_dev_prefill_batch",
+    "laic_dev_prefill_batch", "laic_tensor_check", "laic_selftest_peer_timeout",
 )
 
 
@@ -99,10 +99,13 @@ def lib() -> ctypes.CDLL:
     L.laic_tensor_bytes.argtypes = [P]
     L.laic_tensor_bytes.restype = U64
     L.laic_tensor_matvec_noalloc.argtypes = [P, P, P, I32, P]
+    L.laic_tensor_check.argtypes = [P, P]
+    L.laic_selftest_peer_timeout.argtypes = [I32, ctypes.c_int64, ctypes.POINTER(I32)]
     for name in ("laic_dev_create", "laic_dev_upload", "laic_dev_prefill", "laic_dev_step", "laic_dev_reset_slot",
                  "laic_dev_slot_pos", "laic_dev_fill_kv", "laic_dev_sync", "laic_dev_stats_get",
                  "laic_dev_decode", "laic_dev_profile", "laic_nccl_unique_id", "laic_tensor_create", "laic_tensor_matvec",
-                 "laic_tensor_dequant", "laic_tensor_matvec_noalloc", "laic_dev_prefill_batch"):
+                 "laic_tensor_dequant", "laic_tensor_matvec_noalloc", "laic_dev_prefill_batch", "laic_tensor_check",
+                 "laic_selftest_peer_timeout"):
         getattr(L, name).restype = I32
     _lib = L
     return L

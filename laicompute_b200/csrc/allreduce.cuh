@@ -33,6 +33,7 @@ struct ArParams {
     unsigned* epoch;                // this rank's call counter
     unsigned* done;                 // this rank's finished-CTA counter (zero between calls)
     int* err;                       // set when a wait runs out
+    long long spin_limit;           // clock cycles a flag wait may take (0: about one second)
 };
 
 __global__ void __launch_bounds__(kArThreads) allreduce_oneshot_kernel(const ArParams p) {
@@ -61,11 +62,12 @@ __global__ void __launch_bounds__(kArThreads) allreduce_oneshot_kernel(const ArP
     if (threadIdx.x < p.ranks) {
         const unsigned* f = p.flags[p.rank] + ((size_t)buf * p.ranks + threadIdx.x) * kArCtas + c;
         const long long t0 = clock64();
+        const long long spin = p.spin_limit > 0 ? p.spin_limit : 2000000000LL;
         unsigned v;
         while (true) {
             asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
             if (v == ep) break;
-            if (clock64() - t0 > 2000000000LL) { atomicExch(p.err, 4); break; }
+            if (clock64() - t0 > spin) { atomicExch(p.err, kErrPeerFlag); break; }
         }
     }
     __syncthreads();

@@ -14,6 +14,16 @@ enum : int { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q8_0 = 8 };
 
 constexpr int kWarp = 32;
 
+// Codes a bounded device wait writes into its launch's error word when it runs
+// out (about one second of SM clocks); the host turns them into messages.
+enum : int {
+    kErrMbarrier = 1,     // a bulk copy into shared memory never completed (mbarrier wait)
+    kErrTeamMerge = 2,    // a warp team's partial-sum slot was never released
+    kErrGridBarrier = 3,  // a persistent kernel's grid barrier was not reached by every CTA
+    kErrPeerFlag = 4,     // a tensor-parallel peer never published its allreduce slice
+    kErrDepCounter = 5,   // a persistent kernel's dependency counter never reached its target
+};
+
 // Programmatic dependent launch: wait until the previous kernel in the stream
 // has completed (and its writes are visible); let the next kernel start early.
 // Both are no-ops when the launch did not use the PDL attribute.

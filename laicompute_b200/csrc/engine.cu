@@ -1400,13 +1400,25 @@ static int fill_params(laic_dev* d, int32_t nseq, const laic_sample_params* para
     return LAIC_OK;
 }
 
+// The message of a bounded device wait that ran out (the codes of common.cuh).
+static std::string wait_error_text(int code) {
+    switch (code) {
+    case laic::kErrMbarrier: return "device wait timed out: a bulk copy into shared memory never completed";
+    case laic::kErrTeamMerge: return "device wait timed out: a matvec warp team's partial-sum slot was never released";
+    case laic::kErrGridBarrier: return "device wait timed out: a decode-step grid barrier was not reached by every CTA";
+    case laic::kErrPeerFlag: return "device wait timed out: a tensor-parallel peer never published its allreduce slice";
+    case laic::kErrDepCounter: return "device wait timed out: a decode-step dependency counter never reached its target";
+    }
+    return "device wait timed out (code " + std::to_string(code) + ")";
+}
+
 // After a synchronised MODE_STEP run: the error flags its graph copied to pinned memory.
 static int check_step_err(laic_dev* d) {
     const int mv_err = d->h_err[0], sample_err = d->h_err[1];
     if (mv_err) {
         CK(cudaMemset(d->mvs.err, 0, 4));
         d->h_err[0] = 0;
-        return fail(LAIC_E_CUDA, "a matvec pipeline wait timed out");
+        return fail(LAIC_E_CUDA, wait_error_text(mv_err));
     }
     if (sample_err) {
         CK(cudaMemset(d->d_err, 0, 4));
@@ -1422,7 +1434,7 @@ static int check_sampler_err(laic_dev* d) {
         CK(cudaMemcpy(&err, d->mvs.err, 4, cudaMemcpyDeviceToHost));
         if (err) {
             CK(cudaMemset(d->mvs.err, 0, 4));
-            return fail(LAIC_E_CUDA, "a matvec pipeline wait timed out");
+            return fail(LAIC_E_CUDA, wait_error_text(err));
         }
     }
     CK(cudaMemcpy(&err, d->d_err, 4, cudaMemcpyDeviceToHost));
@@ -1653,8 +1665,11 @@ int laic_tensor_matvec(laic_tensor* t, const float* x, float* y, int32_t batch, 
     if (!t || !x || !y || batch < 1) return fail(LAIC_E_INVALID, "bad argument");
     CK(cudaSetDevice(t->device));
     if (batch > 64) return fail(LAIC_E_UNSUPPORTED, "at most 64 sequences per matvec");
-    int rc = mv_scratch_reserve(t->sc, mv_need(t->m, batch));
+    const MvNeed need = mv_need(t->m, batch);
+    int rc = mv_scratch_reserve(t->sc, need);
     if (rc) return rc;
+    // split-K tickets start at zero: a launch whose wait ran out may have left some raised
+    if (need.ntiles) CK(cudaMemsetAsync(t->sc.tile_cnt, 0, need.ntiles * 4, (cudaStream_t)stream));
     laic::MvParams p{};
     p.nseq = batch; p.x = x; p.ldx = t->m.in; p.out = y; p.ldo = t->m.rows;
     CK(launch_matvec(t->m, p, laic::EPI_STORE, false, t->sc, (cudaStream_t)stream, false));
@@ -1684,10 +1699,11 @@ int laic_tensor_dequant(laic_tensor* t, float* out, void* stream) {
 // this library instead of from the allocator.
 //
 // The array is shared by every call on a device and keeps whatever the last
-// call left in it; the ticket counters and the error flag, which must start
-// at zero, are cleared on the stream at the start of every call. Two calls
-// whose kernels overlap in time (different streams, or host threads without
-// ordering) race on the array.
+// call left in it; the ticket counters, which must start at zero, are cleared
+// on the stream at the start of every call. The error word at its start is
+// sticky: a bounded wait that runs out sets it, and only laic_tensor_check
+// reads and clears it. Two calls whose kernels overlap in time (different
+// streams, or host threads without ordering) race on the array.
 namespace {
 
 constexpr size_t kFixedScratchBytes = LAIC_FIXED_SCRATCH_BYTES;
@@ -1698,7 +1714,9 @@ std::mutex g_fixed_mu;
 unsigned char* g_fixed_base[kFixedMaxDevices] = {};
 
 // Device address of the array on `device` (which must be current); looked up
-// once per device, at that device's first call.
+// once per device, at that device's first call, and kept for the life of the
+// process (a cudaDeviceReset would invalidate it: the library does not support
+// being used across one).
 int fixed_scratch_base(int device, unsigned char** base) {
     if (device < 0 || device >= kFixedMaxDevices) return fail(LAIC_E_INVALID, "device ordinal out of range");
     std::lock_guard<std::mutex> lock(g_fixed_mu);
@@ -1723,9 +1741,9 @@ int laic_tensor_matvec_noalloc(laic_tensor* t, const float* x, float* y, int32_t
     CK(cudaSetDevice(t->device));
     if (batch > 64) return fail(LAIC_E_UNSUPPORTED, "at most 64 sequences per matvec");
     const MvNeed need = mv_need(t->m, batch);
-    // carve: [error flag | tickets] (cleared each call) [partials] [activations] [split scales]
-    const size_t zero_bytes = 256 + round256(need.ntiles * 4);
-    const size_t part_off = zero_bytes;
+    // carve: [error word (sticky)] [tickets (cleared each call)] [partials] [activations] [split scales]
+    const size_t zero_bytes = round256(need.ntiles * 4);
+    const size_t part_off = 256 + zero_bytes;
     const size_t xg_off = part_off + round256(need.part_floats * 4);
     const size_t xinv_off = xg_off + round256(need.xg_bytes);
     const size_t total = xinv_off + round256(need.xinv_floats * 4);
@@ -1737,7 +1755,7 @@ int laic_tensor_matvec_noalloc(laic_tensor* t, const float* x, float* y, int32_t
     int rc = fixed_scratch_base(t->device, &base);
     if (rc) return rc;
     const cudaStream_t st = (cudaStream_t)stream;
-    CK(cudaMemsetAsync(base, 0, zero_bytes, st));
+    if (zero_bytes) CK(cudaMemsetAsync(base + 256, 0, zero_bytes, st));
     MvScratch sc;
     sc.err = reinterpret_cast<int*>(base);
     sc.tile_cnt = reinterpret_cast<unsigned*>(base + 256);
@@ -1747,6 +1765,59 @@ int laic_tensor_matvec_noalloc(laic_tensor* t, const float* x, float* y, int32_t
     laic::MvParams p{};
     p.nseq = batch; p.x = x; p.ldx = t->m.in; p.out = y; p.ldo = t->m.rows;
     CK(launch_matvec(t->m, p, laic::EPI_STORE, false, sc, st, false));
+    return LAIC_OK;
+}
+
+int laic_tensor_check(laic_tensor* t, void* stream) {
+    if (!t) return fail(LAIC_E_INVALID, "bad argument");
+    CK(cudaSetDevice(t->device));
+    const cudaStream_t st = (cudaStream_t)stream;
+    CK(cudaStreamSynchronize(st));
+    int own = 0, fixed = 0;
+    if (t->sc.err) CK(cudaMemcpy(&own, t->sc.err, 4, cudaMemcpyDeviceToHost));
+    unsigned char* base = nullptr;
+    if (int rc = fixed_scratch_base(t->device, &base)) return rc;
+    CK(cudaMemcpy(&fixed, base, 4, cudaMemcpyDeviceToHost));
+    if (own) CK(cudaMemset(t->sc.err, 0, 4));
+    if (fixed) CK(cudaMemset(base, 0, 4));
+    if (own || fixed) return fail(LAIC_E_CUDA, wait_error_text(own ? own : fixed));
+    return LAIC_OK;
+}
+
+int laic_selftest_peer_timeout(int32_t device, int64_t spin_cycles, int32_t* code) {
+    if (!code || spin_cycles <= 0) return fail(LAIC_E_INVALID, "bad argument");
+    *code = 0;
+    CK(cudaSetDevice(device));
+    // rank 0 of two; "rank 1" is a mailbox on this GPU that nothing ever writes
+    const int n = 1024;
+    const size_t box_floats = (size_t)2 * 2 * n, flag_words = (size_t)2 * 2 * laic::kArCtas;
+    float *x = nullptr, *box0 = nullptr, *box1 = nullptr;
+    unsigned *fl0 = nullptr, *fl1 = nullptr, *ctr = nullptr;
+    int* err = nullptr;
+    auto release = [&]() {
+        for (void* b : {(void*)x, (void*)box0, (void*)box1, (void*)fl0, (void*)fl1, (void*)ctr, (void*)err})
+            if (b) cudaFree(b);
+    };
+    cudaError_t e = cudaSuccess;
+    for (auto [ptr, bytes] : {std::pair<void**, size_t>{(void**)&x, n * 4}, {(void**)&box0, box_floats * 4},
+                              {(void**)&box1, box_floats * 4}, {(void**)&fl0, flag_words * 4},
+                              {(void**)&fl1, flag_words * 4}, {(void**)&ctr, 8}, {(void**)&err, 4}}) {
+        if (e == cudaSuccess) e = cudaMalloc(ptr, bytes);
+        if (e == cudaSuccess) e = cudaMemset(*ptr, 0, bytes);
+    }
+    if (e == cudaSuccess) {
+        laic::ArParams ap{};
+        ap.x = x; ap.n = n; ap.rank = 0; ap.ranks = 2; ap.nmax = n;
+        ap.box[0] = box0; ap.box[1] = box1; ap.flags[0] = fl0; ap.flags[1] = fl1;
+        ap.epoch = ctr; ap.done = ctr + 1; ap.err = err; ap.spin_limit = spin_cycles;
+        laic::allreduce_oneshot_kernel<<<laic::kArCtas, laic::kArThreads>>>(ap);
+        e = cudaGetLastError();
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        if (e == cudaSuccess) e = cudaMemcpy(code, err, 4, cudaMemcpyDeviceToHost);
+    }
+    release();
+    if (e != cudaSuccess) return fail(LAIC_E_CUDA, std::string("self-test: ") + cudaGetErrorString(e));
+    if (*code) return fail(LAIC_E_CUDA, wait_error_text(*code));
     return LAIC_OK;
 }
 

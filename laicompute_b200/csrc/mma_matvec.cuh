@@ -156,7 +156,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
     const long long t0 = clock64();
     while (!mbar_try_wait_sleep(bar, parity)) {
         if (clock64() - t0 > 2000000000LL) {
-            atomicExch(err, 1);
+            atomicExch(err, kErrMbarrier);
             return false;
         }
     }

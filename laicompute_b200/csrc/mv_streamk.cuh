@@ -513,7 +513,7 @@ __global__ void __launch_bounds__(kSkWarps * 32, 1) mv_sk_kernel(const MvParams 
             if (lane == 0) {
                 const long long t0 = clock64();
                 while (*reinterpret_cast<volatile int*>(merged + leader * kSkSlots + slot) < tile_idx - kSkSlots + 1) {
-                    if (clock64() - t0 > 2000000000LL) { atomicExch(p.err, 1); break; }
+                    if (clock64() - t0 > 2000000000LL) { atomicExch(p.err, kErrTeamMerge); break; }
                 }
             }
             __syncwarp();

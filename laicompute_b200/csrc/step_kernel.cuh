@@ -89,7 +89,7 @@ __device__ __forceinline__ void step_grid_sync(unsigned* bar, unsigned target, i
             while (true) {
                 asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
                 if (v >= target) break;
-                if (clock64() - t0 > 2000000000LL) { atomicExch(err, 3); break; }
+                if (clock64() - t0 > 2000000000LL) { atomicExch(err, kErrGridBarrier); break; }
             }
         }
     }
@@ -287,7 +287,7 @@ __global__ void __launch_bounds__(kSkWarps * 32, 1) step_kernel(const StepParams
                     if (lane == 0) {
                         const long long c0 = clock64();
                         while (*reinterpret_cast<volatile int*>(merged + leader * kSkSlots + tslot) < ti - kSkSlots + 1) {
-                            if (clock64() - c0 > 2000000000LL) { atomicExch(p.err, 1); break; }
+                            if (clock64() - c0 > 2000000000LL) { atomicExch(p.err, kErrTeamMerge); break; }
                         }
                     }
                     __syncwarp();

@@ -197,6 +197,10 @@ class Matrix:
     def dequant(self, out_ptr: int, stream: int = 0) -> None:
         check(lib().laic_tensor_dequant(self.h, out_ptr, stream))
 
+    def check(self, stream: int = 0) -> None:
+        """Synchronise `stream` and raise if a bounded device wait of this tensor's kernels ran out."""
+        check(lib().laic_tensor_check(self.h, stream))
+
     def close(self) -> None:
         if getattr(self, "h", None) and self.h.value:
             lib().laic_tensor_destroy(self.h)

@@ -25,10 +25,16 @@ class SampleParams(ctypes.Structure):
                 ("repeat_penalty", ctypes.c_float), ("seed", ctypes.c_uint64)]
 
 
+def reference_dir(ref: Optional[str] = None) -> str:
+    """The reference checkout: `ref`, else $LAIC_REF_DIR, else the directory named
+    "reference" beside this repository."""
+    return ref or os.environ.get("LAIC_REF_DIR") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
+
+
 def build(ref: Optional[str] = None) -> None:
     """Compile the oracle library, and the reference drivers when the reference sources exist."""
     targets = ["oracle"]
-    src = ref or "/root/reference"
+    src = reference_dir(ref)
     if os.path.isdir(os.path.join(src, "src")):
         targets.append("ref")
     subprocess.run(["make", "-s", "-C", HERE, f"REF={src}", *targets], check=True)

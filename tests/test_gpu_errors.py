@@ -81,3 +81,21 @@ def test_sampler_candidate_limit_reported_then_cleared():
         assert ex.value.code == LAIC_E_UNSUPPORTED and "1024 candidates" in str(ex.value)
         out, _ = e.step([3], [0])
         assert 0 <= int(out[0]) < arch.vocab
+
+
+def test_bounded_peer_wait_runs_out_with_an_error_status():
+    """The allreduce kernel as rank 0 of two, against a peer mailbox on the same GPU that
+    nothing writes, with a ~10 ms flag-wait limit: the wait runs out, the kernel records
+    code 4 and returns; the host gets the message and the context keeps working."""
+    import ctypes
+    from laicompute_b200._native import LAIC_E_CUDA, lib
+    code = ctypes.c_int32(-1)
+    rc = lib().laic_selftest_peer_timeout(0, 20_000_000, ctypes.byref(code))
+    assert rc == LAIC_E_CUDA and code.value == 4
+    assert "peer never published" in lib().laic_last_error().decode()
+    # the device still runs work afterwards
+    from laicompute_b200.engine import Engine
+    e = Engine(golden_model("tiny_q4"))
+    out, _ = e.step([5], [0])
+    assert 0 <= int(out[0]) < 320
+    e.close()
