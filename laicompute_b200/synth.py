@@ -246,15 +246,23 @@ def _type_of(arch: LlamaArch, name: str) -> int:
     return arch.weight_type
 
 
+# byte -> byte with a zero nibble (value -8) replaced by 8 (value 0) in both halves
+_Q4_NIB = np.where(np.arange(16) == 0, 8, np.arange(16)).astype(np.uint8)
+_Q4_SYMMETRIC = (_Q4_NIB[np.arange(256) & 15] | (_Q4_NIB[np.arange(256) >> 4] << 4)).astype(np.uint8)
+
+
 def random_blocks(n: int, ggml_type: int, rng: np.random.Generator, std: float = 0.02) -> bytes:
-    """Q4_0 / Q8_0 blocks drawn directly (uniform quants, scales of the size a
-    N(0, std) block quantises to), for models too large to quantise quickly."""
+    """Q4_0 / Q8_0 blocks drawn directly (quants uniform and symmetric about zero,
+    scales of the size a N(0, std) block quantises to), for models too large to
+    quantise quickly. Q4_0 nibbles are uniform over 1..15 with 0 moved to 8, so the
+    decoded values (n - 8) * d have mean zero like quantised N(0, std) weights."""
     nb = n // 32
     if ggml_type == gguf.Q4_0:
         d = np.float32(std * 2.2 / 8.0) * (np.float32(1.0) + np.float32(0.1) * rng.standard_normal(nb, dtype=np.float32))
         out = np.empty((nb, 18), dtype=np.uint8)
         out[:, 0:2] = d.astype("<f2").view(np.uint8).reshape(-1, 2)
-        out[:, 2:] = np.frombuffer(rng.bytes(nb * 16), dtype=np.uint8).reshape(nb, 16)
+        z = np.frombuffer(rng.bytes(nb * 16), dtype=np.uint8).reshape(nb, 16)
+        out[:, 2:] = _Q4_SYMMETRIC[z]
         return out.tobytes()
     if ggml_type == gguf.Q8_0:
         d = np.float32(std * 2.2 / 127.0) * (np.float32(1.0) + np.float32(0.1) * rng.standard_normal(nb, dtype=np.float32))

@@ -19,6 +19,10 @@
 // bit-identical to the reference's strict (-O3, non-native) build; the tests
 // pin that against fixtures produced by the reference itself.
 #include <algorithm>
+#include <atomic>
+#include <condition_variable>
+#include <functional>
+#include <mutex>
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
@@ -92,15 +96,78 @@ size_t detect_l1d() {
     return l1;
 }
 
+// f(i) for i < n over a persistent pool of host threads when the job is large
+// enough to repay waking them (`work` = elements one call of f touches); rows
+// are handed out in chunks, and which thread runs a row never changes its result.
+class RowPool {
+public:
+    static RowPool& get() { static RowPool p; return p; }
+    size_t threads() const { return workers_.size() + 1; }
+    template <class F>
+    void run(size_t n, F& f) {
+        std::unique_lock<std::mutex> job_lock(job_mu_);  // one job at a time
+        {
+            std::lock_guard<std::mutex> lk(mu_);
+            fn_ = [&f](size_t i) { f(i); };
+            n_ = n;
+            chunk_ = std::max<size_t>(1, n / (4 * threads()));
+            next_.store(0);
+            busy_ = workers_.size();
+            ++gen_;
+        }
+        cv_.notify_all();
+        drain();
+        std::unique_lock<std::mutex> lk(mu_);
+        done_cv_.wait(lk, [&] { return busy_ == 0; });
+    }
+    ~RowPool() {
+        { std::lock_guard<std::mutex> lk(mu_); stop_ = true; ++gen_; }
+        cv_.notify_all();
+        for (auto& t : workers_) t.join();
+    }
+
+private:
+    RowPool() {
+        const size_t nt = std::max(1u, std::thread::hardware_concurrency());
+        for (size_t t = 1; t < nt; ++t) workers_.emplace_back([this] { loop(); });
+    }
+    void drain() {
+        for (;;) {
+            const size_t i0 = next_.fetch_add(chunk_);
+            if (i0 >= n_) return;
+            const size_t i1 = std::min(n_, i0 + chunk_);
+            for (size_t i = i0; i < i1; ++i) fn_(i);
+        }
+    }
+    void loop() {
+        uint64_t seen = 0;
+        for (;;) {
+            {
+                std::unique_lock<std::mutex> lk(mu_);
+                cv_.wait(lk, [&] { return gen_ != seen; });
+                seen = gen_;
+                if (stop_) return;
+            }
+            drain();
+            std::lock_guard<std::mutex> lk(mu_);
+            if (--busy_ == 0) done_cv_.notify_one();
+        }
+    }
+    std::vector<std::thread> workers_;
+    std::mutex job_mu_, mu_;
+    std::condition_variable cv_, done_cv_;
+    std::function<void(size_t)> fn_;
+    size_t n_ = 0, chunk_ = 1, busy_ = 0;
+    std::atomic<size_t> next_{0};
+    uint64_t gen_ = 0;
+    bool stop_ = false;
+};
+
 template <class F>
-void parallel_rows(size_t n, F&& f) {
-    size_t nt = std::max(1u, std::thread::hardware_concurrency());
-    if (n < 64 || nt == 1) { for (size_t i = 0; i < n; ++i) f(i); return; }
-    nt = std::min(nt, n / 16);
-    std::vector<std::thread> th;
-    for (size_t t = 0; t < nt; ++t)
-        th.emplace_back([&, t] { for (size_t i = t * n / nt; i < (t + 1) * n / nt; ++i) f(i); });
-    for (auto& x : th) x.join();
+void parallel_rows(size_t n, F&& f, size_t work = 1) {
+    RowPool& pool = RowPool::get();
+    if (n < 2 || pool.threads() == 1 || n * work < (size_t(1) << 15)) { for (size_t i = 0; i < n; ++i) f(i); return; }
+    pool.run(n, f);
 }
 
 // Row dot product: dot_cached for F16/F32 (chunks of l1_tile_bytes/(2*sb) elements,
@@ -245,7 +312,7 @@ struct Model {
         if (w.shape.size() != 2 || w.shape[0] != in || w.shape[1] != out) throw std::runtime_error("unexpected weight shape");
         std::vector<float> y(out);
         // each row is one sequential sum on one thread: the split never changes a result
-        parallel_rows(out, [&](size_t o) { y[o] = row_dot(w.type, w.data, x.data(), o * in, in, l1_tile_bytes); });
+        parallel_rows(out, [&](size_t o) { y[o] = row_dot(w.type, w.data, x.data(), o * in, in, l1_tile_bytes); }, in);
         return y;
     }
     void norm(std::vector<float>& x, const Tensor& w) const {
@@ -304,7 +371,7 @@ struct Model {
                     for (size_t t = 0; t <= pos; ++t) z += scores[t] * lc.v[t * kvd + kh * head_dim + d];
                     attn[h * head_dim + d] = z;
                 }
-            });
+            }, (pos + 1) * head_dim * 2);
             auto ao = matvec(tensor(p + "attn_output.weight"), attn, hidden, hidden);
             for (size_t i = 0; i < hidden; ++i) x[i] += 1.f * ao[i];
             auto f = x;
@@ -437,7 +504,7 @@ void oracle_matvec(uint32_t type, const uint8_t* w, const float* x, float* y, ui
     parallel_rows(size_t(out), [&](size_t o) {
         for (size_t b = 0; b < size_t(batch); ++b)
             y[b * out + o] = row_dot(type, w, x + b * in, o * size_t(in), size_t(in), size_t(l1_tile_bytes));
-    });
+    }, size_t(in) * size_t(batch));
 }
 
 // The uniform draw discrete_distribution makes from a freshly seeded mt19937_64
