@@ -66,8 +66,8 @@ typedef struct laic_dev_desc {
 #define LAIC_FLAG_NO_GRAPH 1u   /* launch kernels one by one instead of replaying a CUDA graph */
 #define LAIC_FLAG_NO_PDL 2u     /* no programmatic dependent launch between kernels */
 #define LAIC_FLAG_KV_F32 4u     /* FP32 KV cache (the reference's precision) instead of FP16 */
-#define LAIC_FLAG_STEP_KERNEL 8u /* one sequence of Q4_0/Q8_0 layers: all layers in one persistent cooperative
-                                   launch (decode-step kernel) instead of five launches per layer */
+#define LAIC_FLAG_LAYER_LAUNCHES 8u /* one sequence of Q4_0/Q8_0 layers: launch each projection and attention
+                                      separately instead of the persistent decode-step kernel (comparisons) */
 
 /* Device-side options (no counterpart in the reference, which is CPU-only). */
 typedef struct laic_dev_opts {

@@ -47,7 +47,7 @@
 #include "nccl_dl.h"
 #include "prefill.cuh"
 #include "sampler.cuh"
-#include "step_kernel.cuh"
+#include "stream_step.cuh"
 
 namespace {
 
@@ -458,10 +458,16 @@ struct laic_dev {
     float *logits_l = nullptr, *logits_g = nullptr;  // tp > 1: this rank's vocabulary rows; every rank's
     bool have_lm = false;  // tp > 1: lm holds this rank's lm_head rows
 
-    // one-sequence decode-step kernel (all layers in one cooperative launch)
-    laic::StepLayer* d_step_layers = nullptr;
-    unsigned* step_bar = nullptr;
-    uint8_t *step_rec_x = nullptr, *step_rec_act = nullptr;  // activation digit records between phases
+    // one sequence: the persistent decode-step kernel (stream_step.cuh) and its state
+    laic::LsLayer* ls_layers = nullptr;
+    uint8_t *ls_rec_x = nullptr, *ls_rec_attn = nullptr, *ls_rec_act = nullptr;
+    float *ls_ss = nullptr, *ls_part = nullptr, *ls_apart = nullptr;
+    unsigned *ls_tile_tick = nullptr, *ls_rec_tick = nullptr, *ls_head_tick = nullptr;
+    unsigned long long *ls_done = nullptr, *ls_epoch = nullptr;
+    size_t ls_done_bytes = 0, ls_tile_bytes = 0, ls_rec_bytes = 0;
+    int ls_type = -1, ls_nst = 0, ls_pieces = 0, ls_maxch = 0;
+    size_t ls_smem_bytes = 0;
+    bool ls_ready = false, ls_checked = false, use_ls = true, ls_lm = false;
     // more than 16 sequences on one GPU: binary16 hi/lo activation records written by the producing
     // kernels (embedding, o/down residual epilogues, SwiGLU) for the tile-kernel projections
     uint8_t *rec_x = nullptr, *rec_act = nullptr, *rec_attn = nullptr;
@@ -475,10 +481,6 @@ struct laic_dev {
     void* pf_ws = nullptr;
     size_t pf_ws_bytes = 0;
     float* rec_ss = nullptr;  // [h / 16 row tiles][max_seqs] sums of squares of the residual
-    float* step_ss = nullptr;
-    int step_type = -1;
-    size_t step_smem = 0;
-    bool step_ready = false, step_checked = false, use_step_kernel = false;
 
     Mat embd, lm;
     bool have_embd = false, have_out = false, have_onorm = false;
@@ -652,7 +654,7 @@ struct laic_dev {
             if (full) CK(cudaMemcpyAsync(d_params, h_params, nseq * sizeof(laic::SampleDev), cudaMemcpyHostToDevice, s));
         }
 
-        const bool step_path = nseq == 1 && step_ready;
+        const bool step_path = nseq == 1 && ls_ready;
         const bool recs = !step_path && tile_step(nseq) && rec_x;  // records travel between the tile-kernel projections
         // one sequence on the team kernel's integer variant: each producing epilogue (embedding,
         // attention, o, gate/up, down) writes the next projection's digit records
@@ -674,10 +676,12 @@ struct laic_dev {
         if (dprecs && L > 0) {
             ep.rec_dp = rec_x; ep.rec_w = layers[0].attn_norm; ep.ss_out = rec_ss; ep.rec_type = layers[0].qkv.type;
         }
-        t_begin("embed", 0);
-        CK(launch_k(laic::embed_kernel, dim3(nseq, ecta), dim3(256), 0, s, pdl, ep));
-        ++nl;
-        t_end();
+        if (!step_path) {
+            t_begin("embed", 0);
+            CK(launch_k(laic::embed_kernel, dim3(nseq, ecta), dim3(256), 0, s, pdl, ep));
+            ++nl;
+            t_end();
+        }
 
         const int nsplit = nsplit_for(nseq);
         last_split = nsplit;
@@ -688,20 +692,13 @@ struct laic_dev {
             for (int i = 0; i < nseq; ++i)
                 attn_bytes += (double)(h_pos[h_slots[i]] + 1) * Hkv * D * 2 * kvb + 8.0 * h;
 
-        if (step_path) {  // every layer in one cooperative launch
+        if (step_path) {  // the whole step (and the lm_head when it shares the layers' type) in one launch
             double wb = 0;
             for (auto& ly : layers) wb += ly.qkv.bytes() + ly.o.bytes() + ly.gu.bytes() + ly.down.bytes();
+            if (full && ls_lm) wb += lm_head().bytes();
             t_begin("layers", wb + attn_bytes * L);
-            CK(cudaMemsetAsync(step_bar, 0, 4, s));
-            laic::StepParams sp{};
-            sp.layers = d_step_layers; sp.L = L;
-            sp.h = h; sp.F = F; sp.hq = hq; sp.kv = kv; sp.D = D; sp.heads = H; sp.kv_heads = Hkv;
-            sp.rope_pairs = rope_pairs; sp.eps = a.rms_eps; sp.sqrt_d = sqrtf((float)D);
-            sp.x = x; sp.q = q; sp.attn = attn; sp.act = act; sp.rope_cs = rope_cs;
-            sp.slots = d_slots; sp.pos = pos; sp.kv_slot_stride = kv_slot_stride; sp.kv_cap = cap;
-            sp.part = attn_part; sp.counters = attn_cnt; sp.bar = step_bar; sp.err = mvs.err;
-            sp.rec_x = step_rec_x; sp.rec_act = step_rec_act; sp.ss_x = step_ss;
-            CK(laic::step_launch(step_type, D, G, sp, num_sms(), step_smem, s));
+            laic::LsParams lp = ls_params(full && ls_lm);
+            CK(laic::ls_launch(ls_type, D, G, lp, num_sms(), ls_smem_bytes, s, pdl));
             ++nl;
             t_end();
         }
@@ -784,18 +781,20 @@ struct laic_dev {
             if (int rc = allreduce_residual(nseq, s, t_begin, t_end, &nl)) return rc;
         }
         if (full) {
-            laic::MvParams pl{};
-            pl.nseq = nseq; pl.eps = a.rms_eps; pl.x = x; pl.ldx = h; pl.norm_w = out_norm;
-            pl.out = tp > 1 ? logits_l : logits; pl.ldo = tp > 1 ? Vl : V;
-            t_begin("lm_head", (double)lm_head().bytes() + 4.0 * nseq * (h + Vl));
-            RecIn r_lm;
-            if ((recs || dp_lm) && L > 0) {
-                r_lm.xg = rec_x; r_lm.mode = 1; r_lm.ss = rec_ss; r_lm.ss_tiles = ntiles_h; r_lm.dp = dp_lm;
+            if (!(step_path && ls_lm)) {
+                laic::MvParams pl{};
+                pl.nseq = nseq; pl.eps = a.rms_eps; pl.x = x; pl.ldx = h; pl.norm_w = out_norm;
+                pl.out = tp > 1 ? logits_l : logits; pl.ldo = tp > 1 ? Vl : V;
+                t_begin("lm_head", (double)lm_head().bytes() + 4.0 * nseq * (h + Vl));
+                RecIn r_lm;
+                if ((recs || dp_lm) && L > 0) {
+                    r_lm.xg = rec_x; r_lm.mode = 1; r_lm.ss = rec_ss; r_lm.ss_tiles = ntiles_h; r_lm.dp = dp_lm;
+                }
+                // the lm_head only consumes: the team kernel (its own norm of x) where it is faster
+                CK(launch_matvec(lm_head(), pl, laic::EPI_STORE, kv32, mvs, s, pdl, &nl, &r_lm,
+                                 !recs || nseq <= LAIC_LM_TEAM_MAX_BATCH));
+                t_end();
             }
-            // the lm_head only consumes: the team kernel (its own norm of x) where it is faster
-            CK(launch_matvec(lm_head(), pl, laic::EPI_STORE, kv32, mvs, s, pdl, &nl, &r_lm,
-                             !recs || nseq <= LAIC_LM_TEAM_MAX_BATCH));
-            t_end();
             if (tp > 1) {  // every rank's vocabulary rows -> logits [nseq][V] on every rank
                 t_begin("gather", 4.0 * nseq * V);
                 float* dst = nseq == 1 ? logits : logits_g;
@@ -837,51 +836,119 @@ struct laic_dev {
         return LAIC_OK;
     }
 
-    // Whether one sequence can run as the decode-step kernel: every layer projection Q4_0
-    // (or every one Q8_0), FP16 KV, one GPU, head_dim 64 or 128, and one CTA fits per SM.
-    // Builds the device layer table (before any capture).
-    int prepare_step() {
-        if (step_checked) return LAIC_OK;
-        step_checked = true;
-        step_ready = false;
-        // (at most 64 chunks of 128 positions: the attention split buffers hold 64 partials per head)
-        if (!use_step_kernel || kv32 || tp != 1 || (D != 64 && D != 128) || G > 8 || L < 1 ||
-            cap > 64 * laic::kAttnChunk)
-            return LAIC_OK;
+    // Whether one sequence can run as the persistent decode-step kernel: every layer projection
+    // Q4_0 (or every one Q8_0), FP16 KV, one GPU, head_dim 64 or 128, at most 8 query heads per
+    // kv head, and one CTA per SM with a ring of at least 8 stages. Builds the layer table and
+    // the kernel's state (before any capture).
+    int prepare_ls() {
+        if (ls_checked) return LAIC_OK;
+        ls_checked = true;
+        ls_ready = false;
+        if (!use_ls || kv32 || tp != 1 || (D != 64 && D != 128) || G > 8 || L < 1 || !out_norm) return LAIC_OK;
         const int type = layers[0].qkv.type;
         if (type != T_Q4_0 && type != T_Q8_0) return LAIC_OK;
         for (auto& l : layers)
             if (!l.qkv.q || !l.o.q || !l.gu.q || !l.down.q || l.qkv.type != type || l.o.type != type ||
                 l.gu.type != type || l.down.type != type || !l.attn_norm || !l.ffn_norm)
                 return LAIC_OK;
+        const bool lm_in = lm_head().type == type;
         const int nb_max = std::max(std::max(h, hq), F) / 32;
-        const size_t smem = laic::step_smem(type, nb_max, D);
-        if (smem > 220 * 1024) return LAIC_OK;
+        int nst = laic::ls_max_stages();
+        size_t smem = 0;
+        for (; nst >= 8; --nst)
+            if ((smem = laic::ls_smem(nst, D, G, nb_max)) <= 227 * 1024) break;
+        if (nst < 8) return LAIC_OK;
         int bps = 0;
-        CK(laic::step_prepare(type, D, G, smem, &bps));
+        CK(laic::ls_prepare(type, D, G, smem, &bps));
         if (bps < 1) return LAIC_OK;
-        const size_t kvb = 2;
-        std::vector<laic::StepLayer> tab(L);
+        // layer table
+        std::vector<laic::LsLayer> tab(L);
         for (int l = 0; l < L; ++l) {
             const Layer& ly = layers[l];
-            tab[l].qkv = {ly.qkv.q, ly.qkv.s}; tab[l].o = {ly.o.q, ly.o.s};
-            tab[l].gu = {ly.gu.q, ly.gu.s}; tab[l].down = {ly.down.q, ly.down.s};
-            tab[l].attn_norm = ly.attn_norm; tab[l].ffn_norm = ly.ffn_norm;
-            tab[l].kc = (char*)kc + (size_t)l * kv_layer_stride * kvb;
-            tab[l].vc = (char*)vc + (size_t)l * kv_layer_stride * kvb;
+            tab[l] = laic::LsLayer{ly.qkv.q, ly.qkv.s, ly.o.q, ly.o.s, ly.gu.q, ly.gu.s, ly.down.q, ly.down.s,
+                                   ly.attn_norm, ly.ffn_norm, (char*)kc + (size_t)l * kv_layer_stride * 2,
+                                   (char*)vc + (size_t)l * kv_layer_stride * 2};
         }
-        if (d_step_layers) cudaFree(d_step_layers);
-        d_step_layers = nullptr;
-        CK(cudaMalloc(&d_step_layers, sizeof(laic::StepLayer) * L));
-        CK(cudaMemcpy(d_step_layers, tab.data(), sizeof(laic::StepLayer) * L, cudaMemcpyHostToDevice));
-        if (!step_bar) CK(cudaMalloc(&step_bar, 4));
-        if (!step_rec_x) CK(cudaMalloc(&step_rec_x, (size_t)h * 4));
-        if (!step_rec_act) CK(cudaMalloc(&step_rec_act, (size_t)F * 4));
-        if (!step_ss) CK(cudaMalloc(&step_ss, (size_t)h / 8 * 4));
-        step_type = type;
-        step_smem = smem;
-        step_ready = true;
+        ls_free();
+        CK(cudaMalloc(&ls_layers, sizeof(laic::LsLayer) * L));
+        CK(cudaMemcpy(ls_layers, tab.data(), sizeof(laic::LsLayer) * L, cudaMemcpyHostToDevice));
+        // split-tile scratch: the most pieces one row tile of any projection can be cut into
+        const int Gc = num_sms();
+        int max_tiles = 0, pieces = 2;
+        auto see = [&](const Mat& m) {
+            const long long n = (long long)m.ntiles * m.nb;
+            const long long share = n >= Gc ? n / Gc : 1;
+            max_tiles = std::max(max_tiles, m.ntiles);
+            pieces = std::max(pieces, (int)std::min<long long>(Gc, m.nb / share + 2));
+        };
+        see(layers[0].qkv); see(layers[0].o); see(layers[0].gu); see(layers[0].down);
+        if (lm_in) see(lm_head());
+        const int rec_blocks = std::max(h, F) / 32;
+        const int cp = laic::ls_positions_per_chunk(D);
+        const int gm = G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8;
+        ls_maxch = (cap + cp - 1) / cp;
+        ls_pieces = pieces;
+        const size_t rb = laic::ls_record_bytes();
+        CK(cudaMalloc(&ls_rec_x, (size_t)(h / 32) * rb));
+        CK(cudaMalloc(&ls_rec_attn, (size_t)(hq / 32) * rb));
+        CK(cudaMalloc(&ls_rec_act, (size_t)(F / 32) * rb));
+        CK(cudaMalloc(&ls_ss, (size_t)(h / 16) * 4));
+        CK(cudaMalloc(&ls_part, (size_t)max_tiles * pieces * 16 * 4));
+        CK(cudaMalloc(&ls_apart, (size_t)Hkv * ls_maxch * gm * (D + 2) * 4));
+        ls_tile_bytes = (size_t)max_tiles * 4;
+        ls_rec_bytes = (size_t)rec_blocks * 4;
+        ls_done_bytes = (size_t)laic::ls_phases(L) * 8;
+        CK(cudaMalloc(&ls_tile_tick, ls_tile_bytes));
+        CK(cudaMalloc(&ls_rec_tick, ls_rec_bytes));
+        CK(cudaMalloc(&ls_head_tick, (size_t)Hkv * 4));
+        CK(cudaMalloc(&ls_done, ls_done_bytes));
+        CK(cudaMalloc(&ls_epoch, 8));
+        if (int rc = ls_reset()) return rc;
+        ls_type = type;
+        ls_nst = nst;
+        ls_smem_bytes = smem;
+        ls_lm = lm_in;
+        ls_ready = true;
         return LAIC_OK;
+    }
+
+    // Counters and tickets of the persistent step kernel back to zero (at set-up, and after a
+    // step whose bounded waits ran out and may have left them part-way).
+    int ls_reset() {
+        if (!ls_done) return LAIC_OK;
+        CK(cudaMemset(ls_tile_tick, 0, ls_tile_bytes));
+        CK(cudaMemset(ls_rec_tick, 0, ls_rec_bytes));
+        CK(cudaMemset(ls_head_tick, 0, (size_t)Hkv * 4));
+        CK(cudaMemset(ls_done, 0, ls_done_bytes));
+        CK(cudaMemset(ls_epoch, 0, 8));
+        return LAIC_OK;
+    }
+
+    void ls_free() {
+        void* bufs[] = {ls_layers, ls_rec_x, ls_rec_attn, ls_rec_act, ls_ss, ls_part, ls_apart, ls_tile_tick,
+                        ls_rec_tick, ls_head_tick, ls_done, ls_epoch};
+        for (void* b : bufs) if (b) cudaFree(b);
+        ls_layers = nullptr; ls_rec_x = ls_rec_attn = ls_rec_act = nullptr; ls_ss = ls_part = ls_apart = nullptr;
+        ls_tile_tick = ls_rec_tick = ls_head_tick = nullptr; ls_done = ls_epoch = nullptr;
+    }
+
+    laic::LsParams ls_params(bool lm_on) const {
+        laic::LsParams lp{};
+        lp.layers = ls_layers; lp.L = L;
+        lp.h = h; lp.F = F; lp.hq = hq; lp.kv = kv; lp.heads = H; lp.kv_heads = Hkv; lp.rope_pairs = rope_pairs;
+        lp.gq = G; lp.eps = a.rms_eps; lp.sqrt_d = sqrtf((float)D);
+        lp.emb_type = embd.type; lp.emb_q = embd.q; lp.emb_s = embd.s; lp.emb_nb = embd.nb; lp.vocab = V;
+        lp.tokens = d_tokens; lp.slots = d_slots; lp.pos = pos; lp.counts = counts;
+        const Mat& lm = lm_head();
+        lp.lm_q = lm.q; lp.lm_s = lm.s; lp.lm_rows = lm.rows; lp.lm_on = lm_on ? 1 : 0;
+        lp.out_norm = out_norm; lp.logits = logits;
+        lp.x = x; lp.q = q; lp.attn = attn; lp.act = act;
+        lp.rope_cs = rope_cs; lp.kv_slot_stride = kv_slot_stride; lp.kv_cap = cap;
+        lp.rec_x = ls_rec_x; lp.rec_attn = ls_rec_attn; lp.rec_act = ls_rec_act; lp.ss_x = ls_ss;
+        lp.part = ls_part; lp.part_pieces = ls_pieces; lp.tile_tick = ls_tile_tick; lp.rec_tick = ls_rec_tick;
+        lp.apart = ls_apart; lp.att_maxch = ls_maxch; lp.head_tick = ls_head_tick;
+        lp.done = ls_done; lp.epoch = ls_epoch; lp.err = mvs.err; lp.nstages = ls_nst;
+        return lp;
     }
 
     int prefill_alloc() {
@@ -975,7 +1042,7 @@ struct laic_dev {
 
     // Size the matvec scratch for `nseq` sequences (before any capture).
     int reserve_scratch(int nseq) {
-        if (int rc = prepare_step()) return rc;
+        if (int rc = prepare_ls()) return rc;
         MvNeed need;
         auto see = [&](const Mat& m) {
             if (m.q) need.merge(mv_need(m, nseq));
@@ -1110,7 +1177,7 @@ int laic_dev_create(const laic_dev_desc* desc, const laic_dev_opts* opts, laic_d
     d->kv32 = (o.flags & LAIC_FLAG_KV_F32) != 0;
     d->use_graph = !(o.flags & LAIC_FLAG_NO_GRAPH);
     d->use_pdl = !(o.flags & LAIC_FLAG_NO_PDL);
-    d->use_step_kernel = (o.flags & LAIC_FLAG_STEP_KERNEL) != 0;
+    d->use_ls = (o.flags & LAIC_FLAG_LAYER_LAUNCHES) == 0;
     d->layers.resize(a.layers);
     d->h_pos.assign(o.max_seqs, 0);
     CK(cudaStreamCreateWithFlags(&d->st, cudaStreamNonBlocking));
@@ -1225,10 +1292,11 @@ void laic_dev_destroy(laic_dev* d) {
     }
     mat_free(d->embd); mat_free(d->lm);
     mv_scratch_free(d->mvs);
+    d->ls_free();
     void* bufs[] = {d->out_norm, d->x, d->q, d->attn, d->act, d->logits, d->kc, d->vc, d->pos, d->counts,
                     d->rope_cs, d->attn_part, d->attn_cnt, d->d_tokens, d->d_out_ids, d->d_slots, d->d_err, d->d_params,
-                    d->d_hist, d->d_hist_count, d->logits_l, d->logits_g, d->d_step_layers, d->step_bar,
-                    d->step_rec_x, d->step_rec_act, d->step_ss, d->rec_x, d->rec_act, d->rec_ss, d->rec_attn, d->ar_box, d->ar_flags, d->ar_ctr,
+                    d->d_hist, d->d_hist_count, d->logits_l, d->logits_g, d->rec_x, d->rec_act, d->rec_ss, d->rec_attn,
+                    d->ar_box, d->ar_flags, d->ar_ctr,
                     d->pf_x, d->pf_c, d->pf_q, d->pf_attn, d->pf_a, d->pf_w, d->pf_slots, d->pf_npos, d->pf_tokens,
                     d->pf_ws, d->samp_v, d->samp_i, d->samp_cnt};
     for (void* b : bufs) if (b) cudaFree(b);
@@ -1250,7 +1318,7 @@ int laic_dev_upload(laic_dev* d, const char* cname, int32_t type, const uint64_t
     // any graph captured before this upload points at old buffers
     for (auto& kv : d->graphs) cudaGraphExecDestroy(kv.second);
     d->graphs.clear();
-    d->step_checked = false;
+    d->ls_checked = false;
 
     if (name == "output_norm.weight") {
         if (n != (size_t)d->h) return fail(LAIC_E_INVALID, "invalid norm tensor: " + name);
@@ -1418,6 +1486,7 @@ static int check_step_err(laic_dev* d) {
     if (mv_err) {
         CK(cudaMemset(d->mvs.err, 0, 4));
         d->h_err[0] = 0;
+        if (int rc = d->ls_reset()) return rc;
         return fail(LAIC_E_CUDA, wait_error_text(mv_err));
     }
     if (sample_err) {
@@ -1434,6 +1503,7 @@ static int check_sampler_err(laic_dev* d) {
         CK(cudaMemcpy(&err, d->mvs.err, 4, cudaMemcpyDeviceToHost));
         if (err) {
             CK(cudaMemset(d->mvs.err, 0, 4));
+            if (int rc = d->ls_reset()) return rc;
             return fail(LAIC_E_CUDA, wait_error_text(err));
         }
     }

@@ -66,11 +66,16 @@ size_t gemm_f16_workspace(int M, int N, int K);
 cudaError_t gemm_f16(int M, int N, int K, const void* A, const void* W, float* C, void* workspace, size_t ws_bytes,
                      cudaStream_t st);
 
-struct StepParams;
-// One-sequence decode-step kernel (step.cu): shared memory it needs, attribute setup with the
-// resulting CTAs per SM (call before capture), and its cooperative launch (one CTA per SM).
-size_t step_smem(int type, int nb_max, int D);
-cudaError_t step_prepare(int type, int D, int G, size_t smem, int* blocks_per_sm);
-cudaError_t step_launch(int type, int D, int G, const StepParams& p, int grid, size_t smem, cudaStream_t st);
+struct LsParams;
+// Persistent one-sequence decode-step kernel (stream_step.cu): shared memory for a ring of
+// `stages` stages and activation records of nb_max blocks, its layout constants, attribute
+// setup with the resulting CTAs per SM (call before capture), and its launch (one CTA per SM).
+size_t ls_smem(int stages, int D, int G, int nb_max);
+int ls_stage_bytes();
+int ls_max_stages();
+int ls_positions_per_chunk(int D);
+int ls_record_bytes();
+cudaError_t ls_prepare(int type, int D, int G, size_t smem, int* blocks_per_sm);
+cudaError_t ls_launch(int type, int D, int G, const LsParams& p, int grid, size_t smem, cudaStream_t st, bool pdl);
 
 }  // namespace laic

@@ -1,0 +1,750 @@
+// The decode step of one sequence as one persistent kernel that never stops
+// streaming weights (the batch-1 latency path of LlamaRuntime::step, reference
+// src/inference_v2.cpp:31, for Q4_0 or Q8_0 projections with an FP16 KV cache).
+//
+// One CTA per SM. Inside a CTA one producer warp and eight consumer warps:
+//
+//  * The producer walks the CTA's share of every phase of the step, in step
+//    order, and copies it into a ring of 9 KB shared-memory stages with 1-D
+//    bulk copies (cp.async.bulk + mbarrier): weight tile-blocks of each
+//    projection, and for attention the K and V rows of the positions written by
+//    earlier steps. None of this depends on the step's activations, so the
+//    producer never waits for another CTA: while the consumers wait for a phase
+//    to finish on every SM, the ring keeps filling with the next phase's bytes,
+//    and HBM stays busy across the phase boundaries that separate kernel
+//    launches elsewhere.
+//  * The consumers run the phases in order. Before a phase they wait until every
+//    CTA has arrived at the previous phase's counter (a bounded spin on a 64-bit
+//    monotonic counter: target = CTAs x launch epoch), copy the phase's input
+//    activation records into shared memory with one bulk copy and, for a
+//    projection after an rmsnorm, form 1/rms from the per-tile sums of squares
+//    the producing phase wrote; then they consume the ring.
+//
+// Phases of a step: EMB (token row -> residual x), then per layer QKV (rmsnorm,
+// fused [Wq;Wk;Wv], RoPE, K/V append), ATT (GQA attention), O (Wo, residual
+// add), GU (rmsnorm, interleaved [Wgate;Wup], SwiGLU), DN (Wdown, residual
+// add), and LM (final rmsnorm, lm_head) when the lm_head shares the layers'
+// block type.
+//
+// Projection work is split evenly by tile-blocks: CTA c owns the blocks
+// [c N / G, (c+1) N / G) of the phase's [row tile][block column] order, so a
+// 16-row tile may be shared by consecutive CTAs; its pieces meet in a global
+// scratch slot and the last piece to arrive (atomic ticket) adds them in piece
+// order (deterministic) and runs the epilogue. Epilogues that feed the next
+// projection also write its activation records: a 32-element record block spans
+// 2 row tiles (4 for SwiGLU), and the last tile of the block (another ticket)
+// writes it.
+//
+// The matvec inner loop (one sequence). A 16 x 32 tile-block is one integer
+// tensor-core product mma.m16n8k32 (u8 x s8 for Q4_0 nibbles, s8 x s8 for Q8_0)
+// against an activation record whose columns 0..2 are the three balanced base-128
+// digits of the block's 32 activations scaled to 21-bit integers by a power of two
+// (x = p0 2^14 + p1 2^7 + p2, each digit in [-64, 64]); columns 3..7 are zero.
+// Each column's int32 sum is exact; the Q4_0 offset (nibble - 8) enters as the
+// accumulator's initial value -8 sum_k p_jk of column j. Per block the three sums
+// are scaled by d_row x 2^-s in FP32 and accumulated; at the end of a tile the
+// row value is 2^14 A0 + 2^7 A1 + A2.
+//
+// Every wait is bounded (about one second of SM clocks); a wait that runs out
+// records its code in `err`, and once `err` is set the dependency waits stop
+// waiting, so a failed step still ends. No wait is on a peer GPU.
+#pragma once
+#include "mma_matvec.cuh"
+#include "tiles.cuh"
+
+namespace laic {
+
+constexpr int kLsWarps = 8;                          // consumer warps
+constexpr int kLsThreads = (kLsWarps + 1) * 32;      // + the producer warp
+constexpr int kLsStage = 9216;                       // ring stage bytes
+constexpr int kLsRec = 128;                          // activation record bytes per 32-column block
+constexpr int kLsMaxStages = 24;
+constexpr long long kLsSpin = 2000000000LL;          // clock cycles a dependency wait may take
+
+// tile-blocks per ring stage
+__host__ __device__ constexpr int ls_sb(int type) { return kLsStage / (tile_qbytes(type) + kTileSBytes); }
+// positions of one K (or V) chunk per ring stage
+__host__ __device__ constexpr int ls_cp(int D) { return kLsStage / (D * 2) >= 64 ? 64 : 32; }
+
+struct LsLayer {
+    const uint8_t *qkv_q, *qkv_s, *o_q, *o_s, *gu_q, *gu_s, *dn_q, *dn_s;
+    const float* attn_norm;
+    const float* ffn_norm;
+    void* kc;  // this layer's K cache (FP16)
+    void* vc;
+};
+
+struct LsParams {
+    const LsLayer* layers;
+    int L;
+    int h, F, hq, kv, heads, kv_heads, rope_pairs;
+    int gq;                   // query heads per kv head (at most the kernel's GM)
+    float eps, sqrt_d;
+    // embedding (any of F16 / Q8_0 / Q4_0, fragment-tile layout)
+    int emb_type;
+    const uint8_t *emb_q, *emb_s;
+    int emb_nb, vocab;
+    const unsigned* tokens;   // [1]
+    const int* slots;         // [1]
+    const int* pos;           // [max_seqs]
+    unsigned* counts;         // [max_seqs][vocab] history counts
+    // lm_head in the kernel (lm_q != nullptr and lm_on)
+    const uint8_t *lm_q, *lm_s;
+    int lm_rows;
+    int lm_on;                // 0: the LM phase does no work (prefill steps, or an lm_head of another type)
+    const float* out_norm;
+    float* logits;
+    // state
+    float *x, *q, *attn, *act;
+    const float2* rope_cs;
+    long long kv_slot_stride;
+    int kv_cap;
+    uint8_t *rec_x, *rec_attn, *rec_act;  // activation records of the projections' inputs
+    float* ss_x;                          // [h / 16] sums of squares of the residual per row tile
+    float* part;                          // split tiles: [tile][piece][16]
+    int part_pieces;
+    unsigned* tile_tick;                  // [max row tiles]
+    unsigned* rec_tick;                   // [max record blocks]
+    float* apart;                         // attention partials [kv_head][chunk][G (D + 2)]
+    int att_maxch;                        // chunks per kv head the scratch holds
+    unsigned* head_tick;                  // [kv_heads]
+    unsigned long long* done;             // [phases] arrivals (monotonic)
+    unsigned long long* epoch;            // launches completed
+    int* err;
+    int nstages;                          // ring depth
+};
+
+enum : int { LS_EMB = 0, LS_QKV = 1, LS_ATT = 2, LS_O = 3, LS_GU = 4, LS_DN = 5, LS_LM = 6 };
+
+__host__ __device__ inline int ls_phases(int L) { return 2 + 5 * L; }
+__device__ __forceinline__ int ls_kind(int ph, int L) {
+    if (ph == 0) return LS_EMB;
+    if (ph == 1 + 5 * L) return LS_LM;
+    return 1 + (ph - 1) % 5;
+}
+
+// One projection phase: the matrix, its shape, and the weight type of its consumer's records.
+struct LsMat {
+    const uint8_t *q, *s;
+    int rows, nb, ntiles;
+    long long nblk;
+};
+__device__ __forceinline__ LsMat ls_mat(const LsParams& p, int kind, int layer) {
+    LsMat m{};
+    if (kind == LS_LM) {
+        m.q = p.lm_q; m.s = p.lm_s; m.rows = p.lm_on ? p.lm_rows : 0; m.nb = p.h / 32;
+    } else {
+        const LsLayer& ly = p.layers[layer];
+        if (kind == LS_QKV) { m.q = ly.qkv_q; m.s = ly.qkv_s; m.rows = p.hq + 2 * p.kv; m.nb = p.h / 32; }
+        if (kind == LS_O) { m.q = ly.o_q; m.s = ly.o_s; m.rows = p.h; m.nb = p.hq / 32; }
+        if (kind == LS_GU) { m.q = ly.gu_q; m.s = ly.gu_s; m.rows = 2 * p.F; m.nb = p.h / 32; }
+        if (kind == LS_DN) { m.q = ly.dn_q; m.s = ly.dn_s; m.rows = p.h; m.nb = p.F / 32; }
+    }
+    m.ntiles = (m.rows + 15) / 16;
+    m.nblk = (long long)m.ntiles * m.nb;
+    return m;
+}
+
+// Range [ls_lo(c), ls_lo(c + 1)) of n items owned by CTA c of g (never empty while
+// n >= g; with fewer items than CTAs the first n CTAs take one each), and the CTA
+// owning item i. The CTAs owning the items of any contiguous span are consecutive.
+__device__ __forceinline__ long long ls_lo(long long n, int c, int g) { return n >= g ? n * c / g : min((long long)c, n); }
+__device__ __forceinline__ int ls_owner(long long n, long long i, int g) {
+    return n >= g ? (int)(((i + 1) * g + n - 1) / n) - 1 : (int)i;
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* a) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
+    return v;
+}
+__device__ __forceinline__ int ld_volatile_i32(const int* a) { return *reinterpret_cast<const volatile int*>(a); }
+
+// D = A (u8 or s8, 16x32) x B (s8, 32x8) + C, int32.
+template <bool A_UNSIGNED>
+__device__ __forceinline__ void imma16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                          uint32_t b1, int c0, int c1, int c2, int c3) {
+    if (A_UNSIGNED)
+        asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                     "{%10,%11,%12,%13};"
+                     : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+                     : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c0), "r"(c1), "r"(c2), "r"(c3));
+    else
+        asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                     "{%10,%11,%12,%13};"
+                     : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+                     : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c0), "r"(c1), "r"(c2), "r"(c3));
+}
+
+// Byte of element i (0..31) of a block inside one digit plane of its record: the B
+// fragment of lane (n, t) is the 8 bytes at t * 8 of plane n, bytes 0..3 holding
+// k = 4t..4t+3 and bytes 4..7 k = 4t+16..4t+19. The weights' k order follows the
+// tile layout: Q4_0 lane t holds columns 8t..8t+7 as nibble bytes (low nibbles are
+// the even columns -> k 4t+m, high nibbles the odd ones -> k 4t+16+m); Q8_0 lane t
+// holds them in fragment order (frag_pos), word 0 then word 1.
+template <int WT>
+__device__ __forceinline__ int ls_rec_byte(int i) {
+    if (WT == T_Q4_0) return (i >> 3) * 8 + (i & 1) * 4 + ((i >> 1) & 3);
+    return (i >> 3) * 8 + frag_pos(i & 7);
+}
+
+// Activation record of one 32-element block, built by one warp: lane i holds element i.
+// Layout: planes p0 / p1 / p2 (32 bytes each), then the accumulator seeds of lanes t = 0
+// (-8 P0, -8 P1) and t = 1 (-8 P2, 0) for Q4_0 (zero for Q8_0), then the block scale 2^-s.
+template <int WT>
+__device__ __forceinline__ void ls_write_record(float v, int lane, uint8_t* rec) {
+    float mx = warp_max(fabsf(v));
+    int ex = 0;
+    if (mx > 0.f && isfinite(mx)) frexpf(mx, &ex);  // mx in [2^(ex-1), 2^ex)
+    const int xi = (int)rintf(ldexpf(v, 20 - ex));   // |xi| <= 2^20
+    const int p2 = ((xi + 64) & 127) - 64;
+    const int t1 = (xi - p2) >> 7;
+    const int p1 = ((t1 + 64) & 127) - 64;
+    const int p0 = (t1 - p1) >> 7;
+    const int off = ls_rec_byte<WT>(lane);
+    rec[off] = (uint8_t)(int8_t)p0;
+    rec[32 + off] = (uint8_t)(int8_t)p1;
+    rec[64 + off] = (uint8_t)(int8_t)p2;
+    int s0 = p0, s1 = p1, s2 = p2;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+        s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+        s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+    }
+    if (lane == 0) {
+        const int k = WT == T_Q4_0 ? -8 : 0;
+        *reinterpret_cast<int4*>(rec + 96) = make_int4(k * s0, k * s1, k * s2, 0);
+        *reinterpret_cast<float4*>(rec + 112) = make_float4(ldexpf(1.f, ex - 20), 0.f, 0.f, 0.f);
+    }
+}
+
+// Named barrier of the consumer warps (the producer warp never joins it).
+__device__ __forceinline__ void ls_cbar() { named_sync(1, kLsWarps * 32); }
+
+template <int WT, int D, int GM>
+__global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p) {
+    constexpr int QB = tile_qbytes(WT);
+    constexpr int SB = ls_sb(WT);
+    constexpr int CP = ls_cp(D);
+    constexpr int E = D / 32;               // head dims per lane
+    constexpr int OPT = (GM * D + kLsWarps * 32 - 1) / (kLsWarps * 32);  // attention outputs per thread
+    static_assert(WT == T_Q4_0 || WT == T_Q8_0, "Q4_0 or Q8_0 projections");
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int NST = p.nstages;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = gridDim.x, c = blockIdx.x;
+    const int L = p.L, nph = ls_phases(L);
+
+    // ---- shared memory
+    uint8_t* ring = smem;
+    uint64_t* full = reinterpret_cast<uint64_t*>(ring + (size_t)NST * kLsStage);
+    uint64_t* empty = full + kLsMaxStages;
+    uint64_t* xbar = empty + kLsMaxStages;
+    float* red = reinterpret_cast<float*>(xbar + 2);            // [2][kLsWarps][16]
+    float* qs = red + 2 * kLsWarps * 16;                        // [GM][D] query rows of a kv head
+    float* ss_att = qs + GM * D;                                // [GM][CP] scores, then weights
+    float* hm = ss_att + GM * CP;                               // [GM] running max
+    float* hl = hm + GM;                                        // [GM] running sum
+    float* hsc = hl + GM;                                       // [GM] rescale of the running output
+    int* ictl = reinterpret_cast<int*>((reinterpret_cast<uintptr_t>(hsc + GM) + 15) & ~uintptr_t(15));  // [8]
+    uint8_t* act = reinterpret_cast<uint8_t*>(ictl + 8);        // activation records of the phase
+    act = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(act) + 127) & ~uintptr_t(127));
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NST; ++s) {
+            mbar_init(full + s, 1);
+            mbar_init(empty + s, kLsWarps);
+        }
+        mbar_init(xbar, 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+
+    // =====================================================================
+    // producer warp: every stage of every phase, in order, as the ring frees up
+    // =====================================================================
+    if (warp == kLsWarps) {
+        if (lane != 0) return;
+        int slot = 0;
+        uint32_t round = 0;
+        bool waited = false;
+        bool ok = true;
+        auto acquire = [&]() -> uint8_t* {
+            // the consumers released this slot's previous use (first round: free)
+            if (ok && round > 0 && !mbar_wait(empty + slot, (round - 1) & 1u, p.err)) ok = false;
+            return ring + (size_t)slot * kLsStage;
+        };
+        auto advance = [&]() {
+            if (++slot == NST) { slot = 0; ++round; }
+        };
+        for (int ph = 0; ph < nph; ++ph) {
+            const int kind = ls_kind(ph, L);
+            if (kind == LS_EMB) continue;
+            const int layer = (ph - 1) / 5;
+            if (kind == LS_ATT) {
+                if (!waited) { pdl_wait(); waited = true; }  // positions come from the previous step
+                const int sl = p.slots[0];
+                const int pos = p.pos[sl];
+                const int nch = (pos + 1 + CP - 1) / CP;
+                const long long I = (long long)p.kv_heads * nch;
+                const LsLayer& ly = p.layers[layer];
+                for (long long it = ls_lo(I, c, G); it < ls_lo(I, c + 1, G); ++it) {
+                    const int j = (int)(it / nch), ch = (int)(it % nch);
+                    // rows of the chunk written by earlier steps (the newest row comes later, from L2)
+                    const int r0 = ch * CP, nrows = max(0, min(r0 + CP, pos) - r0);
+                    const size_t off = (size_t)sl * p.kv_slot_stride + ((size_t)j * p.kv_cap + r0) * D;
+                    for (int kvs = 0; kvs < 2; ++kvs) {
+                        uint8_t* dst = acquire();
+                        const __half* src = reinterpret_cast<const __half*>(kvs ? ly.vc : ly.kc) + off;
+                        if (ok && nrows > 0) {
+                            mbar_expect_tx(full + slot, (uint32_t)(nrows * D * 2));
+                            bulk_g2s(dst, src, (uint32_t)(nrows * D * 2), full + slot);
+                        } else {
+                            mbar_arrive(full + slot);  // nothing to copy (or a failed wait): the stage is ready
+                        }
+                        advance();
+                    }
+                }
+                continue;
+            }
+            const LsMat m = ls_mat(p, kind, layer);
+            long long cur = ls_lo(m.nblk, c, G);
+            const long long hi = ls_lo(m.nblk, c + 1, G);
+            while (cur < hi) {
+                const int k0 = (int)(cur % m.nb);
+                const int n = (int)min((long long)min(SB, m.nb - k0), hi - cur);
+                uint8_t* dst = acquire();
+                if (ok) {
+                    mbar_expect_tx(full + slot, (uint32_t)(n * (QB + kTileSBytes)));
+                    bulk_g2s(dst, m.q + cur * QB, (uint32_t)(n * QB), full + slot);
+                    bulk_g2s(dst + SB * QB, m.s + cur * kTileSBytes, (uint32_t)(n * kTileSBytes), full + slot);
+                } else {
+                    mbar_arrive(full + slot);
+                }
+                advance();
+                cur += n;
+            }
+        }
+        return;
+    }
+
+    // =====================================================================
+    // consumer warps
+    // =====================================================================
+    const int ct = threadIdx.x;           // 0 .. 255
+    const int g = lane >> 2, t = lane & 3;
+    const int gq = p.gq;
+    pdl_wait();
+    pdl_launch_dependents();
+    if (ct == 0) {
+        const unsigned long long ep = *reinterpret_cast<volatile unsigned long long*>(p.epoch) + 1ull;
+        reinterpret_cast<unsigned long long*>(ictl)[0] = ep;
+        ictl[2] = p.slots[0];
+        ictl[3] = p.pos[ictl[2]];
+        ictl[4] = (int)p.tokens[0];
+    }
+    ls_cbar();
+    const unsigned long long target = reinterpret_cast<const unsigned long long*>(ictl)[0] * (unsigned long long)G;
+    const int sl = ictl[2], pos = ictl[3];
+    const unsigned tok = (unsigned)ictl[4];
+    int slot = 0;
+    uint32_t round = 0, xphase = 0;
+    bool aborted = false;
+    int tile_i = 0;  // tiles this CTA finished (selects the reduction buffer and the finishing warp)
+
+    // Wait until every CTA arrived at phase `ph`'s counter.
+    auto wait_phase = [&](int ph) {
+        if (ct == 0) {
+            const long long t0 = clock64();
+            while (ld_acquire_u64(p.done + ph) < target) {
+                if (ld_volatile_i32(p.err) != 0) break;
+                if (clock64() - t0 > kLsSpin) { atomicExch(p.err, kErrDepCounter); break; }
+                __nanosleep(20);
+            }
+        }
+        ls_cbar();
+    };
+    auto arrive = [&](int ph) {
+        ls_cbar();  // every consumer's writes of the phase precede the arrival
+        if (ct == 0) {
+            __threadfence();
+            const unsigned long long old = atomicAdd(p.done + ph, 1ull);
+            if (ph == nph - 1 && old + 1 == target) {  // the step's last arrival: next launch's epoch
+                __threadfence();
+                *reinterpret_cast<volatile unsigned long long*>(p.epoch) = target / (unsigned long long)G;
+            }
+        }
+    };
+    auto stage_wait = [&]() -> uint32_t {
+        if (!mbar_wait(full + slot, round & 1u, p.err)) aborted = true;
+        return smem_u32(ring + (size_t)slot * kLsStage);
+    };
+    auto stage_release = [&]() {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty + slot);
+        if (++slot == p.nstages) { slot = 0; ++round; }
+    };
+    // the phase's input records (nb blocks) into `act`; 1/rms from ss_x when `norm`
+    auto load_records = [&](const uint8_t* src, int nb, bool norm, int nss) {
+        if (ct == 0) {
+            mbar_expect_tx(xbar, (uint32_t)(nb * kLsRec));
+            bulk_g2s(act, src, (uint32_t)(nb * kLsRec), xbar);
+        }
+        if (norm && warp == 0) {
+            float a = 0.f;
+            for (int i = lane; i < nss; i += 32) a += __ldcg(p.ss_x + i);
+            a = warp_sum(a);
+            if (lane == 0) reinterpret_cast<float*>(ictl)[5] = 1.f / sqrtf(a / float(p.h) + p.eps);
+        }
+        if (!mbar_wait(xbar, xphase, p.err)) aborted = true;
+        xphase ^= 1u;
+        ls_cbar();
+    };
+    // One record block of 32 values from one warp (lane i: element i).
+    auto record_block = [&](float v, uint8_t* rec) { ls_write_record<WT>(v, lane, rec); };
+
+    const uint32_t act_a = smem_u32(act);
+    uint32_t zero_a = smem_u32(ictl + 6);  // 8 zero bytes (ictl[6], ictl[7])
+    if (ct == 0) { ictl[6] = 0; ictl[7] = 0; }
+    ls_cbar();
+
+    for (int ph = 0; ph < nph; ++ph) {
+        const int kind = ls_kind(ph, L);
+        const int layer = kind == LS_EMB ? 0 : kind == LS_LM ? L - 1 : (ph - 1) / 5;
+        if (ph > 0) wait_phase(ph - 1);
+
+        // ------------------------------------------------------------ EMB
+        if (kind == LS_EMB) {
+            const int nblk = p.h / 32;
+            for (int b = c + G * warp; b < nblk; b += G * kLsWarps) {
+                const int e = 32 * b + lane;
+                const float v = tile_value(p.emb_type, p.emb_q, p.emb_s, p.emb_nb, (int)tok, e);
+                p.x[e] = v;
+                float sq = v * v;
+#pragma unroll
+                for (int o = 8; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+                if (lane == 0) p.ss_x[2 * b] = sq;
+                if (lane == 16) p.ss_x[2 * b + 1] = sq;
+                record_block(v * p.layers[0].attn_norm[e], p.rec_x + (size_t)b * kLsRec);
+            }
+            if (c == 0 && ct == 0) atomicAdd(p.counts + (size_t)sl * p.vocab + tok, 1u);
+            arrive(ph);
+            continue;
+        }
+
+        // ------------------------------------------------------------ ATT
+        if (kind == LS_ATT) {
+            const LsLayer& ly = p.layers[layer];
+            const int nch = (pos + 1 + CP - 1) / CP;
+            const long long I = (long long)p.kv_heads * nch;
+            const long long ilo = ls_lo(I, c, G), ihi = ls_lo(I, c + 1, G);
+            const __half* kg = reinterpret_cast<const __half*>(ly.kc) + (size_t)sl * p.kv_slot_stride;
+            const __half* vg = reinterpret_cast<const __half*>(ly.vc) + (size_t)sl * p.kv_slot_stride;
+            float o_acc[OPT];
+            int run_start = 0;
+            for (long long it = ilo; it < ihi; ++it) {
+                const int j = (int)(it / nch), ch = (int)(it % nch);
+                if (it == ilo || ch == 0) {  // a new kv head: its query rows, fresh softmax state
+                    for (int i = ct; i < GM * D; i += kLsWarps * 32)
+                        qs[i] = i < gq * D ? __ldcg(p.q + (size_t)j * gq * D + i) : 0.f;
+                    if (ct < GM) { hm[ct] = -INFINITY; hl[ct] = 0.f; }
+#pragma unroll
+                    for (int k = 0; k < OPT; ++k) o_acc[k] = 0.f;
+                    run_start = ch;
+                    ls_cbar();
+                }
+                const int r0 = ch * CP, nvalid = min(CP, pos + 1 - r0);
+                // K stage: scores of the chunk's positions for the group's GM heads
+                const uint32_t ka = stage_wait();
+                const __half* ks = reinterpret_cast<const __half*>(ring + (size_t)slot * kLsStage);
+                for (int pl = warp; pl < CP; pl += kLsWarps) {
+                    float dot[GM];
+                    if (pl < nvalid) {
+                        const __half* krow = (r0 + pl == pos) ? kg + ((size_t)j * p.kv_cap + pos) * D : ks + (size_t)pl * D;
+                        float kf[E];
+#pragma unroll
+                        for (int e = 0; e < E; ++e)
+                            kf[e] = (r0 + pl == pos) ? __half2float(__ldcg(krow + lane * E + e)) : __half2float(krow[lane * E + e]);
+#pragma unroll
+                        for (int hh = 0; hh < GM; ++hh) {
+                            float s = 0.f;
+#pragma unroll
+                            for (int e = 0; e < E; ++e) s = fmaf(qs[hh * D + lane * E + e], kf[e], s);
+                            dot[hh] = warp_sum(s);
+                        }
+                        if (lane == 0)
+#pragma unroll
+                            for (int hh = 0; hh < GM; ++hh) ss_att[hh * CP + pl] = dot[hh] / p.sqrt_d;
+                    } else if (lane == 0) {
+#pragma unroll
+                        for (int hh = 0; hh < GM; ++hh) ss_att[hh * CP + pl] = -INFINITY;
+                    }
+                }
+                (void)ka;
+                stage_release();
+                ls_cbar();
+                // softmax update per head (warp hh)
+                if (warp < gq) {
+                    const int hh = warp;
+                    float mx = -INFINITY;
+                    for (int pl = lane; pl < CP; pl += 32) mx = fmaxf(mx, ss_att[hh * CP + pl]);
+                    mx = warp_max(mx);
+                    const float m_old = hm[hh];
+                    const float m_new = fmaxf(m_old, mx);
+                    float sum = 0.f;
+                    for (int pl = lane; pl < CP; pl += 32) {
+                        const float e = pl < nvalid ? expf(ss_att[hh * CP + pl] - m_new) : 0.f;
+                        ss_att[hh * CP + pl] = e;
+                        sum += e;
+                    }
+                    sum = warp_sum(sum);
+                    if (lane == 0) {
+                        const float sc = m_old == -INFINITY ? 0.f : expf(m_old - m_new);
+                        hsc[hh] = sc;
+                        hl[hh] = hl[hh] * sc + sum;
+                        hm[hh] = m_new;
+                    }
+                }
+                ls_cbar();
+                // V stage: o = o * rescale + sum_p w_p v_p
+                stage_wait();
+                const __half* vs = reinterpret_cast<const __half*>(ring + (size_t)slot * kLsStage);
+#pragma unroll
+                for (int k = 0; k < OPT; ++k) {
+                    const int idx = ct + k * kLsWarps * 32;
+                    if (idx < gq * D) {
+                        const int hh = idx / D, d = idx % D;
+                        float a = o_acc[k] * hsc[hh];
+                        for (int pl = 0; pl < nvalid; ++pl) {
+                            const float vv = (r0 + pl == pos) ? __half2float(__ldcg(vg + ((size_t)j * p.kv_cap + pos) * D + d))
+                                                              : __half2float(vs[(size_t)pl * D + d]);
+                            a = fmaf(ss_att[hh * CP + pl], vv, a);
+                        }
+                        o_acc[k] = a;
+                    }
+                }
+                stage_release();
+                ls_cbar();
+                if (it == ihi - 1 || ch == nch - 1) {
+                    // end of this CTA's run over head j: partial (o, m, l) to scratch, then the ticket
+                    float* pp = p.apart + ((size_t)j * p.att_maxch + run_start) * (GM * (D + 2));
+#pragma unroll
+                    for (int k = 0; k < OPT; ++k) {
+                        const int idx = ct + k * kLsWarps * 32;
+                        if (idx < gq * D) pp[idx] = o_acc[k];
+                    }
+                    if (ct < gq) { pp[GM * D + ct] = hm[ct]; pp[GM * D + GM + ct] = hl[ct]; }
+                    ls_cbar();
+                    const long long jlo = (long long)j * nch, jhi = jlo + nch - 1;
+                    const int cf = ls_owner(I, jlo, G), cl = ls_owner(I, jhi, G);
+                    if (ct == 0) {
+                        __threadfence();
+                        const unsigned old = atomicAdd(p.head_tick + j, 1u);
+                        ictl[1] = old == (unsigned)(cl - cf);
+                    }
+                    ls_cbar();
+                    if (ictl[1]) {  // the last run of head j: merge every run in CTA order
+                        __threadfence();
+                        float* mrg = ss_att;  // [GM] merged max, then [GM] 1/sum
+                        if (ct < gq) {
+                            float M = -INFINITY;
+                            for (int cc = cf; cc <= cl; ++cc) {
+                                const int rs = (int)(max(jlo, ls_lo(I, cc, G)) - jlo);
+                                M = fmaxf(M, __ldcg(p.apart + ((size_t)j * p.att_maxch + rs) * (GM * (D + 2)) + GM * D + ct));
+                            }
+                            float S = 0.f;
+                            for (int cc = cf; cc <= cl; ++cc) {
+                                const int rs = (int)(max(jlo, ls_lo(I, cc, G)) - jlo);
+                                const float* q2 = p.apart + ((size_t)j * p.att_maxch + rs) * (GM * (D + 2));
+                                S += __ldcg(q2 + GM * D + GM + ct) * expf(__ldcg(q2 + GM * D + ct) - M);
+                            }
+                            mrg[ct] = M;
+                            mrg[GM + ct] = 1.f / S;
+                        }
+                        ls_cbar();
+                        float* obuf = qs;  // [GM][D] merged output (the query rows are no longer needed)
+                        for (int idx = ct; idx < gq * D; idx += kLsWarps * 32) {
+                            const int hh = idx / D;
+                            float a = 0.f;
+                            for (int cc = cf; cc <= cl; ++cc) {
+                                const int rs = (int)(max(jlo, ls_lo(I, cc, G)) - jlo);
+                                const float* q2 = p.apart + ((size_t)j * p.att_maxch + rs) * (GM * (D + 2));
+                                a = fmaf(__ldcg(q2 + idx), expf(__ldcg(q2 + GM * D + hh) - mrg[hh]), a);
+                            }
+                            obuf[idx] = a * mrg[GM + hh];
+                        }
+                        ls_cbar();
+                        // attention output of heads j*GM .. j*GM+GM-1 and its records for O
+                        for (int b = warp; b < gq * D / 32; b += kLsWarps) {
+                            const float v = obuf[b * 32 + lane];
+                            const size_t e = (size_t)j * gq * D + b * 32 + lane;
+                            p.attn[e] = v;
+                            record_block(v, p.rec_attn + (e / 32) * kLsRec);
+                        }
+                        if (ct == 0) p.head_tick[j] = 0u;
+                        ls_cbar();
+                    }
+                }
+            }
+            arrive(ph);
+            continue;
+        }
+
+        // ------------------------------------------------------------ projections
+        const LsMat m = ls_mat(p, kind, layer);
+        const bool norm = kind == LS_QKV || kind == LS_GU || kind == LS_LM;
+        if (m.rows > 0) {
+            const uint8_t* rsrc = kind == LS_O ? p.rec_attn : kind == LS_DN ? p.rec_act : p.rec_x;
+            load_records(rsrc, m.nb, norm, p.h / 16);
+        }
+        const float inv = reinterpret_cast<const float*>(ictl)[5];
+        const long long lo = ls_lo(m.nblk, c, G), hi = ls_lo(m.nblk, c + 1, G);
+        // this lane's B fragment (digit columns 0..2; lanes of columns 3..7 read zeros) and seed pair
+        const bool bcol = g < 3, cseed = t < 2;
+        const uint32_t b_off = g * 32 + t * 8, c_off = 96 + t * 8;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        long long cur = lo;
+        while (cur < hi) {
+            const int tile = (int)(cur / m.nb);
+            const int k0 = (int)(cur % m.nb);
+            const int n = (int)min((long long)min(SB, m.nb - k0), hi - cur);
+            const uint32_t sq = stage_wait();
+            const uint32_t ssc = sq + SB * QB;
+            for (int jb = warp; jb < n; jb += kLsWarps) {
+                const uint32_t rec = act_a + (uint32_t)(k0 + jb) * kLsRec;
+                uint32_t a0, a1, a2, a3;
+                if (WT == T_Q4_0) {
+                    const uint2 w = lds64(sq + jb * QB + lane * 8);
+                    a0 = w.x & 0x0F0F0F0Fu; a2 = (w.x >> 4) & 0x0F0F0F0Fu;
+                    a1 = w.y & 0x0F0F0F0Fu; a3 = (w.y >> 4) & 0x0F0F0F0Fu;
+                } else {
+                    const uint4 w = lds128(sq + jb * QB + lane * 16);
+                    a0 = w.x; a2 = w.y; a1 = w.z; a3 = w.w;
+                }
+                const uint2 bb = lds64(bcol ? rec + b_off : zero_a);
+                const uint2 cc = WT == T_Q4_0 ? lds64(cseed ? rec + c_off : zero_a) : make_uint2(0u, 0u);
+                int dd[4];
+                imma16832<WT == T_Q4_0>(dd, a0, a1, a2, a3, bb.x, bb.y, (int)cc.x, (int)cc.y, (int)cc.x, (int)cc.y);
+                const uint32_t dsc = lds32(ssc + jb * kTileSBytes + g * 4);
+                const float2 df = __half22float2(*reinterpret_cast<const __half2*>(&dsc));
+                const float sinv = __uint_as_float(lds32(rec + 112));
+                const float s0 = df.x * sinv, s1 = df.y * sinv;
+                acc[0] = fmaf((float)dd[0], s0, acc[0]);
+                acc[1] = fmaf((float)dd[1], s0, acc[1]);
+                acc[2] = fmaf((float)dd[2], s1, acc[2]);
+                acc[3] = fmaf((float)dd[3], s1, acc[3]);
+            }
+            stage_release();
+            cur += n;
+            if (cur != hi && cur % m.nb != 0) continue;
+            // ---- end of this CTA's piece of the tile: rows g and g+8 from the digit columns
+            const float up0 = __shfl_down_sync(0xffffffffu, acc[0], 1);
+            const float up2 = __shfl_down_sync(0xffffffffu, acc[2], 1);
+            float* rb = red + ((tile_i & 1) * kLsWarps + warp) * 16;
+            if (t == 0) {
+                rb[g] = 16384.f * acc[0] + 128.f * acc[1] + up0;
+                rb[g + 8] = 16384.f * acc[2] + 128.f * acc[3] + up2;
+            }
+            acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+            ls_cbar();
+            const int fw = tile_i % kLsWarps;
+            const float* rbuf = red + (tile_i & 1) * kLsWarps * 16;
+            ++tile_i;
+            if (warp != fw) continue;
+            // ---- the finishing warp: the CTA's piece = sum over warps (fixed order)
+            float v = 0.f;
+            if (lane < 16)
+                for (int w = 0; w < kLsWarps; ++w) v += rbuf[w * 16 + lane];
+            // pieces of a tile shared with other CTAs meet in scratch; the last adds them in order
+            const long long t_first = (long long)tile * m.nb;
+            const int cf = ls_owner(m.nblk, t_first, G), cl = ls_owner(m.nblk, t_first + m.nb - 1, G);
+            if (cl > cf) {
+                float* slot_p = p.part + ((size_t)tile * p.part_pieces) * 16;
+                if (lane < 16) slot_p[(c - cf) * 16 + lane] = v;
+                __threadfence();
+                __syncwarp();
+                unsigned last = 0;
+                if (lane == 0) last = atomicAdd(p.tile_tick + tile, 1u) == (unsigned)(cl - cf);
+                last = __shfl_sync(0xffffffffu, last, 0);
+                if (!last) continue;
+                __threadfence();
+                v = 0.f;
+                if (lane < 16)
+                    for (int i = 0; i <= cl - cf; ++i) v += __ldcg(slot_p + i * 16 + lane);
+                if (lane == 0) p.tile_tick[tile] = 0u;
+            }
+            if (norm) v *= inv;
+            const int r = tile * 16 + lane;  // this lane's row (lanes 0..15)
+            const bool live = lane < 16 && r < m.rows;
+            if (kind == LS_LM) {
+                if (live) p.logits[r] = v;
+            } else if (kind == LS_QKV) {
+                const float other = __shfl_xor_sync(0xffffffffu, v, 1);
+                if (live) {
+                    int rr = r, region = 0;
+                    if (rr >= p.hq) { rr -= p.hq; region = 1; if (rr >= p.kv) { rr -= p.kv; region = 2; } }
+                    const int d = rr % D;
+                    float o = v;
+                    if (region < 2 && d < 2 * p.rope_pairs) {
+                        const float2 cs = p.rope_cs[(size_t)pos * p.rope_pairs + (d >> 1)];
+                        // adjacent-pair rotation, unfused like the reference
+                        if ((d & 1) == 0) o = __fsub_rn(__fmul_rn(v, cs.x), __fmul_rn(other, cs.y));
+                        else o = __fadd_rn(__fmul_rn(other, cs.y), __fmul_rn(v, cs.x));
+                    }
+                    if (region == 0) {
+                        p.q[rr] = o;
+                    } else {
+                        __half* base = reinterpret_cast<__half*>(region == 1 ? p.layers[layer].kc : p.layers[layer].vc);
+                        base[(size_t)sl * p.kv_slot_stride + ((size_t)(rr / D) * p.kv_cap + pos) * D + d] = __float2half_rn(o);
+                    }
+                }
+            } else if (kind == LS_GU) {
+                // rows 2o (gate) and 2o+1 (up): act[o] = silu(gate) * up
+                const float up = __shfl_down_sync(0xffffffffu, v, 1);
+                const int o = tile * 8 + (lane >> 1);
+                if (live && (lane & 1) == 0) p.act[o] = (v / (1.f + expf(-v))) * up;
+                __threadfence();
+                __syncwarp();
+                unsigned last = 0;
+                const int b = tile / 4;  // record block of act[32b .. 32b+31]
+                if (lane == 0) last = atomicAdd(p.rec_tick + b, 1u) == 3u;
+                last = __shfl_sync(0xffffffffu, last, 0);
+                if (last) {
+                    __threadfence();
+                    const float a = __ldcg(p.act + (size_t)b * 32 + lane);
+                    record_block(a, p.rec_act + (size_t)b * kLsRec);
+                    if (lane == 0) p.rec_tick[b] = 0u;
+                }
+            } else {  // LS_O, LS_DN: residual add, its sum of squares, records for the next rmsnorm
+                float xn = 0.f;
+                if (live) {
+                    xn = __ldcg(p.x + r) + v;
+                    p.x[r] = xn;
+                }
+                float sq = live ? xn * xn : 0.f;
+#pragma unroll
+                for (int o = 8; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+                if (lane == 0) p.ss_x[tile] = sq;
+                __threadfence();
+                __syncwarp();
+                unsigned last = 0;
+                const int b = tile / 2;
+                if (lane == 0) last = atomicAdd(p.rec_tick + b, 1u) == 1u;
+                last = __shfl_sync(0xffffffffu, last, 0);
+                if (last) {
+                    __threadfence();
+                    const float* wn = kind == LS_O ? p.layers[layer].ffn_norm
+                                                   : (layer + 1 < L ? p.layers[layer + 1].attn_norm : p.out_norm);
+                    const int e = b * 32 + lane;
+                    record_block(__ldcg(p.x + e) * wn[e], p.rec_x + (size_t)b * kLsRec);
+                    if (lane == 0) p.rec_tick[b] = 0u;
+                }
+            }
+        }
+        arrive(ph);
+    }
+    (void)aborted;
+}
+
+}  // namespace laic

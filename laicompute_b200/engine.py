@@ -12,7 +12,7 @@ from typing import Optional, Sequence, Tuple
 import numpy as np
 
 from . import gguf
-from ._native import (DevDesc, DevOpts, DevStats, FLAG_KV_F32, FLAG_NO_GRAPH, FLAG_NO_PDL, FLAG_STEP_KERNEL,
+from ._native import (DevDesc, DevOpts, DevStats, FLAG_KV_F32, FLAG_NO_GRAPH, FLAG_NO_PDL, FLAG_LAYER_LAUNCHES,
                       KernelRecord, SampleParams,
                       check, lib)
 
@@ -37,12 +37,12 @@ def desc_from_gguf(g: gguf.GgufFile) -> DevDesc:
 class Engine:
     def __init__(self, path: str, max_seqs: int = 1, kv_capacity: int = 0, device: int = 0, kv_f32: bool = False,
                  graphs: bool = True, pdl: bool = True, tp_size: int = 1, tp_rank: int = 0,
-                 nccl_id: Optional[bytes] = None, step_kernel: bool = False) -> None:
+                 nccl_id: Optional[bytes] = None, layer_launches: bool = False) -> None:
         L = lib()
         self.file = gguf.GgufFile(path)
         self.desc = desc_from_gguf(self.file)
         flags = ((FLAG_KV_F32 if kv_f32 else 0) | (0 if graphs else FLAG_NO_GRAPH) | (0 if pdl else FLAG_NO_PDL)
-                 | (FLAG_STEP_KERNEL if step_kernel else 0))
+                 | (FLAG_LAYER_LAUNCHES if layer_launches else 0))
         self._nccl_id = ctypes.create_string_buffer(nccl_id, 128) if nccl_id else None
         opts = DevOpts(device=device, max_seqs=max_seqs, kv_capacity=kv_capacity, tp_size=tp_size, tp_rank=tp_rank,
                        nccl_id=ctypes.cast(self._nccl_id, ctypes.c_void_p) if self._nccl_id else None, flags=flags)

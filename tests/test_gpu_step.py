@@ -1,7 +1,9 @@
-"""The one-sequence decode-step kernel (all layers in one cooperative launch)
-against the oracle (reference LlamaRuntime::step, src/inference_v2.cpp:31)
-and against the per-layer launch path, on Q4_0 (head dim 128, GQA groups of 4)
-and Q8_0 (head dim 64) models at contexts spanning several attention chunks."""
+"""The persistent one-sequence decode-step kernel (every phase of a step in one
+launch, the default for one sequence of Q4_0 / Q8_0 layers) against the oracle
+(reference LlamaRuntime::step, src/inference_v2.cpp:31) and against the
+per-layer launch path, on Q4_0 (head dim 128, GQA groups of 4, F16 lm_head
+outside the kernel) and Q8_0 (head dim 64, groups of 3, lm_head inside) models
+at contexts spanning several attention chunks and splits."""
 import os
 import tempfile
 
@@ -20,6 +22,8 @@ ARCHS = {
                                   vocab=512, ctx=1024, rope_theta=500000.0, name="step_q4"),
     "q8_d64_g2": synth.tiny_arch(gguf.Q8_0, hidden=256, layers=3, heads=4, kv_heads=2, ffn=768, vocab=512,
                                  ctx=1024, name="step_q8"),
+    "q8_d64_g3": synth.tiny_arch(gguf.Q8_0, hidden=384, layers=2, heads=6, kv_heads=2, ffn=512, vocab=640,
+                                 ctx=1024, name="step_q8g3"),
 }
 
 
@@ -31,11 +35,11 @@ def test_step_kernel_matches_oracle_and_layer_path(arch):
         path = synth.write_model(os.path.join(d, "m.gguf"), a, seed=51)
         prompt = synth.prompt_ids(a.vocab, 300, seed=52)
         ref_ids, ref_logits = O.OracleModel(path).generate(prompt, 16)
-        e = Engine(path, kv_capacity=1024, step_kernel=True)
+        e = Engine(path, kv_capacity=1024)
         ids, logits = e.generate(prompt, 16, want_logits=True)
         stats = e.stats()
         e.close()
-        e2 = Engine(path, kv_capacity=1024, step_kernel=False)
+        e2 = Engine(path, kv_capacity=1024, layer_launches=True)
         ids2, logits2 = e2.generate(prompt, 16, want_logits=True)
         stats2 = e2.stats()
         e2.close()
