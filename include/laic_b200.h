@@ -68,6 +68,7 @@ typedef struct laic_dev_desc {
 #define LAIC_FLAG_KV_F32 4u     /* FP32 KV cache (the reference's precision) instead of FP16 */
 #define LAIC_FLAG_LAYER_LAUNCHES 8u /* one sequence of Q4_0/Q8_0 layers: launch each projection and attention
                                       separately instead of the persistent decode-step kernel (comparisons) */
+#define LAIC_FLAG_TRACE 16u     /* the persistent decode-step kernel stamps its phases (laic_dev_step_trace) */
 
 /* Device-side options (no counterpart in the reference, which is CPU-only). */
 typedef struct laic_dev_opts {
@@ -174,6 +175,15 @@ typedef struct laic_kernel_record {
  * no programmatic overlap between them in this mode). */
 LAIC_API int laic_dev_profile(laic_dev* dev, int32_t nseq, const uint32_t* tokens, int32_t steps,
                               laic_kernel_record* out, int32_t max_out, int32_t* n_out);
+
+/* Diagnostics of the persistent one-sequence decode-step kernel (engines created
+ * with LAIC_FLAG_TRACE): the globaltimer stamps (ns) of its last launch,
+ * out[(cta * phases + phase) * 3 + k] with k = 0 phase start, 1 inputs ready
+ * (dependency met, activation records loaded), 2 phase done. Phases: 0 the
+ * embedding, then per layer QKV, attention, O, gate/up, down, then the lm_head.
+ * No counterpart in the reference. */
+LAIC_API int laic_dev_step_trace(laic_dev* dev, uint64_t* out, int64_t max_entries, int64_t* n, int32_t* ctas,
+                                 int32_t* phases);
 
 /* 128-byte NCCL unique id for laic_dev_opts.nccl_id (rank 0 creates, all ranks share). */
 LAIC_API int laic_nccl_unique_id(void* out128);

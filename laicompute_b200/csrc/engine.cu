@@ -468,6 +468,8 @@ struct laic_dev {
     int ls_type = -1, ls_nst = 0, ls_pieces = 0, ls_maxch = 0;
     size_t ls_smem_bytes = 0;
     bool ls_ready = false, ls_checked = false, use_ls = true, ls_lm = false;
+    unsigned long long* ls_trace = nullptr;  // LAIC_FLAG_TRACE: per-phase stamps of the last step kernel
+    bool trace_on = false;
     // more than 16 sequences on one GPU: binary16 hi/lo activation records written by the producing
     // kernels (embedding, o/down residual epilogues, SwiGLU) for the tile-kernel projections
     uint8_t *rec_x = nullptr, *rec_act = nullptr, *rec_attn = nullptr;
@@ -903,6 +905,10 @@ struct laic_dev {
         CK(cudaMalloc(&ls_head_tick, (size_t)Hkv * 4));
         CK(cudaMalloc(&ls_done, ls_done_bytes));
         CK(cudaMalloc(&ls_epoch, 8));
+        if (trace_on) {
+            CK(cudaMalloc(&ls_trace, (size_t)Gc * laic::ls_phases(L) * 3 * 8));
+            CK(cudaMemset(ls_trace, 0, (size_t)Gc * laic::ls_phases(L) * 3 * 8));
+        }
         if (int rc = ls_reset()) return rc;
         ls_type = type;
         ls_nst = nst;
@@ -926,10 +932,10 @@ struct laic_dev {
 
     void ls_free() {
         void* bufs[] = {ls_layers, ls_rec_x, ls_rec_attn, ls_rec_act, ls_ss, ls_part, ls_apart, ls_tile_tick,
-                        ls_rec_tick, ls_head_tick, ls_done, ls_epoch};
+                        ls_rec_tick, ls_head_tick, ls_done, ls_epoch, ls_trace};
         for (void* b : bufs) if (b) cudaFree(b);
         ls_layers = nullptr; ls_rec_x = ls_rec_attn = ls_rec_act = nullptr; ls_ss = ls_part = ls_apart = nullptr;
-        ls_tile_tick = ls_rec_tick = ls_head_tick = nullptr; ls_done = ls_epoch = nullptr;
+        ls_tile_tick = ls_rec_tick = ls_head_tick = nullptr; ls_done = ls_epoch = nullptr; ls_trace = nullptr;
     }
 
     laic::LsParams ls_params(bool lm_on) const {
@@ -948,6 +954,7 @@ struct laic_dev {
         lp.part = ls_part; lp.part_pieces = ls_pieces; lp.tile_tick = ls_tile_tick; lp.rec_tick = ls_rec_tick;
         lp.apart = ls_apart; lp.att_maxch = ls_maxch; lp.head_tick = ls_head_tick;
         lp.done = ls_done; lp.epoch = ls_epoch; lp.err = mvs.err; lp.nstages = ls_nst;
+        lp.trace = ls_trace;
         return lp;
     }
 
@@ -1178,6 +1185,7 @@ int laic_dev_create(const laic_dev_desc* desc, const laic_dev_opts* opts, laic_d
     d->use_graph = !(o.flags & LAIC_FLAG_NO_GRAPH);
     d->use_pdl = !(o.flags & LAIC_FLAG_NO_PDL);
     d->use_ls = (o.flags & LAIC_FLAG_LAYER_LAUNCHES) == 0;
+    d->trace_on = (o.flags & LAIC_FLAG_TRACE) != 0;
     d->layers.resize(a.layers);
     d->h_pos.assign(o.max_seqs, 0);
     CK(cudaStreamCreateWithFlags(&d->st, cudaStreamNonBlocking));
@@ -1676,6 +1684,21 @@ int laic_dev_profile(laic_dev* d, int32_t nseq, const uint32_t* tokens, int32_t 
     }
     *n_out = std::min<int32_t>(max_out, (int32_t)recs.size());
     for (int i = 0; i < *n_out; ++i) out[i] = recs[i];
+    return LAIC_OK;
+}
+
+int laic_dev_step_trace(laic_dev* d, uint64_t* out, int64_t max_entries, int64_t* n, int32_t* ctas,
+                        int32_t* phases) {
+    if (!d || !out || !n || !ctas || !phases) return fail(LAIC_E_INVALID, "null argument");
+    if (!d->ls_trace) return fail(LAIC_E_INVALID, "no step trace: create the engine with LAIC_FLAG_TRACE "
+                                               "and run a one-sequence step on the persistent kernel");
+    CK(cudaSetDevice(d->device));
+    CK(cudaStreamSynchronize(d->st));
+    const int64_t total = (int64_t)num_sms() * laic::ls_phases(d->L) * 3;
+    *n = std::min(total, max_entries);
+    *ctas = num_sms();
+    *phases = laic::ls_phases(d->L);
+    CK(cudaMemcpy(out, d->ls_trace, (size_t)*n * 8, cudaMemcpyDeviceToHost));
     return LAIC_OK;
 }
 

@@ -112,7 +112,14 @@ struct LsParams {
     unsigned long long* epoch;            // launches completed
     int* err;
     int nstages;                          // ring depth
+    unsigned long long* trace;            // optional: [CTA][phase][3] globaltimer stamps (start, inputs ready, done)
 };
+
+__device__ __forceinline__ unsigned long long ls_now() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
 
 enum : int { LS_EMB = 0, LS_QKV = 1, LS_ATT = 2, LS_O = 3, LS_GU = 4, LS_DN = 5, LS_LM = 6 };
 
@@ -367,6 +374,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
     };
     auto arrive = [&](int ph) {
         ls_cbar();  // every consumer's writes of the phase precede the arrival
+        if (p.trace && ct == 0) p.trace[((size_t)c * nph + ph) * 3 + 2] = ls_now();
         if (ct == 0) {
             __threadfence();
             const unsigned long long old = atomicAdd(p.done + ph, 1ull);
@@ -409,10 +417,13 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
     if (ct == 0) { ictl[6] = 0; ictl[7] = 0; }
     ls_cbar();
 
+    unsigned long long* trace = p.trace ? p.trace + (size_t)c * nph * 3 : nullptr;
     for (int ph = 0; ph < nph; ++ph) {
         const int kind = ls_kind(ph, L);
         const int layer = kind == LS_EMB ? 0 : kind == LS_LM ? L - 1 : (ph - 1) / 5;
+        if (trace && ct == 0) trace[ph * 3] = ls_now();
         if (ph > 0) wait_phase(ph - 1);
+        if (trace && ct == 0 && (kind == LS_EMB || kind == LS_ATT)) trace[ph * 3 + 1] = ls_now();
 
         // ------------------------------------------------------------ EMB
         if (kind == LS_EMB) {
@@ -599,6 +610,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
             load_records(rsrc, m.nb, norm, p.h / 16);
         }
         const float inv = reinterpret_cast<const float*>(ictl)[5];
+        if (trace && ct == 0) trace[ph * 3 + 1] = ls_now();
         const long long lo = ls_lo(m.nblk, c, G), hi = ls_lo(m.nblk, c + 1, G);
         // this lane's B fragment (digit columns 0..2; lanes of columns 3..7 read zeros) and seed pair
         const bool bcol = g < 3, cseed = t < 2;
