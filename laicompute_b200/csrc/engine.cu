@@ -465,7 +465,7 @@ struct laic_dev {
     unsigned *ls_tile_tick = nullptr, *ls_rec_tick = nullptr, *ls_head_tick = nullptr;
     unsigned long long *ls_done = nullptr, *ls_epoch = nullptr;
     size_t ls_done_bytes = 0, ls_tile_bytes = 0, ls_rec_bytes = 0;
-    int ls_type = -1, ls_nst = 0, ls_pieces = 0, ls_maxch = 0;
+    int ls_type = -1, ls_nst = 0, ls_pieces = 0, ls_maxch = 0, ls_runs = 0;
     size_t ls_smem_bytes = 0;
     bool ls_ready = false, ls_checked = false, use_ls = true, ls_lm = false;
     unsigned long long* ls_trace = nullptr;  // LAIC_FLAG_TRACE: per-phase stamps of the last step kernel
@@ -855,10 +855,12 @@ struct laic_dev {
                 return LAIC_OK;
         const bool lm_in = lm_head().type == type;
         const int nb_max = std::max(std::max(h, hq), F) / 32;
+        // attention chunks of one kv head span at most this many consecutive CTAs
+        const int att_runs = std::min(num_sms(), num_sms() / std::max(1, Hkv) + 2);
         int nst = laic::ls_max_stages();
         size_t smem = 0;
         for (; nst >= 8; --nst)
-            if ((smem = laic::ls_smem(nst, D, G, nb_max)) <= 227 * 1024) break;
+            if ((smem = laic::ls_smem(nst, D, G, nb_max, att_runs)) <= 227 * 1024) break;
         if (nst < 8) return LAIC_OK;
         int bps = 0;
         CK(laic::ls_prepare(type, D, G, smem, &bps));
@@ -912,6 +914,7 @@ struct laic_dev {
         if (int rc = ls_reset()) return rc;
         ls_type = type;
         ls_nst = nst;
+        ls_runs = att_runs;
         ls_smem_bytes = smem;
         ls_lm = lm_in;
         ls_ready = true;
@@ -952,7 +955,7 @@ struct laic_dev {
         lp.rope_cs = rope_cs; lp.kv_slot_stride = kv_slot_stride; lp.kv_cap = cap;
         lp.rec_x = ls_rec_x; lp.rec_attn = ls_rec_attn; lp.rec_act = ls_rec_act; lp.ss_x = ls_ss;
         lp.part = ls_part; lp.part_pieces = ls_pieces; lp.tile_tick = ls_tile_tick; lp.rec_tick = ls_rec_tick;
-        lp.apart = ls_apart; lp.att_maxch = ls_maxch; lp.head_tick = ls_head_tick;
+        lp.apart = ls_apart; lp.att_maxch = ls_maxch; lp.att_runs = ls_runs; lp.head_tick = ls_head_tick;
         lp.done = ls_done; lp.epoch = ls_epoch; lp.err = mvs.err; lp.nstages = ls_nst;
         lp.trace = ls_trace;
         return lp;

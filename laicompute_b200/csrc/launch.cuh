@@ -70,7 +70,7 @@ struct LsParams;
 // Persistent one-sequence decode-step kernel (stream_step.cu): shared memory for a ring of
 // `stages` stages and activation records of nb_max blocks, its layout constants, attribute
 // setup with the resulting CTAs per SM (call before capture), and its launch (one CTA per SM).
-size_t ls_smem(int stages, int D, int G, int nb_max);
+size_t ls_smem(int stages, int D, int G, int nb_max, int att_runs);
 int ls_stage_bytes();
 int ls_max_stages();
 int ls_positions_per_chunk(int D);

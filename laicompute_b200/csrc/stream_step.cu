@@ -26,12 +26,13 @@ static LsFn ls_pick(int type, int D, int G) {
 
 static int pow2_at_least(int g) { return g <= 1 ? 1 : g <= 2 ? 2 : g <= 4 ? 4 : 8; }
 
-size_t ls_smem(int stages, int D, int G, int nb_max) {
+size_t ls_smem(int stages, int D, int G, int nb_max, int att_runs) {
     const int GM = pow2_at_least(G), CP = ls_cp(D);
     size_t b = (size_t)stages * kLsStage;                      // ring
     b += 2 * kLsMaxStages * 8 + 16;                            // full / empty / record barriers
     b += 2 * kLsWarps * 16 * 4;                                // tile reductions
-    b += (size_t)GM * D * 4 + (size_t)GM * CP * 4 + 3 * GM * 4;  // attention: queries, scores, softmax state
+    b += (size_t)GM * D * 4 + (size_t)GM * CP * 4 + 3 * GM * 4;  // attention: merged output, scores, softmax state
+    b += (size_t)att_runs * GM * 4;                               // attention: merge weights
     b += 16 + 32;                                              // alignment + broadcast words
     b += 128 + (size_t)nb_max * kLsRec;                        // alignment + activation records
     return b;

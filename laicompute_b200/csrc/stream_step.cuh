@@ -107,6 +107,7 @@ struct LsParams {
     unsigned* rec_tick;                   // [max record blocks]
     float* apart;                         // attention partials [kv_head][chunk][G (D + 2)]
     int att_maxch;                        // chunks per kv head the scratch holds
+    int att_runs;                         // most CTAs one kv head's chunks can be spread over
     unsigned* head_tick;                  // [kv_heads]
     unsigned long long* done;             // [phases] arrivals (monotonic)
     unsigned long long* epoch;            // launches completed
@@ -235,7 +236,9 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
     constexpr int SB = ls_sb(WT);
     constexpr int CP = ls_cp(D);
     constexpr int E = D / 32;               // head dims per lane
-    constexpr int OPT = (GM * D + kLsWarps * 32 - 1) / (kLsWarps * 32);  // attention outputs per thread
+    constexpr int NBW = SB / kLsWarps;      // tile-blocks of a full stage per consumer warp
+    constexpr int PPW = CP / kLsWarps;      // chunk positions per consumer warp (scores)
+    constexpr int OP2 = (GM * D / 2 + kLsWarps * 32 - 1) / (kLsWarps * 32);  // attention output pairs per thread
     static_assert(WT == T_Q4_0 || WT == T_Q8_0, "Q4_0 or Q8_0 projections");
     extern __shared__ __align__(128) uint8_t smem[];
     const int NST = p.nstages;
@@ -254,7 +257,8 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
     float* hm = ss_att + GM * CP;                               // [GM] running max
     float* hl = hm + GM;                                        // [GM] running sum
     float* hsc = hl + GM;                                       // [GM] rescale of the running output
-    int* ictl = reinterpret_cast<int*>((reinterpret_cast<uintptr_t>(hsc + GM) + 15) & ~uintptr_t(15));  // [8]
+    float* wrun = hsc + GM;                                     // [att_runs][GM] merge weights of the runs
+    int* ictl = reinterpret_cast<int*>((reinterpret_cast<uintptr_t>(wrun + p.att_runs * GM) + 15) & ~uintptr_t(15));
     uint8_t* act = reinterpret_cast<uint8_t*>(ictl + 8);        // activation records of the phase
     act = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(act) + 127) & ~uintptr_t(127));
 
@@ -452,50 +456,76 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
             const long long ilo = ls_lo(I, c, G), ihi = ls_lo(I, c + 1, G);
             const __half* kg = reinterpret_cast<const __half*>(ly.kc) + (size_t)sl * p.kv_slot_stride;
             const __half* vg = reinterpret_cast<const __half*>(ly.vc) + (size_t)sl * p.kv_slot_stride;
-            float o_acc[OPT];
+            float2 o_acc[OP2];
+            float qreg[GM][E];
             int run_start = 0;
             for (long long it = ilo; it < ihi; ++it) {
                 const int j = (int)(it / nch), ch = (int)(it % nch);
-                if (it == ilo || ch == 0) {  // a new kv head: its query rows, fresh softmax state
-                    for (int i = ct; i < GM * D; i += kLsWarps * 32)
-                        qs[i] = i < gq * D ? __ldcg(p.q + (size_t)j * gq * D + i) : 0.f;
+                if (it == ilo || ch == 0) {
+                    // a new kv head: this lane's slice of the group's query rows, fresh softmax state
+#pragma unroll
+                    for (int hh = 0; hh < GM; ++hh)
+#pragma unroll
+                        for (int e = 0; e < E; ++e)
+                            qreg[hh][e] = hh < gq ? __ldcg(p.q + ((size_t)j * gq + hh) * D + lane * E + e) : 0.f;
                     if (ct < GM) { hm[ct] = -INFINITY; hl[ct] = 0.f; }
 #pragma unroll
-                    for (int k = 0; k < OPT; ++k) o_acc[k] = 0.f;
+                    for (int k = 0; k < OP2; ++k) o_acc[k] = make_float2(0.f, 0.f);
                     run_start = ch;
                     ls_cbar();
                 }
                 const int r0 = ch * CP, nvalid = min(CP, pos + 1 - r0);
-                // K stage: scores of the chunk's positions for the group's GM heads
-                const uint32_t ka = stage_wait();
+                const bool has_new = r0 + nvalid - 1 == pos;  // the chunk ends with this step's row (from L2)
+                const int nsm = has_new ? nvalid - 1 : nvalid;  // rows in the ring stage
+                // ---- K stage: the warp's positions pl = warp + 8 i, lanes split the head dims
+                stage_wait();
                 const __half* ks = reinterpret_cast<const __half*>(ring + (size_t)slot * kLsStage);
-                for (int pl = warp; pl < CP; pl += kLsWarps) {
-                    float dot[GM];
-                    if (pl < nvalid) {
-                        const __half* krow = (r0 + pl == pos) ? kg + ((size_t)j * p.kv_cap + pos) * D : ks + (size_t)pl * D;
-                        float kf[E];
+                float sc[PPW][GM];
 #pragma unroll
-                        for (int e = 0; e < E; ++e)
-                            kf[e] = (r0 + pl == pos) ? __half2float(__ldcg(krow + lane * E + e)) : __half2float(krow[lane * E + e]);
+                for (int i = 0; i < PPW; ++i) {
+                    const int pl = warp + i * kLsWarps;
+                    float kf[E];
 #pragma unroll
-                        for (int hh = 0; hh < GM; ++hh) {
-                            float s = 0.f;
+                    for (int e = 0; e < E; ++e) kf[e] = 0.f;
+                    if (pl < nsm) {
 #pragma unroll
-                            for (int e = 0; e < E; ++e) s = fmaf(qs[hh * D + lane * E + e], kf[e], s);
-                            dot[hh] = warp_sum(s);
+                        for (int e = 0; e < E; e += 2) {
+                            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(ks + (size_t)pl * D + lane * E + e));
+                            kf[e] = f.x; kf[e + 1] = f.y;
                         }
-                        if (lane == 0)
+                    } else if (has_new && pl == nvalid - 1) {
+                        const __half2* kr = reinterpret_cast<const __half2*>(kg + ((size_t)j * p.kv_cap + pos) * D + lane * E);
 #pragma unroll
-                            for (int hh = 0; hh < GM; ++hh) ss_att[hh * CP + pl] = dot[hh] / p.sqrt_d;
-                    } else if (lane == 0) {
+                        for (int e = 0; e < E; e += 2) {
+                            const float2 f = __half22float2(__ldcg(kr + e / 2));
+                            kf[e] = f.x; kf[e + 1] = f.y;
+                        }
+                    }
 #pragma unroll
-                        for (int hh = 0; hh < GM; ++hh) ss_att[hh * CP + pl] = -INFINITY;
+                    for (int hh = 0; hh < GM; ++hh) {
+                        float a = 0.f;
+#pragma unroll
+                        for (int e = 0; e < E; ++e) a = fmaf(qreg[hh][e], kf[e], a);
+                        sc[i][hh] = a;
                     }
                 }
-                (void)ka;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                    for (int i = 0; i < PPW; ++i)
+#pragma unroll
+                        for (int hh = 0; hh < GM; ++hh) sc[i][hh] += __shfl_xor_sync(0xffffffffu, sc[i][hh], o);
+                if (lane == 0) {
+#pragma unroll
+                    for (int i = 0; i < PPW; ++i) {
+                        const int pl = warp + i * kLsWarps;
+#pragma unroll
+                        for (int hh = 0; hh < GM; ++hh) ss_att[hh * CP + pl] = pl < nvalid ? sc[i][hh] / p.sqrt_d : -INFINITY;
+                    }
+                }
                 stage_release();
                 ls_cbar();
-                // softmax update per head (warp hh)
+                // ---- softmax update per head (warp hh)
                 if (warp < gq) {
                     const int hh = warp;
                     float mx = -INFINITY;
@@ -511,28 +541,41 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                     }
                     sum = warp_sum(sum);
                     if (lane == 0) {
-                        const float sc = m_old == -INFINITY ? 0.f : expf(m_old - m_new);
-                        hsc[hh] = sc;
-                        hl[hh] = hl[hh] * sc + sum;
+                        const float scl = m_old == -INFINITY ? 0.f : expf(m_old - m_new);
+                        hsc[hh] = scl;
+                        hl[hh] = hl[hh] * scl + sum;
                         hm[hh] = m_new;
                     }
                 }
                 ls_cbar();
-                // V stage: o = o * rescale + sum_p w_p v_p
+                // ---- V stage: o = o * rescale + sum_p w_p v_p, two head dims per thread
                 stage_wait();
                 const __half* vs = reinterpret_cast<const __half*>(ring + (size_t)slot * kLsStage);
 #pragma unroll
-                for (int k = 0; k < OPT; ++k) {
-                    const int idx = ct + k * kLsWarps * 32;
-                    if (idx < gq * D) {
-                        const int hh = idx / D, d = idx % D;
-                        float a = o_acc[k] * hsc[hh];
-                        for (int pl = 0; pl < nvalid; ++pl) {
-                            const float vv = (r0 + pl == pos) ? __half2float(__ldcg(vg + ((size_t)j * p.kv_cap + pos) * D + d))
-                                                              : __half2float(vs[(size_t)pl * D + d]);
-                            a = fmaf(ss_att[hh * CP + pl], vv, a);
+                for (int k = 0; k < OP2; ++k) {
+                    const int i2 = ct + k * kLsWarps * 32;
+                    if (i2 < gq * D / 2) {
+                        const int hh = i2 / (D / 2), d = 2 * (i2 % (D / 2));
+                        const float* wv = ss_att + hh * CP;
+                        const float scl = hsc[hh];
+                        float ax = o_acc[k].x * scl, ay = o_acc[k].y * scl, bx = 0.f, by = 0.f;
+                        int pl = 0;
+                        for (; pl + 1 < nsm; pl += 2) {
+                            const float2 v0 = __half22float2(*reinterpret_cast<const __half2*>(vs + (size_t)pl * D + d));
+                            const float2 v1 = __half22float2(*reinterpret_cast<const __half2*>(vs + (size_t)(pl + 1) * D + d));
+                            ax = fmaf(wv[pl], v0.x, ax); ay = fmaf(wv[pl], v0.y, ay);
+                            bx = fmaf(wv[pl + 1], v1.x, bx); by = fmaf(wv[pl + 1], v1.y, by);
                         }
-                        o_acc[k] = a;
+                        if (pl < nsm) {
+                            const float2 v0 = __half22float2(*reinterpret_cast<const __half2*>(vs + (size_t)pl * D + d));
+                            ax = fmaf(wv[pl], v0.x, ax); ay = fmaf(wv[pl], v0.y, ay);
+                        }
+                        if (has_new) {
+                            const float2 vv = __half22float2(
+                                __ldcg(reinterpret_cast<const __half2*>(vg + ((size_t)j * p.kv_cap + pos) * D + d)));
+                            ax = fmaf(wv[nvalid - 1], vv.x, ax); ay = fmaf(wv[nvalid - 1], vv.y, ay);
+                        }
+                        o_acc[k] = make_float2(ax + bx, ay + by);
                     }
                 }
                 stage_release();
@@ -541,9 +584,9 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                     // end of this CTA's run over head j: partial (o, m, l) to scratch, then the ticket
                     float* pp = p.apart + ((size_t)j * p.att_maxch + run_start) * (GM * (D + 2));
 #pragma unroll
-                    for (int k = 0; k < OPT; ++k) {
-                        const int idx = ct + k * kLsWarps * 32;
-                        if (idx < gq * D) pp[idx] = o_acc[k];
+                    for (int k = 0; k < OP2; ++k) {
+                        const int i2 = ct + k * kLsWarps * 32;
+                        if (i2 < gq * D / 2) reinterpret_cast<float2*>(pp)[i2] = o_acc[k];
                     }
                     if (ct < gq) { pp[GM * D + ct] = hm[ct]; pp[GM * D + GM + ct] = hl[ct]; }
                     ls_cbar();
@@ -555,38 +598,48 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                         ictl[1] = old == (unsigned)(cl - cf);
                     }
                     ls_cbar();
-                    if (ictl[1]) {  // the last run of head j: merge every run in CTA order
+                    if (ictl[1]) {  // the last run of head j: merge every run (CTA order)
                         __threadfence();
-                        float* mrg = ss_att;  // [GM] merged max, then [GM] 1/sum
-                        if (ct < gq) {
+                        const int nruns = cl - cf + 1;
+                        // per-run weights exp(m_r - M) / S of each head (warp hh, lanes over runs)
+                        if (warp < gq) {
+                            const int hh = warp;
                             float M = -INFINITY;
-                            for (int cc = cf; cc <= cl; ++cc) {
-                                const int rs = (int)(max(jlo, ls_lo(I, cc, G)) - jlo);
-                                M = fmaxf(M, __ldcg(p.apart + ((size_t)j * p.att_maxch + rs) * (GM * (D + 2)) + GM * D + ct));
+                            for (int r = lane; r < nruns; r += 32) {
+                                const int rs = (int)(max(jlo, ls_lo(I, cf + r, G)) - jlo);
+                                M = fmaxf(M, __ldcg(p.apart + ((size_t)j * p.att_maxch + rs) * (GM * (D + 2)) + GM * D + hh));
                             }
+                            M = warp_max(M);
                             float S = 0.f;
-                            for (int cc = cf; cc <= cl; ++cc) {
-                                const int rs = (int)(max(jlo, ls_lo(I, cc, G)) - jlo);
+                            for (int r = lane; r < nruns; r += 32) {
+                                const int rs = (int)(max(jlo, ls_lo(I, cf + r, G)) - jlo);
                                 const float* q2 = p.apart + ((size_t)j * p.att_maxch + rs) * (GM * (D + 2));
-                                S += __ldcg(q2 + GM * D + GM + ct) * expf(__ldcg(q2 + GM * D + ct) - M);
+                                const float e = expf(__ldcg(q2 + GM * D + hh) - M);
+                                wrun[r * GM + hh] = e;
+                                S += __ldcg(q2 + GM * D + GM + hh) * e;
                             }
-                            mrg[ct] = M;
-                            mrg[GM + ct] = 1.f / S;
+                            S = warp_sum(S);
+                            const float is = 1.f / S;
+                            for (int r = lane; r < nruns; r += 32) wrun[r * GM + hh] *= is;
                         }
                         ls_cbar();
-                        float* obuf = qs;  // [GM][D] merged output (the query rows are no longer needed)
-                        for (int idx = ct; idx < gq * D; idx += kLsWarps * 32) {
-                            const int hh = idx / D;
-                            float a = 0.f;
-                            for (int cc = cf; cc <= cl; ++cc) {
-                                const int rs = (int)(max(jlo, ls_lo(I, cc, G)) - jlo);
-                                const float* q2 = p.apart + ((size_t)j * p.att_maxch + rs) * (GM * (D + 2));
-                                a = fmaf(__ldcg(q2 + idx), expf(__ldcg(q2 + GM * D + hh) - mrg[hh]), a);
+                        float* obuf = qs;  // [GM][D] merged output
+                        for (int i2 = ct; i2 < gq * D / 2; i2 += kLsWarps * 32) {
+                            const int hh = i2 / (D / 2);
+                            float ax = 0.f, ay = 0.f;
+#pragma unroll 4
+                            for (int r = 0; r < nruns; ++r) {
+                                const int rs = (int)(max(jlo, ls_lo(I, cf + r, G)) - jlo);
+                                const float2 ov = __ldcg(reinterpret_cast<const float2*>(
+                                                             p.apart + ((size_t)j * p.att_maxch + rs) * (GM * (D + 2))) + i2);
+                                const float w = wrun[r * GM + hh];
+                                ax = fmaf(w, ov.x, ax); ay = fmaf(w, ov.y, ay);
                             }
-                            obuf[idx] = a * mrg[GM + hh];
+                            obuf[2 * i2] = ax;
+                            obuf[2 * i2 + 1] = ay;
                         }
                         ls_cbar();
-                        // attention output of heads j*GM .. j*GM+GM-1 and its records for O
+                        // attention output of heads j*gq .. j*gq+gq-1 and its records for O
                         for (int b = warp; b < gq * D / 32; b += kLsWarps) {
                             const float v = obuf[b * 32 + lane];
                             const size_t e = (size_t)j * gq * D + b * 32 + lane;
@@ -623,29 +676,54 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
             const int n = (int)min((long long)min(SB, m.nb - k0), hi - cur);
             const uint32_t sq = stage_wait();
             const uint32_t ssc = sq + SB * QB;
-            for (int jb = warp; jb < n; jb += kLsWarps) {
-                const uint32_t rec = act_a + (uint32_t)(k0 + jb) * kLsRec;
-                uint32_t a0, a1, a2, a3;
-                if (WT == T_Q4_0) {
-                    const uint2 w = lds64(sq + jb * QB + lane * 8);
-                    a0 = w.x & 0x0F0F0F0Fu; a2 = (w.x >> 4) & 0x0F0F0F0Fu;
-                    a1 = w.y & 0x0F0F0F0Fu; a3 = (w.y >> 4) & 0x0F0F0F0Fu;
-                } else {
-                    const uint4 w = lds128(sq + jb * QB + lane * 16);
-                    a0 = w.x; a2 = w.y; a1 = w.z; a3 = w.w;
+            // this warp's blocks of the stage (jb = warp + 8 i): all loads first, then the products
+            uint32_t wq[NBW][WT == T_Q4_0 ? 2 : 4], bx[NBW][2], cx[NBW][2], dsc[NBW];
+            float sv[NBW];
+#pragma unroll
+            for (int i = 0; i < NBW; ++i) {
+                const int jb = warp + i * kLsWarps;
+                if (jb < n) {
+                    const uint32_t rec = act_a + (uint32_t)(k0 + jb) * kLsRec;
+                    if (WT == T_Q4_0) {
+                        const uint2 w = lds64(sq + jb * QB + lane * 8);
+                        wq[i][0] = w.x; wq[i][1] = w.y;
+                    } else {
+                        const uint4 w = lds128(sq + jb * QB + lane * 16);
+                        wq[i][0] = w.x; wq[i][1] = w.y; wq[i][2] = w.z; wq[i][3] = w.w;
+                    }
+                    const uint2 bb = lds64(bcol ? rec + b_off : zero_a);
+                    bx[i][0] = bb.x; bx[i][1] = bb.y;
+                    if (WT == T_Q4_0) {
+                        const uint2 cc = lds64(cseed ? rec + c_off : zero_a);
+                        cx[i][0] = cc.x; cx[i][1] = cc.y;
+                    } else {
+                        cx[i][0] = cx[i][1] = 0u;
+                    }
+                    dsc[i] = lds32(ssc + jb * kTileSBytes + g * 4);
+                    sv[i] = __uint_as_float(lds32(rec + 112));
                 }
-                const uint2 bb = lds64(bcol ? rec + b_off : zero_a);
-                const uint2 cc = WT == T_Q4_0 ? lds64(cseed ? rec + c_off : zero_a) : make_uint2(0u, 0u);
-                int dd[4];
-                imma16832<WT == T_Q4_0>(dd, a0, a1, a2, a3, bb.x, bb.y, (int)cc.x, (int)cc.y, (int)cc.x, (int)cc.y);
-                const uint32_t dsc = lds32(ssc + jb * kTileSBytes + g * 4);
-                const float2 df = __half22float2(*reinterpret_cast<const __half2*>(&dsc));
-                const float sinv = __uint_as_float(lds32(rec + 112));
-                const float s0 = df.x * sinv, s1 = df.y * sinv;
-                acc[0] = fmaf((float)dd[0], s0, acc[0]);
-                acc[1] = fmaf((float)dd[1], s0, acc[1]);
-                acc[2] = fmaf((float)dd[2], s1, acc[2]);
-                acc[3] = fmaf((float)dd[3], s1, acc[3]);
+            }
+#pragma unroll
+            for (int i = 0; i < NBW; ++i) {
+                const int jb = warp + i * kLsWarps;
+                if (jb < n) {
+                    uint32_t a0, a1, a2, a3;
+                    if (WT == T_Q4_0) {
+                        a0 = wq[i][0] & 0x0F0F0F0Fu; a2 = (wq[i][0] >> 4) & 0x0F0F0F0Fu;
+                        a1 = wq[i][1] & 0x0F0F0F0Fu; a3 = (wq[i][1] >> 4) & 0x0F0F0F0Fu;
+                    } else {
+                        a0 = wq[i][0]; a2 = wq[i][1]; a1 = wq[i][2]; a3 = wq[i][3];
+                    }
+                    int dd[4];
+                    imma16832<WT == T_Q4_0>(dd, a0, a1, a2, a3, bx[i][0], bx[i][1], (int)cx[i][0], (int)cx[i][1],
+                                            (int)cx[i][0], (int)cx[i][1]);
+                    const float2 df = __half22float2(*reinterpret_cast<const __half2*>(&dsc[i]));
+                    const float s0 = df.x * sv[i], s1 = df.y * sv[i];
+                    acc[0] = fmaf((float)dd[0], s0, acc[0]);
+                    acc[1] = fmaf((float)dd[1], s0, acc[1]);
+                    acc[2] = fmaf((float)dd[2], s1, acc[2]);
+                    acc[3] = fmaf((float)dd[3], s1, acc[3]);
+                }
             }
             stage_release();
             cur += n;
