@@ -892,10 +892,9 @@ struct laic_dev {
         const int gm = G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8;
         ls_maxch = (cap + cp - 1) / cp;
         ls_pieces = pieces;
-        const size_t rb = laic::ls_record_bytes();
-        CK(cudaMalloc(&ls_rec_x, (size_t)(h / 32) * rb));
-        CK(cudaMalloc(&ls_rec_attn, (size_t)(hq / 32) * rb));
-        CK(cudaMalloc(&ls_rec_act, (size_t)(F / 32) * rb));
+        CK(cudaMalloc(&ls_rec_x, laic::ls_record_bytes(h / 32)));
+        CK(cudaMalloc(&ls_rec_attn, laic::ls_record_bytes(hq / 32)));
+        CK(cudaMalloc(&ls_rec_act, laic::ls_record_bytes(F / 32)));
         CK(cudaMalloc(&ls_ss, (size_t)(h / 16) * 4));
         CK(cudaMalloc(&ls_part, (size_t)max_tiles * pieces * 16 * 4));
         CK(cudaMalloc(&ls_apart, (size_t)Hkv * ls_maxch * gm * (D + 2) * 4));

@@ -74,7 +74,7 @@ size_t ls_smem(int stages, int D, int G, int nb_max, int att_runs);
 int ls_stage_bytes();
 int ls_max_stages();
 int ls_positions_per_chunk(int D);
-int ls_record_bytes();
+size_t ls_record_bytes(int nb);  // activation records of a vector of nb blocks
 cudaError_t ls_prepare(int type, int D, int G, size_t smem, int* blocks_per_sm);
 cudaError_t ls_launch(int type, int D, int G, const LsParams& p, int grid, size_t smem, cudaStream_t st, bool pdl);
 

@@ -33,15 +33,15 @@ size_t ls_smem(int stages, int D, int G, int nb_max, int att_runs) {
     b += 2 * kLsWarps * 16 * 4;                                // tile reductions
     b += (size_t)GM * D * 4 + (size_t)GM * CP * 4 + 3 * GM * 4;  // attention: merged output, scores, softmax state
     b += (size_t)att_runs * GM * 4;                               // attention: merge weights
-    b += 16 + 32;                                              // alignment + broadcast words
-    b += 128 + (size_t)nb_max * kLsRec;                        // alignment + activation records
+    b += 16 + 64;                                              // alignment + broadcast words + zeros
+    b += 128 + ls_rec_bytes(nb_max);                           // alignment + activation records
     return b;
 }
 
 int ls_stage_bytes() { return kLsStage; }
 int ls_max_stages() { return kLsMaxStages; }
 int ls_positions_per_chunk(int D) { return ls_cp(D); }
-int ls_record_bytes() { return kLsRec; }
+size_t ls_record_bytes(int nb) { return ls_rec_bytes(nb); }
 
 cudaError_t ls_prepare(int type, int D, int G, size_t smem, int* blocks_per_sm) {
     auto k = ls_pick(type, D, G);

@@ -35,15 +35,14 @@
 // 2 row tiles (4 for SwiGLU), and the last tile of the block (another ticket)
 // writes it.
 //
-// The matvec inner loop (one sequence). A 16 x 32 tile-block is one integer
-// tensor-core product mma.m16n8k32 (u8 x s8 for Q4_0 nibbles, s8 x s8 for Q8_0)
-// against an activation record whose columns 0..2 are the three balanced base-128
-// digits of the block's 32 activations scaled to 21-bit integers by a power of two
-// (x = p0 2^14 + p1 2^7 + p2, each digit in [-64, 64]); columns 3..7 are zero.
-// Each column's int32 sum is exact; the Q4_0 offset (nibble - 8) enters as the
-// accumulator's initial value -8 sum_k p_jk of column j. Per block the three sums
-// are scaled by d_row x 2^-s in FP32 and accumulated; at the end of a tile the
-// row value is 2^14 A0 + 2^7 A1 + A2.
+// The matvec inner loop (one sequence). A 16 x 32 tile-block is two tensor-core
+// products mma.m16n8k16 (f16 in, f32 accumulate): the block's quants become exact
+// binary16 integers (q - 8 for Q4_0, q for Q8_0) in registers, and the activation
+// record holds the block's 32 values scaled by a power of two 2^s (largest
+// magnitude in [2^10, 2^11)) and split into binary16 hi + lo parts, as columns 0
+// and 1 of the B operand (columns 2..7 zero). Per block the two column sums are
+// scaled by d_row x 2^-s in FP32 and accumulated; a row's value is the sum of its
+// hi and lo accumulators.
 //
 // Every wait is bounded (about one second of SM clocks); a wait that runs out
 // records its code in `err`, and once `err` is set the dependency waits stop
@@ -57,7 +56,7 @@ namespace laic {
 constexpr int kLsWarps = 8;                          // consumer warps
 constexpr int kLsThreads = (kLsWarps + 1) * 32;      // + the producer warp
 constexpr int kLsStage = 9216;                       // ring stage bytes
-constexpr int kLsRec = 128;                          // activation record bytes per 32-column block
+constexpr int kLsRec = 128;                          // activation record bytes per 32-column block (+ 4 B scale)
 constexpr int kLsMaxStages = 24;
 constexpr long long kLsSpin = 2000000000LL;          // clock cycles a dependency wait may take
 
@@ -168,63 +167,25 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
 }
 __device__ __forceinline__ int ld_volatile_i32(const int* a) { return *reinterpret_cast<const volatile int*>(a); }
 
-// D = A (u8 or s8, 16x32) x B (s8, 32x8) + C, int32.
-template <bool A_UNSIGNED>
-__device__ __forceinline__ void imma16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                          uint32_t b1, int c0, int c1, int c2, int c3) {
-    if (A_UNSIGNED)
-        asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-                     "{%10,%11,%12,%13};"
-                     : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-                     : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c0), "r"(c1), "r"(c2), "r"(c3));
-    else
-        asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-                     "{%10,%11,%12,%13};"
-                     : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-                     : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c0), "r"(c1), "r"(c2), "r"(c3));
-}
+// Bytes of the activation records of a vector of nb blocks: nb records of 128 bytes,
+// then the blocks' scales (one float each, padded to 16 bytes).
+__host__ __device__ inline size_t ls_rec_bytes(int nb) { return (size_t)nb * kLsRec + ((size_t)nb * 4 + 15) / 16 * 16; }
 
-// Byte of element i (0..31) of a block inside one digit plane of its record: the B
-// fragment of lane (n, t) is the 8 bytes at t * 8 of plane n, bytes 0..3 holding
-// k = 4t..4t+3 and bytes 4..7 k = 4t+16..4t+19. The weights' k order follows the
-// tile layout: Q4_0 lane t holds columns 8t..8t+7 as nibble bytes (low nibbles are
-// the even columns -> k 4t+m, high nibbles the odd ones -> k 4t+16+m); Q8_0 lane t
-// holds them in fragment order (frag_pos), word 0 then word 1.
-template <int WT>
-__device__ __forceinline__ int ls_rec_byte(int i) {
-    if (WT == T_Q4_0) return (i >> 3) * 8 + (i & 1) * 4 + ((i >> 1) & 3);
-    return (i >> 3) * 8 + frag_pos(i & 7);
-}
-
-// Activation record of one 32-element block, built by one warp: lane i holds element i.
-// Layout: planes p0 / p1 / p2 (32 bytes each), then the accumulator seeds of lanes t = 0
-// (-8 P0, -8 P1) and t = 1 (-8 P2, 0) for Q4_0 (zero for Q8_0), then the block scale 2^-s.
-template <int WT>
-__device__ __forceinline__ void ls_write_record(float v, int lane, uint8_t* rec) {
-    float mx = warp_max(fabsf(v));
+// Activation record of one 32-element block, built by one warp (lane i holds element
+// i): the values times 2^s, split into binary16 hi (bytes 0..63) and lo (64..127),
+// each as 4 column groups of 8 halves in fragment order (the B fragment of
+// mma.m16n8k16 for lanes t = group), and 2^-s into the scale table.
+__device__ __forceinline__ void ls_write_record(float v, int lane, uint8_t* rec, float* scale) {
+    const float mx = warp_max(fabsf(v));
     int ex = 0;
     if (mx > 0.f && isfinite(mx)) frexpf(mx, &ex);  // mx in [2^(ex-1), 2^ex)
-    const int xi = (int)rintf(ldexpf(v, 20 - ex));   // |xi| <= 2^20
-    const int p2 = ((xi + 64) & 127) - 64;
-    const int t1 = (xi - p2) >> 7;
-    const int p1 = ((t1 + 64) & 127) - 64;
-    const int p0 = (t1 - p1) >> 7;
-    const int off = ls_rec_byte<WT>(lane);
-    rec[off] = (uint8_t)(int8_t)p0;
-    rec[32 + off] = (uint8_t)(int8_t)p1;
-    rec[64 + off] = (uint8_t)(int8_t)p2;
-    int s0 = p0, s1 = p1, s2 = p2;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        s0 += __shfl_xor_sync(0xffffffffu, s0, o);
-        s1 += __shfl_xor_sync(0xffffffffu, s1, o);
-        s2 += __shfl_xor_sync(0xffffffffu, s2, o);
-    }
-    if (lane == 0) {
-        const int k = WT == T_Q4_0 ? -8 : 0;
-        *reinterpret_cast<int4*>(rec + 96) = make_int4(k * s0, k * s1, k * s2, 0);
-        *reinterpret_cast<float4*>(rec + 112) = make_float4(ldexpf(1.f, ex - 20), 0.f, 0.f, 0.f);
-    }
+    const float xs = ldexpf(v, 11 - ex);             // exact: a power of two
+    const __half hi = __float2half_rn(xs);
+    const __half lo = __float2half_rn(xs - __half2float(hi));
+    const int off = (lane >> 3) * 16 + frag_pos(lane & 7) * 2;
+    *reinterpret_cast<__half*>(rec + off) = hi;
+    *reinterpret_cast<__half*>(rec + 64 + off) = lo;
+    if (lane == 0) *scale = ldexpf(1.f, ex - 11);
 }
 
 // Named barrier of the consumer warps (the producer warp never joins it).
@@ -259,7 +220,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
     float* hsc = hl + GM;                                       // [GM] rescale of the running output
     float* wrun = hsc + GM;                                     // [att_runs][GM] merge weights of the runs
     int* ictl = reinterpret_cast<int*>((reinterpret_cast<uintptr_t>(wrun + p.att_runs * GM) + 15) & ~uintptr_t(15));
-    uint8_t* act = reinterpret_cast<uint8_t*>(ictl + 8);        // activation records of the phase
+    uint8_t* act = reinterpret_cast<uint8_t*>(ictl + 16);       // activation records of the phase
     act = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(act) + 127) & ~uintptr_t(127));
 
     if (threadIdx.x == 0) {
@@ -400,11 +361,12 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
     // the phase's input records (nb blocks) into `act`; 1/rms from ss_x when `norm`
     auto load_records = [&](const uint8_t* src, int nb, bool norm, int nss) {
         if (ct == 0) {
-            mbar_expect_tx(xbar, (uint32_t)(nb * kLsRec));
-            bulk_g2s(act, src, (uint32_t)(nb * kLsRec), xbar);
+            mbar_expect_tx(xbar, (uint32_t)ls_rec_bytes(nb));
+            bulk_g2s(act, src, (uint32_t)ls_rec_bytes(nb), xbar);
         }
         if (norm && warp == 0) {
             float a = 0.f;
+#pragma unroll 8
             for (int i = lane; i < nss; i += 32) a += __ldcg(p.ss_x + i);
             a = warp_sum(a);
             if (lane == 0) reinterpret_cast<float*>(ictl)[5] = 1.f / sqrtf(a / float(p.h) + p.eps);
@@ -413,12 +375,14 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
         xphase ^= 1u;
         ls_cbar();
     };
-    // One record block of 32 values from one warp (lane i: element i).
-    auto record_block = [&](float v, uint8_t* rec) { ls_write_record<WT>(v, lane, rec); };
+    // Record block b of a vector of nb blocks, from one warp (lane i: element i).
+    auto record_block = [&](float v, uint8_t* recs, int nb, int b) {
+        ls_write_record(v, lane, recs + (size_t)b * kLsRec, reinterpret_cast<float*>(recs + (size_t)nb * kLsRec) + b);
+    };
 
     const uint32_t act_a = smem_u32(act);
-    uint32_t zero_a = smem_u32(ictl + 6);  // 8 zero bytes (ictl[6], ictl[7])
-    if (ct == 0) { ictl[6] = 0; ictl[7] = 0; }
+    const uint32_t zero_a = smem_u32(ictl + 8);  // 16 zero bytes (ictl[8..11])
+    if (ct < 4) ictl[8 + ct] = 0;
     ls_cbar();
 
     unsigned long long* trace = p.trace ? p.trace + (size_t)c * nph * 3 : nullptr;
@@ -441,7 +405,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                 for (int o = 8; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
                 if (lane == 0) p.ss_x[2 * b] = sq;
                 if (lane == 16) p.ss_x[2 * b + 1] = sq;
-                record_block(v * p.layers[0].attn_norm[e], p.rec_x + (size_t)b * kLsRec);
+                record_block(v * p.layers[0].attn_norm[e], p.rec_x, nblk, b);
             }
             if (c == 0 && ct == 0) atomicAdd(p.counts + (size_t)sl * p.vocab + tok, 1u);
             arrive(ph);
@@ -644,7 +608,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                             const float v = obuf[b * 32 + lane];
                             const size_t e = (size_t)j * gq * D + b * 32 + lane;
                             p.attn[e] = v;
-                            record_block(v, p.rec_attn + (e / 32) * kLsRec);
+                            record_block(v, p.rec_attn, p.hq / 32, (int)(e / 32));
                         }
                         if (ct == 0) p.head_tick[j] = 0u;
                         ls_cbar();
@@ -665,10 +629,11 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
         const float inv = reinterpret_cast<const float*>(ictl)[5];
         if (trace && ct == 0) trace[ph * 3 + 1] = ls_now();
         const long long lo = ls_lo(m.nblk, c, G), hi = ls_lo(m.nblk, c + 1, G);
-        // this lane's B fragment (digit columns 0..2; lanes of columns 3..7 read zeros) and seed pair
-        const bool bcol = g < 3, cseed = t < 2;
-        const uint32_t b_off = g * 32 + t * 8, c_off = 96 + t * 8;
+        // this lane's B fragment: column g (0 = hi, 1 = lo, 2..7 zero), k-group t
+        const bool bcol = g < 2;
+        const uint32_t b_off = g * 64 + t * 16;
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        const uint32_t scale_a = act_a + (uint32_t)m.nb * kLsRec;  // the blocks' 2^-s
         long long cur = lo;
         while (cur < hi) {
             const int tile = (int)(cur / m.nb);
@@ -677,13 +642,13 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
             const uint32_t sq = stage_wait();
             const uint32_t ssc = sq + SB * QB;
             // this warp's blocks of the stage (jb = warp + 8 i): all loads first, then the products
-            uint32_t wq[NBW][WT == T_Q4_0 ? 2 : 4], bx[NBW][2], cx[NBW][2], dsc[NBW];
+            uint32_t wq[NBW][WT == T_Q4_0 ? 2 : 4], dsc[NBW];
+            uint4 xv[NBW];
             float sv[NBW];
 #pragma unroll
             for (int i = 0; i < NBW; ++i) {
                 const int jb = warp + i * kLsWarps;
                 if (jb < n) {
-                    const uint32_t rec = act_a + (uint32_t)(k0 + jb) * kLsRec;
                     if (WT == T_Q4_0) {
                         const uint2 w = lds64(sq + jb * QB + lane * 8);
                         wq[i][0] = w.x; wq[i][1] = w.y;
@@ -691,50 +656,42 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                         const uint4 w = lds128(sq + jb * QB + lane * 16);
                         wq[i][0] = w.x; wq[i][1] = w.y; wq[i][2] = w.z; wq[i][3] = w.w;
                     }
-                    const uint2 bb = lds64(bcol ? rec + b_off : zero_a);
-                    bx[i][0] = bb.x; bx[i][1] = bb.y;
-                    if (WT == T_Q4_0) {
-                        const uint2 cc = lds64(cseed ? rec + c_off : zero_a);
-                        cx[i][0] = cc.x; cx[i][1] = cc.y;
-                    } else {
-                        cx[i][0] = cx[i][1] = 0u;
-                    }
+                    xv[i] = lds128(bcol ? act_a + (uint32_t)(k0 + jb) * kLsRec + b_off : zero_a);
                     dsc[i] = lds32(ssc + jb * kTileSBytes + g * 4);
-                    sv[i] = __uint_as_float(lds32(rec + 112));
+                    sv[i] = __uint_as_float(lds32(scale_a + (uint32_t)(k0 + jb) * 4));
                 }
             }
 #pragma unroll
             for (int i = 0; i < NBW; ++i) {
                 const int jb = warp + i * kLsWarps;
                 if (jb < n) {
-                    uint32_t a0, a1, a2, a3;
+                    uint32_t ra[4], rb[4];
                     if (WT == T_Q4_0) {
-                        a0 = wq[i][0] & 0x0F0F0F0Fu; a2 = (wq[i][0] >> 4) & 0x0F0F0F0Fu;
-                        a1 = wq[i][1] & 0x0F0F0F0Fu; a3 = (wq[i][1] >> 4) & 0x0F0F0F0Fu;
+                        decode_q4(wq[i][0], ra);
+                        decode_q4(wq[i][1], rb);
                     } else {
-                        a0 = wq[i][0]; a2 = wq[i][1]; a1 = wq[i][2]; a3 = wq[i][3];
+                        decode_q8(wq[i][0], wq[i][1], ra);
+                        decode_q8(wq[i][2], wq[i][3], rb);
                     }
-                    int dd[4];
-                    imma16832<WT == T_Q4_0>(dd, a0, a1, a2, a3, bx[i][0], bx[i][1], (int)cx[i][0], (int)cx[i][1],
-                                            (int)cx[i][0], (int)cx[i][1]);
+                    float tt[4];
+                    mma16816_z(tt, ra[0], rb[0], ra[1], rb[1], xv[i].x, xv[i].y);
+                    mma16816_acc(tt, ra[2], rb[2], ra[3], rb[3], xv[i].z, xv[i].w);
                     const float2 df = __half22float2(*reinterpret_cast<const __half2*>(&dsc[i]));
                     const float s0 = df.x * sv[i], s1 = df.y * sv[i];
-                    acc[0] = fmaf((float)dd[0], s0, acc[0]);
-                    acc[1] = fmaf((float)dd[1], s0, acc[1]);
-                    acc[2] = fmaf((float)dd[2], s1, acc[2]);
-                    acc[3] = fmaf((float)dd[3], s1, acc[3]);
+                    acc[0] = fmaf(tt[0], s0, acc[0]);
+                    acc[1] = fmaf(tt[1], s0, acc[1]);
+                    acc[2] = fmaf(tt[2], s1, acc[2]);
+                    acc[3] = fmaf(tt[3], s1, acc[3]);
                 }
             }
             stage_release();
             cur += n;
             if (cur != hi && cur % m.nb != 0) continue;
-            // ---- end of this CTA's piece of the tile: rows g and g+8 from the digit columns
-            const float up0 = __shfl_down_sync(0xffffffffu, acc[0], 1);
-            const float up2 = __shfl_down_sync(0xffffffffu, acc[2], 1);
+            // ---- end of this CTA's piece of the tile: rows g and g+8 = hi column + lo column
             float* rb = red + ((tile_i & 1) * kLsWarps + warp) * 16;
             if (t == 0) {
-                rb[g] = 16384.f * acc[0] + 128.f * acc[1] + up0;
-                rb[g + 8] = 16384.f * acc[2] + 128.f * acc[3] + up2;
+                rb[g] = acc[0] + acc[1];
+                rb[g + 8] = acc[2] + acc[3];
             }
             acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
             ls_cbar();
@@ -803,7 +760,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                 if (last) {
                     __threadfence();
                     const float a = __ldcg(p.act + (size_t)b * 32 + lane);
-                    record_block(a, p.rec_act + (size_t)b * kLsRec);
+                    record_block(a, p.rec_act, p.F / 32, b);
                     if (lane == 0) p.rec_tick[b] = 0u;
                 }
             } else {  // LS_O, LS_DN: residual add, its sum of squares, records for the next rmsnorm
@@ -827,7 +784,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                     const float* wn = kind == LS_O ? p.layers[layer].ffn_norm
                                                    : (layer + 1 < L ? p.layers[layer + 1].attn_norm : p.out_norm);
                     const int e = b * 32 + lane;
-                    record_block(__ldcg(p.x + e) * wn[e], p.rec_x + (size_t)b * kLsRec);
+                    record_block(__ldcg(p.x + e) * wn[e], p.rec_x, p.h / 32, b);
                     if (lane == 0) p.rec_tick[b] = 0u;
                 }
             }
