@@ -29,8 +29,8 @@ static int pow2_at_least(int g) { return g <= 1 ? 1 : g <= 2 ? 2 : g <= 4 ? 4 : 
 size_t ls_smem(int stages, int D, int G, int nb_max, int att_runs) {
     const int GM = pow2_at_least(G), CP = ls_cp(D);
     size_t b = (size_t)stages * kLsStage;                      // ring
-    b += 2 * kLsMaxStages * 8 + 16;                            // full / empty / record barriers
-    b += 2 * kLsWarps * 16 * 4;                                // tile reductions
+    b += 2 * kLsMaxStages * 8 + 16 + 2 * kLsQueue * 8;         // full / empty / record / queue barriers
+    b += kLsQueue * kLsWarps * 16 * 4;                         // tile partials queue
     b += (size_t)GM * D * 4 + (size_t)GM * CP * 4 + 3 * GM * 4;  // attention: merged output, scores, softmax state
     b += (size_t)att_runs * GM * 4;                               // attention: merge weights
     b += 16 + 64;                                              // alignment + broadcast words + zeros

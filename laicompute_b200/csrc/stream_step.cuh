@@ -58,6 +58,7 @@ constexpr int kLsThreads = (kLsWarps + 1) * 32;      // + the producer warp
 constexpr int kLsStage = 9216;                       // ring stage bytes
 constexpr int kLsRec = 128;                          // activation record bytes per 32-column block (+ 4 B scale)
 constexpr int kLsMaxStages = 24;
+constexpr int kLsQueue = 8;                          // tile partials in flight between consumers and finishers
 constexpr long long kLsSpin = 2000000000LL;          // clock cycles a dependency wait may take
 
 // tile-blocks per ring stage
@@ -155,9 +156,20 @@ __device__ __forceinline__ LsMat ls_mat(const LsParams& p, int kind, int layer) 
 // Range [ls_lo(c), ls_lo(c + 1)) of n items owned by CTA c of g (never empty while
 // n >= g; with fewer items than CTAs the first n CTAs take one each), and the CTA
 // owning item i. The CTAs owning the items of any contiguous span are consecutive.
-__device__ __forceinline__ long long ls_lo(long long n, int c, int g) { return n >= g ? n * c / g : min((long long)c, n); }
-__device__ __forceinline__ int ls_owner(long long n, long long i, int g) {
-    return n >= g ? (int)(((i + 1) * g + n - 1) / n) - 1 : (int)i;
+// 32-bit arithmetic: n * g stays below 2^32 for every phase (the host checks).
+__device__ __forceinline__ int ls_lo(unsigned n, int c, int g) {
+    return (int)(n >= (unsigned)g ? n * (unsigned)c / (unsigned)g : min((unsigned)c, n));
+}
+__device__ __forceinline__ int ls_owner(unsigned n, unsigned i, int g) {
+    return n >= (unsigned)g ? (int)(((i + 1) * (unsigned)g + n - 1) / n) - 1 : (int)i;
+}
+// atomic add with acquire-release ordering at GPU scope: the caller's earlier writes (and
+// those of its warp, ordered before by __syncwarp) are visible before the count moves,
+// and reads after it see every write released by earlier adds
+__device__ __forceinline__ unsigned atom_add_acq_rel(unsigned* a, unsigned v) {
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(a), "r"(v) : "memory");
+    return old;
 }
 
 __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* a) {
@@ -212,8 +224,10 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
     uint64_t* full = reinterpret_cast<uint64_t*>(ring + (size_t)NST * kLsStage);
     uint64_t* empty = full + kLsMaxStages;
     uint64_t* xbar = empty + kLsMaxStages;
-    float* red = reinterpret_cast<float*>(xbar + 2);            // [2][kLsWarps][16]
-    float* qs = red + 2 * kLsWarps * 16;                        // [GM][D] query rows of a kv head
+    uint64_t* qfull = xbar + 2;                                 // [kLsQueue] a tile's warp partials are in
+    uint64_t* qfree = qfull + kLsQueue;                         // [kLsQueue] the finisher read them
+    float* red = reinterpret_cast<float*>(qfree + kLsQueue);    // [kLsQueue][kLsWarps][16]
+    float* qs = red + kLsQueue * kLsWarps * 16;                 // [GM][D] merged attention output
     float* ss_att = qs + GM * D;                                // [GM][CP] scores, then weights
     float* hm = ss_att + GM * CP;                               // [GM] running max
     float* hl = hm + GM;                                        // [GM] running sum
@@ -229,6 +243,10 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
             mbar_init(empty + s, kLsWarps);
         }
         mbar_init(xbar, 1);
+        for (int q = 0; q < kLsQueue; ++q) {
+            mbar_init(qfull + q, kLsWarps);
+            mbar_init(qfree + q, 1);
+        }
         mbar_fence_init();
     }
     __syncthreads();
@@ -259,10 +277,11 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                 const int sl = p.slots[0];
                 const int pos = p.pos[sl];
                 const int nch = (pos + 1 + CP - 1) / CP;
-                const long long I = (long long)p.kv_heads * nch;
+                const unsigned I = (unsigned)p.kv_heads * nch;
                 const LsLayer& ly = p.layers[layer];
-                for (long long it = ls_lo(I, c, G); it < ls_lo(I, c + 1, G); ++it) {
-                    const int j = (int)(it / nch), ch = (int)(it % nch);
+                const int ilo = ls_lo(I, c, G), ihi = ls_lo(I, c + 1, G);
+                int j = ilo / nch, ch = ilo % nch;
+                for (int it = ilo; it < ihi; ++it, (++ch == nch ? (ch = 0, ++j) : 0)) {
                     // rows of the chunk written by earlier steps (the newest row comes later, from L2)
                     const int r0 = ch * CP, nrows = max(0, min(r0 + CP, pos) - r0);
                     const size_t off = (size_t)sl * p.kv_slot_stride + ((size_t)j * p.kv_cap + r0) * D;
@@ -281,11 +300,11 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                 continue;
             }
             const LsMat m = ls_mat(p, kind, layer);
-            long long cur = ls_lo(m.nblk, c, G);
-            const long long hi = ls_lo(m.nblk, c + 1, G);
+            int cur = ls_lo((unsigned)m.nblk, c, G);
+            const int hi = ls_lo((unsigned)m.nblk, c + 1, G);
+            int k0 = cur % m.nb;
             while (cur < hi) {
-                const int k0 = (int)(cur % m.nb);
-                const int n = (int)min((long long)min(SB, m.nb - k0), hi - cur);
+                const int n = min(min(SB, m.nb - k0), hi - cur);
                 uint8_t* dst = acquire();
                 if (ok) {
                     mbar_expect_tx(full + slot, (uint32_t)(n * (QB + kTileSBytes)));
@@ -296,6 +315,8 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                 }
                 advance();
                 cur += n;
+                k0 += n;
+                if (k0 == m.nb) k0 = 0;
             }
         }
         return;
@@ -323,7 +344,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
     int slot = 0;
     uint32_t round = 0, xphase = 0;
     bool aborted = false;
-    int tile_i = 0;  // tiles this CTA finished (selects the reduction buffer and the finishing warp)
+    int tile_i = 0;  // tile pieces this CTA finished (selects the queue slot and the finishing warp)
 
     // Wait until every CTA arrived at phase `ph`'s counter.
     auto wait_phase = [&](int ph) {
@@ -416,15 +437,15 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
         if (kind == LS_ATT) {
             const LsLayer& ly = p.layers[layer];
             const int nch = (pos + 1 + CP - 1) / CP;
-            const long long I = (long long)p.kv_heads * nch;
-            const long long ilo = ls_lo(I, c, G), ihi = ls_lo(I, c + 1, G);
+            const unsigned I = (unsigned)p.kv_heads * nch;
+            const int ilo = ls_lo(I, c, G), ihi = ls_lo(I, c + 1, G);
             const __half* kg = reinterpret_cast<const __half*>(ly.kc) + (size_t)sl * p.kv_slot_stride;
             const __half* vg = reinterpret_cast<const __half*>(ly.vc) + (size_t)sl * p.kv_slot_stride;
             float2 o_acc[OP2];
             float qreg[GM][E];
             int run_start = 0;
-            for (long long it = ilo; it < ihi; ++it) {
-                const int j = (int)(it / nch), ch = (int)(it % nch);
+            int j = ilo / nch, ch = ilo % nch;
+            for (int it = ilo; it < ihi; ++it, (++ch == nch ? (ch = 0, ++j) : 0)) {
                 if (it == ilo || ch == 0) {
                     // a new kv head: this lane's slice of the group's query rows, fresh softmax state
 #pragma unroll
@@ -554,29 +575,27 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                     }
                     if (ct < gq) { pp[GM * D + ct] = hm[ct]; pp[GM * D + GM + ct] = hl[ct]; }
                     ls_cbar();
-                    const long long jlo = (long long)j * nch, jhi = jlo + nch - 1;
+                    const int jlo = j * nch, jhi = jlo + nch - 1;
                     const int cf = ls_owner(I, jlo, G), cl = ls_owner(I, jhi, G);
                     if (ct == 0) {
-                        __threadfence();
-                        const unsigned old = atomicAdd(p.head_tick + j, 1u);
+                        const unsigned old = atom_add_acq_rel(p.head_tick + j, 1u);
                         ictl[1] = old == (unsigned)(cl - cf);
                     }
                     ls_cbar();
                     if (ictl[1]) {  // the last run of head j: merge every run (CTA order)
-                        __threadfence();
                         const int nruns = cl - cf + 1;
                         // per-run weights exp(m_r - M) / S of each head (warp hh, lanes over runs)
                         if (warp < gq) {
                             const int hh = warp;
                             float M = -INFINITY;
                             for (int r = lane; r < nruns; r += 32) {
-                                const int rs = (int)(max(jlo, ls_lo(I, cf + r, G)) - jlo);
+                                const int rs = max(jlo, ls_lo(I, cf + r, G)) - jlo;
                                 M = fmaxf(M, __ldcg(p.apart + ((size_t)j * p.att_maxch + rs) * (GM * (D + 2)) + GM * D + hh));
                             }
                             M = warp_max(M);
                             float S = 0.f;
                             for (int r = lane; r < nruns; r += 32) {
-                                const int rs = (int)(max(jlo, ls_lo(I, cf + r, G)) - jlo);
+                                const int rs = max(jlo, ls_lo(I, cf + r, G)) - jlo;
                                 const float* q2 = p.apart + ((size_t)j * p.att_maxch + rs) * (GM * (D + 2));
                                 const float e = expf(__ldcg(q2 + GM * D + hh) - M);
                                 wrun[r * GM + hh] = e;
@@ -593,7 +612,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                             float ax = 0.f, ay = 0.f;
 #pragma unroll 4
                             for (int r = 0; r < nruns; ++r) {
-                                const int rs = (int)(max(jlo, ls_lo(I, cf + r, G)) - jlo);
+                                const int rs = max(jlo, ls_lo(I, cf + r, G)) - jlo;
                                 const float2 ov = __ldcg(reinterpret_cast<const float2*>(
                                                              p.apart + ((size_t)j * p.att_maxch + rs) * (GM * (D + 2))) + i2);
                                 const float w = wrun[r * GM + hh];
@@ -628,17 +647,15 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
         }
         const float inv = reinterpret_cast<const float*>(ictl)[5];
         if (trace && ct == 0) trace[ph * 3 + 1] = ls_now();
-        const long long lo = ls_lo(m.nblk, c, G), hi = ls_lo(m.nblk, c + 1, G);
+        const int lo = ls_lo((unsigned)m.nblk, c, G), hi = ls_lo((unsigned)m.nblk, c + 1, G);
         // this lane's B fragment: column g (0 = hi, 1 = lo, 2..7 zero), k-group t
         const bool bcol = g < 2;
         const uint32_t b_off = g * 64 + t * 16;
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         const uint32_t scale_a = act_a + (uint32_t)m.nb * kLsRec;  // the blocks' 2^-s
-        long long cur = lo;
+        int cur = lo, tile = lo / m.nb, k0 = lo % m.nb;
         while (cur < hi) {
-            const int tile = (int)(cur / m.nb);
-            const int k0 = (int)(cur % m.nb);
-            const int n = (int)min((long long)min(SB, m.nb - k0), hi - cur);
+            const int n = min(min(SB, m.nb - k0), hi - cur);
             const uint32_t sq = stage_wait();
             const uint32_t ssc = sq + SB * QB;
             // this warp's blocks of the stage (jb = warp + 8 i): all loads first, then the products
@@ -686,43 +703,51 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
             }
             stage_release();
             cur += n;
-            if (cur != hi && cur % m.nb != 0) continue;
-            // ---- end of this CTA's piece of the tile: rows g and g+8 = hi column + lo column
-            float* rb = red + ((tile_i & 1) * kLsWarps + warp) * 16;
+            k0 += n;
+            const int this_tile = tile;
+            if (k0 == m.nb) { k0 = 0; ++tile; }
+            if (cur != hi && k0 != 0) continue;
+            // ---- end of this CTA's piece of a tile: rows g and g+8 = hi column + lo column, into
+            //      the tile's queue slot; the finishing warp adds the warps' pieces, the others go on
+            const int qs_i = tile_i & (kLsQueue - 1);
+            const uint32_t use = (uint32_t)(tile_i / kLsQueue);
+            if (use > 0 && !mbar_wait(qfree + qs_i, (use - 1) & 1u, p.err)) aborted = true;
+            float* rb = red + (qs_i * kLsWarps + warp) * 16;
             if (t == 0) {
                 rb[g] = acc[0] + acc[1];
                 rb[g + 8] = acc[2] + acc[3];
             }
             acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
-            ls_cbar();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(qfull + qs_i);
             const int fw = tile_i % kLsWarps;
-            const float* rbuf = red + (tile_i & 1) * kLsWarps * 16;
             ++tile_i;
             if (warp != fw) continue;
+            if (!mbar_wait(qfull + qs_i, use & 1u, p.err)) aborted = true;
             // ---- the finishing warp: the CTA's piece = sum over warps (fixed order)
             float v = 0.f;
             if (lane < 16)
-                for (int w = 0; w < kLsWarps; ++w) v += rbuf[w * 16 + lane];
+                for (int w = 0; w < kLsWarps; ++w) v += red[(qs_i * kLsWarps + w) * 16 + lane];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(qfree + qs_i);
             // pieces of a tile shared with other CTAs meet in scratch; the last adds them in order
-            const long long t_first = (long long)tile * m.nb;
-            const int cf = ls_owner(m.nblk, t_first, G), cl = ls_owner(m.nblk, t_first + m.nb - 1, G);
+            const unsigned t_first = (unsigned)this_tile * m.nb;
+            const int cf = ls_owner((unsigned)m.nblk, t_first, G), cl = ls_owner((unsigned)m.nblk, t_first + m.nb - 1, G);
             if (cl > cf) {
-                float* slot_p = p.part + ((size_t)tile * p.part_pieces) * 16;
+                float* slot_p = p.part + ((size_t)this_tile * p.part_pieces) * 16;
                 if (lane < 16) slot_p[(c - cf) * 16 + lane] = v;
-                __threadfence();
                 __syncwarp();
                 unsigned last = 0;
-                if (lane == 0) last = atomicAdd(p.tile_tick + tile, 1u) == (unsigned)(cl - cf);
+                if (lane == 0) last = atom_add_acq_rel(p.tile_tick + this_tile, 1u) == (unsigned)(cl - cf);
                 last = __shfl_sync(0xffffffffu, last, 0);
                 if (!last) continue;
-                __threadfence();
                 v = 0.f;
                 if (lane < 16)
                     for (int i = 0; i <= cl - cf; ++i) v += __ldcg(slot_p + i * 16 + lane);
-                if (lane == 0) p.tile_tick[tile] = 0u;
+                if (lane == 0) p.tile_tick[this_tile] = 0u;
             }
             if (norm) v *= inv;
-            const int r = tile * 16 + lane;  // this lane's row (lanes 0..15)
+            const int r = this_tile * 16 + lane;  // this lane's row (lanes 0..15)
             const bool live = lane < 16 && r < m.rows;
             if (kind == LS_LM) {
                 if (live) p.logits[r] = v;
@@ -749,16 +774,14 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
             } else if (kind == LS_GU) {
                 // rows 2o (gate) and 2o+1 (up): act[o] = silu(gate) * up
                 const float up = __shfl_down_sync(0xffffffffu, v, 1);
-                const int o = tile * 8 + (lane >> 1);
+                const int o = this_tile * 8 + (lane >> 1);
                 if (live && (lane & 1) == 0) p.act[o] = (v / (1.f + expf(-v))) * up;
-                __threadfence();
                 __syncwarp();
                 unsigned last = 0;
-                const int b = tile / 4;  // record block of act[32b .. 32b+31]
-                if (lane == 0) last = atomicAdd(p.rec_tick + b, 1u) == 3u;
+                const int b = this_tile / 4;  // record block of act[32b .. 32b+31]
+                if (lane == 0) last = atom_add_acq_rel(p.rec_tick + b, 1u) == 3u;
                 last = __shfl_sync(0xffffffffu, last, 0);
                 if (last) {
-                    __threadfence();
                     const float a = __ldcg(p.act + (size_t)b * 32 + lane);
                     record_block(a, p.rec_act, p.F / 32, b);
                     if (lane == 0) p.rec_tick[b] = 0u;
@@ -772,15 +795,13 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                 float sq = live ? xn * xn : 0.f;
 #pragma unroll
                 for (int o = 8; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-                if (lane == 0) p.ss_x[tile] = sq;
-                __threadfence();
+                if (lane == 0) p.ss_x[this_tile] = sq;
                 __syncwarp();
                 unsigned last = 0;
-                const int b = tile / 2;
-                if (lane == 0) last = atomicAdd(p.rec_tick + b, 1u) == 1u;
+                const int b = this_tile / 2;
+                if (lane == 0) last = atom_add_acq_rel(p.rec_tick + b, 1u) == 1u;
                 last = __shfl_sync(0xffffffffu, last, 0);
                 if (last) {
-                    __threadfence();
                     const float* wn = kind == LS_O ? p.layers[layer].ffn_norm
                                                    : (layer + 1 < L ? p.layers[layer + 1].attn_norm : p.out_norm);
                     const int e = b * 32 + lane;
