@@ -113,7 +113,8 @@ struct LsParams {
     unsigned long long* epoch;            // launches completed
     int* err;
     int nstages;                          // ring depth
-    unsigned long long* trace;            // optional: [CTA][phase][3] globaltimer stamps (start, inputs ready, done)
+    unsigned long long* trace;            // optional: [CTA][phase][3] globaltimer stamps (start, inputs ready, done),
+                                          // then [CTA][4] wait statistics (see ls_step_kernel)
 };
 
 __device__ __forceinline__ unsigned long long ls_now() {
@@ -260,9 +261,18 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
         uint32_t round = 0;
         bool waited = false;
         bool ok = true;
+        unsigned long long pw_n = 0, pw_t = 0;  // trace: empty-slot waits that blocked, their ns
         auto acquire = [&]() -> uint8_t* {
             // the consumers released this slot's previous use (first round: free)
-            if (ok && round > 0 && !mbar_wait(empty + slot, (round - 1) & 1u, p.err)) ok = false;
+            if (ok && round > 0) {
+                if (p.trace && !mbar_try_wait(empty + slot, (round - 1) & 1u)) {
+                    const unsigned long long t0 = ls_now();
+                    if (!mbar_wait(empty + slot, (round - 1) & 1u, p.err)) ok = false;
+                    ++pw_n; pw_t += ls_now() - t0;
+                } else if (!mbar_wait(empty + slot, (round - 1) & 1u, p.err)) {
+                    ok = false;
+                }
+            }
             return ring + (size_t)slot * kLsStage;
         };
         auto advance = [&]() {
@@ -319,6 +329,10 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                 if (k0 == m.nb) k0 = 0;
             }
         }
+        if (p.trace) {
+            unsigned long long* st = p.trace + (size_t)G * nph * 3 + (size_t)c * 4;
+            st[0] = pw_n; st[1] = pw_t;
+        }
         return;
     }
 
@@ -370,8 +384,15 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
             }
         }
     };
+    unsigned long long cw_n = 0, cw_t = 0;  // trace: warp 0's stage waits that blocked, their ns
     auto stage_wait = [&]() -> uint32_t {
-        if (!mbar_wait(full + slot, round & 1u, p.err)) aborted = true;
+        if (p.trace && ct == 0 && !mbar_try_wait(full + slot, round & 1u)) {
+            const unsigned long long t0 = ls_now();
+            if (!mbar_wait(full + slot, round & 1u, p.err)) aborted = true;
+            ++cw_n; cw_t += ls_now() - t0;
+        } else if (!mbar_wait(full + slot, round & 1u, p.err)) {
+            aborted = true;
+        }
         return smem_u32(ring + (size_t)slot * kLsStage);
     };
     auto stage_release = [&]() {
@@ -811,6 +832,10 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
             }
         }
         arrive(ph);
+    }
+    if (p.trace && ct == 0) {
+        unsigned long long* st = p.trace + (size_t)G * nph * 3 + (size_t)c * 4;
+        st[2] = cw_n; st[3] = cw_t;
     }
     (void)aborted;
 }

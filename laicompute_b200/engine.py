@@ -146,7 +146,9 @@ class Engine:
         n, ctas, phases = ctypes.c_int64(), ctypes.c_int32(), ctypes.c_int32()
         check(lib().laic_dev_step_trace(self.h, out.ctypes.data, cap, ctypes.byref(n), ctypes.byref(ctas),
                                         ctypes.byref(phases)))
-        return out[: n.value].reshape(ctas.value, phases.value, 3)
+        stamps = ctas.value * phases.value * 3
+        self.last_wait_stats = out[stamps: n.value].reshape(ctas.value, 4)
+        return out[:stamps].reshape(ctas.value, phases.value, 3)
 
     def profile(self, tokens: np.ndarray, steps: int) -> dict:
         """Per-kernel-family {name: (launches, total_us, bytes)} over `steps` eager full steps of slots 0..n-1."""
