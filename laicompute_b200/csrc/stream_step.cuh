@@ -201,6 +201,24 @@ __device__ __forceinline__ void ls_write_record(float v, int lane, uint8_t* rec,
     if (lane == 0) *scale = ldexpf(1.f, ex - 11);
 }
 
+// Bounded wait for an mbarrier phase that backs off with nanosleep between polls, for a
+// thread that may wait long (the producer on a full ring): a hot poll would take issue
+// slots from the consumer warps of its scheduler. Returns false after ~1 s (err set).
+__device__ __forceinline__ bool ls_mbar_wait_backoff(uint64_t* bar, uint32_t parity, int* err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    unsigned ns = 32;
+    while (!mbar_try_wait(bar, parity)) {
+        __nanosleep(ns);
+        ns = ns < 256 ? ns * 2 : 256;
+        if (clock64() - t0 > kLsSpin) {
+            atomicExch(err, kErrMbarrier);
+            return false;
+        }
+    }
+    return true;
+}
+
 // Named barrier of the consumer warps (the producer warp never joins it).
 __device__ __forceinline__ void ls_cbar() { named_sync(1, kLsWarps * 32); }
 
@@ -267,9 +285,9 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
             if (ok && round > 0) {
                 if (p.trace && !mbar_try_wait(empty + slot, (round - 1) & 1u)) {
                     const unsigned long long t0 = ls_now();
-                    if (!mbar_wait(empty + slot, (round - 1) & 1u, p.err)) ok = false;
+                    if (!ls_mbar_wait_backoff(empty + slot, (round - 1) & 1u, p.err)) ok = false;
                     ++pw_n; pw_t += ls_now() - t0;
-                } else if (!mbar_wait(empty + slot, (round - 1) & 1u, p.err)) {
+                } else if (!ls_mbar_wait_backoff(empty + slot, (round - 1) & 1u, p.err)) {
                     ok = false;
                 }
             }
