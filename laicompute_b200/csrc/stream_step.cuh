@@ -201,16 +201,16 @@ __device__ __forceinline__ void ls_write_record(float v, int lane, uint8_t* rec,
     if (lane == 0) *scale = ldexpf(1.f, ex - 11);
 }
 
-// Bounded wait for an mbarrier phase that backs off with nanosleep between polls, for a
-// thread that may wait long (the producer on a full ring): a hot poll would take issue
-// slots from the consumer warps of its scheduler. Returns false after ~1 s (err set).
-__device__ __forceinline__ bool ls_mbar_wait_backoff(uint64_t* bar, uint32_t parity, int* err) {
+// Bounded wait for an mbarrier phase that backs off with nanosleep between polls: a hot
+// poll (try_wait and the clock read in a tight loop) takes issue slots and the
+// conversion pipe from the warps doing the step's work. Returns false after ~1 s (err set).
+__device__ __forceinline__ bool ls_mbar_wait_backoff(uint64_t* bar, uint32_t parity, int* err, unsigned max_ns = 256) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
-    unsigned ns = 32;
+    unsigned ns = 16;
     while (!mbar_try_wait(bar, parity)) {
         __nanosleep(ns);
-        ns = ns < 256 ? ns * 2 : 256;
+        ns = ns < max_ns ? ns * 2 : max_ns;
         if (clock64() - t0 > kLsSpin) {
             atomicExch(err, kErrMbarrier);
             return false;
@@ -402,15 +402,16 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
             }
         }
     };
-    unsigned long long cw_n = 0, cw_t = 0;  // trace: warp 0's stage waits that blocked, their ns
     auto stage_wait = [&]() -> uint32_t {
-        if (p.trace && ct == 0 && !mbar_try_wait(full + slot, round & 1u)) {
+        if (p.trace && lane == 0 && !mbar_try_wait(full + slot, round & 1u)) {
             const unsigned long long t0 = ls_now();
-            if (!mbar_wait(full + slot, round & 1u, p.err)) aborted = true;
-            ++cw_n; cw_t += ls_now() - t0;
-        } else if (!mbar_wait(full + slot, round & 1u, p.err)) {
+            if (!ls_mbar_wait_backoff(full + slot, round & 1u, p.err, 64)) aborted = true;
+            atomicAdd(reinterpret_cast<unsigned long long*>(ictl + 12), 1ull);
+            atomicAdd(reinterpret_cast<unsigned long long*>(ictl + 14), ls_now() - t0);
+        } else if (!ls_mbar_wait_backoff(full + slot, round & 1u, p.err, 64)) {
             aborted = true;
         }
+        __syncwarp();
         return smem_u32(ring + (size_t)slot * kLsStage);
     };
     auto stage_release = [&]() {
@@ -431,7 +432,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
             a = warp_sum(a);
             if (lane == 0) reinterpret_cast<float*>(ictl)[5] = 1.f / sqrtf(a / float(p.h) + p.eps);
         }
-        if (!mbar_wait(xbar, xphase, p.err)) aborted = true;
+        if (!ls_mbar_wait_backoff(xbar, xphase, p.err, 64)) aborted = true;
         xphase ^= 1u;
         ls_cbar();
     };
@@ -441,8 +442,8 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
     };
 
     const uint32_t act_a = smem_u32(act);
-    const uint32_t zero_a = smem_u32(ictl + 8);  // 16 zero bytes (ictl[8..11])
-    if (ct < 4) ictl[8 + ct] = 0;
+    const uint32_t zero_a = smem_u32(ictl + 8);  // 16 zero bytes (ictl[8..11]); [12..15] trace wait counters
+    if (ct < 8) ictl[8 + ct] = 0;
     ls_cbar();
 
     unsigned long long* trace = p.trace ? p.trace + (size_t)c * nph * 3 : nullptr;
@@ -750,7 +751,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
             //      the tile's queue slot; the finishing warp adds the warps' pieces, the others go on
             const int qs_i = tile_i & (kLsQueue - 1);
             const uint32_t use = (uint32_t)(tile_i / kLsQueue);
-            if (use > 0 && !mbar_wait(qfree + qs_i, (use - 1) & 1u, p.err)) aborted = true;
+            if (use > 0 && !ls_mbar_wait_backoff(qfree + qs_i, (use - 1) & 1u, p.err, 64)) aborted = true;
             float* rb = red + (qs_i * kLsWarps + warp) * 16;
             if (t == 0) {
                 rb[g] = acc[0] + acc[1];
@@ -762,7 +763,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
             const int fw = tile_i % kLsWarps;
             ++tile_i;
             if (warp != fw) continue;
-            if (!mbar_wait(qfull + qs_i, use & 1u, p.err)) aborted = true;
+            if (!ls_mbar_wait_backoff(qfull + qs_i, use & 1u, p.err, 64)) aborted = true;
             // ---- the finishing warp: the CTA's piece = sum over warps (fixed order)
             float v = 0.f;
             if (lane < 16)
@@ -851,9 +852,11 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
         }
         arrive(ph);
     }
+    ls_cbar();
     if (p.trace && ct == 0) {
         unsigned long long* st = p.trace + (size_t)G * nph * 3 + (size_t)c * 4;
-        st[2] = cw_n; st[3] = cw_t;
+        st[2] = reinterpret_cast<unsigned long long*>(ictl + 12)[0];
+        st[3] = reinterpret_cast<unsigned long long*>(ictl + 14)[0];
     }
     (void)aborted;
 }
