@@ -402,16 +402,24 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
             }
         }
     };
+    // The next stage's readiness is polled right after a stage is acquired, so the poll's
+    // round trip overlaps the current stage's work instead of preceding the next one.
+    bool next_ready = false;
     auto stage_wait = [&]() -> uint32_t {
-        if (p.trace && lane == 0 && !mbar_try_wait(full + slot, round & 1u)) {
-            const unsigned long long t0 = ls_now();
-            if (!ls_mbar_wait_backoff(full + slot, round & 1u, p.err, 64)) aborted = true;
-            atomicAdd(reinterpret_cast<unsigned long long*>(ictl + 12), 1ull);
-            atomicAdd(reinterpret_cast<unsigned long long*>(ictl + 14), ls_now() - t0);
-        } else if (!ls_mbar_wait_backoff(full + slot, round & 1u, p.err, 64)) {
-            aborted = true;
+        if (!next_ready) {
+            if (p.trace && lane == 0 && !mbar_try_wait(full + slot, round & 1u)) {
+                const unsigned long long t0 = ls_now();
+                if (!ls_mbar_wait_backoff(full + slot, round & 1u, p.err, 64)) aborted = true;
+                atomicAdd(reinterpret_cast<unsigned long long*>(ictl + 12), 1ull);
+                atomicAdd(reinterpret_cast<unsigned long long*>(ictl + 14), ls_now() - t0);
+            } else if (!ls_mbar_wait_backoff(full + slot, round & 1u, p.err, 64)) {
+                aborted = true;
+            }
         }
         __syncwarp();
+        const int ns = slot + 1 == p.nstages ? 0 : slot + 1;
+        const uint32_t nr = slot + 1 == p.nstages ? round + 1 : round;
+        next_ready = mbar_try_wait(full + ns, nr & 1u);
         return smem_u32(ring + (size_t)slot * kLsStage);
     };
     auto stage_release = [&]() {
