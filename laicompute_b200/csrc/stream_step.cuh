@@ -53,7 +53,7 @@
 
 namespace laic {
 
-constexpr int kLsWarps = 8;                          // consumer warps
+constexpr int kLsWarps = 16;                         // consumer warps
 constexpr int kLsThreads = (kLsWarps + 1) * 32;      // + the producer warp
 constexpr int kLsStage = 9216;                       // ring stage bytes
 constexpr int kLsRec = 128;                          // activation record bytes per 32-column block (+ 4 B scale)
