@@ -59,6 +59,7 @@ constexpr int kLsStage = 9216;                       // ring stage bytes
 constexpr int kLsRec = 128;                          // activation record bytes per 32-column block (+ 4 B scale)
 constexpr int kLsMaxStages = 24;
 constexpr int kLsQueue = 8;                          // tile partials in flight between consumers and finishers
+constexpr int kLsIssue = 8;                          // ring stages the producer warp's lanes issue together
 constexpr long long kLsSpin = 2000000000LL;          // clock cycles a dependency wait may take
 
 // tile-blocks per ring stage
@@ -274,82 +275,86 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
     // producer warp: every stage of every phase, in order, as the ring frees up
     // =====================================================================
     if (warp == kLsWarps) {
-        if (lane != 0) return;
-        int slot = 0;
-        uint32_t round = 0;
+        // Every lane steps the same stage sequence; in each batch of kLsIssue stages lane l
+        // waits for the slot of stage i0 + l and issues its copies, so the copies of a batch
+        // go out together (one lane alone issues about one copy per 250 ns).
+        int ph = -1, kind = LS_EMB, cur = 0, hi = 0, k0 = 0;
+        LsMat m{};
+        const LsLayer* aly = nullptr;
+        int apos = 0, asl = 0, nch = 1, it = 0, ihi = 0, j = 0, ch = 0, kvs = 0;
         bool waited = false;
-        bool ok = true;
-        unsigned long long pw_n = 0, pw_t = 0;  // trace: empty-slot waits that blocked, their ns
-        auto acquire = [&]() -> uint8_t* {
-            // the consumers released this slot's previous use (first round: free)
-            if (ok && round > 0) {
-                if (p.trace && !mbar_try_wait(empty + slot, (round - 1) & 1u)) {
-                    const unsigned long long t0 = ls_now();
-                    if (!ls_mbar_wait_backoff(empty + slot, (round - 1) & 1u, p.err)) ok = false;
-                    ++pw_n; pw_t += ls_now() - t0;
-                } else if (!ls_mbar_wait_backoff(empty + slot, (round - 1) & 1u, p.err)) {
-                    ok = false;
-                }
-            }
-            return ring + (size_t)slot * kLsStage;
-        };
-        auto advance = [&]() {
-            if (++slot == NST) { slot = 0; ++round; }
-        };
-        for (int ph = 0; ph < nph; ++ph) {
-            const int kind = ls_kind(ph, L);
-            if (kind == LS_EMB) continue;
-            const int layer = (ph - 1) / 5;
-            if (kind == LS_ATT) {
-                if (!waited) { pdl_wait(); waited = true; }  // positions come from the previous step
-                const int sl = p.slots[0];
-                const int pos = p.pos[sl];
-                const int nch = (pos + 1 + CP - 1) / CP;
-                const unsigned I = (unsigned)p.kv_heads * nch;
-                const LsLayer& ly = p.layers[layer];
-                const int ilo = ls_lo(I, c, G), ihi = ls_lo(I, c + 1, G);
-                int j = ilo / nch, ch = ilo % nch;
-                for (int it = ilo; it < ihi; ++it, (++ch == nch ? (ch = 0, ++j) : 0)) {
-                    // rows of the chunk written by earlier steps (the newest row comes later, from L2)
-                    const int r0 = ch * CP, nrows = max(0, min(r0 + CP, pos) - r0);
-                    const size_t off = (size_t)sl * p.kv_slot_stride + ((size_t)j * p.kv_cap + r0) * D;
-                    for (int kvs = 0; kvs < 2; ++kvs) {
-                        uint8_t* dst = acquire();
-                        const __half* src = reinterpret_cast<const __half*>(kvs ? ly.vc : ly.kc) + off;
-                        if (ok && nrows > 0) {
-                            mbar_expect_tx(full + slot, (uint32_t)(nrows * D * 2));
-                            bulk_g2s(dst, src, (uint32_t)(nrows * D * 2), full + slot);
-                        } else {
-                            mbar_arrive(full + slot);  // nothing to copy (or a failed wait): the stage is ready
-                        }
-                        advance();
+        // the next stage's copies: (src0, bytes0) into the stage, (src1, bytes1) at SB * QB
+        auto next = [&](const uint8_t*& s0, uint32_t& b0, const uint8_t*& s1, uint32_t& b1) -> bool {
+            for (;;) {
+                if (kind == LS_ATT) {
+                    if (it < ihi) {
+                        // rows of the chunk written by earlier steps (the newest row comes later, from L2)
+                        const int r0 = ch * CP, nrows = max(0, min(r0 + CP, apos) - r0);
+                        const size_t off = (size_t)asl * p.kv_slot_stride + ((size_t)j * p.kv_cap + r0) * D;
+                        s0 = reinterpret_cast<const uint8_t*>(reinterpret_cast<const __half*>(kvs ? aly->vc : aly->kc) + off);
+                        b0 = (uint32_t)(nrows * D * 2);
+                        s1 = nullptr; b1 = 0;
+                        if (++kvs == 2) { kvs = 0; ++it; if (++ch == nch) { ch = 0; ++j; } }
+                        return true;
+                    }
+                } else if (kind != LS_EMB) {
+                    if (cur < hi) {
+                        const int n = min(min(SB, m.nb - k0), hi - cur);
+                        s0 = m.q + (size_t)cur * QB; b0 = (uint32_t)(n * QB);
+                        s1 = m.s + (size_t)cur * kTileSBytes; b1 = (uint32_t)(n * kTileSBytes);
+                        cur += n; k0 += n;
+                        if (k0 == m.nb) k0 = 0;
+                        return true;
                     }
                 }
-                continue;
-            }
-            const LsMat m = ls_mat(p, kind, layer);
-            int cur = ls_lo((unsigned)m.nblk, c, G);
-            const int hi = ls_lo((unsigned)m.nblk, c + 1, G);
-            int k0 = cur % m.nb;
-            while (cur < hi) {
-                const int n = min(min(SB, m.nb - k0), hi - cur);
-                uint8_t* dst = acquire();
-                if (ok) {
-                    mbar_expect_tx(full + slot, (uint32_t)(n * (QB + kTileSBytes)));
-                    bulk_g2s(dst, m.q + cur * QB, (uint32_t)(n * QB), full + slot);
-                    bulk_g2s(dst + SB * QB, m.s + cur * kTileSBytes, (uint32_t)(n * kTileSBytes), full + slot);
-                } else {
-                    mbar_arrive(full + slot);
+                if (++ph >= nph) return false;  // the next phase with stages
+                kind = ls_kind(ph, L);
+                const int layer = (ph - 1) / 5;
+                if (kind == LS_ATT) {
+                    if (!waited) { pdl_wait(); waited = true; }  // positions come from the previous step
+                    asl = p.slots[0];
+                    apos = p.pos[asl];
+                    nch = (apos + 1 + CP - 1) / CP;
+                    const unsigned I = (unsigned)p.kv_heads * nch;
+                    aly = p.layers + layer;
+                    it = ls_lo(I, c, G); ihi = ls_lo(I, c + 1, G);
+                    j = it / nch; ch = it % nch; kvs = 0;
+                } else if (kind != LS_EMB) {
+                    m = ls_mat(p, kind, layer);
+                    cur = ls_lo((unsigned)m.nblk, c, G); hi = ls_lo((unsigned)m.nblk, c + 1, G);
+                    k0 = m.nb > 0 ? cur % m.nb : 0;
                 }
-                advance();
-                cur += n;
-                k0 += n;
-                if (k0 == m.nb) k0 = 0;
             }
-        }
-        if (p.trace) {
-            unsigned long long* st = p.trace + (size_t)G * nph * 3 + (size_t)c * 4;
-            st[0] = pw_n; st[1] = pw_t;
+        };
+        bool ok = true;
+        for (int i0 = 0;;) {
+            const uint8_t *s0 = nullptr, *s1 = nullptr;
+            uint32_t b0 = 0, b1 = 0;
+            int cnt = 0;
+            for (int l = 0; l < kLsIssue; ++l) {
+                const uint8_t *t0, *t1;
+                uint32_t c0, c1;
+                if (!next(t0, c0, t1, c1)) break;
+                if (lane == l) { s0 = t0; b0 = c0; s1 = t1; b1 = c1; }
+                ++cnt;
+            }
+            if (cnt == 0) break;
+            if (lane < cnt) {
+                const int i = i0 + lane, sl = i % NST;
+                const uint32_t r = (uint32_t)(i / NST);
+                // the consumers released this slot's previous use (first round: free)
+                if (ok && r > 0 && !ls_mbar_wait_backoff(empty + sl, (r - 1) & 1u, p.err)) ok = false;
+                uint8_t* dst = ring + (size_t)sl * kLsStage;
+                if (ok && b0 + b1 > 0) {
+                    mbar_expect_tx(full + sl, b0 + b1);
+                    if (b0) bulk_g2s(dst, s0, b0, full + sl);
+                    if (b1) bulk_g2s(dst + SB * QB, s1, b1, full + sl);
+                } else {
+                    mbar_arrive(full + sl);  // nothing to copy (or a failed wait): the stage is ready
+                }
+            }
+            __syncwarp();
+            i0 += cnt;
         }
         return;
     }
