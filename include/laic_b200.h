@@ -181,8 +181,9 @@ LAIC_API int laic_dev_profile(laic_dev* dev, int32_t nseq, const uint32_t* token
  * out[(cta * phases + phase) * 3 + k] with k = 0 phase start, 1 inputs ready
  * (dependency met, activation records loaded), 2 phase done. Phases: 0 the
  * embedding, then per layer QKV, attention, O, gate/up, down, then the lm_head.
- * After those, per CTA 4 counters: the producer's waits for a free ring slot
- * (count, ns) and the consumer warps' waits for a filled slot (count, ns, all warps).
+ * After those, per CTA and consumer warp 5 counters (ns): waits for a filled
+ * ring stage, waits at tile ends, finishing epilogues, phase waits, and the
+ * whole phase loop.
  * No counterpart in the reference. */
 LAIC_API int laic_dev_step_trace(laic_dev* dev, uint64_t* out, int64_t max_entries, int64_t* n, int32_t* ctas,
                                  int32_t* phases);

@@ -907,7 +907,7 @@ struct laic_dev {
         CK(cudaMalloc(&ls_done, ls_done_bytes));
         CK(cudaMalloc(&ls_epoch, 8));
         if (trace_on) {
-            const size_t tb = ((size_t)Gc * laic::ls_phases(L) * 3 + (size_t)Gc * 4) * 8;
+            const size_t tb = ((size_t)Gc * laic::ls_phases(L) * 3 + (size_t)Gc * laic::ls_trace_warp_words()) * 8;
             CK(cudaMalloc(&ls_trace, tb));
             CK(cudaMemset(ls_trace, 0, tb));
         }
@@ -1697,7 +1697,7 @@ int laic_dev_step_trace(laic_dev* d, uint64_t* out, int64_t max_entries, int64_t
                                                "and run a one-sequence step on the persistent kernel");
     CK(cudaSetDevice(d->device));
     CK(cudaStreamSynchronize(d->st));
-    const int64_t total = (int64_t)num_sms() * laic::ls_phases(d->L) * 3 + (int64_t)num_sms() * 4;
+    const int64_t total = (int64_t)num_sms() * laic::ls_phases(d->L) * 3 + (int64_t)num_sms() * laic::ls_trace_warp_words();
     *n = std::min(total, max_entries);
     *ctas = num_sms();
     *phases = laic::ls_phases(d->L);

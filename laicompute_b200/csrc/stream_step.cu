@@ -39,6 +39,7 @@ size_t ls_smem(int stages, int D, int G, int nb_max, int att_runs) {
 }
 
 int ls_stage_bytes() { return kLsStage; }
+int ls_trace_warp_words() { return kLsWarps * 5; }
 int ls_max_stages() { return kLsMaxStages; }
 int ls_positions_per_chunk(int D) { return ls_cp(D); }
 size_t ls_record_bytes(int nb) { return ls_rec_bytes(nb); }

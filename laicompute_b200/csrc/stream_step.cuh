@@ -410,7 +410,11 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
     // The next stage's readiness is polled right after a stage is acquired, so the poll's
     // round trip overlaps the current stage's work instead of preceding the next one.
     bool next_ready = false;
+    // trace: per-warp ns spent in [0] stage waits, [1] tile-end queue waits, [2] finishing epilogues,
+    // [3] phase waits (dependency + records), [4] the whole phase loop
+    unsigned long long tt_acc[5] = {0, 0, 0, 0, 0};
     auto stage_wait = [&]() -> uint32_t {
+        const unsigned long long tw0 = p.trace ? ls_now() : 0;
         if (!next_ready) {
             if (p.trace && lane == 0 && !mbar_try_wait(full + slot, round & 1u)) {
                 const unsigned long long t0 = ls_now();
@@ -425,6 +429,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
         const int ns = slot + 1 == p.nstages ? 0 : slot + 1;
         const uint32_t nr = slot + 1 == p.nstages ? round + 1 : round;
         next_ready = mbar_try_wait(full + ns, nr & 1u);
+        if (p.trace) tt_acc[0] += ls_now() - tw0;
         return smem_u32(ring + (size_t)slot * kLsStage);
     };
     auto stage_release = [&]() {
@@ -460,11 +465,14 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
     ls_cbar();
 
     unsigned long long* trace = p.trace ? p.trace + (size_t)c * nph * 3 : nullptr;
+    const unsigned long long tl0 = p.trace ? ls_now() : 0;
     for (int ph = 0; ph < nph; ++ph) {
         const int kind = ls_kind(ph, L);
         const int layer = kind == LS_EMB ? 0 : kind == LS_LM ? L - 1 : (ph - 1) / 5;
         if (trace && ct == 0) trace[ph * 3] = ls_now();
+        const unsigned long long tp0 = p.trace ? ls_now() : 0;
         if (ph > 0) wait_phase(ph - 1);
+        if (p.trace) tt_acc[3] += ls_now() - tp0;
         if (trace && ct == 0 && (kind == LS_EMB || kind == LS_ATT)) trace[ph * 3 + 1] = ls_now();
 
         // ------------------------------------------------------------ EMB
@@ -696,7 +704,9 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
         const bool norm = kind == LS_QKV || kind == LS_GU || kind == LS_LM;
         if (m.rows > 0) {
             const uint8_t* rsrc = kind == LS_O ? p.rec_attn : kind == LS_DN ? p.rec_act : p.rec_x;
+            const unsigned long long tr0 = p.trace ? ls_now() : 0;
             load_records(rsrc, m.nb, norm, p.h / 16);
+            if (p.trace) tt_acc[3] += ls_now() - tr0;
         }
         const float inv = reinterpret_cast<const float*>(ictl)[5];
         if (trace && ct == 0) trace[ph * 3 + 1] = ls_now();
@@ -764,7 +774,9 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
             //      the tile's queue slot; the finishing warp adds the warps' pieces, the others go on
             const int qs_i = tile_i & (kLsQueue - 1);
             const uint32_t use = (uint32_t)(tile_i / kLsQueue);
+            const unsigned long long tq0 = p.trace ? ls_now() : 0;
             if (use > 0 && !ls_mbar_wait_backoff(qfree + qs_i, (use - 1) & 1u, p.err, 64)) aborted = true;
+            if (p.trace) tt_acc[1] += ls_now() - tq0;
             float* rb = red + (qs_i * kLsWarps + warp) * 16;
             if (t == 0) {
                 rb[g] = acc[0] + acc[1];
@@ -776,7 +788,10 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
             const int fw = tile_i % kLsWarps;
             ++tile_i;
             if (warp != fw) continue;
+            const unsigned long long te0 = p.trace ? ls_now() : 0;
             if (!ls_mbar_wait_backoff(qfull + qs_i, use & 1u, p.err, 64)) aborted = true;
+            if (p.trace) tt_acc[1] += ls_now() - te0;
+            const unsigned long long te1 = p.trace ? ls_now() : 0;
             // ---- the finishing warp: the CTA's piece = sum over warps (fixed order)
             float v = 0.f;
             if (lane < 16)
@@ -793,7 +808,10 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                 unsigned last = 0;
                 if (lane == 0) last = atom_add_acq_rel(p.tile_tick + this_tile, 1u) == (unsigned)(cl - cf);
                 last = __shfl_sync(0xffffffffu, last, 0);
-                if (!last) continue;
+                if (!last) {
+                    if (p.trace) tt_acc[2] += ls_now() - te1;
+                    continue;
+                }
                 v = 0.f;
                 if (lane < 16)
                     for (int i = 0; i <= cl - cf; ++i) v += __ldcg(slot_p + i * 16 + lane);
@@ -862,14 +880,16 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                     if (lane == 0) p.rec_tick[b] = 0u;
                 }
             }
+            if (p.trace) tt_acc[2] += ls_now() - te1;
         }
         arrive(ph);
     }
-    ls_cbar();
-    if (p.trace && ct == 0) {
-        unsigned long long* st = p.trace + (size_t)G * nph * 3 + (size_t)c * 4;
-        st[2] = reinterpret_cast<unsigned long long*>(ictl + 12)[0];
-        st[3] = reinterpret_cast<unsigned long long*>(ictl + 14)[0];
+    if (p.trace) {
+        tt_acc[4] = ls_now() - tl0;
+        if (lane == 0) {  // one warp's share per CTA row: [CTA][warp][5]
+            unsigned long long* st = p.trace + (size_t)G * nph * 3 + ((size_t)c * kLsWarps + warp) * 5;
+            for (int k = 0; k < 5; ++k) st[k] = tt_acc[k];
+        }
     }
     (void)aborted;
 }

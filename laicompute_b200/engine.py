@@ -147,7 +147,7 @@ class Engine:
         check(lib().laic_dev_step_trace(self.h, out.ctypes.data, cap, ctypes.byref(n), ctypes.byref(ctas),
                                         ctypes.byref(phases)))
         stamps = ctas.value * phases.value * 3
-        self.last_wait_stats = out[stamps: n.value].reshape(ctas.value, 4)
+        self.last_wait_stats = out[stamps: n.value].reshape(ctas.value, -1, 5)
         return out[:stamps].reshape(ctas.value, phases.value, 3)
 
     def profile(self, tokens: np.ndarray, steps: int) -> dict:
