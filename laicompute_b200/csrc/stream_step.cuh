@@ -54,7 +54,8 @@
 namespace laic {
 
 constexpr int kLsWarps = 16;                         // consumer warps
-constexpr int kLsThreads = (kLsWarps + 1) * 32;      // + the producer warp
+constexpr int kLsEpi = 2;                            // epilogue warps
+constexpr int kLsThreads = (kLsWarps + 1 + kLsEpi) * 32;  // + the producer warp + the epilogue warps
 constexpr int kLsStage = 9216;                       // ring stage bytes
 constexpr int kLsRec = 128;                          // activation record bytes per 32-column block (+ 4 B scale)
 constexpr int kLsMaxStages = 24;
@@ -223,6 +224,99 @@ __device__ __forceinline__ bool ls_mbar_wait_backoff(uint64_t* bar, uint32_t par
 // Named barrier of the consumer warps (the producer warp never joins it).
 __device__ __forceinline__ void ls_cbar() { named_sync(1, kLsWarps * 32); }
 
+// The epilogue of one row tile's piece (an epilogue warp; lanes 0..15 hold the piece's 16
+// row sums in v): pieces of a tile shared with other CTAs meet in scratch and the last to
+// arrive adds them in piece order, then the phase's epilogue runs on the finished rows.
+template <int D>
+__device__ __forceinline__ void ls_finish_tile(const LsParams& p, int kind, int layer, const LsMat& m, int tile, float v,
+                                               float inv, bool norm, int pos, int sl, int c, int G, int lane) {
+    const unsigned t_first = (unsigned)tile * m.nb;
+    const int cf = ls_owner((unsigned)m.nblk, t_first, G), cl = ls_owner((unsigned)m.nblk, t_first + m.nb - 1, G);
+    if (cl > cf) {
+        float* slot_p = p.part + ((size_t)tile * p.part_pieces) * 16;
+        if (lane < 16) slot_p[(c - cf) * 16 + lane] = v;
+        __syncwarp();
+        unsigned last = 0;
+        if (lane == 0) last = atom_add_acq_rel(p.tile_tick + tile, 1u) == (unsigned)(cl - cf);
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (!last) return;
+        v = 0.f;
+        if (lane < 16)
+            for (int i = 0; i <= cl - cf; ++i) v += __ldcg(slot_p + i * 16 + lane);
+        if (lane == 0) p.tile_tick[tile] = 0u;
+    }
+    if (norm) v *= inv;
+    const int r = tile * 16 + lane;  // this lane's row (lanes 0..15)
+    const bool live = lane < 16 && r < m.rows;
+    auto record_block = [&](float val, uint8_t* recs, int nb, int b) {
+        ls_write_record(val, lane, recs + (size_t)b * kLsRec, reinterpret_cast<float*>(recs + (size_t)nb * kLsRec) + b);
+    };
+    if (kind == LS_LM) {
+        if (live) p.logits[r] = v;
+    } else if (kind == LS_QKV) {
+        const float other = __shfl_xor_sync(0xffffffffu, v, 1);
+        if (live) {
+            int rr = r, region = 0;
+            if (rr >= p.hq) { rr -= p.hq; region = 1; if (rr >= p.kv) { rr -= p.kv; region = 2; } }
+            const int d = rr % D;
+            float o = v;
+            if (region < 2 && d < 2 * p.rope_pairs) {
+                const float2 cs = p.rope_cs[(size_t)pos * p.rope_pairs + (d >> 1)];
+                // adjacent-pair rotation, unfused like the reference
+                if ((d & 1) == 0) o = __fsub_rn(__fmul_rn(v, cs.x), __fmul_rn(other, cs.y));
+                else o = __fadd_rn(__fmul_rn(other, cs.y), __fmul_rn(v, cs.x));
+            }
+            if (region == 0) {
+                p.q[rr] = o;
+            } else {
+                __half* base = reinterpret_cast<__half*>(region == 1 ? p.layers[layer].kc : p.layers[layer].vc);
+                base[(size_t)sl * p.kv_slot_stride + ((size_t)(rr / D) * p.kv_cap + pos) * D + d] = __float2half_rn(o);
+            }
+        }
+    } else if (kind == LS_GU) {
+        // rows 2o (gate) and 2o+1 (up): act[o] = silu(gate) * up
+        const float up = __shfl_down_sync(0xffffffffu, v, 1);
+        const int o = tile * 8 + (lane >> 1);
+        if (live && (lane & 1) == 0) p.act[o] = (v / (1.f + expf(-v))) * up;
+        __syncwarp();
+        unsigned last = 0;
+        const int b = tile / 4;  // record block of act[32b .. 32b+31]
+        if (lane == 0) last = atom_add_acq_rel(p.rec_tick + b, 1u) == 3u;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+            const float a = __ldcg(p.act + (size_t)b * 32 + lane);
+            record_block(a, p.rec_act, p.F / 32, b);
+            if (lane == 0) p.rec_tick[b] = 0u;
+        }
+    } else {  // LS_O, LS_DN: residual add, its sum of squares, records for the next rmsnorm
+        float xn = 0.f;
+        if (live) {
+            xn = __ldcg(p.x + r) + v;
+            p.x[r] = xn;
+        }
+        float sq = live ? xn * xn : 0.f;
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+        if (lane == 0) p.ss_x[tile] = sq;
+        __syncwarp();
+        unsigned last = 0;
+        const int b = tile / 2;
+        if (lane == 0) last = atom_add_acq_rel(p.rec_tick + b, 1u) == 1u;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+            const float* wn = kind == LS_O ? p.layers[layer].ffn_norm
+                                           : (layer + 1 < p.L ? p.layers[layer + 1].attn_norm : p.out_norm);
+            const int e = b * 32 + lane;
+            record_block(__ldcg(p.x + e) * wn[e], p.rec_x, p.h / 32, b);
+            if (lane == 0) p.rec_tick[b] = 0u;
+        }
+    }
+}
+
+// Named barrier of the consumer and epilogue warps: a phase's inputs are ready (the
+// epilogue warps read 1/rms), and a phase's work is complete (before the arrival).
+__device__ __forceinline__ void ls_sync_all() { named_sync(2, (kLsWarps + kLsEpi) * 32); }
+
 template <int WT, int D, int GM>
 __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p) {
     constexpr int QB = tile_qbytes(WT);
@@ -360,6 +454,49 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
     }
 
     // =====================================================================
+    // epilogue warps: the row tiles' global epilogues, from the consumers' queue
+    // =====================================================================
+    if (warp > kLsWarps) {
+        const int e = warp - kLsWarps - 1;
+        int tile_i = 0;
+        for (int ph = 0; ph < nph; ++ph) {
+            const int kind = ls_kind(ph, L);
+            const int layer = kind == LS_EMB ? 0 : kind == LS_LM ? L - 1 : (ph - 1) / 5;
+            ls_sync_all();  // the phase's inputs are ready (1/rms, position, slot)
+            if (kind != LS_EMB && kind != LS_ATT) {
+                const LsMat m = ls_mat(p, kind, layer);
+                const bool norm = kind == LS_QKV || kind == LS_GU || kind == LS_LM;
+                const float inv = reinterpret_cast<const float*>(ictl)[5];
+                const int sl = ictl[2], pos = ictl[3];
+                const int lo = ls_lo((unsigned)m.nblk, c, G), hi = ls_lo((unsigned)m.nblk, c + 1, G);
+                int cur = lo, tile = m.nb > 0 ? lo / m.nb : 0, k0 = m.nb > 0 ? lo % m.nb : 0;
+                while (cur < hi) {  // the consumers' stage walk: one queue entry per tile piece
+                    const int n = min(min(SB, m.nb - k0), hi - cur);
+                    cur += n;
+                    k0 += n;
+                    const int this_tile = tile;
+                    if (k0 == m.nb) { k0 = 0; ++tile; }
+                    if (cur != hi && k0 != 0) continue;
+                    const int qs_i = tile_i & (kLsQueue - 1);
+                    const uint32_t use = (uint32_t)(tile_i / kLsQueue);
+                    const bool mine = (tile_i % kLsEpi) == e;
+                    ++tile_i;
+                    if (!mine) continue;
+                    ls_mbar_wait_backoff(qfull + qs_i, use & 1u, p.err, 64);
+                    float v = 0.f;
+                    if (lane < 16)
+                        for (int w = 0; w < kLsWarps; ++w) v += red[(qs_i * kLsWarps + w) * 16 + lane];
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(qfree + qs_i);
+                    ls_finish_tile<D>(p, kind, layer, m, this_tile, v, inv, norm, pos, sl, c, G, lane);
+                }
+            }
+            ls_sync_all();  // every tile of the phase finished: the consumers may arrive
+        }
+        return;
+    }
+
+    // =====================================================================
     // consumer warps
     // =====================================================================
     const int ct = threadIdx.x;           // 0 .. 255
@@ -396,7 +533,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
         ls_cbar();
     };
     auto arrive = [&](int ph) {
-        ls_cbar();  // every consumer's writes of the phase precede the arrival
+        ls_sync_all();  // every consumer's and epilogue warp's writes of the phase precede the arrival
         if (p.trace && ct == 0) p.trace[((size_t)c * nph + ph) * 3 + 2] = ls_now();
         if (ct == 0) {
             __threadfence();
@@ -473,6 +610,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
         const unsigned long long tp0 = p.trace ? ls_now() : 0;
         if (ph > 0) wait_phase(ph - 1);
         if (p.trace) tt_acc[3] += ls_now() - tp0;
+        if (kind == LS_EMB || kind == LS_ATT) ls_sync_all();  // (the epilogue warps have nothing to do)
         if (trace && ct == 0 && (kind == LS_EMB || kind == LS_ATT)) trace[ph * 3 + 1] = ls_now();
 
         // ------------------------------------------------------------ EMB
@@ -708,7 +846,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
             load_records(rsrc, m.nb, norm, p.h / 16);
             if (p.trace) tt_acc[3] += ls_now() - tr0;
         }
-        const float inv = reinterpret_cast<const float*>(ictl)[5];
+        ls_sync_all();  // the epilogue warps read 1/rms after this
         if (trace && ct == 0) trace[ph * 3 + 1] = ls_now();
         const int lo = ls_lo((unsigned)m.nblk, c, G), hi = ls_lo((unsigned)m.nblk, c + 1, G);
         // this lane's B fragment: column g (0 = hi, 1 = lo, 2..7 zero), k-group t
@@ -785,102 +923,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
             acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
             __syncwarp();
             if (lane == 0) mbar_arrive(qfull + qs_i);
-            const int fw = tile_i % kLsWarps;
             ++tile_i;
-            if (warp != fw) continue;
-            const unsigned long long te0 = p.trace ? ls_now() : 0;
-            if (!ls_mbar_wait_backoff(qfull + qs_i, use & 1u, p.err, 64)) aborted = true;
-            if (p.trace) tt_acc[1] += ls_now() - te0;
-            const unsigned long long te1 = p.trace ? ls_now() : 0;
-            // ---- the finishing warp: the CTA's piece = sum over warps (fixed order)
-            float v = 0.f;
-            if (lane < 16)
-                for (int w = 0; w < kLsWarps; ++w) v += red[(qs_i * kLsWarps + w) * 16 + lane];
-            __syncwarp();
-            if (lane == 0) mbar_arrive(qfree + qs_i);
-            // pieces of a tile shared with other CTAs meet in scratch; the last adds them in order
-            const unsigned t_first = (unsigned)this_tile * m.nb;
-            const int cf = ls_owner((unsigned)m.nblk, t_first, G), cl = ls_owner((unsigned)m.nblk, t_first + m.nb - 1, G);
-            if (cl > cf) {
-                float* slot_p = p.part + ((size_t)this_tile * p.part_pieces) * 16;
-                if (lane < 16) slot_p[(c - cf) * 16 + lane] = v;
-                __syncwarp();
-                unsigned last = 0;
-                if (lane == 0) last = atom_add_acq_rel(p.tile_tick + this_tile, 1u) == (unsigned)(cl - cf);
-                last = __shfl_sync(0xffffffffu, last, 0);
-                if (!last) {
-                    if (p.trace) tt_acc[2] += ls_now() - te1;
-                    continue;
-                }
-                v = 0.f;
-                if (lane < 16)
-                    for (int i = 0; i <= cl - cf; ++i) v += __ldcg(slot_p + i * 16 + lane);
-                if (lane == 0) p.tile_tick[this_tile] = 0u;
-            }
-            if (norm) v *= inv;
-            const int r = this_tile * 16 + lane;  // this lane's row (lanes 0..15)
-            const bool live = lane < 16 && r < m.rows;
-            if (kind == LS_LM) {
-                if (live) p.logits[r] = v;
-            } else if (kind == LS_QKV) {
-                const float other = __shfl_xor_sync(0xffffffffu, v, 1);
-                if (live) {
-                    int rr = r, region = 0;
-                    if (rr >= p.hq) { rr -= p.hq; region = 1; if (rr >= p.kv) { rr -= p.kv; region = 2; } }
-                    const int d = rr % D;
-                    float o = v;
-                    if (region < 2 && d < 2 * p.rope_pairs) {
-                        const float2 cs = p.rope_cs[(size_t)pos * p.rope_pairs + (d >> 1)];
-                        // adjacent-pair rotation, unfused like the reference
-                        if ((d & 1) == 0) o = __fsub_rn(__fmul_rn(v, cs.x), __fmul_rn(other, cs.y));
-                        else o = __fadd_rn(__fmul_rn(other, cs.y), __fmul_rn(v, cs.x));
-                    }
-                    if (region == 0) {
-                        p.q[rr] = o;
-                    } else {
-                        __half* base = reinterpret_cast<__half*>(region == 1 ? p.layers[layer].kc : p.layers[layer].vc);
-                        base[(size_t)sl * p.kv_slot_stride + ((size_t)(rr / D) * p.kv_cap + pos) * D + d] = __float2half_rn(o);
-                    }
-                }
-            } else if (kind == LS_GU) {
-                // rows 2o (gate) and 2o+1 (up): act[o] = silu(gate) * up
-                const float up = __shfl_down_sync(0xffffffffu, v, 1);
-                const int o = this_tile * 8 + (lane >> 1);
-                if (live && (lane & 1) == 0) p.act[o] = (v / (1.f + expf(-v))) * up;
-                __syncwarp();
-                unsigned last = 0;
-                const int b = this_tile / 4;  // record block of act[32b .. 32b+31]
-                if (lane == 0) last = atom_add_acq_rel(p.rec_tick + b, 1u) == 3u;
-                last = __shfl_sync(0xffffffffu, last, 0);
-                if (last) {
-                    const float a = __ldcg(p.act + (size_t)b * 32 + lane);
-                    record_block(a, p.rec_act, p.F / 32, b);
-                    if (lane == 0) p.rec_tick[b] = 0u;
-                }
-            } else {  // LS_O, LS_DN: residual add, its sum of squares, records for the next rmsnorm
-                float xn = 0.f;
-                if (live) {
-                    xn = __ldcg(p.x + r) + v;
-                    p.x[r] = xn;
-                }
-                float sq = live ? xn * xn : 0.f;
-#pragma unroll
-                for (int o = 8; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-                if (lane == 0) p.ss_x[this_tile] = sq;
-                __syncwarp();
-                unsigned last = 0;
-                const int b = this_tile / 2;
-                if (lane == 0) last = atom_add_acq_rel(p.rec_tick + b, 1u) == 1u;
-                last = __shfl_sync(0xffffffffu, last, 0);
-                if (last) {
-                    const float* wn = kind == LS_O ? p.layers[layer].ffn_norm
-                                                   : (layer + 1 < L ? p.layers[layer + 1].attn_norm : p.out_norm);
-                    const int e = b * 32 + lane;
-                    record_block(__ldcg(p.x + e) * wn[e], p.rec_x, p.h / 32, b);
-                    if (lane == 0) p.rec_tick[b] = 0u;
-                }
-            }
-            if (p.trace) tt_acc[2] += ls_now() - te1;
         }
         arrive(ph);
     }
