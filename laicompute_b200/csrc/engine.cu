@@ -840,7 +840,7 @@ struct laic_dev {
 
     // Whether one sequence can run as the persistent decode-step kernel: every layer projection
     // Q4_0 (or every one Q8_0), FP16 KV, one GPU, head_dim 64 or 128, at most 8 query heads per
-    // kv head, and one CTA per SM with a ring of at least 8 stages. Builds the layer table and
+    // kv head, and one CTA per SM with its shared memory. Builds the layer table and
     // the kernel's state (before any capture).
     int prepare_ls() {
         if (ls_checked) return LAIC_OK;
@@ -857,11 +857,11 @@ struct laic_dev {
         const int nb_max = std::max(std::max(h, hq), F) / 32;
         // attention chunks of one kv head span at most this many consecutive CTAs
         const int att_runs = std::min(num_sms(), num_sms() / std::max(1, Hkv) + 2);
-        int nst = laic::ls_max_stages();
+        int nst = 8;  // attention ring stages (K / V chunks), as many as fit
         size_t smem = 0;
-        for (; nst >= 8; --nst)
-            if ((smem = laic::ls_smem(nst, D, G, nb_max, att_runs)) <= 227 * 1024) break;
-        if (nst < 8) return LAIC_OK;
+        for (; nst >= 2; --nst)
+            if ((smem = laic::ls_smem(type, nst, D, G, nb_max, att_runs)) <= 227 * 1024) break;
+        if (nst < 2) return LAIC_OK;
         int bps = 0;
         CK(laic::ls_prepare(type, D, G, smem, &bps));
         if (bps < 1) return LAIC_OK;

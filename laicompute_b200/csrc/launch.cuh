@@ -67,10 +67,10 @@ cudaError_t gemm_f16(int M, int N, int K, const void* A, const void* W, float* C
                      cudaStream_t st);
 
 struct LsParams;
-// Persistent one-sequence decode-step kernel (stream_step.cu): shared memory for a ring of
-// `stages` stages and activation records of nb_max blocks, its layout constants, attribute
+// Persistent one-sequence decode-step kernel (stream_step.cu): shared memory for an attention
+// ring of `stages` stages, the consumer warps' weight rings and activation records of nb_max blocks, its layout constants, attribute
 // setup with the resulting CTAs per SM (call before capture), and its launch (one CTA per SM).
-size_t ls_smem(int stages, int D, int G, int nb_max, int att_runs);
+size_t ls_smem(int type, int stages, int D, int G, int nb_max, int att_runs);
 int ls_stage_bytes();
 int ls_trace_warp_words();  // trace words per CTA after the phase stamps
 int ls_max_stages();

@@ -49,6 +49,7 @@
 // waiting, so a failed step still ends. No wait is on a peer GPU.
 #pragma once
 #include "mma_matvec.cuh"
+#include "mv_streamk.cuh"
 #include "tiles.cuh"
 
 namespace laic {
@@ -56,15 +57,17 @@ namespace laic {
 constexpr int kLsWarps = 16;                         // consumer warps
 constexpr int kLsEpi = 2;                            // epilogue warps
 constexpr int kLsThreads = (kLsWarps + 1 + kLsEpi) * 32;  // + the producer warp + the epilogue warps
-constexpr int kLsStage = 9216;                       // ring stage bytes
+constexpr int kLsStage = 9216;                       // attention ring stage bytes (a K or V chunk)
+constexpr int kLsWRing = 3;                          // weight stages in flight per consumer warp
 constexpr int kLsRec = 128;                          // activation record bytes per 32-column block (+ 4 B scale)
 constexpr int kLsMaxStages = 24;
 constexpr int kLsQueue = 8;                          // tile partials in flight between consumers and finishers
 constexpr int kLsIssue = 8;                          // ring stages the producer warp's lanes issue together
 constexpr long long kLsSpin = 2000000000LL;          // clock cycles a dependency wait may take
 
-// tile-blocks per ring stage
-__host__ __device__ constexpr int ls_sb(int type) { return kLsStage / (tile_qbytes(type) + kTileSBytes); }
+// tile-blocks per weight stage of a consumer warp's ring (about 2.2 KB), and its bytes
+__host__ __device__ constexpr int ls_sb(int type) { return type == T_Q4_0 ? 8 : 4; }
+__host__ __device__ constexpr int ls_wstage(int type) { return ls_sb(type) * (tile_qbytes(type) + kTileSBytes); }
 // positions of one K (or V) chunk per ring stage
 __host__ __device__ constexpr int ls_cp(int D) { return kLsStage / (D * 2) >= 64 ? 64 : 32; }
 
@@ -182,26 +185,9 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
 }
 __device__ __forceinline__ int ld_volatile_i32(const int* a) { return *reinterpret_cast<const volatile int*>(a); }
 
-// Bytes of the activation records of a vector of nb blocks: nb records of 128 bytes,
-// then the blocks' scales (one float each, padded to 16 bytes).
-__host__ __device__ inline size_t ls_rec_bytes(int nb) { return (size_t)nb * kLsRec + ((size_t)nb * 4 + 15) / 16 * 16; }
-
-// Activation record of one 32-element block, built by one warp (lane i holds element
-// i): the values times 2^s, split into binary16 hi (bytes 0..63) and lo (64..127),
-// each as 4 column groups of 8 halves in fragment order (the B fragment of
-// mma.m16n8k16 for lanes t = group), and 2^-s into the scale table.
-__device__ __forceinline__ void ls_write_record(float v, int lane, uint8_t* rec, float* scale) {
-    const float mx = warp_max(fabsf(v));
-    int ex = 0;
-    if (mx > 0.f && isfinite(mx)) frexpf(mx, &ex);  // mx in [2^(ex-1), 2^ex)
-    const float xs = ldexpf(v, 11 - ex);             // exact: a power of two
-    const __half hi = __float2half_rn(xs);
-    const __half lo = __float2half_rn(xs - __half2float(hi));
-    const int off = (lane >> 3) * 16 + frag_pos(lane & 7) * 2;
-    *reinterpret_cast<__half*>(rec + off) = hi;
-    *reinterpret_cast<__half*>(rec + 64 + off) = lo;
-    if (lane == 0) *scale = ldexpf(1.f, ex - 11);
-}
+// Bytes of the activation records of a vector of nb blocks (the integer digit records of
+// mv_streamk.cuh: per 8-element group the three base-128 digits, -8 sum x and 2^-s).
+__host__ __device__ inline size_t ls_rec_bytes(int nb) { return (size_t)nb * kLsRec; }
 
 // Bounded wait for an mbarrier phase that backs off with nanosleep between polls: a hot
 // poll (try_wait and the clock read in a tight loop) takes issue slots and the
@@ -227,7 +213,7 @@ __device__ __forceinline__ void ls_cbar() { named_sync(1, kLsWarps * 32); }
 // The epilogue of one row tile's piece (an epilogue warp; lanes 0..15 hold the piece's 16
 // row sums in v): pieces of a tile shared with other CTAs meet in scratch and the last to
 // arrive adds them in piece order, then the phase's epilogue runs on the finished rows.
-template <int D>
+template <int WT, int D>
 __device__ __forceinline__ void ls_finish_tile(const LsParams& p, int kind, int layer, const LsMat& m, int tile, float v,
                                                float inv, bool norm, int pos, int sl, int c, int G, int lane) {
     const unsigned t_first = (unsigned)tile * m.nb;
@@ -248,9 +234,6 @@ __device__ __forceinline__ void ls_finish_tile(const LsParams& p, int kind, int 
     if (norm) v *= inv;
     const int r = tile * 16 + lane;  // this lane's row (lanes 0..15)
     const bool live = lane < 16 && r < m.rows;
-    auto record_block = [&](float val, uint8_t* recs, int nb, int b) {
-        ls_write_record(val, lane, recs + (size_t)b * kLsRec, reinterpret_cast<float*>(recs + (size_t)nb * kLsRec) + b);
-    };
     if (kind == LS_LM) {
         if (live) p.logits[r] = v;
     } else if (kind == LS_QKV) {
@@ -275,41 +258,27 @@ __device__ __forceinline__ void ls_finish_tile(const LsParams& p, int kind, int 
         }
     } else if (kind == LS_GU) {
         // rows 2o (gate) and 2o+1 (up): act[o] = silu(gate) * up
+        // outputs tile * 8 + lane / 2 on the even lanes 0..14: one 8-element group of records
         const float up = __shfl_down_sync(0xffffffffu, v, 1);
         const int o = tile * 8 + (lane >> 1);
-        if (live && (lane & 1) == 0) p.act[o] = (v / (1.f + expf(-v))) * up;
-        __syncwarp();
-        unsigned last = 0;
-        const int b = tile / 4;  // record block of act[32b .. 32b+31]
-        if (lane == 0) last = atom_add_acq_rel(p.rec_tick + b, 1u) == 3u;
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (last) {
-            const float a = __ldcg(p.act + (size_t)b * 32 + lane);
-            record_block(a, p.rec_act, p.F / 32, b);
-            if (lane == 0) p.rec_tick[b] = 0u;
-        }
+        const bool on = live && (lane & 1) == 0;
+        const float a = on ? (v / (1.f + expf(-v))) * up : 0.f;
+        if (on) p.act[o] = a;
+        dp_lane_record<WT>(a, 0.f, lane >> 1, on ? (o >> 3) : -1, p.rec_act, 2, 4, 8);
     } else {  // LS_O, LS_DN: residual add, its sum of squares, records for the next rmsnorm
+        // rows tile * 16 + lane on lanes 0..15: two 8-element groups of records of x * (next
+        // rmsnorm weight), and the tile's sum of x^2
         float xn = 0.f;
         if (live) {
             xn = __ldcg(p.x + r) + v;
             p.x[r] = xn;
         }
-        float sq = live ? xn * xn : 0.f;
-#pragma unroll
-        for (int o = 8; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-        if (lane == 0) p.ss_x[tile] = sq;
-        __syncwarp();
-        unsigned last = 0;
-        const int b = tile / 2;
-        if (lane == 0) last = atom_add_acq_rel(p.rec_tick + b, 1u) == 1u;
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (last) {
-            const float* wn = kind == LS_O ? p.layers[layer].ffn_norm
-                                           : (layer + 1 < p.L ? p.layers[layer + 1].attn_norm : p.out_norm);
-            const int e = b * 32 + lane;
-            record_block(__ldcg(p.x + e) * wn[e], p.rec_x, p.h / 32, b);
-            if (lane == 0) p.rec_tick[b] = 0u;
-        }
+        const float* wn = kind == LS_O ? p.layers[layer].ffn_norm
+                                       : (layer + 1 < p.L ? p.layers[layer + 1].attn_norm : p.out_norm);
+        const float sg = dp_lane_record<WT>(live ? xn * wn[r] : 0.f, xn * xn, lane & 7, live ? (r >> 3) : -1, p.rec_x,
+                                            1, 2, 4);
+        const float s8 = __shfl_sync(0xffffffffu, sg, 8);
+        if (lane == 0) p.ss_x[tile] = sg + s8;
     }
 }
 
@@ -321,25 +290,28 @@ template <int WT, int D, int GM>
 __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p) {
     constexpr int QB = tile_qbytes(WT);
     constexpr int SB = ls_sb(WT);
+    constexpr int WS = ls_wstage(WT);
     constexpr int CP = ls_cp(D);
     constexpr int E = D / 32;               // head dims per lane
-    constexpr int NBW = SB / kLsWarps;      // tile-blocks of a full stage per consumer warp
     constexpr int PPW = CP / kLsWarps;      // chunk positions per consumer warp (scores)
     constexpr int OP2 = (GM * D / 2 + kLsWarps * 32 - 1) / (kLsWarps * 32);  // attention output pairs per thread
     static_assert(WT == T_Q4_0 || WT == T_Q8_0, "Q4_0 or Q8_0 projections");
+    static_assert(PPW >= 1, "at least one chunk position per warp");
     extern __shared__ __align__(128) uint8_t smem[];
-    const int NST = p.nstages;
+    const int NST = p.nstages;  // attention ring stages
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = gridDim.x, c = blockIdx.x;
     const int L = p.L, nph = ls_phases(L);
 
     // ---- shared memory
-    uint8_t* ring = smem;
-    uint64_t* full = reinterpret_cast<uint64_t*>(ring + (size_t)NST * kLsStage);
+    uint8_t* ring = smem;                                                   // [NST][kLsStage] K / V chunks
+    uint8_t* wring = ring + (size_t)NST * kLsStage;                         // [kLsWarps][kLsWRing][WS] weights
+    uint64_t* full = reinterpret_cast<uint64_t*>(wring + (size_t)kLsWarps * kLsWRing * WS);
     uint64_t* empty = full + kLsMaxStages;
-    uint64_t* xbar = empty + kLsMaxStages;
+    uint64_t* wfull = empty + kLsMaxStages;                                 // [kLsWarps][kLsWRing]
+    uint64_t* xbar = wfull + kLsWarps * kLsWRing;
     uint64_t* qfull = xbar + 2;                                 // [kLsQueue] a tile's warp partials are in
-    uint64_t* qfree = qfull + kLsQueue;                         // [kLsQueue] the finisher read them
+    uint64_t* qfree = qfull + kLsQueue;                         // [kLsQueue] an epilogue warp read them
     float* red = reinterpret_cast<float*>(qfree + kLsQueue);    // [kLsQueue][kLsWarps][16]
     float* qs = red + kLsQueue * kLsWarps * 16;                 // [GM][D] merged attention output
     float* ss_att = qs + GM * D;                                // [GM][CP] scores, then weights
@@ -356,6 +328,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
             mbar_init(full + s, 1);
             mbar_init(empty + s, kLsWarps);
         }
+        for (int s = 0; s < kLsWarps * kLsWRing; ++s) mbar_init(wfull + s, 1);
         mbar_init(xbar, 1);
         for (int q = 0; q < kLsQueue; ++q) {
             mbar_init(qfull + q, kLsWarps);
@@ -366,70 +339,48 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
     __syncthreads();
 
     // =====================================================================
-    // producer warp: every stage of every phase, in order, as the ring frees up
+    // producer warp: the attention phases' K and V chunks (rows of earlier steps), in order,
+    // into the shared ring as it frees up; every lane steps the same sequence and lane l
+    // issues stage i0 + l of each batch
     // =====================================================================
     if (warp == kLsWarps) {
-        // Every lane steps the same stage sequence; in each batch of kLsIssue stages lane l
-        // waits for the slot of stage i0 + l and issues its copies, so the copies of a batch
-        // go out together (one lane alone issues about one copy per 250 ns).
-        int ph = -1, kind = LS_EMB, cur = 0, hi = 0, k0 = 0;
-        LsMat m{};
+        int ph = -1, kind = LS_EMB;
         const LsLayer* aly = nullptr;
         int apos = 0, asl = 0, nch = 1, it = 0, ihi = 0, j = 0, ch = 0, kvs = 0;
         bool waited = false;
-        // the next stage's copies: (src0, bytes0) into the stage, (src1, bytes1) at SB * QB
-        auto next = [&](const uint8_t*& s0, uint32_t& b0, const uint8_t*& s1, uint32_t& b1) -> bool {
+        auto next = [&](const uint8_t*& s0, uint32_t& b0) -> bool {
             for (;;) {
-                if (kind == LS_ATT) {
-                    if (it < ihi) {
-                        // rows of the chunk written by earlier steps (the newest row comes later, from L2)
-                        const int r0 = ch * CP, nrows = max(0, min(r0 + CP, apos) - r0);
-                        const size_t off = (size_t)asl * p.kv_slot_stride + ((size_t)j * p.kv_cap + r0) * D;
-                        s0 = reinterpret_cast<const uint8_t*>(reinterpret_cast<const __half*>(kvs ? aly->vc : aly->kc) + off);
-                        b0 = (uint32_t)(nrows * D * 2);
-                        s1 = nullptr; b1 = 0;
-                        if (++kvs == 2) { kvs = 0; ++it; if (++ch == nch) { ch = 0; ++j; } }
-                        return true;
-                    }
-                } else if (kind != LS_EMB) {
-                    if (cur < hi) {
-                        const int n = min(min(SB, m.nb - k0), hi - cur);
-                        s0 = m.q + (size_t)cur * QB; b0 = (uint32_t)(n * QB);
-                        s1 = m.s + (size_t)cur * kTileSBytes; b1 = (uint32_t)(n * kTileSBytes);
-                        cur += n; k0 += n;
-                        if (k0 == m.nb) k0 = 0;
-                        return true;
-                    }
+                if (kind == LS_ATT && it < ihi) {
+                    const int r0 = ch * CP, nrows = max(0, min(r0 + CP, apos) - r0);
+                    const size_t off = (size_t)asl * p.kv_slot_stride + ((size_t)j * p.kv_cap + r0) * D;
+                    s0 = reinterpret_cast<const uint8_t*>(reinterpret_cast<const __half*>(kvs ? aly->vc : aly->kc) + off);
+                    b0 = (uint32_t)(nrows * D * 2);
+                    if (++kvs == 2) { kvs = 0; ++it; if (++ch == nch) { ch = 0; ++j; } }
+                    return true;
                 }
-                if (++ph >= nph) return false;  // the next phase with stages
+                if (++ph >= nph) return false;
                 kind = ls_kind(ph, L);
-                const int layer = (ph - 1) / 5;
-                if (kind == LS_ATT) {
-                    if (!waited) { pdl_wait(); waited = true; }  // positions come from the previous step
-                    asl = p.slots[0];
-                    apos = p.pos[asl];
-                    nch = (apos + 1 + CP - 1) / CP;
-                    const unsigned I = (unsigned)p.kv_heads * nch;
-                    aly = p.layers + layer;
-                    it = ls_lo(I, c, G); ihi = ls_lo(I, c + 1, G);
-                    j = it / nch; ch = it % nch; kvs = 0;
-                } else if (kind != LS_EMB) {
-                    m = ls_mat(p, kind, layer);
-                    cur = ls_lo((unsigned)m.nblk, c, G); hi = ls_lo((unsigned)m.nblk, c + 1, G);
-                    k0 = m.nb > 0 ? cur % m.nb : 0;
-                }
+                if (kind != LS_ATT) continue;
+                if (!waited) { pdl_wait(); waited = true; }  // positions come from the previous step
+                asl = p.slots[0];
+                apos = p.pos[asl];
+                nch = (apos + 1 + CP - 1) / CP;
+                const unsigned I = (unsigned)p.kv_heads * nch;
+                aly = p.layers + (ph - 1) / 5;
+                it = ls_lo(I, c, G); ihi = ls_lo(I, c + 1, G);
+                j = it / nch; ch = it % nch; kvs = 0;
             }
         };
         bool ok = true;
         for (int i0 = 0;;) {
-            const uint8_t *s0 = nullptr, *s1 = nullptr;
-            uint32_t b0 = 0, b1 = 0;
+            const uint8_t* s0 = nullptr;
+            uint32_t b0 = 0;
             int cnt = 0;
             for (int l = 0; l < kLsIssue; ++l) {
-                const uint8_t *t0, *t1;
-                uint32_t c0, c1;
-                if (!next(t0, c0, t1, c1)) break;
-                if (lane == l) { s0 = t0; b0 = c0; s1 = t1; b1 = c1; }
+                const uint8_t* t0;
+                uint32_t c0;
+                if (!next(t0, c0)) break;
+                if (lane == l) { s0 = t0; b0 = c0; }
                 ++cnt;
             }
             if (cnt == 0) break;
@@ -438,11 +389,9 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                 const uint32_t r = (uint32_t)(i / NST);
                 // the consumers released this slot's previous use (first round: free)
                 if (ok && r > 0 && !ls_mbar_wait_backoff(empty + sl, (r - 1) & 1u, p.err)) ok = false;
-                uint8_t* dst = ring + (size_t)sl * kLsStage;
-                if (ok && b0 + b1 > 0) {
-                    mbar_expect_tx(full + sl, b0 + b1);
-                    if (b0) bulk_g2s(dst, s0, b0, full + sl);
-                    if (b1) bulk_g2s(dst + SB * QB, s1, b1, full + sl);
+                if (ok && b0 > 0) {
+                    mbar_expect_tx(full + sl, b0);
+                    bulk_g2s(ring + (size_t)sl * kLsStage, s0, b0, full + sl);
                 } else {
                     mbar_arrive(full + sl);  // nothing to copy (or a failed wait): the stage is ready
                 }
@@ -469,26 +418,19 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                 const float inv = reinterpret_cast<const float*>(ictl)[5];
                 const int sl = ictl[2], pos = ictl[3];
                 const int lo = ls_lo((unsigned)m.nblk, c, G), hi = ls_lo((unsigned)m.nblk, c + 1, G);
-                int cur = lo, tile = m.nb > 0 ? lo / m.nb : 0, k0 = m.nb > 0 ? lo % m.nb : 0;
-                while (cur < hi) {  // the consumers' stage walk: one queue entry per tile piece
-                    const int n = min(min(SB, m.nb - k0), hi - cur);
-                    cur += n;
-                    k0 += n;
-                    const int this_tile = tile;
-                    if (k0 == m.nb) { k0 = 0; ++tile; }
-                    if (cur != hi && k0 != 0) continue;
-                    const int qs_i = tile_i & (kLsQueue - 1);
-                    const uint32_t use = (uint32_t)(tile_i / kLsQueue);
-                    const bool mine = (tile_i % kLsEpi) == e;
-                    ++tile_i;
-                    if (!mine) continue;
-                    ls_mbar_wait_backoff(qfull + qs_i, use & 1u, p.err, 64);
-                    float v = 0.f;
-                    if (lane < 16)
-                        for (int w = 0; w < kLsWarps; ++w) v += red[(qs_i * kLsWarps + w) * 16 + lane];
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(qfree + qs_i);
-                    ls_finish_tile<D>(p, kind, layer, m, this_tile, v, inv, norm, pos, sl, c, G, lane);
+                if (lo < hi) {
+                    for (int tile = lo / m.nb; tile <= (hi - 1) / m.nb; ++tile, ++tile_i) {
+                        if ((tile_i % kLsEpi) != e) continue;
+                        const int qs_i = tile_i & (kLsQueue - 1);
+                        const uint32_t use = (uint32_t)(tile_i / kLsQueue);
+                        ls_mbar_wait_backoff(qfull + qs_i, use & 1u, p.err, 64);
+                        float v = 0.f;
+                        if (lane < 16)
+                            for (int w = 0; w < kLsWarps; ++w) v += red[(qs_i * kLsWarps + w) * 16 + lane];
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(qfree + qs_i);
+                        ls_finish_tile<WT, D>(p, kind, layer, m, tile, v, inv, norm, pos, sl, c, G, lane);
+                    }
                 }
             }
             ls_sync_all();  // every tile of the phase finished: the consumers may arrive
@@ -499,9 +441,58 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
     // =====================================================================
     // consumer warps
     // =====================================================================
-    const int ct = threadIdx.x;           // 0 .. 255
+    const int ct = threadIdx.x;           // 0 .. kLsWarps * 32 - 1
     const int g = lane >> 2, t = lane & 3;
     const int gq = p.gq;
+
+    // ---- this warp's weight stream: its contiguous share of the CTA's tile-blocks in every
+    //      projection phase, cut at row-tile ends and into stages of at most SB blocks; lane 0
+    //      keeps kLsWRing stages in flight, across phase boundaries (weights never depend on
+    //      the step's activations)
+    uint8_t* myring = wring + (size_t)warp * kLsWRing * WS;
+    uint64_t* mybar = wfull + warp * kLsWRing;
+    int w_ph = 0, w_cur = 0, w_hi = 0, w_k0 = 0, w_nb = 1;
+    const uint8_t *w_q = nullptr, *w_s = nullptr;
+    auto wnext = [&](const uint8_t*& sq, const uint8_t*& ss, int& n) -> bool {
+        for (;;) {
+            if (w_cur < w_hi) {
+                n = min(min(SB, w_nb - w_k0), w_hi - w_cur);
+                sq = w_q + (size_t)w_cur * QB;
+                ss = w_s + (size_t)w_cur * kTileSBytes;
+                w_cur += n;
+                w_k0 += n;
+                if (w_k0 == w_nb) w_k0 = 0;
+                return true;
+            }
+            if (++w_ph >= nph) return false;
+            const int kind = ls_kind(w_ph, L);
+            if (kind == LS_EMB || kind == LS_ATT) continue;
+            const LsMat m = ls_mat(p, kind, kind == LS_LM ? L - 1 : (w_ph - 1) / 5);
+            const int lo = ls_lo((unsigned)m.nblk, c, G), hi = ls_lo((unsigned)m.nblk, c + 1, G);
+            w_cur = lo + (hi - lo) * warp / kLsWarps;
+            w_hi = lo + (hi - lo) * (warp + 1) / kLsWarps;
+            w_nb = m.nb;
+            w_k0 = m.nb > 0 ? w_cur % m.nb : 0;
+            w_q = m.q;
+            w_s = m.s;
+        }
+    };
+    int wissue = 0;  // stages issued by this warp
+    auto wissue_one = [&]() {
+        const uint8_t *sq, *ss;
+        int n;
+        if (!wnext(sq, ss, n)) return;
+        if (lane == 0) {
+            const int slot = wissue % kLsWRing;
+            uint8_t* dst = myring + (size_t)slot * WS;
+            mbar_expect_tx(mybar + slot, (uint32_t)(n * (QB + kTileSBytes)));
+            bulk_g2s(dst, sq, (uint32_t)(n * QB), mybar + slot);
+            bulk_g2s(dst + SB * QB, ss, (uint32_t)(n * kTileSBytes), mybar + slot);
+        }
+        ++wissue;
+    };
+    for (int i = 0; i < kLsWRing; ++i) wissue_one();
+
     pdl_wait();
     pdl_launch_dependents();
     if (ct == 0) {
@@ -518,7 +509,8 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
     int slot = 0;
     uint32_t round = 0, xphase = 0;
     bool aborted = false;
-    int tile_i = 0;  // tile pieces this CTA finished (selects the queue slot and the finishing warp)
+    int tile_i = 0;   // tile pieces this CTA handed to the epilogue warps (queue slot)
+    int wcons = 0;    // weight stages this warp consumed
 
     // Wait until every CTA arrived at phase `ph`'s counter.
     auto wait_phase = [&](int ph) {
@@ -544,28 +536,14 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
             }
         }
     };
-    // The next stage's readiness is polled right after a stage is acquired, so the poll's
-    // round trip overlaps the current stage's work instead of preceding the next one.
-    bool next_ready = false;
-    // trace: per-warp ns spent in [0] stage waits, [1] tile-end queue waits, [2] finishing epilogues,
+    // trace: per-warp ns spent in [0] stage waits, [1] tile-end queue waits, [2] unused,
     // [3] phase waits (dependency + records), [4] the whole phase loop
     unsigned long long tt_acc[5] = {0, 0, 0, 0, 0};
+    // the attention ring (K / V chunks from the producer warp)
     auto stage_wait = [&]() -> uint32_t {
         const unsigned long long tw0 = p.trace ? ls_now() : 0;
-        if (!next_ready) {
-            if (p.trace && lane == 0 && !mbar_try_wait(full + slot, round & 1u)) {
-                const unsigned long long t0 = ls_now();
-                if (!ls_mbar_wait_backoff(full + slot, round & 1u, p.err, 64)) aborted = true;
-                atomicAdd(reinterpret_cast<unsigned long long*>(ictl + 12), 1ull);
-                atomicAdd(reinterpret_cast<unsigned long long*>(ictl + 14), ls_now() - t0);
-            } else if (!ls_mbar_wait_backoff(full + slot, round & 1u, p.err, 64)) {
-                aborted = true;
-            }
-        }
+        if (!ls_mbar_wait_backoff(full + slot, round & 1u, p.err, 64)) aborted = true;
         __syncwarp();
-        const int ns = slot + 1 == p.nstages ? 0 : slot + 1;
-        const uint32_t nr = slot + 1 == p.nstages ? round + 1 : round;
-        next_ready = mbar_try_wait(full + ns, nr & 1u);
         if (p.trace) tt_acc[0] += ls_now() - tw0;
         return smem_u32(ring + (size_t)slot * kLsStage);
     };
@@ -591,13 +569,8 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
         xphase ^= 1u;
         ls_cbar();
     };
-    // Record block b of a vector of nb blocks, from one warp (lane i: element i).
-    auto record_block = [&](float v, uint8_t* recs, int nb, int b) {
-        ls_write_record(v, lane, recs + (size_t)b * kLsRec, reinterpret_cast<float*>(recs + (size_t)nb * kLsRec) + b);
-    };
 
     const uint32_t act_a = smem_u32(act);
-    const uint32_t zero_a = smem_u32(ictl + 8);  // 16 zero bytes (ictl[8..11]); [12..15] trace wait counters
     if (ct < 8) ictl[8 + ct] = 0;
     ls_cbar();
 
@@ -625,7 +598,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                 for (int o = 8; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
                 if (lane == 0) p.ss_x[2 * b] = sq;
                 if (lane == 16) p.ss_x[2 * b + 1] = sq;
-                record_block(v * p.layers[0].attn_norm[e], p.rec_x, nblk, b);
+                dp_lane_record<WT>(v * p.layers[0].attn_norm[e], 0.f, lane & 7, e >> 3, p.rec_x, 1, 2, 4);
             }
             if (c == 0 && ct == 0) atomicAdd(p.counts + (size_t)sl * p.vocab + tok, 1u);
             arrive(ph);
@@ -826,7 +799,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                             const float v = obuf[b * 32 + lane];
                             const size_t e = (size_t)j * gq * D + b * 32 + lane;
                             p.attn[e] = v;
-                            record_block(v, p.rec_attn, p.hq / 32, (int)(e / 32));
+                            dp_lane_record<WT>(v, 0.f, lane & 7, (int)(e >> 3), p.rec_attn, 1, 2, 4);
                         }
                         if (ct == 0) p.head_tick[j] = 0u;
                         ls_cbar();
@@ -849,87 +822,63 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
         ls_sync_all();  // the epilogue warps read 1/rms after this
         if (trace && ct == 0) trace[ph * 3 + 1] = ls_now();
         const int lo = ls_lo((unsigned)m.nblk, c, G), hi = ls_lo((unsigned)m.nblk, c + 1, G);
-        // this lane's B fragment: column g (0 = hi, 1 = lo, 2..7 zero), k-group t
-        const bool bcol = g < 2;
-        const uint32_t b_off = g * 64 + t * 16;
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        const uint32_t scale_a = act_a + (uint32_t)m.nb * kLsRec;  // the blocks' 2^-s
-        int cur = lo, tile = lo / m.nb, k0 = lo % m.nb;
-        while (cur < hi) {
-            const int n = min(min(SB, m.nb - k0), hi - cur);
-            const uint32_t sq = stage_wait();
-            const uint32_t ssc = sq + SB * QB;
-            // this warp's blocks of the stage (jb = warp + 8 i): all loads first, then the products
-            uint32_t wq[NBW][WT == T_Q4_0 ? 2 : 4], dsc[NBW];
-            uint4 xv[NBW];
-            float sv[NBW];
+        const int whi = lo + (hi - lo) * (warp + 1) / kLsWarps;
+        int cur = lo + (hi - lo) * warp / kLsWarps;
+        const uint32_t xlane = act_a + t * 32;  // this lane's 8-column group of each block record
+        if (lo < hi) {
+            for (int tile = lo / m.nb; tile <= (hi - 1) / m.nb; ++tile) {
+                const int t_end = min(hi, (tile + 1) * m.nb);
+                float dacc[2] = {0.f, 0.f};
+                while (cur < whi && cur < t_end) {  // this warp's stages inside the tile
+                    const int k0 = cur - tile * m.nb;
+                    const int n = min(min(SB, m.nb - k0), whi - cur);
+                    const int wslot = wcons % kLsWRing;
+                    const unsigned long long tw0 = p.trace ? ls_now() : 0;
+                    if (!ls_mbar_wait_backoff(mybar + wslot, (uint32_t)(wcons / kLsWRing) & 1u, p.err, 64)) aborted = true;
+                    if (p.trace) tt_acc[0] += ls_now() - tw0;
+                    const uint32_t sq = smem_u32(myring + (size_t)wslot * WS);
+                    const uint32_t ssc = sq + SB * QB;
+                    const uint32_t xr = xlane + (uint32_t)k0 * kLsRec;
+                    if (n == SB) {
 #pragma unroll
-            for (int i = 0; i < NBW; ++i) {
-                const int jb = warp + i * kLsWarps;
-                if (jb < n) {
-                    if (WT == T_Q4_0) {
-                        const uint2 w = lds64(sq + jb * QB + lane * 8);
-                        wq[i][0] = w.x; wq[i][1] = w.y;
+                        for (int jb = 0; jb < SB; ++jb)
+                            tile_block_dp<WT>(sq + jb * QB, ssc + jb * kTileSBytes, xr + jb * kLsRec, lane, dacc);
                     } else {
-                        const uint4 w = lds128(sq + jb * QB + lane * 16);
-                        wq[i][0] = w.x; wq[i][1] = w.y; wq[i][2] = w.z; wq[i][3] = w.w;
+                        for (int jb = 0; jb < n; ++jb)
+                            tile_block_dp<WT>(sq + jb * QB, ssc + jb * kTileSBytes, xr + jb * kLsRec, lane, dacc);
                     }
-                    xv[i] = lds128(bcol ? act_a + (uint32_t)(k0 + jb) * kLsRec + b_off : zero_a);
-                    dsc[i] = lds32(ssc + jb * kTileSBytes + g * 4);
-                    sv[i] = __uint_as_float(lds32(scale_a + (uint32_t)(k0 + jb) * 4));
+                    __syncwarp();
+                    ++wcons;
+                    if (lane == 0) fence_proxy_async_smem();  // the reads of this slot precede its refill
+                    wissue_one();
+                    cur += n;
                 }
-            }
-#pragma unroll
-            for (int i = 0; i < NBW; ++i) {
-                const int jb = warp + i * kLsWarps;
-                if (jb < n) {
-                    uint32_t ra[4], rb[4];
-                    if (WT == T_Q4_0) {
-                        decode_q4(wq[i][0], ra);
-                        decode_q4(wq[i][1], rb);
-                    } else {
-                        decode_q8(wq[i][0], wq[i][1], ra);
-                        decode_q8(wq[i][2], wq[i][3], rb);
-                    }
-                    float tt[4];
-                    mma16816_z(tt, ra[0], rb[0], ra[1], rb[1], xv[i].x, xv[i].y);
-                    mma16816_acc(tt, ra[2], rb[2], ra[3], rb[3], xv[i].z, xv[i].w);
-                    const float2 df = __half22float2(*reinterpret_cast<const __half2*>(&dsc[i]));
-                    const float s0 = df.x * sv[i], s1 = df.y * sv[i];
-                    acc[0] = fmaf(tt[0], s0, acc[0]);
-                    acc[1] = fmaf(tt[1], s0, acc[1]);
-                    acc[2] = fmaf(tt[2], s1, acc[2]);
-                    acc[3] = fmaf(tt[3], s1, acc[3]);
+                // ---- this warp's part of the tile piece (zero when it has none) into the queue:
+                //      the four lanes of a row hold its four 8-column groups
+                float r0 = dacc[0], r1 = dacc[1];
+                r0 += __shfl_xor_sync(0xffffffffu, r0, 1);
+                r1 += __shfl_xor_sync(0xffffffffu, r1, 1);
+                r0 += __shfl_xor_sync(0xffffffffu, r0, 2);
+                r1 += __shfl_xor_sync(0xffffffffu, r1, 2);
+                const int qs_i = tile_i & (kLsQueue - 1);
+                const uint32_t use = (uint32_t)(tile_i / kLsQueue);
+                const unsigned long long tq0 = p.trace ? ls_now() : 0;
+                if (use > 0 && !ls_mbar_wait_backoff(qfree + qs_i, (use - 1) & 1u, p.err, 64)) aborted = true;
+                if (p.trace) tt_acc[1] += ls_now() - tq0;
+                if (t == 0) {
+                    red[(qs_i * kLsWarps + warp) * 16 + g] = r0;
+                    red[(qs_i * kLsWarps + warp) * 16 + g + 8] = r1;
                 }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(qfull + qs_i);
+                ++tile_i;
             }
-            stage_release();
-            cur += n;
-            k0 += n;
-            const int this_tile = tile;
-            if (k0 == m.nb) { k0 = 0; ++tile; }
-            if (cur != hi && k0 != 0) continue;
-            // ---- end of this CTA's piece of a tile: rows g and g+8 = hi column + lo column, into
-            //      the tile's queue slot; the finishing warp adds the warps' pieces, the others go on
-            const int qs_i = tile_i & (kLsQueue - 1);
-            const uint32_t use = (uint32_t)(tile_i / kLsQueue);
-            const unsigned long long tq0 = p.trace ? ls_now() : 0;
-            if (use > 0 && !ls_mbar_wait_backoff(qfree + qs_i, (use - 1) & 1u, p.err, 64)) aborted = true;
-            if (p.trace) tt_acc[1] += ls_now() - tq0;
-            float* rb = red + (qs_i * kLsWarps + warp) * 16;
-            if (t == 0) {
-                rb[g] = acc[0] + acc[1];
-                rb[g + 8] = acc[2] + acc[3];
-            }
-            acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
-            __syncwarp();
-            if (lane == 0) mbar_arrive(qfull + qs_i);
-            ++tile_i;
         }
         arrive(ph);
     }
     if (p.trace) {
         tt_acc[4] = ls_now() - tl0;
-        if (lane == 0) {  // one warp's share per CTA row: [CTA][warp][5]
+        if (lane == 0) {  // [CTA][warp][5]
             unsigned long long* st = p.trace + (size_t)G * nph * 3 + ((size_t)c * kLsWarps + warp) * 5;
             for (int k = 0; k < 5; ++k) st[k] = tt_acc[k];
         }
