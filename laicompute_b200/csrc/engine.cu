@@ -855,8 +855,10 @@ struct laic_dev {
                 return LAIC_OK;
         const bool lm_in = lm_head().type == type;
         const int nb_max = std::max(std::max(h, hq), F) / 32;
-        // attention chunks of one kv head span at most this many consecutive CTAs
-        const int att_runs = std::min(num_sms(), num_sms() / std::max(1, Hkv) + 2);
+        // the attention chunks of one kv head (at most cap / positions-per-chunk of them) span at
+        // most one CTA per chunk: the merge's per-run weights are sized for that
+        const int att_runs = std::min(num_sms(), (cap + laic::ls_positions_per_chunk(D) - 1) /
+                                                     laic::ls_positions_per_chunk(D));
         int nst = 8;  // attention ring stages (K / V chunks), as many as fit
         size_t smem = 0;
         for (; nst >= 2; --nst)

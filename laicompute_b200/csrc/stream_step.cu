@@ -30,8 +30,8 @@ size_t ls_smem(int type, int stages, int D, int G, int nb_max, int att_runs) {
     const int GM = pow2_at_least(G), CP = ls_cp(D);
     size_t b = (size_t)stages * kLsStage;                                   // attention ring
     b += (size_t)kLsWarps * kLsWRing * (type == T_Q4_0 ? ls_wstage(T_Q4_0) : ls_wstage(T_Q8_0));  // weight rings
-    b += (size_t)(2 * kLsMaxStages + kLsWarps * kLsWRing + 2 + 2 * kLsQueue) * 8;  // mbarriers
-    b += (size_t)kLsQueue * kLsWarps * 16 * 4;                              // tile partials queue
+    b += (size_t)(2 * kLsMaxStages + kLsWarps * kLsWRing + 2 + 2 * kLsWarps * kLsPQ) * 8;  // mbarriers
+    b += (size_t)kLsWarps * kLsPQ * 16 * 4;                                 // tile pieces queues
     b += (size_t)GM * D * 4 + (size_t)GM * CP * 4 + 3 * GM * 4;             // attention: output, scores, state
     b += (size_t)att_runs * GM * 4;                                         // attention: merge weights
     b += 16 + 64;                                                           // alignment + broadcast words

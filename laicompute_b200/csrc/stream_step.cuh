@@ -2,23 +2,29 @@
 // streaming weights (the batch-1 latency path of LlamaRuntime::step, reference
 // src/inference_v2.cpp:31, for Q4_0 or Q8_0 projections with an FP16 KV cache).
 //
-// One CTA per SM. Inside a CTA one producer warp and eight consumer warps:
+// One CTA per SM; inside a CTA sixteen consumer warps, one producer warp and two
+// epilogue warps.
 //
-//  * The producer walks the CTA's share of every phase of the step, in step
-//    order, and copies it into a ring of 9 KB shared-memory stages with 1-D
-//    bulk copies (cp.async.bulk + mbarrier): weight tile-blocks of each
-//    projection, and for attention the K and V rows of the positions written by
-//    earlier steps. None of this depends on the step's activations, so the
-//    producer never waits for another CTA: while the consumers wait for a phase
-//    to finish on every SM, the ring keeps filling with the next phase's bytes,
-//    and HBM stays busy across the phase boundaries that separate kernel
-//    launches elsewhere.
+//  * Each consumer warp streams its own contiguous share of the CTA's tile-blocks
+//    of every projection phase, in step order, through its own ring of three
+//    ~2.2 KB shared-memory stages (1-D bulk copies, cp.async.bulk + mbarrier,
+//    issued by its lane 0). Weights never depend on the step's activations, so a
+//    warp's ring keeps filling with the next phase's bytes while the warp waits
+//    for the other SMs at a phase boundary, and HBM stays busy across the
+//    boundaries that separate kernel launches elsewhere.
+//  * The producer warp copies the attention phases' K and V chunks (the rows of
+//    earlier steps) into a shared ring of 9 KB stages, its lanes issuing a batch
+//    of stages together.
 //  * The consumers run the phases in order. Before a phase they wait until every
 //    CTA has arrived at the previous phase's counter (a bounded spin on a 64-bit
 //    monotonic counter: target = CTAs x launch epoch), copy the phase's input
 //    activation records into shared memory with one bulk copy and, for a
 //    projection after an rmsnorm, form 1/rms from the per-tile sums of squares
-//    the producing phase wrote; then they consume the ring.
+//    the producing phase wrote.
+//  * A consumer warp hands the 16 row sums of each row tile its share touches
+//    (a "piece") to the epilogue warps through its own small queue. An epilogue
+//    warp adds a tile's pieces in warp order and runs the tile's global epilogue,
+//    so consumer warps never wait on a global round trip.
 //
 // Phases of a step: EMB (token row -> residual x), then per layer QKV (rmsnorm,
 // fused [Wq;Wk;Wv], RoPE, K/V append), ATT (GQA attention), O (Wo, residual
@@ -28,21 +34,17 @@
 //
 // Projection work is split evenly by tile-blocks: CTA c owns the blocks
 // [c N / G, (c+1) N / G) of the phase's [row tile][block column] order, so a
-// 16-row tile may be shared by consecutive CTAs; its pieces meet in a global
-// scratch slot and the last piece to arrive (atomic ticket) adds them in piece
-// order (deterministic) and runs the epilogue. Epilogues that feed the next
-// projection also write its activation records: a 32-element record block spans
-// 2 row tiles (4 for SwiGLU), and the last tile of the block (another ticket)
-// writes it.
+// 16-row tile may be shared by consecutive CTAs; its CTA pieces meet in a global
+// scratch slot and the last to arrive (atomic ticket) adds them in CTA order
+// (deterministic) and runs the epilogue. Epilogues that feed the next projection
+// also write its activation records, one 8-element group at a time.
 //
-// The matvec inner loop (one sequence). A 16 x 32 tile-block is two tensor-core
-// products mma.m16n8k16 (f16 in, f32 accumulate): the block's quants become exact
-// binary16 integers (q - 8 for Q4_0, q for Q8_0) in registers, and the activation
-// record holds the block's 32 values scaled by a power of two 2^s (largest
-// magnitude in [2^10, 2^11)) and split into binary16 hi + lo parts, as columns 0
-// and 1 of the B operand (columns 2..7 zero). Per block the two column sums are
-// scaled by d_row x 2^-s in FP32 and accumulated; a row's value is the sum of its
-// hi and lo accumulators.
+// The matvec inner loop (one sequence) is integer: the activation record of a
+// 32-column block holds, per 8-element group, the values scaled by a power of two
+// and split into three balanced base-128 int8 digits, plus -8 x (sum of the
+// group) for Q4_0's nibble offset and the inverse scale; a lane multiplies a
+// row's 8 quants with each digit word by dp4a, joins the three exact integer sums
+// and adds d_row x 2^-s x sum in FP32 (tile_block_dp in mv_streamk.cuh).
 //
 // Every wait is bounded (about one second of SM clocks); a wait that runs out
 // records its code in `err`, and once `err` is set the dependency waits stop
@@ -61,7 +63,8 @@ constexpr int kLsStage = 9216;                       // attention ring stage byt
 constexpr int kLsWRing = 3;                          // weight stages in flight per consumer warp
 constexpr int kLsRec = 128;                          // activation record bytes per 32-column block (+ 4 B scale)
 constexpr int kLsMaxStages = 24;
-constexpr int kLsQueue = 8;                          // tile partials in flight between consumers and finishers
+constexpr int kLsPQ = 4;                             // tile pieces in flight from one consumer warp to the
+                                                     // epilogue warps (a multiple of kLsEpi)
 constexpr int kLsIssue = 8;                          // ring stages the producer warp's lanes issue together
 constexpr long long kLsSpin = 2000000000LL;          // clock cycles a dependency wait may take
 
@@ -112,7 +115,7 @@ struct LsParams {
     unsigned* rec_tick;                   // [max record blocks]
     float* apart;                         // attention partials [kv_head][chunk][G (D + 2)]
     int att_maxch;                        // chunks per kv head the scratch holds
-    int att_runs;                         // most CTAs one kv head's chunks can be spread over
+    int att_runs;                         // most CTAs one kv head's chunks can be spread over (one per chunk)
     unsigned* head_tick;                  // [kv_heads]
     unsigned long long* done;             // [phases] arrivals (monotonic)
     unsigned long long* epoch;            // launches completed
@@ -169,6 +172,11 @@ __device__ __forceinline__ int ls_lo(unsigned n, int c, int g) {
 __device__ __forceinline__ int ls_owner(unsigned n, unsigned i, int g) {
     return n >= (unsigned)g ? (int)(((i + 1) * (unsigned)g + n - 1) / n) - 1 : (int)i;
 }
+// The consumer warp owning item i of a CTA's n items (n > 0) split as
+// [n w / kLsWarps, n (w + 1) / kLsWarps): the last warp whose range starts at or before i.
+__device__ __forceinline__ int ls_warp_owner(unsigned n, unsigned i) {
+    return (int)(((i + 1) * (unsigned)kLsWarps + n - 1) / n) - 1;
+}
 // atomic add with acquire-release ordering at GPU scope: the caller's earlier writes (and
 // those of its warp, ordered before by __syncwarp) are visible before the count moves,
 // and reads after it see every write released by earlier adds
@@ -191,7 +199,9 @@ __host__ __device__ inline size_t ls_rec_bytes(int nb) { return (size_t)nb * kLs
 
 // Bounded wait for an mbarrier phase that backs off with nanosleep between polls: a hot
 // poll (try_wait and the clock read in a tight loop) takes issue slots and the
-// conversion pipe from the warps doing the step's work. Returns false after ~1 s (err set).
+// conversion pipe from the warps doing the step's work. Returns false after ~1 s (err set),
+// or at once when another wait of the step already failed (err already set), so that a
+// failed step ends after one timeout rather than one per wait.
 __device__ __forceinline__ bool ls_mbar_wait_backoff(uint64_t* bar, uint32_t parity, int* err, unsigned max_ns = 256) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
@@ -199,12 +209,20 @@ __device__ __forceinline__ bool ls_mbar_wait_backoff(uint64_t* bar, uint32_t par
     while (!mbar_try_wait(bar, parity)) {
         __nanosleep(ns);
         ns = ns < max_ns ? ns * 2 : max_ns;
+        if (ld_volatile_i32(err) != 0) return false;
         if (clock64() - t0 > kLsSpin) {
             atomicExch(err, kErrMbarrier);
             return false;
         }
     }
     return true;
+}
+
+// After a wait gave up (err set), a warp may leave while bulk copies it issued are still in
+// flight: it lingers ~20 us first so that they land in this CTA's shared memory.
+__device__ __forceinline__ void ls_settle(const int* err) {
+    if (ld_volatile_i32(err) != 0)
+        for (int i = 0; i < 20; ++i) __nanosleep(1000);
 }
 
 // Named barrier of the consumer warps (the producer warp never joins it).
@@ -297,6 +315,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
     constexpr int OP2 = (GM * D / 2 + kLsWarps * 32 - 1) / (kLsWarps * 32);  // attention output pairs per thread
     static_assert(WT == T_Q4_0 || WT == T_Q8_0, "Q4_0 or Q8_0 projections");
     static_assert(PPW >= 1, "at least one chunk position per warp");
+    static_assert(kLsPQ % kLsEpi == 0, "an epilogue warp sees every kLsPQ-th piece of a consumer warp before the next use");
     extern __shared__ __align__(128) uint8_t smem[];
     const int NST = p.nstages;  // attention ring stages
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -310,10 +329,10 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
     uint64_t* empty = full + kLsMaxStages;
     uint64_t* wfull = empty + kLsMaxStages;                                 // [kLsWarps][kLsWRing]
     uint64_t* xbar = wfull + kLsWarps * kLsWRing;
-    uint64_t* qfull = xbar + 2;                                 // [kLsQueue] a tile's warp partials are in
-    uint64_t* qfree = qfull + kLsQueue;                         // [kLsQueue] an epilogue warp read them
-    float* red = reinterpret_cast<float*>(qfree + kLsQueue);    // [kLsQueue][kLsWarps][16]
-    float* qs = red + kLsQueue * kLsWarps * 16;                 // [GM][D] merged attention output
+    uint64_t* pfull = xbar + 2;                                 // [kLsWarps][kLsPQ] a warp's tile piece is in
+    uint64_t* pfree = pfull + kLsWarps * kLsPQ;                 // [kLsWarps][kLsPQ] an epilogue warp read it
+    float* red = reinterpret_cast<float*>(pfree + kLsWarps * kLsPQ);  // [kLsWarps][kLsPQ][16] piece row sums
+    float* qs = red + kLsWarps * kLsPQ * 16;                    // [GM][D] merged attention output
     float* ss_att = qs + GM * D;                                // [GM][CP] scores, then weights
     float* hm = ss_att + GM * CP;                               // [GM] running max
     float* hl = hm + GM;                                        // [GM] running sum
@@ -330,9 +349,9 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
         }
         for (int s = 0; s < kLsWarps * kLsWRing; ++s) mbar_init(wfull + s, 1);
         mbar_init(xbar, 1);
-        for (int q = 0; q < kLsQueue; ++q) {
-            mbar_init(qfull + q, kLsWarps);
-            mbar_init(qfree + q, 1);
+        for (int q = 0; q < kLsWarps * kLsPQ; ++q) {
+            mbar_init(pfull + q, 1);
+            mbar_init(pfree + q, 1);
         }
         mbar_fence_init();
     }
@@ -376,7 +395,10 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
             const uint8_t* s0 = nullptr;
             uint32_t b0 = 0;
             int cnt = 0;
-            for (int l = 0; l < kLsIssue; ++l) {
+            // at most one use of each slot per batch: a lane waits for its slot's previous use
+            // only, so its parity wait never aliases a phase two uses back
+            const int batch = min(kLsIssue, NST);
+            for (int l = 0; l < batch; ++l) {
                 const uint8_t* t0;
                 uint32_t c0;
                 if (!next(t0, c0)) break;
@@ -399,6 +421,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
             __syncwarp();
             i0 += cnt;
         }
+        ls_settle(p.err);
         return;
     }
 
@@ -407,7 +430,9 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
     // =====================================================================
     if (warp > kLsWarps) {
         const int e = warp - kLsWarps - 1;
-        int tile_i = 0;
+        // lane w < kLsWarps: pieces consumer warp w queued in earlier phases (both epilogue
+        // warps keep the same counts)
+        int wbase = 0;
         for (int ph = 0; ph < nph; ++ph) {
             const int kind = ls_kind(ph, L);
             const int layer = kind == LS_EMB ? 0 : kind == LS_LM ? L - 1 : (ph - 1) / 5;
@@ -418,23 +443,38 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                 const float inv = reinterpret_cast<const float*>(ictl)[5];
                 const int sl = ictl[2], pos = ictl[3];
                 const int lo = ls_lo((unsigned)m.nblk, c, G), hi = ls_lo((unsigned)m.nblk, c + 1, G);
+                const unsigned n = (unsigned)(hi - lo);
+                // consumer warp `lane`'s share of the phase: its first tile and its piece count
+                const int wl = lo + (int)(n * (unsigned)lane / kLsWarps), wh = lo + (int)(n * (unsigned)(lane + 1) / kLsWarps);
+                const int wtile = wl / max(m.nb, 1);
+                const int wcnt = lane < kLsWarps && wl < wh ? (wh - 1) / m.nb - wl / m.nb + 1 : 0;
                 if (lo < hi) {
-                    for (int tile = lo / m.nb; tile <= (hi - 1) / m.nb; ++tile, ++tile_i) {
+                    for (int tile = lo / m.nb, tile_i = 0; tile <= (hi - 1) / m.nb; ++tile, ++tile_i) {
                         if ((tile_i % kLsEpi) != e) continue;
-                        const int qs_i = tile_i & (kLsQueue - 1);
-                        const uint32_t use = (uint32_t)(tile_i / kLsQueue);
-                        ls_mbar_wait_backoff(qfull + qs_i, use & 1u, p.err, 64);
+                        // the tile's pieces come from consumer warps wf..wt (their pieces in warp
+                        // order); with fewer blocks than warps some of them have an empty share
+                        // and queue nothing
+                        const int wf = ls_warp_owner(n, (unsigned)(max(lo, tile * m.nb) - lo));
+                        const int wt = ls_warp_owner(n, (unsigned)(min(hi, (tile + 1) * m.nb) - 1 - lo));
+                        const int kme = wbase + tile - wtile;  // (lane w: warp w's piece number for this tile)
                         float v = 0.f;
-                        if (lane < 16)
-                            for (int w = 0; w < kLsWarps; ++w) v += red[(qs_i * kLsWarps + w) * 16 + lane];
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(qfree + qs_i);
+                        for (int w = wf; w <= wt; ++w) {
+                            if (__shfl_sync(0xffffffffu, wcnt, w) == 0) continue;
+                            const int k = __shfl_sync(0xffffffffu, kme, w);
+                            const int qi = w * kLsPQ + k % kLsPQ;
+                            ls_mbar_wait_backoff(pfull + qi, (uint32_t)(k / kLsPQ) & 1u, p.err, 64);
+                            if (lane < 16) v += red[qi * 16 + lane];
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(pfree + qi);
+                        }
                         ls_finish_tile<WT, D>(p, kind, layer, m, tile, v, inv, norm, pos, sl, c, G, lane);
                     }
                 }
+                wbase += wcnt;
             }
             ls_sync_all();  // every tile of the phase finished: the consumers may arrive
         }
+        ls_settle(p.err);
         return;
     }
 
@@ -509,7 +549,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
     int slot = 0;
     uint32_t round = 0, xphase = 0;
     bool aborted = false;
-    int tile_i = 0;   // tile pieces this CTA handed to the epilogue warps (queue slot)
+    int npiece = 0;   // tile pieces this warp queued for the epilogue warps
     int wcons = 0;    // weight stages this warp consumed
 
     // Wait until every CTA arrived at phase `ph`'s counter.
@@ -755,7 +795,11 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                     }
                     ls_cbar();
                     if (ictl[1]) {  // the last run of head j: merge every run (CTA order)
-                        const int nruns = cl - cf + 1;
+                        int nruns = cl - cf + 1;
+                        if (nruns > p.att_runs) {  // (the host sizes att_runs for every position; never taken)
+                            if (ct == 0) atomicExch(p.err, kErrDepCounter);
+                            nruns = p.att_runs;
+                        }
                         // per-run weights exp(m_r - M) / S of each head (warp hh, lanes over runs)
                         if (warp < gq) {
                             const int hh = warp;
@@ -825,8 +869,8 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
         const int whi = lo + (hi - lo) * (warp + 1) / kLsWarps;
         int cur = lo + (hi - lo) * warp / kLsWarps;
         const uint32_t xlane = act_a + t * 32;  // this lane's 8-column group of each block record
-        if (lo < hi) {
-            for (int tile = lo / m.nb; tile <= (hi - 1) / m.nb; ++tile) {
+        if (cur < whi) {  // one piece per row tile this warp's share touches
+            for (int tile = cur / m.nb, tlast = (whi - 1) / m.nb; tile <= tlast; ++tile) {
                 const int t_end = min(hi, (tile + 1) * m.nb);
                 float dacc[2] = {0.f, 0.f};
                 while (cur < whi && cur < t_end) {  // this warp's stages inside the tile
@@ -853,25 +897,25 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                     wissue_one();
                     cur += n;
                 }
-                // ---- this warp's part of the tile piece (zero when it has none) into the queue:
-                //      the four lanes of a row hold its four 8-column groups
+                // ---- this warp's piece of the tile into its queue: the four lanes of a row hold
+                //      its four 8-column groups
                 float r0 = dacc[0], r1 = dacc[1];
                 r0 += __shfl_xor_sync(0xffffffffu, r0, 1);
                 r1 += __shfl_xor_sync(0xffffffffu, r1, 1);
                 r0 += __shfl_xor_sync(0xffffffffu, r0, 2);
                 r1 += __shfl_xor_sync(0xffffffffu, r1, 2);
-                const int qs_i = tile_i & (kLsQueue - 1);
-                const uint32_t use = (uint32_t)(tile_i / kLsQueue);
+                const int qi = warp * kLsPQ + npiece % kLsPQ;
+                const uint32_t use = (uint32_t)(npiece / kLsPQ);
                 const unsigned long long tq0 = p.trace ? ls_now() : 0;
-                if (use > 0 && !ls_mbar_wait_backoff(qfree + qs_i, (use - 1) & 1u, p.err, 64)) aborted = true;
+                if (use > 0 && !ls_mbar_wait_backoff(pfree + qi, (use - 1) & 1u, p.err, 64)) aborted = true;
                 if (p.trace) tt_acc[1] += ls_now() - tq0;
                 if (t == 0) {
-                    red[(qs_i * kLsWarps + warp) * 16 + g] = r0;
-                    red[(qs_i * kLsWarps + warp) * 16 + g + 8] = r1;
+                    red[qi * 16 + g] = r0;
+                    red[qi * 16 + g + 8] = r1;
                 }
                 __syncwarp();
-                if (lane == 0) mbar_arrive(qfull + qs_i);
-                ++tile_i;
+                if (lane == 0) mbar_arrive(pfull + qi);
+                ++npiece;
             }
         }
         arrive(ph);
@@ -884,6 +928,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
         }
     }
     (void)aborted;
+    ls_settle(p.err);
 }
 
 }  // namespace laic

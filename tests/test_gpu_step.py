@@ -24,6 +24,11 @@ ARCHS = {
                                  ctx=1024, name="step_q8"),
     "q8_d64_g3": synth.tiny_arch(gguf.Q8_0, hidden=384, layers=2, heads=6, kv_heads=2, ffn=512, vocab=640,
                                  ctx=1024, name="step_q8g3"),
+    # the 8B model's ffn width (its records leave room for only 5 attention stages, fewer
+    # than the producer's batch) and a tied Q4_0 lm_head of the 8B vocabulary on a narrow
+    # model (54 row tiles per CTA, up to 5 pieces per consumer warp in the LM phase)
+    "q4_wide": synth.tiny_arch(gguf.Q4_0, gguf.Q4_0, hidden=256, layers=3, heads=2, kv_heads=1, ffn=14336,
+                               vocab=128256, ctx=1024, rope_theta=500000.0, name="step_q4wide"),
 }
 
 
@@ -32,7 +37,7 @@ def test_step_kernel_matches_oracle_and_layer_path(arch):
     from laicompute_b200.engine import Engine
     a = ARCHS[arch]
     with tempfile.TemporaryDirectory() as d:
-        path = synth.write_model(os.path.join(d, "m.gguf"), a, seed=51)
+        path = synth.write_model(os.path.join(d, "m.gguf"), a, seed=51, direct_blocks=a.vocab > 65536)
         prompt = synth.prompt_ids(a.vocab, 300, seed=52)
         ref_ids, ref_logits = O.OracleModel(path).generate(prompt, 16)
         e = Engine(path, kv_capacity=1024)
