@@ -182,8 +182,8 @@ LAIC_API int laic_dev_profile(laic_dev* dev, int32_t nseq, const uint32_t* token
  * (dependency met, activation records loaded), 2 phase done. Phases: 0 the
  * embedding, then per layer QKV, attention, O, gate/up, down, then the lm_head.
  * After those, per CTA and consumer warp 5 counters (ns): waits for a filled
- * ring stage, waits at tile ends, finishing epilogues, phase waits, and the
- * whole phase loop.
+ * ring stage, waits to queue a tile piece, waits for the epilogue warps at
+ * the end of a phase, phase waits, and the whole phase loop.
  * No counterpart in the reference. */
 LAIC_API int laic_dev_step_trace(laic_dev* dev, uint64_t* out, int64_t max_entries, int64_t* n, int32_t* ctas,
                                  int32_t* phases);

@@ -461,11 +461,11 @@ struct laic_dev {
     // one sequence: the persistent decode-step kernel (stream_step.cuh) and its state
     laic::LsLayer* ls_layers = nullptr;
     uint8_t *ls_rec_x = nullptr, *ls_rec_attn = nullptr, *ls_rec_act = nullptr;
-    float *ls_ss = nullptr, *ls_part = nullptr, *ls_apart = nullptr;
-    unsigned *ls_tile_tick = nullptr, *ls_rec_tick = nullptr, *ls_head_tick = nullptr;
+    float *ls_ss = nullptr, *ls_apart = nullptr;
+    unsigned* ls_head_tick = nullptr;
     unsigned long long *ls_done = nullptr, *ls_epoch = nullptr;
-    size_t ls_done_bytes = 0, ls_tile_bytes = 0, ls_rec_bytes = 0;
-    int ls_type = -1, ls_nst = 0, ls_pieces = 0, ls_maxch = 0, ls_runs = 0;
+    size_t ls_done_bytes = 0;
+    int ls_type = -1, ls_nst = 0, ls_maxch = 0, ls_runs = 0;
     size_t ls_smem_bytes = 0;
     bool ls_ready = false, ls_checked = false, use_ls = true, ls_lm = false;
     unsigned long long* ls_trace = nullptr;  // LAIC_FLAG_TRACE: per-phase stamps of the last step kernel
@@ -878,33 +878,16 @@ struct laic_dev {
         ls_free();
         CK(cudaMalloc(&ls_layers, sizeof(laic::LsLayer) * L));
         CK(cudaMemcpy(ls_layers, tab.data(), sizeof(laic::LsLayer) * L, cudaMemcpyHostToDevice));
-        // split-tile scratch: the most pieces one row tile of any projection can be cut into
         const int Gc = num_sms();
-        int max_tiles = 0, pieces = 2;
-        auto see = [&](const Mat& m) {
-            const long long n = (long long)m.ntiles * m.nb;
-            const long long share = n >= Gc ? n / Gc : 1;
-            max_tiles = std::max(max_tiles, m.ntiles);
-            pieces = std::max(pieces, (int)std::min<long long>(Gc, m.nb / share + 2));
-        };
-        see(layers[0].qkv); see(layers[0].o); see(layers[0].gu); see(layers[0].down);
-        if (lm_in) see(lm_head());
-        const int rec_blocks = std::max(h, F) / 32;
         const int cp = laic::ls_positions_per_chunk(D);
         const int gm = G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8;
         ls_maxch = (cap + cp - 1) / cp;
-        ls_pieces = pieces;
         CK(cudaMalloc(&ls_rec_x, laic::ls_record_bytes(h / 32)));
         CK(cudaMalloc(&ls_rec_attn, laic::ls_record_bytes(hq / 32)));
         CK(cudaMalloc(&ls_rec_act, laic::ls_record_bytes(F / 32)));
         CK(cudaMalloc(&ls_ss, (size_t)(h / 16) * 4));
-        CK(cudaMalloc(&ls_part, (size_t)max_tiles * pieces * 16 * 4));
         CK(cudaMalloc(&ls_apart, (size_t)Hkv * ls_maxch * gm * (D + 2) * 4));
-        ls_tile_bytes = (size_t)max_tiles * 4;
-        ls_rec_bytes = (size_t)rec_blocks * 4;
         ls_done_bytes = (size_t)laic::ls_phases(L) * 8;
-        CK(cudaMalloc(&ls_tile_tick, ls_tile_bytes));
-        CK(cudaMalloc(&ls_rec_tick, ls_rec_bytes));
         CK(cudaMalloc(&ls_head_tick, (size_t)Hkv * 4));
         CK(cudaMalloc(&ls_done, ls_done_bytes));
         CK(cudaMalloc(&ls_epoch, 8));
@@ -927,8 +910,6 @@ struct laic_dev {
     // step whose bounded waits ran out and may have left them part-way).
     int ls_reset() {
         if (!ls_done) return LAIC_OK;
-        CK(cudaMemset(ls_tile_tick, 0, ls_tile_bytes));
-        CK(cudaMemset(ls_rec_tick, 0, ls_rec_bytes));
         CK(cudaMemset(ls_head_tick, 0, (size_t)Hkv * 4));
         CK(cudaMemset(ls_done, 0, ls_done_bytes));
         CK(cudaMemset(ls_epoch, 0, 8));
@@ -936,11 +917,11 @@ struct laic_dev {
     }
 
     void ls_free() {
-        void* bufs[] = {ls_layers, ls_rec_x, ls_rec_attn, ls_rec_act, ls_ss, ls_part, ls_apart, ls_tile_tick,
-                        ls_rec_tick, ls_head_tick, ls_done, ls_epoch, ls_trace};
+        void* bufs[] = {ls_layers, ls_rec_x, ls_rec_attn, ls_rec_act, ls_ss, ls_apart, ls_head_tick, ls_done, ls_epoch,
+                        ls_trace};
         for (void* b : bufs) if (b) cudaFree(b);
-        ls_layers = nullptr; ls_rec_x = ls_rec_attn = ls_rec_act = nullptr; ls_ss = ls_part = ls_apart = nullptr;
-        ls_tile_tick = ls_rec_tick = ls_head_tick = nullptr; ls_done = ls_epoch = nullptr; ls_trace = nullptr;
+        ls_layers = nullptr; ls_rec_x = ls_rec_attn = ls_rec_act = nullptr; ls_ss = ls_apart = nullptr;
+        ls_head_tick = nullptr; ls_done = ls_epoch = nullptr; ls_trace = nullptr;
     }
 
     laic::LsParams ls_params(bool lm_on) const {
@@ -956,7 +937,6 @@ struct laic_dev {
         lp.x = x; lp.q = q; lp.attn = attn; lp.act = act;
         lp.rope_cs = rope_cs; lp.kv_slot_stride = kv_slot_stride; lp.kv_cap = cap;
         lp.rec_x = ls_rec_x; lp.rec_attn = ls_rec_attn; lp.rec_act = ls_rec_act; lp.ss_x = ls_ss;
-        lp.part = ls_part; lp.part_pieces = ls_pieces; lp.tile_tick = ls_tile_tick; lp.rec_tick = ls_rec_tick;
         lp.apart = ls_apart; lp.att_maxch = ls_maxch; lp.att_runs = ls_runs; lp.head_tick = ls_head_tick;
         lp.done = ls_done; lp.epoch = ls_epoch; lp.err = mvs.err; lp.nstages = ls_nst;
         lp.trace = ls_trace;

@@ -1,6 +1,8 @@
 // Instantiations and launch of the persistent one-sequence decode-step kernel
 // (stream_step.cuh): Q4_0 or Q8_0 projections, head_dim 64 or 128, 1 to 8 query
 // heads per KV head.
+#include <algorithm>
+
 #include "launch.cuh"
 #include "stream_step.cuh"
 
@@ -27,15 +29,16 @@ static LsFn ls_pick(int type, int D, int G) {
 static int pow2_at_least(int g) { return g <= 1 ? 1 : g <= 2 ? 2 : g <= 4 ? 4 : 8; }
 
 size_t ls_smem(int type, int stages, int D, int G, int nb_max, int att_runs) {
-    const int GM = pow2_at_least(G), CP = ls_cp(D);
+    const int GM = pow2_at_least(G);
     size_t b = (size_t)stages * kLsStage;                                   // attention ring
     b += (size_t)kLsWarps * kLsWRing * (type == T_Q4_0 ? ls_wstage(T_Q4_0) : ls_wstage(T_Q8_0));  // weight rings
     b += (size_t)(2 * kLsMaxStages + kLsWarps * kLsWRing + 2 + 2 * kLsWarps * kLsPQ) * 8;  // mbarriers
     b += (size_t)kLsWarps * kLsPQ * 16 * 4;                                 // tile pieces queues
-    b += (size_t)GM * D * 4 + (size_t)GM * CP * 4 + 3 * GM * 4;             // attention: output, scores, state
+    b += (size_t)GM * D * 4;                                                // attention: merged output
     b += (size_t)att_runs * GM * 4;                                         // attention: merge weights
-    b += 16 + 64;                                                           // alignment + broadcast words
-    b += 128 + ls_rec_bytes(nb_max);                                        // alignment + activation records
+    b += 16 + 64 + kLsWarps * 5 * 4;                                        // alignment + broadcast words + trace counters
+    // alignment + activation records, or the consumer warps' attention states and weights
+    b += 128 + std::max(ls_rec_bytes(nb_max), (size_t)kLsWarps * GM * (D + 3) * 4);
     return b;
 }
 

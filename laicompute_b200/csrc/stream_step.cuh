@@ -32,12 +32,12 @@
 // add), and LM (final rmsnorm, lm_head) when the lm_head shares the layers'
 // block type.
 //
-// Projection work is split evenly by tile-blocks: CTA c owns the blocks
-// [c N / G, (c+1) N / G) of the phase's [row tile][block column] order, so a
-// 16-row tile may be shared by consecutive CTAs; its CTA pieces meet in a global
-// scratch slot and the last to arrive (atomic ticket) adds them in CTA order
-// (deterministic) and runs the epilogue. Epilogues that feed the next projection
-// also write its activation records, one 8-element group at a time.
+// Projection work is split by whole 16-row tiles: CTA c owns the tiles
+// [c T / G, (c+1) T / G) of the phase's T tiles (all their block columns), so a
+// tile's row sums never cross CTAs and its epilogue needs no global round trip;
+// inside the CTA the tile-blocks are split evenly over the consumer warps.
+// Epilogues that feed the next projection also write its activation records, one
+// 8-element group at a time.
 //
 // The matvec inner loop (one sequence) is integer: the activation record of a
 // 32-column block holds, per 8-element group, the values scaled by a power of two
@@ -109,10 +109,6 @@ struct LsParams {
     int kv_cap;
     uint8_t *rec_x, *rec_attn, *rec_act;  // activation records of the projections' inputs
     float* ss_x;                          // [h / 16] sums of squares of the residual per row tile
-    float* part;                          // split tiles: [tile][piece][16]
-    int part_pieces;
-    unsigned* tile_tick;                  // [max row tiles]
-    unsigned* rec_tick;                   // [max record blocks]
     float* apart;                         // attention partials [kv_head][chunk][G (D + 2)]
     int att_maxch;                        // chunks per kv head the scratch holds
     int att_runs;                         // most CTAs one kv head's chunks can be spread over (one per chunk)
@@ -172,6 +168,12 @@ __device__ __forceinline__ int ls_lo(unsigned n, int c, int g) {
 __device__ __forceinline__ int ls_owner(unsigned n, unsigned i, int g) {
     return n >= (unsigned)g ? (int)(((i + 1) * (unsigned)g + n - 1) / n) - 1 : (int)i;
 }
+// The tile-blocks [lo, hi) of a projection phase owned by CTA c: whole row tiles
+// [c T / G, (c+1) T / G) of its T tiles, so that no tile's row sums are split across CTAs.
+__device__ __forceinline__ void ls_range(const LsMat& m, int c, int G, int& lo, int& hi) {
+    lo = ls_lo((unsigned)m.ntiles, c, G) * m.nb;
+    hi = ls_lo((unsigned)m.ntiles, c + 1, G) * m.nb;
+}
 // The consumer warp owning item i of a CTA's n items (n > 0) split as
 // [n w / kLsWarps, n (w + 1) / kLsWarps): the last warp whose range starts at or before i.
 __device__ __forceinline__ int ls_warp_owner(unsigned n, unsigned i) {
@@ -228,27 +230,11 @@ __device__ __forceinline__ void ls_settle(const int* err) {
 // Named barrier of the consumer warps (the producer warp never joins it).
 __device__ __forceinline__ void ls_cbar() { named_sync(1, kLsWarps * 32); }
 
-// The epilogue of one row tile's piece (an epilogue warp; lanes 0..15 hold the piece's 16
-// row sums in v): pieces of a tile shared with other CTAs meet in scratch and the last to
-// arrive adds them in piece order, then the phase's epilogue runs on the finished rows.
+// The epilogue of one finished row tile (an epilogue warp; lanes 0..15 hold the tile's
+// 16 row sums in v).
 template <int WT, int D>
 __device__ __forceinline__ void ls_finish_tile(const LsParams& p, int kind, int layer, const LsMat& m, int tile, float v,
-                                               float inv, bool norm, int pos, int sl, int c, int G, int lane) {
-    const unsigned t_first = (unsigned)tile * m.nb;
-    const int cf = ls_owner((unsigned)m.nblk, t_first, G), cl = ls_owner((unsigned)m.nblk, t_first + m.nb - 1, G);
-    if (cl > cf) {
-        float* slot_p = p.part + ((size_t)tile * p.part_pieces) * 16;
-        if (lane < 16) slot_p[(c - cf) * 16 + lane] = v;
-        __syncwarp();
-        unsigned last = 0;
-        if (lane == 0) last = atom_add_acq_rel(p.tile_tick + tile, 1u) == (unsigned)(cl - cf);
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (!last) return;
-        v = 0.f;
-        if (lane < 16)
-            for (int i = 0; i <= cl - cf; ++i) v += __ldcg(slot_p + i * 16 + lane);
-        if (lane == 0) p.tile_tick[tile] = 0u;
-    }
+                                               float inv, bool norm, int pos, int sl, int lane) {
     if (norm) v *= inv;
     const int r = tile * 16 + lane;  // this lane's row (lanes 0..15)
     const bool live = lane < 16 && r < m.rows;
@@ -312,7 +298,6 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
     constexpr int CP = ls_cp(D);
     constexpr int E = D / 32;               // head dims per lane
     constexpr int PPW = CP / kLsWarps;      // chunk positions per consumer warp (scores)
-    constexpr int OP2 = (GM * D / 2 + kLsWarps * 32 - 1) / (kLsWarps * 32);  // attention output pairs per thread
     static_assert(WT == T_Q4_0 || WT == T_Q8_0, "Q4_0 or Q8_0 projections");
     static_assert(PPW >= 1, "at least one chunk position per warp");
     static_assert(kLsPQ % kLsEpi == 0, "an epilogue warp sees every kLsPQ-th piece of a consumer warp before the next use");
@@ -333,13 +318,11 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
     uint64_t* pfree = pfull + kLsWarps * kLsPQ;                 // [kLsWarps][kLsPQ] an epilogue warp read it
     float* red = reinterpret_cast<float*>(pfree + kLsWarps * kLsPQ);  // [kLsWarps][kLsPQ][16] piece row sums
     float* qs = red + kLsWarps * kLsPQ * 16;                    // [GM][D] merged attention output
-    float* ss_att = qs + GM * D;                                // [GM][CP] scores, then weights
-    float* hm = ss_att + GM * CP;                               // [GM] running max
-    float* hl = hm + GM;                                        // [GM] running sum
-    float* hsc = hl + GM;                                       // [GM] rescale of the running output
-    float* wrun = hsc + GM;                                     // [att_runs][GM] merge weights of the runs
+    float* wrun = qs + GM * D;                                  // [att_runs][GM] merge weights of the runs
     int* ictl = reinterpret_cast<int*>((reinterpret_cast<uintptr_t>(wrun + p.att_runs * GM) + 15) & ~uintptr_t(15));
-    uint8_t* act = reinterpret_cast<uint8_t*>(ictl + 16);       // activation records of the phase
+    // ictl: [16] broadcast words, then [kLsWarps][5] trace counters
+    uint8_t* act = reinterpret_cast<uint8_t*>(ictl + 16 + kLsWarps * 5);  // activation records of the phase (attention:
+                                                                // the warps' softmax states of a run)
     act = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(act) + 127) & ~uintptr_t(127));
 
     if (threadIdx.x == 0) {
@@ -442,7 +425,8 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                 const bool norm = kind == LS_QKV || kind == LS_GU || kind == LS_LM;
                 const float inv = reinterpret_cast<const float*>(ictl)[5];
                 const int sl = ictl[2], pos = ictl[3];
-                const int lo = ls_lo((unsigned)m.nblk, c, G), hi = ls_lo((unsigned)m.nblk, c + 1, G);
+                int lo, hi;
+                ls_range(m, c, G, lo, hi);
                 const unsigned n = (unsigned)(hi - lo);
                 // consumer warp `lane`'s share of the phase: its first tile and its piece count
                 const int wl = lo + (int)(n * (unsigned)lane / kLsWarps), wh = lo + (int)(n * (unsigned)(lane + 1) / kLsWarps);
@@ -467,7 +451,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                             __syncwarp();
                             if (lane == 0) mbar_arrive(pfree + qi);
                         }
-                        ls_finish_tile<WT, D>(p, kind, layer, m, tile, v, inv, norm, pos, sl, c, G, lane);
+                        ls_finish_tile<WT, D>(p, kind, layer, m, tile, v, inv, norm, pos, sl, lane);
                     }
                 }
                 wbase += wcnt;
@@ -508,7 +492,8 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
             const int kind = ls_kind(w_ph, L);
             if (kind == LS_EMB || kind == LS_ATT) continue;
             const LsMat m = ls_mat(p, kind, kind == LS_LM ? L - 1 : (w_ph - 1) / 5);
-            const int lo = ls_lo((unsigned)m.nblk, c, G), hi = ls_lo((unsigned)m.nblk, c + 1, G);
+            int lo, hi;
+            ls_range(m, c, G, lo, hi);
             w_cur = lo + (hi - lo) * warp / kLsWarps;
             w_hi = lo + (hi - lo) * (warp + 1) / kLsWarps;
             w_nb = m.nb;
@@ -564,34 +549,28 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
         }
         ls_cbar();
     };
+    // trace: per-warp ns spent in [0] stage waits, [1] tile-end queue waits, [2] waits for the
+    // epilogue warps to finish the phase, [3] phase waits (dependency + records), [4] the whole
+    // phase loop
+    unsigned* tt_acc = reinterpret_cast<unsigned*>(ictl + 16) + warp * 5;  // (lane 0 adds)
+    if (lane == 0)
+        for (int k = 0; k < 5; ++k) tt_acc[k] = 0u;
     auto arrive = [&](int ph) {
+        const unsigned long long te0 = p.trace ? ls_now() : 0;
         ls_sync_all();  // every consumer's and epilogue warp's writes of the phase precede the arrival
+        if (p.trace && lane == 0) tt_acc[2] += (unsigned)(ls_now() - te0);
         if (p.trace && ct == 0) p.trace[((size_t)c * nph + ph) * 3 + 2] = ls_now();
         if (ct == 0) {
             __threadfence();
-            const unsigned long long old = atomicAdd(p.done + ph, 1ull);
-            if (ph == nph - 1 && old + 1 == target) {  // the step's last arrival: next launch's epoch
+            if (ph < nph - 1) {
+                atomicAdd(p.done + ph, 1ull);  // (result unused: a reduction, no round trip to wait for)
+            } else if (atomicAdd(p.done + ph, 1ull) + 1 == target) {  // the step's last arrival
                 __threadfence();
                 *reinterpret_cast<volatile unsigned long long*>(p.epoch) = target / (unsigned long long)G;
             }
         }
     };
-    // trace: per-warp ns spent in [0] stage waits, [1] tile-end queue waits, [2] unused,
-    // [3] phase waits (dependency + records), [4] the whole phase loop
-    unsigned long long tt_acc[5] = {0, 0, 0, 0, 0};
     // the attention ring (K / V chunks from the producer warp)
-    auto stage_wait = [&]() -> uint32_t {
-        const unsigned long long tw0 = p.trace ? ls_now() : 0;
-        if (!ls_mbar_wait_backoff(full + slot, round & 1u, p.err, 64)) aborted = true;
-        __syncwarp();
-        if (p.trace) tt_acc[0] += ls_now() - tw0;
-        return smem_u32(ring + (size_t)slot * kLsStage);
-    };
-    auto stage_release = [&]() {
-        __syncwarp();
-        if (lane == 0) mbar_arrive(empty + slot);
-        if (++slot == p.nstages) { slot = 0; ++round; }
-    };
     // the phase's input records (nb blocks) into `act`; 1/rms from ss_x when `norm`
     auto load_records = [&](const uint8_t* src, int nb, bool norm, int nss) {
         if (ct == 0) {
@@ -622,7 +601,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
         if (trace && ct == 0) trace[ph * 3] = ls_now();
         const unsigned long long tp0 = p.trace ? ls_now() : 0;
         if (ph > 0) wait_phase(ph - 1);
-        if (p.trace) tt_acc[3] += ls_now() - tp0;
+        if (p.trace && lane == 0) tt_acc[3] += (unsigned)(ls_now() - tp0);
         if (kind == LS_EMB || kind == LS_ATT) ls_sync_all();  // (the epilogue warps have nothing to do)
         if (trace && ct == 0 && (kind == LS_EMB || kind == LS_ATT)) trace[ph * 3 + 1] = ls_now();
 
@@ -646,6 +625,13 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
         }
 
         // ------------------------------------------------------------ ATT
+        // Chunks [ilo, ihi) of the step's (kv head, CP-position chunk) list. Every consumer
+        // warp keeps its own online-softmax state (running max, sum and output of the
+        // group's query heads over the positions it owns: pl = warp + 16 i of each chunk),
+        // so a chunk needs no CTA barrier; at the end of a run over one kv head the warps'
+        // states are merged in shared memory into the CTA's partial, and the last CTA of
+        // the head (ticket) merges the partials of its runs and writes the attention output
+        // and its records.
         if (kind == LS_ATT) {
             const LsLayer& ly = p.layers[layer];
             const int nch = (pos + 1 + CP - 1) / CP;
@@ -653,139 +639,132 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
             const int ilo = ls_lo(I, c, G), ihi = ls_lo(I, c + 1, G);
             const __half* kg = reinterpret_cast<const __half*>(ly.kc) + (size_t)sl * p.kv_slot_stride;
             const __half* vg = reinterpret_cast<const __half*>(ly.vc) + (size_t)sl * p.kv_slot_stride;
-            float2 o_acc[OP2];
-            float qreg[GM][E];
+            float* comb = reinterpret_cast<float*>(act);   // [kLsWarps][GM][D + 2] warp states of a run
+            float* cw = comb + kLsWarps * GM * (D + 2);    // [kLsWarps][GM] their merge weights
+            float o[GM][E], hmx[GM], hsum[GM];
             int run_start = 0;
             int j = ilo / nch, ch = ilo % nch;
             for (int it = ilo; it < ihi; ++it, (++ch == nch ? (ch = 0, ++j) : 0)) {
                 if (it == ilo || ch == 0) {
-                    // a new kv head: this lane's slice of the group's query rows, fresh softmax state
+                    // a new kv head: the group's query rows into shared memory, fresh state
+                    if (it != ilo) ls_cbar();  // (every warp is done with the previous head's rows)
+                    for (int i = ct; i < GM * D; i += kLsWarps * 32)
+                        qs[i] = i < gq * D ? __ldcg(p.q + (size_t)j * gq * D + i) : 0.f;
 #pragma unroll
-                    for (int hh = 0; hh < GM; ++hh)
+                    for (int hh = 0; hh < GM; ++hh) {
 #pragma unroll
-                        for (int e = 0; e < E; ++e)
-                            qreg[hh][e] = hh < gq ? __ldcg(p.q + ((size_t)j * gq + hh) * D + lane * E + e) : 0.f;
-                    if (ct < GM) { hm[ct] = -INFINITY; hl[ct] = 0.f; }
-#pragma unroll
-                    for (int k = 0; k < OP2; ++k) o_acc[k] = make_float2(0.f, 0.f);
+                        for (int e = 0; e < E; ++e) o[hh][e] = 0.f;
+                        hmx[hh] = -INFINITY;
+                        hsum[hh] = 0.f;
+                    }
                     run_start = ch;
                     ls_cbar();
                 }
                 const int r0 = ch * CP, nvalid = min(CP, pos + 1 - r0);
-                const bool has_new = r0 + nvalid - 1 == pos;  // the chunk ends with this step's row (from L2)
-                const int nsm = has_new ? nvalid - 1 : nvalid;  // rows in the ring stage
-                // ---- K stage: the warp's positions pl = warp + 8 i, lanes split the head dims
-                stage_wait();
-                const __half* ks = reinterpret_cast<const __half*>(ring + (size_t)slot * kLsStage);
-                float sc[PPW][GM];
+                // the chunk ends with this step's row when it holds position pos: the ring stages
+                // hold the rows before it (written by earlier steps), and the warp owning that
+                // position copies this step's K and V rows (from L2) into the stages' next row
+                const bool has_new = r0 + nvalid - 1 == pos;
+                // the chunk's K and V stages (consecutive in the ring)
+                const int slot_v = slot + 1 == NST ? 0 : slot + 1;
+                const uint32_t round_v = slot + 1 == NST ? round + 1 : round;
+                {
+                    const unsigned long long tw0 = p.trace ? ls_now() : 0;
+                    if (!ls_mbar_wait_backoff(full + slot, round & 1u, p.err, 64)) aborted = true;
+                    if (!ls_mbar_wait_backoff(full + slot_v, round_v & 1u, p.err, 64)) aborted = true;
+                    __syncwarp();
+                    if (p.trace && lane == 0) tt_acc[0] += (unsigned)(ls_now() - tw0);
+                }
+                __half* ks = reinterpret_cast<__half*>(ring + (size_t)slot * kLsStage);
+                __half* vs = reinterpret_cast<__half*>(ring + (size_t)slot_v * kLsStage);
+                const bool own_new = has_new && (nvalid - 1) % kLsWarps == warp;
+                if (own_new) {
+                    using R = typename std::conditional<E == 4, uint2, uint32_t>::type;  // E halves
+                    const size_t off = ((size_t)j * p.kv_cap + pos) * D + lane * E;
+                    const R kk = __ldcg(reinterpret_cast<const R*>(kg + off));
+                    const R vv = __ldcg(reinterpret_cast<const R*>(vg + off));
+                    *reinterpret_cast<R*>(ks + (size_t)(nvalid - 1) * D + lane * E) = kk;
+                    *reinterpret_cast<R*>(vs + (size_t)(nvalid - 1) * D + lane * E) = vv;
+                    __syncwarp();
+                }
+                // this warp's positions, one at a time: score, then the online softmax update
 #pragma unroll
                 for (int i = 0; i < PPW; ++i) {
                     const int pl = warp + i * kLsWarps;
-                    float kf[E];
+                    if (pl >= nvalid) break;
+                    float kf[E], vf[E];
 #pragma unroll
-                    for (int e = 0; e < E; ++e) kf[e] = 0.f;
-                    if (pl < nsm) {
-#pragma unroll
-                        for (int e = 0; e < E; e += 2) {
-                            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(ks + (size_t)pl * D + lane * E + e));
-                            kf[e] = f.x; kf[e + 1] = f.y;
-                        }
-                    } else if (has_new && pl == nvalid - 1) {
-                        const __half2* kr = reinterpret_cast<const __half2*>(kg + ((size_t)j * p.kv_cap + pos) * D + lane * E);
-#pragma unroll
-                        for (int e = 0; e < E; e += 2) {
-                            const float2 f = __half22float2(__ldcg(kr + e / 2));
-                            kf[e] = f.x; kf[e + 1] = f.y;
-                        }
+                    for (int e = 0; e < E; e += 2) {
+                        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(ks + (size_t)pl * D + lane * E + e));
+                        const float2 g2 = __half22float2(*reinterpret_cast<const __half2*>(vs + (size_t)pl * D + lane * E + e));
+                        kf[e] = f.x; kf[e + 1] = f.y; vf[e] = g2.x; vf[e + 1] = g2.y;
                     }
+                    float sc[GM];
 #pragma unroll
                     for (int hh = 0; hh < GM; ++hh) {
                         float a = 0.f;
 #pragma unroll
-                        for (int e = 0; e < E; ++e) a = fmaf(qreg[hh][e], kf[e], a);
-                        sc[i][hh] = a;
+                        for (int e = 0; e < E; ++e) a = fmaf(qs[hh * D + lane * E + e], kf[e], a);
+                        sc[hh] = a;
+                    }
+#pragma unroll
+                    for (int sh = 16; sh > 0; sh >>= 1)
+#pragma unroll
+                        for (int hh = 0; hh < GM; ++hh) sc[hh] += __shfl_xor_sync(0xffffffffu, sc[hh], sh);
+#pragma unroll
+                    for (int hh = 0; hh < GM; ++hh) {
+                        const float sv = sc[hh] / p.sqrt_d;
+                        const float mn = fmaxf(hmx[hh], sv);
+                        const float cs = hmx[hh] == -INFINITY ? 0.f : expf(hmx[hh] - mn);
+                        const float pw = expf(sv - mn);
+                        hsum[hh] = fmaf(hsum[hh], cs, pw);
+#pragma unroll
+                        for (int e = 0; e < E; ++e) o[hh][e] = fmaf(o[hh][e], cs, pw * vf[e]);
+                        hmx[hh] = mn;
                     }
                 }
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-                    for (int i = 0; i < PPW; ++i)
-#pragma unroll
-                        for (int hh = 0; hh < GM; ++hh) sc[i][hh] += __shfl_xor_sync(0xffffffffu, sc[i][hh], o);
+                // release both stages (the owner's generic writes precede the next bulk copy into them)
+                __syncwarp();
                 if (lane == 0) {
-#pragma unroll
-                    for (int i = 0; i < PPW; ++i) {
-                        const int pl = warp + i * kLsWarps;
-#pragma unroll
-                        for (int hh = 0; hh < GM; ++hh) ss_att[hh * CP + pl] = pl < nvalid ? sc[i][hh] / p.sqrt_d : -INFINITY;
-                    }
+                    if (own_new) fence_proxy_async_smem();
+                    mbar_arrive(empty + slot);
+                    mbar_arrive(empty + slot_v);
                 }
-                stage_release();
-                ls_cbar();
-                // ---- softmax update per head (warp hh)
-                if (warp < gq) {
-                    const int hh = warp;
-                    float mx = -INFINITY;
-                    for (int pl = lane; pl < CP; pl += 32) mx = fmaxf(mx, ss_att[hh * CP + pl]);
-                    mx = warp_max(mx);
-                    const float m_old = hm[hh];
-                    const float m_new = fmaxf(m_old, mx);
-                    float sum = 0.f;
-                    for (int pl = lane; pl < CP; pl += 32) {
-                        const float e = pl < nvalid ? expf(ss_att[hh * CP + pl] - m_new) : 0.f;
-                        ss_att[hh * CP + pl] = e;
-                        sum += e;
-                    }
-                    sum = warp_sum(sum);
-                    if (lane == 0) {
-                        const float scl = m_old == -INFINITY ? 0.f : expf(m_old - m_new);
-                        hsc[hh] = scl;
-                        hl[hh] = hl[hh] * scl + sum;
-                        hm[hh] = m_new;
-                    }
-                }
-                ls_cbar();
-                // ---- V stage: o = o * rescale + sum_p w_p v_p, two head dims per thread
-                stage_wait();
-                const __half* vs = reinterpret_cast<const __half*>(ring + (size_t)slot * kLsStage);
-#pragma unroll
-                for (int k = 0; k < OP2; ++k) {
-                    const int i2 = ct + k * kLsWarps * 32;
-                    if (i2 < gq * D / 2) {
-                        const int hh = i2 / (D / 2), d = 2 * (i2 % (D / 2));
-                        const float* wv = ss_att + hh * CP;
-                        const float scl = hsc[hh];
-                        float ax = o_acc[k].x * scl, ay = o_acc[k].y * scl, bx = 0.f, by = 0.f;
-                        int pl = 0;
-                        for (; pl + 1 < nsm; pl += 2) {
-                            const float2 v0 = __half22float2(*reinterpret_cast<const __half2*>(vs + (size_t)pl * D + d));
-                            const float2 v1 = __half22float2(*reinterpret_cast<const __half2*>(vs + (size_t)(pl + 1) * D + d));
-                            ax = fmaf(wv[pl], v0.x, ax); ay = fmaf(wv[pl], v0.y, ay);
-                            bx = fmaf(wv[pl + 1], v1.x, bx); by = fmaf(wv[pl + 1], v1.y, by);
-                        }
-                        if (pl < nsm) {
-                            const float2 v0 = __half22float2(*reinterpret_cast<const __half2*>(vs + (size_t)pl * D + d));
-                            ax = fmaf(wv[pl], v0.x, ax); ay = fmaf(wv[pl], v0.y, ay);
-                        }
-                        if (has_new) {
-                            const float2 vv = __half22float2(
-                                __ldcg(reinterpret_cast<const __half2*>(vg + ((size_t)j * p.kv_cap + pos) * D + d)));
-                            ax = fmaf(wv[nvalid - 1], vv.x, ax); ay = fmaf(wv[nvalid - 1], vv.y, ay);
-                        }
-                        o_acc[k] = make_float2(ax + bx, ay + by);
-                    }
-                }
-                stage_release();
-                ls_cbar();
+                slot += 2;
+                if (slot >= NST) { slot -= NST; ++round; }
+
                 if (it == ihi - 1 || ch == nch - 1) {
-                    // end of this CTA's run over head j: partial (o, m, l) to scratch, then the ticket
-                    float* pp = p.apart + ((size_t)j * p.att_maxch + run_start) * (GM * (D + 2));
+                    // end of this CTA's run over head j: the warps' states into shared memory
 #pragma unroll
-                    for (int k = 0; k < OP2; ++k) {
-                        const int i2 = ct + k * kLsWarps * 32;
-                        if (i2 < gq * D / 2) reinterpret_cast<float2*>(pp)[i2] = o_acc[k];
+                    for (int hh = 0; hh < GM; ++hh) {
+                        float* st = comb + (warp * GM + hh) * (D + 2);
+#pragma unroll
+                        for (int e = 0; e < E; ++e) st[lane * E + e] = o[hh][e];
+                        if (lane == 0) { st[D] = hmx[hh]; st[D + 1] = hsum[hh]; }
                     }
-                    if (ct < gq) { pp[GM * D + ct] = hm[ct]; pp[GM * D + GM + ct] = hl[ct]; }
+                    ls_cbar();
+                    float* pp = p.apart + ((size_t)j * p.att_maxch + run_start) * (GM * (D + 2));
+                    if (warp < gq && lane < kLsWarps) {  // warp hh: the warps' merge weights
+                        const int hh = warp;
+                        const float m = comb[(lane * GM + hh) * (D + 2) + D];
+                        float M = m;
+#pragma unroll
+                        for (int sh = kLsWarps / 2; sh > 0; sh >>= 1) M = fmaxf(M, __shfl_xor_sync(0x0000ffffu, M, sh));
+                        const float e = m == -INFINITY ? 0.f : expf(m - M);
+                        float S = e * comb[(lane * GM + hh) * (D + 2) + D + 1];
+#pragma unroll
+                        for (int sh = kLsWarps / 2; sh > 0; sh >>= 1) S += __shfl_xor_sync(0x0000ffffu, S, sh);
+                        cw[lane * GM + hh] = e;
+                        if (lane == 0) { pp[GM * D + hh] = M; pp[GM * D + GM + hh] = S; }
+                    }
+                    ls_cbar();
+                    for (int i = ct; i < gq * D; i += kLsWarps * 32) {
+                        const int hh = i / D;
+                        float a = 0.f;
+#pragma unroll
+                        for (int w = 0; w < kLsWarps; ++w) a = fmaf(cw[w * GM + hh], comb[(w * GM + hh) * (D + 2) + (i % D)], a);
+                        pp[i] = a;
+                    }
                     ls_cbar();
                     const int jlo = j * nch, jhi = jlo + nch - 1;
                     const int cf = ls_owner(I, jlo, G), cl = ls_owner(I, jhi, G);
@@ -803,16 +782,37 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                         // per-run weights exp(m_r - M) / S of each head (warp hh, lanes over runs)
                         if (warp < gq) {
                             const int hh = warp;
+                            float mr[2], lr[2];
                             float M = -INFINITY;
-                            for (int r = lane; r < nruns; r += 32) {
-                                const int rs = max(jlo, ls_lo(I, cf + r, G)) - jlo;
-                                M = fmaxf(M, __ldcg(p.apart + ((size_t)j * p.att_maxch + rs) * (GM * (D + 2)) + GM * D + hh));
+#pragma unroll
+                            for (int k = 0; k < 2; ++k) {
+                                const int r = lane + 32 * k;
+                                mr[k] = -INFINITY; lr[k] = 0.f;
+                                if (r < nruns) {
+                                    const int rs = max(jlo, ls_lo(I, cf + r, G)) - jlo;
+                                    const float* q2 = p.apart + ((size_t)j * p.att_maxch + rs) * (GM * (D + 2));
+                                    mr[k] = __ldcg(q2 + GM * D + hh);
+                                    lr[k] = __ldcg(q2 + GM * D + GM + hh);
+                                }
+                                M = fmaxf(M, mr[k]);
                             }
+                            for (int r = lane + 64; r < nruns; r += 32)  // (more than 64 runs: rare)
+                                M = fmaxf(M, __ldcg(p.apart + ((size_t)j * p.att_maxch + max(jlo, ls_lo(I, cf + r, G)) - jlo) *
+                                                                   (GM * (D + 2)) + GM * D + hh));
                             M = warp_max(M);
                             float S = 0.f;
-                            for (int r = lane; r < nruns; r += 32) {
-                                const int rs = max(jlo, ls_lo(I, cf + r, G)) - jlo;
-                                const float* q2 = p.apart + ((size_t)j * p.att_maxch + rs) * (GM * (D + 2));
+#pragma unroll
+                            for (int k = 0; k < 2; ++k) {
+                                const int r = lane + 32 * k;
+                                if (r < nruns) {
+                                    const float e = expf(mr[k] - M);
+                                    wrun[r * GM + hh] = e;
+                                    S += lr[k] * e;
+                                }
+                            }
+                            for (int r = lane + 64; r < nruns; r += 32) {
+                                const float* q2 = p.apart + ((size_t)j * p.att_maxch + max(jlo, ls_lo(I, cf + r, G)) - jlo) *
+                                                                (GM * (D + 2));
                                 const float e = expf(__ldcg(q2 + GM * D + hh) - M);
                                 wrun[r * GM + hh] = e;
                                 S += __ldcg(q2 + GM * D + GM + hh) * e;
@@ -822,20 +822,25 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                             for (int r = lane; r < nruns; r += 32) wrun[r * GM + hh] *= is;
                         }
                         ls_cbar();
-                        float* obuf = qs;  // [GM][D] merged output
-                        for (int i2 = ct; i2 < gq * D / 2; i2 += kLsWarps * 32) {
-                            const int hh = i2 / (D / 2);
-                            float ax = 0.f, ay = 0.f;
-#pragma unroll 4
-                            for (int r = 0; r < nruns; ++r) {
-                                const int rs = max(jlo, ls_lo(I, cf + r, G)) - jlo;
-                                const float2 ov = __ldcg(reinterpret_cast<const float2*>(
-                                                             p.apart + ((size_t)j * p.att_maxch + rs) * (GM * (D + 2))) + i2);
-                                const float w = wrun[r * GM + hh];
-                                ax = fmaf(w, ov.x, ax); ay = fmaf(w, ov.y, ay);
+                        // merged output: the runs' partial outputs, loaded 16 at a time
+                        float* obuf = qs;  // [GM][D]
+                        for (int i = ct; i < gq * D; i += kLsWarps * 32) {
+                            const int hh = i / D;
+                            float a = 0.f;
+                            for (int r0 = 0; r0 < nruns; r0 += 16) {
+                                float ov[16];
+#pragma unroll
+                                for (int k = 0; k < 16; ++k) {
+                                    const int r = r0 + k;
+                                    ov[k] = r < nruns ? __ldcg(p.apart + ((size_t)j * p.att_maxch + max(jlo, ls_lo(I, cf + r, G)) - jlo) *
+                                                                             (GM * (D + 2)) + i)
+                                                      : 0.f;
+                                }
+#pragma unroll
+                                for (int k = 0; k < 16; ++k)
+                                    if (r0 + k < nruns) a = fmaf(wrun[(r0 + k) * GM + hh], ov[k], a);
                             }
-                            obuf[2 * i2] = ax;
-                            obuf[2 * i2 + 1] = ay;
+                            obuf[i] = a;
                         }
                         ls_cbar();
                         // attention output of heads j*gq .. j*gq+gq-1 and its records for O
@@ -861,11 +866,12 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
             const uint8_t* rsrc = kind == LS_O ? p.rec_attn : kind == LS_DN ? p.rec_act : p.rec_x;
             const unsigned long long tr0 = p.trace ? ls_now() : 0;
             load_records(rsrc, m.nb, norm, p.h / 16);
-            if (p.trace) tt_acc[3] += ls_now() - tr0;
+            if (p.trace && lane == 0) tt_acc[3] += (unsigned)(ls_now() - tr0);
         }
         ls_sync_all();  // the epilogue warps read 1/rms after this
         if (trace && ct == 0) trace[ph * 3 + 1] = ls_now();
-        const int lo = ls_lo((unsigned)m.nblk, c, G), hi = ls_lo((unsigned)m.nblk, c + 1, G);
+        int lo, hi;
+        ls_range(m, c, G, lo, hi);
         const int whi = lo + (hi - lo) * (warp + 1) / kLsWarps;
         int cur = lo + (hi - lo) * warp / kLsWarps;
         const uint32_t xlane = act_a + t * 32;  // this lane's 8-column group of each block record
@@ -879,7 +885,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                     const int wslot = wcons % kLsWRing;
                     const unsigned long long tw0 = p.trace ? ls_now() : 0;
                     if (!ls_mbar_wait_backoff(mybar + wslot, (uint32_t)(wcons / kLsWRing) & 1u, p.err, 64)) aborted = true;
-                    if (p.trace) tt_acc[0] += ls_now() - tw0;
+                    if (p.trace && lane == 0) tt_acc[0] += (unsigned)(ls_now() - tw0);
                     const uint32_t sq = smem_u32(myring + (size_t)wslot * WS);
                     const uint32_t ssc = sq + SB * QB;
                     const uint32_t xr = xlane + (uint32_t)k0 * kLsRec;
@@ -908,7 +914,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                 const uint32_t use = (uint32_t)(npiece / kLsPQ);
                 const unsigned long long tq0 = p.trace ? ls_now() : 0;
                 if (use > 0 && !ls_mbar_wait_backoff(pfree + qi, (use - 1) & 1u, p.err, 64)) aborted = true;
-                if (p.trace) tt_acc[1] += ls_now() - tq0;
+                if (p.trace && lane == 0) tt_acc[1] += (unsigned)(ls_now() - tq0);
                 if (t == 0) {
                     red[qi * 16 + g] = r0;
                     red[qi * 16 + g + 8] = r1;
@@ -921,8 +927,8 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
         arrive(ph);
     }
     if (p.trace) {
-        tt_acc[4] = ls_now() - tl0;
         if (lane == 0) {  // [CTA][warp][5]
+            tt_acc[4] = (unsigned)(ls_now() - tl0);
             unsigned long long* st = p.trace + (size_t)G * nph * 3 + ((size_t)c * kLsWarps + warp) * 5;
             for (int k = 0; k < 5; ++k) st[k] = tt_acc[k];
         }
