@@ -66,9 +66,13 @@ typedef struct laic_dev_desc {
 #define LAIC_FLAG_NO_GRAPH 1u   /* launch kernels one by one instead of replaying a CUDA graph */
 #define LAIC_FLAG_NO_PDL 2u     /* no programmatic dependent launch between kernels */
 #define LAIC_FLAG_KV_F32 4u     /* FP32 KV cache (the reference's precision) instead of FP16 */
-#define LAIC_FLAG_LAYER_LAUNCHES 8u /* one sequence of Q4_0/Q8_0 layers: launch each projection and attention
-                                      separately instead of the persistent decode-step kernel (comparisons) */
+#define LAIC_FLAG_LAYER_LAUNCHES 8u /* one sequence of Q4_0/Q8_0 layers: always launch each projection and
+                                      attention separately, never the persistent decode-step kernel */
 #define LAIC_FLAG_TRACE 16u     /* the persistent decode-step kernel stamps its phases (laic_dev_step_trace) */
+#define LAIC_FLAG_STEP_KERNEL 32u /* one sequence of Q4_0/Q8_0 layers: always the persistent decode-step kernel
+                                     where it applies. With neither this nor LAIC_FLAG_LAYER_LAUNCHES the engine
+                                     takes it for models whose layers stream at least 64 MB each (where it
+                                     measured faster than per-projection launches), else launches per layer */
 
 /* Device-side options (no counterpart in the reference, which is CPU-only). */
 typedef struct laic_dev_opts {
@@ -178,8 +182,10 @@ LAIC_API int laic_dev_profile(laic_dev* dev, int32_t nseq, const uint32_t* token
 
 /* Diagnostics of the persistent one-sequence decode-step kernel (engines created
  * with LAIC_FLAG_TRACE): the globaltimer stamps (ns) of its last launch,
- * out[(cta * phases + phase) * 3 + k] with k = 0 phase start, 1 inputs ready
- * (dependency met, activation records loaded), 2 phase done. Phases: 0 the
+ * out[(cta * phases + phase) * 5 + k] with k = 0 phase start, 1 inputs ready
+ * (dependency met, activation records loaded), 2 the CTA's first consumer warp
+ * done (attention: before the kv head's ticket), 3 every warp done (attention:
+ * after the ticket and any merge of the head), 4 phase done. Phases: 0 the
  * embedding, then per layer QKV, attention, O, gate/up, down, then the lm_head.
  * After those, per CTA and consumer warp 5 counters (ns): waits for a filled
  * ring stage, waits to queue a tile piece, waits for the epilogue warps at

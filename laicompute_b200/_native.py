@@ -12,7 +12,7 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libl
 
 LAIC_OK = 0
 LAIC_E_INVALID, LAIC_E_CUDA, LAIC_E_NCCL, LAIC_E_CONTEXT, LAIC_E_UNSUPPORTED, LAIC_E_MISSING = -1, -2, -3, -4, -5, -6
-FLAG_NO_GRAPH, FLAG_NO_PDL, FLAG_KV_F32, FLAG_LAYER_LAUNCHES, FLAG_TRACE = 1, 2, 4, 8, 16
+FLAG_NO_GRAPH, FLAG_NO_PDL, FLAG_KV_F32, FLAG_LAYER_LAUNCHES, FLAG_TRACE, FLAG_STEP_KERNEL = 1, 2, 4, 8, 16, 32
 
 # Every entry point include/laic_b200.h declares (checked by the tests).
 EXPORTS = (

@@ -467,7 +467,7 @@ struct laic_dev {
     size_t ls_done_bytes = 0;
     int ls_type = -1, ls_nst = 0, ls_maxch = 0, ls_runs = 0;
     size_t ls_smem_bytes = 0;
-    bool ls_ready = false, ls_checked = false, use_ls = true, ls_lm = false;
+    bool ls_ready = false, ls_checked = false, use_ls = true, force_ls = false, ls_lm = false;
     unsigned long long* ls_trace = nullptr;  // LAIC_FLAG_TRACE: per-phase stamps of the last step kernel
     bool trace_on = false;
     // more than 16 sequences on one GPU: binary16 hi/lo activation records written by the producing
@@ -853,6 +853,11 @@ struct laic_dev {
             if (!l.qkv.q || !l.o.q || !l.gu.q || !l.down.q || l.qkv.type != type || l.o.type != type ||
                 l.gu.type != type || l.down.type != type || !l.attn_norm || !l.ffn_norm)
                 return LAIC_OK;
+        // by default only for layers of at least 64 MB: below that, per-phase synchronisation costs more
+        // than the per-projection launches it replaces (measured on 1B- and 135M-shaped models)
+        const Layer& l0 = layers[0];
+        const size_t layer_bytes = l0.qkv.bytes() + l0.o.bytes() + l0.gu.bytes() + l0.down.bytes();
+        if (!force_ls && layer_bytes < ((size_t)64 << 20)) return LAIC_OK;
         const bool lm_in = lm_head().type == type;
         const int nb_max = std::max(std::max(h, hq), F) / 32;
         // the attention chunks of one kv head (at most cap / positions-per-chunk of them) span at
@@ -892,7 +897,8 @@ struct laic_dev {
         CK(cudaMalloc(&ls_done, ls_done_bytes));
         CK(cudaMalloc(&ls_epoch, 8));
         if (trace_on) {
-            const size_t tb = ((size_t)Gc * laic::ls_phases(L) * 3 + (size_t)Gc * laic::ls_trace_warp_words()) * 8;
+            const size_t tb = ((size_t)Gc * laic::ls_phases(L) * laic::ls_trace_stamps() +
+                               (size_t)Gc * laic::ls_trace_warp_words()) * 8;
             CK(cudaMalloc(&ls_trace, tb));
             CK(cudaMemset(ls_trace, 0, tb));
         }
@@ -1170,6 +1176,7 @@ int laic_dev_create(const laic_dev_desc* desc, const laic_dev_opts* opts, laic_d
     d->use_graph = !(o.flags & LAIC_FLAG_NO_GRAPH);
     d->use_pdl = !(o.flags & LAIC_FLAG_NO_PDL);
     d->use_ls = (o.flags & LAIC_FLAG_LAYER_LAUNCHES) == 0;
+    d->force_ls = (o.flags & LAIC_FLAG_STEP_KERNEL) != 0;
     d->trace_on = (o.flags & LAIC_FLAG_TRACE) != 0;
     d->layers.resize(a.layers);
     d->h_pos.assign(o.max_seqs, 0);
@@ -1679,7 +1686,8 @@ int laic_dev_step_trace(laic_dev* d, uint64_t* out, int64_t max_entries, int64_t
                                                "and run a one-sequence step on the persistent kernel");
     CK(cudaSetDevice(d->device));
     CK(cudaStreamSynchronize(d->st));
-    const int64_t total = (int64_t)num_sms() * laic::ls_phases(d->L) * 3 + (int64_t)num_sms() * laic::ls_trace_warp_words();
+    const int64_t total = (int64_t)num_sms() * laic::ls_phases(d->L) * laic::ls_trace_stamps() +
+                          (int64_t)num_sms() * laic::ls_trace_warp_words();
     *n = std::min(total, max_entries);
     *ctas = num_sms();
     *phases = laic::ls_phases(d->L);

@@ -72,6 +72,7 @@ struct LsParams;
 // setup with the resulting CTAs per SM (call before capture), and its launch (one CTA per SM).
 size_t ls_smem(int type, int stages, int D, int G, int nb_max, int att_runs);
 int ls_stage_bytes();
+int ls_trace_stamps();
 int ls_trace_warp_words();  // trace words per CTA after the phase stamps
 int ls_max_stages();
 int ls_positions_per_chunk(int D);

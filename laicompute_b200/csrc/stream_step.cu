@@ -35,7 +35,7 @@ size_t ls_smem(int type, int stages, int D, int G, int nb_max, int att_runs) {
     b += (size_t)(2 * kLsMaxStages + kLsWarps * kLsWRing + 2 + 2 * kLsWarps * kLsPQ) * 8;  // mbarriers
     b += (size_t)kLsWarps * kLsPQ * 16 * 4;                                 // tile pieces queues
     b += (size_t)GM * D * 4;                                                // attention: merged output
-    b += (size_t)att_runs * GM * 4;                                         // attention: merge weights
+    b += (size_t)att_runs * (GM + 1) * 4;                                   // attention: merge weights, run offsets
     b += 16 + 64 + kLsWarps * 5 * 4;                                        // alignment + broadcast words + trace counters
     // alignment + activation records, or the consumer warps' attention states and weights
     b += 128 + std::max(ls_rec_bytes(nb_max), (size_t)kLsWarps * GM * (D + 3) * 4);
@@ -44,6 +44,7 @@ size_t ls_smem(int type, int stages, int D, int G, int nb_max, int att_runs) {
 
 int ls_stage_bytes() { return kLsStage; }
 int ls_trace_warp_words() { return kLsWarps * 5; }
+int ls_trace_stamps() { return kLsStamps; }
 int ls_max_stages() { return kLsMaxStages; }
 int ls_positions_per_chunk(int D) { return ls_cp(D); }
 size_t ls_record_bytes(int nb) { return ls_rec_bytes(nb); }

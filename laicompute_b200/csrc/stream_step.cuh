@@ -67,6 +67,10 @@ constexpr int kLsPQ = 4;                             // tile pieces in flight fr
                                                      // epilogue warps (a multiple of kLsEpi)
 constexpr int kLsIssue = 8;                          // ring stages the producer warp's lanes issue together
 constexpr long long kLsSpin = 2000000000LL;          // clock cycles a dependency wait may take
+// Trace stamps per CTA and phase: [0] start, [1] inputs ready, [2] warp 0's own work done
+// (attention: before the head ticket), [3] every warp's work done (attention: after the
+// ticket and any head merge), [4] done (before the arrival).
+constexpr int kLsStamps = 5;
 
 // tile-blocks per weight stage of a consumer warp's ring (about 2.2 KB), and its bytes
 __host__ __device__ constexpr int ls_sb(int type) { return type == T_Q4_0 ? 8 : 4; }
@@ -117,8 +121,8 @@ struct LsParams {
     unsigned long long* epoch;            // launches completed
     int* err;
     int nstages;                          // ring depth
-    unsigned long long* trace;            // optional: [CTA][phase][3] globaltimer stamps (start, inputs ready, done),
-                                          // then [CTA][4] wait statistics (see ls_step_kernel)
+    unsigned long long* trace;            // optional: [CTA][phase][kLsStamps] globaltimer stamps, then
+                                          // [CTA][consumer warp][5] wait statistics (see ls_step_kernel)
 };
 
 __device__ __forceinline__ unsigned long long ls_now() {
@@ -230,11 +234,54 @@ __device__ __forceinline__ void ls_settle(const int* err) {
 // Named barrier of the consumer warps (the producer warp never joins it).
 __device__ __forceinline__ void ls_cbar() { named_sync(1, kLsWarps * 32); }
 
+// What a tile's epilogue reads from global memory besides its row sums, loaded by the
+// epilogue warp before it waits for the tile's pieces (the loads overlap the consumers'
+// work): per lane (row tile * 16 + lane) the residual and the next rmsnorm's weight (O,
+// DN), or the RoPE factors of the row (QKV).
+struct LsTilePre {
+    float x, w;
+    float2 cs;
+};
+// Per phase: the layer's pointers an epilogue needs (loaded once per phase).
+struct LsEpiPtrs {
+    const float* wn;   // O, DN: weights of the next rmsnorm
+    __half *kc, *vc;   // QKV: this layer's K and V caches
+};
+__device__ __forceinline__ LsEpiPtrs ls_epi_ptrs(const LsParams& p, int kind, int layer) {
+    LsEpiPtrs e{nullptr, nullptr, nullptr};
+    if (kind == LS_QKV) {
+        e.kc = reinterpret_cast<__half*>(p.layers[layer].kc);
+        e.vc = reinterpret_cast<__half*>(p.layers[layer].vc);
+    } else if (kind == LS_O) {
+        e.wn = p.layers[layer].ffn_norm;
+    } else if (kind == LS_DN) {
+        e.wn = layer + 1 < p.L ? p.layers[layer + 1].attn_norm : p.out_norm;
+    }
+    return e;
+}
+template <int D>
+__device__ __forceinline__ LsTilePre ls_tile_pre(const LsParams& p, int kind, const LsMat& m, const LsEpiPtrs& e, int tile,
+                                                 int pos, int lane) {
+    LsTilePre t{0.f, 0.f, make_float2(1.f, 0.f)};
+    const int r = tile * 16 + lane;
+    if (lane >= 16 || r >= m.rows) return t;
+    if (kind == LS_O || kind == LS_DN) {
+        t.x = __ldcg(p.x + r);
+        t.w = e.wn[r];
+    } else if (kind == LS_QKV) {
+        const int rr = r < p.hq ? r : r - p.hq;
+        const int d = rr % D;
+        if (r < p.hq + p.kv && d < 2 * p.rope_pairs) t.cs = p.rope_cs[(size_t)pos * p.rope_pairs + (d >> 1)];
+    }
+    return t;
+}
+
 // The epilogue of one finished row tile (an epilogue warp; lanes 0..15 hold the tile's
 // 16 row sums in v).
 template <int WT, int D>
-__device__ __forceinline__ void ls_finish_tile(const LsParams& p, int kind, int layer, const LsMat& m, int tile, float v,
-                                               float inv, bool norm, int pos, int sl, int lane) {
+__device__ __forceinline__ void ls_finish_tile(const LsParams& p, int kind, const LsMat& m, const LsEpiPtrs& e,
+                                               const LsTilePre& t, int tile, float v, float inv, bool norm, int pos,
+                                               int sl, int lane) {
     if (norm) v *= inv;
     const int r = tile * 16 + lane;  // this lane's row (lanes 0..15)
     const bool live = lane < 16 && r < m.rows;
@@ -248,15 +295,14 @@ __device__ __forceinline__ void ls_finish_tile(const LsParams& p, int kind, int 
             const int d = rr % D;
             float o = v;
             if (region < 2 && d < 2 * p.rope_pairs) {
-                const float2 cs = p.rope_cs[(size_t)pos * p.rope_pairs + (d >> 1)];
                 // adjacent-pair rotation, unfused like the reference
-                if ((d & 1) == 0) o = __fsub_rn(__fmul_rn(v, cs.x), __fmul_rn(other, cs.y));
-                else o = __fadd_rn(__fmul_rn(other, cs.y), __fmul_rn(v, cs.x));
+                if ((d & 1) == 0) o = __fsub_rn(__fmul_rn(v, t.cs.x), __fmul_rn(other, t.cs.y));
+                else o = __fadd_rn(__fmul_rn(other, t.cs.y), __fmul_rn(v, t.cs.x));
             }
             if (region == 0) {
                 p.q[rr] = o;
             } else {
-                __half* base = reinterpret_cast<__half*>(region == 1 ? p.layers[layer].kc : p.layers[layer].vc);
+                __half* base = region == 1 ? e.kc : e.vc;
                 base[(size_t)sl * p.kv_slot_stride + ((size_t)(rr / D) * p.kv_cap + pos) * D + d] = __float2half_rn(o);
             }
         }
@@ -274,12 +320,10 @@ __device__ __forceinline__ void ls_finish_tile(const LsParams& p, int kind, int 
         // rmsnorm weight), and the tile's sum of x^2
         float xn = 0.f;
         if (live) {
-            xn = __ldcg(p.x + r) + v;
+            xn = t.x + v;
             p.x[r] = xn;
         }
-        const float* wn = kind == LS_O ? p.layers[layer].ffn_norm
-                                       : (layer + 1 < p.L ? p.layers[layer + 1].attn_norm : p.out_norm);
-        const float sg = dp_lane_record<WT>(live ? xn * wn[r] : 0.f, xn * xn, lane & 7, live ? (r >> 3) : -1, p.rec_x,
+        const float sg = dp_lane_record<WT>(live ? xn * t.w : 0.f, xn * xn, lane & 7, live ? (r >> 3) : -1, p.rec_x,
                                             1, 2, 4);
         const float s8 = __shfl_sync(0xffffffffu, sg, 8);
         if (lane == 0) p.ss_x[tile] = sg + s8;
@@ -319,7 +363,8 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
     float* red = reinterpret_cast<float*>(pfree + kLsWarps * kLsPQ);  // [kLsWarps][kLsPQ][16] piece row sums
     float* qs = red + kLsWarps * kLsPQ * 16;                    // [GM][D] merged attention output
     float* wrun = qs + GM * D;                                  // [att_runs][GM] merge weights of the runs
-    int* ictl = reinterpret_cast<int*>((reinterpret_cast<uintptr_t>(wrun + p.att_runs * GM) + 15) & ~uintptr_t(15));
+    int* roff = reinterpret_cast<int*>(wrun + p.att_runs * GM);  // [att_runs] scratch offsets of the runs
+    int* ictl = reinterpret_cast<int*>((reinterpret_cast<uintptr_t>(roff + p.att_runs) + 15) & ~uintptr_t(15));
     // ictl: [16] broadcast words, then [kLsWarps][5] trace counters
     uint8_t* act = reinterpret_cast<uint8_t*>(ictl + 16 + kLsWarps * 5);  // activation records of the phase (attention:
                                                                 // the warps' softmax states of a run)
@@ -423,8 +468,8 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
             if (kind != LS_EMB && kind != LS_ATT) {
                 const LsMat m = ls_mat(p, kind, layer);
                 const bool norm = kind == LS_QKV || kind == LS_GU || kind == LS_LM;
-                const float inv = reinterpret_cast<const float*>(ictl)[5];
                 const int sl = ictl[2], pos = ictl[3];
+                const LsEpiPtrs ep = ls_epi_ptrs(p, kind, layer);
                 int lo, hi;
                 ls_range(m, c, G, lo, hi);
                 const unsigned n = (unsigned)(hi - lo);
@@ -441,6 +486,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                         const int wf = ls_warp_owner(n, (unsigned)(max(lo, tile * m.nb) - lo));
                         const int wt = ls_warp_owner(n, (unsigned)(min(hi, (tile + 1) * m.nb) - 1 - lo));
                         const int kme = wbase + tile - wtile;  // (lane w: warp w's piece number for this tile)
+                        const LsTilePre tp = ls_tile_pre<D>(p, kind, m, ep, tile, pos, lane);
                         float v = 0.f;
                         for (int w = wf; w <= wt; ++w) {
                             if (__shfl_sync(0xffffffffu, wcnt, w) == 0) continue;
@@ -451,7 +497,8 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                             __syncwarp();
                             if (lane == 0) mbar_arrive(pfree + qi);
                         }
-                        ls_finish_tile<WT, D>(p, kind, layer, m, tile, v, inv, norm, pos, sl, lane);
+                        const float inv = reinterpret_cast<const volatile float*>(ictl)[5];
+                        ls_finish_tile<WT, D>(p, kind, m, ep, tp, tile, v, inv, norm, pos, sl, lane);
                     }
                 }
                 wbase += wcnt;
@@ -557,9 +604,11 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
         for (int k = 0; k < 5; ++k) tt_acc[k] = 0u;
     auto arrive = [&](int ph) {
         const unsigned long long te0 = p.trace ? ls_now() : 0;
+        if (p.trace && ct == 0 && ls_kind(ph, L) != LS_ATT) p.trace[((size_t)c * nph + ph) * kLsStamps + 2] = te0;
         ls_sync_all();  // every consumer's and epilogue warp's writes of the phase precede the arrival
         if (p.trace && lane == 0) tt_acc[2] += (unsigned)(ls_now() - te0);
-        if (p.trace && ct == 0) p.trace[((size_t)c * nph + ph) * 3 + 2] = ls_now();
+        if (p.trace && ct == 0 && ls_kind(ph, L) != LS_ATT) p.trace[((size_t)c * nph + ph) * kLsStamps + 3] = ls_now();
+        if (p.trace && ct == 0) p.trace[((size_t)c * nph + ph) * kLsStamps + 4] = ls_now();
         if (ct == 0) {
             __threadfence();
             if (ph < nph - 1) {
@@ -593,17 +642,17 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
     if (ct < 8) ictl[8 + ct] = 0;
     ls_cbar();
 
-    unsigned long long* trace = p.trace ? p.trace + (size_t)c * nph * 3 : nullptr;
+    unsigned long long* trace = p.trace ? p.trace + (size_t)c * nph * kLsStamps : nullptr;
     const unsigned long long tl0 = p.trace ? ls_now() : 0;
     for (int ph = 0; ph < nph; ++ph) {
         const int kind = ls_kind(ph, L);
         const int layer = kind == LS_EMB ? 0 : kind == LS_LM ? L - 1 : (ph - 1) / 5;
-        if (trace && ct == 0) trace[ph * 3] = ls_now();
+        if (trace && ct == 0) trace[ph * kLsStamps] = ls_now();
         const unsigned long long tp0 = p.trace ? ls_now() : 0;
         if (ph > 0) wait_phase(ph - 1);
         if (p.trace && lane == 0) tt_acc[3] += (unsigned)(ls_now() - tp0);
         if (kind == LS_EMB || kind == LS_ATT) ls_sync_all();  // (the epilogue warps have nothing to do)
-        if (trace && ct == 0 && (kind == LS_EMB || kind == LS_ATT)) trace[ph * 3 + 1] = ls_now();
+        if (trace && ct == 0 && (kind == LS_EMB || kind == LS_ATT)) trace[ph * kLsStamps + 1] = ls_now();
 
         // ------------------------------------------------------------ EMB
         if (kind == LS_EMB) {
@@ -637,6 +686,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
             const int nch = (pos + 1 + CP - 1) / CP;
             const unsigned I = (unsigned)p.kv_heads * nch;
             const int ilo = ls_lo(I, c, G), ihi = ls_lo(I, c + 1, G);
+            if (ilo >= ihi && trace && ct == 0) trace[ph * kLsStamps + 2] = trace[ph * kLsStamps + 3] = ls_now();
             const __half* kg = reinterpret_cast<const __half*>(ly.kc) + (size_t)sl * p.kv_slot_stride;
             const __half* vg = reinterpret_cast<const __half*>(ly.vc) + (size_t)sl * p.kv_slot_stride;
             float* comb = reinterpret_cast<float*>(act);   // [kLsWarps][GM][D + 2] warp states of a run
@@ -769,6 +819,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                     const int jlo = j * nch, jhi = jlo + nch - 1;
                     const int cf = ls_owner(I, jlo, G), cl = ls_owner(I, jhi, G);
                     if (ct == 0) {
+                        if (trace) trace[ph * kLsStamps + 2] = ls_now();
                         const unsigned old = atom_add_acq_rel(p.head_tick + j, 1u);
                         ictl[1] = old == (unsigned)(cl - cf);
                     }
@@ -779,40 +830,19 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                             if (ct == 0) atomicExch(p.err, kErrDepCounter);
                             nruns = p.att_runs;
                         }
+                        // the runs' partials in the scratch (run r: CTA cf + r's first chunk of head j)
+                        for (int r = ct; r < nruns; r += kLsWarps * 32)
+                            roff[r] = (j * p.att_maxch + max(jlo, ls_lo(I, cf + r, G)) - jlo) * (GM * (D + 2));
+                        ls_cbar();
                         // per-run weights exp(m_r - M) / S of each head (warp hh, lanes over runs)
                         if (warp < gq) {
                             const int hh = warp;
-                            float mr[2], lr[2];
                             float M = -INFINITY;
-#pragma unroll
-                            for (int k = 0; k < 2; ++k) {
-                                const int r = lane + 32 * k;
-                                mr[k] = -INFINITY; lr[k] = 0.f;
-                                if (r < nruns) {
-                                    const int rs = max(jlo, ls_lo(I, cf + r, G)) - jlo;
-                                    const float* q2 = p.apart + ((size_t)j * p.att_maxch + rs) * (GM * (D + 2));
-                                    mr[k] = __ldcg(q2 + GM * D + hh);
-                                    lr[k] = __ldcg(q2 + GM * D + GM + hh);
-                                }
-                                M = fmaxf(M, mr[k]);
-                            }
-                            for (int r = lane + 64; r < nruns; r += 32)  // (more than 64 runs: rare)
-                                M = fmaxf(M, __ldcg(p.apart + ((size_t)j * p.att_maxch + max(jlo, ls_lo(I, cf + r, G)) - jlo) *
-                                                                   (GM * (D + 2)) + GM * D + hh));
+                            for (int r = lane; r < nruns; r += 32) M = fmaxf(M, __ldcg(p.apart + roff[r] + GM * D + hh));
                             M = warp_max(M);
                             float S = 0.f;
-#pragma unroll
-                            for (int k = 0; k < 2; ++k) {
-                                const int r = lane + 32 * k;
-                                if (r < nruns) {
-                                    const float e = expf(mr[k] - M);
-                                    wrun[r * GM + hh] = e;
-                                    S += lr[k] * e;
-                                }
-                            }
-                            for (int r = lane + 64; r < nruns; r += 32) {
-                                const float* q2 = p.apart + ((size_t)j * p.att_maxch + max(jlo, ls_lo(I, cf + r, G)) - jlo) *
-                                                                (GM * (D + 2));
+                            for (int r = lane; r < nruns; r += 32) {
+                                const float* q2 = p.apart + roff[r];
                                 const float e = expf(__ldcg(q2 + GM * D + hh) - M);
                                 wrun[r * GM + hh] = e;
                                 S += __ldcg(q2 + GM * D + GM + hh) * e;
@@ -830,12 +860,8 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                             for (int r0 = 0; r0 < nruns; r0 += 16) {
                                 float ov[16];
 #pragma unroll
-                                for (int k = 0; k < 16; ++k) {
-                                    const int r = r0 + k;
-                                    ov[k] = r < nruns ? __ldcg(p.apart + ((size_t)j * p.att_maxch + max(jlo, ls_lo(I, cf + r, G)) - jlo) *
-                                                                             (GM * (D + 2)) + i)
-                                                      : 0.f;
-                                }
+                                for (int k = 0; k < 16; ++k)
+                                    ov[k] = r0 + k < nruns ? __ldcg(p.apart + roff[r0 + k] + i) : 0.f;
 #pragma unroll
                                 for (int k = 0; k < 16; ++k)
                                     if (r0 + k < nruns) a = fmaf(wrun[(r0 + k) * GM + hh], ov[k], a);
@@ -853,6 +879,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                         if (ct == 0) p.head_tick[j] = 0u;
                         ls_cbar();
                     }
+                    if (trace && ct == 0) trace[ph * kLsStamps + 3] = ls_now();
                 }
             }
             arrive(ph);
@@ -869,7 +896,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
             if (p.trace && lane == 0) tt_acc[3] += (unsigned)(ls_now() - tr0);
         }
         ls_sync_all();  // the epilogue warps read 1/rms after this
-        if (trace && ct == 0) trace[ph * 3 + 1] = ls_now();
+        if (trace && ct == 0) trace[ph * kLsStamps + 1] = ls_now();
         int lo, hi;
         ls_range(m, c, G, lo, hi);
         const int whi = lo + (hi - lo) * (warp + 1) / kLsWarps;
@@ -929,7 +956,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
     if (p.trace) {
         if (lane == 0) {  // [CTA][warp][5]
             tt_acc[4] = (unsigned)(ls_now() - tl0);
-            unsigned long long* st = p.trace + (size_t)G * nph * 3 + ((size_t)c * kLsWarps + warp) * 5;
+            unsigned long long* st = p.trace + (size_t)G * nph * kLsStamps + ((size_t)c * kLsWarps + warp) * 5;
             for (int k = 0; k < 5; ++k) st[k] = tt_acc[k];
         }
     }

@@ -13,7 +13,7 @@ import numpy as np
 
 from . import gguf
 from ._native import (DevDesc, DevOpts, DevStats, FLAG_KV_F32, FLAG_NO_GRAPH, FLAG_NO_PDL, FLAG_LAYER_LAUNCHES, FLAG_TRACE,
-                      KernelRecord, SampleParams,
+                      FLAG_STEP_KERNEL, KernelRecord, SampleParams,
                       check, lib)
 
 
@@ -37,12 +37,18 @@ def desc_from_gguf(g: gguf.GgufFile) -> DevDesc:
 class Engine:
     def __init__(self, path: str, max_seqs: int = 1, kv_capacity: int = 0, device: int = 0, kv_f32: bool = False,
                  graphs: bool = True, pdl: bool = True, tp_size: int = 1, tp_rank: int = 0,
-                 nccl_id: Optional[bytes] = None, layer_launches: bool = False, trace: bool = False) -> None:
+                 nccl_id: Optional[bytes] = None, layer_launches: bool = False, trace: bool = False,
+                 step_kernel: Optional[bool] = None) -> None:
+        """`step_kernel`: True always runs one-sequence Q4_0/Q8_0 steps as the persistent decode-step kernel,
+        False (or `layer_launches`) never does, None lets the engine choose by layer size."""
         L = lib()
+        if step_kernel is False:
+            layer_launches = True
         self.file = gguf.GgufFile(path)
         self.desc = desc_from_gguf(self.file)
         flags = ((FLAG_KV_F32 if kv_f32 else 0) | (0 if graphs else FLAG_NO_GRAPH) | (0 if pdl else FLAG_NO_PDL)
-                 | (FLAG_LAYER_LAUNCHES if layer_launches else 0) | (FLAG_TRACE if trace else 0))
+                 | (FLAG_LAYER_LAUNCHES if layer_launches else 0) | (FLAG_TRACE if trace else 0)
+                 | (FLAG_STEP_KERNEL if step_kernel else 0))
         self._nccl_id = ctypes.create_string_buffer(nccl_id, 128) if nccl_id else None
         opts = DevOpts(device=device, max_seqs=max_seqs, kv_capacity=kv_capacity, tp_size=tp_size, tp_rank=tp_rank,
                        nccl_id=ctypes.cast(self._nccl_id, ctypes.c_void_p) if self._nccl_id else None, flags=flags)
@@ -140,15 +146,16 @@ class Engine:
         return out, ms.value
 
     def step_trace(self) -> np.ndarray:
-        """[CTA][phase][3] globaltimer stamps (ns) of the last persistent step kernel (engines with trace=True)."""
-        cap = 200 * 8192 * 3
+        """[CTA][phase][5] globaltimer stamps (ns) of the last persistent step kernel (engines with trace=True):
+        start, inputs ready, first warp done, all warps done, done."""
+        cap = 200 * 8192 * 5
         out = np.zeros(cap, dtype=np.uint64)
         n, ctas, phases = ctypes.c_int64(), ctypes.c_int32(), ctypes.c_int32()
         check(lib().laic_dev_step_trace(self.h, out.ctypes.data, cap, ctypes.byref(n), ctypes.byref(ctas),
                                         ctypes.byref(phases)))
-        stamps = ctas.value * phases.value * 3
+        stamps = ctas.value * phases.value * 5
         self.last_wait_stats = out[stamps: n.value].reshape(ctas.value, -1, 5)
-        return out[:stamps].reshape(ctas.value, phases.value, 3)
+        return out[:stamps].reshape(ctas.value, phases.value, 5)
 
     def profile(self, tokens: np.ndarray, steps: int) -> dict:
         """Per-kernel-family {name: (launches, total_us, bytes)} over `steps` eager full steps of slots 0..n-1."""

@@ -47,8 +47,21 @@ def _slice_model(slice_dir, arch, seed):
     return path
 
 
+# both one-sequence decode paths: per-projection launches, and the persistent decode-step kernel
+PATHS = {"layers": dict(step_kernel=False), "step": dict(step_kernel=True)}
+_oracle_runs = {}
+
+
+def _oracle_generate(path, prompt, steps):
+    key = (path, steps)
+    if key not in _oracle_runs:
+        _oracle_runs[key] = O.OracleModel(path).generate(prompt, steps)
+    return _oracle_runs[key]
+
+
 @pytest.mark.parametrize("which", ["llama8b", "llama1b"])
-def test_large_layer_slice_matches_oracle(slice_dir, which):
+@pytest.mark.parametrize("dpath", sorted(PATHS))
+def test_large_layer_slice_matches_oracle(slice_dir, which, dpath):
     """Two layers of the 8B (or 1B) shape, one sequence: the benchmark's batch-1 path."""
     from laicompute_b200.engine import Engine
     base = synth.LLAMA_8B_Q4 if which == "llama8b" else synth.LLAMA_1B_Q4
@@ -56,8 +69,8 @@ def test_large_layer_slice_matches_oracle(slice_dir, which):
     path = _slice_model(slice_dir, arch, seed=51 if which == "llama8b" else 52)
     prompt = synth.prompt_ids(arch.vocab, 6, seed=53)
     steps = 8
-    ref_ids, ref_logits = O.OracleModel(path).generate(prompt, steps)
-    e = Engine(path, kv_capacity=8192)
+    ref_ids, ref_logits = _oracle_generate(path, prompt, steps)
+    e = Engine(path, kv_capacity=8192, **PATHS[dpath])
     ids, logits = e.generate(prompt, steps, want_logits=True)
     e.close()
     err = _rel_err(logits, ref_logits)
@@ -66,20 +79,25 @@ def test_large_layer_slice_matches_oracle(slice_dir, which):
 
 
 @pytest.mark.parametrize("ctx,head_dim", [(4096, 128), (8192, 128), (4096, 64), (8192, 64)])
-def test_attention_at_benchmark_contexts(slice_dir, ctx, head_dim):
+@pytest.mark.parametrize("dpath", sorted(PATHS))
+def test_attention_at_benchmark_contexts(slice_dir, ctx, head_dim, dpath):
     """A one-layer model with 4 query heads per KV head whose prompt fills the KV cache to
-    `ctx` - 2 positions; the last decode steps attend over ~ctx positions in 8 splits."""
+    `ctx` - 2 positions; the last decode steps attend over ~ctx positions (per-projection
+    launches: in 8 splits merged inside a thread-block cluster; the step kernel: spread over
+    every SM, up to 256 chunks of 32 positions)."""
     from laicompute_b200.engine import Engine
     heads, kv_heads = (4, 1) if head_dim == 128 else (8, 2)
     arch = synth.tiny_arch(gguf.Q4_0, gguf.F16, hidden=heads * head_dim, layers=1, heads=heads, kv_heads=kv_heads,
                            ffn=128, vocab=256, ctx=ctx, rope_theta=500000.0, name=f"attn{ctx}_{head_dim}")
     path = os.path.join(slice_dir, arch.name + ".gguf")
-    synth.write_model(path, arch, seed=61)
+    if not os.path.exists(path):
+        synth.write_model(path, arch, seed=61)
     prompt = synth.prompt_ids(arch.vocab, ctx - 2, seed=62)
-    ref_ids, ref_logits = O.OracleModel(path).generate(prompt, 3)
-    e = Engine(path, kv_capacity=ctx)
+    ref_ids, ref_logits = _oracle_generate(path, prompt, 3)
+    e = Engine(path, kv_capacity=ctx, **PATHS[dpath])
     ids, logits = e.generate(prompt, 3, want_logits=True)
-    assert e.stats().attn_splits >= 2  # the splits merge inside a thread-block cluster
+    if dpath == "layers":
+        assert e.stats().attn_splits >= 2  # the splits merge inside a thread-block cluster
     e.close()
     err = _rel_err(logits, ref_logits)
     assert err.max() <= LOGIT_RTOL, err

@@ -40,7 +40,7 @@ def test_step_kernel_matches_oracle_and_layer_path(arch):
         path = synth.write_model(os.path.join(d, "m.gguf"), a, seed=51, direct_blocks=a.vocab > 65536)
         prompt = synth.prompt_ids(a.vocab, 300, seed=52)
         ref_ids, ref_logits = O.OracleModel(path).generate(prompt, 16)
-        e = Engine(path, kv_capacity=1024)
+        e = Engine(path, kv_capacity=1024, step_kernel=True)
         ids, logits = e.generate(prompt, 16, want_logits=True)
         stats = e.stats()
         e.close()
@@ -56,3 +56,25 @@ def test_step_kernel_matches_oracle_and_layer_path(arch):
     # same integer dot products, different split of the work: FP32-rounding level apart
     d2 = np.abs(logits - logits2).max(axis=1) / np.abs(logits2).max(axis=1)
     assert d2.max() <= 1e-4, d2.max()
+
+
+def test_step_trace_stamps_every_phase():
+    """The persistent kernel's trace (LAIC_FLAG_TRACE): per CTA and phase five ordered stamps
+    (start <= inputs ready <= first warp done <= all warps done <= done), phases in step order."""
+    from laicompute_b200.engine import Engine
+    a = ARCHS["q4_d128_g4"]
+    with tempfile.TemporaryDirectory() as d:
+        path = synth.write_model(os.path.join(d, "m.gguf"), a, seed=51)
+        prompt = synth.prompt_ids(a.vocab, 40, seed=52)
+        e = Engine(path, kv_capacity=1024, step_kernel=True, trace=True)
+        e.prefill_batch(prompt[:-1], 0)
+        e.step([int(prompt[-1])], [0])
+        tr = e.step_trace().astype(np.int64)
+        waits = e.last_wait_stats
+        e.close()
+    ctas, phases, k = tr.shape
+    assert k == 5 and phases == 2 + 5 * a.layers and ctas >= 1
+    assert (tr > 0).all()
+    assert (np.diff(tr, axis=2) >= 0).all()              # within a phase
+    assert (tr[:, 1:, 0] >= tr[:, :-1, 4]).all()          # a phase starts after the previous one is done
+    assert waits.shape == (ctas, 16, 5) and (waits[:, :, 4] > 0).all()
