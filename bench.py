@@ -274,7 +274,8 @@ def run_decode(name: str, args, world: int, rank: int, local: int, batch: int, s
     seq_rank = 0 if tp > 1 else rank  # tensor-parallel ranks decode the same sequences
     ctx_need = plen + 2 * args.warmup + 2 * args.steps + 64  # decode, e2e and profiling steps
     ctx_need = max(ctx_need, KV_CAPACITY.get(name, 0))
-    eng = Engine(path, max_seqs=batch, device=local, kv_capacity=ctx_need, layer_launches=args.layer_launches, **tp_kw)
+    eng = Engine(path, max_seqs=batch, device=local, kv_capacity=ctx_need, layer_launches=args.layer_launches,
+                 step_kernel=True if args.step_kernel else None, **tp_kw)
     slots = np.arange(batch, dtype=np.int32)
     prompts = np.stack([synth.prompt_ids(arch.vocab, plen, seed=seed + 100 + 1000 * seq_rank + i)
                         for i in range(batch)])
@@ -432,7 +433,10 @@ def main() -> None:
     ap.add_argument("--no-llama8b", action="store_true", help="skip the 8B batch-1 tensor-parallel measurement")
     ap.add_argument("--no-sweep", action="store_true", help="skip the Q4_0 matvec sweep")
     ap.add_argument("--layer-launches", action="store_true",
-                    help="one sequence: per-layer launches instead of the persistent decode-step kernel")
+                    help="one sequence: always per-layer launches, never the persistent decode-step kernel")
+    ap.add_argument("--step-kernel", action="store_true",
+                    help="one sequence: always the persistent decode-step kernel (default: the engine's choice "
+                         "by layer size)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
