@@ -69,10 +69,9 @@ typedef struct laic_dev_desc {
 #define LAIC_FLAG_LAYER_LAUNCHES 8u /* one sequence of Q4_0/Q8_0 layers: always launch each projection and
                                       attention separately, never the persistent decode-step kernel */
 #define LAIC_FLAG_TRACE 16u     /* the persistent decode-step kernel stamps its phases (laic_dev_step_trace) */
-#define LAIC_FLAG_STEP_KERNEL 32u /* one sequence of Q4_0/Q8_0 layers: always the persistent decode-step kernel
-                                     where it applies. With neither this nor LAIC_FLAG_LAYER_LAUNCHES the engine
-                                     takes it for models whose layers stream at least 64 MB each (where it
-                                     measured faster than per-projection launches), else launches per layer */
+#define LAIC_FLAG_STEP_KERNEL 32u /* one sequence of Q4_0/Q8_0 layers: run each step as the persistent
+                                     decode-step kernel where it applies (off by default: per-projection launches
+                                     measured faster) */
 
 /* Device-side options (no counterpart in the reference, which is CPU-only). */
 typedef struct laic_dev_opts {

@@ -853,11 +853,9 @@ struct laic_dev {
             if (!l.qkv.q || !l.o.q || !l.gu.q || !l.down.q || l.qkv.type != type || l.o.type != type ||
                 l.gu.type != type || l.down.type != type || !l.attn_norm || !l.ffn_norm)
                 return LAIC_OK;
-        // by default only for layers of at least 64 MB: below that, per-phase synchronisation costs more
-        // than the per-projection launches it replaces (measured on 1B- and 135M-shaped models)
-        const Layer& l0 = layers[0];
-        const size_t layer_bytes = l0.qkv.bytes() + l0.o.bytes() + l0.gu.bytes() + l0.down.bytes();
-        if (!force_ls && layer_bytes < ((size_t)64 << 20)) return LAIC_OK;
+        // only on request: per-projection launches measured faster on the 135M-, 1B- and 8B-shaped
+        // models (per-phase synchronisation of the one-launch step costs more)
+        if (!force_ls) return LAIC_OK;
         const bool lm_in = lm_head().type == type;
         const int nb_max = std::max(std::max(h, hq), F) / 32;
         // the attention chunks of one kv head (at most cap / positions-per-chunk of them) span at

@@ -234,6 +234,52 @@ __device__ __forceinline__ void ls_settle(const int* err) {
 // Named barrier of the consumer warps (the producer warp never joins it).
 __device__ __forceinline__ void ls_cbar() { named_sync(1, kLsWarps * 32); }
 
+// One 16x32 tile-block of the integer dot products with four rows per lane: lane (u, t)
+// of a half warp does the work of tile_block_dp's layout lanes 8u + t and 8u + 4 + t
+// (rows 2u, 2u+8, 2u+1, 2u+9; column group t), so a block's activation record reaches 16
+// lanes rather than 32 and the shared-memory delivery per block drops from ~1.4 KB to
+// ~0.9 KB (the crossbar delivers 128 B per clock; it bounds this loop). acc[] holds the
+// four rows in that order; the products, their order and the FP32 steps per (row, group)
+// are tile_block_dp's.
+template <int WT>
+__device__ __forceinline__ void ls_block_dp4(uint32_t q, uint32_t sc, uint32_t xrec, int u, int t, float (&acc)[4]) {
+    const uint4 xa = lds128(xrec + t * 32), xb = lds128(xrec + t * 32 + 16);
+    const int x8 = (int)xb.z;
+    const float sinv = __uint_as_float(xb.w);
+    const uint2 dp = lds64(sc + u * 8);  // halves of rows (2u, 2u+8) and (2u+1, 2u+9)
+    const float2 d0 = __half22float2(*reinterpret_cast<const __half2*>(&dp.x));
+    const float2 d1 = __half22float2(*reinterpret_cast<const __half2*>(&dp.y));
+    const float dr[4] = {d0.x, d0.y, d1.x, d1.y};
+    uint32_t wl[4], wh[4];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int l = 8 * u + 4 * h + t;  // the layout lane whose rows these are
+        if (WT == T_Q4_0) {
+            const uint2 w = lds64(q + l * 8);
+            wl[2 * h] = w.x & 0x0F0F0F0Fu; wh[2 * h] = (w.x >> 4) & 0x0F0F0F0Fu;
+            wl[2 * h + 1] = w.y & 0x0F0F0F0Fu; wh[2 * h + 1] = (w.y >> 4) & 0x0F0F0F0Fu;
+        } else {
+            const uint4 w = lds128(q + l * 16);
+            wl[2 * h] = w.x; wh[2 * h] = w.y; wl[2 * h + 1] = w.z; wh[2 * h + 1] = w.w;
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        int s0, s1, s2;
+        if (WT == T_Q4_0) {
+            s2 = dp4a_us(wh[r], xb.y, dp4a_us(wl[r], xb.x, x8));
+            s1 = dp4a_us(wh[r], xa.w, dp4a_us(wl[r], xa.z, 0));
+            s0 = dp4a_us(wh[r], xa.y, dp4a_us(wl[r], xa.x, 0));
+        } else {
+            s2 = dp4a_ss(wh[r], xb.y, dp4a_ss(wl[r], xb.x, 0));
+            s1 = dp4a_ss(wh[r], xa.w, dp4a_ss(wl[r], xa.z, 0));
+            s0 = dp4a_ss(wh[r], xa.y, dp4a_ss(wl[r], xa.x, 0));
+        }
+        const int v = s0 * 16384 + s1 * 128 + s2;
+        acc[r] = fmaf((float)v, dr[r] * sinv, acc[r]);
+    }
+}
+
 // What a tile's epilogue reads from global memory besides its row sums, loaded by the
 // epilogue warp before it waits for the tile's pieces (the loads overlap the consumers'
 // work): per lane (row tile * 16 + lane) the residual and the next rmsnorm's weight (O,
@@ -513,7 +559,6 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
     // consumer warps
     // =====================================================================
     const int ct = threadIdx.x;           // 0 .. kLsWarps * 32 - 1
-    const int g = lane >> 2, t = lane & 3;
     const int gq = p.gq;
 
     // ---- this warp's weight stream: its contiguous share of the CTA's tile-blocks in every
@@ -901,11 +946,11 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
         ls_range(m, c, G, lo, hi);
         const int whi = lo + (hi - lo) * (warp + 1) / kLsWarps;
         int cur = lo + (hi - lo) * warp / kLsWarps;
-        const uint32_t xlane = act_a + t * 32;  // this lane's 8-column group of each block record
+        const int hb = lane >> 4, hu = (lane >> 2) & 3, ht = lane & 3;  // block half, row quad, column group
         if (cur < whi) {  // one piece per row tile this warp's share touches
             for (int tile = cur / m.nb, tlast = (whi - 1) / m.nb; tile <= tlast; ++tile) {
                 const int t_end = min(hi, (tile + 1) * m.nb);
-                float dacc[2] = {0.f, 0.f};
+                float dacc[4] = {0.f, 0.f, 0.f, 0.f};  // rows 2u, 2u+8, 2u+1, 2u+9 (u = hu)
                 while (cur < whi && cur < t_end) {  // this warp's stages inside the tile
                     const int k0 = cur - tile * m.nb;
                     const int n = min(min(SB, m.nb - k0), whi - cur);
@@ -915,14 +960,20 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                     if (p.trace && lane == 0) tt_acc[0] += (unsigned)(ls_now() - tw0);
                     const uint32_t sq = smem_u32(myring + (size_t)wslot * WS);
                     const uint32_t ssc = sq + SB * QB;
-                    const uint32_t xr = xlane + (uint32_t)k0 * kLsRec;
+                    const uint32_t xr = act_a + (uint32_t)k0 * kLsRec;
+                    // the two half warps take alternate blocks of the stage
                     if (n == SB) {
 #pragma unroll
-                        for (int jb = 0; jb < SB; ++jb)
-                            tile_block_dp<WT>(sq + jb * QB, ssc + jb * kTileSBytes, xr + jb * kLsRec, lane, dacc);
+                        for (int jb = 0; jb < SB; jb += 2) {
+                            const int j = jb + hb;
+                            ls_block_dp4<WT>(sq + j * QB, ssc + j * kTileSBytes, xr + j * kLsRec, hu, ht, dacc);
+                        }
                     } else {
-                        for (int jb = 0; jb < n; ++jb)
-                            tile_block_dp<WT>(sq + jb * QB, ssc + jb * kTileSBytes, xr + jb * kLsRec, lane, dacc);
+                        for (int jb = 0; jb < n; jb += 2) {
+                            const int j = jb + hb;
+                            if (j < n)
+                                ls_block_dp4<WT>(sq + j * QB, ssc + j * kTileSBytes, xr + j * kLsRec, hu, ht, dacc);
+                        }
                     }
                     __syncwarp();
                     ++wcons;
@@ -930,21 +981,25 @@ __global__ void __launch_bounds__(kLsThreads, 1) ls_step_kernel(const LsParams p
                     wissue_one();
                     cur += n;
                 }
-                // ---- this warp's piece of the tile into its queue: the four lanes of a row hold
-                //      its four 8-column groups
-                float r0 = dacc[0], r1 = dacc[1];
-                r0 += __shfl_xor_sync(0xffffffffu, r0, 1);
-                r1 += __shfl_xor_sync(0xffffffffu, r1, 1);
-                r0 += __shfl_xor_sync(0xffffffffu, r0, 2);
-                r1 += __shfl_xor_sync(0xffffffffu, r1, 2);
+                // ---- this warp's piece of the tile into its queue: a row's sums are spread over
+                //      its four column-group lanes and the two half warps
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    dacc[r] += __shfl_xor_sync(0xffffffffu, dacc[r], 1);
+                    dacc[r] += __shfl_xor_sync(0xffffffffu, dacc[r], 2);
+                    dacc[r] += __shfl_xor_sync(0xffffffffu, dacc[r], 16);
+                }
                 const int qi = warp * kLsPQ + npiece % kLsPQ;
                 const uint32_t use = (uint32_t)(npiece / kLsPQ);
                 const unsigned long long tq0 = p.trace ? ls_now() : 0;
                 if (use > 0 && !ls_mbar_wait_backoff(pfree + qi, (use - 1) & 1u, p.err, 64)) aborted = true;
                 if (p.trace && lane == 0) tt_acc[1] += (unsigned)(ls_now() - tq0);
-                if (t == 0) {
-                    red[qi * 16 + g] = r0;
-                    red[qi * 16 + g + 8] = r1;
+                if (lane < 16 && ht == 0) {
+                    float* rp = red + qi * 16 + 2 * hu;
+                    rp[0] = dacc[0];
+                    rp[8] = dacc[1];
+                    rp[1] = dacc[2];
+                    rp[9] = dacc[3];
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(pfull + qi);

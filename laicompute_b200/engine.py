@@ -39,8 +39,8 @@ class Engine:
                  graphs: bool = True, pdl: bool = True, tp_size: int = 1, tp_rank: int = 0,
                  nccl_id: Optional[bytes] = None, layer_launches: bool = False, trace: bool = False,
                  step_kernel: Optional[bool] = None) -> None:
-        """`step_kernel`: True always runs one-sequence Q4_0/Q8_0 steps as the persistent decode-step kernel,
-        False (or `layer_launches`) never does, None lets the engine choose by layer size."""
+        """`step_kernel`: True runs one-sequence Q4_0/Q8_0 steps as the persistent decode-step kernel, False
+        (or `layer_launches`) and None (the default) launch per projection."""
         L = lib()
         if step_kernel is False:
             layer_launches = True
