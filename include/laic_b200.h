@@ -69,6 +69,8 @@ typedef struct laic_dev_desc {
 #define LAIC_FLAG_LAYER_LAUNCHES 8u /* one sequence of Q4_0/Q8_0 layers: always launch each projection and
                                       attention separately, never the persistent decode-step kernel */
 #define LAIC_FLAG_TRACE 16u     /* the persistent decode-step kernel stamps its phases (laic_dev_step_trace) */
+#define LAIC_FLAG_Q4_0_UPSTREAM 128u /* Q4_0 tensors arrive in upstream ggml's nibble order (elements j and
+                                        j+16 share byte j); they are reordered to the reference's at upload */
 #define LAIC_FLAG_STEP_KERNEL 32u /* one sequence of Q4_0/Q8_0 layers: run each step as the persistent
                                      decode-step kernel where it applies (off by default: per-projection launches
                                      measured faster) */
@@ -192,6 +194,19 @@ LAIC_API int laic_dev_profile(laic_dev* dev, int32_t nseq, const uint32_t* token
  * No counterpart in the reference. */
 LAIC_API int laic_dev_step_trace(laic_dev* dev, uint64_t* out, int64_t max_entries, int64_t* n, int32_t* ctas,
                                  int32_t* phases);
+
+/* Host-only conversion of `n` elements of GGML blocks into the block type the
+ * device holds for them (what laic_dev_upload and laic_tensor_create do before
+ * the tile repack): Q5_0 becomes Q8_0 with the same scales and int8 values
+ * v - 16 (identical values: quant_v2::value, reference src/quant_v2.cpp:12,
+ * forms d * (v - 16)); Q4_0 with LAIC_FLAG_Q4_0_UPSTREAM in `flags` is
+ * reordered from upstream ggml's nibble order to the reference's
+ * (src/quant_v2.cpp:10); F32 / F16 / Q8_0 / Q4_0 are copied. *out_type and
+ * *dst_bytes receive the result's type and size; dst == NULL only queries
+ * them. Q4_1, Q5_1 and the K-quants are not held on the device
+ * (LAIC_E_UNSUPPORTED). No counterpart in the reference. */
+LAIC_API int laic_blocks_convert(int32_t ggml_type, const void* src, uint64_t n, uint32_t flags, int32_t* out_type,
+                                 void* dst, uint64_t dst_cap, uint64_t* dst_bytes);
 
 /* 128-byte NCCL unique id for laic_dev_opts.nccl_id (rank 0 creates, all ranks share). */
 LAIC_API int laic_nccl_unique_id(void* out128);

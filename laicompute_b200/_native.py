@@ -13,6 +13,7 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libl
 LAIC_OK = 0
 LAIC_E_INVALID, LAIC_E_CUDA, LAIC_E_NCCL, LAIC_E_CONTEXT, LAIC_E_UNSUPPORTED, LAIC_E_MISSING = -1, -2, -3, -4, -5, -6
 FLAG_NO_GRAPH, FLAG_NO_PDL, FLAG_KV_F32, FLAG_LAYER_LAUNCHES, FLAG_TRACE, FLAG_STEP_KERNEL = 1, 2, 4, 8, 16, 32
+FLAG_Q4_0_UPSTREAM = 128
 
 # Every entry point include/laic_b200.h declares (checked by the tests).
 EXPORTS = (
@@ -21,7 +22,7 @@ EXPORTS = (
     "laic_dev_stream", "laic_dev_decode", "laic_dev_profile", "laic_nccl_unique_id", "laic_tensor_create", "laic_tensor_destroy",
     "laic_tensor_matvec", "laic_tensor_dequant", "laic_tensor_bytes", "laic_tensor_matvec_noalloc",
     "laic_dev_prefill_batch", "laic_tensor_check", "laic_selftest_peer_timeout",
-    "laic_dev_step_trace",
+    "laic_dev_step_trace", "laic_blocks_convert",
 )
 
 
@@ -104,11 +105,12 @@ def lib() -> ctypes.CDLL:
     L.laic_dev_step_trace.argtypes = [P, P, ctypes.c_int64, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(I32),
                                       ctypes.POINTER(I32)]
     L.laic_selftest_peer_timeout.argtypes = [I32, ctypes.c_int64, ctypes.POINTER(I32)]
+    L.laic_blocks_convert.argtypes = [I32, P, U64, ctypes.c_uint32, ctypes.POINTER(I32), P, U64, ctypes.POINTER(U64)]
     for name in ("laic_dev_create", "laic_dev_upload", "laic_dev_prefill", "laic_dev_step", "laic_dev_reset_slot",
                  "laic_dev_slot_pos", "laic_dev_fill_kv", "laic_dev_sync", "laic_dev_stats_get",
                  "laic_dev_decode", "laic_dev_profile", "laic_nccl_unique_id", "laic_tensor_create", "laic_tensor_matvec",
                  "laic_tensor_dequant", "laic_tensor_matvec_noalloc", "laic_dev_prefill_batch", "laic_tensor_check",
-                 "laic_selftest_peer_timeout", "laic_dev_step_trace"):
+                 "laic_selftest_peer_timeout", "laic_dev_step_trace", "laic_blocks_convert"):
         getattr(L, name).restype = I32
     _lib = L
     return L

@@ -11,6 +11,8 @@
 namespace laic {
 
 enum : int { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q8_0 = 8 };
+// GGML block types accepted at upload and held on the device as one of the above
+enum : int { T_Q5_0 = 6 };
 
 constexpr int kWarp = 32;
 

@@ -68,6 +68,7 @@ using laic::T_F16;
 using laic::T_F32;
 using laic::T_Q4_0;
 using laic::T_Q8_0;
+using laic::T_Q5_0;
 
 size_t elem_bytes(int type, size_t n) {
     switch (type) {
@@ -75,8 +76,55 @@ size_t elem_bytes(int type, size_t n) {
     case T_F16: return n * 2;
     case T_Q4_0: return n / 32 * 18;
     case T_Q8_0: return n / 32 * 34;
+    case T_Q5_0: return n / 32 * 22;
     }
     return 0;
+}
+
+// Blocks of a type the device holds as another type with identical values (the reference's
+// decode, src/quant_v2.cpp:10 and :12), converted on the host before the tile repack:
+//  * Q5_0 (d, 32-bit high bits qh, 16 nibble bytes; element o = d * (v - 16) with v the nibble
+//    of byte o/2, low for even o, plus bit o of qh as bit 4) -> Q8_0 (the same d, int8 v - 16):
+//    d * float(v - 16) is the very product quant_v2::value forms, so the values are identical;
+//  * Q4_0 in upstream ggml's nibble order (elements j and j + 16 share byte j, low nibble
+//    first) -> the reference's order (element o in byte o/2, low nibble for even o).
+// Returns false for a type that needs no conversion.
+static bool convert_blocks(int type, const uint8_t* src, size_t nblocks, bool q4_upstream, int* out_type,
+                           std::vector<uint8_t>& out) {
+    if (type == T_Q5_0) {
+        out.resize(nblocks * 34);
+        for (size_t b = 0; b < nblocks; ++b) {
+            const uint8_t* p = src + b * 22;
+            uint8_t* o = out.data() + b * 34;
+            uint32_t qh;
+            std::memcpy(&qh, p + 2, 4);
+            o[0] = p[0];
+            o[1] = p[1];
+            for (int e = 0; e < 32; ++e) {
+                const uint8_t z = p[6 + e / 2];
+                const int v = ((e & 1) ? z >> 4 : z & 15) | (int)(((qh >> e) & 1u) << 4);
+                o[2 + e] = (uint8_t)(int8_t)(v - 16);
+            }
+        }
+        *out_type = T_Q8_0;
+        return true;
+    }
+    if (type == T_Q4_0 && q4_upstream) {
+        out.resize(nblocks * 18);
+        for (size_t b = 0; b < nblocks; ++b) {
+            const uint8_t* p = src + b * 18;
+            uint8_t* o = out.data() + b * 18;
+            o[0] = p[0];
+            o[1] = p[1];
+            for (int k = 0; k < 16; ++k) {  // byte k holds elements 2k and 2k+1 in the reference's order
+                auto nib = [&](int e) { return e < 16 ? p[2 + e] & 15 : p[2 + e - 16] >> 4; };
+                o[2 + k] = (uint8_t)(nib(2 * k) | (nib(2 * k + 1) << 4));
+            }
+        }
+        *out_type = T_Q4_0;
+        return true;
+    }
+    return false;
 }
 
 // A projection matrix in the fragment-tile layout of mma_matvec.cuh.
@@ -468,6 +516,7 @@ struct laic_dev {
     int ls_type = -1, ls_nst = 0, ls_maxch = 0, ls_runs = 0;
     size_t ls_smem_bytes = 0;
     bool ls_ready = false, ls_checked = false, use_ls = true, force_ls = false, ls_lm = false;
+    bool q4_upstream = false;  // Q4_0 uploads arrive in upstream ggml's nibble order
     unsigned long long* ls_trace = nullptr;  // LAIC_FLAG_TRACE: per-phase stamps of the last step kernel
     bool trace_on = false;
     // more than 16 sequences on one GPU: binary16 hi/lo activation records written by the producing
@@ -1175,6 +1224,7 @@ int laic_dev_create(const laic_dev_desc* desc, const laic_dev_opts* opts, laic_d
     d->use_pdl = !(o.flags & LAIC_FLAG_NO_PDL);
     d->use_ls = (o.flags & LAIC_FLAG_LAYER_LAUNCHES) == 0;
     d->force_ls = (o.flags & LAIC_FLAG_STEP_KERNEL) != 0;
+    d->q4_upstream = (o.flags & LAIC_FLAG_Q4_0_UPSTREAM) != 0;
     d->trace_on = (o.flags & LAIC_FLAG_TRACE) != 0;
     d->layers.resize(a.layers);
     d->h_pos.assign(o.max_seqs, 0);
@@ -1312,6 +1362,13 @@ int laic_dev_upload(laic_dev* d, const char* cname, int32_t type, const uint64_t
     size_t n = 1;
     for (int i = 0; i < ndim; ++i) n *= shape[i];
     if (nbytes < elem_bytes(type, n)) return fail(LAIC_E_INVALID, "tensor data out of range: " + name);
+    std::vector<uint8_t> conv;  // blocks held as another type with the same values (convert_blocks)
+    int ctype = type;
+    if (convert_blocks(type, (const uint8_t*)data, n / 32, d->q4_upstream, &ctype, conv)) {
+        type = ctype;
+        data = conv.data();
+        nbytes = conv.size();
+    }
     auto shape_is = [&](uint64_t in, uint64_t out) { return ndim == 2 && shape[0] == in && shape[1] == out; };
     // any graph captured before this upload points at old buffers
     for (auto& kv : d->graphs) cudaGraphExecDestroy(kv.second);
@@ -1693,6 +1750,26 @@ int laic_dev_step_trace(laic_dev* d, uint64_t* out, int64_t max_entries, int64_t
     return LAIC_OK;
 }
 
+int laic_blocks_convert(int32_t ggml_type, const void* src, uint64_t n, uint32_t flags, int32_t* out_type, void* dst,
+                        uint64_t dst_cap, uint64_t* dst_bytes) {
+    if (!src || !out_type || !dst_bytes) return fail(LAIC_E_INVALID, "null argument");
+    if (n % 32) return fail(LAIC_E_INVALID, "element count must be a multiple of 32");
+    const size_t in_bytes = elem_bytes(ggml_type, n);
+    if (ggml_type != T_F32 && ggml_type != T_F16 && !in_bytes)
+        return fail(LAIC_E_UNSUPPORTED, "unsupported GGML type " + std::to_string(ggml_type));
+    std::vector<uint8_t> conv;
+    int t = ggml_type;
+    const bool c = convert_blocks(ggml_type, (const uint8_t*)src, n / 32, (flags & LAIC_FLAG_Q4_0_UPSTREAM) != 0, &t,
+                                  conv);
+    const size_t bytes = c ? conv.size() : in_bytes;
+    *out_type = t;
+    *dst_bytes = bytes;
+    if (!dst) return LAIC_OK;  // size query
+    if (dst_cap < bytes) return fail(LAIC_E_INVALID, "destination too small");
+    std::memcpy(dst, c ? (const void*)conv.data() : src, bytes);
+    return LAIC_OK;
+}
+
 int laic_nccl_unique_id(void* out128) {
     if (!out128) return fail(LAIC_E_INVALID, "null argument");
     std::string why;
@@ -1720,6 +1797,13 @@ int laic_tensor_create(int32_t device, int32_t type, uint64_t in, uint64_t out, 
                        laic_tensor** t) {
     if (!data || !t || !in || !out) return fail(LAIC_E_INVALID, "bad argument");
     if (nbytes < elem_bytes(type, in * out)) return fail(LAIC_E_INVALID, "tensor data out of range");
+    std::vector<uint8_t> conv;
+    int ctype = type;
+    if (convert_blocks(type, (const uint8_t*)data, in * out / 32, false, &ctype, conv)) {
+        type = ctype;
+        data = conv.data();
+        nbytes = conv.size();
+    }
     CK(cudaSetDevice(device));
     CK(laic::mv_set_attributes());
     std::unique_ptr<laic_tensor> x(new laic_tensor());

@@ -13,7 +13,7 @@ import numpy as np
 
 from . import gguf
 from ._native import (DevDesc, DevOpts, DevStats, FLAG_KV_F32, FLAG_NO_GRAPH, FLAG_NO_PDL, FLAG_LAYER_LAUNCHES, FLAG_TRACE,
-                      FLAG_STEP_KERNEL, KernelRecord, SampleParams,
+                      FLAG_STEP_KERNEL, FLAG_Q4_0_UPSTREAM, KernelRecord, SampleParams,
                       check, lib)
 
 
@@ -38,9 +38,10 @@ class Engine:
     def __init__(self, path: str, max_seqs: int = 1, kv_capacity: int = 0, device: int = 0, kv_f32: bool = False,
                  graphs: bool = True, pdl: bool = True, tp_size: int = 1, tp_rank: int = 0,
                  nccl_id: Optional[bytes] = None, layer_launches: bool = False, trace: bool = False,
-                 step_kernel: Optional[bool] = None) -> None:
+                 step_kernel: Optional[bool] = None, q4_0_upstream: bool = False) -> None:
         """`step_kernel`: True runs one-sequence Q4_0/Q8_0 steps as the persistent decode-step kernel, False
-        (or `layer_launches`) and None (the default) launch per projection."""
+        (or `layer_launches`) and None (the default) launch per projection. `q4_0_upstream`: the file's Q4_0
+        tensors use upstream ggml's nibble order (llama.cpp's files) rather than the reference's."""
         L = lib()
         if step_kernel is False:
             layer_launches = True
@@ -48,7 +49,7 @@ class Engine:
         self.desc = desc_from_gguf(self.file)
         flags = ((FLAG_KV_F32 if kv_f32 else 0) | (0 if graphs else FLAG_NO_GRAPH) | (0 if pdl else FLAG_NO_PDL)
                  | (FLAG_LAYER_LAUNCHES if layer_launches else 0) | (FLAG_TRACE if trace else 0)
-                 | (FLAG_STEP_KERNEL if step_kernel else 0))
+                 | (FLAG_STEP_KERNEL if step_kernel else 0) | (FLAG_Q4_0_UPSTREAM if q4_0_upstream else 0))
         self._nccl_id = ctypes.create_string_buffer(nccl_id, 128) if nccl_id else None
         opts = DevOpts(device=device, max_seqs=max_seqs, kv_capacity=kv_capacity, tp_size=tp_size, tp_rank=tp_rank,
                        nccl_id=ctypes.cast(self._nccl_id, ctypes.c_void_p) if self._nccl_id else None, flags=flags)
@@ -226,3 +227,15 @@ class Matrix:
 
     def __del__(self) -> None:
         self.close()
+
+
+def blocks_convert(ggml_type: int, raw: np.ndarray, n: int, q4_0_upstream: bool = False) -> Tuple[int, np.ndarray]:
+    """The device's block type and bytes for `n` elements of GGML blocks (laic_blocks_convert, host only)."""
+    raw = np.ascontiguousarray(raw, dtype=np.uint8)
+    t, nb = ctypes.c_int32(), ctypes.c_uint64()
+    flags = FLAG_Q4_0_UPSTREAM if q4_0_upstream else 0
+    check(lib().laic_blocks_convert(ggml_type, raw.ctypes.data, n, flags, ctypes.byref(t), None, 0, ctypes.byref(nb)))
+    out = np.zeros(nb.value, dtype=np.uint8)
+    check(lib().laic_blocks_convert(ggml_type, raw.ctypes.data, n, flags, ctypes.byref(t), out.ctypes.data, out.nbytes,
+                                    ctypes.byref(nb)))
+    return t.value, out

@@ -19,7 +19,7 @@ GGUF_MAGIC = 0x46554747  # "GGUF"
 
 # GGML tensor types used by the reference (include/laic/gguf.hpp:9).
 F32, F16, Q4_0, Q4_1, Q5_0, Q5_1, Q8_0 = 0, 1, 2, 3, 6, 7, 8
-TYPE_NAMES = {F32: "F32", F16: "F16", Q4_0: "Q4_0", Q8_0: "Q8_0"}
+TYPE_NAMES = {F32: "F32", F16: "F16", Q4_0: "Q4_0", Q5_0: "Q5_0", Q8_0: "Q8_0"}
 BLOCK_BYTES = {Q4_0: 18, Q4_1: 20, Q5_0: 22, Q5_1: 24, Q8_0: 34}
 
 # metadata value type codes (src/gguf.cpp:10)

@@ -115,6 +115,25 @@ def quantize_q4_0(x: np.ndarray) -> bytes:
     return out.tobytes()
 
 
+def quantize_q5_0(x: np.ndarray) -> bytes:
+    """Encode float32 values as Q5_0 blocks (22 B: fp16 d, 32 high bits, 16 nibble bytes) in the
+    reference's order (src/quant_v2.cpp:12): element o is d * (v - 16), v = the nibble of byte
+    o/2 (low for even o) with bit o of the high bits as its bit 4."""
+    b = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, 32)
+    idx = np.abs(b).argmax(axis=1)
+    m = b[np.arange(b.shape[0]), idx]
+    d = (m / np.float32(-16.0)).astype(np.float32)
+    idv = np.where(d != 0, np.float32(1.0) / np.where(d != 0, d, 1), 0).astype(np.float32)
+    v = np.minimum(31, np.trunc(b * idv[:, None] + np.float32(16.5))).astype(np.uint32)
+    out = np.empty((b.shape[0], 22), dtype=np.uint8)
+    out[:, 0:2] = d.astype("<f2").view(np.uint8).reshape(-1, 2)
+    qh = ((v >> 4) << np.arange(32, dtype=np.uint32)).sum(axis=1, dtype=np.uint64).astype("<u4")
+    out[:, 2:6] = qh.view(np.uint8).reshape(-1, 4)
+    lo = (v & 15).astype(np.uint8)
+    out[:, 6:] = lo[:, 0::2] | (lo[:, 1::2] << 4)
+    return out.tobytes()
+
+
 def encode(x: np.ndarray, ggml_type: int) -> bytes:
     if ggml_type == gguf.F32:
         return np.ascontiguousarray(x, dtype="<f4").tobytes()
@@ -124,6 +143,8 @@ def encode(x: np.ndarray, ggml_type: int) -> bytes:
         return quantize_q8_0(x)
     if ggml_type == gguf.Q4_0:
         return quantize_q4_0(x)
+    if ggml_type == gguf.Q5_0:
+        return quantize_q5_0(x)
     raise ValueError(f"no encoder for ggml type {ggml_type}")
 
 
@@ -147,6 +168,16 @@ def dequantize(raw: bytes | np.ndarray, ggml_type: int, n: int) -> np.ndarray:
         q[:, 0::2] = (z & 15).astype(np.float32) - 8
         q[:, 1::2] = (z >> 4).astype(np.float32) - 8
         return (d * q).reshape(-1)[:n]
+    if ggml_type == gguf.Q5_0:
+        blk = a[: (n // 32) * 22].reshape(-1, 22)
+        d = blk[:, 0:2].copy().view("<f2").astype(np.float32)
+        qh = blk[:, 2:6].copy().view("<u4").astype(np.uint32)
+        z = blk[:, 6:]
+        v = np.empty((blk.shape[0], 32), dtype=np.uint32)
+        v[:, 0::2] = z & 15
+        v[:, 1::2] = z >> 4
+        v |= ((qh >> np.arange(32, dtype=np.uint32)) & 1) << 4
+        return (d * (v.astype(np.float32) - 16)).reshape(-1)[:n]
     raise ValueError(f"no decoder for ggml type {ggml_type}")
 
 

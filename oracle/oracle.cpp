@@ -40,7 +40,7 @@
 
 namespace {
 
-enum : uint32_t { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q8_0 = 8 };
+enum : uint32_t { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q4_1 = 3, T_Q5_0 = 6, T_Q5_1 = 7, T_Q8_0 = 8 };
 
 // Exact binary16 -> float (src/half.cpp:30-51).
 float half_to_float(uint16_t h) {
@@ -60,11 +60,14 @@ float half_to_float(uint16_t h) {
 inline float h16(const uint8_t* p) { return half_to_float(uint16_t(p[0]) | (uint16_t(p[1]) << 8)); }
 
 size_t block_bytes(uint32_t t) {
-    switch (t) { case T_F32: return 4; case T_F16: return 2; case T_Q4_0: return 18; case T_Q8_0: return 34; }
+    switch (t) {
+    case T_F32: return 4; case T_F16: return 2; case T_Q4_0: return 18; case T_Q8_0: return 34;
+    case T_Q4_1: return 20; case T_Q5_0: return 22; case T_Q5_1: return 24;
+    }
     throw std::runtime_error("unsupported GGML type");
 }
 
-// One element of a tensor (quant_v2::value for Q8_0/Q4_0, GgufTensor::value for F16/F32).
+// One element of a tensor (quant_v2::value for Q8_0/Q4_0/Q4_1/Q5_0/Q5_1, GgufTensor::value for F16/F32).
 inline float value(uint32_t type, const uint8_t* data, size_t i) {
     switch (type) {
     case T_F32: { float v; std::memcpy(&v, data + i * 4, 4); return v; }
@@ -73,6 +76,22 @@ inline float value(uint32_t type, const uint8_t* data, size_t i) {
     case T_Q4_0: {
         const uint8_t* p = data + (i / 32) * 18; size_t o = i % 32; uint8_t z = p[2 + o / 2];
         return h16(p) * float(((o & 1) ? (z >> 4) : (z & 15)) - 8);
+    }
+    // src/quant_v2.cpp:11 (Q4_1: d * q + m), :12 (Q5_0: d * (v - 16)), :13 (Q5_1: d * v + m); the
+    // fifth bit of element o is bit o of the 32-bit qh that follows the scale(s)
+    case T_Q4_1: {
+        const uint8_t* p = data + (i / 32) * 20; size_t o = i % 32; uint8_t z = p[4 + o / 2];
+        return h16(p) * float((o & 1) ? (z >> 4) : (z & 15)) + h16(p + 2);
+    }
+    case T_Q5_0: {
+        const uint8_t* p = data + (i / 32) * 22; size_t o = i % 32; uint32_t qh; std::memcpy(&qh, p + 2, 4);
+        uint8_t z = p[6 + o / 2]; int v = ((o & 1) ? (z >> 4) : (z & 15)) | int(((qh >> o) & 1u) << 4);
+        return h16(p) * float(v - 16);
+    }
+    case T_Q5_1: {
+        const uint8_t* p = data + (i / 32) * 24; size_t o = i % 32; uint32_t qh; std::memcpy(&qh, p + 4, 4);
+        uint8_t z = p[8 + o / 2]; int v = ((o & 1) ? (z >> 4) : (z & 15)) | int(((qh >> o) & 1u) << 4);
+        return h16(p) * float(v) + h16(p + 2);
     }
     }
     throw std::runtime_error("unsupported quantized GGML type");

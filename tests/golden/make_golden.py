@@ -19,8 +19,12 @@ reference sources). Writes:
                          ids, per-step argmax / max / top-2 margin / sum and
                          the first 64 logits
 
-Run from the repository root:  python tests/golden/make_golden.py [generate]
-("generate" writes only generate_text.json).
+  blocks.npz             the reference's decode (quant_v2::value) of random and
+                         edge-case blocks of Q4_1, Q5_0, Q5_1 and Q4_0 (the raw
+                         blocks and the float32 values)
+
+Run from the repository root:  python tests/golden/make_golden.py [generate|blocks]
+("generate" writes only generate_text.json, "blocks" only blocks.npz).
 """
 from __future__ import annotations
 
@@ -214,12 +218,52 @@ def make_generate() -> None:
     print("generate_text.json:", len(cases), "cases")
 
 
+# block bytes, offset of the nibbles, offset of the 32 high bits (Q5_*), and the number of fp16
+# scales in front of them
+BLOCK_TYPES = {"q4_1": (gguf.Q4_1, 20, 4, None, 2), "q5_0": (gguf.Q5_0, 22, 6, 2, 1),
+               "q5_1": (gguf.Q5_1, 24, 8, 4, 2), "q4_0": (gguf.Q4_0, 18, 2, None, 1)}
+EDGE_HALVES = [0x0001, 0x03FF, 0x0400, 0x7BFF, 0x8000, 0x0000, 0xFBFF, 0x3C00, 0xBC00, 0x2E66]
+
+
+def random_blocks(kind: str, nblocks: int, rng: np.random.Generator) -> bytes:
+    """Random blocks (scales of modest size, edge-case scales in the first blocks)."""
+    gt, bb, qoff, hoff, nsc = BLOCK_TYPES[kind]
+    raw = rng.integers(0, 256, size=(nblocks, bb), dtype=np.uint8)
+    scales = (rng.uniform(1e-3, 5e-2, size=(nblocks, nsc)) * rng.choice([-1, 1], size=(nblocks, nsc)))
+    h = scales.astype(np.float16).view(np.uint16)
+    for i, e in enumerate(EDGE_HALVES):  # edge scales (subnormal, max, signed zero, ...) in the first blocks
+        h[i % nblocks, i % nsc] = e
+    raw[:, :2 * nsc] = h.astype("<u2").view(np.uint8).reshape(nblocks, 2 * nsc)
+    return raw.tobytes()
+
+
+def make_blocks() -> None:
+    rng = np.random.default_rng(2024)
+    nblocks = 96
+    tensors, out = [], {}
+    for kind, (gt, bb, _, _, _) in BLOCK_TYPES.items():
+        raw = random_blocks(kind, nblocks, rng)
+        tensors.append((f"blocks.{kind}", (32 * nblocks,), gt, raw))
+        out[f"raw_{kind}"] = np.frombuffer(raw, dtype=np.uint8)
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "blocks.gguf")
+        gguf.write_gguf(path, {"general.architecture": "llama", "general.name": "blocks"}, tensors)
+        for kind in BLOCK_TYPES:
+            out[f"value_{kind}"] = ref_dequant(path, f"blocks.{kind}")
+    np.savez_compressed(os.path.join(HERE, "blocks.npz"), **out)
+    print("blocks.npz", {k: v.shape for k, v in out.items()})
+
+
 if __name__ == "__main__":
     if O.ref_driver("strict") is None:
         O.build()
     if len(sys.argv) > 1 and sys.argv[1] == "generate":
         make_generate()
         sys.exit(0)
+    if len(sys.argv) > 1 and sys.argv[1] == "blocks":
+        make_blocks()
+        sys.exit(0)
+    make_blocks()
     make_tiny()
     make_generate()
     work = tempfile.mkdtemp(prefix="laic_golden_")
