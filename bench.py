@@ -49,6 +49,8 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+from dataclasses import replace  # noqa: E402
+
 from laicompute_b200 import synth  # noqa: E402
 
 WORKLOADS = {
@@ -57,11 +59,15 @@ WORKLOADS = {
     "smollm135m-f16": (synth.SMOL_135M_F16, 1, 8, 1, "SmolLM-135M-shaped Llama, F16"),
     "llama1b-q4_0": (synth.LLAMA_1B_Q4, 4, 512, 32, "1B-shaped Llama, Q4_0 projections, F16 embeddings"),
     "llama8b-q4_0": (synth.LLAMA_8B_Q4, 5, 1024, 1, "8B-shaped Llama, Q4_0 projections, tied Q4_0 embeddings"),
+    # two layers of the 8B shape: the same kernels and launch shapes on ~0.5 GB of weights, the
+    # small case for multi-pass profiler captures of the 8B kernels
+    "llama8b-2l-q4_0": (replace(synth.LLAMA_8B_Q4, name="llama-8b-2l-q4_0", layers=2), 5, 1024, 1,
+                        "two layers of the 8B-shaped Llama (profiling case)"),
 }
 # workloads split tensor-parallel over the GPUs of the run (the others run one replica per GPU)
 TP_WORKLOADS = {"llama8b-q4_0"}
 # KV positions allocated per slot, where the workload asks for more than it decodes
-KV_CAPACITY = {"llama8b-q4_0": 8192}
+KV_CAPACITY = {"llama8b-q4_0": 8192, "llama8b-2l-q4_0": 8192}
 # CPU sample of the large models: (prompt tokens, timed decode steps) — a reference step takes seconds
 CPU_SAMPLE = {"llama1b-q4_0": (64, 16), "llama8b-q4_0": (32, 8)}
 DEFAULT_WORKLOAD = "smollm135m-q8_0"
