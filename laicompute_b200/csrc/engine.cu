@@ -198,6 +198,7 @@ int num_sms() {
 // Launch shape of one fragment-tile matvec: n-tiles, K split, ring, grid, shared memory.
 struct MvShape {
     bool sk = false;  // team kernel (small batches whose activations fit in shared memory)
+    int warps = laic::kSkWarps;  // team kernel: warps per CTA
     int nt = 1, nk = 1, kr = 1, kb = 1, stages = 2, grid = 1;
     int groups = 1, sgrp = 1;  // tile kernel: sequence groups (grid.y) of sgrp sequences
     bool wide = false;         // the wide kernel (EPI_STORE, warps own whole row tiles)
@@ -235,11 +236,18 @@ constexpr size_t kSmemBudget = 220 * 1024;
 MvShape mv_shape(const Mat& m, int B, bool team_ok = true, bool store = false) {
     MvShape sh;
     if (team_ok && B <= LAIC_SK_MAX_BATCH) {
-        const size_t smem = laic::sk_smem_bytes(m.type, m.nb, B);
+        // one sequence of Q4_0 / Q8_0: integer dot products (nt 0); else hi and lo columns side by side
+        const int nt = (B == 1 && m.type != T_F16) ? 0 : B <= 4 ? 1 : B <= 8 ? 2 : 4;
+        int warps = laic::sk_warps_for(m.type, nt, m.nb, m.rows);
+        size_t smem = laic::sk_smem_bytes(m.type, m.nb, B, warps);
+        if (smem > kSmemBudget && warps != laic::kSkWarps) {
+            warps = laic::kSkWarps;
+            smem = laic::sk_smem_bytes(m.type, m.nb, B, warps);
+        }
         if (smem <= kSmemBudget) {
             sh.sk = true;
-            // one sequence of Q4_0 / Q8_0: integer dot products (nt 0); else hi and lo columns side by side
-            sh.nt = (B == 1 && m.type != T_F16) ? 0 : B <= 4 ? 1 : B <= 8 ? 2 : 4;
+            sh.warps = warps;
+            sh.nt = nt;
             sh.grid = std::max(1, std::min(num_sms(), m.ntiles));  // each CTA owns whole row tiles
             sh.smem = smem;
             sh.part_floats = 0;
@@ -421,7 +429,7 @@ cudaError_t launch_matvec(const Mat& m, laic::MvParams p, int epi, bool kv32, co
             p.xg = rin->xg; p.scale_mode = rin->mode; p.ss = rin->ss; p.ss_tiles = rin->ss_tiles; p.ss_n = m.in;
         }
         if (launches) *launches += 1;
-        return laic::mv_sk_launch(m.type, sh.nt, epi, kv32, p, sh.grid, sh.smem, st, pdl);
+        return laic::mv_sk_launch(m.type, sh.nt, epi, kv32, p, sh.grid, sh.smem, st, pdl, sh.warps);
     }
     p.nk = sh.nk; p.kr = sh.kr; p.kb = sh.kb; p.stages = sh.stages; p.sgrp = sh.sgrp;
     p.part = sc.part; p.tile_cnt = sc.tile_cnt; p.err = sc.err;

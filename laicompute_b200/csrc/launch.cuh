@@ -55,9 +55,13 @@ cudaError_t mv_launch(int type, int nt, int epi, bool kv32, const MvParams& p, i
 // Launch the wide matvec (EPI_STORE; each warp owns whole row tiles), grid (grid, groups).
 cudaError_t mv_wide_launch(int type, int nt, const MvParams& p, int grid, int groups, size_t smem, cudaStream_t st,
                            bool pdl);
-// Launch the team matvec (defined in mv_<type>.cu), nt = 1, 2 or 4; nt = 0 is the one-sequence integer variant.
+// Launch the team matvec (defined in mv_<type>.cu), nt = 1, 2 or 4; nt = 0 is the one-sequence integer
+// variant, which runs with `warps` = kSkWarps or kSkWarpsWide warps per CTA (sk_warps_for).
 cudaError_t mv_sk_launch(int type, int nt, int epi, bool kv32, const MvParams& p, int grid, size_t smem,
-                         cudaStream_t st, bool pdl);
+                         cudaStream_t st, bool pdl, int warps);
+// Warps per CTA of a team-matvec launch: kSkWarpsWide for one sequence of a Q4_0/Q8_0 matrix with at
+// least 128 blocks per row and 4096 rows, else kSkWarps.
+int sk_warps_for(int type, int nt, int nb, int rows);
 // Raise the dynamic shared memory limit of every instantiation (call before any graph capture).
 cudaError_t mv_set_attributes();
 

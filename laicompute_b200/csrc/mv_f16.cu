@@ -34,7 +34,7 @@ static void (*pick_sk_f16(int epi, bool kv32))(MvParams) {
     }
 }
 
-void (*mv_sk_kernel_f16(int nt, int epi, bool kv32))(MvParams) {
+void (*mv_sk_kernel_f16(int nt, int epi, bool kv32, int /*warps: F16 runs kSkWarps*/))(MvParams) {
     return nt == 1 ? pick_sk_f16<1>(epi, kv32) : nt == 2 ? pick_sk_f16<2>(epi, kv32) : pick_sk_f16<4>(epi, kv32);
 }
 

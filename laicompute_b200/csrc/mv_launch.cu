@@ -8,9 +8,9 @@ namespace laic {
 void (*mv_kernel_q4_0(int nt, int epi, bool kv32))(MvParams);
 void (*mv_kernel_q8_0(int nt, int epi, bool kv32))(MvParams);
 void (*mv_kernel_f16(int nt, int epi, bool kv32))(MvParams);
-void (*mv_sk_kernel_q4_0(int nt, int epi, bool kv32))(MvParams);
-void (*mv_sk_kernel_q8_0(int nt, int epi, bool kv32))(MvParams);
-void (*mv_sk_kernel_f16(int nt, int epi, bool kv32))(MvParams);
+void (*mv_sk_kernel_q4_0(int nt, int epi, bool kv32, int warps))(MvParams);
+void (*mv_sk_kernel_q8_0(int nt, int epi, bool kv32, int warps))(MvParams);
+void (*mv_sk_kernel_f16(int nt, int epi, bool kv32, int warps))(MvParams);
 void (*mv_wide_kernel_q4_0(int nt))(MvParams);
 void (*mv_wide_kernel_q8_0(int nt))(MvParams);
 void (*mv_wide_kernel_f16(int nt))(MvParams);
@@ -26,15 +26,19 @@ cudaError_t mv_wide_launch(int type, int nt, const MvParams& p, int grid, int gr
     return launch_k(mv_wide_kernel(type, nt), dim3(grid, groups), dim3(kMvThreads), smem, st, pdl, p);
 }
 
-static void (*mv_sk_kernel(int type, int nt, int epi, bool kv32))(MvParams) {
-    if (type == T_Q4_0) return mv_sk_kernel_q4_0(nt, epi, kv32);
-    if (type == T_Q8_0) return mv_sk_kernel_q8_0(nt, epi, kv32);
-    return mv_sk_kernel_f16(nt, epi, kv32);
+static void (*mv_sk_kernel(int type, int nt, int epi, bool kv32, int warps = kSkWarps))(MvParams) {
+    if (type == T_Q4_0) return mv_sk_kernel_q4_0(nt, epi, kv32, warps);
+    if (type == T_Q8_0) return mv_sk_kernel_q8_0(nt, epi, kv32, warps);
+    return mv_sk_kernel_f16(nt, epi, kv32, warps);
+}
+
+int sk_warps_for(int type, int nt, int nb, int rows) {
+    return nt == 0 && type != T_F16 && nb >= 128 && rows >= 4096 ? kSkWarpsWide : kSkWarps;
 }
 
 cudaError_t mv_sk_launch(int type, int nt, int epi, bool kv32, const MvParams& p, int grid, size_t smem,
-                         cudaStream_t st, bool pdl) {
-    return launch_k(mv_sk_kernel(type, nt, epi, kv32), dim3(grid), dim3(kSkWarps * 32), smem, st, pdl, p);
+                         cudaStream_t st, bool pdl, int warps) {
+    return launch_k(mv_sk_kernel(type, nt, epi, kv32, warps), dim3(grid), dim3(warps * 32), smem, st, pdl, p);
 }
 
 static void (*mv_kernel(int type, int nt, int epi, bool kv32))(MvParams) {
@@ -71,11 +75,12 @@ cudaError_t mv_set_attributes() {
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
                         if (e != cudaSuccess) return e;
                     }
-                    if (nt == 1 && type != T_F16) {  // the integer variant (nt 0)
-                        e = cudaFuncSetAttribute(mv_sk_kernel(type, 0, epi, kv32),
-                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-                        if (e != cudaSuccess) return e;
-                    }
+                    if (nt == 1 && type != T_F16)  // the integer variant (nt 0), with either warp count
+                        for (int w : {kSkWarps, kSkWarpsWide}) {
+                            e = cudaFuncSetAttribute(mv_sk_kernel(type, 0, epi, kv32, w),
+                                                     cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+                            if (e != cudaSuccess) return e;
+                        }
                 }
     return cudaSuccess;
 }

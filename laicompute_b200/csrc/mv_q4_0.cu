@@ -24,18 +24,19 @@ void (*mv_kernel_q4_0(int nt, int epi, bool kv32))(MvParams) {
     }
 }
 
-template <int NT>
+template <int NT, int W = kSkWarps>
 static void (*pick_sk_q4_0(int epi, bool kv32))(MvParams) {
     switch (epi) {
-    case EPI_STORE: return mv_sk_kernel<T_Q4_0, NT, EPI_STORE, __half>;
-    case EPI_ADD: return mv_sk_kernel<T_Q4_0, NT, EPI_ADD, __half>;
-    case EPI_SWIGLU: return mv_sk_kernel<T_Q4_0, NT, EPI_SWIGLU, __half>;
-    default: return kv32 ? mv_sk_kernel<T_Q4_0, NT, EPI_QKV, float> : mv_sk_kernel<T_Q4_0, NT, EPI_QKV, __half>;
+    case EPI_STORE: return mv_sk_kernel<T_Q4_0, NT, EPI_STORE, __half, W>;
+    case EPI_ADD: return mv_sk_kernel<T_Q4_0, NT, EPI_ADD, __half, W>;
+    case EPI_SWIGLU: return mv_sk_kernel<T_Q4_0, NT, EPI_SWIGLU, __half, W>;
+    default: return kv32 ? mv_sk_kernel<T_Q4_0, NT, EPI_QKV, float, W> : mv_sk_kernel<T_Q4_0, NT, EPI_QKV, __half, W>;
     }
 }
 
-void (*mv_sk_kernel_q4_0(int nt, int epi, bool kv32))(MvParams) {
-    // nt 0: the single-sequence integer variant
+void (*mv_sk_kernel_q4_0(int nt, int epi, bool kv32, int warps))(MvParams) {
+    // nt 0: the single-sequence integer variant (also with kSkWarpsWide warps)
+    if (nt == 0 && warps == kSkWarpsWide) return pick_sk_q4_0<0, kSkWarpsWide>(epi, kv32);
     return nt == 0 ? pick_sk_q4_0<0>(epi, kv32) : nt == 1 ? pick_sk_q4_0<1>(epi, kv32)
          : nt == 2 ? pick_sk_q4_0<2>(epi, kv32) : pick_sk_q4_0<4>(epi, kv32);
 }

@@ -45,7 +45,11 @@ constexpr int kSkWarps = LAIC_SK_WARPS;          // warps per CTA
 constexpr int kSkRingBytes = LAIC_SK_RING_BYTES;  // per warp: stages in flight
 constexpr int kSkSlots = 2;                       // tile slots per team (a team's warps may drift apart)
 // largest power of two dividing the warp count: the widest team
-constexpr int kSkMaxTeam = (kSkWarps & -kSkWarps) < 16 ? (kSkWarps & -kSkWarps) : 16;
+// Large one-sequence matrices (at least 128 blocks per row and 4096 rows) run with more warps
+// per CTA: more weight stages in flight and more warps to hide the integer loop's latencies
+// (measured: the 8B-shaped step 8 % faster; 1B-shaped projections ~4 % slower, so they keep 16).
+constexpr int kSkWarpsWide = 24;
+__host__ __device__ constexpr int sk_max_team(int w) { return (w & -w) < 16 ? (w & -w) : 16; }
 // tile-blocks per ring stage (about LAIC_SK_STAGE_BYTES for every type)
 __host__ __device__ constexpr int sk_kb(int type) {
     return LAIC_SK_STAGE_BYTES / (tile_qbytes(type) + (type == T_F16 ? 0 : kTileSBytes)) > 0
@@ -56,21 +60,21 @@ __host__ __device__ constexpr int sk_stage_bytes(int type) {
 }
 __host__ __device__ constexpr int sk_stages(int type) { return kSkRingBytes / sk_stage_bytes(type); }
 // warps per tile: long rows are split over more warps
-__host__ __device__ inline int sk_team(int nb) {
+__host__ __device__ inline int sk_team(int nb, int w = kSkWarps) {
     const int k = nb >= 256 ? 16 : nb >= 128 ? 8 : nb >= 64 ? 4 : nb >= 32 ? 2 : 1;
-    return k < kSkMaxTeam ? k : kSkMaxTeam;
+    return k < sk_max_team(w) ? k : sk_max_team(w);
 }
 
 // tickets, merged-tile marks, per-warp statistics, 1/rms and split scale per sequence
-__host__ __device__ inline size_t sk_small_bytes(int B) {
-    return ((size_t)kSkWarps * kSkSlots * 2 * 4 + (size_t)kSkWarps * B * 2 * 4 + 2 * (size_t)B * 4 + 15) / 16 * 16;
+__host__ __device__ inline size_t sk_small_bytes(int B, int w = kSkWarps) {
+    return ((size_t)w * kSkSlots * 2 * 4 + (size_t)w * B * 2 * 4 + 2 * (size_t)B * 4 + 15) / 16 * 16;
 }
 // Shared memory of one CTA: rings, activations (whole K), partial slots + tickets, statistics, barriers.
-__host__ __device__ inline size_t sk_smem_bytes(int type, int nb, int B) {
-    const size_t rings = (size_t)kSkWarps * sk_stages(type) * sk_stage_bytes(type);
+__host__ __device__ inline size_t sk_smem_bytes(int type, int nb, int B, int w = kSkWarps) {
+    const size_t rings = (size_t)w * sk_stages(type) * sk_stage_bytes(type);
     const size_t xs = (size_t)nb * B * 128;
-    const size_t parts = (size_t)kSkWarps * kSkSlots * 16 * B * 4;  // [warp][slot][16][B]
-    return rings + xs + parts + sk_small_bytes(B) + (size_t)kSkWarps * sk_stages(type) * 8;
+    const size_t parts = (size_t)w * kSkSlots * 16 * B * 4;  // [warp][slot][16][B]
+    return rings + xs + parts + sk_small_bytes(B, w) + (size_t)w * sk_stages(type) * 8;
 }
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -306,7 +310,7 @@ __device__ __forceinline__ void dp_build_records(const float* x, const float* no
         if (lane == 0) wstat[warp * 2] = ss;
         __syncthreads();
         float a = 0.f;
-        for (int w = 0; w < kSkWarps; ++w) a += wstat[w * 2];
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) a += wstat[w * 2];
         const float iv = norm_w ? 1.f / sqrtf(a / float(in) + eps) : 1.f;
         for (int base = 0; base < ng; base += nt) {
             const int gi = base + threadIdx.x;
@@ -336,7 +340,7 @@ __device__ __forceinline__ void dp_build_records(const float* x, const float* no
             if (lane == 0) wstat[warp * 2] = ss;
             __syncthreads();
             float a = 0.f;
-            for (int w = 0; w < kSkWarps; ++w) a += wstat[w * 2];
+            for (int w = 0; w < (int)(blockDim.x >> 5); ++w) a += wstat[w * 2];
             iv = 1.f / sqrtf(a / float(in) + eps);
         }
 #pragma unroll
@@ -351,8 +355,8 @@ __device__ __forceinline__ void dp_build_records(const float* x, const float* no
     __syncthreads();
 }
 
-template <int WT, int NT, int EPI, typename KV>
-__global__ void __launch_bounds__(kSkWarps * 32, 1) mv_sk_kernel(const MvParams p) {
+template <int WT, int NT, int EPI, typename KV, int W = kSkWarps>
+__global__ void __launch_bounds__(W * 32, 1) mv_sk_kernel(const MvParams p) {
     constexpr int QB = tile_qbytes(WT);
     constexpr int SB = WT == T_F16 ? 0 : kTileSBytes;
     constexpr int KB = sk_kb(WT);
@@ -367,19 +371,19 @@ __global__ void __launch_bounds__(kSkWarps * 32, 1) mv_sk_kernel(const MvParams 
     const int nb = p.nb;
 
     uint8_t* ring = smem + warp * R * STAGE;
-    uint8_t* xs = smem + kSkWarps * R * STAGE;
+    uint8_t* xs = smem + W * R * STAGE;
     float* parts = reinterpret_cast<float*>(xs + (size_t)nb * B * 128);  // [warp][slot][16][B]
-    uint8_t* small = reinterpret_cast<uint8_t*>(parts + kSkWarps * kSkSlots * 16 * B);
+    uint8_t* small = reinterpret_cast<uint8_t*>(parts + W * kSkSlots * 16 * B);
     int* tickets = reinterpret_cast<int*>(small);                        // [team leader][slot]
-    int* merged = tickets + kSkWarps * kSkSlots;                         // [team leader][slot] last merged tile + 1
-    float* wstat = reinterpret_cast<float*>(merged + kSkWarps * kSkSlots);  // [warps][B][2]
-    float* inv = wstat + kSkWarps * B * 2;                               // [B] rmsnorm 1/rms
+    int* merged = tickets + W * kSkSlots;                         // [team leader][slot] last merged tile + 1
+    float* wstat = reinterpret_cast<float*>(merged + W * kSkSlots);  // [warps][B][2]
+    float* inv = wstat + W * B * 2;                               // [B] rmsnorm 1/rms
     float* xsc = inv + B;                                                // [B] power-of-two split scale
-    uint64_t* bars = reinterpret_cast<uint64_t*>(small + sk_small_bytes(B)) + warp * R;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(small + sk_small_bytes(B, W)) + warp * R;
 
     // this CTA's tiles, this warp's team and K slice
-    const int k = sk_team(nb);
-    const int teams = kSkWarps / k, team = warp / k, wi = warp % k, leader = team * k;
+    const int k = sk_team(nb, W);
+    const int teams = W / k, team = warp / k, wi = warp % k, leader = team * k;
     const int t_lo = (int)((long long)blockIdx.x * p.ntiles / gridDim.x);
     const int t_hi = (int)((long long)(blockIdx.x + 1) * p.ntiles / gridDim.x);
     const int b_lo = wi * nb / k, b_hi = (wi + 1) * nb / k;  // slice of every tile
@@ -410,7 +414,7 @@ __global__ void __launch_bounds__(kSkWarps * 32, 1) mv_sk_kernel(const MvParams 
         mbar_fence_init();
         for (; issued < min(R, nst); ++issued) issue();
     }
-    for (int i = threadIdx.x; i < 2 * kSkWarps * kSkSlots; i += blockDim.x) tickets[i] = 0;  // and merged[]
+    for (int i = threadIdx.x; i < 2 * W * kSkSlots; i += blockDim.x) tickets[i] = 0;  // and merged[]
     __syncwarp();
     pdl_launch_dependents();
     pdl_wait();
@@ -469,7 +473,7 @@ __global__ void __launch_bounds__(kSkWarps * 32, 1) mv_sk_kernel(const MvParams 
         if (threadIdx.x < B) {
             const int s = threadIdx.x;
             float a = 0.f, m = 0.f;
-            for (int w = 0; w < kSkWarps; ++w) { a += wstat[(w * B + s) * 2]; m = fmaxf(m, wstat[(w * B + s) * 2 + 1]); }
+            for (int w = 0; w < W; ++w) { a += wstat[(w * B + s) * 2]; m = fmaxf(m, wstat[(w * B + s) * 2 + 1]); }
             const float iv = p.norm_w ? 1.f / sqrtf(a / float(p.in) + p.eps) : 1.f;
             m *= iv;
             int ex = 0;
