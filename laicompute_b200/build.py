@@ -3,6 +3,7 @@
 Outputs, in-tree:
   laicompute_b200/lib/liblaic_b200.so   C ABI (include/laic_b200.h) + C++ API (include/laic/*.hpp)
   laicompute_b200/bin/laic_generate     command-line generator (the reference's tools/generate usage)
+  laicompute_b200/bin/laic_server       HTTP API server (the reference's tools/server usage)
 
 Objects go to laicompute_b200/_build/ and are rebuilt only when a source or
 header is newer than them.
@@ -94,10 +95,11 @@ def build(verbose: bool = False) -> str:
         list(ex.map(lambda j: _run(j[2]), jobs))
     if _stale(LIB, objs):
         _run([NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lpthread", "-ldl"])
-    tool = os.path.join(CSRC, "tools", "laic_generate.cpp")
-    if _stale(BIN, [tool, LIB, *hdrs]):
-        _run(["g++", *CXXFLAGS, tool, "-o", BIN, f"-L{os.path.dirname(LIB)}", "-llaic_b200",
-              "-Wl,-rpath,$ORIGIN/../lib"])
+    for tool in sorted(glob.glob(os.path.join(CSRC, "tools", "*.cpp"))):  # laic_generate, laic_server
+        exe = os.path.join(os.path.dirname(BIN), os.path.splitext(os.path.basename(tool))[0])
+        if _stale(exe, [tool, LIB, *hdrs]):
+            _run(["g++", *CXXFLAGS, tool, "-o", exe, f"-L{os.path.dirname(LIB)}", "-llaic_b200",
+                  "-Wl,-rpath,$ORIGIN/../lib", "-lpthread"])
     return LIB
 
 
