@@ -71,6 +71,7 @@ typedef struct laic_dev_desc {
 #define LAIC_FLAG_TRACE 16u     /* the persistent decode-step kernel stamps its phases (laic_dev_step_trace) */
 #define LAIC_FLAG_Q4_0_UPSTREAM 128u /* Q4_0 tensors arrive in upstream ggml's nibble order (elements j and
                                         j+16 share byte j); they are reordered to the reference's at upload */
+#define LAIC_FLAG_NO_SPECULATION 256u /* laic_dev_step never starts the next step ahead (see laic_dev_step) */
 #define LAIC_FLAG_STEP_KERNEL 32u /* one sequence of Q4_0/Q8_0 layers: run each step as the persistent
                                      decode-step kernel where it applies (off by default: per-projection launches
                                      measured faster) */
@@ -138,7 +139,12 @@ LAIC_API int laic_dev_prefill_batch(laic_dev* dev, int32_t slot, const uint32_t*
  * the full forward pass, then the token choice on the device. `params` holds
  * nparams entries (1 = shared by all sequences, else one per sequence).
  * out_ids[nseq] receives the sampled ids; out_logits (nullable, [nseq][vocab])
- * the raw logits step() would return. Advances each slot's position by one. */
+ * the raw logits step() would return. Advances each slot's position by one.
+ * When a call's tokens are the ids the previous call returned (same slots and
+ * sampling parameters), the device starts the following step on those ids
+ * before returning; a next call that sends them again only waits for it, any
+ * other call (or entry point) first undoes it. Results are the same either way;
+ * LAIC_FLAG_NO_SPECULATION turns it off. */
 LAIC_API int laic_dev_step(laic_dev* dev, int32_t nseq, const uint32_t* tokens, const int32_t* slots,
                   const laic_sample_params* params, int32_t nparams, uint32_t* out_ids, float* out_logits);
 

@@ -14,6 +14,7 @@ LAIC_OK = 0
 LAIC_E_INVALID, LAIC_E_CUDA, LAIC_E_NCCL, LAIC_E_CONTEXT, LAIC_E_UNSUPPORTED, LAIC_E_MISSING = -1, -2, -3, -4, -5, -6
 FLAG_NO_GRAPH, FLAG_NO_PDL, FLAG_KV_F32, FLAG_LAYER_LAUNCHES, FLAG_TRACE, FLAG_STEP_KERNEL = 1, 2, 4, 8, 16, 32
 FLAG_Q4_0_UPSTREAM = 128
+FLAG_NO_SPECULATION = 256
 
 # Every entry point include/laic_b200.h declares (checked by the tests).
 EXPORTS = (

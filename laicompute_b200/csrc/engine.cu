@@ -489,7 +489,11 @@ struct Layer {
 enum : unsigned { H_ANORM = 1, H_Q = 2, H_K = 4, H_V = 8, H_O = 16, H_FNORM = 32, H_GATE = 64, H_UP = 128, H_DOWN = 256,
                   H_ALL = 511 };
 
-enum StepMode : int { MODE_PREFILL = 0, MODE_STEP = 1, MODE_CHAIN = 2 };
+// MODE_SPEC0 / MODE_SPEC1: a speculative step of laic_dev_step, inputs like MODE_CHAIN (the
+// previous step's sampled ids, slots and parameters already on the device), outputs like
+// MODE_STEP (ids and error words copied to pinned host memory: buffer 0 or 1, so that the
+// next guess can be queued before this one's outputs are read).
+enum StepMode : int { MODE_PREFILL = 0, MODE_STEP = 1, MODE_CHAIN = 2, MODE_SPEC0 = 3, MODE_SPEC1 = 4 };
 
 }  // namespace
 
@@ -525,6 +529,45 @@ struct laic_dev {
     size_t ls_smem_bytes = 0;
     bool ls_ready = false, ls_checked = false, use_ls = true, force_ls = false, ls_lm = false;
     bool q4_upstream = false;  // Q4_0 uploads arrive in upstream ggml's nibble order
+    // Speculative next step of laic_dev_step: after a step whose tokens were the previous step's
+    // sampled ids (same slots and parameters), one more step runs on the device's own ids while
+    // the host takes its answer; the next call uses it when it brings exactly those tokens again,
+    // else undoes it (positions, repeat-penalty counts, error words) before its own step.
+    bool use_spec = true;
+    bool spec_pending = false;
+    int last_nseq = 0;
+    std::vector<int32_t> last_slots;
+    std::vector<uint32_t> last_ids;      // ids the last step returned: the speculative step's tokens
+    std::vector<laic::SampleDev> last_params;
+    int spec_buf = 0;                    // host output buffer of the pending guess
+    cudaEvent_t spec_ev[2] = {nullptr, nullptr};  // recorded after the guess writing buffer 0 / 1
+    int* d_spec = nullptr;               // [2][max_seqs]: tokens and positions to restore on a rollback
+    int* h_spec = nullptr;               // pinned staging of the same
+
+    // Wait for a pending speculative step and undo it (the caller is about to change the state it
+    // assumed). No-op without one.
+    int spec_cancel() {
+        if (!spec_pending) return LAIC_OK;
+        spec_pending = false;
+        CK(cudaStreamSynchronize(st));
+        const int n = last_nseq;
+        for (int i = 0; i < n; ++i) {
+            h_spec[i] = (int)last_ids[i];
+            h_spec[S + i] = (int)h_pos[last_slots[i]];
+        }
+        CK(cudaMemcpyAsync(d_spec, h_spec, 2 * S * sizeof(int), cudaMemcpyHostToDevice, st));
+        CK(cudaMemcpyAsync(d_slots, last_slots.data(), n * sizeof(int), cudaMemcpyHostToDevice, st));
+        laic::unstep_kernel<<<1, 256, 0, st>>>(d_slots, (const unsigned*)d_spec, d_spec + S, pos, counts, V, n);
+        CK(cudaGetLastError());
+        CK(cudaMemsetAsync(mvs.err, 0, 4, st));  // the discarded step's wait or sampler errors are not the caller's
+        CK(cudaMemsetAsync(d_err, 0, 4, st));
+        CK(cudaStreamSynchronize(st));
+        const bool waits_failed = h_err[2 * spec_buf] != 0;
+        h_err[0] = h_err[1] = h_err[2] = h_err[3] = 0;
+        if (waits_failed)
+            if (int rc = ls_reset()) return rc;  // a failed wait may have left the step kernel's counters part-way
+        return LAIC_OK;
+    }
     unsigned long long* ls_trace = nullptr;  // LAIC_FLAG_TRACE: per-phase stamps of the last step kernel
     bool trace_on = false;
     // more than 16 sequences on one GPU: binary16 hi/lo activation records written by the producing
@@ -561,7 +604,7 @@ struct laic_dev {
     size_t hist_cap = 0;  // entries of d_hist
     laic::SampleDev* d_params = nullptr;
     unsigned *h_tokens = nullptr, *h_out_ids = nullptr;
-    int* h_err = nullptr;  // pinned: the step's copies of the two device error flags (matvec waits, sampler)
+    int* h_err = nullptr;  // pinned [2][2]: a step's copies of the two device error flags (matvec waits, sampler)
     float* samp_v = nullptr;  // sampler slices: [S][kSampleSlices] maxima, ids and per-sequence tickets
     int* samp_i = nullptr;
     unsigned* samp_cnt = nullptr;
@@ -707,7 +750,7 @@ struct laic_dev {
         auto t_end = [&]() {
             if (timer) cudaEventRecord(timer->ev.back().second.second, s);
         };
-        if (mode != MODE_CHAIN) {  // a chained step reads the ids the previous step sampled
+        if (mode == MODE_PREFILL || mode == MODE_STEP) {  // chained / speculative steps read the ids the previous step sampled
             CK(cudaMemcpyAsync(d_tokens, h_tokens, nseq * sizeof(unsigned), cudaMemcpyHostToDevice, s));
             CK(cudaMemcpyAsync(d_slots, h_slots, nseq * sizeof(int), cudaMemcpyHostToDevice, s));
             if (full) CK(cudaMemcpyAsync(d_params, h_params, nseq * sizeof(laic::SampleDev), cudaMemcpyHostToDevice, s));
@@ -881,9 +924,10 @@ struct laic_dev {
                 ++nl;
             } else {
                 // the sampled ids and both error flags come back with the step (no extra round trip)
-                CK(cudaMemcpyAsync(h_out_ids, d_out_ids, nseq * sizeof(unsigned), cudaMemcpyDeviceToHost, s));
-                CK(cudaMemcpyAsync(h_err, mvs.err, 4, cudaMemcpyDeviceToHost, s));
-                CK(cudaMemcpyAsync(h_err + 1, d_err, 4, cudaMemcpyDeviceToHost, s));
+                const int ob = mode == MODE_SPEC1 ? 1 : 0;  // host output buffer
+                CK(cudaMemcpyAsync(h_out_ids + (size_t)ob * S, d_out_ids, nseq * sizeof(unsigned), cudaMemcpyDeviceToHost, s));
+                CK(cudaMemcpyAsync(h_err + 2 * ob, mvs.err, 4, cudaMemcpyDeviceToHost, s));
+                CK(cudaMemcpyAsync(h_err + 2 * ob + 1, d_err, 4, cudaMemcpyDeviceToHost, s));
             }
         } else {
             t_begin("advance", 0);
@@ -1233,6 +1277,7 @@ int laic_dev_create(const laic_dev_desc* desc, const laic_dev_opts* opts, laic_d
     d->use_ls = (o.flags & LAIC_FLAG_LAYER_LAUNCHES) == 0;
     d->force_ls = (o.flags & LAIC_FLAG_STEP_KERNEL) != 0;
     d->q4_upstream = (o.flags & LAIC_FLAG_Q4_0_UPSTREAM) != 0;
+    d->use_spec = (o.flags & LAIC_FLAG_NO_SPECULATION) == 0;
     d->trace_on = (o.flags & LAIC_FLAG_TRACE) != 0;
     d->layers.resize(a.layers);
     d->h_pos.assign(o.max_seqs, 0);
@@ -1310,9 +1355,13 @@ int laic_dev_create(const laic_dev_desc* desc, const laic_dev_opts* opts, laic_d
     CK(cudaMalloc(&d->d_hist_count, 4));
     CK(cudaMalloc(&d->d_params, S * sizeof(laic::SampleDev)));
     CK(cudaMallocHost(&d->h_tokens, S * 4));
-    CK(cudaMallocHost(&d->h_out_ids, S * 4));
-    CK(cudaMallocHost(&d->h_err, 2 * sizeof(int)));
-    d->h_err[0] = d->h_err[1] = 0;
+    CK(cudaMallocHost(&d->h_out_ids, 2 * S * 4));
+    CK(cudaMallocHost(&d->h_err, 4 * sizeof(int)));
+    CK(cudaEventCreateWithFlags(&d->spec_ev[0], cudaEventDisableTiming));
+    CK(cudaEventCreateWithFlags(&d->spec_ev[1], cudaEventDisableTiming));
+    CK(cudaMallocHost(&d->h_spec, 2 * (size_t)o.max_seqs * sizeof(int)));
+    CK(cudaMalloc(&d->d_spec, 2 * (size_t)o.max_seqs * sizeof(int)));
+    d->h_err[0] = d->h_err[1] = d->h_err[2] = d->h_err[3] = 0;
     CK(cudaMallocHost(&d->h_slots, S * 4));
     CK(cudaMallocHost(&d->h_params, S * sizeof(laic::SampleDev)));
     if (tp > 1) {
@@ -1333,6 +1382,7 @@ void laic_dev_destroy(laic_dev* d) {
     if (!d) return;
     cudaSetDevice(d->device);
     cudaStreamSynchronize(d->st);
+    for (cudaEvent_t ev : d->spec_ev) if (ev) cudaEventDestroy(ev);
     for (auto& kv : d->graphs) cudaGraphExecDestroy(kv.second);  // graphs holding NCCL calls go first
     d->graphs.clear();
     for (int q = 0; q < d->tp && d->ar_p2p; ++q) {
@@ -1354,8 +1404,9 @@ void laic_dev_destroy(laic_dev* d) {
                     d->d_hist, d->d_hist_count, d->logits_l, d->logits_g, d->rec_x, d->rec_act, d->rec_ss, d->rec_attn,
                     d->ar_box, d->ar_flags, d->ar_ctr,
                     d->pf_x, d->pf_c, d->pf_q, d->pf_attn, d->pf_a, d->pf_w, d->pf_slots, d->pf_npos, d->pf_tokens,
-                    d->pf_ws, d->samp_v, d->samp_i, d->samp_cnt};
+                    d->pf_ws, d->samp_v, d->samp_i, d->samp_cnt, d->d_spec};
     for (void* b : bufs) if (b) cudaFree(b);
+    if (d->h_spec) cudaFreeHost(d->h_spec);
     void* hb[] = {d->h_tokens, d->h_out_ids, d->h_slots, d->h_params, d->h_err};
     for (void* b : hb) if (b) cudaFreeHost(b);
     if (d->st) cudaStreamDestroy(d->st);
@@ -1366,6 +1417,7 @@ int laic_dev_upload(laic_dev* d, const char* cname, int32_t type, const uint64_t
                     const void* data, size_t nbytes) {
     if (!d || !cname || !shape || !data) return fail(LAIC_E_INVALID, "null argument");
     CK(cudaSetDevice(d->device));
+    if (int rc_ = d->spec_cancel()) return rc_;  // (a pending speculative step assumed the old state)
     const std::string name(cname);
     size_t n = 1;
     for (int i = 0; i < ndim; ++i) n *= shape[i];
@@ -1483,6 +1535,7 @@ int laic_dev_prefill_batch(laic_dev* d, int32_t slot, const uint32_t* tokens, in
     if (n < 0) return fail(LAIC_E_INVALID, "negative token count");
     if (n == 0) return LAIC_OK;
     CK(cudaSetDevice(d->device));
+    if (int rc_ = d->spec_cancel()) return rc_;  // (a pending speculative step assumed the old state)
     if (slot < 0 || slot >= d->S) return fail(LAIC_E_INVALID, "slot out of range");
     std::string missing;
     if (!d->ready(missing)) return fail(LAIC_E_MISSING, "missing tensor: " + missing);
@@ -1504,6 +1557,7 @@ int laic_dev_prefill_batch(laic_dev* d, int32_t slot, const uint32_t* tokens, in
 int laic_dev_prefill(laic_dev* d, int32_t nseq, const uint32_t* tokens, const int32_t* slots) {
     if (!d) return fail(LAIC_E_INVALID, "null device");
     CK(cudaSetDevice(d->device));
+    if (int rc_ = d->spec_cancel()) return rc_;  // (a pending speculative step assumed the old state)
     int rc = fill_inputs(d, nseq, tokens, slots);
     if (rc) return rc;
     if ((rc = d->run(nseq, MODE_PREFILL))) return rc;
@@ -1544,17 +1598,17 @@ static std::string wait_error_text(int code) {
 }
 
 // After a synchronised MODE_STEP run: the error flags its graph copied to pinned memory.
-static int check_step_err(laic_dev* d) {
-    const int mv_err = d->h_err[0], sample_err = d->h_err[1];
+static int check_step_err(laic_dev* d, int buf = 0) {
+    const int mv_err = d->h_err[2 * buf], sample_err = d->h_err[2 * buf + 1];
     if (mv_err) {
         CK(cudaMemset(d->mvs.err, 0, 4));
-        d->h_err[0] = 0;
+        d->h_err[2 * buf] = 0;
         if (int rc = d->ls_reset()) return rc;
         return fail(LAIC_E_CUDA, wait_error_text(mv_err));
     }
     if (sample_err) {
         CK(cudaMemset(d->d_err, 0, 4));
-        d->h_err[1] = 0;
+        d->h_err[2 * buf + 1] = 0;
         return fail(LAIC_E_UNSUPPORTED, "sampling request needs more than 1024 candidates (top_k or top_p mass)");
     }
     return LAIC_OK;
@@ -1583,21 +1637,70 @@ int laic_dev_step(laic_dev* d, int32_t nseq, const uint32_t* tokens, const int32
     if (!d) return fail(LAIC_E_INVALID, "null device");
     CK(cudaSetDevice(d->device));
     int rc = fill_inputs(d, nseq, tokens, slots);
-    if (rc) return rc;
-    if ((rc = fill_params(d, nseq, params, nparams))) return rc;
-    if ((rc = d->run(nseq, MODE_STEP))) return rc;
-    if (out_logits)
-        CK(cudaMemcpyAsync(out_logits, d->logits, (size_t)nseq * d->V * 4, cudaMemcpyDeviceToHost, d->st));
-    CK(cudaStreamSynchronize(d->st));
+    if (rc == LAIC_OK) rc = fill_params(d, nseq, params, nparams);
+    if (rc) {
+        if (int rc2 = d->spec_cancel()) return rc2;
+        return rc;
+    }
+    // this call feeds back the previous step's sampled ids (same slots and parameters)?
+    bool feedback = nseq == d->last_nseq;
+    for (int i = 0; feedback && i < nseq; ++i) {
+        const laic::SampleDev &a = d->h_params[i], &b = d->last_params[i];
+        feedback = slots[i] == d->last_slots[i] && tokens[i] == d->last_ids[i] && a.temperature == b.temperature &&
+                   a.top_k == b.top_k && a.top_p == b.top_p && a.repeat_penalty == b.repeat_penalty && a.u == b.u;
+    }
+    // room for a further guess after this step: every slot one position below the capacity
+    bool room = true;
+    for (int i = 0; i < nseq; ++i) room = room && d->h_pos[slots[i]] + 1 < d->cap;
+    const bool guess = d->use_spec && feedback && d->tp == 1;
+    int buf = 0;  // host output buffer of this call's step
+    if (d->spec_pending && feedback) {
+        // the pending guess is this call's step: queue the following guess behind it before
+        // waiting, so the stream never drains while the caller keeps feeding back its ids
+        d->spec_pending = false;
+        buf = d->spec_buf;
+        if (out_logits)  // (in stream order, before the next guess overwrites them)
+            CK(cudaMemcpyAsync(out_logits, d->logits, (size_t)nseq * d->V * 4, cudaMemcpyDeviceToHost, d->st));
+        const bool next = guess && room;
+        if (next) {
+            if ((rc = d->run(nseq, buf ? MODE_SPEC0 : MODE_SPEC1))) return rc;
+            CK(cudaEventRecord(d->spec_ev[buf ^ 1], d->st));
+        }
+        CK(cudaEventSynchronize(d->spec_ev[buf]));
+        d->spec_pending = next;
+        d->spec_buf = buf ^ 1;
+    } else {
+        if ((rc = d->spec_cancel())) return rc;
+        if ((rc = d->run(nseq, MODE_STEP))) return rc;
+        if (out_logits)
+            CK(cudaMemcpyAsync(out_logits, d->logits, (size_t)nseq * d->V * 4, cudaMemcpyDeviceToHost, d->st));
+        CK(cudaStreamSynchronize(d->st));
+        if (guess && room) {  // the first guess of a feedback loop (buffer 1: this step's outputs are in 0)
+            if ((rc = d->run(nseq, MODE_SPEC1))) return rc;
+            CK(cudaEventRecord(d->spec_ev[1], d->st));
+            d->spec_pending = true;
+            d->spec_buf = 1;
+        }
+    }
     for (int i = 0; i < nseq; ++i) d->h_pos[slots[i]] += 1;
-    if ((rc = check_step_err(d))) return rc;
-    if (out_ids) std::memcpy(out_ids, d->h_out_ids, nseq * 4);
+    if ((rc = check_step_err(d, buf))) {
+        if (int rc2 = d->spec_cancel()) return rc2;  // (the guess behind a failed step is not kept)
+        d->last_nseq = 0;
+        return rc;
+    }
+    const unsigned* ids = d->h_out_ids + (size_t)buf * d->S;
+    d->last_nseq = nseq;
+    d->last_slots.assign(slots, slots + nseq);
+    d->last_ids.assign(ids, ids + nseq);
+    d->last_params.assign(d->h_params, d->h_params + nseq);
+    if (out_ids) std::memcpy(out_ids, ids, nseq * 4);
     return LAIC_OK;
 }
 
 int laic_dev_reset_slot(laic_dev* d, int32_t slot) {
     if (!d || slot < 0 || slot >= d->S) return fail(LAIC_E_INVALID, "slot out of range");
     CK(cudaSetDevice(d->device));
+    if (int rc_ = d->spec_cancel()) return rc_;  // (a pending speculative step assumed the old state)
     CK(cudaStreamSynchronize(d->st));
     CK(cudaMemset(d->pos + slot, 0, 4));
     CK(cudaMemset(d->counts + (size_t)slot * d->V, 0, (size_t)d->V * 4));
@@ -1615,6 +1718,7 @@ int laic_dev_fill_kv(laic_dev* d, int32_t slot, int32_t npos, uint64_t seed) {
     if (!d || slot < 0 || slot >= d->S) return fail(LAIC_E_INVALID, "slot out of range");
     if (npos < 0 || npos > d->cap) return fail(LAIC_E_CONTEXT, "context length exceeded");
     CK(cudaSetDevice(d->device));
+    if (int rc_ = d->spec_cancel()) return rc_;  // (a pending speculative step assumed the old state)
     if (npos > 0) {
         const long long slot_off = (long long)slot * d->kv_slot_stride;
         if (d->kv32)
@@ -1661,6 +1765,7 @@ int laic_dev_decode(laic_dev* d, int32_t nseq, const uint32_t* tokens, const int
     if (!d) return fail(LAIC_E_INVALID, "null device");
     if (steps < 1 || !out_ids) return fail(LAIC_E_INVALID, "steps must be >= 1 and out_ids non-null");
     CK(cudaSetDevice(d->device));
+    if (int rc_ = d->spec_cancel()) return rc_;  // (a pending speculative step assumed the old state)
     int rc = fill_inputs(d, nseq, tokens, slots);
     if (rc) return rc;
     for (int i = 0; i < nseq; ++i)
@@ -1702,6 +1807,7 @@ int laic_dev_profile(laic_dev* d, int32_t nseq, const uint32_t* tokens, int32_t 
                      int32_t max_out, int32_t* n_out) {
     if (!d || !tokens || steps < 1 || !out || !n_out) return fail(LAIC_E_INVALID, "bad argument");
     CK(cudaSetDevice(d->device));
+    if (int rc_ = d->spec_cancel()) return rc_;  // (a pending speculative step assumed the old state)
     std::vector<int32_t> slots(nseq);
     for (int i = 0; i < nseq; ++i) slots[i] = i;
     std::vector<laic_kernel_record> recs;
@@ -1748,6 +1854,7 @@ int laic_dev_step_trace(laic_dev* d, uint64_t* out, int64_t max_entries, int64_t
     if (!d->ls_trace) return fail(LAIC_E_INVALID, "no step trace: create the engine with LAIC_FLAG_TRACE "
                                                "and run a one-sequence step on the persistent kernel");
     CK(cudaSetDevice(d->device));
+    if (int rc_ = d->spec_cancel()) return rc_;  // (a pending speculative step assumed the old state)
     CK(cudaStreamSynchronize(d->st));
     const int64_t total = (int64_t)num_sms() * laic::ls_phases(d->L) * laic::ls_trace_stamps() +
                           (int64_t)num_sms() * laic::ls_trace_warp_words();

@@ -87,6 +87,16 @@ __global__ void gather_logits_kernel(const float* g, float* out, int ranks, int 
 }
 
 // End of a prefill step (no sampler): every listed slot moves to the next position.
+// Undo a discarded speculative step's bookkeeping: each listed slot's position back to `pos_to`
+// and one history count of the token its embedding counted (repeat penalty) taken off.
+__global__ void unstep_kernel(const int* slots, const unsigned* toks, const int* pos_to, int* pos, unsigned* counts,
+                              int vocab, int nseq) {
+    for (int i = threadIdx.x; i < nseq; i += blockDim.x) {
+        pos[slots[i]] = pos_to[i];
+        atomicSub(counts + (size_t)slots[i] * vocab + toks[i], 1u);
+    }
+}
+
 __global__ void advance_pos_kernel(const int* slots, int* pos, int nseq) {
     pdl_wait();
     for (int s = threadIdx.x; s < nseq; s += blockDim.x) pos[slots[s]] += 1;

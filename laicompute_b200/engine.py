@@ -13,7 +13,7 @@ import numpy as np
 
 from . import gguf
 from ._native import (DevDesc, DevOpts, DevStats, FLAG_KV_F32, FLAG_NO_GRAPH, FLAG_NO_PDL, FLAG_LAYER_LAUNCHES, FLAG_TRACE,
-                      FLAG_STEP_KERNEL, FLAG_Q4_0_UPSTREAM, KernelRecord, SampleParams,
+                      FLAG_STEP_KERNEL, FLAG_Q4_0_UPSTREAM, FLAG_NO_SPECULATION, KernelRecord, SampleParams,
                       check, lib)
 
 
@@ -38,10 +38,12 @@ class Engine:
     def __init__(self, path: str, max_seqs: int = 1, kv_capacity: int = 0, device: int = 0, kv_f32: bool = False,
                  graphs: bool = True, pdl: bool = True, tp_size: int = 1, tp_rank: int = 0,
                  nccl_id: Optional[bytes] = None, layer_launches: bool = False, trace: bool = False,
-                 step_kernel: Optional[bool] = None, q4_0_upstream: bool = False) -> None:
+                 step_kernel: Optional[bool] = None, q4_0_upstream: bool = False,
+                 speculate: bool = True) -> None:
         """`step_kernel`: True runs one-sequence Q4_0/Q8_0 steps as the persistent decode-step kernel, False
         (or `layer_launches`) and None (the default) launch per projection. `q4_0_upstream`: the file's Q4_0
-        tensors use upstream ggml's nibble order (llama.cpp's files) rather than the reference's."""
+        tensors use upstream ggml's nibble order (llama.cpp's files) rather than the reference's. `speculate`:
+        step() starts the next step on its own sampled ids while the caller decides (laic_dev_step)."""
         L = lib()
         if step_kernel is False:
             layer_launches = True
@@ -49,7 +51,8 @@ class Engine:
         self.desc = desc_from_gguf(self.file)
         flags = ((FLAG_KV_F32 if kv_f32 else 0) | (0 if graphs else FLAG_NO_GRAPH) | (0 if pdl else FLAG_NO_PDL)
                  | (FLAG_LAYER_LAUNCHES if layer_launches else 0) | (FLAG_TRACE if trace else 0)
-                 | (FLAG_STEP_KERNEL if step_kernel else 0) | (FLAG_Q4_0_UPSTREAM if q4_0_upstream else 0))
+                 | (FLAG_STEP_KERNEL if step_kernel else 0) | (FLAG_Q4_0_UPSTREAM if q4_0_upstream else 0)
+                 | (0 if speculate else FLAG_NO_SPECULATION))
         self._nccl_id = ctypes.create_string_buffer(nccl_id, 128) if nccl_id else None
         opts = DevOpts(device=device, max_seqs=max_seqs, kv_capacity=kv_capacity, tp_size=tp_size, tp_rank=tp_rank,
                        nccl_id=ctypes.cast(self._nccl_id, ctypes.c_void_p) if self._nccl_id else None, flags=flags)
