@@ -597,17 +597,23 @@ __device__ __forceinline__ void attn_mma_body(const AttnParams& p, int split, in
         //      is split j; each CTA merges every nsplit-th slice of the elements
         namespace cg = cooperative_groups;
         cg::cluster_group cluster = cg::this_cluster();
-        __shared__ float cw[kAttnMaxCluster][8], cLs[8];
+        __shared__ float cw[kAttnMaxCluster][8], cLs[8], rM[kAttnMaxCluster][8], rL[kAttnMaxCluster][8];
         cluster.sync();  // every partial is written
+        // every split's (max, sum) per head in one round of remote loads, one thread per pair
+        if (tid < active * G) {
+            const int j = tid / G, g = tid % G;
+            rM[j][g] = *cluster.map_shared_rank(&cpM[g], j);
+            rL[j][g] = *cluster.map_shared_rank(&cpL[g], j);
+        }
+        gsync();
         if (tid < G) {
             const int g = tid;
             float M = -INFINITY, L = 0.f;
-            for (int j = 0; j < active; ++j) M = fmaxf(M, *cluster.map_shared_rank(&cpM[g], j));
+            for (int j = 0; j < active; ++j) M = fmaxf(M, rM[j][g]);
             for (int j = 0; j < active; ++j) {
-                const float mj = *cluster.map_shared_rank(&cpM[g], j);
-                const float e = mj == -INFINITY ? 0.f : expf(mj - M);
+                const float e = rM[j][g] == -INFINITY ? 0.f : expf(rM[j][g] - M);
                 cw[j][g] = e;
-                L = fmaf(*cluster.map_shared_rank(&cpL[g], j), e, L);
+                L = fmaf(rL[j][g], e, L);
             }
             cLs[g] = L;
         }
@@ -617,8 +623,14 @@ __device__ __forceinline__ void attn_mma_body(const AttnParams& p, int split, in
             const bool in = i < G * D;
             const int g = in ? i / D : 0;
             float A = 0.f;
-            if (in)
-                for (int j = 0; j < active; ++j) A = fmaf(*cluster.map_shared_rank(&cpart[i], j), cw[j][g], A);
+            if (in) {
+                float v[kAttnMaxCluster];  // the splits' partials, loaded together, added in split order
+#pragma unroll
+                for (int j = 0; j < kAttnMaxCluster; ++j) v[j] = j < active ? *cluster.map_shared_rank(&cpart[i], j) : 0.f;
+#pragma unroll
+                for (int j = 0; j < kAttnMaxCluster; ++j)
+                    if (j < active) A = fmaf(v[j], cw[j][g], A);
+            }
             attn_emit(p, seq, kvh * G * D + i, A / cLs[g], in);
         }
         cluster.sync();  // no CTA leaves while the others may still read its partial
