@@ -428,6 +428,7 @@ cudaError_t launch_matvec(const Mat& m, laic::MvParams p, int epi, bool kv32, co
         if (rin && rin->xg && rin->dp && sh.nt == 0) {
             p.xg = rin->xg; p.scale_mode = rin->mode; p.ss = rin->ss; p.ss_tiles = rin->ss_tiles; p.ss_n = m.in;
         }
+        laic::sk_split(p, sh.grid, sh.warps);
         if (launches) *launches += 1;
         return laic::mv_sk_launch(m.type, sh.nt, epi, kv32, p, sh.grid, sh.smem, st, pdl, sh.warps);
     }

@@ -79,6 +79,11 @@ struct MvParams {
     // (scale_mode, ss, ss_tiles, ss_n as above) and `rec_out` receives them for the next
     // projection, whose weight type is rec_type (T_Q4_0 or T_Q8_0)
     int rec_type;
+    // team kernel: its split, computed on the host (the kernel takes no divisions): warps per
+    // team, teams per CTA and ceil(65536 / team_k) (warp / team_k = warp * team_inv >> 16);
+    // tiles per CTA (tq, one more in the first tr CTAs) and blocks per warp's slice of a tile
+    // (sq, one more for the first sr warps of a team)
+    int team_k, team_n, team_inv, tq, tr, sq, sr;
 };
 
 // Activation records (the tile and wide kernels' B operands): per GGUF block column bl

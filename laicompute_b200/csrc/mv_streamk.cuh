@@ -64,6 +64,38 @@ __host__ __device__ inline int sk_team(int nb, int w = kSkWarps) {
     const int k = nb >= 256 ? 16 : nb >= 128 ? 8 : nb >= 64 ? 4 : nb >= 32 ? 2 : 1;
     return k < sk_max_team(w) ? k : sk_max_team(w);
 }
+// Rough cost of one warp's work with teams of k warps, in eighths of a tile-block: the
+// rounds of tiles its team takes (a CTA owns ceil(ntiles / grid) whole tiles), each a
+// slice of ceil(nb / k) blocks plus the team's merge (about k / 8 blocks).
+__host__ __device__ inline int sk_team_cost(int k, int nb, int ntiles, int grid, int w) {
+    const int tpc = (ntiles + grid - 1) / grid, teams = w / k;
+    return (tpc + teams - 1) / teams * (8 * ((nb + k - 1) / k) + k);
+}
+// Team size of a launch: sk_team, or a larger divisor of w that cuts the cost by more
+// than 10 % (few tiles per CTA leave teams idle: the 4096-row projections of an 8B-shaped
+// model own one or two tiles per CTA), keeping at least two blocks per warp.
+__host__ __device__ inline int sk_team_for(int nb, int ntiles, int grid, int w) {
+    int k = sk_team(nb, w);
+    int best = sk_team_cost(k, nb, ntiles, grid, w);
+    for (int kk = k + 1; kk <= w; ++kk) {
+        if (w % kk != 0 || 2 * kk > nb) continue;
+        const int c = sk_team_cost(kk, nb, ntiles, grid, w);
+        if (10 * c < 9 * best) { best = c; k = kk; }
+    }
+    return k;
+}
+// The team kernel's split of a launch (grid CTAs of w warps) into MvParams: teams of
+// sk_team_for warps, whole tiles per CTA, equal K slices per warp of a team.
+inline void sk_split(MvParams& p, int grid, int w) {
+    const int k = sk_team_for(p.nb, p.ntiles, grid, w);
+    p.team_k = k;
+    p.team_n = w / k;
+    p.team_inv = (65536 + k - 1) / k;  // exact for warp indices below 64
+    p.tq = p.ntiles / grid;
+    p.tr = p.ntiles % grid;
+    p.sq = p.nb / k;
+    p.sr = p.nb % k;
+}
 
 // tickets, merged-tile marks, per-warp statistics, 1/rms and split scale per sequence
 __host__ __device__ inline size_t sk_small_bytes(int B, int w = kSkWarps) {
@@ -381,12 +413,12 @@ __global__ void __launch_bounds__(W * 32, 1) mv_sk_kernel(const MvParams p) {
     float* xsc = inv + B;                                                // [B] power-of-two split scale
     uint64_t* bars = reinterpret_cast<uint64_t*>(small + sk_small_bytes(B, W)) + warp * R;
 
-    // this CTA's tiles, this warp's team and K slice
-    const int k = sk_team(nb, W);
-    const int teams = W / k, team = warp / k, wi = warp % k, leader = team * k;
-    const int t_lo = (int)((long long)blockIdx.x * p.ntiles / gridDim.x);
-    const int t_hi = (int)((long long)(blockIdx.x + 1) * p.ntiles / gridDim.x);
-    const int b_lo = wi * nb / k, b_hi = (wi + 1) * nb / k;  // slice of every tile
+    // this CTA's tiles, this warp's team and K slice (sk_split: the host's arithmetic)
+    const int k = p.team_k, teams = p.team_n;
+    const int team = (warp * p.team_inv) >> 16, wi = warp - team * k, leader = team * k;
+    const int cta = blockIdx.x;
+    const int t_lo = cta * p.tq + min(cta, p.tr), t_hi = t_lo + p.tq + (cta < p.tr ? 1 : 0);
+    const int b_lo = wi * p.sq + min(wi, p.sr), b_hi = b_lo + p.sq + (wi < p.sr ? 1 : 0);  // slice of every tile
     const int slice = b_hi - b_lo;
     const int st_per_tile = (slice + KB - 1) / KB;
     int my_tiles = 0;
