@@ -21,7 +21,6 @@
 
 #include "common.cuh"
 #include "mma_matvec.cuh"  // smem_u32, mma16816
-#include "mv_streamk.cuh"  // dp_lane_record_rt
 
 namespace laic {
 
@@ -47,8 +46,6 @@ struct AttnParams {
     const int* npos;           // optional: per query row, its position (batched prefill: causal per row)
     int nbuf;                  // chunk buffers in shared memory (0 or 1: one); a split takes at most
                                // this many chunks when nsplit allows, all fetched before the dependency wait
-    uint8_t* rec_dp;           // optional, one sequence: the team kernel's integer records of `out`
-    int rec_type;              //   for a projection of this weight type (T_Q4_0 or T_Q8_0)
 };
 
 // out[seq][e] = v, plus its activation record when requested.
@@ -56,11 +53,9 @@ __device__ __forceinline__ void attn_store(const AttnParams& p, int seq, int e, 
     p.out[(size_t)seq * p.ldo + e] = v;
     if (p.rec_out) store_act_record(p.rec_out, p.nseq, e, seq, v);
 }
-// attn_store where `live`, plus the integer records (one sequence) when requested: every
-// lane of the warp calls it, lanes 8j..8j+7 with the eight elements of one 8-column group.
+// attn_store where `live` (every lane of the warp calls it).
 __device__ __forceinline__ void attn_emit(const AttnParams& p, int seq, int e, float v, bool live) {
     if (live) attn_store(p, seq, e, v);
-    if (p.rec_dp) dp_lane_record_rt(p.rec_type, live ? v : 0.f, 0.f, e & 7, live ? e >> 3 : -1, p.rec_dp, 1, 2, 4);
 }
 
 template <typename KV, int N> struct KvLoad;

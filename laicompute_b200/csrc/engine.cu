@@ -425,8 +425,8 @@ cudaError_t launch_matvec(const Mat& m, laic::MvParams p, int epi, bool kv32, co
     p.q = m.q; p.s = m.s; p.rows = m.rows; p.ntiles = m.ntiles; p.in = m.in; p.nb = m.nb;
     if (sh.sk) {
         p.err = sc.err;
-        if (rin && rin->xg && rin->dp && sh.nt == 0) {
-            p.xg = rin->xg; p.scale_mode = rin->mode; p.ss = rin->ss; p.ss_tiles = rin->ss_tiles; p.ss_n = m.in;
+        if (rin && rin->dp && sh.nt == 0) {  // records from x, the rmsnorm scale from the partial sums
+            p.scale_mode = rin->mode; p.ss = rin->ss; p.ss_tiles = rin->ss_tiles; p.ss_n = m.in;
         }
         laic::sk_split(p, sh.grid, sh.warps);
         if (launches) *launches += 1;
@@ -759,8 +759,9 @@ struct laic_dev {
 
         const bool step_path = nseq == 1 && ls_ready;
         const bool recs = !step_path && tile_step(nseq) && rec_x;  // records travel between the tile-kernel projections
-        // one sequence on the team kernel's integer variant: each producing epilogue (embedding,
-        // attention, o, gate/up, down) writes the next projection's digit records
+        // one sequence on the team kernel's integer variant: each projection builds its digit
+        // records from x; the producers of an rmsnorm input (embedding, o, down) write the
+        // partial sums of squares its 1/rms comes from
         auto dp_mat = [](const Mat& m) {
             if (m.type != T_Q4_0 && m.type != T_Q8_0) return false;
             const MvShape sh = mv_shape(m, 1);
@@ -776,9 +777,7 @@ struct laic_dev {
         if (recs) { ep.rec_out = rec_x; ep.rec_w = layers[0].attn_norm; ep.ss_out = rec_ss; }
         // one sequence with integer records: the row in slices of 256 over several CTAs
         const int ecta = dprecs && L > 0 ? std::max(1, std::min(16, h / 256)) : 1;
-        if (dprecs && L > 0) {
-            ep.rec_dp = rec_x; ep.rec_w = layers[0].attn_norm; ep.ss_out = rec_ss; ep.rec_type = layers[0].qkv.type;
-        }
+        if (dprecs && L > 0) ep.ss_out = rec_ss;
         if (!step_path) {
             t_begin("embed", 0);
             CK(launch_k(laic::embed_kernel, dim3(nseq, ecta), dim3(256), 0, s, pdl, ep));
@@ -832,7 +831,6 @@ struct laic_dev {
             ap.heads = H; ap.kv_heads = Hkv; ap.slots = d_slots; ap.pos = pos; ap.nsplit = nsplit;
             ap.part = attn_part; ap.counters = attn_cnt; ap.sqrt_d = sqrtf((float)D); ap.err = mvs.err;
             ap.nseq = nseq; ap.rec_out = recs ? rec_attn : nullptr; ap.nbuf = attn_nbuf(nseq);
-            if (dprecs) { ap.rec_dp = rec_attn; ap.rec_type = ly.o.type; }
             t_begin("attention", attn_bytes);
             if (attn_cluster(nsplit, kv32))
                 CK(laic::launch_cluster_k(attn_pick(D, G, kv32, true), dim3(nsplit, Hkv, nseq), dim3(laic::kAttnWarps * 32),
@@ -846,9 +844,10 @@ struct laic_dev {
             laic::MvParams po{};
             po.nseq = nseq; po.x = attn; po.ldx = hq; po.out = x; po.ldo = h;
             RecIn r_o;
-            if (recs || dprecs) {
+            if (recs) {
                 po.rec_out = rec_x; po.rec_w = ly.ffn_norm; po.ss_out = rec_ss; r_o.xg = rec_attn; r_o.mode = 2;
-                po.rec_type = ly.gu.type; r_o.dp = dprecs;
+            } else if (dprecs) {
+                po.ss_out = rec_ss; r_o.mode = 2; r_o.dp = true;
             }
             t_begin("o", (double)ly.o.bytes() + 4.0 * nseq * hq + 8.0 * nseq * h);
             CK(launch_matvec(ly.o, po, residual_epi, kv32, mvs, s, pdl, &nl, &r_o, !recs));
@@ -859,8 +858,8 @@ struct laic_dev {
             pg.nseq = nseq; pg.eps = a.rms_eps; pg.x = x; pg.ldx = h; pg.norm_w = ly.ffn_norm; pg.out = act; pg.ldo = F;
             RecIn r_gu;
             if (recs || dprecs) {
-                r_gu.xg = rec_x; r_gu.mode = 1; r_gu.ss = rec_ss; r_gu.ss_tiles = ntiles_h; pg.rec_out = rec_act;
-                pg.rec_type = ly.down.type; r_gu.dp = dprecs;
+                r_gu.xg = rec_x; r_gu.mode = 1; r_gu.ss = rec_ss; r_gu.ss_tiles = ntiles_h; r_gu.dp = dprecs;
+                if (recs) pg.rec_out = rec_act;
             }
             t_begin("gate_up", (double)ly.gu.bytes() + 4.0 * nseq * (h + F));
             CK(launch_matvec(ly.gu, pg, laic::EPI_SWIGLU, kv32, mvs, s, pdl, &nl, &r_gu, !recs));
@@ -871,11 +870,10 @@ struct laic_dev {
             RecIn r_dn;
             if (recs || dprecs) {
                 r_dn.xg = rec_act; r_dn.mode = 2; r_dn.dp = dprecs;
-                pd.rec_out = rec_x; pd.ss_out = rec_ss;
-                pd.rec_w = l + 1 < L ? layers[l + 1].attn_norm : out_norm;  // next: QKV, or the lm_head
-                if (dprecs) {
-                    pd.rec_type = l + 1 < L ? layers[l + 1].qkv.type : lm_head().type;
-                    if (l + 1 == L && !dp_lm) pd.rec_out = nullptr;  // the lm_head normalises x itself
+                pd.ss_out = rec_ss;
+                if (recs) {
+                    pd.rec_out = rec_x;
+                    pd.rec_w = l + 1 < L ? layers[l + 1].attn_norm : out_norm;  // next: QKV, or the lm_head
                 }
             }
             t_begin("down", (double)ly.down.bytes() + 4.0 * nseq * (F + 2 * h));

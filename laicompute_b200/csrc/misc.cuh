@@ -5,7 +5,6 @@
 #include "common.cuh"
 #include "tiles.cuh"
 #include "mma_matvec.cuh"  // store_act_record
-#include "mv_streamk.cuh"  // dp_lane_record_rt
 
 namespace laic {
 
@@ -19,14 +18,11 @@ struct EmbedParams {
     float* x;                // [nseq][hidden]
     unsigned* counts;        // [max_seqs][vocab] history counts (repeat penalty)
     int vocab;
-    // optional: binary16 hi/lo records of x * rec_w for a tile-kernel projection, and sum x^2
+    // optional: binary16 hi/lo records of x * rec_w for a tile-kernel projection
     uint8_t* rec_out;        // activation records of x * rec_w (rec_off layout)
     const float* rec_w;      // the first rmsnorm weight
-    float* ss_out;           // [nseq]
+    float* ss_out;           // optional: [slices][nseq] sums of x^2 (the next rmsnorm's partials)
     int nseq;
-    // optional, one sequence: the team kernel's integer records of x * rec_w (and ss_out)
-    uint8_t* rec_dp;
-    int rec_type;            // the consuming projection's weight type (T_Q4_0 or T_Q8_0)
 };
 
 // x[s] = row tokens[s] of token_embd; the token joins its slot's history. Grid (nseq,
@@ -45,16 +41,10 @@ __global__ void embed_kernel(const EmbedParams p) {
         const bool in = i < hi;
         const float v = in ? tile_value(p.type, p.q, p.s, p.nb, (int)tok, i) : 0.f;
         if (in) p.x[(size_t)s * p.hidden + i] = v;
-        if (p.rec_out && in) {
-            ss = fmaf(v, v, ss);
-            store_act_record(p.rec_out, p.nseq, i, s, v * p.rec_w[i]);
-        }
-        if (p.rec_dp) {  // whole warps: lanes 8j..8j+7 hold one 8-column group
-            ss = fmaf(v, v, ss);
-            dp_lane_record_rt(p.rec_type, in ? v * p.rec_w[i] : 0.f, 0.f, i & 7, in ? i >> 3 : -1, p.rec_dp, 1, 2, 4);
-        }
+        if (p.ss_out && in) ss = fmaf(v, v, ss);
+        if (p.rec_out && in) store_act_record(p.rec_out, p.nseq, i, s, v * p.rec_w[i]);
     }
-    if (p.rec_out || p.rec_dp) {
+    if (p.ss_out) {
         ss = block_sum(ss, red);
         if (threadIdx.x == 0) p.ss_out[(size_t)blockIdx.y * p.nseq + s] = ss;
     }

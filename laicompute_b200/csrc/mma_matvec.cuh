@@ -75,10 +75,9 @@ struct MvParams {
     uint8_t* rec_out;          // records (rec_off) of rows or rows/2 elements (nullptr: none)
     const float* rec_w;        // EPI_ADD: the next rmsnorm weight (records of out * w), or nullptr
     float* ss_out;             // EPI_ADD: [row tiles][nseq] sums of squares of the new residual
-    // team kernel, one sequence (integer variant): `xg` may bring the integer digit records
-    // (scale_mode, ss, ss_tiles, ss_n as above) and `rec_out` receives them for the next
-    // projection, whose weight type is rec_type (T_Q4_0 or T_Q8_0)
-    int rec_type;
+    // team kernel, one sequence (integer variant): scale_mode 1 or 2 with ss, ss_tiles, ss_n as
+    // above: it builds the records of x * norm_w itself and scales the rows by the rmsnorm's 1/rms
+    // from the partial sums (EPI_ADD writes them to ss_out for the next projection)
     // team kernel: its split, computed on the host (the kernel takes no divisions): warps per
     // team, teams per CTA and ceil(65536 / team_k) (warp / team_k = warp * team_inv >> 16);
     // tiles per CTA (tq, one more in the first tr CTAs) and blocks per warp's slice of a tile

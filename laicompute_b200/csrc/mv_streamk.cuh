@@ -14,14 +14,16 @@
 // CTA-wide barrier is taken after the activation prologue.
 //
 // NT = 0 is the single-sequence integer variant for Q4_0 / Q8_0: the same
-// tiles and rings, but each lane forms exact integer dot products of its
-// quants with the activation split into three int8 digits (dp4a), instead of
-// converting quants to binary16 for mma.sync, where one sequence fills 2 of
-// the 8 product columns. Per 32-column block the activation is scaled by a
-// power of two that puts its largest magnitude in [2^19, 2^20), rounded to an
-// integer x (21 bits, exact in the digits below) and written as balanced
-// base-128 digits x = p0 * 2^14 + p1 * 2^7 + p2 (each in [-64, 64]). For a
-// row's 8 columns c..c+7 of the block:
+// tiles and rings, but exact integer dot products of the quants with the
+// activation split into three int8 digits, on the integer tensor-core path
+// (mma.m16n8k32, u8 x s8 or s8 x s8 -> s32), instead of converting quants to
+// binary16, where one sequence fills 2 of the 8 product columns. Per 32-column
+// block the activation is scaled by a power of two that puts its largest
+// magnitude in [2^19, 2^20), rounded to an integer x (21 bits, exact in the
+// digits below) and written as balanced base-128 digits
+// x = p0 * 2^14 + p1 * 2^7 + p2 (each in [-64, 64]). The digits are the first
+// three columns of the product's B operand, so one mma gives, per row of the
+// 16-row tile-block,
 //   sum_k q_k x_k = 2^14 sum q p0 + 2^7 sum q p1 + sum q p2
 // with q the stored quant (Q4_0: the nibble n, corrected by -8 * sum x; Q8_0:
 // the int8 value), all in int32 without rounding; then
@@ -73,9 +75,12 @@ __host__ __device__ inline int sk_team_cost(int k, int nb, int ntiles, int grid,
 }
 // Team size of a launch: sk_team, or a larger divisor of w that cuts the cost by more
 // than 10 % (few tiles per CTA leave teams idle: the 4096-row projections of an 8B-shaped
-// model own one or two tiles per CTA), keeping at least two blocks per warp.
+// model own one or two tiles per CTA), keeping at least two blocks per warp. Rows of more
+// than 256 blocks keep sk_team: their slices are long already (measured: 12-warp teams
+// on 448-block rows were 6 % slower than 8-warp teams).
 __host__ __device__ inline int sk_team_for(int nb, int ntiles, int grid, int w) {
     int k = sk_team(nb, w);
+    if (nb > 256) return k;
     int best = sk_team_cost(k, nb, ntiles, grid, w);
     for (int kk = k + 1; kk <= w; ++kk) {
         if (w % kk != 0 || 2 * kk > nb) continue;
@@ -125,11 +130,17 @@ __device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
     return d;
 }
 
-// Activation record of one 32-column block for the integer variant: for each
-// 8-column group c (32 bytes at c * 32): digits p0, p1, p2 as two words each
-// (the quants' byte order of this lane's fragment), then -8 * sum x over the
-// group (Q4_0, else 0) and the block's scale 2^-s as a float.
+// Activation record of one 32-column block for the team kernel's integer variant,
+// laid out as the B operand of mma.m16n8k32 (column n = digit, k = the 32 columns
+// in the quants' fragment order): at d * 32 + c * 8 the two words of digit d (p0,
+// p1, p2) over 8-column group c (the bytes in the order of the quants of group c
+// in a lane's fragment, dp_byte_of), then at 96 the int -8 * sum x over the block
+// (Q4_0, else 0) and the block's scale 2^-s as a float; 24 bytes of padding.
 constexpr int kDpRecBytes = 128;
+// The decode-step kernel's records (dp_lane_record) keep one scale per 8-column
+// group instead: for each group c, 32 bytes at c * 32 with digits p0, p1, p2 as
+// two words each, then -8 * sum x over the group (Q4_0, else 0) and the group's
+// scale 2^-s as a float.
 
 // Byte of element k (0..7) of an 8-column group inside the two words of a
 // lane's fragment: Q4_0 packs (e0,e1) (e2,e3) (e4,e5) (e6,e7) as nibble pairs,
@@ -182,46 +193,64 @@ __device__ __forceinline__ float dp_lane_record(float val, float sq, int k, int 
     return sq;
 }
 
-// The same for a consumer whose weight type is known at run time (T_Q4_0 or T_Q8_0).
-__device__ __forceinline__ float dp_lane_record_rt(int type, float val, float sq, int k, int gidx, uint8_t* recs, int m1,
-                                                   int m2, int m3) {
-    return type == T_Q4_0 ? dp_lane_record<T_Q4_0>(val, sq, k, gidx, recs, m1, m2, m3)
-                          : dp_lane_record<T_Q8_0>(val, sq, k, gidx, recs, m1, m2, m3);
+// d = A (16x32, unsigned or signed bytes) x B (32x8, signed bytes) + c, in int32 (mma.m16n8k32)
+template <bool AU8>
+__device__ __forceinline__ void imma16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                          uint32_t b1) {
+    if constexpr (AU8)
+        asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
+            : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
+    else
+        asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
+            : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
 }
 
-// One 16x32 tile-block of the integer variant: rows g and g+8, columns 8c..8c+7.
+// Per-lane constants of the integer variant. The product's columns 0, 1, 2 are the digit
+// sums of rows g and g+8 (lane c holds columns 2c and 2c+1; lanes g = 3..7 load digit
+// g mod 3, so columns 3..7 repeat them and are ignored): lane c = 0 forms
+// 2^14 s0 + 2^7 s1, lane c = 1 forms s2 plus the block's -8 sum x, lanes c = 2, 3 nothing.
+struct DpLane {
+    int ka, kb, kx;       // weights of columns 2c, 2c+1 and of the block's correction (0 / -1 mask)
+    uint32_t boff;        // this lane's B fragment in a record: digit g mod 3, group c
+};
+__device__ __forceinline__ DpLane dp_lane(int lane) {
+    const int g = lane >> 2, c = lane & 3;
+    DpLane l;
+    l.ka = c == 0 ? 16384 : c == 1 ? 1 : 0;
+    l.kb = c == 0 ? 128 : 0;
+    l.kx = c == 1 ? -1 : 0;
+    l.boff = (uint32_t)((g % 3) * 32 + c * 8);
+    return l;
+}
+
+// One 16x32 tile-block of the integer variant: rows g and g+8 of this lane's share of the
+// sum (added over the row's four lanes at the end of the tile).
 template <int WT>
-__device__ __forceinline__ void tile_block_dp(uint32_t q, uint32_t sc, uint32_t xrec, int lane, float (&acc)[2]) {
+__device__ __forceinline__ void tile_block_dp(uint32_t q, uint32_t sc, uint32_t xrec, const DpLane& ln, int lane,
+                                              float (&acc)[2]) {
     const int g = lane >> 2;
-    const uint4 xa = lds128(xrec), xb = lds128(xrec + 16);
-    const int x8 = (int)xb.z;
-    const float sinv = __uint_as_float(xb.w);
+    const uint2 b = lds64(xrec + ln.boff);
+    const uint2 xs = lds64(xrec + 96);  // -8 sum x, 2^-s
     const uint32_t dp = lds32(sc + g * 4);
     const float2 df = __half22float2(*reinterpret_cast<const __half2*>(&dp));
-    uint32_t wl[2], wh[2];  // per row: the two quant words in the activation digits' byte order
+    int r[4];
     if (WT == T_Q4_0) {
+        // A fragment: row g / g+8, k = 4c..4c+3 the low nibbles, k = 16+4c.. the high nibbles
         const uint2 w = lds64(q + lane * 8);
-        wl[0] = w.x & 0x0F0F0F0Fu; wh[0] = (w.x >> 4) & 0x0F0F0F0Fu;
-        wl[1] = w.y & 0x0F0F0F0Fu; wh[1] = (w.y >> 4) & 0x0F0F0F0Fu;
+        imma16832<true>(r, w.x & 0x0F0F0F0Fu, w.y & 0x0F0F0F0Fu, (w.x >> 4) & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu,
+                        b.x, b.y);
     } else {
         const uint4 w = lds128(q + lane * 16);
-        wl[0] = w.x; wh[0] = w.y; wl[1] = w.z; wh[1] = w.w;
+        imma16832<false>(r, w.x, w.z, w.y, w.w, b.x, b.y);
     }
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-        int s0, s1, s2;
-        if (WT == T_Q4_0) {
-            s2 = dp4a_us(wh[r], xb.y, dp4a_us(wl[r], xb.x, x8));  // x8 = -8 * sum x (the nibbles' offset)
-            s1 = dp4a_us(wh[r], xa.w, dp4a_us(wl[r], xa.z, 0));
-            s0 = dp4a_us(wh[r], xa.y, dp4a_us(wl[r], xa.x, 0));
-        } else {
-            s2 = dp4a_ss(wh[r], xb.y, dp4a_ss(wl[r], xb.x, 0));
-            s1 = dp4a_ss(wh[r], xa.w, dp4a_ss(wl[r], xa.z, 0));
-            s0 = dp4a_ss(wh[r], xa.y, dp4a_ss(wl[r], xa.x, 0));
-        }
-        const int v = s0 * 16384 + s1 * 128 + s2;  // exact: |v| < 2^30
-        acc[r] = fmaf((float)v, (r ? df.y : df.x) * sinv, acc[r]);
-    }
+    const int x8 = (int)xs.x & ln.kx;
+    const float sinv = __uint_as_float(xs.y);
+    const int v0 = r[0] * ln.ka + r[1] * ln.kb + x8;  // exact: |v| < 2^30
+    const int v1 = r[2] * ln.ka + r[3] * ln.kb + x8;
+    acc[0] = fmaf((float)v0, df.x * sinv, acc[0]);
+    acc[1] = fmaf((float)v1, df.y * sinv, acc[1]);
 }
 
 // One 16x32 tile-block: decode this lane's A fragments, multiply with the
@@ -272,10 +301,10 @@ __device__ __forceinline__ void tile_block(uint32_t q, uint32_t sc, const uint32
     }
 }
 
-// One 8-column group of the activation (thread-per-group, whole warp active):
-// optional rmsnorm scaling, the group's power-of-two scale (shared with the
-// three other groups of its block through the adjacent lanes), the digits in
-// the quants' byte order, and the record store when `live`.
+// One 8-column group of the activation (thread-per-group, whole warp active, the
+// four groups of a block in adjacent lanes): optional rmsnorm scaling, the block's
+// power-of-two scale, the digits in the quants' byte order, and the record store
+// (kDpRecBytes layout) when `live`.
 template <int WT>
 __device__ __forceinline__ void dp_group_record(float (&v)[8], const float* norm_w, float iv, int gi, bool live,
                                                 uint8_t* xs) {
@@ -308,22 +337,29 @@ __device__ __forceinline__ void dp_group_record(float (&v)[8], const float* norm
         dw[1][wd] |= (uint32_t)(p1 & 0xFF) << sh;
         dw[2][wd] |= (uint32_t)(p2 & 0xFF) << sh;
     }
+    gs += __shfl_xor_sync(0xffffffffu, gs, 1);  // the block's sum over its four groups
+    gs += __shfl_xor_sync(0xffffffffu, gs, 2);
     if (live) {
-        uint4* rec = reinterpret_cast<uint4*>(xs + (size_t)gi * 32);  // block gi/4, group gi%4
-        rec[0] = make_uint4(dw[0][0], dw[0][1], dw[1][0], dw[1][1]);
-        rec[1] = make_uint4(dw[2][0], dw[2][1], (uint32_t)(WT == T_Q4_0 ? -8 * gs : 0),
-                            __float_as_uint(ldexpf(1.f, ex - 20)));
+        uint8_t* rec = xs + (size_t)(gi >> 2) * kDpRecBytes;  // block gi/4, group gi%4
+        const int c = gi & 3;
+#pragma unroll
+        for (int d = 0; d < 3; ++d) *reinterpret_cast<uint2*>(rec + d * 32 + c * 8) = make_uint2(dw[d][0], dw[d][1]);
+        if (c == 0)
+            *reinterpret_cast<uint2*>(rec + 96) =
+                make_uint2((uint32_t)(WT == T_Q4_0 ? -8 * gs : 0), __float_as_uint(ldexpf(1.f, ex - 20)));
     }
 }
 
 // Activation digit records of the integer variant for one sequence (whole CTA):
 // rmsnorm by norm_w when given, then per 32-column block the power-of-two
 // scale and the balanced base-128 digits, one thread per 8-column group.
-// Reads the activations through L2 (they may come from other CTAs of the same
-// kernel). Ends with a CTA barrier.
+// `unscaled`: records of x * norm_w without the 1/rms (the caller scales the
+// finished rows), so no pass over x for the sum of squares. Reads the
+// activations through L2 (the producing kernel wrote them). Ends with a CTA
+// barrier.
 template <int WT>
 __device__ __forceinline__ void dp_build_records(const float* x, const float* norm_w, float eps, int in, uint8_t* xs,
-                                                 float* wstat, float* inv) {
+                                                 float* wstat, float* inv, bool unscaled = false) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int nb = in / 32, ng = nb * 4;  // 8-column groups
     const float4* src = reinterpret_cast<const float4*>(x);
@@ -332,7 +368,7 @@ __device__ __forceinline__ void dp_build_records(const float* x, const float* no
     const int nt = blockDim.x;
     if (ng > RMAX * nt) {  // too long to hold: the sum of squares first, then the groups round by round
         float ss = 0.f;
-        if (norm_w) {
+        if (norm_w && !unscaled) {
             for (int f = threadIdx.x; f < (in >> 2); f += nt) {
                 const float4 v = __ldcg(src + f);
                 ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
@@ -343,7 +379,7 @@ __device__ __forceinline__ void dp_build_records(const float* x, const float* no
         __syncthreads();
         float a = 0.f;
         for (int w = 0; w < (int)(blockDim.x >> 5); ++w) a += wstat[w * 2];
-        const float iv = norm_w ? 1.f / sqrtf(a / float(in) + eps) : 1.f;
+        const float iv = norm_w && !unscaled ? 1.f / sqrtf(a / float(in) + eps) : 1.f;
         for (int base = 0; base < ng; base += nt) {
             const int gi = base + threadIdx.x;
             const bool live = gi < ng;
@@ -367,7 +403,7 @@ __device__ __forceinline__ void dp_build_records(const float* x, const float* no
             for (int k = 0; k < 8; ++k) ss = fmaf(v[r][k], v[r][k], ss);
         }
         float iv = 1.f;
-        if (norm_w) {
+        if (norm_w && !unscaled) {
             ss = warp_sum(ss);
             if (lane == 0) wstat[warp * 2] = ss;
             __syncthreads();
@@ -454,13 +490,10 @@ __global__ void __launch_bounds__(W * 32, 1) mv_sk_kernel(const MvParams p) {
     // ---- prologue: the whole activation vector -> binary16 hi/lo in fragment order
     //      (integer variant: int8 digit records, one warp per 32-column block)
     if constexpr (DP) {
-        if (p.xg) {
-            // records written by the producing kernel's epilogue (of x * norm weight, without
-            // the 1/rms): copy them in; the rmsnorm scale from the producer's partial sums
-            // multiplies the finished rows instead
-            const int nchunk = nb * (kDpRecBytes / 16);
-            for (int i = threadIdx.x; i < nchunk; i += blockDim.x) cp_async16(xs + i * 16, p.xg + (size_t)i * 16);
-            cp_async_commit();
+        if (p.scale_mode != 0) {
+            // records of x * norm weight without the 1/rms; the rmsnorm scale comes from the
+            // producing kernel's partial sums of squares (mode 1, else unit) and multiplies the
+            // finished rows instead
             if (warp == 0) {
                 float a = 0.f;
                 if (p.scale_mode == 1) {
@@ -475,7 +508,7 @@ __global__ void __launch_bounds__(W * 32, 1) mv_sk_kernel(const MvParams p) {
                 }
                 if (lane == 0) xsc[0] = p.scale_mode == 1 ? 1.f / sqrtf(a / float(p.ss_n) + p.eps) : 1.f;
             }
-            cp_async_wait_all();
+            dp_build_records<WT>(p.x, p.norm_w, p.eps, p.in, xs, wstat, inv, true);
         } else {
             dp_build_records<WT>(p.x, p.norm_w, p.eps, p.in, xs, wstat, inv);
             if (threadIdx.x == 0) xsc[0] = 1.f;  // the digit scales are applied per block
@@ -631,27 +664,16 @@ __global__ void __launch_bounds__(W * 32, 1) mv_sk_kernel(const MvParams p) {
             }
         }
         __syncwarp();
-        if constexpr (DP && (EPI == EPI_ADD || EPI == EPI_SWIGLU)) {
-            if (p.rec_out) {  // the integer records of this tile's outputs for the next projection
-                if (EPI == EPI_ADD) {
-                    // rows r0 + lane (lanes 0..15 wrote them above): records of x * next norm
-                    // weight (groups 2t, 2t + 1) and the tile's sum of x^2
-                    const int r = r0 + lane;
-                    const bool live = lane < 16 && r < p.rows;
-                    const float xn = live ? p.out[r] : 0.f;
-                    const float wv = live && p.rec_w ? p.rec_w[r] : 1.f;
-                    const float sg = dp_lane_record_rt(p.rec_type, live ? xn * wv : 0.f, xn * xn, lane & 7,
-                                                       live ? (r >> 3) : -1, p.rec_out, 1, 2, 4);
-                    const float s8 = __shfl_sync(0xffffffffu, sg, 8);
-                    if (lane == 0 && p.ss_out) p.ss_out[t] = sg + s8;
-                } else {
-                    // outputs r0 / 2 + lane / 2 on the even lanes 0..14: group t
-                    const int o = (r0 >> 1) + (lane >> 1);
-                    const bool live = lane < 16 && (lane & 1) == 0 && r0 + lane < p.rows;
-                    const float a = live ? p.out[o] : 0.f;
-                    dp_lane_record_rt(p.rec_type, a, 0.f, lane >> 1, live ? (o >> 3) : -1, p.rec_out, 2, 4, 8);
-                }
-                __syncwarp();
+        if constexpr (DP && EPI == EPI_ADD) {
+            if (p.ss_out) {  // the tile's sum of squares of the new residual (rows r0 + lane), for the next rmsnorm
+                const int r = r0 + lane;
+                const float xn = lane < 16 && r < p.rows ? p.out[r] : 0.f;
+                float sq = xn * xn;
+                sq += __shfl_xor_sync(0xffffffffu, sq, 1);
+                sq += __shfl_xor_sync(0xffffffffu, sq, 2);
+                sq += __shfl_xor_sync(0xffffffffu, sq, 4);
+                sq += __shfl_xor_sync(0xffffffffu, sq, 8);
+                if (lane == 0) p.ss_out[t] = sq;
             }
         }
     };
@@ -662,8 +684,9 @@ __global__ void __launch_bounds__(W * 32, 1) mv_sk_kernel(const MvParams p) {
     // this lane's activation column in each n-tile
     uint32_t xlane[DP ? 1 : NT];  // shared-memory addresses
     const int xstride = DP ? kDpRecBytes : 2 * B * 4 * 16;  // bytes between the records of consecutive blocks
+    const DpLane dln = dp_lane(lane);  // (integer variant)
     if constexpr (DP) {
-        xlane[0] = smem_u32(xs) + c * 32;  // this lane's 8-column group of each block record
+        xlane[0] = smem_u32(xs);  // the block records (tile_block_dp adds this lane's fragment)
     } else {
 #pragma unroll
         for (int j = 0; j < NT; ++j) {
@@ -686,7 +709,7 @@ __global__ void __launch_bounds__(W * 32, 1) mv_sk_kernel(const MvParams p) {
             // two blocks per iteration: a fully unrolled stage made instruction fetch the top stall
             // (measured 2-3 % slower steps on the 8B and 1B shapes)
 #pragma unroll 2
-            for (int j = 0; j < n; ++j) tile_block_dp<WT>(sq + j * QB, ssc + j * SB, xr + j * kDpRecBytes, lane, dacc);
+            for (int j = 0; j < n; ++j) tile_block_dp<WT>(sq + j * QB, ssc + j * SB, xr + j * kDpRecBytes, dln, lane, dacc);
         } else if (n == KB) {
 #pragma unroll
             for (int j = 0; j < KB; ++j) tile_block<WT, NT>(sq + j * QB, ssc + j * SB, xlane, b0 + j, xstride, lane, acc);
