@@ -301,32 +301,29 @@ __device__ __forceinline__ void tile_block(uint32_t q, uint32_t sc, const uint32
     }
 }
 
-// One 8-column group of the activation (thread-per-group, whole warp active, the
-// four groups of a block in adjacent lanes): optional rmsnorm scaling, the block's
-// power-of-two scale, the digits in the quants' byte order, and the record store
-// (kDpRecBytes layout) when `live`.
+// The digit record of one 8-column group of values v (thread-per-group, whole warp
+// active, the four groups of a block in adjacent lanes): the block's power-of-two scale,
+// the digits in the quants' byte order, and the record store (kDpRecBytes layout) when
+// `live`. The block's exponent ex (its largest magnitude in [2^(ex-1), 2^ex)) comes from
+// the float's bits and the scaling is one exact multiply by 2^(20-ex), rounded to nearest
+// even as rintf(ldexpf(v, 20 - ex)) would; a block whose largest magnitude is below 2^-100,
+// or not finite, is written as zeros.
 template <int WT>
-__device__ __forceinline__ void dp_group_record(float (&v)[8], const float* norm_w, float iv, int gi, bool live,
-                                                uint8_t* xs) {
-    if (norm_w && live) {
-        const float4 w0 = reinterpret_cast<const float4*>(norm_w)[2 * gi];
-        const float4 w1 = reinterpret_cast<const float4*>(norm_w)[2 * gi + 1];
-        const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-#pragma unroll
-        for (int k = 0; k < 8; ++k) v[k] = v[k] * (iv * w[k]);
-    }
+__device__ __forceinline__ void dp_group_digits(const float (&v)[8], int gi, bool live, uint8_t* xs) {
     float mx = 0.f;
 #pragma unroll
     for (int k = 0; k < 8; ++k) mx = fmaxf(mx, fabsf(v[k]));
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    int ex = 0;
-    if (mx > 0.f && isfinite(mx)) frexpf(mx, &ex);  // mx in [2^(ex-1), 2^ex)
+    const int eb = (__float_as_int(mx) >> 23) & 0xFF;  // biased exponent (mx >= 0)
+    const int ex = eb - 126;                             // mx in [2^(ex-1), 2^ex) for normal mx
+    const bool ok = eb != 0xFF && ex > -100;
+    const float sc = ok ? __int_as_float((147 - ex) << 23) : 0.f;  // 2^(20-ex), a normal float
     uint32_t dw[3][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}};  // digit words p0 p1 p2, quant byte order
     int gs = 0;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-        const int xi = (int)rintf(ldexpf(v[k], 20 - ex));  // |xi| <= 2^20
+        const int xi = ok ? __float2int_rn(v[k] * sc) : 0;  // |xi| <= 2^20
         const int p2 = ((xi + 64) & 127) - 64;
         const int t1 = (xi - p2) >> 7;
         const int p1 = ((t1 + 64) & 127) - 64;
@@ -345,21 +342,64 @@ __device__ __forceinline__ void dp_group_record(float (&v)[8], const float* norm
 #pragma unroll
         for (int d = 0; d < 3; ++d) *reinterpret_cast<uint2*>(rec + d * 32 + c * 8) = make_uint2(dw[d][0], dw[d][1]);
         if (c == 0)
-            *reinterpret_cast<uint2*>(rec + 96) =
-                make_uint2((uint32_t)(WT == T_Q4_0 ? -8 * gs : 0), __float_as_uint(ldexpf(1.f, ex - 20)));
+            *reinterpret_cast<uint2*>(rec + 96) = make_uint2((uint32_t)(WT == T_Q4_0 ? -8 * gs : 0),
+                                                             ok ? (uint32_t)(107 + ex) << 23 : 0u);  // 2^(ex-20)
     }
+}
+
+// dp_group_digits of v scaled by iv * norm_w (when norm_w is given).
+template <int WT>
+__device__ __forceinline__ void dp_group_record(float (&v)[8], const float* norm_w, float iv, int gi, bool live,
+                                                uint8_t* xs) {
+    if (norm_w && live) {
+        const float4 w0 = reinterpret_cast<const float4*>(norm_w)[2 * gi];
+        const float4 w1 = reinterpret_cast<const float4*>(norm_w)[2 * gi + 1];
+        const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = v[k] * (iv * w[k]);
+    }
+    dp_group_digits<WT>(v, gi, live, xs);
+}
+
+// Records of x * norm_w (norm_w may be null) for `nb` blocks, without the rmsnorm's 1/rms
+// (whole CTA; ends with a CTA barrier): every thread loads its groups' activations and
+// norm weights first (up to kDpGroupsInFlight groups per thread), then forms the digits.
+constexpr int kDpGroupsInFlight = 3;
+template <int WT>
+__device__ __forceinline__ void dp_records_unscaled(const float* x, const float* norm_w, int nb, uint8_t* xs) {
+    const int ng = nb * 4, nt = blockDim.x;
+    const float4* src = reinterpret_cast<const float4*>(x);
+    const float4* nw4 = reinterpret_cast<const float4*>(norm_w);
+    for (int base = 0; base < ng; base += kDpGroupsInFlight * nt) {  // the same trip count in every thread
+        float v[kDpGroupsInFlight][8];
+#pragma unroll
+        for (int u = 0; u < kDpGroupsInFlight; ++u) {
+            const int gi = base + u * nt + (int)threadIdx.x;
+            const bool live = gi < ng;
+            const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f), o4 = make_float4(1.f, 1.f, 1.f, 1.f);
+            const float4 a0 = live ? __ldcg(src + 2 * gi) : z4, a1 = live ? __ldcg(src + 2 * gi + 1) : z4;
+            const float4 w0 = live && norm_w ? __ldg(nw4 + 2 * gi) : o4, w1 = live && norm_w ? __ldg(nw4 + 2 * gi + 1) : o4;
+            v[u][0] = a0.x * w0.x; v[u][1] = a0.y * w0.y; v[u][2] = a0.z * w0.z; v[u][3] = a0.w * w0.w;
+            v[u][4] = a1.x * w1.x; v[u][5] = a1.y * w1.y; v[u][6] = a1.z * w1.z; v[u][7] = a1.w * w1.w;
+        }
+#pragma unroll
+        for (int u = 0; u < kDpGroupsInFlight; ++u) {
+            if (base + u * nt >= ng) break;  // uniform over the CTA
+            const int gi = base + u * nt + (int)threadIdx.x;
+            dp_group_digits<WT>(v[u], gi, gi < ng, xs);
+        }
+    }
+    __syncthreads();
 }
 
 // Activation digit records of the integer variant for one sequence (whole CTA):
 // rmsnorm by norm_w when given, then per 32-column block the power-of-two
 // scale and the balanced base-128 digits, one thread per 8-column group.
-// `unscaled`: records of x * norm_w without the 1/rms (the caller scales the
-// finished rows), so no pass over x for the sum of squares. Reads the
-// activations through L2 (the producing kernel wrote them). Ends with a CTA
-// barrier.
+// Reads the activations through L2 (the producing kernel wrote them). Ends with
+// a CTA barrier.
 template <int WT>
 __device__ __forceinline__ void dp_build_records(const float* x, const float* norm_w, float eps, int in, uint8_t* xs,
-                                                 float* wstat, float* inv, bool unscaled = false) {
+                                                 float* wstat, float* inv) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int nb = in / 32, ng = nb * 4;  // 8-column groups
     const float4* src = reinterpret_cast<const float4*>(x);
@@ -368,7 +408,7 @@ __device__ __forceinline__ void dp_build_records(const float* x, const float* no
     const int nt = blockDim.x;
     if (ng > RMAX * nt) {  // too long to hold: the sum of squares first, then the groups round by round
         float ss = 0.f;
-        if (norm_w && !unscaled) {
+        if (norm_w) {
             for (int f = threadIdx.x; f < (in >> 2); f += nt) {
                 const float4 v = __ldcg(src + f);
                 ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
@@ -379,7 +419,7 @@ __device__ __forceinline__ void dp_build_records(const float* x, const float* no
         __syncthreads();
         float a = 0.f;
         for (int w = 0; w < (int)(blockDim.x >> 5); ++w) a += wstat[w * 2];
-        const float iv = norm_w && !unscaled ? 1.f / sqrtf(a / float(in) + eps) : 1.f;
+        const float iv = norm_w ? 1.f / sqrtf(a / float(in) + eps) : 1.f;
         for (int base = 0; base < ng; base += nt) {
             const int gi = base + threadIdx.x;
             const bool live = gi < ng;
@@ -403,7 +443,7 @@ __device__ __forceinline__ void dp_build_records(const float* x, const float* no
             for (int k = 0; k < 8; ++k) ss = fmaf(v[r][k], v[r][k], ss);
         }
         float iv = 1.f;
-        if (norm_w && !unscaled) {
+        if (norm_w) {
             ss = warp_sum(ss);
             if (lane == 0) wstat[warp * 2] = ss;
             __syncthreads();
@@ -508,7 +548,7 @@ __global__ void __launch_bounds__(W * 32, 1) mv_sk_kernel(const MvParams p) {
                 }
                 if (lane == 0) xsc[0] = p.scale_mode == 1 ? 1.f / sqrtf(a / float(p.ss_n) + p.eps) : 1.f;
             }
-            dp_build_records<WT>(p.x, p.norm_w, p.eps, p.in, xs, wstat, inv, true);
+            dp_records_unscaled<WT>(p.x, p.norm_w, nb, xs);
         } else {
             dp_build_records<WT>(p.x, p.norm_w, p.eps, p.in, xs, wstat, inv);
             if (threadIdx.x == 0) xsc[0] = 1.f;  // the digit scales are applied per block
