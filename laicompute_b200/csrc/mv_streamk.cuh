@@ -533,8 +533,9 @@ __global__ void __launch_bounds__(W * 32, 1) mv_sk_kernel(const MvParams p) {
         if (p.scale_mode != 0) {
             // records of x * norm weight without the 1/rms; the rmsnorm scale comes from the
             // producing kernel's partial sums of squares (mode 1, else unit) and multiplies the
-            // finished rows instead
-            if (warp == 0) {
+            // finished rows instead. The last warp sums them: with at most (W - 1) * 32 groups
+            // (4096 columns at 24 warps) it has no records to build
+            if (warp == W - 1) {
                 float a = 0.f;
                 if (p.scale_mode == 1) {
                     int t = lane;
