@@ -102,6 +102,25 @@ inline void sk_split(MvParams& p, int grid, int w) {
     p.sr = p.nb % k;
 }
 
+// One warp's share of a team-kernel launch, from sk_split's parameters: its team, its place in the
+// team and the team's first warp, the CTA's row tiles [t_lo, t_hi) (the team takes t_lo + team,
+// + teams, ...) and the warp's K slice [b_lo, b_hi) of every tile. Shared by the kernel and the
+// host-side check of the split.
+struct SkWarpRange {
+    int team, wi, leader, t_lo, t_hi, b_lo, b_hi;
+};
+__host__ __device__ inline SkWarpRange sk_warp_range(const MvParams& p, int cta, int warp) {
+    SkWarpRange r;
+    r.team = (warp * p.team_inv) >> 16;
+    r.wi = warp - r.team * p.team_k;
+    r.leader = r.team * p.team_k;
+    r.t_lo = cta * p.tq + (cta < p.tr ? cta : p.tr);
+    r.t_hi = r.t_lo + p.tq + (cta < p.tr ? 1 : 0);
+    r.b_lo = r.wi * p.sq + (r.wi < p.sr ? r.wi : p.sr);
+    r.b_hi = r.b_lo + p.sq + (r.wi < p.sr ? 1 : 0);
+    return r;
+}
+
 // tickets, merged-tile marks, per-warp statistics, 1/rms and split scale per sequence
 __host__ __device__ inline size_t sk_small_bytes(int B, int w = kSkWarps) {
     return ((size_t)w * kSkSlots * 2 * 4 + (size_t)w * B * 2 * 4 + 2 * (size_t)B * 4 + 15) / 16 * 16;
@@ -491,10 +510,10 @@ __global__ void __launch_bounds__(W * 32, 1) mv_sk_kernel(const MvParams p) {
 
     // this CTA's tiles, this warp's team and K slice (sk_split: the host's arithmetic)
     const int k = p.team_k, teams = p.team_n;
-    const int team = (warp * p.team_inv) >> 16, wi = warp - team * k, leader = team * k;
-    const int cta = blockIdx.x;
-    const int t_lo = cta * p.tq + min(cta, p.tr), t_hi = t_lo + p.tq + (cta < p.tr ? 1 : 0);
-    const int b_lo = wi * p.sq + min(wi, p.sr), b_hi = b_lo + p.sq + (wi < p.sr ? 1 : 0);  // slice of every tile
+    const SkWarpRange wr = sk_warp_range(p, blockIdx.x, warp);
+    const int team = wr.team, leader = wr.leader;
+    const int t_lo = wr.t_lo, t_hi = wr.t_hi;
+    const int b_lo = wr.b_lo, b_hi = wr.b_hi;  // slice of every tile
     const int slice = b_hi - b_lo;
     const int st_per_tile = (slice + KB - 1) / KB;
     int my_tiles = 0;
