@@ -1,5 +1,6 @@
 """CPU emulation of the fragment-tile layout and of the tensor-core matvec's
-lane arithmetic (laicompute_b200/csrc/tiles.cuh, mma_matvec.cuh).
+lane arithmetic (laicompute_b200/csrc/tiles.cuh, mma_matvec.cuh, and the one-sequence
+integer variant of mv_streamk.cuh).
 
 The repack, the per-lane decode (bit tricks evaluated in binary16 with numpy),
 the activation hi/lo split in fragment order and the mma.m16n8k16 operand
@@ -190,46 +191,105 @@ def dp_byte_of(t_, k):
 
 
 def digits(x):
-    """Per 32-column block: integers |xi| <= 2^20 and balanced base-128 digits (the integer variant's prologue)."""
-    mx = np.abs(x).max()
-    ex = int(np.frexp(np.float32(mx))[1]) if mx > 0 else 0
-    xi = np.rint(np.ldexp(x.astype(np.float32), 20 - ex)).astype(np.int64)
+    """One 32-column block of the integer variant's records (dp_group_digits): the block exponent
+    ex from the largest magnitude's float bits (mx in [2^(ex-1), 2^ex)), xi = rint(x * 2^(20-ex))
+    by one exact multiply (|xi| <= 2^20), balanced base-128 digits, and the scale 2^(ex-20);
+    blocks whose largest magnitude is below 2^-100 are zeros."""
+    x = x.astype(np.float32)
+    mx = np.float32(np.abs(x).max())
+    eb = (int(mx.view(np.uint32)) >> 23) & 0xFF
+    ex = eb - 126
+    ok = eb != 0xFF and ex > -100
+    sc = np.float32(np.ldexp(np.float32(1.0), 20 - ex)) if ok else np.float32(0.0)
+    xi = np.rint(x * sc).astype(np.int64) if ok else np.zeros(32, np.int64)
+    if ok:  # the multiply equals ldexp: the same integers as rintf(ldexpf(x, 20 - ex))
+        assert np.array_equal(xi, np.rint(np.ldexp(x, 20 - ex)).astype(np.int64))
     p2 = ((xi + 64) & 127) - 64
     t1 = (xi - p2) >> 7
     p1 = ((t1 + 64) & 127) - 64
     p0 = (t1 - p1) >> 7
     assert np.all(np.abs(np.stack([p0, p1, p2])) <= 64)
     assert np.array_equal(p0 * 16384 + p1 * 128 + p2, xi)
-    return xi, (p0, p1, p2), np.float32(np.ldexp(1.0, ex - 20))
+    return xi, (p0, p1, p2), np.float32(np.ldexp(1.0, ex - 20)) if ok else np.float32(0.0)
+
+
+def block_record(t_, x):
+    """The 128-byte record of one block (kDpRecBytes layout): at d*32 + c*8 the two words of digit
+    d over group c in the quants' byte order, at 96 the int -8 * sum xi (Q4_0) and 2^-s."""
+    xi, pcs, sinv = digits(x)
+    rec = np.zeros(128, np.uint8)
+    for d in range(3):
+        for c in range(4):
+            for k in range(8):
+                rec[d * 32 + c * 8 + dp_byte_of(t_, k)] = np.uint8(np.int64(pcs[d][8 * c + k]) & 0xFF)
+    rec[96:100] = np.array([-8 * int(xi.sum()) if t_ == gguf.Q4_0 else 0], "<i4").view(np.uint8)
+    rec[100:104] = np.array([sinv], "<f4").view(np.uint8)
+    return rec
+
+
+def imma16832(a_frag, b_frag, signed_a):
+    """mma.m16n8k32 (int8): a_frag[lane] = 4 words (a0..a3), b_frag[lane] = 2 words (b0, b1) as in
+    the PTX fragment layout; returns the int32 D fragments [lane][4]."""
+    def bytes_of(wd, signed):
+        v = np.array([(wd >> (8 * i)) & 0xFF for i in range(4)], np.int64)
+        return np.where(v > 127, v - 256, v) if signed else v
+    A = np.zeros((16, 32), np.int64)
+    Bm = np.zeros((32, 8), np.int64)
+    for lane in range(32):
+        g, c = lane >> 2, lane & 3
+        a0, a1, a2, a3 = a_frag[lane]
+        A[g, 4 * c:4 * c + 4] = bytes_of(a0, signed_a)
+        A[g + 8, 4 * c:4 * c + 4] = bytes_of(a1, signed_a)
+        A[g, 16 + 4 * c:16 + 4 * c + 4] = bytes_of(a2, signed_a)
+        A[g + 8, 16 + 4 * c:16 + 4 * c + 4] = bytes_of(a3, signed_a)
+        b0, b1 = b_frag[lane]
+        Bm[4 * c:4 * c + 4, g] = bytes_of(b0, True)
+        Bm[16 + 4 * c:16 + 4 * c + 4, g] = bytes_of(b1, True)
+    D = A @ Bm
+    return [[D[l >> 2, 2 * (l & 3)], D[l >> 2, 2 * (l & 3) + 1], D[(l >> 2) + 8, 2 * (l & 3)],
+             D[(l >> 2) + 8, 2 * (l & 3) + 1]] for l in range(32)]
 
 
 def emulate_integer(t_, q, s, x, rows, nb):
-    """Replay the one-sequence integer variant (mv_streamk.cuh, NT = 0) on the fragment layout."""
+    """Replay the one-sequence integer variant (mv_streamk.cuh, NT = 0) on the fragment layout:
+    per tile-block the lanes' A fragments from the quant words, the B fragments from the block
+    record (lane 4g + c: digit g mod 3 of group c), one mma.m16n8k32, and the lane constants that
+    combine the digit columns (tile_block_dp, dp_lane); the row's four lanes are added at the end."""
     ntiles = (rows + 15) // 16
     y = np.zeros(ntiles * 16)
-    for b in range(nb):
-        xi, pcs, sinv = digits(x[b * 32:(b + 1) * 32])
-        for t in range(ntiles):
+    u32 = lambda buf, off: int(np.frombuffer(buf[off:off + 4].tobytes(), "<u4")[0])
+    for t in range(ntiles):
+        acc = np.zeros((32, 2))
+        for b in range(nb):
+            rec = block_record(t_, x[b * 32:(b + 1) * 32])
             chunk = q[(t * nb + b) * QB[t_]:(t * nb + b + 1) * QB[t_]]
+            a_frag, b_frag = [], []
             for lane in range(32):
                 g, c = lane >> 2, lane & 3
-                # digit words of group c in the quants' byte order
-                dw = np.zeros((3, 8), np.int64)
-                for k in range(8):
-                    for pi in range(3):
-                        dw[pi, dp_byte_of(t_, k)] = pcs[pi][8 * c + k]
-                x8 = -8 * int(xi[8 * c:8 * c + 8].sum()) if t_ == gguf.Q4_0 else 0
-                for r, row in ((0, g), (1, g + 8)):
-                    if t_ == gguf.Q4_0:
-                        w = int(chunk[lane * 8 + 4 * r:lane * 8 + 4 * r + 4].view("<u4")[0])
-                        qb = [((w & 0x0F0F0F0F) >> (8 * j)) & 0xFF for j in range(4)] + \
-                             [(((w >> 4) & 0x0F0F0F0F) >> (8 * j)) & 0xFF for j in range(4)]
-                    else:
-                        qb = list(chunk[lane * 16 + 8 * r:lane * 16 + 8 * r + 8].view(np.int8).astype(np.int64))
-                    sums = [int(np.dot(qb, dw[pi])) for pi in range(3)]
-                    v = sums[0] * 16384 + sums[1] * 128 + sums[2] + x8
-                    d = s[scale_offset(nb, t * 16 + row, b):][:2].view("<f2")[0]
-                    y[t * 16 + row] += float(v) * float(d) * float(sinv)
+                if t_ == gguf.Q4_0:
+                    wx, wy = u32(chunk, lane * 8), u32(chunk, lane * 8 + 4)
+                    m = 0x0F0F0F0F
+                    a_frag.append((wx & m, wy & m, (wx >> 4) & m, (wy >> 4) & m))
+                else:
+                    wx, wy, wz, ww = (u32(chunk, lane * 16 + 4 * i) for i in range(4))
+                    a_frag.append((wx, wz, wy, ww))
+                boff = (g % 3) * 32 + c * 8
+                b_frag.append((u32(rec, boff), u32(rec, boff + 4)))
+            r = imma16832(a_frag, b_frag, signed_a=(t_ != gguf.Q4_0))
+            x8 = int(np.frombuffer(rec[96:100].tobytes(), "<i4")[0])
+            sinv = float(np.frombuffer(rec[100:104].tobytes(), "<f4")[0])
+            for lane in range(32):
+                g, c = lane >> 2, lane & 3
+                ka, kb, kx = (16384, 128, 0) if c == 0 else (1, 0, 1) if c == 1 else (0, 0, 0)
+                for h, row in ((0, g), (1, g + 8)):
+                    v = r[lane][2 * h] * ka + r[lane][2 * h + 1] * kb + x8 * kx
+                    assert abs(v) < 2 ** 30
+                    d = float(s[scale_offset(nb, t * 16 + row, b):][:2].view("<f2")[0])
+                    acc[lane, h] += float(v) * d * sinv
+        for lane in range(32):
+            g = lane >> 2
+            y[t * 16 + g] += acc[lane, 0]
+            y[t * 16 + g + 8] += acc[lane, 1]
     return y[:rows]
 
 
@@ -242,7 +302,16 @@ def test_integer_variant_emulation_matches_dense(t_):
     q, s = repack(t_, raw, rows, nb)
     x = rng.standard_normal(nb * 32).astype(np.float32) * np.float32(3.0)
     x[5] = np.float32(40.0)  # a large entry in one block
+    x[64:96] = 0.0  # an all-zero block
+    x[70] = np.float32(1e-35)  # a block below 2^-100: written as zeros
     y = emulate_integer(t_, q, s, x, rows, nb)
     wd = O.dequant(t_, raw, rows * nb * 32).reshape(rows, nb * 32).astype(np.float64)
     ref = wd @ x.astype(np.float64)
-    assert np.allclose(y, ref, rtol=0, atol=1e-6 * (np.abs(wd) @ np.abs(x)).max())
+    # the products are exact in int32; the only rounding is of x, to half a step 2^(ex-21) of its
+    # block (nothing for the blocks written as zeros, whose entries are below 2^-100), plus FP32 sums
+    bound = 1e-6 * (np.abs(wd) @ np.abs(x))
+    for b in range(nb):
+        mx = np.abs(x[b * 32:(b + 1) * 32]).max()
+        half_step = np.ldexp(1.0, int(np.frexp(mx)[1]) - 21) if mx >= 2.0 ** -100 else 2.0 ** -100
+        bound += half_step * np.abs(wd[:, b * 32:(b + 1) * 32]).sum(axis=1)
+    assert np.all(np.abs(y - ref) <= bound)
