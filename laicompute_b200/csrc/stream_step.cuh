@@ -44,7 +44,8 @@
 // and split into three balanced base-128 int8 digits, plus -8 x (sum of the
 // group) for Q4_0's nibble offset and the inverse scale; a lane multiplies a
 // row's 8 quants with each digit word by dp4a, joins the three exact integer sums
-// and adds d_row x 2^-s x sum in FP32 (tile_block_dp in mv_streamk.cuh).
+// and adds d_row x 2^-s x sum in FP32 (ls_block_dp4 below; the team kernel instead
+// forms a whole block's sums with one mma.m16n8k32, tile_block_dp in mv_streamk.cuh).
 //
 // Every wait is bounded (about one second of SM clocks); a wait that runs out
 // records its code in `err`, and once `err` is set the dependency waits stop
@@ -235,12 +236,12 @@ __device__ __forceinline__ void ls_settle(const int* err) {
 __device__ __forceinline__ void ls_cbar() { named_sync(1, kLsWarps * 32); }
 
 // One 16x32 tile-block of the integer dot products with four rows per lane: lane (u, t)
-// of a half warp does the work of tile_block_dp's layout lanes 8u + t and 8u + 4 + t
+// of a half warp does the work of the fragment layout's lanes 8u + t and 8u + 4 + t
 // (rows 2u, 2u+8, 2u+1, 2u+9; column group t), so a block's activation record reaches 16
 // lanes rather than 32 and the shared-memory delivery per block drops from ~1.4 KB to
 // ~0.9 KB (the crossbar delivers 128 B per clock; it bounds this loop). acc[] holds the
-// four rows in that order; the products, their order and the FP32 steps per (row, group)
-// are tile_block_dp's.
+// four rows in that order; per (row, group) three dp4a chains, their exact sum
+// 2^14 s0 + 2^7 s1 + s2 (+ the group's -8 sum x) and one FP32 multiply-add by d x 2^-s.
 template <int WT>
 __device__ __forceinline__ void ls_block_dp4(uint32_t q, uint32_t sc, uint32_t xrec, int u, int t, float (&acc)[4]) {
     const uint4 xa = lds128(xrec + t * 32), xb = lds128(xrec + t * 32 + 16);
