@@ -407,13 +407,15 @@ void mv_scratch_free(MvScratch& sc) {
     sc = MvScratch{};
 }
 
-// Activation records a producing kernel already wrote for a tile-kernel projection.
+// What a producing kernel left for a projection: the tile kernel's activation records (xg), and
+// the rmsnorm's partial sums of squares (mode 1) or a unit scale (mode 2).
 struct RecIn {
     const uint8_t* xg = nullptr;
     int mode = 0;             // 1: rmsnorm scale from ss; 2: unit scale
     const float* ss = nullptr;
     int ss_tiles = 0;
-    bool dp = false;          // the team kernel's integer records (one sequence), not the tile kernel's
+    bool dp = false;          // one sequence on the team kernel's integer variant: it builds its records
+                              // from x and takes only mode / ss from here
 };
 
 // One projection: the team kernel for small batches, else activation

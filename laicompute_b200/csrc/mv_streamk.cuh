@@ -171,12 +171,12 @@ __device__ __forceinline__ int dp_byte_of(int k) {
     return frag_pos(k);
 }
 
-// A producing epilogue makes the integer variant's records of the values it
-// writes for the next projection, one 8-column group per 8 lanes: `val` is this
-// lane's value (0 where none), `k` its index in the group and `gidx` the group
-// (negative: no record). The group's maximum, digit sum and the record bytes
-// follow dp_group_record; every lane of the warp must call it. Returns the
-// group's sum of `sq` (for the next rmsnorm), valid in the group's lane k = 0.
+// A phase of the decode-step kernel makes the records of the values it writes for
+// its next projection (one scale per 8-column group, the step kernel's layout), one
+// 8-column group per 8 lanes: `val` is this lane's value (0 where none), `k` its
+// index in the group and `gidx` the group (negative: no record); every lane of the
+// warp must call it. Returns the group's sum of `sq` (for the next rmsnorm), valid
+// in the group's lane k = 0.
 template <int WT>
 __device__ __forceinline__ float dp_lane_record(float val, float sq, int k, int gidx, uint8_t* recs, int m1, int m2,
                                                    int m3) {
